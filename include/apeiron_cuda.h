@@ -1,0 +1,197 @@
+/*
+ * apeiron_cuda.h — C ABI of the B200 (sm_100a) backend for apeiron's integer
+ * Q8-activation projection: the decode GEMV `matvec_q8act` and the prefill GEMM
+ * `matmat_q8act` over GGUF Q8_0 / Q4_K / Q6_K weight payloads.
+ *
+ * Every exact entry point returns, bit for bit, what the reference's CPU kernel
+ * returns: `matvec_fixed(W, dequant(q))` in Q32.32 (`i64` words worth v / 2^32),
+ * or the same refusal.  Plain pointers and sizes only; no torch or CUDA types.
+ *
+ * Reference interfaces (paths inside the apeiron tree):
+ *   matvec_q8act                src/engine/chart/mod.rs:1887-1925
+ *   matvec_q8act_quant_chunked  src/engine/chart/ffn.rs:667-745
+ *   matmat_q8act                src/engine/kern/matmat.rs:134-200
+ *   quant_act / QuantAct        src/engine/chart/mod.rs:67-334
+ *   MatvecError                 src/engine/ops/matvec.rs:11-48
+ *   f32_to_fixed                src/engine/num/f32_convert.rs:44-49
+ *   PayloadRef / resident()     src/engine/loader.rs:421-434, :1469
+ *
+ * Activation encoding.  A reference `QuantAct` is `{scales: Vec<i64>, codes: Vec<i8>}`
+ * with every scale 0 or a power of two 2^e, e <= 62 (`act_scale`,
+ * src/engine/kern/pow2.rs:22-39).  Across this ABI a scale travels as its
+ * exponent byte: `exps[b] = e` for S_b = 2^e and `exps[b] = APX_EXP_ZERO` for S_b = 0.
+ *
+ * Threading.  One context per thread of control: calls on one context are
+ * serialised by an internal mutex (the engine calls from its pool's dispatching
+ * thread, src/engine/chart/pool.rs:895-905).  Synchronous entry points return
+ * after the result is in the caller's host buffer.
+ */
+#ifndef APEIRON_CUDA_H
+#define APEIRON_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ggml type ids the backend serves (src/format/quant.rs:27-37). */
+#define APX_GGML_TYPE_Q8_0 8u
+#define APX_GGML_TYPE_Q4_K 12u
+#define APX_GGML_TYPE_Q6_K 14u
+
+/* Exponent byte of a zero activation scale. */
+#define APX_EXP_ZERO 0xFFu
+
+/* Status codes.  1..9 mirror `MatvecError` (src/engine/ops/matvec.rs:11-48). */
+typedef enum apx_status {
+  APX_OK = 0,
+  APX_ERR_SHAPE_MISMATCH = 1,       /* ShapeMismatch { x = a, n_in = b }            */
+  APX_ERR_ROW_LENGTH = 2,           /* RowLength (unreachable for served families)  */
+  APX_ERR_SHORT_PAYLOAD = 3,        /* ShortPayload { need = a, have = b }          */
+  APX_ERR_LENGTH_OVERFLOW = 4,      /* LengthOverflow                               */
+  APX_ERR_UNSUPPORTED_QUANT = 5,    /* UnsupportedQuant { ggml_type }               */
+  APX_ERR_NONFINITE_SCALE = 6,      /* Dequant(NonFiniteScale { bits })             */
+  APX_ERR_FIXED_OVERFLOW = 7,       /* Dequant(FixedOverflow)                       */
+  APX_ERR_ACCUMULATOR_OVERFLOW = 8, /* AccumulatorOverflow                          */
+  APX_ERR_OUTPUT_OVERFLOW = 9,      /* OutputOverflow                               */
+  APX_ERR_QUANT_REFUSED = 10,       /* quant_act / f32_to_fixed returned None       */
+  /* Backend conditions with no reference counterpart. */
+  APX_ERR_INVALID_ARGUMENT = 20,    /* null pointer, unknown handle, bad size       */
+  APX_ERR_LAYOUT_MISMATCH = 21,     /* call geometry differs from the upload's      */
+  APX_ERR_CUDA = 22,                /* CUDA runtime error, code in cuda_error       */
+  APX_ERR_OUT_OF_MEMORY = 23,
+  APX_ERR_TOO_LARGE = 24            /* a size beyond a documented backend maximum   */
+} apx_status;
+
+/* Refusal detail.  Field meaning depends on `code` as noted in apx_status. */
+typedef struct apx_err {
+  int32_t code;       /* apx_status */
+  uint32_t ggml_type; /* UnsupportedQuant                                  */
+  uint64_t a;         /* ShapeMismatch.x, ShortPayload.need                */
+  uint64_t b;         /* ShapeMismatch.n_in, ShortPayload.have             */
+  uint64_t row;       /* first refusing output row (kernel-side refusals)  */
+  uint64_t col;       /* refusing column of a matmat call                  */
+  uint32_t bits;      /* NonFiniteScale.bits                               */
+  int32_t cuda_error; /* cudaError_t when code == APX_ERR_CUDA             */
+} apx_err;
+
+typedef struct apx_ctx apx_ctx;
+
+/* Per-call activation descriptor, produced on the device by apx_act_describe_async /
+ * apx_quant_*_async and read by the projection kernels.  Layout is part of the ABI
+ * so callers can allocate it; its contents are private. */
+typedef struct apx_act_desc {
+  uint32_t words[8];
+} apx_act_desc;
+
+/* Per-call refusal word written by the asynchronous projections (device memory).
+ * Decode with apx_status_decode after the stream is synchronised. */
+typedef struct apx_call_status {
+  unsigned long long first; /* (row << 24) | (kind << 16) | bits, minimum over rows */
+  unsigned long long spare;
+} apx_call_status;
+
+/* ---- context ---------------------------------------------------------------- */
+
+/* Open a backend context on CUDA device `device`.  Returns NULL on failure. */
+apx_ctx *apx_open(int device, apx_err *err);
+/* Free every device buffer the context owns. */
+void apx_close(apx_ctx *ctx);
+/* The backend's version string. */
+const char *apx_version(void);
+
+/* ---- weights ------------------------------------------------------------------ */
+
+/* Upload one projection's weight payload and repack it once for the kernels.
+ * `raw` is the borrowed `&resident()[at.off .. at.off + at.len]` slice the engine
+ * passes to matvec_q8act (src/engine/step.rs:346-378).  Validation follows
+ * matvec_fixed (src/engine/ops/matvec.rs:149-178): UnsupportedQuant, LengthOverflow,
+ * ShortPayload { need = n_out * row_bytes, have = raw_len }.  Non-finite block
+ * scales are found here, once, and reported by every later call exactly where the
+ * reference reports them. */
+int apx_tensor_upload(apx_ctx *ctx, uint32_t ggml_type, const uint8_t *raw,
+                      size_t raw_len, size_t n_out, size_t n_in, uint64_t *handle,
+                      apx_err *err);
+/* Release an uploaded tensor. */
+int apx_tensor_free(apx_ctx *ctx, uint64_t handle);
+/* Device bytes held by an uploaded tensor (repacked payload + row metadata). */
+size_t apx_tensor_device_bytes(apx_ctx *ctx, uint64_t handle);
+
+/* ---- synchronous drop-in entry points (host buffers) ----------------------------- */
+
+/* The decode contract (replaces matvec_q8act, src/engine/chart/mod.rs:1887).
+ * codes: q_len int8 activation codes; exps: ceil(q_len/32) exponent bytes;
+ * out: n_out Q32.32 words.  Refusals in the reference's order. */
+int apx_matvec_q8act(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
+                     const int8_t *codes, size_t q_len, const uint8_t *exps,
+                     int64_t *out, apx_err *err);
+
+/* Same result as apx_matvec_q8act with the validation order of the chunked caller
+ * (replaces matvec_q8act_quant_chunked, src/engine/chart/ffn.rs:667-745).  `chunks`
+ * is the CPU row-task count; the device kernel's decomposition does not depend on it. */
+int apx_matvec_q8act_chunked(apx_ctx *ctx, uint64_t tensor, size_t n_out,
+                             size_t n_in, const int8_t *codes, size_t q_len,
+                             const uint8_t *exps, size_t chunks, int64_t *out,
+                             apx_err *err);
+
+/* The prefill contract (replaces matmat_q8act, src/engine/kern/matmat.rs:134).
+ * k_cols activation columns; column c has codes[c*q_len ..] and exps[c*ceil(q_len/32) ..].
+ * out is column-major: out[c*n_out + r].  The call refuses with the lowest refusing
+ * column's refusal (err->col). */
+int apx_matmat_q8act(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
+                     size_t k_cols, const int8_t *codes, size_t q_len,
+                     const uint8_t *exps, int64_t *out, apx_err *err);
+
+/* quant_act on the device (src/engine/chart/mod.rs:258-334): Q32.32 in, codes and
+ * exponent bytes out.  APX_ERR_QUANT_REFUSED where the reference returns None. */
+int apx_quant_act(apx_ctx *ctx, const int64_t *x, size_t n, int8_t *codes,
+                  uint8_t *exps, apx_err *err);
+
+/* f32 boundary: y = from_q32(matvec_q8act(W, quant_act(f32_to_fixed(x)))).
+ * x: n_in floats, y: n_out floats, each the Q32.32 result rounded once to f32. */
+int apx_matvec_f32(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
+                   const float *x, float *y, apx_err *err);
+
+/* Parity hook: the exact int32 group dots the kernels form, one per (row, group)
+ * in group order (32-lane groups for Q8_0/Q4_K, 16-lane groups for Q6_K). */
+int apx_debug_block_dots(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
+                         const int8_t *codes, int32_t *dots, apx_err *err);
+
+/* ---- asynchronous device-buffer entry points ----------------------------------- */
+
+/* Validate device-resident codes/exps and fill the descriptor (device kernel). */
+int apx_act_describe_async(apx_ctx *ctx, const int8_t *d_codes,
+                           const uint8_t *d_exps, size_t n_in, apx_act_desc *d_desc,
+                           void *stream);
+/* Device quant_act of a Q32.32 vector. */
+int apx_quant_q32_async(apx_ctx *ctx, const int64_t *d_x, size_t n, int8_t *d_codes,
+                        uint8_t *d_exps, apx_act_desc *d_desc, void *stream);
+/* Device f32_to_fixed + quant_act of an f32 vector. */
+int apx_quant_f32_async(apx_ctx *ctx, const float *d_x, size_t n, int8_t *d_codes,
+                        uint8_t *d_exps, apx_act_desc *d_desc, void *stream);
+/* Exact projection of device activations; d_out_q32 and/or d_out_f32 may be NULL.
+ * d_status receives the refusal word (apx_status_decode).  Buffers padded by the
+ * caller: d_codes holds apx_act_padded_len(n_in) bytes (zero beyond n_in). */
+int apx_matvec_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
+                     const int8_t *d_codes, const uint8_t *d_exps,
+                     const apx_act_desc *d_desc, int64_t *d_out_q32, float *d_out_f32,
+                     apx_call_status *d_status, void *stream);
+/* Exact k-column projection of device activations (column-major outputs). */
+int apx_matmat_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
+                     size_t k_cols, const int8_t *d_codes, const uint8_t *d_exps,
+                     const apx_act_desc *d_descs, int64_t *d_out_q32,
+                     float *d_out_f32, apx_call_status *d_status, void *stream);
+/* Activation buffer length (bytes of codes) the async kernels read for width n_in. */
+size_t apx_act_padded_len(size_t n_in);
+/* Decode a refusal word (host copy of *d_status) together with the tensor's
+ * upload-time findings into err; returns err->code. */
+int apx_status_decode(apx_ctx *ctx, uint64_t tensor, const apx_call_status *status,
+                      apx_err *err);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* APEIRON_CUDA_H */

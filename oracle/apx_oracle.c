@@ -1,0 +1,768 @@
+/*
+ * apx_oracle.c — CPU restatement of apeiron's integer Q8-activation projection.
+ *
+ * TEST INFRASTRUCTURE ONLY (see apx_oracle.h).  The product library never links it.
+ *
+ * Two independent restatements live here, as in the reference:
+ *   - the contract: row dequantization to Q32.32 and an exact checked i128 dot
+ *     (`matvec_fixed`, src/engine/ops/matvec.rs:86-222);
+ *   - the fused row kernel: per 32-lane group `acc += S_b*(w_scale*D - w_min*sum(xq))`
+ *     (`matvec_q8act`, src/engine/chart/mod.rs:497-1013, 1645-1925).
+ * tests/test_oracle_golden.py checks them against each other and against the reference's
+ * known-answer values.  Paths in comments are relative to the apeiron source tree.
+ */
+#include "apx_oracle.h"
+
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+
+typedef __int128 i128;
+typedef unsigned __int128 u128;
+
+#define I128_MAX ((i128)(((u128)1 << 127) - 1))
+#define ACT_QK 32
+#define QK_K 256
+#define Q8_0_BYTES 34
+#define Q4_K_BYTES 144
+#define Q6_K_BYTES 210
+
+static int fail(apx_err *e, int code) {
+  if (e) {
+    memset(e, 0, sizeof *e);
+    e->code = code;
+  }
+  return code;
+}
+
+static void clear(apx_err *e) {
+  if (e) memset(e, 0, sizeof *e);
+}
+
+/* round_shift_32 (src/engine/num/value.rs:10-12): floor((v + 2^31) / 2^32), evaluated as
+ * q + [r >= 2^31] with v = q*2^32 + r so the add cannot leave i128. */
+static i128 rs32(i128 v) {
+  i128 q = v >> 32;
+  uint64_t r = (uint64_t)v & 0xFFFFFFFFull;
+  return q + (r >= 0x80000000ull ? 1 : 0);
+}
+
+void apxo_round_shift_32(int64_t hi, uint64_t lo, int64_t *out_hi, uint64_t *out_lo) {
+  i128 v = ((i128)hi << 64) | (i128)lo;
+  i128 r = rs32(v);
+  *out_hi = (int64_t)(r >> 64);
+  *out_lo = (uint64_t)r;
+}
+
+/* `round_to_i64` (chart/mod.rs:1746-1753): the rounded value when it fits i64. */
+static int round_to_i64(i128 acc, int64_t *out) {
+  i128 r = rs32(acc);
+  if (r > (i128)INT64_MAX || r < (i128)INT64_MIN) return 1;
+  *out = (int64_t)r;
+  return 0;
+}
+
+/* f16_to_fixed (src/engine/num/dequant.rs:25-42). */
+int apxo_f16_to_fixed(uint16_t h, int64_t *out) {
+  uint16_t sign = h >> 15, e = (h >> 10) & 0x1f, m = h & 0x3ff;
+  int64_t mag;
+  if (e == 0) {
+    mag = (int64_t)m << 8;
+  } else if (e == 0x1f) {
+    return APX_ERR_NONFINITE_SCALE;
+  } else {
+    mag = ((int64_t)m + 1024) << (e + 7);
+  }
+  *out = sign ? -mag : mag;
+  return 0;
+}
+
+/* f16_split (src/engine/kern/pow2.rs:52-64). */
+int apxo_f16_split(uint16_t h, int32_t *m, uint32_t *k) {
+  uint32_t e = (h >> 10) & 0x1f;
+  int32_t f = (int32_t)(h & 0x3ff);
+  if (e == 31) return 1;
+  int32_t mm = e == 0 ? f : f + 1024;
+  uint32_t kk = e == 0 ? 8 : e + 7;
+  *m = (h >> 15) ? -mm : mm;
+  *k = kk;
+  return 0;
+}
+
+/* act_scale (src/engine/kern/pow2.rs:22-39). */
+int apxo_act_scale(uint64_t absmax, uint64_t *s_out) {
+  if (absmax == 0) {
+    *s_out = 0;
+    return 0;
+  }
+  uint64_t need = absmax / 127 + (absmax % 127 != 0);
+  uint64_t s = 1;
+  uint32_t steps = 0;
+  while (s < need && steps < 62) {
+    s *= 2;
+    steps++;
+  }
+  if (s < need) return 1;
+  *s_out = s;
+  return 0;
+}
+
+/* finish (src/engine/kern/pow2.rs:76-96). */
+int apxo_finish(int64_t acc, uint32_t s, int64_t *out) {
+  i128 wide = acc, v;
+  if (s >= 32) {
+    uint32_t up = s - 32;
+    if (acc == 0) {
+      v = 0;
+    } else if (up > 63) {
+      return 1;
+    } else {
+      /* wide * 2^up with up <= 63 fits i128 for any i64 wide. */
+      v = wide * ((i128)1 << up);
+    }
+  } else {
+    uint32_t down = 32 - s;
+    v = (wide + ((i128)1 << (down - 1))) >> down;
+  }
+  if (v < (i128)INT64_MIN || v > (i128)INT64_MAX) return 1;
+  *out = (int64_t)v;
+  return 0;
+}
+
+/* F32::to_q32 (src/engine/num/fp.rs:186-230) behind f32_to_fixed (f32_convert.rs:44-49):
+ * round(v * 2^32) with ties away from zero; None for NaN/Inf or outside [-2^63, 2^63). */
+int apxo_f32_to_q32(uint32_t bits, int64_t *out) {
+  uint32_t e = (bits >> 23) & 0xff;
+  if (e == 0xff) return 1;
+  uint32_t frac = bits & 0x007fffff;
+  uint64_t m = e == 0 ? frac : (frac | 0x00800000u);
+  int neg = (bits & 0x80000000u) != 0;
+  uint32_t ee = e == 0 ? 1 : e;
+  u128 mag;
+  if (ee >= 118) {
+    uint32_t k = ee - 118;
+    if (k > 40) return 1;
+    mag = (u128)m << k;
+  } else {
+    uint32_t sh = 118 - ee;
+    if (sh > 24)
+      mag = 0;
+    else
+      mag = (u128)((m + (1ull << (sh - 1))) >> sh);
+  }
+  u128 lim = (u128)1 << 63;
+  if (neg) {
+    if (mag > lim) return 1;
+    if (mag == lim) {
+      *out = INT64_MIN;
+      return 0;
+    }
+    *out = -(int64_t)mag;
+    return 0;
+  }
+  if (mag >= lim) return 1;
+  *out = (int64_t)mag;
+  return 0;
+}
+
+/* QuantAct::dequantizes (chart/mod.rs:124-146). */
+static int dequantizes(const int8_t *codes, size_t n, const int64_t *scales) {
+  size_t nb = (n + ACT_QK - 1) / ACT_QK;
+  for (size_t b = 0; b < nb; b++) {
+    int64_t p;
+    if (__builtin_mul_overflow(scales[b], (int64_t)127, &p)) {
+      size_t end = (b + 1) * ACT_QK < n ? (b + 1) * ACT_QK : n;
+      for (size_t l = b * ACT_QK; l < end; l++)
+        if (__builtin_mul_overflow(scales[b], (int64_t)codes[l], &p)) return 0;
+    }
+  }
+  return 1;
+}
+
+/* quant_act (src/engine/chart/mod.rs:258-334). */
+int apxo_quant_act(const int64_t *x, size_t n, int8_t *codes, int64_t *scales) {
+  size_t blocks = (n + ACT_QK - 1) / ACT_QK;
+  for (size_t b = 0; b < blocks; b++) {
+    size_t base = b * ACT_QK;
+    size_t take = n - base < ACT_QK ? n - base : ACT_QK;
+    uint64_t absmax = 0;
+    for (size_t l = 0; l < take; l++) {
+      int64_t v = x[base + l];
+      uint64_t mag = v < 0 ? (uint64_t)0 - (uint64_t)v : (uint64_t)v;
+      if (mag > absmax) absmax = mag;
+    }
+    uint64_t s;
+    if (apxo_act_scale(absmax, &s)) s = UINT64_MAX;
+    if (s > (uint64_t)INT64_MAX) return 1;
+    scales[b] = (int64_t)s;
+    for (size_t l = 0; l < take; l++) {
+      int64_t v = x[base + l];
+      int8_t code = 0;
+      if (s != 0) {
+        uint64_t m = v < 0 ? (uint64_t)0 - (uint64_t)v : (uint64_t)v;
+        uint32_t shift = (uint32_t)__builtin_ctzll(s);
+        uint64_t q = m >> shift, r = m & (s - 1);
+        uint64_t mag = q + (2 * r >= s ? 1 : 0);
+        if (mag > 127) return 1;
+        code = (int8_t)(v < 0 ? -(int64_t)mag : (int64_t)mag);
+      }
+      codes[base + l] = code;
+    }
+  }
+  if (!dequantizes(codes, n, scales)) return 1;
+  return 0;
+}
+
+/* QuantAct::dequant (chart/mod.rs:188-212). */
+int apxo_dequant_act(const int8_t *codes, size_t n, const int64_t *scales,
+                     size_t n_scales, int64_t *out) {
+  for (size_t i = 0; i < n; i++) {
+    if (i / ACT_QK >= n_scales) return 1;
+    if (__builtin_mul_overflow(scales[i / ACT_QK], (int64_t)codes[i], &out[i])) return 1;
+  }
+  return 0;
+}
+
+/* block_geom (src/format/quant.rs:129-148), restricted to the served families. */
+static int geom(uint32_t t, size_t *qk, size_t *bb) {
+  switch (t) {
+    case APX_GGML_TYPE_Q8_0: *qk = 32; *bb = Q8_0_BYTES; return 1;
+    case APX_GGML_TYPE_Q4_K: *qk = QK_K; *bb = Q4_K_BYTES; return 1;
+    case APX_GGML_TYPE_Q6_K: *qk = QK_K; *bb = Q6_K_BYTES; return 1;
+    default: return 0;
+  }
+}
+
+/* fused_type (src/engine/ops/fused.rs): the families with a fused row kernel. */
+static int fused_type(uint32_t t) {
+  return t == 8 || t == 6 || t == 10 || t == 11 || t == 12 || t == 14;
+}
+
+static uint16_t rd16(const uint8_t *p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+static int nonfinite(apx_err *err, uint16_t bits) {
+  fail(err, APX_ERR_NONFINITE_SCALE);
+  if (err) err->bits = bits;
+  return APX_ERR_NONFINITE_SCALE;
+}
+
+/* get_scale_min_k4 (src/format/quant.rs:482-491). */
+static void q4k_scale_min(const uint8_t *sc, int j, int *s, int *m) {
+  if (j < 4) {
+    *s = sc[j] & 63;
+    *m = sc[j + 4] & 63;
+  } else {
+    *s = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4);
+    *m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+  }
+}
+
+/* q6_k_codes (src/format/quant.rs:574-599): 256 signed codes in output order. */
+static void q6k_codes(const uint8_t *blk, int8_t *out) {
+  const uint8_t *ql = blk, *qh = blk + 128;
+  for (int n = 0; n < 2; n++) {
+    for (int l = 0; l < 32; l++) {
+      uint8_t hi = qh[32 * n + l];
+      out[128 * n + l] = (int8_t)(((ql[64 * n + l] & 0xF) | (((hi >> 0) & 3) << 4)) - 32);
+      out[128 * n + l + 32] = (int8_t)(((ql[64 * n + l + 32] & 0xF) | (((hi >> 2) & 3) << 4)) - 32);
+      out[128 * n + l + 64] = (int8_t)(((ql[64 * n + l] >> 4) | (((hi >> 4) & 3) << 4)) - 32);
+      out[128 * n + l + 96] = (int8_t)(((ql[64 * n + l + 32] >> 4) | (((hi >> 6) & 3) << 4)) - 32);
+    }
+  }
+}
+
+static int mul_chk(int64_t a, int64_t b, int64_t *o, apx_err *err) {
+  if (__builtin_mul_overflow(a, b, o)) return fail(err, APX_ERR_FIXED_OVERFLOW);
+  return 0;
+}
+
+/* dequant_row_fixed (src/engine/num/dequant.rs:99-129) with the Q8_0 (:311-346),
+ * Q4_K (:487-593) and Q6_K (:595-640) row bodies. */
+int apxo_dequant_row(uint32_t t, const uint8_t *row, size_t row_len, size_t n,
+                     int64_t *out, apx_err *err) {
+  size_t qk, bb;
+  clear(err);
+  if (!geom(t, &qk, &bb)) return fail(err, APX_ERR_UNSUPPORTED_QUANT);
+  size_t blocks = (n + qk - 1) / qk;
+  if (blocks * bb > row_len) return fail(err, APX_ERR_SHORT_PAYLOAD);
+  size_t pushed = 0;
+  for (size_t b = 0; b < blocks; b++) {
+    const uint8_t *blk = row + b * bb;
+    size_t take = n - b * qk < qk ? n - b * qk : qk;
+    int64_t v;
+    if (t == APX_GGML_TYPE_Q8_0) {
+      int64_t d;
+      if (apxo_f16_to_fixed(rd16(blk), &d)) return nonfinite(err, rd16(blk));
+      for (size_t l = 0; l < take; l++) {
+        if (mul_chk(d, (int8_t)blk[2 + l], &v, err)) return APX_ERR_FIXED_OVERFLOW;
+        out[pushed++] = v;
+      }
+    } else if (t == APX_GGML_TYPE_Q4_K) {
+      int64_t d, dmin, vals[QK_K];
+      if (apxo_f16_to_fixed(rd16(blk), &d)) return nonfinite(err, rd16(blk));
+      if (apxo_f16_to_fixed(rd16(blk + 2), &dmin)) return nonfinite(err, rd16(blk + 2));
+      const uint8_t *sc = blk + 4, *qs = blk + 16;
+      for (int g = 0; g < 4; g++) {
+        int sl, ml, sh, mh;
+        q4k_scale_min(sc, 2 * g, &sl, &ml);
+        q4k_scale_min(sc, 2 * g + 1, &sh, &mh);
+        int64_t slope_lo, icpt_lo, slope_hi, icpt_hi;
+        if (mul_chk(d, sl, &slope_lo, err) || mul_chk(dmin, ml, &icpt_lo, err) ||
+            mul_chk(d, sh, &slope_hi, err) || mul_chk(dmin, mh, &icpt_hi, err))
+          return APX_ERR_FIXED_OVERFLOW;
+        for (int l = 0; l < 32; l++) {
+          int64_t p;
+          if (mul_chk(slope_lo, qs[32 * g + l] & 0xF, &p, err) ||
+              __builtin_sub_overflow(p, icpt_lo, &vals[64 * g + l]))
+            return fail(err, APX_ERR_FIXED_OVERFLOW);
+          if (mul_chk(slope_hi, qs[32 * g + l] >> 4, &p, err) ||
+              __builtin_sub_overflow(p, icpt_hi, &vals[64 * g + 32 + l]))
+            return fail(err, APX_ERR_FIXED_OVERFLOW);
+        }
+      }
+      for (size_t l = 0; l < take; l++) out[pushed++] = vals[l];
+    } else { /* Q6_K */
+      int64_t d, vals[QK_K];
+      int8_t codes[QK_K];
+      uint16_t dbits = rd16(blk + 208);
+      if (apxo_f16_to_fixed(dbits, &d)) return nonfinite(err, dbits);
+      q6k_codes(blk, codes);
+      for (int g = 0; g < 16; g++) {
+        int64_t slope;
+        if (mul_chk(d, (int8_t)blk[192 + g], &slope, err)) return APX_ERR_FIXED_OVERFLOW;
+        for (int l = 0; l < 16; l++)
+          if (mul_chk(slope, codes[16 * g + l], &vals[16 * g + l], err))
+            return APX_ERR_FIXED_OVERFLOW;
+      }
+      for (size_t l = 0; l < take; l++) out[pushed++] = vals[l];
+    }
+  }
+  return 0;
+}
+
+/* The shared geometry checks of matvec_fixed (ops/matvec.rs:156-172). */
+static int row_geometry(uint32_t t, size_t n_out, size_t n_in, size_t raw_len,
+                        size_t *row_bytes, apx_err *err) {
+  size_t qk = 1, bb = 0, need;
+  geom(t, &qk, &bb);
+  size_t blocks = (n_in + qk - 1) / qk;
+  if (__builtin_mul_overflow(blocks, bb, row_bytes)) return fail(err, APX_ERR_LENGTH_OVERFLOW);
+  if (__builtin_mul_overflow(n_out, *row_bytes, &need)) return fail(err, APX_ERR_LENGTH_OVERFLOW);
+  if (raw_len < need) {
+    fail(err, APX_ERR_SHORT_PAYLOAD);
+    if (err) {
+      err->a = need;
+      err->b = raw_len;
+    }
+    return APX_ERR_SHORT_PAYLOAD;
+  }
+  return 0;
+}
+
+static int shape_mismatch(apx_err *err, size_t x, size_t n_in) {
+  fail(err, APX_ERR_SHAPE_MISMATCH);
+  if (err) {
+    err->a = x;
+    err->b = n_in;
+  }
+  return APX_ERR_SHAPE_MISMATCH;
+}
+
+/* matvec_fixed (src/engine/ops/matvec.rs:149-222) with row_dot_fixed (:86-119). */
+int apxo_matvec_fixed(uint32_t t, const uint8_t *raw, size_t raw_len, size_t n_out,
+                      size_t n_in, const int64_t *x, size_t x_len, int64_t *out,
+                      apx_err *err) {
+  size_t qk, bb, row_bytes;
+  clear(err);
+  if (!geom(t, &qk, &bb)) {
+    fail(err, APX_ERR_UNSUPPORTED_QUANT);
+    if (err) err->ggml_type = t;
+    return APX_ERR_UNSUPPORTED_QUANT;
+  }
+  if (x_len != n_in) return shape_mismatch(err, x_len, n_in);
+  int rc = row_geometry(t, n_out, n_in, raw_len, &row_bytes, err);
+  if (rc) return rc;
+  int64_t *w = (int64_t *)malloc((n_in ? n_in : 1) * sizeof(int64_t));
+  for (size_t o = 0; o < n_out; o++) {
+    rc = apxo_dequant_row(t, raw + o * row_bytes, row_bytes, n_in, w, err);
+    if (rc) {
+      if (err) err->row = o;
+      free(w);
+      return rc;
+    }
+    i128 acc = 0;
+    for (size_t i = 0; i < n_in; i++) {
+      i128 prod = (i128)w[i] * (i128)x[i]; /* |i64 * i64| < 2^126: no overflow */
+      if (__builtin_add_overflow(acc, prod, &acc)) {
+        fail(err, APX_ERR_ACCUMULATOR_OVERFLOW);
+        if (err) err->row = o;
+        free(w);
+        return APX_ERR_ACCUMULATOR_OVERFLOW;
+      }
+    }
+    if (round_to_i64(acc, &out[o])) {
+      fail(err, APX_ERR_OUTPUT_OVERFLOW);
+      if (err) err->row = o;
+      free(w);
+      return APX_ERR_OUTPUT_OVERFLOW;
+    }
+  }
+  free(w);
+  return 0;
+}
+
+/* ---- the fused rows (chart/mod.rs:497-1013) ------------------------------------ */
+
+/* QuantAct::magnitude (chart/mod.rs:159-181): 0 exact, 1 NoQ32, 2 TotalOverflow. */
+static int magnitude(const int8_t *codes, size_t n, const int64_t *scales, size_t n_scales) {
+  i128 acc = 0;
+  for (size_t i = 0; i < n; i++) {
+    if (i / ACT_QK >= n_scales) return 1;
+    int64_t v;
+    if (__builtin_mul_overflow(scales[i / ACT_QK], (int64_t)codes[i], &v)) return 1;
+    i128 mag = v < 0 ? -(i128)v : (i128)v;
+    if (__builtin_add_overflow(acc, mag, &acc)) return 2;
+  }
+  return 0;
+}
+
+static i128 sat_mul(i128 a, i128 b) {
+  i128 r;
+  if (__builtin_mul_overflow(a, b, &r)) return I128_MAX;
+  return r;
+}
+
+/* q8act_fast_bound_ok (chart/mod.rs:362-383). */
+static int fast_bound_ok(size_t n_in, i128 top, const int64_t *scales, size_t n_scales,
+                         int narrow) {
+  i128 s_max = 0;
+  for (size_t b = 0; b < n_scales; b++) {
+    i128 a = scales[b] < 0 ? -(i128)scales[b] : (i128)scales[b];
+    if (a > s_max) s_max = a;
+  }
+  if (narrow && sat_mul(s_max, 32 * top * 127) > (i128)INT64_MAX) return 0;
+  i128 f16max = (i128)65504 << 32;
+  i128 bound = sat_mul(sat_mul(sat_mul(sat_mul((i128)n_in, f16max), top), 127), s_max);
+  return bound < I128_MAX;
+}
+
+/* One fast row's exact pre-rounding accumulator (RowAcc over the family decoder's
+ * groups, chart/mod.rs:497-514, 554-938, 947-1013); 1 on a non-finite scale. */
+static int fast_row(uint32_t t, const uint8_t *row, size_t n_in, const int8_t *codes,
+                    const int64_t *S, i128 *acc_out) {
+  i128 acc = 0;
+  size_t groups = n_in / ACT_QK;
+  if (t == APX_GGML_TYPE_Q8_0) {
+    for (size_t g = 0; g < groups; g++) {
+      const uint8_t *blk = row + g * Q8_0_BYTES;
+      int64_t d;
+      if (apxo_f16_to_fixed(rd16(blk), &d)) return 1;
+      const int8_t *q = (const int8_t *)(blk + 2);
+      const int8_t *x = codes + g * ACT_QK;
+      int32_t dot = 0;
+      for (int l = 0; l < 32; l++) dot += (int32_t)q[l] * (int32_t)x[l];
+      acc += (i128)S[g] * ((i128)d * (i128)dot);
+    }
+  } else if (t == APX_GGML_TYPE_Q4_K) {
+    for (size_t g = 0; g < groups; g += 2) {
+      size_t pp = g / 2, b = pp / 4, p = pp % 4;
+      const uint8_t *blk = row + b * Q4_K_BYTES;
+      int64_t d, dmin;
+      if (apxo_f16_to_fixed(rd16(blk), &d)) return 1;
+      if (apxo_f16_to_fixed(rd16(blk + 2), &dmin)) return 1;
+      int sl, ml, sh, mh;
+      q4k_scale_min(blk + 4, (int)(2 * p), &sl, &ml);
+      q4k_scale_min(blk + 4, (int)(2 * p + 1), &sh, &mh);
+      const uint8_t *qs = blk + 16 + 32 * p;
+      const int8_t *xl = codes + g * ACT_QK, *xh = codes + (g + 1) * ACT_QK;
+      int32_t dl = 0, dh = 0, sxl = 0, sxh = 0;
+      for (int l = 0; l < 32; l++) {
+        dl += (int32_t)(qs[l] & 0xF) * xl[l];
+        dh += (int32_t)(qs[l] >> 4) * xh[l];
+        sxl += xl[l];
+        sxh += xh[l];
+      }
+      i128 in_lo = (i128)(d * sl) * dl - (i128)(dmin * ml) * sxl;
+      i128 in_hi = (i128)(d * sh) * dh - (i128)(dmin * mh) * sxh;
+      acc += (i128)S[g] * in_lo;
+      acc += (i128)S[g + 1] * in_hi;
+    }
+  } else { /* Q6_K, n_in % 256 == 0 */
+    for (size_t b = 0; b < n_in / QK_K; b++) {
+      const uint8_t *blk = row + b * Q6_K_BYTES;
+      int64_t d;
+      if (apxo_f16_to_fixed(rd16(blk + 208), &d)) return 1;
+      int8_t q[QK_K];
+      q6k_codes(blk, q);
+      for (int c = 0; c < 8; c++) {
+        int64_t gd = 0;
+        for (int h = 0; h < 2; h++) {
+          int g16 = 2 * c + h;
+          int32_t dot = 0;
+          for (int l = 0; l < 16; l++)
+            dot += (int32_t)q[16 * g16 + l] * codes[(b * 16 + g16) * 16 + l];
+          gd += (int64_t)(int8_t)blk[192 + g16] * dot;
+        }
+        acc += (i128)S[b * 8 + c] * ((i128)d * gd);
+      }
+    }
+  }
+  *acc_out = acc;
+  return 0;
+}
+
+/* The plan of matvec_q8act (q8act_plan, chart/mod.rs:1676-1727) reduced to what the
+ * result depends on: 0 = fused fast rows, 1 = the contract (matvec_fixed on x-hat),
+ * 2 = NoQ32 (FixedOverflow refusal). */
+static int plan(uint32_t t, size_t n_in, const int8_t *codes, size_t q_len,
+                const int64_t *scales, size_t n_scales, int *fast) {
+  int mag = magnitude(codes, q_len, scales, n_scales);
+  if (mag == 1) return 2;
+  if (mag == 2 || !fused_type(t)) return 1;
+  *fast = 0;
+  if (t == APX_GGML_TYPE_Q8_0 && n_in % 32 == 0)
+    *fast = fast_bound_ok(n_in, 128, scales, n_scales, 1);
+  else if (t == APX_GGML_TYPE_Q4_K && n_in % 64 == 0)
+    *fast = fast_bound_ok(n_in, 1008, scales, n_scales, 0);
+  else if (t == APX_GGML_TYPE_Q6_K && n_in % 256 == 0)
+    *fast = fast_bound_ok(n_in, 4096, scales, n_scales, 0);
+  return 0;
+}
+
+static int contract(uint32_t t, const uint8_t *raw, size_t raw_len, size_t n_out,
+                    size_t n_in, const int8_t *codes, size_t q_len,
+                    const int64_t *scales, size_t n_scales, int64_t *out, apx_err *err) {
+  int64_t *xhat = (int64_t *)malloc((q_len ? q_len : 1) * sizeof(int64_t));
+  if (apxo_dequant_act(codes, q_len, scales, n_scales, xhat)) {
+    free(xhat);
+    return fail(err, APX_ERR_FIXED_OVERFLOW);
+  }
+  int rc = apxo_matvec_fixed(t, raw, raw_len, n_out, n_in, xhat, q_len, out, err);
+  free(xhat);
+  return rc;
+}
+
+/* Fast rows [lo, hi): 0 ok, APX_ERR_OUTPUT_OVERFLOW (row in *bad), or -1 for a
+ * non-finite scale at row *bad (the caller falls back to the contract). */
+static int fast_rows(uint32_t t, const uint8_t *raw, size_t row_bytes, size_t lo,
+                     size_t hi, size_t n_in, const int8_t *codes, const int64_t *S,
+                     int64_t *out, size_t *bad) {
+  for (size_t o = lo; o < hi; o++) {
+    i128 acc;
+    if (fast_row(t, raw + o * row_bytes, n_in, codes, S, &acc)) {
+      *bad = o;
+      return -1;
+    }
+    if (round_to_i64(acc, &out[o])) {
+      *bad = o;
+      return APX_ERR_OUTPUT_OVERFLOW;
+    }
+  }
+  return 0;
+}
+
+/* matvec_q8act (src/engine/chart/mod.rs:1887-1925) with q8act_rows (:1777-1859). */
+int apxo_matvec_q8act(uint32_t t, const uint8_t *raw, size_t raw_len, size_t n_out,
+                      size_t n_in, const int8_t *codes, size_t q_len,
+                      const int64_t *scales, size_t n_scales, int64_t *out,
+                      apx_err *err) {
+  clear(err);
+  int fast = 0;
+  int p = plan(t, n_in, codes, q_len, scales, n_scales, &fast);
+  if (p == 2) return fail(err, APX_ERR_FIXED_OVERFLOW);
+  if (p == 1)
+    return contract(t, raw, raw_len, n_out, n_in, codes, q_len, scales, n_scales, out, err);
+  size_t qk, bb, row_bytes;
+  if (!geom(t, &qk, &bb)) {
+    fail(err, APX_ERR_UNSUPPORTED_QUANT);
+    if (err) err->ggml_type = t;
+    return APX_ERR_UNSUPPORTED_QUANT;
+  }
+  if (q_len != n_in) return shape_mismatch(err, q_len, n_in);
+  int rc = row_geometry(t, n_out, n_in, raw_len, &row_bytes, err);
+  if (rc) return rc;
+  if (!fast)
+    return contract(t, raw, raw_len, n_out, n_in, codes, q_len, scales, n_scales, out, err);
+  size_t bad = 0;
+  rc = fast_rows(t, raw, row_bytes, 0, n_out, n_in, codes, scales, out, &bad);
+  if (rc == -1)
+    return contract(t, raw, raw_len, n_out, n_in, codes, q_len, scales, n_scales, out, err);
+  if (rc) {
+    fail(err, rc);
+    if (err) err->row = bad;
+  }
+  return rc;
+}
+
+/* matvec_q8act_quant_chunked (src/engine/chart/ffn.rs:667-745): with more than one
+ * chunk the payload and shape checks run before the plan. */
+int apxo_matvec_q8act_chunked(uint32_t t, const uint8_t *raw, size_t raw_len,
+                              size_t n_out, size_t n_in, const int8_t *codes,
+                              size_t q_len, const int64_t *scales, size_t n_scales,
+                              size_t chunks, int64_t *out, apx_err *err) {
+  size_t upper = n_out == 0 ? 1 : n_out, actual = chunks < 8 ? chunks : 8;
+  if (actual < 1) actual = 1;
+  if (actual > upper) actual = upper;
+  size_t qk, bb, row_bytes;
+  if (actual == 1 || !geom(t, &qk, &bb))
+    return apxo_matvec_q8act(t, raw, raw_len, n_out, n_in, codes, q_len, scales, n_scales,
+                             out, err);
+  clear(err);
+  int rc = row_geometry(t, n_out, n_in, raw_len, &row_bytes, err);
+  if (rc) return rc;
+  if (q_len != n_in) return shape_mismatch(err, q_len, n_in);
+  return apxo_matvec_q8act(t, raw, raw_len, n_out, n_in, codes, q_len, scales, n_scales,
+                           out, err);
+}
+
+/* matmat_q8act (src/engine/kern/matmat.rs:92-134): column c equals the per-column
+ * call; the call refuses with the lowest refusing column's refusal. */
+int apxo_matmat_q8act(uint32_t t, const uint8_t *raw, size_t raw_len, size_t n_out,
+                      size_t n_in, size_t k_cols, const int8_t *codes, size_t q_len,
+                      const int64_t *scales, int64_t *out, apx_err *err) {
+  size_t nb = (q_len + ACT_QK - 1) / ACT_QK;
+  clear(err);
+  for (size_t c = 0; c < k_cols; c++) {
+    int rc = apxo_matvec_q8act(t, raw, raw_len, n_out, n_in, codes + c * q_len, q_len,
+                               scales + c * nb, nb, out + c * n_out, err);
+    if (rc) {
+      if (err) err->col = c;
+      return rc;
+    }
+  }
+  return 0;
+}
+
+/* exact_dot (src/engine/kern/gemm.rs:470-486). */
+int apxo_exact_dot_q8_0(const uint8_t *row, size_t blocks, const int8_t *codes,
+                        const int64_t *scales, int64_t *out) {
+  i128 acc = 0;
+  for (size_t b = 0; b < blocks; b++) {
+    const uint8_t *blk = row + b * Q8_0_BYTES;
+    int32_t m;
+    uint32_t k;
+    if (apxo_f16_split(rd16(blk), &m, &k)) return 1;
+    int32_t dot = 0;
+    for (int l = 0; l < 32; l++) dot += (int32_t)(int8_t)blk[2 + l] * codes[b * 32 + l];
+    i128 d = (i128)m << k, term;
+    if (__builtin_mul_overflow(d, (i128)scales[b], &term)) return 1;
+    if (__builtin_mul_overflow(term, (i128)dot, &term)) return 1;
+    if (__builtin_add_overflow(acc, term, &acc)) return 1;
+  }
+  return round_to_i64(acc, out);
+}
+
+/* Exact int32 group dots (the decoders' `dot` values, chart/mod.rs:554-938). */
+int apxo_block_dots(uint32_t t, const uint8_t *raw, size_t n_out, size_t n_in,
+                    const int8_t *codes, int32_t *dots) {
+  size_t qk, bb;
+  if (!geom(t, &qk, &bb)) return APX_ERR_UNSUPPORTED_QUANT;
+  size_t blocks = (n_in + qk - 1) / qk, row_bytes = blocks * bb;
+  size_t per_row = t == APX_GGML_TYPE_Q6_K ? blocks * 16 : blocks * (qk / 32);
+  for (size_t o = 0; o < n_out; o++) {
+    const uint8_t *row = raw + o * row_bytes;
+    int32_t *dst = dots + o * per_row;
+    for (size_t b = 0; b < blocks; b++) {
+      const uint8_t *blk = row + b * bb;
+      if (t == APX_GGML_TYPE_Q8_0) {
+        int32_t dot = 0;
+        for (int l = 0; l < 32; l++) dot += (int32_t)(int8_t)blk[2 + l] * codes[b * 32 + l];
+        dst[b] = dot;
+      } else if (t == APX_GGML_TYPE_Q4_K) {
+        for (int p = 0; p < 4; p++) {
+          int32_t dl = 0, dh = 0;
+          for (int l = 0; l < 32; l++) {
+            dl += (int32_t)(blk[16 + 32 * p + l] & 0xF) * codes[b * 256 + 64 * p + l];
+            dh += (int32_t)(blk[16 + 32 * p + l] >> 4) * codes[b * 256 + 64 * p + 32 + l];
+          }
+          dst[b * 8 + 2 * p] = dl;
+          dst[b * 8 + 2 * p + 1] = dh;
+        }
+      } else {
+        int8_t q[QK_K];
+        q6k_codes(blk, q);
+        for (int g = 0; g < 16; g++) {
+          int32_t dot = 0;
+          for (int l = 0; l < 16; l++) dot += (int32_t)q[16 * g + l] * codes[b * 256 + 16 * g + l];
+          dst[b * 16 + g] = dot;
+        }
+      }
+    }
+  }
+  return 0;
+}
+
+/* ---- CPU baseline: the fused rows over contiguous row chunks on threads ------------
+ * (the pool split of matvec_q8act_quant_chunked, src/engine/chart/ffn.rs:667-745). */
+
+typedef struct {
+  uint32_t t;
+  const uint8_t *raw;
+  size_t row_bytes, lo, hi, n_in, k_cols, n_out;
+  const int8_t *codes;
+  const int64_t *scales;
+  int64_t *out;
+  int rc;
+  size_t bad;
+} mt_task;
+
+static void *mt_run(void *arg) {
+  mt_task *a = (mt_task *)arg;
+  size_t nb = (a->n_in + ACT_QK - 1) / ACT_QK;
+  a->rc = 0;
+  for (size_t c = 0; c < a->k_cols && a->rc == 0; c++)
+    a->rc = fast_rows(a->t, a->raw, a->row_bytes, a->lo, a->hi, a->n_in,
+                      a->codes + c * a->n_in, a->scales + c * nb, a->out + c * a->n_out,
+                      &a->bad);
+  return NULL;
+}
+
+static int run_mt(uint32_t t, const uint8_t *raw, size_t raw_len, size_t n_out,
+                  size_t n_in, size_t k_cols, const int8_t *codes, const int64_t *scales,
+                  int threads, int64_t *out, apx_err *err) {
+  size_t nb = (n_in + ACT_QK - 1) / ACT_QK;
+  clear(err);
+  for (size_t c = 0; c < k_cols; c++) {
+    int fast = 0;
+    int p = plan(t, n_in, codes + c * n_in, n_in, scales + c * nb, nb, &fast);
+    if (p != 0 || !fast)
+      return apxo_matmat_q8act(t, raw, raw_len, n_out, n_in, k_cols, codes, n_in, scales,
+                               out, err);
+  }
+  size_t row_bytes;
+  int rc = row_geometry(t, n_out, n_in, raw_len, &row_bytes, err);
+  if (rc) return rc;
+  if (threads < 1) threads = 1;
+  if ((size_t)threads > n_out) threads = n_out ? (int)n_out : 1;
+  mt_task *tasks = (mt_task *)calloc((size_t)threads, sizeof(mt_task));
+  pthread_t *tid = (pthread_t *)calloc((size_t)threads, sizeof(pthread_t));
+  size_t per = (n_out + (size_t)threads - 1) / (size_t)threads;
+  for (int i = 0; i < threads; i++) {
+    size_t lo = (size_t)i * per, hi = lo + per < n_out ? lo + per : n_out;
+    if (lo > n_out) lo = n_out;
+    tasks[i] = (mt_task){t, raw, row_bytes, lo, hi, n_in, k_cols, n_out,
+                         codes, scales, out, 0, 0};
+    pthread_create(&tid[i], NULL, mt_run, &tasks[i]);
+  }
+  for (int i = 0; i < threads; i++) pthread_join(tid[i], NULL);
+  rc = 0;
+  for (int i = 0; i < threads && rc == 0; i++) rc = tasks[i].rc;
+  free(tasks);
+  free(tid);
+  if (rc != 0) /* any refusal: the single-threaded contract decides it */
+    return apxo_matmat_q8act(t, raw, raw_len, n_out, n_in, k_cols, codes, n_in, scales,
+                             out, err);
+  return 0;
+}
+
+int apxo_matvec_q8act_mt(uint32_t t, const uint8_t *raw, size_t raw_len, size_t n_out,
+                         size_t n_in, const int8_t *codes, const int64_t *scales,
+                         int threads, int64_t *out, apx_err *err) {
+  return run_mt(t, raw, raw_len, n_out, n_in, 1, codes, scales, threads, out, err);
+}
+
+int apxo_matmat_q8act_mt(uint32_t t, const uint8_t *raw, size_t raw_len, size_t n_out,
+                         size_t n_in, size_t k_cols, const int8_t *codes,
+                         const int64_t *scales, int threads, int64_t *out, apx_err *err) {
+  return run_mt(t, raw, raw_len, n_out, n_in, k_cols, codes, scales, threads, out, err);
+}
