@@ -1,0 +1,106 @@
+"""ctypes binding of ``libapeiron_cuda.so`` (the C ABI of include/apeiron_cuda.h).
+
+The library is built in place by ``apeiron_b200.build``.  There is no fallback: when the
+library is missing or cannot be loaded, importing a projection raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "libapeiron_cuda.so")
+
+APX_OK = 0
+APX_ERR_SHAPE_MISMATCH = 1
+APX_ERR_ROW_LENGTH = 2
+APX_ERR_SHORT_PAYLOAD = 3
+APX_ERR_LENGTH_OVERFLOW = 4
+APX_ERR_UNSUPPORTED_QUANT = 5
+APX_ERR_NONFINITE_SCALE = 6
+APX_ERR_FIXED_OVERFLOW = 7
+APX_ERR_ACCUMULATOR_OVERFLOW = 8
+APX_ERR_OUTPUT_OVERFLOW = 9
+APX_ERR_QUANT_REFUSED = 10
+APX_ERR_INVALID_ARGUMENT = 20
+APX_ERR_LAYOUT_MISMATCH = 21
+APX_ERR_CUDA = 22
+APX_ERR_OUT_OF_MEMORY = 23
+APX_ERR_TOO_LARGE = 24
+
+Q8_0, Q4_K, Q6_K = 8, 12, 14
+EXP_ZERO = 0xFF
+
+# Every symbol the header declares (tests/test_abi.py checks the library exports them).
+EXPORTS = [
+    "apx_open", "apx_close", "apx_version", "apx_tensor_upload", "apx_tensor_free",
+    "apx_tensor_device_bytes", "apx_matvec_q8act", "apx_matvec_q8act_chunked",
+    "apx_matmat_q8act", "apx_quant_act", "apx_matvec_f32", "apx_debug_block_dots",
+    "apx_act_describe_async", "apx_quant_q32_async", "apx_quant_f32_async",
+    "apx_matvec_async", "apx_matmat_async", "apx_act_padded_len", "apx_status_decode",
+]
+
+
+class ApxErr(C.Structure):
+    _fields_ = [
+        ("code", C.c_int32),
+        ("ggml_type", C.c_uint32),
+        ("a", C.c_uint64),
+        ("b", C.c_uint64),
+        ("row", C.c_uint64),
+        ("col", C.c_uint64),
+        ("bits", C.c_uint32),
+        ("cuda_error", C.c_int32),
+    ]
+
+
+class CallStatus(C.Structure):
+    _fields_ = [("first", C.c_uint64), ("spare", C.c_uint64)]
+
+
+P = C.c_void_p
+SZ = C.c_size_t
+U64 = C.c_uint64
+EP = C.POINTER(ApxErr)
+
+_SIGS = {
+    "apx_open": (P, [C.c_int, EP]),
+    "apx_close": (None, [P]),
+    "apx_version": (C.c_char_p, []),
+    "apx_tensor_upload": (C.c_int, [P, C.c_uint32, P, SZ, SZ, SZ, C.POINTER(U64), EP]),
+    "apx_tensor_free": (C.c_int, [P, U64]),
+    "apx_tensor_device_bytes": (SZ, [P, U64]),
+    "apx_matvec_q8act": (C.c_int, [P, U64, SZ, SZ, P, SZ, P, P, EP]),
+    "apx_matvec_q8act_chunked": (C.c_int, [P, U64, SZ, SZ, P, SZ, P, SZ, P, EP]),
+    "apx_matmat_q8act": (C.c_int, [P, U64, SZ, SZ, SZ, P, SZ, P, P, EP]),
+    "apx_quant_act": (C.c_int, [P, P, SZ, P, P, EP]),
+    "apx_matvec_f32": (C.c_int, [P, U64, SZ, SZ, P, P, EP]),
+    "apx_debug_block_dots": (C.c_int, [P, U64, SZ, SZ, P, P, EP]),
+    "apx_act_describe_async": (C.c_int, [P, P, P, SZ, P, P]),
+    "apx_quant_q32_async": (C.c_int, [P, P, SZ, P, P, P, P]),
+    "apx_quant_f32_async": (C.c_int, [P, P, SZ, P, P, P, P]),
+    "apx_matvec_async": (C.c_int, [P, U64, SZ, SZ, P, P, P, P, P, P, P]),
+    "apx_matmat_async": (C.c_int, [P, U64, SZ, SZ, SZ, P, P, P, P, P, P, P]),
+    "apx_act_padded_len": (SZ, [SZ]),
+    "apx_status_decode": (C.c_int, [P, U64, C.POINTER(CallStatus), EP]),
+}
+
+_lib = None
+
+
+def load(path: str | None = None):
+    """Load the backend library (once).  Raises OSError when it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = path or LIB_PATH
+    if not os.path.exists(path):
+        raise OSError(f"apeiron_b200: CUDA backend library not built: {path} "
+                      "(run `python -m apeiron_b200.build`)")
+    lib = C.CDLL(path)
+    for name, (res, args) in _SIGS.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib

@@ -1,0 +1,156 @@
+// apx_common.cuh — device helpers shared by the projection kernels.
+//
+// Exact integer arithmetic only: every kernel accumulates the reference's
+// `Σ_b S_b·(w_scale·D − w_min·Σxq)` (src/engine/chart/mod.rs:497-514) as a two's-complement
+// 128-bit integer held in two 64-bit words, and finishes with the reference's single
+// `round_shift_32` (src/engine/num/value.rs:10-12).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#include "../../include/apeiron_cuda.h"
+
+namespace apx {
+
+constexpr int kLanes = 32;       // rows per tile: one row per lane
+constexpr int kActQK = 32;       // activation block (chart/mod.rs:63)
+constexpr int kQK_K = 256;       // k-quant super-block (format/quant.rs:18)
+constexpr uint32_t kQ8_0 = APX_GGML_TYPE_Q8_0;
+constexpr uint32_t kQ4_K = APX_GGML_TYPE_Q4_K;
+constexpr uint32_t kQ6_K = APX_GGML_TYPE_Q6_K;
+
+// Repacked unit sizes (bytes per 32-row tile per unit): the same bytes as 32 rows of the
+// GGUF payload for that unit, regrouped so lane l's 16-byte chunk c sits at (c*32+l)*16.
+constexpr int kQ8Blocks = 4;                       // Q8_0 blocks per unit
+constexpr int kUnitQ8_0 = 32 * kQ8Blocks * 34;     // 4352: codes 4096 + f16 scales 256
+constexpr int kUnitQ4_K = 32 * 144;                // 4608: qs 4096 + headers 512
+constexpr int kUnitQ6_K = 32 * 210;                // 6720: ql|qh 6144 + scales 512 + d 64
+
+// Kinds in the refusal word.
+constexpr unsigned kKindOutputOverflow = APX_ERR_OUTPUT_OVERFLOW;
+constexpr unsigned kKindAccOverflow = APX_ERR_ACCUMULATOR_OVERFLOW;
+
+// Device view of apx_act_desc (include/apeiron_cuda.h): written by the quant / describe
+// kernels or uploaded by the host, read by every projection kernel of the call.
+struct ActDesc {
+  int32_t status;   // APX_OK, APX_ERR_FIXED_OVERFLOW (a product S·xq leaves i64) or
+                    // APX_ERR_QUANT_REFUSED (quant_act returned None)
+  int32_t emin;     // smallest exponent over non-zero scales (0 when all are zero)
+  int32_t emax;     // largest exponent over non-zero scales (-1 when all are zero)
+  int32_t n_in;     // activation length the descriptor was built for
+  uint32_t nz;      // number of non-zero scales
+  uint32_t pad[3];
+};
+static_assert(sizeof(ActDesc) == sizeof(apx_act_desc), "descriptor layout");
+
+// ---- 128-bit two's-complement accumulator ------------------------------------------
+
+struct Acc128 {
+  unsigned long long lo, hi;
+};
+
+__device__ __forceinline__ void acc_zero(Acc128 &a) { a.lo = 0ull; a.hi = 0ull; }
+
+__device__ __forceinline__ void acc_add(Acc128 &a, unsigned long long lo, unsigned long long hi) {
+  asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;"
+      : "+l"(a.lo), "+l"(a.hi)
+      : "l"(lo), "l"(hi));
+}
+
+__device__ __forceinline__ void acc_add(Acc128 &a, const Acc128 &b) { acc_add(a, b.lo, b.hi); }
+
+__device__ __forceinline__ void acc_sub(Acc128 &a, unsigned long long lo, unsigned long long hi) {
+  asm("sub.cc.u64 %0, %0, %2;\n\tsubc.u64 %1, %1, %3;"
+      : "+l"(a.lo), "+l"(a.hi)
+      : "l"(lo), "l"(hi));
+}
+
+// v * 2^s as a 128-bit value, 0 <= s < 128.
+__device__ __forceinline__ void shl128(long long v, unsigned s, unsigned long long &lo,
+                                       unsigned long long &hi) {
+  if (s < 64) {
+    lo = (unsigned long long)v << s;
+    hi = (unsigned long long)((v >> 1) >> (63 - s));
+  } else {
+    lo = 0ull;
+    hi = (unsigned long long)v << (s - 64);
+  }
+}
+
+// a += v * 2^s
+__device__ __forceinline__ void acc_add_shl(Acc128 &a, long long v, unsigned s) {
+  unsigned long long lo, hi;
+  shl128(v, s, lo, hi);
+  acc_add(a, lo, hi);
+}
+
+// a -= v * 2^s
+__device__ __forceinline__ void acc_sub_shl(Acc128 &a, long long v, unsigned s) {
+  unsigned long long lo, hi;
+  shl128(v, s, lo, hi);
+  acc_sub(a, lo, hi);
+}
+
+// round_shift_32 (src/engine/num/value.rs:10-12) and the i64 range check of round_to_i64
+// (src/engine/chart/mod.rs:1746-1753).  Returns false when the result leaves i64.
+__device__ __forceinline__ bool acc_round_to_i64(const Acc128 &a, long long &out) {
+  // v = q*2^32 + r; result = q + [r >= 2^31]; q = v >> 32 (arithmetic, 96 bits).
+  unsigned long long qlo = (a.lo >> 32) | (a.hi << 32);
+  long long qhi = (long long)a.hi >> 32;  // sign-extended top 32 bits of q
+  unsigned long long r = a.lo & 0xFFFFFFFFull;
+  unsigned long long inc = r >= 0x80000000ull ? 1ull : 0ull;
+  unsigned long long lo = qlo + inc;
+  long long hi = qhi + (lo < qlo ? 1 : 0);
+  // fits i64 iff hi equals the sign extension of lo
+  if (hi != ((long long)lo >> 63)) return false;
+  out = (long long)lo;
+  return true;
+}
+
+// ---- f16 scale split (src/engine/kern/pow2.rs:52-64) ---------------------------------
+// finite f16 h = m * 2^k in Q32.32 with |m| <= 2047, k in [8, 37].  A non-finite word
+// (exponent 31) decodes to m = 0: its row is refused from the upload-time scan.
+__device__ __forceinline__ void f16_split(unsigned h, int &m, unsigned &k) {
+  unsigned e = (h >> 10) & 31u;
+  int f = (int)(h & 1023u);
+  int mm = e == 0 ? f : (e == 31 ? 0 : f + 1024);
+  k = e == 0 ? 8u : e + 7u;
+  m = (h & 0x8000u) ? -mm : mm;
+}
+
+__device__ __forceinline__ unsigned long long pack_status(unsigned long long row, unsigned kind,
+                                                          unsigned bits) {
+  return (row << 24) | ((unsigned long long)kind << 16) | (bits & 0xFFFFu);
+}
+
+__device__ __forceinline__ int dp4a_ss(int a, int b, int c) {
+  int d;
+  asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+// unsigned bytes of a times signed bytes of b
+__device__ __forceinline__ int dp4a_us(unsigned a, int b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// Streaming 16-byte load of weight bytes: read once per call, kept out of L1.
+__device__ __forceinline__ uint4 ld_stream(const void *p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ uint2 ld_stream8(const void *p) {
+  uint2 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+               : "=r"(v.x), "=r"(v.y)
+               : "l"(p));
+  return v;
+}
+
+}  // namespace apx

@@ -1,0 +1,45 @@
+// apx_kernels.h — internal launch interface between the C-ABI runtime and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+namespace apx {
+
+struct GemvPlan {
+  int units;       // units per 32-row tile
+  size_t n_rt;     // row tiles
+  int R, P;        // row tiles per CTA, warps per row tile
+  int ksplit;      // CTAs per cluster along K
+  bool pipe;       // warps stream several units with one unit of prefetch
+  unsigned grid;
+  int block;
+  size_t smem;
+};
+
+int units_per_row_tile(uint32_t type, size_t n_in);
+size_t packed_bytes(uint32_t type, size_t n_out, size_t n_in);
+cudaError_t launch_repack(const uint8_t *d_raw, uint8_t *d_pack, uint32_t type, size_t n_out,
+                          size_t n_in, size_t row_bytes, cudaStream_t stream);
+GemvPlan plan_gemv(uint32_t type, size_t n_out, size_t n_in, int sm_count);
+cudaError_t launch_gemv(const GemvPlan &pl, uint32_t type, const uint8_t *pack, size_t n_out,
+                        size_t n_in, const int8_t *codes, const uint8_t *exps, const void *desc,
+                        long long *out_q32, float *out_f32, unsigned long long *status,
+                        cudaStream_t stream);
+
+// Activation kernels (apx_quant.cu).  `cols` activation vectors of width n laid out with
+// stride `ld` codes and `ldb` exponent bytes; one descriptor per column.
+cudaError_t launch_describe(const int8_t *codes, const uint8_t *exps, size_t n, int cols,
+                            size_t ld, size_t ldb, void *desc, cudaStream_t stream);
+cudaError_t launch_quant_q32(const long long *x, size_t n, int8_t *codes, uint8_t *exps,
+                             void *desc, cudaStream_t stream);
+cudaError_t launch_quant_f32(const float *x, size_t n, int8_t *codes, uint8_t *exps, void *desc,
+                             cudaStream_t stream);
+
+// Debug: exact int32 group dots from the repacked layout (apx_quant.cu).
+cudaError_t launch_block_dots(uint32_t type, const uint8_t *pack, size_t n_out, size_t n_in,
+                              const int8_t *codes, int32_t *dots, cudaStream_t stream);
+
+}  // namespace apx

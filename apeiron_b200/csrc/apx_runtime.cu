@@ -1,0 +1,654 @@
+// apx_runtime.cu — the C ABI (include/apeiron_cuda.h): contexts, weight uploads, validation
+// in the reference's order, staging, launches and refusal decoding.
+//
+// Validation order follows the reference exactly:
+//   matvec_q8act (src/engine/chart/mod.rs:1887-1925): plan first (an activation product
+//     S·xq outside i64 refuses with Dequant(FixedOverflow)), then ShapeMismatch,
+//     LengthOverflow, ShortPayload, then the rows;
+//   matvec_q8act_quant_chunked (src/engine/chart/ffn.rs:667-745): with more than one chunk,
+//     LengthOverflow and ShortPayload, then ShapeMismatch, then the plan;
+//   matmat_q8act (src/engine/kern/matmat.rs:92-134): the lowest refusing column.
+// Row refusals: the first row in row order wins (ffn.rs:659-661); a row whose block scale
+// is Inf/NaN refuses with that scale's bits (num/dequant.rs:25-42), found once at upload.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+#include <vector>
+
+#include "apx_common.cuh"
+#include "apx_kernels.h"
+
+using namespace apx;
+
+namespace {
+
+struct Tensor {
+  uint32_t type = 0;
+  size_t n_out = 0, n_in = 0, raw_len = 0, row_bytes = 0;
+  uint8_t *d_pack = nullptr;
+  size_t pack_bytes = 0;
+  size_t nonfinite_row = SIZE_MAX;  // first row holding an Inf/NaN block scale
+  uint16_t nonfinite_bits = 0;
+  GemvPlan plan{};
+};
+
+struct DevBuf {
+  void *p = nullptr;
+  size_t cap = 0;
+  cudaError_t ensure(size_t n) {
+    if (n <= cap) return cudaSuccess;
+    if (p) cudaFree(p);
+    p = nullptr;
+    cap = 0;
+    size_t want = std::max(n, (size_t)1 << 16);
+    cudaError_t e = cudaMalloc(&p, want);
+    if (e == cudaSuccess) cap = want;
+    return e;
+  }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    cap = 0;
+  }
+};
+
+struct HostBuf {
+  void *p = nullptr;
+  size_t cap = 0;
+  cudaError_t ensure(size_t n) {
+    if (n <= cap) return cudaSuccess;
+    if (p) cudaFreeHost(p);
+    p = nullptr;
+    cap = 0;
+    size_t want = std::max(n, (size_t)1 << 16);
+    cudaError_t e = cudaHostAlloc(&p, want, cudaHostAllocDefault);
+    if (e == cudaSuccess) cap = want;
+    return e;
+  }
+  void release() {
+    if (p) cudaFreeHost(p);
+    p = nullptr;
+    cap = 0;
+  }
+};
+
+size_t align16(size_t n) { return (n + 15) & ~(size_t)15; }
+
+bool geom(uint32_t t, size_t &qk, size_t &bb) {
+  switch (t) {
+    case APX_GGML_TYPE_Q8_0: qk = 32; bb = 34; return true;
+    case APX_GGML_TYPE_Q4_K: qk = 256; bb = 144; return true;
+    case APX_GGML_TYPE_Q6_K: qk = 256; bb = 210; return true;
+    default: return false;
+  }
+}
+
+int set_err(apx_err *err, int code) {
+  if (err) {
+    std::memset(err, 0, sizeof *err);
+    err->code = code;
+  }
+  return code;
+}
+
+int cuda_err(apx_err *err, cudaError_t e) {
+  set_err(err, APX_ERR_CUDA);
+  if (err) err->cuda_error = (int32_t)e;
+  return APX_ERR_CUDA;
+}
+
+}  // namespace
+
+struct apx_ctx {
+  int device = 0;
+  int sm_count = 148;
+  cudaStream_t stream = nullptr;
+  std::mutex mu;
+  std::unordered_map<uint64_t, Tensor> tensors;
+  uint64_t next = 1;
+  DevBuf dev;      // [out | status | desc | exps | codes] of the synchronous calls
+  DevBuf scratch;  // device-side quantization scratch of the f32 path
+  HostBuf host;    // pinned mirror of `dev`
+};
+
+namespace {
+
+// Refusal of an activation that has no Q32.32 image (QuantAct::magnitude's NoQ32 case,
+// chart/mod.rs:159-181), plus the descriptor the kernels read.
+struct HostAct {
+  int status = APX_OK;
+  ActDesc desc{};
+};
+
+HostAct describe_host(const int8_t *codes, size_t q_len, const uint8_t *exps) {
+  HostAct h;
+  int emin = 1 << 30, emax = -1;
+  unsigned nz = 0, m128 = 0;
+  const size_t nb = (q_len + 31) / 32;
+  for (size_t b = 0; b < nb; b++) {
+    unsigned e = exps[b];
+    if (e == APX_EXP_ZERO) continue;
+    if (e > 62) {
+      h.status = APX_ERR_INVALID_ARGUMENT;
+      continue;
+    }
+    size_t end = std::min(q_len, b * 32 + 32);
+    for (size_t j = b * 32; j < end; j++) {
+      int c = codes[j];
+      if (c == -128) m128 = 1;
+      if (e >= 57) {
+        long long lim = 1ll << (63 - e);
+        if (c < -lim || c > lim - 1) {
+          if (h.status == APX_OK) h.status = APX_ERR_FIXED_OVERFLOW;
+        }
+      }
+    }
+    emin = std::min(emin, (int)e);
+    emax = std::max(emax, (int)e);
+    nz++;
+  }
+  h.desc.status = h.status;
+  h.desc.emin = emax >= 0 ? emin : 0;
+  h.desc.emax = emax;
+  h.desc.n_in = (int32_t)q_len;
+  h.desc.nz = nz;
+  h.desc.pad[0] = m128;
+  return h;
+}
+
+// ShapeMismatch / LengthOverflow / ShortPayload / layout checks of one call.
+int check_geometry(const Tensor &t, size_t n_out, size_t n_in, size_t q_len, bool chunked_order,
+                   apx_err *err) {
+  size_t qk, bb, row_bytes, need;
+  geom(t.type, qk, bb);
+  auto shape = [&]() {
+    set_err(err, APX_ERR_SHAPE_MISMATCH);
+    if (err) {
+      err->a = q_len;
+      err->b = n_in;
+    }
+    return APX_ERR_SHAPE_MISMATCH;
+  };
+  if (!chunked_order && q_len != n_in) return shape();
+  if (__builtin_mul_overflow((n_in + qk - 1) / qk, bb, &row_bytes) ||
+      __builtin_mul_overflow(n_out, row_bytes, &need))
+    return set_err(err, APX_ERR_LENGTH_OVERFLOW);
+  if (t.raw_len < need) {
+    set_err(err, APX_ERR_SHORT_PAYLOAD);
+    if (err) {
+      err->a = need;
+      err->b = t.raw_len;
+    }
+    return APX_ERR_SHORT_PAYLOAD;
+  }
+  if (chunked_order && q_len != n_in) return shape();
+  if (n_in != t.n_in || n_out > t.n_out) return set_err(err, APX_ERR_LAYOUT_MISMATCH);
+  return APX_OK;
+}
+
+bool is_activation_kind(unsigned kind) {
+  return kind == APX_ERR_FIXED_OVERFLOW || kind == APX_ERR_QUANT_REFUSED ||
+         kind == APX_ERR_INVALID_ARGUMENT;
+}
+
+// Merge the kernel's refusal word with the upload-time non-finite finding.
+int decode_status(const Tensor &t, size_t n_out, unsigned long long word, apx_err *err) {
+  unsigned kind = (unsigned)((word >> 16) & 0xFF);
+  size_t krow = word == ~0ull ? SIZE_MAX : (size_t)(word >> 24);
+  if (word != ~0ull && is_activation_kind(kind)) return set_err(err, (int)kind);
+  size_t nrow = t.nonfinite_row < n_out ? t.nonfinite_row : SIZE_MAX;
+  if (nrow == SIZE_MAX && krow == SIZE_MAX) return set_err(err, APX_OK);
+  if (nrow <= krow) {
+    set_err(err, APX_ERR_NONFINITE_SCALE);
+    if (err) {
+      err->bits = t.nonfinite_bits;
+      err->row = nrow;
+    }
+    return APX_ERR_NONFINITE_SCALE;
+  }
+  set_err(err, (int)kind);
+  if (err) err->row = krow;
+  return (int)kind;
+}
+
+Tensor *find(apx_ctx *ctx, uint64_t h) {
+  auto it = ctx->tensors.find(h);
+  return it == ctx->tensors.end() ? nullptr : &it->second;
+}
+
+uint16_t rd16(const uint8_t *p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+bool nonfinite(uint16_t h) { return ((h >> 10) & 0x1F) == 0x1F; }
+
+// First Inf/NaN block scale in row order, in each row's dequantization order
+// (num/dequant.rs: Q8_0 d per block; Q4_K d then dmin per super-block; Q6_K d).
+void scan_nonfinite(Tensor &t, const uint8_t *raw) {
+  size_t qk, bb;
+  geom(t.type, qk, bb);
+  const size_t blocks = (t.n_in + qk - 1) / qk;
+  for (size_t r = 0; r < t.n_out; r++) {
+    const uint8_t *row = raw + r * t.row_bytes;
+    for (size_t b = 0; b < blocks; b++) {
+      const uint8_t *blk = row + b * bb;
+      uint16_t cand[2];
+      int nc = 0;
+      if (t.type == APX_GGML_TYPE_Q8_0) {
+        cand[nc++] = rd16(blk);
+      } else if (t.type == APX_GGML_TYPE_Q4_K) {
+        cand[nc++] = rd16(blk);
+        cand[nc++] = rd16(blk + 2);
+      } else {
+        cand[nc++] = rd16(blk + 208);
+      }
+      for (int i = 0; i < nc; i++) {
+        if (nonfinite(cand[i])) {
+          t.nonfinite_row = r;
+          t.nonfinite_bits = cand[i];
+          return;
+        }
+      }
+    }
+  }
+}
+
+// Synchronous single-column projection of host activations.
+int matvec_sync(apx_ctx *ctx, Tensor &t, size_t n_out, size_t n_in, const int8_t *codes,
+                size_t q_len, const uint8_t *exps, int64_t *out, apx_err *err) {
+  HostAct ha = describe_host(codes, q_len, exps);
+  const size_t nb = (q_len + 31) / 32;
+  const size_t out_sz = align16(n_out * 8);
+  const size_t head = 16 + 32;  // status + desc
+  const size_t exps_sz = align16(nb), codes_sz = align16(q_len);
+  const size_t in_sz = head + exps_sz + codes_sz;
+  cudaError_t e;
+  if ((e = ctx->dev.ensure(out_sz + in_sz)) != cudaSuccess) return cuda_err(err, e);
+  if ((e = ctx->host.ensure(out_sz + in_sz)) != cudaSuccess) return cuda_err(err, e);
+  uint8_t *h = (uint8_t *)ctx->host.p, *d = (uint8_t *)ctx->dev.p;
+  std::memset(h + out_sz, 0xFF, 16);
+  std::memcpy(h + out_sz + 16, &ha.desc, sizeof(ActDesc));
+  std::memcpy(h + out_sz + head, exps, nb);
+  std::memcpy(h + out_sz + head + exps_sz, codes, q_len);
+  if ((e = cudaMemcpyAsync(d + out_sz, h + out_sz, in_sz, cudaMemcpyHostToDevice,
+                           ctx->stream)) != cudaSuccess)
+    return cuda_err(err, e);
+  if ((e = launch_gemv(t.plan, t.type, t.d_pack, n_out, n_in,
+                       (const int8_t *)(d + out_sz + head + exps_sz), d + out_sz + head,
+                       d + out_sz + 16, (long long *)d, nullptr,
+                       (unsigned long long *)(d + out_sz), ctx->stream)) != cudaSuccess)
+    return cuda_err(err, e);
+  if ((e = cudaMemcpyAsync(h, d, out_sz + 16, cudaMemcpyDeviceToHost, ctx->stream)) !=
+      cudaSuccess)
+    return cuda_err(err, e);
+  if ((e = cudaStreamSynchronize(ctx->stream)) != cudaSuccess) return cuda_err(err, e);
+  unsigned long long word;
+  std::memcpy(&word, h + out_sz, 8);
+  int rc = decode_status(t, n_out, word, err);
+  if (rc == APX_OK && n_out) std::memcpy(out, h, n_out * 8);
+  return rc;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *apx_version(void) { return "apeiron_b200 0.1 (sm_100a)"; }
+
+apx_ctx *apx_open(int device, apx_err *err) {
+  set_err(err, APX_OK);
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || device < 0 || device >= n) {
+    set_err(err, e != cudaSuccess ? APX_ERR_CUDA : APX_ERR_INVALID_ARGUMENT);
+    if (err) err->cuda_error = (int32_t)e;
+    return nullptr;
+  }
+  if ((e = cudaSetDevice(device)) != cudaSuccess) {
+    cuda_err(err, e);
+    return nullptr;
+  }
+  apx_ctx *ctx = new apx_ctx();
+  ctx->device = device;
+  cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device);
+  if ((e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking)) != cudaSuccess) {
+    delete ctx;
+    cuda_err(err, e);
+    return nullptr;
+  }
+  return ctx;
+}
+
+void apx_close(apx_ctx *ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  for (auto &kv : ctx->tensors) cudaFree(kv.second.d_pack);
+  ctx->dev.release();
+  ctx->scratch.release();
+  ctx->host.release();
+  cudaStreamDestroy(ctx->stream);
+  delete ctx;
+}
+
+int apx_tensor_upload(apx_ctx *ctx, uint32_t ggml_type, const uint8_t *raw, size_t raw_len,
+                      size_t n_out, size_t n_in, uint64_t *handle, apx_err *err) {
+  if (!ctx || !handle || (!raw && raw_len)) return set_err(err, APX_ERR_INVALID_ARGUMENT);
+  std::lock_guard<std::mutex> g(ctx->mu);
+  cudaSetDevice(ctx->device);
+  size_t qk, bb, row_bytes, need;
+  if (!geom(ggml_type, qk, bb)) {
+    set_err(err, APX_ERR_UNSUPPORTED_QUANT);
+    if (err) err->ggml_type = ggml_type;
+    return APX_ERR_UNSUPPORTED_QUANT;
+  }
+  if (__builtin_mul_overflow((n_in + qk - 1) / qk, bb, &row_bytes) ||
+      __builtin_mul_overflow(n_out, row_bytes, &need))
+    return set_err(err, APX_ERR_LENGTH_OVERFLOW);
+  if (raw_len < need) {
+    set_err(err, APX_ERR_SHORT_PAYLOAD);
+    if (err) {
+      err->a = need;
+      err->b = raw_len;
+    }
+    return APX_ERR_SHORT_PAYLOAD;
+  }
+  if (n_in > ((size_t)1 << 28) || n_out > ((size_t)1 << 36))
+    return set_err(err, APX_ERR_TOO_LARGE);
+  Tensor t;
+  t.type = ggml_type;
+  t.n_out = n_out;
+  t.n_in = n_in;
+  t.raw_len = raw_len;
+  t.row_bytes = row_bytes;
+  scan_nonfinite(t, raw);
+  t.plan = plan_gemv(ggml_type, n_out, n_in, ctx->sm_count);
+  t.pack_bytes = packed_bytes(ggml_type, n_out, n_in);
+  cudaError_t e;
+  uint8_t *d_raw = nullptr;
+  if (t.pack_bytes) {
+    if ((e = cudaMalloc(&t.d_pack, t.pack_bytes)) != cudaSuccess) {
+      set_err(err, APX_ERR_OUT_OF_MEMORY);
+      if (err) err->cuda_error = (int32_t)e;
+      return APX_ERR_OUT_OF_MEMORY;
+    }
+    if ((e = cudaMalloc(&d_raw, std::max(need, (size_t)1))) != cudaSuccess) {
+      cudaFree(t.d_pack);
+      set_err(err, APX_ERR_OUT_OF_MEMORY);
+      if (err) err->cuda_error = (int32_t)e;
+      return APX_ERR_OUT_OF_MEMORY;
+    }
+    e = cudaMemcpyAsync(d_raw, raw, need, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess)
+      e = launch_repack(d_raw, t.d_pack, ggml_type, n_out, n_in, row_bytes, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    cudaFree(d_raw);
+    if (e != cudaSuccess) {
+      cudaFree(t.d_pack);
+      return cuda_err(err, e);
+    }
+  }
+  uint64_t h = ctx->next++;
+  ctx->tensors[h] = t;
+  *handle = h;
+  return set_err(err, APX_OK);
+}
+
+int apx_tensor_free(apx_ctx *ctx, uint64_t handle) {
+  if (!ctx) return APX_ERR_INVALID_ARGUMENT;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  Tensor *t = find(ctx, handle);
+  if (!t) return APX_ERR_INVALID_ARGUMENT;
+  cudaSetDevice(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  cudaFree(t->d_pack);
+  ctx->tensors.erase(handle);
+  return APX_OK;
+}
+
+size_t apx_tensor_device_bytes(apx_ctx *ctx, uint64_t handle) {
+  if (!ctx) return 0;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  Tensor *t = find(ctx, handle);
+  return t ? t->pack_bytes : 0;
+}
+
+int apx_matvec_q8act(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
+                     const int8_t *codes, size_t q_len, const uint8_t *exps, int64_t *out,
+                     apx_err *err) {
+  if (!ctx || (!codes && q_len) || (!exps && q_len) || (!out && n_out))
+    return set_err(err, APX_ERR_INVALID_ARGUMENT);
+  std::lock_guard<std::mutex> g(ctx->mu);
+  Tensor *t = find(ctx, tensor);
+  if (!t) return set_err(err, APX_ERR_INVALID_ARGUMENT);
+  cudaSetDevice(ctx->device);
+  HostAct ha = describe_host(codes, q_len, exps);  // the plan runs first (chart/mod.rs:1893)
+  if (ha.status != APX_OK) return set_err(err, ha.status);
+  int rc = check_geometry(*t, n_out, n_in, q_len, false, err);
+  if (rc != APX_OK) return rc;
+  return matvec_sync(ctx, *t, n_out, n_in, codes, q_len, exps, out, err);
+}
+
+int apx_matvec_q8act_chunked(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
+                             const int8_t *codes, size_t q_len, const uint8_t *exps,
+                             size_t chunks, int64_t *out, apx_err *err) {
+  size_t upper = n_out == 0 ? 1 : n_out;
+  size_t actual = std::min(std::max(std::min(chunks, (size_t)8), (size_t)1), upper);
+  if (actual == 1)
+    return apx_matvec_q8act(ctx, tensor, n_out, n_in, codes, q_len, exps, out, err);
+  if (!ctx || (!codes && q_len) || (!exps && q_len) || (!out && n_out))
+    return set_err(err, APX_ERR_INVALID_ARGUMENT);
+  std::lock_guard<std::mutex> g(ctx->mu);
+  Tensor *t = find(ctx, tensor);
+  if (!t) return set_err(err, APX_ERR_INVALID_ARGUMENT);
+  cudaSetDevice(ctx->device);
+  int rc = check_geometry(*t, n_out, n_in, q_len, true, err);
+  if (rc != APX_OK) return rc;
+  HostAct ha = describe_host(codes, q_len, exps);
+  if (ha.status != APX_OK) return set_err(err, ha.status);
+  return matvec_sync(ctx, *t, n_out, n_in, codes, q_len, exps, out, err);
+}
+
+int apx_matmat_q8act(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in, size_t k_cols,
+                     const int8_t *codes, size_t q_len, const uint8_t *exps, int64_t *out,
+                     apx_err *err) {
+  if (!ctx || (k_cols && ((!codes && q_len) || (!exps && q_len) || (!out && n_out))))
+    return set_err(err, APX_ERR_INVALID_ARGUMENT);
+  std::lock_guard<std::mutex> g(ctx->mu);
+  Tensor *t = find(ctx, tensor);
+  if (!t) return set_err(err, APX_ERR_INVALID_ARGUMENT);
+  cudaSetDevice(ctx->device);
+  const size_t nb = (q_len + 31) / 32;
+  for (size_t c = 0; c < k_cols; c++) {
+    HostAct ha = describe_host(codes + c * q_len, q_len, exps + c * nb);
+    int rc = ha.status;
+    if (rc == APX_OK) rc = check_geometry(*t, n_out, n_in, q_len, false, err);
+    else set_err(err, rc);
+    if (rc == APX_OK)
+      rc = matvec_sync(ctx, *t, n_out, n_in, codes + c * q_len, q_len, exps + c * nb,
+                       out + c * n_out, err);
+    if (rc != APX_OK) {
+      if (err) err->col = c;
+      return rc;
+    }
+  }
+  return set_err(err, APX_OK);
+}
+
+int apx_quant_act(apx_ctx *ctx, const int64_t *x, size_t n, int8_t *codes, uint8_t *exps,
+                  apx_err *err) {
+  if (!ctx || (n && (!x || !codes || !exps))) return set_err(err, APX_ERR_INVALID_ARGUMENT);
+  std::lock_guard<std::mutex> g(ctx->mu);
+  cudaSetDevice(ctx->device);
+  const size_t nb = (n + 31) / 32;
+  const size_t x_sz = align16(n * 8), c_sz = align16(n), e_sz = align16(nb), d_sz = 32;
+  cudaError_t e;
+  if ((e = ctx->dev.ensure(x_sz + c_sz + e_sz + d_sz)) != cudaSuccess) return cuda_err(err, e);
+  if ((e = ctx->host.ensure(x_sz + c_sz + e_sz + d_sz)) != cudaSuccess) return cuda_err(err, e);
+  uint8_t *h = (uint8_t *)ctx->host.p, *d = (uint8_t *)ctx->dev.p;
+  std::memcpy(h, x, n * 8);
+  e = cudaMemcpyAsync(d, h, n * 8, cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess)
+    e = launch_quant_q32((const long long *)d, n, (int8_t *)(d + x_sz), d + x_sz + c_sz,
+                         d + x_sz + c_sz + e_sz, ctx->stream);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(h + x_sz, d + x_sz, c_sz + e_sz + d_sz, cudaMemcpyDeviceToHost,
+                        ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return cuda_err(err, e);
+  ActDesc desc;
+  std::memcpy(&desc, h + x_sz + c_sz + e_sz, sizeof desc);
+  if (desc.status != APX_OK) return set_err(err, desc.status);
+  std::memcpy(codes, h + x_sz, n);
+  std::memcpy(exps, h + x_sz + c_sz, nb);
+  return set_err(err, APX_OK);
+}
+
+int apx_matvec_f32(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in, const float *x,
+                   float *y, apx_err *err) {
+  if (!ctx || (n_in && !x) || (n_out && !y)) return set_err(err, APX_ERR_INVALID_ARGUMENT);
+  std::lock_guard<std::mutex> g(ctx->mu);
+  Tensor *t = find(ctx, tensor);
+  if (!t) return set_err(err, APX_ERR_INVALID_ARGUMENT);
+  cudaSetDevice(ctx->device);
+  int rc = check_geometry(*t, n_out, n_in, n_in, false, err);
+  if (rc != APX_OK) return rc;
+  const size_t nb = (n_in + 31) / 32;
+  const size_t out_sz = align16(n_out * 4), x_sz = align16(n_in * 4);
+  const size_t c_sz = align16(n_in), e_sz = align16(nb);
+  cudaError_t e;
+  if ((e = ctx->dev.ensure(out_sz + 16 + x_sz)) != cudaSuccess) return cuda_err(err, e);
+  if ((e = ctx->host.ensure(out_sz + 16 + x_sz)) != cudaSuccess) return cuda_err(err, e);
+  if ((e = ctx->scratch.ensure(32 + e_sz + c_sz)) != cudaSuccess) return cuda_err(err, e);
+  uint8_t *h = (uint8_t *)ctx->host.p, *d = (uint8_t *)ctx->dev.p;
+  uint8_t *s = (uint8_t *)ctx->scratch.p;
+  std::memset(h + out_sz, 0xFF, 16);
+  std::memcpy(h + out_sz + 16, x, n_in * 4);
+  e = cudaMemcpyAsync(d + out_sz, h + out_sz, 16 + n_in * 4, cudaMemcpyHostToDevice,
+                      ctx->stream);
+  if (e == cudaSuccess)
+    e = launch_quant_f32((const float *)(d + out_sz + 16), n_in, (int8_t *)(s + 32 + e_sz),
+                         s + 32, s, ctx->stream);
+  if (e == cudaSuccess)
+    e = launch_gemv(t->plan, t->type, t->d_pack, n_out, n_in, (const int8_t *)(s + 32 + e_sz),
+                    s + 32, s, nullptr, (float *)d, (unsigned long long *)(d + out_sz),
+                    ctx->stream);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(h, d, out_sz + 16, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return cuda_err(err, e);
+  unsigned long long word;
+  std::memcpy(&word, h + out_sz, 8);
+  rc = decode_status(*t, n_out, word, err);
+  if (rc == APX_OK && n_out) std::memcpy(y, h, n_out * 4);
+  return rc;
+}
+
+int apx_debug_block_dots(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
+                         const int8_t *codes, int32_t *dots, apx_err *err) {
+  if (!ctx || !codes || !dots) return set_err(err, APX_ERR_INVALID_ARGUMENT);
+  std::lock_guard<std::mutex> g(ctx->mu);
+  Tensor *t = find(ctx, tensor);
+  if (!t || n_in != t->n_in || n_out > t->n_out) return set_err(err, APX_ERR_INVALID_ARGUMENT);
+  cudaSetDevice(ctx->device);
+  const int units = units_per_row_tile(t->type, n_in);
+  const size_t span = t->type == APX_GGML_TYPE_Q8_0 ? 128 : 256;
+  const size_t padded = units * span;
+  const size_t per_row = t->type == APX_GGML_TYPE_Q8_0 ? (n_in + 31) / 32
+                                                       : (size_t)units * (t->type == APX_GGML_TYPE_Q6_K ? 16 : 8);
+  const size_t c_sz = align16(padded), d_sz = n_out * per_row * 4;
+  cudaError_t e;
+  if ((e = ctx->dev.ensure(c_sz + d_sz)) != cudaSuccess) return cuda_err(err, e);
+  if ((e = ctx->host.ensure(c_sz + d_sz)) != cudaSuccess) return cuda_err(err, e);
+  uint8_t *h = (uint8_t *)ctx->host.p, *d = (uint8_t *)ctx->dev.p;
+  std::memset(h, 0, c_sz);
+  std::memcpy(h, codes, n_in);
+  e = cudaMemcpyAsync(d, h, c_sz, cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess)
+    e = launch_block_dots(t->type, t->d_pack, n_out, n_in, (const int8_t *)d,
+                          (int32_t *)(d + c_sz), ctx->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(h + c_sz, d + c_sz, d_sz, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return cuda_err(err, e);
+  std::memcpy(dots, h + c_sz, d_sz);
+  return set_err(err, APX_OK);
+}
+
+// ---- asynchronous device-buffer entry points ------------------------------------------------
+
+size_t apx_act_padded_len(size_t n_in) { return (n_in + 255) / 256 * 256; }
+
+int apx_act_describe_async(apx_ctx *ctx, const int8_t *d_codes, const uint8_t *d_exps,
+                           size_t n_in, apx_act_desc *d_desc, void *stream) {
+  if (!ctx || !d_desc) return APX_ERR_INVALID_ARGUMENT;
+  cudaError_t e = launch_describe(d_codes, d_exps, n_in, 1, 0, 0, d_desc, (cudaStream_t)stream);
+  return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
+}
+
+int apx_quant_q32_async(apx_ctx *ctx, const int64_t *d_x, size_t n, int8_t *d_codes,
+                        uint8_t *d_exps, apx_act_desc *d_desc, void *stream) {
+  if (!ctx || !d_desc) return APX_ERR_INVALID_ARGUMENT;
+  cudaError_t e = launch_quant_q32((const long long *)d_x, n, d_codes, d_exps, d_desc,
+                                   (cudaStream_t)stream);
+  return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
+}
+
+int apx_quant_f32_async(apx_ctx *ctx, const float *d_x, size_t n, int8_t *d_codes,
+                        uint8_t *d_exps, apx_act_desc *d_desc, void *stream) {
+  if (!ctx || !d_desc) return APX_ERR_INVALID_ARGUMENT;
+  cudaError_t e = launch_quant_f32(d_x, n, d_codes, d_exps, d_desc, (cudaStream_t)stream);
+  return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
+}
+
+int apx_matvec_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
+                     const int8_t *d_codes, const uint8_t *d_exps, const apx_act_desc *d_desc,
+                     int64_t *d_out_q32, float *d_out_f32, apx_call_status *d_status,
+                     void *stream) {
+  if (!ctx || !d_desc || !d_status) return APX_ERR_INVALID_ARGUMENT;
+  Tensor *t;
+  {
+    std::lock_guard<std::mutex> g(ctx->mu);
+    t = find(ctx, tensor);
+  }
+  if (!t || n_in != t->n_in || n_out > t->n_out) return APX_ERR_LAYOUT_MISMATCH;
+  cudaError_t e = launch_gemv(t->plan, t->type, t->d_pack, n_out, n_in, d_codes, d_exps, d_desc,
+                              (long long *)d_out_q32, d_out_f32,
+                              (unsigned long long *)&d_status->first, (cudaStream_t)stream);
+  return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
+}
+
+int apx_matmat_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in, size_t k_cols,
+                     const int8_t *d_codes, const uint8_t *d_exps, const apx_act_desc *d_descs,
+                     int64_t *d_out_q32, float *d_out_f32, apx_call_status *d_status,
+                     void *stream) {
+  if (!ctx || !d_descs || !d_status) return APX_ERR_INVALID_ARGUMENT;
+  Tensor *t;
+  {
+    std::lock_guard<std::mutex> g(ctx->mu);
+    t = find(ctx, tensor);
+  }
+  if (!t || n_in != t->n_in || n_out > t->n_out) return APX_ERR_LAYOUT_MISMATCH;
+  const size_t ld = apx_act_padded_len(n_in), ldb = ld / 32;
+  for (size_t c = 0; c < k_cols; c++) {
+    cudaError_t e = launch_gemv(t->plan, t->type, t->d_pack, n_out, n_in, d_codes + c * ld,
+                                d_exps + c * ldb, d_descs + c,
+                                d_out_q32 ? (long long *)d_out_q32 + c * n_out : nullptr,
+                                d_out_f32 ? d_out_f32 + c * n_out : nullptr,
+                                (unsigned long long *)&d_status[c].first, (cudaStream_t)stream);
+    if (e != cudaSuccess) return APX_ERR_CUDA;
+  }
+  return APX_OK;
+}
+
+int apx_status_decode(apx_ctx *ctx, uint64_t tensor, const apx_call_status *status,
+                      apx_err *err) {
+  if (!ctx || !status) return set_err(err, APX_ERR_INVALID_ARGUMENT);
+  std::lock_guard<std::mutex> g(ctx->mu);
+  Tensor *t = find(ctx, tensor);
+  if (!t) return set_err(err, APX_ERR_INVALID_ARGUMENT);
+  return decode_status(*t, t->n_out, status->first, err);
+}
+
+}  // extern "C"

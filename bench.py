@@ -1,0 +1,412 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 Q8-activation projection backend (one JSON line on rank 0).
+
+Default workload: the Q4_K decode GEMVs of a Qwen2.5-1.5B FFN,
+W 8960x1536 and W 1536x8960, exact Q32.32 outputs (`matvec_q8act`), batch 1.  One step
+is both projections over one activation each.  Weights rotate over enough device copies
+that every step streams them from HBM (copies > 3x the 126 MB L2), the reference's own
+bench does the same with 256 MB of cycled copies (src/engine/chart/tests.rs:884-887).
+
+  value  — algorithmic bytes (weights + int8 codes + exponents + i64 outputs) per second,
+           device-timed with CUDA events, inputs already resident in HBM;
+  e2e    — the same metric through the public C ABI with host buffers
+           (apx_matvec_q8act: H2D of codes/exponents, D2H of outputs, every step);
+  roofline — the Q4_K GEMV kernel: algorithmic bytes per launch / mean launch time
+           (CUDA events on the launching stream) against the measured HBM copy peak.
+
+`--impl reference` times the CPU restatement of the reference kernel (oracle/, the
+reference is Rust and cannot be built here) on all host threads, same metric.
+Multi-GPU: replicas (independent decode streams per GPU, weak scaling), time = max over
+ranks.  `--config 3` measures the prefill GEMM instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "GEMV HBM GB/s (% of 8 TB/s); pp512 int8 GEMM TOPS (% peak); 1/2/4/8 GPU"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("hbm_gbs", 6650.0), "measured"
+    return 6650.0, "fallback"
+
+
+def gemv_bytes(t, n_out, n_in):
+    from apeiron_b200 import synth
+    qk, bb = synth.GEOM[t]
+    w = n_out * (-(-n_in // qk)) * bb
+    return w + n_in + (-(-n_in // 32)) + 8 * n_out
+
+
+WORKLOADS = {
+    1: ("Q8_0 GEMV 4864x896 (Qwen2.5-0.5B FFN up), configs[0]", [(8, 4864, 896)]),
+    2: ("Q4_K GEMV 8960x1536 + 1536x8960 (Qwen2.5-1.5B FFN), configs[1]",
+        [(12, 8960, 1536), (12, 1536, 8960)]),
+}
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region (clocks, throttle reasons)."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.proc, self.lines = index, None, []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device(f"cuda:{local}"))
+        pg = dist
+    return world, rank, local, pg
+
+
+def max_over_ranks(v, pg, local):
+    if pg is None:
+        return v
+    import torch
+
+    t = torch.tensor([v], dtype=torch.float64, device=f"cuda:{local}")
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(pg, local):
+    if pg is not None:
+        import torch
+
+        pg.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+
+def cpu_data(mats, min_bytes=256 << 20):
+    """Host copies of the workload cycled so every pass streams DRAM, as the reference's
+    bench_pooled_shapes does with 256 MB of copies (src/engine/chart/tests.rs:835-911)."""
+    from apeiron_b200 import synth
+    from oracle import oracle as O
+
+    base = []
+    for t, n_out, n_in in mats:
+        raw = synth.payload(t, n_out, n_in, 17 + n_out)
+        c, e = synth.quant_act_np(synth.f32_to_q32(synth.activation_f32(n_in, 3)))
+        base.append((t, raw, n_out, n_in, c, O.exps_to_scales(e)))
+    per = sum(d[1].size for d in base)
+    copies = max(1, -(-min_bytes // per))
+    return [[(t, raw.copy(), n_out, n_in, c, s) for (t, raw, n_out, n_in, c, s) in base]
+            for _ in range(copies)], copies
+
+
+def cpu_passes(data, max_passes, max_seconds):
+    """Timed passes of the oracle's threaded fused rows (restating the reference's AVX2
+    chunked decode, src/engine/chart/ffn.rs:667-745) on every host thread."""
+    from oracle import oracle as O
+
+    threads = os.cpu_count() or 1
+    total = done = 0
+    t0 = time.perf_counter()
+    while done < max_passes:
+        for t, raw, n_out, n_in, c, s in data[done % len(data)]:
+            r = O.matvec_q8act_mt(t, raw, n_out, n_in, c, s, threads)
+            assert not isinstance(r, tuple)
+            total += gemv_bytes(t, n_out, n_in)
+        done += 1
+        if time.perf_counter() - t0 > max_seconds:
+            break
+    return total, done, time.perf_counter() - t0, threads
+
+
+def cpu_gemv_baseline(mats, seconds=10.0):
+    data, copies = cpu_data(mats)
+    cpu_passes(data, 3, 2.0)
+    total, done, el, threads = cpu_passes(data, 1 << 30, seconds)
+    return {"value": total / el / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{done} passes of the workload over {copies} cycled host copies "
+                      f"(>= 256 MB, streamed from DRAM) in {el:.1f} s"}
+
+
+def run_reference(args, world, rank, local, pg):
+    if rank != 0:
+        return
+    name, mats = WORKLOADS[args.config]
+    data, copies = cpu_data(mats)
+    cpu_passes(data, args.warmup, 10.0)
+    total, done, el, threads = cpu_passes(data, args.steps, 60.0)
+    v = total / el / 1e9
+    sample = (f"{done} of {args.steps} steps (capped at 60 s) over {copies} cycled host "
+              f"copies (>= 256 MB, streamed from DRAM)")
+    line = {"metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": done, "warmup": args.warmup, "ms_per_step": el * 1e3 / max(done, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int64",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": name, "parallelism": f"{threads} host threads"},
+            "cpu_baseline": {"value": v, "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, world, rank, local, pg):
+    import ctypes as C
+
+    import torch
+
+    from apeiron_b200 import _abi, synth
+    from apeiron_b200.chart import Backend, QuantAct
+
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    be = Backend(local)
+    lib = be.lib
+    name, mats = WORKLOADS[args.config]
+    per_step = sum(gemv_bytes(*m) for m in mats)
+    copies = max(4, int(np.ceil(3 * L2_BYTES / sum(
+        synth.GEOM[t][1] * n_out * (-(-n_in // synth.GEOM[t][0])) for t, n_out, n_in in mats))))
+    tensors = []  # [copy][mat]
+    for m, (t, n_out, n_in) in enumerate(mats):
+        raw = synth.payload(t, n_out, n_in, 1000 + m)
+        for c in range(copies):
+            if m == 0:
+                tensors.append([])
+            tensors[c].append(be.upload(t, raw, n_out, n_in))
+    stream = torch.cuda.Stream(device=dev)
+    sp = stream.cuda_stream
+    acts = []
+    for m, (t, n_out, n_in) in enumerate(mats):
+        x = synth.activation_f32(n_in, 50 + m)
+        c, e = synth.quant_act_np(synth.f32_to_q32(x))
+        pad = lib.apx_act_padded_len(n_in)
+        codes = torch.zeros(pad, dtype=torch.int8, device=dev)
+        codes[:n_in] = torch.from_numpy(c).to(dev)
+        exps = torch.full((pad // 32,), 0xFF, dtype=torch.uint8, device=dev)
+        exps[:e.size] = torch.from_numpy(e).to(dev)
+        desc = torch.zeros(8, dtype=torch.int32, device=dev)
+        with torch.cuda.stream(stream):
+            assert lib.apx_act_describe_async(be.ctx, codes.data_ptr(), exps.data_ptr(), n_in,
+                                              desc.data_ptr(), sp) == 0
+        out = torch.zeros(n_out, dtype=torch.int64, device=dev)
+        acts.append((codes, exps, desc, out, c, e))
+    status = torch.full((2,), -1, dtype=torch.int64, device=dev)
+
+    def step(i):
+        for m, (t, n_out, n_in) in enumerate(mats):
+            codes, exps, desc, out, _, _ = acts[m]
+            rc = lib.apx_matvec_async(be.ctx, tensors[i % copies][m].handle, n_out, n_in,
+                                      codes.data_ptr(), exps.data_ptr(), desc.data_ptr(),
+                                      out.data_ptr(), None, status.data_ptr(), sp)
+            assert rc == 0
+
+    # correctness of the timed configuration against the oracle (small, untimed)
+    from oracle import oracle as O
+    for m, (t, n_out, n_in) in enumerate(mats):
+        with torch.cuda.stream(stream):
+            step(0)
+        stream.synchronize()
+        codes, exps, desc, out, c, e = acts[m]
+        raw = synth.payload(t, n_out, n_in, 1000 + m)
+        want = O.matvec_q8act(t, raw, n_out, n_in, c, O.exps_to_scales(e))
+        assert np.array_equal(out.cpu().numpy(), want), "parity failure in bench workload"
+    assert int(status[0].item()) == -1
+
+    # The timed steps are replayed from CUDA graphs (captured once, untimed), so the device
+    # time is the kernels' and not the Python launch loop's.
+    def capture(first, count, only_first=False):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            for i in range(first, first + count):
+                if only_first:
+                    t, n_out, n_in = mats[0]
+                    codes, exps, desc, out, _, _ = acts[0]
+                    assert lib.apx_matvec_async(be.ctx, tensors[i % copies][0].handle, n_out,
+                                                n_in, codes.data_ptr(), exps.data_ptr(),
+                                                desc.data_ptr(), out.data_ptr(), None,
+                                                status.data_ptr(), sp) == 0
+                else:
+                    step(i)
+        return gr
+
+    G = min(args.steps, 1000)
+    g_main = capture(0, G)
+    g_rem = capture(0, args.steps % G) if args.steps % G else None
+    n_k = min(max(args.steps, 64), 1000)
+    g_kernel = capture(0, n_k, only_first=True)
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i)
+        g_main.replay()
+    stream.synchronize()
+    barrier(pg, local)
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.3)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for _ in range(args.steps // G):
+            g_main.replay()
+        if g_rem is not None:
+            g_rem.replay()
+        t1.record(stream)
+    stream.synchronize()
+    barrier(pg, local)
+    ms = t0.elapsed_time(t1)
+    # the dominant kernel alone, n_k back-to-back launches over the rotating copies
+    k0e, k1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        g_kernel.replay()
+        k0e.record(stream)
+        g_kernel.replay()
+        k1e.record(stream)
+    stream.synchronize()
+    kms = k0e.elapsed_time(k1e) / n_k
+    clk = clocks.stop()
+    clk["timed_region_ms"] = ms
+    ms_max = max_over_ranks(ms, pg, local)
+    value = world * per_step * args.steps / (ms_max / 1e3) / 1e9
+    assert int(status[0].item()) == -1
+
+    # e2e through the synchronous C ABI with host buffers
+    qs = [QuantAct.from_exps(a[5], a[4]) for a in acts]
+    for i in range(args.warmup):
+        for m, (t, n_out, n_in) in enumerate(mats):
+            be.matvec_q8act(t, tensors[i % copies][m], n_out, n_in, qs[m])
+    barrier(pg, local)
+    e_steps = min(args.steps, 2000)
+    e0 = time.perf_counter()
+    for i in range(e_steps):
+        for m, (t, n_out, n_in) in enumerate(mats):
+            be.matvec_q8act(t, tensors[(args.warmup + i) % copies][m], n_out, n_in, qs[m])
+    e_s = time.perf_counter() - e0
+    e_s = max_over_ranks(e_s, pg, local)
+    e2e = world * per_step * e_steps / e_s / 1e9
+    h2d = sum(16 + 32 + ((-(-n_in // 32) + 15) // 16) * 16 + ((n_in + 15) // 16) * 16
+              for _, _, n_in in mats)
+    d2h = sum(((8 * n_out + 15) // 16) * 16 + 16 for _, n_out, _ in mats)
+
+    if rank != 0:
+        return
+    hbm, src = peaks()
+    t0m = mats[0]
+    kbytes = gemv_bytes(*t0m)
+    achieved = kbytes / (kms / 1e3) / 1e9
+    traffic = None
+    prof = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(prof):
+        traffic = json.load(open(prof)).get(f"{t0m[0]}:{t0m[1]}x{t0m[2]}")
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
+        "config": {"workload": name, "weight_copies": copies,
+                   "l2": "rotating weight copies, 3x the 126 MB L2",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "exact": "Q32.32 outputs bit-equal to the CPU oracle (checked before timing)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "traffic": traffic,
+                     "kernel": f"gemv_kernel<Q4_K> {t0m[1]}x{t0m[2]}",
+                     "algorithmic_bytes": kbytes, "peak_source": src},
+        "e2e": {"value": e2e, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": len(mats) * args.steps,
+        "kernel_us": kms * 1e3,
+        "clocks": clk,
+    }
+    if world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_gemv_baseline(mats, seconds=args.cpu_seconds)
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", type=int, default=2, choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world, rank, local, pg = dist_setup(args.gpus)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank, local, pg)
+        else:
+            run_ours(args, world, rank, local, pg)
+    finally:
+        if pg is not None:
+            pg.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -32,6 +32,12 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#if defined(__GNUC__)
+#define APX_API __attribute__((visibility("default")))
+#else
+#define APX_API
+#endif
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -96,11 +102,11 @@ typedef struct apx_call_status {
 /* ---- context ---------------------------------------------------------------- */
 
 /* Open a backend context on CUDA device `device`.  Returns NULL on failure. */
-apx_ctx *apx_open(int device, apx_err *err);
+APX_API apx_ctx *apx_open(int device, apx_err *err);
 /* Free every device buffer the context owns. */
-void apx_close(apx_ctx *ctx);
+APX_API void apx_close(apx_ctx *ctx);
 /* The backend's version string. */
-const char *apx_version(void);
+APX_API const char *apx_version(void);
 
 /* ---- weights ------------------------------------------------------------------ */
 
@@ -111,27 +117,27 @@ const char *apx_version(void);
  * ShortPayload { need = n_out * row_bytes, have = raw_len }.  Non-finite block
  * scales are found here, once, and reported by every later call exactly where the
  * reference reports them. */
-int apx_tensor_upload(apx_ctx *ctx, uint32_t ggml_type, const uint8_t *raw,
+APX_API int apx_tensor_upload(apx_ctx *ctx, uint32_t ggml_type, const uint8_t *raw,
                       size_t raw_len, size_t n_out, size_t n_in, uint64_t *handle,
                       apx_err *err);
 /* Release an uploaded tensor. */
-int apx_tensor_free(apx_ctx *ctx, uint64_t handle);
+APX_API int apx_tensor_free(apx_ctx *ctx, uint64_t handle);
 /* Device bytes held by an uploaded tensor (repacked payload + row metadata). */
-size_t apx_tensor_device_bytes(apx_ctx *ctx, uint64_t handle);
+APX_API size_t apx_tensor_device_bytes(apx_ctx *ctx, uint64_t handle);
 
 /* ---- synchronous drop-in entry points (host buffers) ----------------------------- */
 
 /* The decode contract (replaces matvec_q8act, src/engine/chart/mod.rs:1887).
  * codes: q_len int8 activation codes; exps: ceil(q_len/32) exponent bytes;
  * out: n_out Q32.32 words.  Refusals in the reference's order. */
-int apx_matvec_q8act(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
+APX_API int apx_matvec_q8act(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
                      const int8_t *codes, size_t q_len, const uint8_t *exps,
                      int64_t *out, apx_err *err);
 
 /* Same result as apx_matvec_q8act with the validation order of the chunked caller
  * (replaces matvec_q8act_quant_chunked, src/engine/chart/ffn.rs:667-745).  `chunks`
  * is the CPU row-task count; the device kernel's decomposition does not depend on it. */
-int apx_matvec_q8act_chunked(apx_ctx *ctx, uint64_t tensor, size_t n_out,
+APX_API int apx_matvec_q8act_chunked(apx_ctx *ctx, uint64_t tensor, size_t n_out,
                              size_t n_in, const int8_t *codes, size_t q_len,
                              const uint8_t *exps, size_t chunks, int64_t *out,
                              apx_err *err);
@@ -140,54 +146,54 @@ int apx_matvec_q8act_chunked(apx_ctx *ctx, uint64_t tensor, size_t n_out,
  * k_cols activation columns; column c has codes[c*q_len ..] and exps[c*ceil(q_len/32) ..].
  * out is column-major: out[c*n_out + r].  The call refuses with the lowest refusing
  * column's refusal (err->col). */
-int apx_matmat_q8act(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
+APX_API int apx_matmat_q8act(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
                      size_t k_cols, const int8_t *codes, size_t q_len,
                      const uint8_t *exps, int64_t *out, apx_err *err);
 
 /* quant_act on the device (src/engine/chart/mod.rs:258-334): Q32.32 in, codes and
  * exponent bytes out.  APX_ERR_QUANT_REFUSED where the reference returns None. */
-int apx_quant_act(apx_ctx *ctx, const int64_t *x, size_t n, int8_t *codes,
+APX_API int apx_quant_act(apx_ctx *ctx, const int64_t *x, size_t n, int8_t *codes,
                   uint8_t *exps, apx_err *err);
 
 /* f32 boundary: y = from_q32(matvec_q8act(W, quant_act(f32_to_fixed(x)))).
  * x: n_in floats, y: n_out floats, each the Q32.32 result rounded once to f32. */
-int apx_matvec_f32(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
+APX_API int apx_matvec_f32(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
                    const float *x, float *y, apx_err *err);
 
 /* Parity hook: the exact int32 group dots the kernels form, one per (row, group)
  * in group order (32-lane groups for Q8_0/Q4_K, 16-lane groups for Q6_K). */
-int apx_debug_block_dots(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
+APX_API int apx_debug_block_dots(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
                          const int8_t *codes, int32_t *dots, apx_err *err);
 
 /* ---- asynchronous device-buffer entry points ----------------------------------- */
 
 /* Validate device-resident codes/exps and fill the descriptor (device kernel). */
-int apx_act_describe_async(apx_ctx *ctx, const int8_t *d_codes,
+APX_API int apx_act_describe_async(apx_ctx *ctx, const int8_t *d_codes,
                            const uint8_t *d_exps, size_t n_in, apx_act_desc *d_desc,
                            void *stream);
 /* Device quant_act of a Q32.32 vector. */
-int apx_quant_q32_async(apx_ctx *ctx, const int64_t *d_x, size_t n, int8_t *d_codes,
+APX_API int apx_quant_q32_async(apx_ctx *ctx, const int64_t *d_x, size_t n, int8_t *d_codes,
                         uint8_t *d_exps, apx_act_desc *d_desc, void *stream);
 /* Device f32_to_fixed + quant_act of an f32 vector. */
-int apx_quant_f32_async(apx_ctx *ctx, const float *d_x, size_t n, int8_t *d_codes,
+APX_API int apx_quant_f32_async(apx_ctx *ctx, const float *d_x, size_t n, int8_t *d_codes,
                         uint8_t *d_exps, apx_act_desc *d_desc, void *stream);
 /* Exact projection of device activations; d_out_q32 and/or d_out_f32 may be NULL.
  * d_status receives the refusal word (apx_status_decode).  Buffers padded by the
  * caller: d_codes holds apx_act_padded_len(n_in) bytes (zero beyond n_in). */
-int apx_matvec_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
+APX_API int apx_matvec_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
                      const int8_t *d_codes, const uint8_t *d_exps,
                      const apx_act_desc *d_desc, int64_t *d_out_q32, float *d_out_f32,
                      apx_call_status *d_status, void *stream);
 /* Exact k-column projection of device activations (column-major outputs). */
-int apx_matmat_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
+APX_API int apx_matmat_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
                      size_t k_cols, const int8_t *d_codes, const uint8_t *d_exps,
                      const apx_act_desc *d_descs, int64_t *d_out_q32,
                      float *d_out_f32, apx_call_status *d_status, void *stream);
 /* Activation buffer length (bytes of codes) the async kernels read for width n_in. */
-size_t apx_act_padded_len(size_t n_in);
+APX_API size_t apx_act_padded_len(size_t n_in);
 /* Decode a refusal word (host copy of *d_status) together with the tensor's
  * upload-time findings into err; returns err->code. */
-int apx_status_decode(apx_ctx *ctx, uint64_t tensor, const apx_call_status *status,
+APX_API int apx_status_decode(apx_ctx *ctx, uint64_t tensor, const apx_call_status *status,
                       apx_err *err);
 
 #ifdef __cplusplus
