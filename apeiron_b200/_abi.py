@@ -38,7 +38,10 @@ EXPORTS = [
     "apx_matmat_q8act", "apx_quant_act", "apx_matvec_f32", "apx_debug_block_dots",
     "apx_act_describe_async", "apx_quant_q32_async", "apx_quant_f32_async",
     "apx_matvec_async", "apx_matmat_async", "apx_act_padded_len", "apx_status_decode",
+    "apx_matvec_f32_noalloc",
 ]
+
+NOALLOC_MAX_N_IN = 65536
 
 
 class ApxErr(C.Structure):
@@ -83,6 +86,7 @@ _SIGS = {
     "apx_matmat_async": (C.c_int, [P, U64, SZ, SZ, SZ, P, P, P, P, P, P, P]),
     "apx_act_padded_len": (SZ, [SZ]),
     "apx_status_decode": (C.c_int, [P, U64, C.POINTER(CallStatus), EP]),
+    "apx_matvec_f32_noalloc": (C.c_int, [P, U64, SZ, SZ, P, P, P, P]),
 }
 
 _lib = None

@@ -293,6 +293,23 @@ int matvec_sync(apx_ctx *ctx, Tensor &t, size_t n_out, size_t n_in, const int8_t
 
 }  // namespace
 
+namespace apx {
+// The launch view of an uploaded tensor, for entry points defined in other files.
+bool tensor_launch_info(apx_ctx *ctx, uint64_t handle, uint32_t *type, const uint8_t **pack,
+                        size_t *n_out, size_t *n_in, GemvPlan *plan, int *device) {
+  std::lock_guard<std::mutex> g(ctx->mu);
+  Tensor *t = find(ctx, handle);
+  if (!t) return false;
+  *type = t->type;
+  *pack = t->d_pack;
+  *n_out = t->n_out;
+  *n_in = t->n_in;
+  *plan = t->plan;
+  *device = ctx->device;
+  return true;
+}
+}  // namespace apx
+
 extern "C" {
 
 const char *apx_version(void) { return "apeiron_b200 0.1 (sm_100a)"; }

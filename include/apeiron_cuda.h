@@ -196,6 +196,35 @@ APX_API size_t apx_act_padded_len(size_t n_in);
 APX_API int apx_status_decode(apx_ctx *ctx, uint64_t tensor, const apx_call_status *status,
                       apx_err *err);
 
+/* ---- allocation-free entry point ------------------------------------------------ */
+
+/* Widest activation the allocation-free entry point accepts, and the size of the fixed
+ * device array it stages in (descriptor, exponent bytes, int8 codes). */
+#define APX_NOALLOC_MAX_N_IN 65536u
+#define APX_NOALLOC_SCRATCH_BYTES (256u + APX_NOALLOC_MAX_N_IN / 32u + APX_NOALLOC_MAX_N_IN)
+
+/* apx_matvec_f32 for callers that cannot allocate device memory on the call path: an engine
+ * that reserves its whole HBM budget at start-up, a process held to a fixed GPU memory
+ * quota, a decode loop that cannot take an allocation's latency or failure.  It has no
+ * counterpart in the reference (whose CPU kernels allocate freely).
+ *
+ * Same result as apx_matvec_f32 (f32_to_fixed + quant_act on the device, the exact
+ * projection, one rounding to f32), on device buffers: d_x holds n_in floats, d_y receives
+ * n_out floats, *d_status the refusal word (decode with apx_status_decode after the stream
+ * has finished).  The call is asynchronous on `stream` and allocates nothing: the quantized
+ * activation is staged in one array of APX_NOALLOC_SCRATCH_BYTES compiled into the library,
+ * which every GPU that loads the library holds until the process exits.
+ *   - n_in above APX_NOALLOC_MAX_N_IN is refused with APX_ERR_TOO_LARGE.
+ *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress);
+ *     make that first call before any stream capture.
+ *   - Every call on a device shares the one array and it keeps the last call's contents:
+ *     calls whose kernels overlap on the GPU (other streams, other host threads) race.
+ *     Serialise them on one stream.
+ * The tensor itself is uploaded beforehand with apx_tensor_upload (which does allocate). */
+APX_API int apx_matvec_f32_noalloc(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
+                                   const float *d_x, float *d_y, apx_call_status *d_status,
+                                   void *stream);
+
 #ifdef __cplusplus
 }
 #endif
