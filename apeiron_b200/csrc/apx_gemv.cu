@@ -21,14 +21,11 @@
 // activation exponent) and the activation exponent spread fits the family's i64 super-block
 // fold; otherwise the same kernel takes the checked path, one lane per row summing
 // Σ w_i·x̂_i in element order with i128 overflow detection, which is matvec_fixed itself.
-#include <cooperative_groups.h>
-
 #include <algorithm>
+#include <cstdlib>
 
 #include "apx_common.cuh"
 #include "apx_kernels.h"
-
-namespace cg = cooperative_groups;
 
 namespace apx {
 
@@ -385,7 +382,9 @@ struct GemvArgs {
   long long *out_q32;
   float *out_f32;
   unsigned long long *status;
-  int R, P, ksplit;  // row tiles per CTA, warps per row tile, CTAs per cluster along K
+  Acc128 *partials;     // [n_rt][ksplit][32] partial sums of a K-split row tile
+  unsigned *counters;   // [n_rt] arrivals of a K-split row tile (self-resetting)
+  int R, P, ksplit;     // row tiles per CTA, warps per row tile, CTAs per row tile along K
 };
 
 // Programmatic dependent launch: the next projection may start streaming its (constant)
@@ -396,12 +395,81 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Per-warp activation staging of one unit: its int8 codes (zero for a zero-scale block or
+// past n_in), and per 32-lane block the exponent data and Σxq the family's fold reads.
+template <uint32_t T>
+struct WarpAct {
+  int codes[Fam<T>::span / 4];
+  int e[Fam<T>::span / 32];                     // Q8_0: absolute exponent or -1; else er
+  long long xs[T == kQ6_K ? 16 : Fam<T>::span / 32];  // Σxq·2^er (per 16 lanes for Q6_K)
+};
+
+// The raw activation bytes a lane stages for unit u: 16 codes and their block's exponent,
+// loaded together (one round trip) right after the dependency wait.
+struct StageRegs {
+  uint4 v;
+  unsigned e;
+};
+
+template <uint32_t T>
+__device__ __forceinline__ StageRegs stage_load(const int8_t *codes, const uint8_t *exps,
+                                                size_t n_in, int u, int lane) {
+  constexpr int span = Fam<T>::span;
+  StageRegs s{make_uint4(0, 0, 0, 0), APX_EXP_ZERO};
+  if (lane < span / 16) {
+    const size_t j = (size_t)u * span + 16 * lane;
+    const size_t b = j / 32;
+    if (j < n_in) {
+      s.e = exps[b];
+      if (j + 16 <= n_in && ((reinterpret_cast<uintptr_t>(codes + j) & 15) == 0)) {
+        s.v = __ldg(reinterpret_cast<const uint4 *>(codes + j));
+      } else {
+        unsigned t[4] = {0, 0, 0, 0};
+        for (int i = 0; i < 16; i++)
+          if (j + i < n_in) t[i / 4] |= ((unsigned)(uint8_t)codes[j + i]) << (8 * (i % 4));
+        s.v = make_uint4(t[0], t[1], t[2], t[3]);
+      }
+    }
+  }
+  return s;
+}
+
+template <uint32_t T>
+__device__ __forceinline__ void stage_store(WarpAct<T> &w, StageRegs s, int emin, int lane) {
+  constexpr int span = Fam<T>::span;
+  const bool zero = s.e == APX_EXP_ZERO;
+  const uint4 v = zero ? make_uint4(0, 0, 0, 0) : s.v;
+  const int er = zero ? 0 : (int)s.e - emin;
+  const int eabs = zero ? -1 : (int)s.e;
+  if (lane < span / 16) reinterpret_cast<uint4 *>(w.codes)[lane] = v;
+  // Σ of this lane's 16 codes, then the 32-lane block's sum across the lane pair
+  int s16 = dp4a_ss((int)v.x, 0x01010101, 0);
+  s16 = dp4a_ss((int)v.y, 0x01010101, s16);
+  s16 = dp4a_ss((int)v.z, 0x01010101, s16);
+  s16 = dp4a_ss((int)v.w, 0x01010101, s16);
+  const int s32 = s16 + __shfl_xor_sync(0xFFFFFFFFu, s16, 1);
+  if (lane < span / 16) {
+    if (T == kQ6_K) w.xs[lane] = (long long)s16 << er;
+    if ((lane & 1) == 0) {
+      w.e[lane / 2] = T == kQ8_0 ? eabs : er;
+      if (T == kQ4_K) w.xs[lane / 2] = (long long)s32 << er;
+    }
+  }
+  __syncwarp();
+}
+
+template <uint32_t T>
+__device__ __forceinline__ void fold(Acc128 &acc, const UnitRegs<T> &r, const WarpAct<T> &w,
+                                     int emin) {
+  fold_unit(acc, r, w.codes, w.e, w.xs, emin);
+}
+
 template <uint32_t T, bool PIPE>
 __global__ void __launch_bounds__(PIPE ? 256 : 512) gemv_kernel(GemvArgs g) {
   extern __shared__ __align__(16) unsigned char smem[];
   using F = Fam<T>;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int ks = g.ksplit > 1 ? (int)(blockIdx.x % g.ksplit) : 0;
+  const int ks = (int)(blockIdx.x % g.ksplit);
   const size_t rt0 = (size_t)(blockIdx.x / g.ksplit) * g.R;
   const int k0 = (int)((long long)g.units * ks / g.ksplit);
   const int k1 = (int)((long long)g.units * (ks + 1) / g.ksplit);
@@ -413,10 +481,14 @@ __global__ void __launch_bounds__(PIPE ? 256 : 512) gemv_kernel(GemvArgs g) {
   pdl_launch_dependents();
   // weights first: they depend on nothing the previous kernel writes
   UnitRegs<T> cur;
-  if (active && k0 + p < k1) load_unit(cur, base + (size_t)(k0 + p) * F::unit_bytes, lane);
+  const bool first = active && k0 + p < k1;
+  if (first) load_unit(cur, base + (size_t)(k0 + p) * F::unit_bytes, lane);
   pdl_wait();
 
+  // the descriptor and the first unit's activation bytes in one round trip
   const ActDesc desc = *g.desc;
+  StageRegs sr = first ? stage_load<T>(g.codes, g.exps, g.n_in, k0 + p, lane)
+                       : StageRegs{make_uint4(0, 0, 0, 0), APX_EXP_ZERO};
   if (desc.status != APX_OK) {  // the activation itself is refused (chart/mod.rs:1904-1907)
     if (blockIdx.x == 0 && threadIdx.x == 0)
       atomicMin(g.status, pack_status(0, (unsigned)desc.status, 0));
@@ -432,50 +504,8 @@ __global__ void __launch_bounds__(PIPE ? 256 : 512) gemv_kernel(GemvArgs g) {
     return;
   }
 
-  // -- activation prologue: codes, exponents and Σxq of units [k0, k1) ------------------
-  const int nunits = k1 - k0;
-  const int nel = nunits * F::span;  // multiple of 128
-  const int nw4 = nel / 4;           // multiple of 32
-  int *s_codes = reinterpret_cast<int *>(smem);
-  int *s_e = s_codes + nw4;  // per 32-block: eabs (Q8_0) or er (K-quants)
-  long long *s_xs = reinterpret_cast<long long *>(s_e + (((nel / 32) + 3) & ~3));
-  const size_t e0 = (size_t)k0 * F::span;
-  const size_t nb_act = (g.n_in + 31) / 32;
-  for (int j4 = threadIdx.x; j4 < nw4; j4 += blockDim.x) {  // whole warps per iteration
-    const size_t j = e0 + 4 * (size_t)j4;
-    const size_t b = j / 32;
-    const unsigned e = b < nb_act ? g.exps[b] : APX_EXP_ZERO;
-    unsigned word = 0;
-    if (e != APX_EXP_ZERO) {
-      if (j + 4 <= g.n_in && ((reinterpret_cast<uintptr_t>(g.codes + j) & 3) == 0)) {
-        word = *reinterpret_cast<const unsigned *>(g.codes + j);
-      } else {
-#pragma unroll
-        for (int t = 0; t < 4; t++)
-          if (j + t < g.n_in) word |= ((unsigned)(uint8_t)g.codes[j + t]) << (8 * t);
-      }
-    }
-    s_codes[j4] = (int)word;
-    if (T == kQ8_0) {
-      if ((j4 & 7) == 0) s_e[j4 >> 3] = e == APX_EXP_ZERO ? -1 : (int)e;
-    } else {
-      const int er = e == APX_EXP_ZERO ? 0 : (int)e - desc.emin;
-      int s4 = dp4a_ss((int)word, 0x01010101, 0);  // Σ of the four signed codes
-      s4 += __shfl_xor_sync(0xFFFFFFFFu, s4, 1);
-      s4 += __shfl_xor_sync(0xFFFFFFFFu, s4, 2);
-      if (T == kQ6_K) {
-        if ((j4 & 3) == 0) s_xs[j4 >> 2] = (long long)s4 << er;  // per 16 lanes
-      }
-      s4 += __shfl_xor_sync(0xFFFFFFFFu, s4, 4);
-      if ((j4 & 7) == 0) {
-        s_e[j4 >> 3] = er;
-        if (T == kQ4_K) s_xs[j4 >> 3] = (long long)s4 << er;  // per 32 lanes
-      }
-    }
-  }
-  __syncthreads();
-
-  // -- stream the units: fold the current registers while the next unit is in flight -----
+  // -- stream the units: each warp stages its unit's activation and folds its registers ---
+  WarpAct<T> *wact = reinterpret_cast<WarpAct<T> *>(smem) + warp;
   Acc128 acc;
   acc_zero(acc);
   if (active) {
@@ -484,54 +514,227 @@ __global__ void __launch_bounds__(PIPE ? 256 : 512) gemv_kernel(GemvArgs g) {
       const bool more = u + g.P < k1;
       if (PIPE && more) load_unit(nxt, base + (size_t)(u + g.P) * F::unit_bytes, lane);
       if (!PIPE && u != k0 + p) load_unit(cur, base + (size_t)u * F::unit_bytes, lane);
-      const int lu = u - k0;
-      if (T == kQ8_0)
-        fold_unit(acc, cur, s_codes + lu * 32, s_e + lu * 4, nullptr, 0);
-      else if (T == kQ4_K)
-        fold_unit(acc, cur, s_codes + lu * 64, s_e + lu * 8, s_xs + lu * 8, desc.emin);
-      else
-        fold_unit(acc, cur, s_codes + lu * 64, s_e + lu * 8, s_xs + lu * 16, desc.emin);
+      if (u != k0 + p) {
+        __syncwarp();  // the previous unit's reads of the staging are done
+        sr = stage_load<T>(g.codes, g.exps, g.n_in, u, lane);
+      }
+      stage_store<T>(*wact, sr, desc.emin, lane);
+      fold<T>(acc, cur, *wact, desc.emin);
       if (PIPE && more) cur = nxt;
     }
   }
 
-  // -- reduce: warps of a row tile, then CTAs of the cluster ------------------------------
-  __syncthreads();  // the activation region is reused for the partial sums
+  // -- reduce: warps of a row tile in shared memory, CTAs of a row tile through scratch ----
+  __syncthreads();  // the staging region is reused for the partial sums
   Acc128 *part = reinterpret_cast<Acc128 *>(smem);  // [R*P][32]
-  if (r < g.R) part[warp * 32 + lane] = acc;
+  part[warp * 32 + lane] = acc;
   __syncthreads();
-  Acc128 *csum = part + g.R * g.P * 32;  // [R][32]: this CTA's sums, read by cluster rank 0
+  Acc128 s;
+  acc_zero(s);
   if (p == 0 && r < g.R) {
-    Acc128 s = part[(r * g.P) * 32 + lane];
+    s = part[(r * g.P) * 32 + lane];
     for (int q = 1; q < g.P; q++) acc_add(s, part[(r * g.P + q) * 32 + lane]);
-    csum[r * 32 + lane] = s;
   }
+  bool finalize = ks == 0;
   if (g.ksplit > 1) {
-    cg::cluster_group cluster = cg::this_cluster();
-    cluster.sync();
-    if (ks == 0 && p == 0 && r < g.R) {
-      Acc128 s = csum[r * 32 + lane];
-      for (int q = 1; q < g.ksplit; q++) {
-        const Acc128 *remote = cluster.map_shared_rank(csum, q);
-        acc_add(s, remote[r * 32 + lane]);
-      }
-      csum[r * 32 + lane] = s;
+    // last-arriving CTA of the row tile sums the others' partials (threadfence reduction)
+    unsigned *ticket = reinterpret_cast<unsigned *>(part + g.R * g.P * 32);
+    if (p == 0 && active) {
+      Acc128 *slot = g.partials + (rt * g.ksplit + ks) * 32 + lane;
+      slot->lo = s.lo;
+      slot->hi = s.hi;
+      __threadfence();
     }
-    cluster.sync();  // keep every CTA's shared memory alive until rank 0 has read it
-  } else {
     __syncthreads();
+    if (threadIdx.x < (unsigned)g.R)
+      ticket[threadIdx.x] = rt0 + threadIdx.x < g.n_rt
+                                ? atomicAdd(g.counters + rt0 + threadIdx.x, 1u)
+                                : 0u;
+    __syncthreads();
+    finalize = active && ticket[r] == (unsigned)(g.ksplit - 1);
+    if (finalize && p == 0) {
+      __threadfence();
+      acc_zero(s);
+      for (int q = 0; q < g.ksplit; q++) {
+        const Acc128 *src = g.partials + (rt * g.ksplit + q) * 32 + lane;
+        acc_add(s, __ldcg(&src->lo), __ldcg(&src->hi));
+      }
+      if (lane == 0) g.counters[rt] = 0u;  // ready for the next call
+    }
   }
-  if (ks == 0 && p == 0 && active) {
+  if (finalize && p == 0 && active) {
     const size_t row = rt * 32 + lane;
     if (row < g.n_out) {
       long long v;
-      if (!acc_round_to_i64(csum[r * 32 + lane], v)) {
+      if (!acc_round_to_i64(s, v)) {
         atomicMin(g.status, pack_status(row, kKindOutputOverflow, 0));
       } else {
         if (g.out_q32) g.out_q32[row] = v;
         if (g.out_f32) g.out_f32[row] = __ll2float_rn(v) * 2.3283064365386963e-10f;
       }
     }
+  }
+}
+
+// ---- streaming kernel for matrices larger than one resident wave ---------------------------
+//
+// Persistent: V = gridDim.x × warps-per-CTA warps, warp v streams the contiguous unit chunk
+// [v·C, (v+1)·C) of the (row tile, K unit) order, C = ceil(T/V), folding one unit while the
+// next is in flight.  The CTA stages the whole activation once.  A row tile covered by one
+// warp is finished by it; a row tile split between warps is finished by whichever of them
+// arrives last (partial sums in the tensor's scratch, an arrival counter that resets itself).
+
+struct StreamArgs {
+  const uint8_t *pack;
+  int units;          // U, units per row tile
+  size_t n_rt, n_out, n_in;
+  const int8_t *codes;
+  const uint8_t *exps;
+  const ActDesc *desc;
+  long long *out_q32;
+  float *out_f32;
+  unsigned long long *status;
+  Acc128 *partials;   // [n_rt][kmax][32]
+  unsigned *counters; // [n_rt]
+  long long chunk;    // C
+  int kmax;           // most warps that can share a row tile
+};
+
+template <uint32_t T>
+__device__ __forceinline__ void finish_row(const Acc128 &s, size_t row, size_t n_out,
+                                           long long *out_q32, float *out_f32,
+                                           unsigned long long *status) {
+  if (row >= n_out) return;
+  long long v;
+  if (!acc_round_to_i64(s, v)) {
+    atomicMin(status, pack_status(row, kKindOutputOverflow, 0));
+  } else {
+    if (out_q32) out_q32[row] = v;
+    if (out_f32) out_f32[row] = __ll2float_rn(v) * 2.3283064365386963e-10f;
+  }
+}
+
+template <uint32_t T>
+__global__ void __launch_bounds__(256, 2) gemv_stream_kernel(StreamArgs g) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  using F = Fam<T>;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = blockDim.x / 32;
+  const long long U = g.units, Ttot = (long long)g.n_rt * U;
+  const long long v = (long long)blockIdx.x * nw + warp;
+  const long long x0 = v * g.chunk, x1 = min(Ttot, x0 + g.chunk);
+
+  pdl_launch_dependents();
+  UnitRegs<T> cur;
+  if (x0 < x1)
+    load_unit(cur, g.pack + (size_t)x0 * F::unit_bytes, lane);
+  pdl_wait();
+
+  const ActDesc desc = *g.desc;
+  if (desc.status != APX_OK) {
+    if (blockIdx.x == 0 && threadIdx.x == 0)
+      atomicMin(g.status, pack_status(0, (unsigned)desc.status, 0));
+    return;
+  }
+  const int es = desc.emax >= 0 ? desc.emax - desc.emin : 0;
+  const bool fast = bound_ok((long long)g.n_in, F::top, desc.emax) && es <= F::es_limit &&
+                    !(desc.pad[0] & 1u);
+  if (!fast) {
+    // the warp holding a row tile's first unit runs that tile's checked rows
+    for (long long x = x0; x < x1; x++)
+      if (x % U == 0)
+        checked_rows<T>(g.pack, g.units, (size_t)(x / U), lane, g.n_out, g.n_in, g.codes,
+                        g.exps, g.out_q32, g.out_f32, g.status);
+    return;
+  }
+
+  // -- the whole activation, staged once per CTA ---------------------------------------
+  const int nel = (int)U * F::span;
+  int *s_codes = reinterpret_cast<int *>(smem);
+  int *s_e = s_codes + nel / 4;
+  long long *s_xs = reinterpret_cast<long long *>(s_e + ((nel / 32 + 3) & ~3));
+  const int n16 = nel / 16;
+  for (int base = 0; base < n16; base += blockDim.x) {  // whole warps: the shuffle below
+    const int j16 = base + threadIdx.x;
+    const bool in = j16 < n16;
+    const size_t j = 16 * (size_t)j16, b = j / 32;
+    uint4 val = make_uint4(0, 0, 0, 0);
+    unsigned e = APX_EXP_ZERO;
+    if (in && j < g.n_in) {
+      e = g.exps[b];
+      if (j + 16 <= g.n_in && ((reinterpret_cast<uintptr_t>(g.codes + j) & 15) == 0)) {
+        val = __ldg(reinterpret_cast<const uint4 *>(g.codes + j));
+      } else {
+        unsigned t[4] = {0, 0, 0, 0};
+        for (int i = 0; i < 16; i++)
+          if (j + i < g.n_in) t[i / 4] |= ((unsigned)(uint8_t)g.codes[j + i]) << (8 * (i % 4));
+        val = make_uint4(t[0], t[1], t[2], t[3]);
+      }
+    }
+    const bool zero = e == APX_EXP_ZERO;
+    if (zero) val = make_uint4(0, 0, 0, 0);
+    if (in) reinterpret_cast<uint4 *>(s_codes)[j16] = val;
+    const int er = zero ? 0 : (int)e - desc.emin;
+    int s16 = dp4a_ss((int)val.x, 0x01010101, 0);
+    s16 = dp4a_ss((int)val.y, 0x01010101, s16);
+    s16 = dp4a_ss((int)val.z, 0x01010101, s16);
+    s16 = dp4a_ss((int)val.w, 0x01010101, s16);
+    const int s32 = s16 + __shfl_xor_sync(0xFFFFFFFFu, s16, 1);
+    if (!in) continue;
+    if (T == kQ6_K) s_xs[j16] = (long long)s16 << er;
+    if ((j16 & 1) == 0) {
+      s_e[j16 / 2] = T == kQ8_0 ? (zero ? -1 : (int)e) : er;
+      if (T == kQ4_K) s_xs[j16 / 2] = (long long)s32 << er;
+    }
+  }
+  __syncthreads();
+
+  // -- stream the chunk ---------------------------------------------------------------------
+  Acc128 acc;
+  acc_zero(acc);
+  for (long long x = x0; x < x1; x++) {
+    UnitRegs<T> nxt;
+    const bool more = x + 1 < x1;
+    if (more) load_unit(nxt, g.pack + (size_t)(x + 1) * F::unit_bytes, lane);
+    const long long rt = x / U;
+    const int u = (int)(x % U);
+    if (T == kQ8_0)
+      fold_unit(acc, cur, s_codes + u * 32, s_e + u * 4, nullptr, 0);
+    else if (T == kQ4_K)
+      fold_unit(acc, cur, s_codes + u * 64, s_e + u * 8, s_xs + u * 8, desc.emin);
+    else
+      fold_unit(acc, cur, s_codes + u * 64, s_e + u * 8, s_xs + u * 16, desc.emin);
+    if (u == U - 1 || !more) {
+      // flush this warp's share of row tile rt
+      const long long first_v = (rt * U) / g.chunk;
+      const long long last_v = (rt * U + U - 1) / g.chunk;
+      const size_t row = (size_t)rt * 32 + lane;
+      if (first_v == last_v) {
+        finish_row<T>(acc, row, g.n_out, g.out_q32, g.out_f32, g.status);
+      } else {
+        const int k = (int)(v - first_v), count = (int)(last_v - first_v + 1);
+        Acc128 *slot = g.partials + ((size_t)rt * g.kmax + k) * 32 + lane;
+        slot->lo = acc.lo;
+        slot->hi = acc.hi;
+        __threadfence();
+        __syncwarp();
+        unsigned ticket = 0;
+        if (lane == 0) ticket = atomicAdd(g.counters + rt, 1u);
+        ticket = __shfl_sync(0xFFFFFFFFu, ticket, 0);
+        if (ticket == (unsigned)(count - 1)) {
+          __threadfence();
+          Acc128 s;
+          acc_zero(s);
+          for (int q = 0; q < count; q++) {
+            const Acc128 *src = g.partials + ((size_t)rt * g.kmax + q) * 32 + lane;
+            acc_add(s, __ldcg(&src->lo), __ldcg(&src->hi));
+          }
+          finish_row<T>(s, row, g.n_out, g.out_q32, g.out_f32, g.status);
+          if (lane == 0) g.counters[rt] = 0u;
+        }
+      }
+      acc_zero(acc);
+    }
+    if (more) cur = nxt;
   }
 }
 
@@ -565,57 +768,80 @@ cudaError_t launch_repack(const uint8_t *d_raw, uint8_t *d_pack, uint32_t type, 
   return cudaGetLastError();
 }
 
+static size_t warp_act_bytes(uint32_t t) {
+  return t == kQ8_0 ? sizeof(WarpAct<kQ8_0>)
+                    : (t == kQ4_K ? sizeof(WarpAct<kQ4_K>) : sizeof(WarpAct<kQ6_K>));
+}
+
 GemvPlan plan_gemv(uint32_t type, size_t n_out, size_t n_in, int sm_count) {
   GemvPlan pl{};
-  const int U = units_per_row_tile(type, n_in);
+  const int U = units_per_row_tile(type, n_in);  // 0 for n_in = 0: no loads, rows are 0
   const size_t n_rt = (n_out + 31) / 32;
   const size_t T = n_rt * (size_t)U;
   const size_t wave = (size_t)sm_count * 24;
-  if (T <= wave) {
-    // The whole matrix fits one resident wave: one unit per warp, every load in flight at
-    // once; CTAs of one row tile along K form a cluster when a row has more than 16 units.
-    pl.pipe = false;
-    int w = U < 1 ? 1 : U;
-    if (w <= 16) {
-      pl.ksplit = 1;
-      pl.P = w;
-      pl.R = std::max(1, std::min(16 / pl.P, (int)std::max<size_t>(1, n_rt / sm_count)));
-    } else {
-      pl.ksplit = std::min(8, (w + 15) / 16);
-      pl.P = std::min(16, (w + pl.ksplit - 1) / pl.ksplit);
-      pl.R = 1;
-    }
-  } else {
-    // Streaming: each warp folds one unit while its next unit is in flight.
+  // One unit per warp while the whole matrix fits one resident wave (every load in flight at
+  // once); otherwise warps stream several units, folding one while the next is in flight.
+  pl.units = U;
+  pl.n_rt = n_rt;
+  if (T > wave) {
+    // persistent streaming kernel: 2 CTAs of 8 warps per SM, one contiguous chunk per warp
     pl.pipe = true;
-    int w = std::max(1, (U + 1) / 2);
-    if (w <= 8) {
-      pl.ksplit = 1;
-      pl.P = w;
-      pl.R = std::max(1, 8 / pl.P);
-    } else {
-      pl.ksplit = std::min(8, (w + 7) / 8);
-      pl.P = std::min(8, (w + pl.ksplit - 1) / pl.ksplit);
-      pl.R = 1;
-    }
+    const int span = type == kQ8_0 ? 128 : 256;
+    const size_t nel = (size_t)U * span;
+    pl.smem = nel + ((nel / 32 + 3) & ~(size_t)3) * 4 + nel / 16 * 8;
+    const int per_sm = pl.smem * 2 <= 200 * 1024 ? 2 : 1;
+    pl.block = 256;
+    pl.grid = (unsigned)(sm_count * per_sm);
+    const long long V = (long long)pl.grid * 8;
+    pl.chunk = (long long)((T + V - 1) / V);
+    pl.kmax = (int)((U + pl.chunk - 1) / pl.chunk) + 1;
+    pl.R = pl.P = pl.ksplit = 1;
+    return pl;
+  }
+  int upw = 1;
+  pl.pipe = false;
+  const int cap = pl.pipe ? 8 : 16;  // warps per CTA
+  int w = std::max(1, (U + upw - 1) / upw);
+  if (w <= cap) {
+    pl.ksplit = 1;
+    pl.P = w;
+    pl.R = std::max(1, cap / pl.P);
+    if (!pl.pipe)
+      pl.R = std::max(1, std::min(pl.R, (int)std::max<size_t>(1, n_rt / sm_count)));
+  } else {
+    pl.ksplit = (w + cap - 1) / cap;
+    pl.P = (w + pl.ksplit - 1) / pl.ksplit;
+    pl.R = 1;
   }
   if ((size_t)pl.R > n_rt) pl.R = (int)(n_rt ? n_rt : 1);
   pl.units = U;
   pl.n_rt = n_rt;
   pl.grid = (unsigned)(((n_rt + pl.R - 1) / pl.R) * pl.ksplit);
   pl.block = 32 * pl.R * pl.P;
-  const int span = type == kQ8_0 ? 128 : 256;
-  int kmax = (U + pl.ksplit - 1) / pl.ksplit;  // widest K-range of one CTA
-  int nel = kmax * span, nblk32 = nel / 32;
-  size_t act = (size_t)nel + (size_t)((nblk32 + 3) & ~3) * 4 + (size_t)nblk32 * 2 * 8;
-  size_t red = (size_t)(pl.R * pl.P + pl.R) * 32 * sizeof(Acc128);
-  pl.smem = act > red ? act : red;
+  size_t stage = (size_t)pl.R * pl.P * warp_act_bytes(type);
+  size_t red = (size_t)pl.R * pl.P * 32 * sizeof(Acc128) + 64;
+  pl.smem = std::max(stage, red);
   return pl;
 }
 
+size_t gemv_scratch_bytes(const GemvPlan &pl) {
+  if (pl.pipe) return pl.n_rt * (size_t)pl.kmax * 32 * sizeof(Acc128) + pl.n_rt * sizeof(unsigned);
+  if (pl.ksplit <= 1) return 0;
+  return pl.n_rt * (size_t)pl.ksplit * 32 * sizeof(Acc128) + pl.n_rt * sizeof(unsigned);
+}
+
+// Programmatic dependent launch is on unless APX_PDL=0 in the environment (read once).
+static bool pdl_enabled() {
+  static const bool on = [] {
+    const char *v = std::getenv("APX_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 template <uint32_t T>
-static cudaError_t launch_t(const GemvPlan &pl, const GemvArgs &a, cudaStream_t stream) {
-  auto kern = pl.pipe ? gemv_kernel<T, true> : gemv_kernel<T, false>;
+static cudaError_t launch_stream(const GemvPlan &pl, const StreamArgs &a, cudaStream_t stream) {
+  auto kern = gemv_stream_kernel<T>;
   if (pl.smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)pl.smem);
@@ -626,28 +852,68 @@ static cudaError_t launch_t(const GemvPlan &pl, const GemvArgs &a, cudaStream_t 
   cfg.blockDim = dim3(pl.block);
   cfg.dynamicSmemBytes = pl.smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
-  int na = 0;
-  attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[na].val.programmaticStreamSerializationAllowed = 1;
-  na++;
-  if (pl.ksplit > 1) {
-    attr[na].id = cudaLaunchAttributeClusterDimension;
-    attr[na].val.clusterDim.x = pl.ksplit;
-    attr[na].val.clusterDim.y = 1;
-    attr[na].val.clusterDim.z = 1;
-    na++;
-  }
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = na;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
-cudaError_t launch_gemv(const GemvPlan &pl, uint32_t type, const uint8_t *pack, size_t n_out,
-                        size_t n_in, const int8_t *codes, const uint8_t *exps,
+template <uint32_t T>
+static cudaError_t launch_t(const GemvPlan &pl, const GemvArgs &a, cudaStream_t stream) {
+  auto kern = gemv_kernel<T, false>;
+  if (pl.smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)pl.smem);
+    if (e != cudaSuccess) return e;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.grid);
+  cfg.blockDim = dim3(pl.block);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+cudaError_t launch_gemv(const GemvPlan &pl, uint32_t type, const uint8_t *pack, void *scratch,
+                        size_t n_out, size_t n_in, const int8_t *codes, const uint8_t *exps,
                         const void *desc, long long *out_q32, float *out_f32,
                         unsigned long long *status, cudaStream_t stream) {
   if (n_out == 0) return cudaSuccess;
+  if (pl.ksplit > 1 && !scratch) return cudaErrorInvalidValue;
+  if (pl.units > 0 && !pack) return cudaErrorInvalidValue;  // a plan that reads no payload
+  if (pl.pipe) {
+    if (!scratch) return cudaErrorInvalidValue;
+    StreamArgs sa;
+    sa.pack = pack;
+    sa.units = pl.units;
+    sa.n_rt = pl.n_rt;
+    sa.n_out = n_out;
+    sa.n_in = n_in;
+    sa.codes = codes;
+    sa.exps = exps;
+    sa.desc = reinterpret_cast<const ActDesc *>(desc);
+    sa.out_q32 = out_q32;
+    sa.out_f32 = out_f32;
+    sa.status = status;
+    sa.partials = reinterpret_cast<Acc128 *>(scratch);
+    sa.counters = reinterpret_cast<unsigned *>(reinterpret_cast<Acc128 *>(scratch) +
+                                               pl.n_rt * (size_t)pl.kmax * 32);
+    sa.chunk = pl.chunk;
+    sa.kmax = pl.kmax;
+    switch (type) {
+      case kQ8_0: return launch_stream<kQ8_0>(pl, sa, stream);
+      case kQ4_K: return launch_stream<kQ4_K>(pl, sa, stream);
+      case kQ6_K: return launch_stream<kQ6_K>(pl, sa, stream);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   GemvArgs a;
   a.pack = pack;
   a.units = pl.units;
@@ -660,6 +926,10 @@ cudaError_t launch_gemv(const GemvPlan &pl, uint32_t type, const uint8_t *pack, 
   a.out_q32 = out_q32;
   a.out_f32 = out_f32;
   a.status = status;
+  a.partials = reinterpret_cast<Acc128 *>(scratch);
+  a.counters = pl.ksplit > 1 ? reinterpret_cast<unsigned *>(
+                                   reinterpret_cast<Acc128 *>(scratch) + pl.n_rt * pl.ksplit * 32)
+                             : nullptr;
   a.R = pl.R;
   a.P = pl.P;
   a.ksplit = pl.ksplit;

@@ -12,8 +12,10 @@ struct GemvPlan {
   int units;       // units per 32-row tile
   size_t n_rt;     // row tiles
   int R, P;        // row tiles per CTA, warps per row tile
-  int ksplit;      // CTAs per cluster along K
-  bool pipe;       // warps stream several units with one unit of prefetch
+  int ksplit;      // CTAs per row tile along K
+  bool pipe;       // persistent streaming kernel (matrices beyond one resident wave)
+  long long chunk; // streaming: units per warp
+  int kmax;        // streaming: most warps sharing one row tile
   unsigned grid;
   int block;
   size_t smem;
@@ -24,10 +26,12 @@ size_t packed_bytes(uint32_t type, size_t n_out, size_t n_in);
 cudaError_t launch_repack(const uint8_t *d_raw, uint8_t *d_pack, uint32_t type, size_t n_out,
                           size_t n_in, size_t row_bytes, cudaStream_t stream);
 GemvPlan plan_gemv(uint32_t type, size_t n_out, size_t n_in, int sm_count);
-cudaError_t launch_gemv(const GemvPlan &pl, uint32_t type, const uint8_t *pack, size_t n_out,
-                        size_t n_in, const int8_t *codes, const uint8_t *exps, const void *desc,
-                        long long *out_q32, float *out_f32, unsigned long long *status,
-                        cudaStream_t stream);
+// Per-tensor device scratch of a K-split plan (partial sums + arrival counters, zeroed once).
+size_t gemv_scratch_bytes(const GemvPlan &pl);
+cudaError_t launch_gemv(const GemvPlan &pl, uint32_t type, const uint8_t *pack, void *scratch,
+                        size_t n_out, size_t n_in, const int8_t *codes, const uint8_t *exps,
+                        const void *desc, long long *out_q32, float *out_f32,
+                        unsigned long long *status, cudaStream_t stream);
 
 // Activation kernels (apx_quant.cu).  `cols` activation vectors of width n laid out with
 // stride `ld` codes and `ldb` exponent bytes; one descriptor per column.

@@ -53,7 +53,8 @@ cudaError_t scratch_address(int device, void **out) {
 // Defined in apx_runtime.cu: the tensor's device payload, launch plan and geometry.
 namespace apx {
 bool tensor_launch_info(apx_ctx *ctx, uint64_t handle, uint32_t *type, const uint8_t **pack,
-                        size_t *n_out, size_t *n_in, GemvPlan *plan, int *device);
+                        void **scratch, size_t *n_out, size_t *n_in, GemvPlan *plan,
+                        int *device);
 }
 
 extern "C" APX_API int apx_matvec_f32_noalloc(apx_ctx *ctx, uint64_t tensor, size_t n_out,
@@ -63,10 +64,12 @@ extern "C" APX_API int apx_matvec_f32_noalloc(apx_ctx *ctx, uint64_t tensor, siz
   if (n_in > kMaxN) return APX_ERR_TOO_LARGE;
   uint32_t type;
   const uint8_t *pack;
+  void *tscratch;
   size_t t_out, t_in;
   apx::GemvPlan plan;
   int device;
-  if (!apx::tensor_launch_info(ctx, tensor, &type, &pack, &t_out, &t_in, &plan, &device))
+  if (!apx::tensor_launch_info(ctx, tensor, &type, &pack, &tscratch, &t_out, &t_in, &plan,
+                               &device))
     return APX_ERR_INVALID_ARGUMENT;
   if (n_in != t_in || n_out > t_out) return APX_ERR_LAYOUT_MISMATCH;
   cudaError_t e = cudaSetDevice(device);
@@ -82,7 +85,7 @@ extern "C" APX_API int apx_matvec_f32_noalloc(apx_ctx *ctx, uint64_t tensor, siz
     e = apx::launch_quant_f32(d_x, n_in, reinterpret_cast<int8_t *>(s + kCodesOff),
                               s + kExpsOff, s + kDescOff, st);
   if (e == cudaSuccess)
-    e = apx::launch_gemv(plan, type, pack, n_out, n_in,
+    e = apx::launch_gemv(plan, type, pack, tscratch, n_out, n_in,
                          reinterpret_cast<const int8_t *>(s + kCodesOff), s + kExpsOff,
                          s + kDescOff, nullptr, d_y, &d_status->first, st);
   return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;

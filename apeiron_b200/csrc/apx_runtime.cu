@@ -31,6 +31,7 @@ struct Tensor {
   size_t n_out = 0, n_in = 0, raw_len = 0, row_bytes = 0;
   uint8_t *d_pack = nullptr;
   size_t pack_bytes = 0;
+  void *d_scratch = nullptr;  // K-split partial sums and arrival counters (zeroed once)
   size_t nonfinite_row = SIZE_MAX;  // first row holding an Inf/NaN block scale
   uint16_t nonfinite_bits = 0;
   GemvPlan plan{};
@@ -275,7 +276,7 @@ int matvec_sync(apx_ctx *ctx, Tensor &t, size_t n_out, size_t n_in, const int8_t
   if ((e = cudaMemcpyAsync(d + out_sz, h + out_sz, in_sz, cudaMemcpyHostToDevice,
                            ctx->stream)) != cudaSuccess)
     return cuda_err(err, e);
-  if ((e = launch_gemv(t.plan, t.type, t.d_pack, n_out, n_in,
+  if ((e = launch_gemv(t.plan, t.type, t.d_pack, t.d_scratch, n_out, n_in,
                        (const int8_t *)(d + out_sz + head + exps_sz), d + out_sz + head,
                        d + out_sz + 16, (long long *)d, nullptr,
                        (unsigned long long *)(d + out_sz), ctx->stream)) != cudaSuccess)
@@ -296,12 +297,14 @@ int matvec_sync(apx_ctx *ctx, Tensor &t, size_t n_out, size_t n_in, const int8_t
 namespace apx {
 // The launch view of an uploaded tensor, for entry points defined in other files.
 bool tensor_launch_info(apx_ctx *ctx, uint64_t handle, uint32_t *type, const uint8_t **pack,
-                        size_t *n_out, size_t *n_in, GemvPlan *plan, int *device) {
+                        void **scratch, size_t *n_out, size_t *n_in, GemvPlan *plan,
+                        int *device) {
   std::lock_guard<std::mutex> g(ctx->mu);
   Tensor *t = find(ctx, handle);
   if (!t) return false;
   *type = t->type;
   *pack = t->d_pack;
+  *scratch = t->d_scratch;
   *n_out = t->n_out;
   *n_in = t->n_in;
   *plan = t->plan;
@@ -342,7 +345,10 @@ void apx_close(apx_ctx *ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
-  for (auto &kv : ctx->tensors) cudaFree(kv.second.d_pack);
+  for (auto &kv : ctx->tensors) {
+    cudaFree(kv.second.d_pack);
+    if (kv.second.d_scratch) cudaFree(kv.second.d_scratch);
+  }
   ctx->dev.release();
   ctx->scratch.release();
   ctx->host.release();
@@ -407,6 +413,17 @@ int apx_tensor_upload(apx_ctx *ctx, uint32_t ggml_type, const uint8_t *raw, size
       return cuda_err(err, e);
     }
   }
+  const size_t sb = gemv_scratch_bytes(t.plan);
+  if (sb) {
+    if ((e = cudaMalloc(&t.d_scratch, sb)) != cudaSuccess ||
+        (e = cudaMemset(t.d_scratch, 0, sb)) != cudaSuccess) {
+      cudaFree(t.d_pack);
+      if (t.d_scratch) cudaFree(t.d_scratch);
+      set_err(err, APX_ERR_OUT_OF_MEMORY);
+      if (err) err->cuda_error = (int32_t)e;
+      return APX_ERR_OUT_OF_MEMORY;
+    }
+  }
   uint64_t h = ctx->next++;
   ctx->tensors[h] = t;
   *handle = h;
@@ -421,6 +438,7 @@ int apx_tensor_free(apx_ctx *ctx, uint64_t handle) {
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
   cudaFree(t->d_pack);
+  if (t->d_scratch) cudaFree(t->d_scratch);
   ctx->tensors.erase(handle);
   return APX_OK;
 }
@@ -549,7 +567,7 @@ int apx_matvec_f32(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in, con
     e = launch_quant_f32((const float *)(d + out_sz + 16), n_in, (int8_t *)(s + 32 + e_sz),
                          s + 32, s, ctx->stream);
   if (e == cudaSuccess)
-    e = launch_gemv(t->plan, t->type, t->d_pack, n_out, n_in, (const int8_t *)(s + 32 + e_sz),
+    e = launch_gemv(t->plan, t->type, t->d_pack, t->d_scratch, n_out, n_in, (const int8_t *)(s + 32 + e_sz),
                     s + 32, s, nullptr, (float *)d, (unsigned long long *)(d + out_sz),
                     ctx->stream);
   if (e == cudaSuccess)
@@ -630,7 +648,7 @@ int apx_matvec_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
     t = find(ctx, tensor);
   }
   if (!t || n_in != t->n_in || n_out > t->n_out) return APX_ERR_LAYOUT_MISMATCH;
-  cudaError_t e = launch_gemv(t->plan, t->type, t->d_pack, n_out, n_in, d_codes, d_exps, d_desc,
+  cudaError_t e = launch_gemv(t->plan, t->type, t->d_pack, t->d_scratch, n_out, n_in, d_codes, d_exps, d_desc,
                               (long long *)d_out_q32, d_out_f32,
                               (unsigned long long *)&d_status->first, (cudaStream_t)stream);
   return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
@@ -649,7 +667,7 @@ int apx_matmat_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in, s
   if (!t || n_in != t->n_in || n_out > t->n_out) return APX_ERR_LAYOUT_MISMATCH;
   const size_t ld = apx_act_padded_len(n_in), ldb = ld / 32;
   for (size_t c = 0; c < k_cols; c++) {
-    cudaError_t e = launch_gemv(t->plan, t->type, t->d_pack, n_out, n_in, d_codes + c * ld,
+    cudaError_t e = launch_gemv(t->plan, t->type, t->d_pack, t->d_scratch, n_out, n_in, d_codes + c * ld,
                                 d_exps + c * ldb, d_descs + c,
                                 d_out_q32 ? (long long *)d_out_q32 + c * n_out : nullptr,
                                 d_out_f32 ? d_out_f32 + c * n_out : nullptr,

@@ -300,3 +300,38 @@ def test_async_device_path_matches_sync(be):
     c, e = synth.quant_act_np(synth.f32_to_q32(x))
     want = be.matvec_q8act(t, tens, n_out, n_in, QuantAct.from_exps(e, c))
     assert np.array_equal(out.cpu().numpy(), want)
+
+
+# ---- matrices beyond one resident wave: the persistent streaming kernel --------------------
+
+@pytest.mark.parametrize("t,n_out,n_in", [
+    (Q8_0, 16384, 4096),
+    (Q8_0, 20000, 1000),    # ragged last block, padded final row tile
+    (Q4_K, 14336, 4096),
+    (Q4_K, 8200, 2304),
+    (Q6_K, 151936, 896),    # config 4 LM head, whole vocabulary
+])
+def test_streaming_shapes_exact(be, t, n_out, n_in):
+    raw = synth.payload(t, n_out, n_in, 77 + n_out)
+    c, e = synth.quant_act_np(synth.f32_to_q32(synth.activation_f32(n_in, 9)))
+    check(be, t, raw, n_out, n_in, QuantAct.from_exps(e, c))
+
+
+def test_streaming_checked_path_and_refusals(be):
+    """The streaming kernel's checked path (a wide exponent spread) and an output overflow
+    in a late row."""
+    rng = np.random.default_rng(3)
+    n_out, n_in = 8192, 4096
+    raw = synth.payload(Q4_K, n_out, n_in, 5)
+    x = rng.integers(-(1 << 20), 1 << 20, size=n_in).astype(np.int64)
+    shifts = rng.integers(0, 31, size=n_in // 32)
+    x = (x.reshape(-1, 32) << shifts[:, None].astype(np.int64)).reshape(-1)
+    check(be, Q4_K, raw, n_out, n_in, qa(x))
+    big = synth.payload(Q8_0, 16384, 4096, 6)
+    row = 12345
+    blk = big.reshape(16384, -1)[row].reshape(-1, 34)
+    blk[:, 0:2] = (0xFF, 0x7B)   # 65504 scales
+    blk[:, 2:] = 127
+    q = QuantAct.from_parts(np.full(128, 1 << 40, dtype=np.int64), np.full(4096, 127, dtype=np.int8))
+    e = check(be, Q8_0, big, 16384, 4096, q)
+    assert isinstance(e, chart.OutputOverflow)
