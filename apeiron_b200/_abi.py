@@ -27,6 +27,7 @@ APX_ERR_LAYOUT_MISMATCH = 21
 APX_ERR_CUDA = 22
 APX_ERR_OUT_OF_MEMORY = 23
 APX_ERR_TOO_LARGE = 24
+APX_ERR_DEVICE_TIMEOUT = 25
 
 Q8_0, Q4_K, Q6_K = 8, 12, 14
 EXP_ZERO = 0xFF

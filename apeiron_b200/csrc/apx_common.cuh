@@ -153,4 +153,47 @@ __device__ __forceinline__ uint2 ld_stream8(const void *p) {
   return v;
 }
 
+// ---- TMA bulk copies into shared memory, completion on an mbarrier --------------------------
+// One-dimensional bulk copies (cp.async.bulk, no tensor map, no multicast): 16-byte aligned
+// addresses, sizes a multiple of 16.  Waits are bounded: a wait that gives up reports
+// APX_ERR_DEVICE_TIMEOUT through the call's refusal word instead of spinning forever.
+
+constexpr int kWaitLimit = 1 << 22;  // try_wait rounds before a wait gives up
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes,
+                                         uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Wait for phase `parity` of the barrier; false if the bounded wait gave up.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t done = 0;
+  for (int it = 0; it < kWaitLimit && !done; it++)
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+  return done != 0;
+}
+
 }  // namespace apx

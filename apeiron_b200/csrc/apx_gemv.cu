@@ -4,17 +4,20 @@
 // w the Q32.32 dequantized weight and x̂_i = S_b·xq_i, i.e. `matvec_fixed(W, dequant(q))`
 // (src/engine/ops/matvec.rs:149-222), bit for bit, with the same refusals.
 //
-// Layout in HBM.  At upload each tensor is regrouped once into units of 32 rows (one row per
-// lane) × one K-slice: 4 Q8_0 blocks, or one Q4_K / Q6_K super-block.  Inside a unit the
-// 16-byte chunk c of lane l sits at (c*32 + l)*16, so every warp-wide 16-byte load reads 512
-// contiguous bytes; the per-row block headers follow the chunks.  The bytes are the GGUF
-// bytes, only their positions change (format/quant.rs:52-68 block layouts).
+// Layout in HBM.  At upload each tensor is regrouped once into units of 32 lanes.  A K-slot
+// is 4 Q8_0 blocks or one Q4_K / Q6_K super-block; lane l of unit (rt, j) holds row
+// rt·H + l/L, K-slot j·L + l%L, where L (1, 2 or 4) lanes share a row and H = 32/L rows
+// form a row tile.  Inside a unit the 16-byte chunk c of lane l sits at (c*32 + l)*16, so
+// every warp-wide 16-byte load reads 512 contiguous bytes; the per-row block headers follow
+// the chunks.  The bytes are the GGUF bytes, only their positions change (format/quant.rs:
+// 52-68 block layouts).  L > 1 is chosen for few, long rows (down projections), so a row's
+// K-slots spread over lanes instead of over CTAs.
 //
-// Work.  One warp streams one unit: lane l owns row 32*rt + l and accumulates its exact
-// contribution in a 128-bit integer (apx_common.cuh).  The activation codes of the CTA's
-// K-range live in shared memory and are read as warp-wide broadcasts.  Units of one row tile
-// are spread over the warps of a CTA and, for long rows, over the CTAs of a thread-block
-// cluster; partial sums meet in shared memory and then through distributed shared memory.
+// Work.  One warp folds one unit: each lane accumulates its slot of its row exactly in a
+// 128-bit integer (apx_common.cuh); the L lanes of a row combine by shuffles, the warps of a
+// row tile in shared memory.  Matrices that fit one resident wave use one unit per warp
+// (every load in flight at once); larger ones use a persistent kernel in which each warp
+// streams a contiguous chunk of units with one unit of prefetch.
 //
 // Exactness.  The kernels run when every partial sum is provably inside i128 (the reference's
 // call-level bound q8act_fast_bound_ok, chart/mod.rs:362-383, evaluated from the largest
@@ -29,59 +32,6 @@
 
 namespace apx {
 
-// ---- upload-time repack ----------------------------------------------------------------
-
-__global__ void repack_kernel(const uint8_t *__restrict__ raw, uint8_t *__restrict__ pack,
-                              uint32_t type, size_t n_out, size_t row_bytes, int units,
-                              int nblk, size_t total) {
-  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
-       idx += (size_t)gridDim.x * blockDim.x) {
-    int unit_bytes = type == kQ8_0 ? kUnitQ8_0 : (type == kQ4_K ? kUnitQ4_K : kUnitQ6_K);
-    size_t unit = idx / unit_bytes;
-    int off = (int)(idx % unit_bytes);
-    size_t rt = unit / units;
-    int u = (int)(unit % units);
-    int lane, blk;
-    size_t src;  // byte offset inside the row
-    if (type == kQ8_0) {
-      if (off < 4096) {
-        int c = off / 512, i = off % 16;
-        lane = (off / 16) % 32;
-        blk = 4 * u + c / 2;
-        src = (size_t)blk * 34 + 2 + 16 * (c % 2) + i;
-      } else {
-        int o2 = off - 4096;
-        lane = o2 / 8;
-        blk = 4 * u + (o2 % 8) / 2;
-        src = (size_t)blk * 34 + (o2 % 2);
-      }
-    } else if (type == kQ4_K) {
-      blk = u;
-      if (off < 4096) {
-        lane = (off / 16) % 32;
-        src = (size_t)u * 144 + 16 + 16 * (off / 512) + off % 16;
-      } else {
-        lane = (off - 4096) / 16;
-        src = (size_t)u * 144 + (off - 4096) % 16;
-      }
-    } else {
-      blk = u;
-      if (off < 6144) {
-        lane = (off / 16) % 32;
-        src = (size_t)u * 210 + 16 * (off / 512) + off % 16;
-      } else if (off < 6656) {
-        lane = (off - 6144) / 16;
-        src = (size_t)u * 210 + 192 + (off - 6144) % 16;
-      } else {
-        lane = (off - 6656) / 2;
-        src = (size_t)u * 210 + 208 + (off - 6656) % 2;
-      }
-    }
-    size_t row = rt * 32 + lane;
-    pack[idx] = (row < n_out && blk < nblk) ? raw[row * row_bytes + src] : (uint8_t)0;
-  }
-}
-
 // ---- family traits ---------------------------------------------------------------------
 
 template <uint32_t T>
@@ -89,10 +39,11 @@ struct Fam;
 
 template <>
 struct Fam<kQ8_0> {
-  static constexpr int span = 128;  // activation elements per unit
+  static constexpr int span = 128;  // activation elements per K-slot
   static constexpr int unit_bytes = kUnitQ8_0;
   static constexpr int es_limit = 1 << 30;  // no spread limit: per-block i128 terms
   static constexpr long long top = 128;    // chart/mod.rs:1697
+  static constexpr int nxs = 4;            // Σxq entries per K-slot (unused)
 };
 template <>
 struct Fam<kQ4_K> {
@@ -100,6 +51,7 @@ struct Fam<kQ4_K> {
   static constexpr int unit_bytes = kUnitQ4_K;
   static constexpr int es_limit = 23;
   static constexpr long long top = 1008;  // chart/mod.rs:1703
+  static constexpr int nxs = 8;           // per 32 lanes
 };
 template <>
 struct Fam<kQ6_K> {
@@ -107,7 +59,18 @@ struct Fam<kQ6_K> {
   static constexpr int unit_bytes = kUnitQ6_K;
   static constexpr int es_limit = 22;
   static constexpr long long top = 4096;  // chart/mod.rs:1706
+  static constexpr int nxs = 16;          // per 16 lanes
 };
+
+static __host__ __device__ int unit_bytes_of(uint32_t t) {
+  return t == kQ8_0 ? kUnitQ8_0 : (t == kQ4_K ? kUnitQ4_K : kUnitQ6_K);
+}
+
+// K-slots per row: Q8_0 counts quads of 32-lane blocks, the k-quants super-blocks.
+int units_per_row_tile(uint32_t type, size_t n_in) {
+  if (type == kQ8_0) return (int)((((n_in + 31) / 32) + 3) / 4);
+  return (int)((n_in + 255) / 256);
+}
 
 // The call-level bound of q8act_fast_bound_ok (chart/mod.rs:362-383):
 // n_in·(65504·2^32)·top·127·S_max < 2^127 with S_max = 2^emax, decided exactly.
@@ -119,6 +82,80 @@ __device__ __forceinline__ bool bound_ok(long long n_in, long long top, int emax
   if (room <= 0) return false;
   if (room >= 64) return true;
   return P < (1ull << room);
+}
+
+// Where row `row`'s K-slot `slot` lives: the unit's first byte and the lane inside it.
+struct PackGeo {
+  const uint8_t *pack;
+  int units;  // units per row tile (K-slots / L, rounded up)
+  int L;      // lanes per row
+};
+
+__host__ __device__ __forceinline__ const uint8_t *slot_unit(const PackGeo &g, uint32_t type,
+                                                             size_t row, size_t slot,
+                                                             int &lane) {
+  const int H = 32 / g.L;
+  const size_t rt = row / H;
+  lane = (int)(row % H) * g.L + (int)(slot % g.L);
+  return g.pack + (rt * g.units + slot / g.L) * (size_t)unit_bytes_of(type);
+}
+
+// ---- upload-time repack ----------------------------------------------------------------
+
+__global__ void repack_kernel(const uint8_t *__restrict__ raw, uint8_t *__restrict__ pack,
+                              uint32_t type, size_t n_out, size_t row_bytes, int units, int L,
+                              int kslots, int nblk, size_t total) {
+  const int H = 32 / L;
+  const int unit_bytes = unit_bytes_of(type);
+  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (size_t)gridDim.x * blockDim.x) {
+    const size_t unit = idx / unit_bytes;
+    const int off = (int)(idx % unit_bytes);
+    const size_t rt = unit / units;
+    const int j = (int)(unit % units);
+    int lane, within;  // lane, and byte offset inside that lane's K-slot of the GGUF row
+    if (type == kQ8_0) {
+      if (off < 4096) {
+        lane = (off / 16) % 32;
+        const int c = off / 512;  // block c/2 of the slot, half c%2
+        within = (c / 2) * 34 + 2 + 16 * (c % 2) + off % 16;
+      } else {
+        lane = (off - 4096) / 8;
+        within = ((off - 4096) % 8 / 2) * 34 + (off - 4096) % 2;
+      }
+    } else if (type == kQ4_K) {
+      if (off < 4096) {
+        lane = (off / 16) % 32;
+        within = 16 + 16 * (off / 512) + off % 16;
+      } else {
+        lane = (off - 4096) / 16;
+        within = (off - 4096) % 16;
+      }
+    } else {
+      if (off < 6144) {
+        lane = (off / 16) % 32;
+        within = 16 * (off / 512) + off % 16;
+      } else if (off < 6656) {
+        lane = (off - 6144) / 16;
+        within = 192 + (off - 6144) % 16;
+      } else {
+        lane = (off - 6656) / 2;
+        within = 208 + (off - 6656) % 2;
+      }
+    }
+    const size_t row = rt * H + lane / L;
+    const int slot = j * L + lane % L;
+    bool valid = row < n_out && slot < kslots;
+    size_t src = 0;
+    if (type == kQ8_0) {
+      const int blk = 4 * slot + within / 34;
+      valid = valid && blk < nblk;
+      src = (size_t)slot * 4 * 34 + within;
+    } else {
+      src = (size_t)slot * (type == kQ4_K ? 144 : 210) + within;
+    }
+    pack[idx] = valid ? raw[row * row_bytes + src] : (uint8_t)0;
+  }
 }
 
 // ---- per-unit exact accumulation ---------------------------------------------------------
@@ -159,6 +196,25 @@ __device__ __forceinline__ void load_unit(UnitRegs<kQ6_K> &w, const uint8_t *ub,
   for (int c = 0; c < 12; c++) w.q[c] = ld_stream(ub + (c * 32 + lane) * 16);
   w.sc = ld_stream(ub + 6144 + lane * 16);
   asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(w.d) : "l"(ub + 6656 + lane * 2));
+}
+
+// The same registers from a unit already staged in shared memory.
+__device__ __forceinline__ void load_unit_smem(UnitRegs<kQ8_0> &w, const uint8_t *ub, int lane) {
+#pragma unroll
+  for (int c = 0; c < 8; c++) w.q[c] = *reinterpret_cast<const uint4 *>(ub + (c * 32 + lane) * 16);
+  w.s = *reinterpret_cast<const uint2 *>(ub + 4096 + lane * 8);
+}
+__device__ __forceinline__ void load_unit_smem(UnitRegs<kQ4_K> &w, const uint8_t *ub, int lane) {
+#pragma unroll
+  for (int c = 0; c < 8; c++) w.q[c] = *reinterpret_cast<const uint4 *>(ub + (c * 32 + lane) * 16);
+  w.h = *reinterpret_cast<const uint4 *>(ub + 4096 + lane * 16);
+}
+__device__ __forceinline__ void load_unit_smem(UnitRegs<kQ6_K> &w, const uint8_t *ub, int lane) {
+#pragma unroll
+  for (int c = 0; c < 12; c++)
+    w.q[c] = *reinterpret_cast<const uint4 *>(ub + (c * 32 + lane) * 16);
+  w.sc = *reinterpret_cast<const uint4 *>(ub + 6144 + lane * 16);
+  w.d = *reinterpret_cast<const unsigned short *>(ub + 6656 + lane * 2);
 }
 
 __device__ __forceinline__ void fold_unit(Acc128 &acc, const UnitRegs<kQ8_0> &w, const int *a,
@@ -273,30 +329,30 @@ __device__ __forceinline__ void fold_unit(Acc128 &acc, const UnitRegs<kQ6_K> &wr
 
 // ---- checked path: matvec_fixed in element order ------------------------------------------
 
-// Exact Q32.32 weight of element i of the row held by `lane` in row tile `rt`
-// (dequant_row_fixed, src/engine/num/dequant.rs:311-640, from the repacked bytes).
+// Exact Q32.32 weight of element i of `row` (dequant_row_fixed, src/engine/num/dequant.rs:
+// 311-640, read from the repacked bytes).
 template <uint32_t T>
-__device__ long long weight_at(const uint8_t *pack, int units, size_t rt, int lane, size_t i) {
+__device__ long long weight_at(const PackGeo &g, size_t row, size_t i) {
+  int lane;
   if (T == kQ8_0) {
-    size_t b = i / 32;
-    const uint8_t *ub = pack + (rt * units + b / 4) * (size_t)kUnitQ8_0;
-    int bi = (int)(b % 4), qi = (int)(i % 32);
-    int c = 2 * bi + qi / 16;
-    signed char code = (signed char)ub[(c * 32 + lane) * 16 + qi % 16];
-    unsigned bits = ub[4096 + lane * 8 + 2 * bi] | (ub[4096 + lane * 8 + 2 * bi + 1] << 8);
+    const uint8_t *ub = slot_unit(g, T, row, i / 128, lane);
+    const int bi = (int)(i % 128) / 32, qi = (int)(i % 32);
+    const int c = 2 * bi + qi / 16;
+    const signed char code = (signed char)ub[(c * 32 + lane) * 16 + qi % 16];
+    const unsigned bits = ub[4096 + lane * 8 + 2 * bi] | (ub[4096 + lane * 8 + 2 * bi + 1] << 8);
     int m;
     unsigned k;
     f16_split(bits, m, k);
     return ((long long)m << k) * code;
   } else if (T == kQ4_K) {
-    size_t s = i / 256;
-    int p = (int)(i % 256);
-    const uint8_t *ub = pack + (rt * units + s) * (size_t)kUnitQ4_K;
-    int wb = 32 * (p / 64) + p % 32;
-    unsigned byte = ub[((wb / 16) * 32 + lane) * 16 + wb % 16];
-    unsigned code = (p % 64) < 32 ? (byte & 0xF) : (byte >> 4);
+    const uint8_t *ub = slot_unit(g, T, row, i / 256, lane);
+    const int p = (int)(i % 256);
+    const int wb = 32 * (p / 64) + p % 32;
+    const unsigned byte = ub[((wb / 16) * 32 + lane) * 16 + wb % 16];
+    const unsigned code = (p % 64) < 32 ? (byte & 0xF) : (byte >> 4);
     const uint8_t *hd = ub + 4096 + lane * 16;
-    int j = p / 32, sc, mn;
+    const int j = p / 32;
+    int sc, mn;
     if (j < 4) {
       sc = hd[4 + j] & 63;
       mn = hd[4 + j + 4] & 63;
@@ -308,20 +364,19 @@ __device__ long long weight_at(const uint8_t *pack, int units, size_t rt, int la
     unsigned kd, km;
     f16_split(hd[0] | (hd[1] << 8), md, kd);
     f16_split(hd[2] | (hd[3] << 8), mm, km);
-    long long d = (long long)md << kd, dmin = (long long)mm << km;
+    const long long d = (long long)md << kd, dmin = (long long)mm << km;
     return (d * sc) * (long long)code - dmin * mn;
   } else {
-    size_t s = i / 256;
-    int p = (int)(i % 256);
-    const uint8_t *ub = pack + (rt * units + s) * (size_t)kUnitQ6_K;
-    int n = p / 128, r = p % 128, quarter = r / 32, l = r % 32;
-    int qlb = 64 * n + l + ((quarter & 1) ? 32 : 0);
-    int qhb = 128 + 32 * n + l;
-    unsigned qlv = ub[((qlb / 16) * 32 + lane) * 16 + qlb % 16];
-    unsigned qhv = ub[((qhb / 16) * 32 + lane) * 16 + qhb % 16];
-    unsigned lo = quarter < 2 ? (qlv & 0xF) : (qlv >> 4);
-    int code = (int)(lo | (((qhv >> (2 * quarter)) & 3) << 4)) - 32;
-    int sc = (int)(signed char)ub[6144 + lane * 16 + p / 16];
+    const uint8_t *ub = slot_unit(g, T, row, i / 256, lane);
+    const int p = (int)(i % 256);
+    const int n = p / 128, r = p % 128, quarter = r / 32, l = r % 32;
+    const int qlb = 64 * n + l + ((quarter & 1) ? 32 : 0);
+    const int qhb = 128 + 32 * n + l;
+    const unsigned qlv = ub[((qlb / 16) * 32 + lane) * 16 + qlb % 16];
+    const unsigned qhv = ub[((qhb / 16) * 32 + lane) * 16 + qhb % 16];
+    const unsigned lo = quarter < 2 ? (qlv & 0xF) : (qlv >> 4);
+    const int code = (int)(lo | (((qhv >> (2 * quarter)) & 3) << 4)) - 32;
+    const int sc = (int)(signed char)ub[6144 + lane * 16 + p / 16];
     int md;
     unsigned kd;
     f16_split(ub[6656 + lane * 2] | (ub[6656 + lane * 2 + 1] << 8), md, kd);
@@ -341,21 +396,19 @@ __device__ __forceinline__ bool add_checked(Acc128 &a, long long plo, long long 
 }
 
 template <uint32_t T>
-__device__ __noinline__ void checked_rows(const uint8_t *pack, int units, size_t rt, int lane,
-                                          size_t n_out, size_t n_in, const int8_t *codes,
-                                          const uint8_t *exps, long long *out_q32,
-                                          float *out_f32, unsigned long long *status) {
-  size_t row = rt * 32 + lane;
+__device__ __noinline__ void checked_row(const PackGeo &g, size_t row, size_t n_out, size_t n_in,
+                                         const int8_t *codes, const uint8_t *exps,
+                                         long long *out_q32, float *out_f32,
+                                         unsigned long long *status) {
   if (row >= n_out) return;
   Acc128 acc;
   acc_zero(acc);
   for (size_t i = 0; i < n_in; i++) {
-    unsigned e = exps[i / 32];
-    long long x = e == APX_EXP_ZERO ? 0 : (long long)codes[i] << e;  // fits: desc checked
-    long long w = weight_at<T>(pack, units, rt, lane, i);
-    long long plo = w * x;                          // low 64 bits of the exact product
-    long long phi = __mul64hi(w, x);                // high 64 bits
-    if (!add_checked(acc, plo, phi)) {
+    const unsigned e = exps[i / 32];
+    // S·xq fits i64: the descriptor refused every activation where it does not
+    const long long x = e == APX_EXP_ZERO ? 0 : (long long)codes[i] * (1ll << e);
+    const long long w = weight_at<T>(g, row, i);
+    if (!add_checked(acc, w * x, __mul64hi(w, x))) {
       atomicMin(status, pack_status(row, kKindAccOverflow, 0));
       return;
     }
@@ -369,12 +422,105 @@ __device__ __noinline__ void checked_rows(const uint8_t *pack, int units, size_t
   if (out_f32) out_f32[row] = __ll2float_rn(v) * 2.3283064365386963e-10f;
 }
 
-// ---- the projection kernel --------------------------------------------------------------
+__device__ __forceinline__ void finish_row(const Acc128 &s, size_t row, size_t n_out,
+                                           long long *out_q32, float *out_f32,
+                                           unsigned long long *status) {
+  if (row >= n_out) return;
+  long long v;
+  if (!acc_round_to_i64(s, v)) {
+    atomicMin(status, pack_status(row, kKindOutputOverflow, 0));
+  } else {
+    if (out_q32) out_q32[row] = v;
+    if (out_f32) out_f32[row] = __ll2float_rn(v) * 2.3283064365386963e-10f;
+  }
+}
+
+// Programmatic dependent launch: the next projection may start streaming its (constant)
+// weights as soon as every CTA of this one is running; it waits for this grid's completion
+// before it reads anything this grid or an earlier kernel writes.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <uint32_t T>
+__device__ __forceinline__ bool fast_path(const ActDesc &desc, size_t n_in) {
+  const int es = desc.emax >= 0 ? desc.emax - desc.emin : 0;
+  return bound_ok((long long)n_in, Fam<T>::top, desc.emax) && es <= Fam<T>::es_limit &&
+         !(desc.pad[0] & 1u);  // pad[0] bit 0: a code of -128 is present
+}
+
+// ---- activation staging --------------------------------------------------------------------
+// A warp stages the activation of the L K-slots its unit covers: int8 codes (zero for a
+// zero-scale block or past n_in), and per 32-lane block the exponent data and Σxq the
+// family's fold reads.  Lanes load 16-byte chunks; slot s of the unit is chunks
+// [s·span/16, (s+1)·span/16).
+
+template <uint32_t T>
+struct WarpAct {
+  int codes[4 * Fam<T>::span / 4];
+  int e[4 * Fam<T>::span / 32];  // Q8_0: absolute exponent or -1; k-quants: er
+  long long xs[4 * Fam<T>::nxs];
+};
+
+struct Chunk {
+  uint4 v;
+  unsigned e;
+};
+
+// Chunk c of the activation whose first element is k_first (16 elements).
+__device__ __forceinline__ Chunk load_chunk(const int8_t *codes, const uint8_t *exps,
+                                            size_t n_in, size_t j) {
+  Chunk s{make_uint4(0, 0, 0, 0), APX_EXP_ZERO};
+  if (j < n_in) {
+    s.e = exps[j / 32];
+    if (j + 16 <= n_in && ((reinterpret_cast<uintptr_t>(codes + j) & 15) == 0)) {
+      s.v = __ldg(reinterpret_cast<const uint4 *>(codes + j));
+    } else {
+      unsigned t[4] = {0, 0, 0, 0};
+      for (int i = 0; i < 16; i++)
+        if (j + i < n_in) t[i / 4] |= ((unsigned)(uint8_t)codes[j + i]) << (8 * (i % 4));
+      s.v = make_uint4(t[0], t[1], t[2], t[3]);
+    }
+  }
+  return s;
+}
+
+// Stage chunk c (of the staged region) with its sums; every lane of the warp calls this
+// for the same c-round (the pair sum is a shuffle).
+template <uint32_t T>
+__device__ __forceinline__ void store_chunk(WarpAct<T> &w, Chunk s, int c, bool in, int emin) {
+  const bool zero = s.e == APX_EXP_ZERO;
+  const uint4 v = zero ? make_uint4(0, 0, 0, 0) : s.v;
+  const int er = zero ? 0 : (int)s.e - emin;
+  int s16 = dp4a_ss((int)v.x, 0x01010101, 0);
+  s16 = dp4a_ss((int)v.y, 0x01010101, s16);
+  s16 = dp4a_ss((int)v.z, 0x01010101, s16);
+  s16 = dp4a_ss((int)v.w, 0x01010101, s16);
+  const int s32 = s16 + __shfl_xor_sync(0xFFFFFFFFu, s16, 1);
+  if (!in) return;
+  reinterpret_cast<uint4 *>(w.codes)[c] = v;
+  if (T == kQ6_K) w.xs[c] = (long long)s16 << er;
+  if ((c & 1) == 0) {
+    w.e[c / 2] = T == kQ8_0 ? (zero ? -1 : (int)s.e) : er;
+    if (T == kQ4_K) w.xs[c / 2] = (long long)s32 << er;
+  }
+}
+
+// Elements of chunk c of unit j (K-slots j·L .. j·L+L-1).
+template <uint32_t T>
+__device__ __forceinline__ size_t chunk_first(int j, int L, int c) {
+  constexpr int per = Fam<T>::span / 16;
+  return ((size_t)j * L + c / per) * Fam<T>::span + 16 * (size_t)(c % per);
+}
+
+// ---- the one-wave kernel --------------------------------------------------------------------
 
 struct GemvArgs {
   const uint8_t *pack;
   int units;        // units per row tile
-  size_t n_rt;      // row tiles
+  int L;            // lanes per row
+  size_t n_rt;      // row tiles (of 32/L rows)
   size_t n_out, n_in;
   const int8_t *codes;
   const uint8_t *exps;
@@ -385,87 +531,11 @@ struct GemvArgs {
   Acc128 *partials;     // [n_rt][ksplit][32] partial sums of a K-split row tile
   unsigned *counters;   // [n_rt] arrivals of a K-split row tile (self-resetting)
   int R, P, ksplit;     // row tiles per CTA, warps per row tile, CTAs per row tile along K
-};
-
-// Programmatic dependent launch: the next projection may start streaming its (constant)
-// weights as soon as every CTA of this one is running; it waits for this grid's completion
-// before it reads anything this grid or an earlier kernel writes.
-__device__ __forceinline__ void pdl_launch_dependents() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
-// Per-warp activation staging of one unit: its int8 codes (zero for a zero-scale block or
-// past n_in), and per 32-lane block the exponent data and Σxq the family's fold reads.
-template <uint32_t T>
-struct WarpAct {
-  int codes[Fam<T>::span / 4];
-  int e[Fam<T>::span / 32];                     // Q8_0: absolute exponent or -1; else er
-  long long xs[T == kQ6_K ? 16 : Fam<T>::span / 32];  // Σxq·2^er (per 16 lanes for Q6_K)
-};
-
-// The raw activation bytes a lane stages for unit u: 16 codes and their block's exponent,
-// loaded together (one round trip) right after the dependency wait.
-struct StageRegs {
-  uint4 v;
-  unsigned e;
+  int act_bytes;        // shared bytes of the activation staging / partial sums
 };
 
 template <uint32_t T>
-__device__ __forceinline__ StageRegs stage_load(const int8_t *codes, const uint8_t *exps,
-                                                size_t n_in, int u, int lane) {
-  constexpr int span = Fam<T>::span;
-  StageRegs s{make_uint4(0, 0, 0, 0), APX_EXP_ZERO};
-  if (lane < span / 16) {
-    const size_t j = (size_t)u * span + 16 * lane;
-    const size_t b = j / 32;
-    if (j < n_in) {
-      s.e = exps[b];
-      if (j + 16 <= n_in && ((reinterpret_cast<uintptr_t>(codes + j) & 15) == 0)) {
-        s.v = __ldg(reinterpret_cast<const uint4 *>(codes + j));
-      } else {
-        unsigned t[4] = {0, 0, 0, 0};
-        for (int i = 0; i < 16; i++)
-          if (j + i < n_in) t[i / 4] |= ((unsigned)(uint8_t)codes[j + i]) << (8 * (i % 4));
-        s.v = make_uint4(t[0], t[1], t[2], t[3]);
-      }
-    }
-  }
-  return s;
-}
-
-template <uint32_t T>
-__device__ __forceinline__ void stage_store(WarpAct<T> &w, StageRegs s, int emin, int lane) {
-  constexpr int span = Fam<T>::span;
-  const bool zero = s.e == APX_EXP_ZERO;
-  const uint4 v = zero ? make_uint4(0, 0, 0, 0) : s.v;
-  const int er = zero ? 0 : (int)s.e - emin;
-  const int eabs = zero ? -1 : (int)s.e;
-  if (lane < span / 16) reinterpret_cast<uint4 *>(w.codes)[lane] = v;
-  // Σ of this lane's 16 codes, then the 32-lane block's sum across the lane pair
-  int s16 = dp4a_ss((int)v.x, 0x01010101, 0);
-  s16 = dp4a_ss((int)v.y, 0x01010101, s16);
-  s16 = dp4a_ss((int)v.z, 0x01010101, s16);
-  s16 = dp4a_ss((int)v.w, 0x01010101, s16);
-  const int s32 = s16 + __shfl_xor_sync(0xFFFFFFFFu, s16, 1);
-  if (lane < span / 16) {
-    if (T == kQ6_K) w.xs[lane] = (long long)s16 << er;
-    if ((lane & 1) == 0) {
-      w.e[lane / 2] = T == kQ8_0 ? eabs : er;
-      if (T == kQ4_K) w.xs[lane / 2] = (long long)s32 << er;
-    }
-  }
-  __syncwarp();
-}
-
-template <uint32_t T>
-__device__ __forceinline__ void fold(Acc128 &acc, const UnitRegs<T> &r, const WarpAct<T> &w,
-                                     int emin) {
-  fold_unit(acc, r, w.codes, w.e, w.xs, emin);
-}
-
-template <uint32_t T, bool PIPE>
-__global__ void __launch_bounds__(PIPE ? 256 : 512) gemv_kernel(GemvArgs g) {
+__global__ void __launch_bounds__(384, 2) gemv_kernel(GemvArgs g) {
   extern __shared__ __align__(16) unsigned char smem[];
   using F = Fam<T>;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -477,51 +547,53 @@ __global__ void __launch_bounds__(PIPE ? 256 : 512) gemv_kernel(GemvArgs g) {
   const size_t rt = rt0 + r;
   const bool active = r < g.R && rt < g.n_rt;
   const uint8_t *base = g.pack + rt * (size_t)g.units * F::unit_bytes;
+  const int L = g.L, H = 32 / L, slot = lane % L;
+  const int nch = L * F::span / 16;  // chunks staged per unit: 8, 16, 32 or 64
 
   pdl_launch_dependents();
-  // weights first: they depend on nothing the previous kernel writes
+  // weights first, straight into registers: they depend on nothing the previous kernel
+  // writes, and the plan gives every warp at most one unit (k1 - k0 <= P)
   UnitRegs<T> cur;
   const bool first = active && k0 + p < k1;
   if (first) load_unit(cur, base + (size_t)(k0 + p) * F::unit_bytes, lane);
   pdl_wait();
 
-  // the descriptor and the first unit's activation bytes in one round trip
+  // the descriptor and this warp's activation chunks in one round trip
   const ActDesc desc = *g.desc;
-  StageRegs sr = first ? stage_load<T>(g.codes, g.exps, g.n_in, k0 + p, lane)
-                       : StageRegs{make_uint4(0, 0, 0, 0), APX_EXP_ZERO};
+  Chunk ch0 = {make_uint4(0, 0, 0, 0), APX_EXP_ZERO}, ch1 = ch0;
+  if (first) {
+    if (lane < nch) ch0 = load_chunk(g.codes, g.exps, g.n_in, chunk_first<T>(k0 + p, L, lane));
+    if (lane + 32 < nch)
+      ch1 = load_chunk(g.codes, g.exps, g.n_in, chunk_first<T>(k0 + p, L, lane + 32));
+  }
   if (desc.status != APX_OK) {  // the activation itself is refused (chart/mod.rs:1904-1907)
     if (blockIdx.x == 0 && threadIdx.x == 0)
       atomicMin(g.status, pack_status(0, (unsigned)desc.status, 0));
     return;
   }
-  const int es = desc.emax >= 0 ? desc.emax - desc.emin : 0;
-  const bool fast = bound_ok((long long)g.n_in, F::top, desc.emax) && es <= F::es_limit &&
-                    !(desc.pad[0] & 1u);  // pad[0] bit 0: a code of -128 is present
-  if (!fast) {
-    if (ks == 0 && p == 0 && active)
-      checked_rows<T>(g.pack, g.units, rt, lane, g.n_out, g.n_in, g.codes, g.exps, g.out_q32,
-                      g.out_f32, g.status);
+  if (!fast_path<T>(desc, g.n_in)) {
+    if (ks == 0 && p == 0 && active && slot == 0)
+      checked_row<T>(PackGeo{g.pack, g.units, L}, rt * H + lane / L, g.n_out, g.n_in, g.codes,
+                     g.exps, g.out_q32, g.out_f32, g.status);
     return;
   }
 
-  // -- stream the units: each warp stages its unit's activation and folds its registers ---
-  WarpAct<T> *wact = reinterpret_cast<WarpAct<T> *>(smem) + warp;
+  // -- fold this warp's unit ------------------------------------------------------------------
+  WarpAct<T> *w = reinterpret_cast<WarpAct<T> *>(smem) + warp;
   Acc128 acc;
   acc_zero(acc);
-  if (active) {
-    for (int u = k0 + p; u < k1; u += g.P) {
-      UnitRegs<T> nxt;
-      const bool more = u + g.P < k1;
-      if (PIPE && more) load_unit(nxt, base + (size_t)(u + g.P) * F::unit_bytes, lane);
-      if (!PIPE && u != k0 + p) load_unit(cur, base + (size_t)u * F::unit_bytes, lane);
-      if (u != k0 + p) {
-        __syncwarp();  // the previous unit's reads of the staging are done
-        sr = stage_load<T>(g.codes, g.exps, g.n_in, u, lane);
-      }
-      stage_store<T>(*wact, sr, desc.emin, lane);
-      fold<T>(acc, cur, *wact, desc.emin);
-      if (PIPE && more) cur = nxt;
-    }
+  if (first) {
+    store_chunk<T>(*w, ch0, lane, lane < nch, desc.emin);
+    if (nch > 32) store_chunk<T>(*w, ch1, lane + 32, lane + 32 < nch, desc.emin);
+    __syncwarp();
+    fold_unit(acc, cur, w->codes + slot * (F::span / 4), w->e + slot * (F::span / 32),
+              w->xs + slot * F::nxs, desc.emin);
+  }
+  // the L lanes of a row combine
+  for (int o = 1; o < L; o <<= 1) {
+    const unsigned long long lo = __shfl_xor_sync(0xFFFFFFFFu, acc.lo, o);
+    const unsigned long long hi = __shfl_xor_sync(0xFFFFFFFFu, acc.hi, o);
+    acc_add(acc, lo, hi);
   }
 
   // -- reduce: warps of a row tile in shared memory, CTAs of a row tile through scratch ----
@@ -540,9 +612,9 @@ __global__ void __launch_bounds__(PIPE ? 256 : 512) gemv_kernel(GemvArgs g) {
     // last-arriving CTA of the row tile sums the others' partials (threadfence reduction)
     unsigned *ticket = reinterpret_cast<unsigned *>(part + g.R * g.P * 32);
     if (p == 0 && active) {
-      Acc128 *slot = g.partials + (rt * g.ksplit + ks) * 32 + lane;
-      slot->lo = s.lo;
-      slot->hi = s.hi;
+      Acc128 *dst = g.partials + (rt * g.ksplit + ks) * 32 + lane;
+      dst->lo = s.lo;
+      dst->hi = s.hi;
       __threadfence();
     }
     __syncthreads();
@@ -562,26 +634,16 @@ __global__ void __launch_bounds__(PIPE ? 256 : 512) gemv_kernel(GemvArgs g) {
       if (lane == 0) g.counters[rt] = 0u;  // ready for the next call
     }
   }
-  if (finalize && p == 0 && active) {
-    const size_t row = rt * 32 + lane;
-    if (row < g.n_out) {
-      long long v;
-      if (!acc_round_to_i64(s, v)) {
-        atomicMin(g.status, pack_status(row, kKindOutputOverflow, 0));
-      } else {
-        if (g.out_q32) g.out_q32[row] = v;
-        if (g.out_f32) g.out_f32[row] = __ll2float_rn(v) * 2.3283064365386963e-10f;
-      }
-    }
-  }
+  if (finalize && p == 0 && active && slot == 0)
+    finish_row(s, rt * H + lane / L, g.n_out, g.out_q32, g.out_f32, g.status);
 }
 
 // ---- streaming kernel for matrices larger than one resident wave ---------------------------
 //
-// Persistent: V = gridDim.x × warps-per-CTA warps, warp v streams the contiguous unit chunk
-// [v·C, (v+1)·C) of the (row tile, K unit) order, C = ceil(T/V), folding one unit while the
-// next is in flight.  The CTA stages the whole activation once.  A row tile covered by one
-// warp is finished by it; a row tile split between warps is finished by whichever of them
+// Persistent (L = 1): V = gridDim.x × warps-per-CTA warps, warp v streams the contiguous unit
+// chunk [v·C, (v+1)·C) of the (row tile, K unit) order, C = ceil(T/V), folding one unit while
+// the next is in flight.  The CTA stages the whole activation once.  A row tile covered by
+// one warp is finished by it; a row tile split between warps is finished by whichever of them
 // arrives last (partial sums in the tensor's scratch, an arrival counter that resets itself).
 
 struct StreamArgs {
@@ -601,20 +663,6 @@ struct StreamArgs {
 };
 
 template <uint32_t T>
-__device__ __forceinline__ void finish_row(const Acc128 &s, size_t row, size_t n_out,
-                                           long long *out_q32, float *out_f32,
-                                           unsigned long long *status) {
-  if (row >= n_out) return;
-  long long v;
-  if (!acc_round_to_i64(s, v)) {
-    atomicMin(status, pack_status(row, kKindOutputOverflow, 0));
-  } else {
-    if (out_q32) out_q32[row] = v;
-    if (out_f32) out_f32[row] = __ll2float_rn(v) * 2.3283064365386963e-10f;
-  }
-}
-
-template <uint32_t T>
 __global__ void __launch_bounds__(256, 2) gemv_stream_kernel(StreamArgs g) {
   extern __shared__ __align__(16) unsigned char smem[];
   using F = Fam<T>;
@@ -625,8 +673,7 @@ __global__ void __launch_bounds__(256, 2) gemv_stream_kernel(StreamArgs g) {
 
   pdl_launch_dependents();
   UnitRegs<T> cur;
-  if (x0 < x1)
-    load_unit(cur, g.pack + (size_t)x0 * F::unit_bytes, lane);
+  if (x0 < x1) load_unit(cur, g.pack + (size_t)x0 * F::unit_bytes, lane);
   pdl_wait();
 
   const ActDesc desc = *g.desc;
@@ -635,15 +682,12 @@ __global__ void __launch_bounds__(256, 2) gemv_stream_kernel(StreamArgs g) {
       atomicMin(g.status, pack_status(0, (unsigned)desc.status, 0));
     return;
   }
-  const int es = desc.emax >= 0 ? desc.emax - desc.emin : 0;
-  const bool fast = bound_ok((long long)g.n_in, F::top, desc.emax) && es <= F::es_limit &&
-                    !(desc.pad[0] & 1u);
-  if (!fast) {
+  if (!fast_path<T>(desc, g.n_in)) {
     // the warp holding a row tile's first unit runs that tile's checked rows
     for (long long x = x0; x < x1; x++)
       if (x % U == 0)
-        checked_rows<T>(g.pack, g.units, (size_t)(x / U), lane, g.n_out, g.n_in, g.codes,
-                        g.exps, g.out_q32, g.out_f32, g.status);
+        checked_row<T>(PackGeo{g.pack, g.units, 1}, (size_t)(x / U) * 32 + lane, g.n_out,
+                       g.n_in, g.codes, g.exps, g.out_q32, g.out_f32, g.status);
     return;
   }
 
@@ -656,33 +700,21 @@ __global__ void __launch_bounds__(256, 2) gemv_stream_kernel(StreamArgs g) {
   for (int base = 0; base < n16; base += blockDim.x) {  // whole warps: the shuffle below
     const int j16 = base + threadIdx.x;
     const bool in = j16 < n16;
-    const size_t j = 16 * (size_t)j16, b = j / 32;
-    uint4 val = make_uint4(0, 0, 0, 0);
-    unsigned e = APX_EXP_ZERO;
-    if (in && j < g.n_in) {
-      e = g.exps[b];
-      if (j + 16 <= g.n_in && ((reinterpret_cast<uintptr_t>(g.codes + j) & 15) == 0)) {
-        val = __ldg(reinterpret_cast<const uint4 *>(g.codes + j));
-      } else {
-        unsigned t[4] = {0, 0, 0, 0};
-        for (int i = 0; i < 16; i++)
-          if (j + i < g.n_in) t[i / 4] |= ((unsigned)(uint8_t)g.codes[j + i]) << (8 * (i % 4));
-        val = make_uint4(t[0], t[1], t[2], t[3]);
-      }
-    }
-    const bool zero = e == APX_EXP_ZERO;
-    if (zero) val = make_uint4(0, 0, 0, 0);
-    if (in) reinterpret_cast<uint4 *>(s_codes)[j16] = val;
-    const int er = zero ? 0 : (int)e - desc.emin;
+    const Chunk ch = in ? load_chunk(g.codes, g.exps, g.n_in, 16 * (size_t)j16)
+                        : Chunk{make_uint4(0, 0, 0, 0), APX_EXP_ZERO};
+    const bool zero = ch.e == APX_EXP_ZERO;
+    const uint4 val = zero ? make_uint4(0, 0, 0, 0) : ch.v;
+    const int er = zero ? 0 : (int)ch.e - desc.emin;
     int s16 = dp4a_ss((int)val.x, 0x01010101, 0);
     s16 = dp4a_ss((int)val.y, 0x01010101, s16);
     s16 = dp4a_ss((int)val.z, 0x01010101, s16);
     s16 = dp4a_ss((int)val.w, 0x01010101, s16);
     const int s32 = s16 + __shfl_xor_sync(0xFFFFFFFFu, s16, 1);
     if (!in) continue;
+    reinterpret_cast<uint4 *>(s_codes)[j16] = val;
     if (T == kQ6_K) s_xs[j16] = (long long)s16 << er;
     if ((j16 & 1) == 0) {
-      s_e[j16 / 2] = T == kQ8_0 ? (zero ? -1 : (int)e) : er;
+      s_e[j16 / 2] = T == kQ8_0 ? (zero ? -1 : (int)ch.e) : er;
       if (T == kQ4_K) s_xs[j16 / 2] = (long long)s32 << er;
     }
   }
@@ -697,19 +729,15 @@ __global__ void __launch_bounds__(256, 2) gemv_stream_kernel(StreamArgs g) {
     if (more) load_unit(nxt, g.pack + (size_t)(x + 1) * F::unit_bytes, lane);
     const long long rt = x / U;
     const int u = (int)(x % U);
-    if (T == kQ8_0)
-      fold_unit(acc, cur, s_codes + u * 32, s_e + u * 4, nullptr, 0);
-    else if (T == kQ4_K)
-      fold_unit(acc, cur, s_codes + u * 64, s_e + u * 8, s_xs + u * 8, desc.emin);
-    else
-      fold_unit(acc, cur, s_codes + u * 64, s_e + u * 8, s_xs + u * 16, desc.emin);
+    fold_unit(acc, cur, s_codes + u * (F::span / 4), s_e + u * (F::span / 32),
+              s_xs + u * F::nxs, desc.emin);
     if (u == U - 1 || !more) {
       // flush this warp's share of row tile rt
       const long long first_v = (rt * U) / g.chunk;
       const long long last_v = (rt * U + U - 1) / g.chunk;
       const size_t row = (size_t)rt * 32 + lane;
       if (first_v == last_v) {
-        finish_row<T>(acc, row, g.n_out, g.out_q32, g.out_f32, g.status);
+        finish_row(acc, row, g.n_out, g.out_q32, g.out_f32, g.status);
       } else {
         const int k = (int)(v - first_v), count = (int)(last_v - first_v + 1);
         Acc128 *slot = g.partials + ((size_t)rt * g.kmax + k) * 32 + lane;
@@ -728,7 +756,7 @@ __global__ void __launch_bounds__(256, 2) gemv_stream_kernel(StreamArgs g) {
             const Acc128 *src = g.partials + ((size_t)rt * g.kmax + q) * 32 + lane;
             acc_add(s, __ldcg(&src->lo), __ldcg(&src->hi));
           }
-          finish_row<T>(s, row, g.n_out, g.out_q32, g.out_f32, g.status);
+          finish_row(s, row, g.n_out, g.out_q32, g.out_f32, g.status);
           if (lane == 0) g.counters[rt] = 0u;
         }
       }
@@ -738,33 +766,80 @@ __global__ void __launch_bounds__(256, 2) gemv_stream_kernel(StreamArgs g) {
   }
 }
 
-// ---- host-side launch planning -----------------------------------------------------------
+// ---- exact int32 group dots from the repacked layout (parity hook) -------------------------
 
-static int unit_bytes_of(uint32_t t) {
-  return t == kQ8_0 ? kUnitQ8_0 : (t == kQ4_K ? kUnitQ4_K : kUnitQ6_K);
+__global__ void block_dots_kernel(uint32_t type, PackGeo geo, size_t n_out, size_t per_row,
+                                  const int8_t *codes, int32_t *dots) {
+  const size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (idx >= n_out * per_row) return;
+  const size_t row = idx / per_row, g = idx % per_row;
+  int lane, dot = 0;
+  if (type == kQ8_0) {
+    const uint8_t *ub = slot_unit(geo, type, row, g / 4, lane);
+    const int bi = (int)(g % 4);
+    for (int qi = 0; qi < 32; qi++) {
+      const int c = 2 * bi + qi / 16;
+      dot += (int)(signed char)ub[(c * 32 + lane) * 16 + qi % 16] * codes[g * 32 + qi];
+    }
+  } else if (type == kQ4_K) {
+    const size_t s = g / 8;
+    const int grp = (int)(g % 8);
+    const uint8_t *ub = slot_unit(geo, type, row, s, lane);
+    for (int l = 0; l < 32; l++) {
+      const int wb = 32 * (grp / 2) + l;
+      const unsigned byte = ub[((wb / 16) * 32 + lane) * 16 + wb % 16];
+      const unsigned code = (grp % 2) == 0 ? (byte & 0xF) : (byte >> 4);
+      dot += (int)code * codes[s * 256 + 32 * grp + l];
+    }
+  } else {
+    const size_t s = g / 16;
+    const int grp = (int)(g % 16);
+    const uint8_t *ub = slot_unit(geo, type, row, s, lane);
+    for (int l16 = 0; l16 < 16; l16++) {
+      const int p = 16 * grp + l16;
+      const int n = p / 128, r = p % 128, quarter = r / 32, l = r % 32;
+      const int qlb = 64 * n + l + ((quarter & 1) ? 32 : 0), qhb = 128 + 32 * n + l;
+      const unsigned qlv = ub[((qlb / 16) * 32 + lane) * 16 + qlb % 16];
+      const unsigned qhv = ub[((qhb / 16) * 32 + lane) * 16 + qhb % 16];
+      const unsigned lo = quarter < 2 ? (qlv & 0xF) : (qlv >> 4);
+      const int code = (int)(lo | (((qhv >> (2 * quarter)) & 3) << 4)) - 32;
+      dot += code * codes[s * 256 + p];
+    }
+  }
+  dots[idx] = dot;
 }
 
-int units_per_row_tile(uint32_t type, size_t n_in) {
-  if (type == kQ8_0) return (int)((((n_in + 31) / 32) + 3) / 4);
-  return (int)((n_in + 255) / 256);
+// ---- host side: planning, repack, launches ---------------------------------------------------
+
+size_t packed_bytes(const GemvPlan &pl, uint32_t type) {
+  return pl.n_rt * (size_t)pl.units * (size_t)unit_bytes_of(type);
 }
 
-size_t packed_bytes(uint32_t type, size_t n_out, size_t n_in) {
-  size_t n_rt = (n_out + 31) / 32;
-  return n_rt * (size_t)units_per_row_tile(type, n_in) * (size_t)unit_bytes_of(type);
-}
-
-cudaError_t launch_repack(const uint8_t *d_raw, uint8_t *d_pack, uint32_t type, size_t n_out,
-                          size_t n_in, size_t row_bytes, cudaStream_t stream) {
-  int units = units_per_row_tile(type, n_in);
-  int nblk = type == kQ8_0 ? (int)((n_in + 31) / 32) : units;
-  size_t total = packed_bytes(type, n_out, n_in);
+cudaError_t launch_repack(const GemvPlan &pl, const uint8_t *d_raw, uint8_t *d_pack,
+                          uint32_t type, size_t n_out, size_t n_in, size_t row_bytes,
+                          cudaStream_t stream) {
+  const int kslots = units_per_row_tile(type, n_in);
+  const int nblk = type == kQ8_0 ? (int)((n_in + 31) / 32) : kslots;
+  const size_t total = packed_bytes(pl, type);
   if (total == 0) return cudaSuccess;
-  int threads = 256;
+  const int threads = 256;
   size_t blocks = (total + threads - 1) / threads;
   if (blocks > 65535u * 16u) blocks = 65535u * 16u;
   repack_kernel<<<(unsigned)blocks, threads, 0, stream>>>(d_raw, d_pack, type, n_out, row_bytes,
-                                                          units, nblk, total);
+                                                          pl.units, pl.L, kslots, nblk, total);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_block_dots(const GemvPlan &pl, uint32_t type, const uint8_t *pack,
+                              size_t n_out, size_t n_in, const int8_t *codes, int32_t *dots,
+                              cudaStream_t stream) {
+  const int kslots = units_per_row_tile(type, n_in);
+  const size_t per_row =
+      type == kQ8_0 ? (n_in + 31) / 32 : (size_t)kslots * (type == kQ6_K ? 16 : 8);
+  const size_t total = n_out * per_row;
+  if (total == 0) return cudaSuccess;
+  block_dots_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(
+      type, PackGeo{pack, pl.units, pl.L}, n_out, per_row, codes, dots);
   return cudaGetLastError();
 }
 
@@ -775,52 +850,54 @@ static size_t warp_act_bytes(uint32_t t) {
 
 GemvPlan plan_gemv(uint32_t type, size_t n_out, size_t n_in, int sm_count) {
   GemvPlan pl{};
-  const int U = units_per_row_tile(type, n_in);  // 0 for n_in = 0: no loads, rows are 0
-  const size_t n_rt = (n_out + 31) / 32;
-  const size_t T = n_rt * (size_t)U;
-  const size_t wave = (size_t)sm_count * 24;
-  // One unit per warp while the whole matrix fits one resident wave (every load in flight at
-  // once); otherwise warps stream several units, folding one while the next is in flight.
-  pl.units = U;
-  pl.n_rt = n_rt;
-  if (T > wave) {
+  const int K = units_per_row_tile(type, n_in);  // K-slots per row (0 for n_in = 0)
+  const size_t wave = (size_t)sm_count * 24;     // units one resident wave takes at once
+  const size_t T1 = (n_out + 31) / 32 * (size_t)K;
+  if (T1 > wave) {
     // persistent streaming kernel: 2 CTAs of 8 warps per SM, one contiguous chunk per warp
     pl.pipe = true;
+    pl.L = 1;
+    pl.units = K;
+    pl.n_rt = (n_out + 31) / 32;
     const int span = type == kQ8_0 ? 128 : 256;
-    const size_t nel = (size_t)U * span;
+    const size_t nel = (size_t)K * span;
     pl.smem = nel + ((nel / 32 + 3) & ~(size_t)3) * 4 + nel / 16 * 8;
     const int per_sm = pl.smem * 2 <= 200 * 1024 ? 2 : 1;
     pl.block = 256;
     pl.grid = (unsigned)(sm_count * per_sm);
     const long long V = (long long)pl.grid * 8;
-    pl.chunk = (long long)((T + V - 1) / V);
-    pl.kmax = (int)((U + pl.chunk - 1) / pl.chunk) + 1;
+    pl.chunk = (long long)((T1 + V - 1) / V);
+    pl.kmax = (int)((K + pl.chunk - 1) / pl.chunk) + 1;
     pl.R = pl.P = pl.ksplit = 1;
     return pl;
   }
-  int upw = 1;
+  // One wave: one unit per warp, every load in flight at once.  Few, long rows spread
+  // their K-slots over 2 or 4 lanes so a row tile's units fit one CTA.
   pl.pipe = false;
-  const int cap = pl.pipe ? 8 : 16;  // warps per CTA
-  int w = std::max(1, (U + upw - 1) / upw);
-  if (w <= cap) {
+  pl.L = 1;
+  while (pl.L < 4 && (K + pl.L - 1) / pl.L > 12) pl.L *= 2;
+  const int H = 32 / pl.L;
+  const int U = (K + pl.L - 1) / pl.L;
+  const size_t n_rt = (n_out + H - 1) / H;
+  pl.units = U;
+  pl.n_rt = n_rt;
+  const int w = std::max(1, U);
+  if (w <= 12) {
     pl.ksplit = 1;
     pl.P = w;
-    pl.R = std::max(1, cap / pl.P);
-    if (!pl.pipe)
-      pl.R = std::max(1, std::min(pl.R, (int)std::max<size_t>(1, n_rt / sm_count)));
+    pl.R = std::max(1, std::min(12 / pl.P, (int)std::max<size_t>(1, n_rt / sm_count)));
   } else {
-    pl.ksplit = (w + cap - 1) / cap;
+    pl.ksplit = (w + 11) / 12;
     pl.P = (w + pl.ksplit - 1) / pl.ksplit;
     pl.R = 1;
   }
   if ((size_t)pl.R > n_rt) pl.R = (int)(n_rt ? n_rt : 1);
-  pl.units = U;
-  pl.n_rt = n_rt;
   pl.grid = (unsigned)(((n_rt + pl.R - 1) / pl.R) * pl.ksplit);
   pl.block = 32 * pl.R * pl.P;
-  size_t stage = (size_t)pl.R * pl.P * warp_act_bytes(type);
-  size_t red = (size_t)pl.R * pl.P * 32 * sizeof(Acc128) + 64;
-  pl.smem = std::max(stage, red);
+  const size_t stage = (size_t)pl.R * pl.P * warp_act_bytes(type);
+  const size_t red = (size_t)pl.R * pl.P * 32 * sizeof(Acc128) + 64;
+  pl.act_bytes = (int)((std::max(stage, red) + 15) & ~(size_t)15);
+  pl.smem = pl.act_bytes;
   return pl;
 }
 
@@ -839,30 +916,8 @@ static bool pdl_enabled() {
   return on;
 }
 
-template <uint32_t T>
-static cudaError_t launch_stream(const GemvPlan &pl, const StreamArgs &a, cudaStream_t stream) {
-  auto kern = gemv_stream_kernel<T>;
-  if (pl.smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)pl.smem);
-    if (e != cudaSuccess) return e;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(pl.grid);
-  cfg.blockDim = dim3(pl.block);
-  cfg.dynamicSmemBytes = pl.smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, kern, a);
-}
-
-template <uint32_t T>
-static cudaError_t launch_t(const GemvPlan &pl, const GemvArgs &a, cudaStream_t stream) {
-  auto kern = gemv_kernel<T, false>;
+template <typename Kern, typename Args>
+static cudaError_t launch_cfg(Kern kern, const GemvPlan &pl, const Args &a, cudaStream_t stream) {
   if (pl.smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)pl.smem);
@@ -886,10 +941,9 @@ cudaError_t launch_gemv(const GemvPlan &pl, uint32_t type, const uint8_t *pack, 
                         const void *desc, long long *out_q32, float *out_f32,
                         unsigned long long *status, cudaStream_t stream) {
   if (n_out == 0) return cudaSuccess;
-  if (pl.ksplit > 1 && !scratch) return cudaErrorInvalidValue;
+  if ((pl.pipe || pl.ksplit > 1) && !scratch) return cudaErrorInvalidValue;
   if (pl.units > 0 && !pack) return cudaErrorInvalidValue;  // a plan that reads no payload
   if (pl.pipe) {
-    if (!scratch) return cudaErrorInvalidValue;
     StreamArgs sa;
     sa.pack = pack;
     sa.units = pl.units;
@@ -908,15 +962,16 @@ cudaError_t launch_gemv(const GemvPlan &pl, uint32_t type, const uint8_t *pack, 
     sa.chunk = pl.chunk;
     sa.kmax = pl.kmax;
     switch (type) {
-      case kQ8_0: return launch_stream<kQ8_0>(pl, sa, stream);
-      case kQ4_K: return launch_stream<kQ4_K>(pl, sa, stream);
-      case kQ6_K: return launch_stream<kQ6_K>(pl, sa, stream);
+      case kQ8_0: return launch_cfg(gemv_stream_kernel<kQ8_0>, pl, sa, stream);
+      case kQ4_K: return launch_cfg(gemv_stream_kernel<kQ4_K>, pl, sa, stream);
+      case kQ6_K: return launch_cfg(gemv_stream_kernel<kQ6_K>, pl, sa, stream);
       default: return cudaErrorInvalidValue;
     }
   }
   GemvArgs a;
   a.pack = pack;
   a.units = pl.units;
+  a.L = pl.L;
   a.n_rt = pl.n_rt;
   a.n_out = n_out;
   a.n_in = n_in;
@@ -933,10 +988,11 @@ cudaError_t launch_gemv(const GemvPlan &pl, uint32_t type, const uint8_t *pack, 
   a.R = pl.R;
   a.P = pl.P;
   a.ksplit = pl.ksplit;
+  a.act_bytes = pl.act_bytes;
   switch (type) {
-    case kQ8_0: return launch_t<kQ8_0>(pl, a, stream);
-    case kQ4_K: return launch_t<kQ4_K>(pl, a, stream);
-    case kQ6_K: return launch_t<kQ6_K>(pl, a, stream);
+    case kQ8_0: return launch_cfg(gemv_kernel<kQ8_0>, pl, a, stream);
+    case kQ4_K: return launch_cfg(gemv_kernel<kQ4_K>, pl, a, stream);
+    case kQ6_K: return launch_cfg(gemv_kernel<kQ6_K>, pl, a, stream);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -212,61 +212,4 @@ cudaError_t launch_quant_f32(const float *x, size_t n, int8_t *codes, uint8_t *e
   return cudaGetLastError();
 }
 
-// ---- debug: exact int32 group dots from the repacked layout -------------------------------
-
-__global__ void block_dots_kernel(uint32_t type, const uint8_t *pack, int units, size_t n_out,
-                                  size_t n_in, const int8_t *codes, int32_t *dots,
-                                  size_t per_row) {
-  size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  if (idx >= n_out * per_row) return;
-  size_t row = idx / per_row, g = idx % per_row;
-  size_t rt = row / 32;
-  int lane = (int)(row % 32);
-  int dot = 0;
-  if (type == kQ8_0) {
-    const uint8_t *ub = pack + (rt * units + g / 4) * (size_t)kUnitQ8_0;
-    int bi = (int)(g % 4);
-    for (int qi = 0; qi < 32; qi++) {
-      int c = 2 * bi + qi / 16;
-      dot += (int)(signed char)ub[(c * 32 + lane) * 16 + qi % 16] * codes[g * 32 + qi];
-    }
-  } else if (type == kQ4_K) {
-    size_t s = g / 8;
-    int grp = (int)(g % 8);
-    const uint8_t *ub = pack + (rt * units + s) * (size_t)kUnitQ4_K;
-    for (int l = 0; l < 32; l++) {
-      int wb = 32 * (grp / 2) + l;
-      unsigned byte = ub[((wb / 16) * 32 + lane) * 16 + wb % 16];
-      unsigned code = (grp % 2) == 0 ? (byte & 0xF) : (byte >> 4);
-      dot += (int)code * codes[s * 256 + 32 * grp + l];
-    }
-  } else {
-    size_t s = g / 16;
-    int grp = (int)(g % 16);
-    const uint8_t *ub = pack + (rt * units + s) * (size_t)kUnitQ6_K;
-    for (int l16 = 0; l16 < 16; l16++) {
-      int p = 16 * grp + l16;
-      int n = p / 128, r = p % 128, quarter = r / 32, l = r % 32;
-      int qlb = 64 * n + l + ((quarter & 1) ? 32 : 0), qhb = 128 + 32 * n + l;
-      unsigned qlv = ub[((qlb / 16) * 32 + lane) * 16 + qlb % 16];
-      unsigned qhv = ub[((qhb / 16) * 32 + lane) * 16 + qhb % 16];
-      unsigned lo = quarter < 2 ? (qlv & 0xF) : (qlv >> 4);
-      int code = (int)(lo | (((qhv >> (2 * quarter)) & 3) << 4)) - 32;
-      dot += code * codes[s * 256 + p];
-    }
-  }
-  dots[idx] = dot;
-}
-
-cudaError_t launch_block_dots(uint32_t type, const uint8_t *pack, size_t n_out, size_t n_in,
-                              const int8_t *codes, int32_t *dots, cudaStream_t stream) {
-  int units = units_per_row_tile(type, n_in);
-  size_t per_row = type == kQ8_0 ? (n_in + 31) / 32 : (size_t)units * (type == kQ6_K ? 16 : 8);
-  size_t total = n_out * per_row;
-  if (total == 0) return cudaSuccess;
-  block_dots_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(
-      type, pack, units, n_out, n_in, codes, dots, per_row);
-  return cudaGetLastError();
-}
-
 }  // namespace apx

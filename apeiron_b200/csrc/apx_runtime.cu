@@ -388,7 +388,7 @@ int apx_tensor_upload(apx_ctx *ctx, uint32_t ggml_type, const uint8_t *raw, size
   t.row_bytes = row_bytes;
   scan_nonfinite(t, raw);
   t.plan = plan_gemv(ggml_type, n_out, n_in, ctx->sm_count);
-  t.pack_bytes = packed_bytes(ggml_type, n_out, n_in);
+  t.pack_bytes = packed_bytes(t.plan, ggml_type);
   cudaError_t e;
   uint8_t *d_raw = nullptr;
   if (t.pack_bytes) {
@@ -405,7 +405,7 @@ int apx_tensor_upload(apx_ctx *ctx, uint32_t ggml_type, const uint8_t *raw, size
     }
     e = cudaMemcpyAsync(d_raw, raw, need, cudaMemcpyHostToDevice, ctx->stream);
     if (e == cudaSuccess)
-      e = launch_repack(d_raw, t.d_pack, ggml_type, n_out, n_in, row_bytes, ctx->stream);
+      e = launch_repack(t.plan, d_raw, t.d_pack, ggml_type, n_out, n_in, row_bytes, ctx->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
     cudaFree(d_raw);
     if (e != cudaSuccess) {
@@ -602,7 +602,7 @@ int apx_debug_block_dots(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_i
   std::memcpy(h, codes, n_in);
   e = cudaMemcpyAsync(d, h, c_sz, cudaMemcpyHostToDevice, ctx->stream);
   if (e == cudaSuccess)
-    e = launch_block_dots(t->type, t->d_pack, n_out, n_in, (const int8_t *)d,
+    e = launch_block_dots(t->plan, t->type, t->d_pack, n_out, n_in, (const int8_t *)d,
                           (int32_t *)(d + c_sz), ctx->stream);
   if (e == cudaSuccess) e = cudaMemcpyAsync(h + c_sz, d + c_sz, d_sz, cudaMemcpyDeviceToHost, ctx->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);

@@ -68,7 +68,8 @@ typedef enum apx_status {
   APX_ERR_LAYOUT_MISMATCH = 21,     /* call geometry differs from the upload's      */
   APX_ERR_CUDA = 22,                /* CUDA runtime error, code in cuda_error       */
   APX_ERR_OUT_OF_MEMORY = 23,
-  APX_ERR_TOO_LARGE = 24            /* a size beyond a documented backend maximum   */
+  APX_ERR_TOO_LARGE = 24,           /* a size beyond a documented backend maximum   */
+  APX_ERR_DEVICE_TIMEOUT = 25       /* a bounded device-side wait gave up            */
 } apx_status;
 
 /* Refusal detail.  Field meaning depends on `code` as noted in apx_status. */

@@ -223,6 +223,7 @@ def test_matmat_equals_per_column(be, t):
 # ---- block dots, f32 boundary, benchmark shapes ------------------------------------------
 
 @pytest.mark.parametrize("t,n_out,n_in", [(Q8_0, 64, 896), (Q4_K, 64, 1536), (Q4_K, 32, 896),
+                                          (Q8_0, 40, 4864), (Q4_K, 48, 8960), (Q6_K, 24, 4096),
                                           (Q6_K, 32, 896), (Q6_K, 33, 512)])
 def test_block_dots_bit_exact(be, t, n_out, n_in):
     raw = synth.payload(t, n_out, n_in, 11)
