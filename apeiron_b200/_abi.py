@@ -39,7 +39,7 @@ EXPORTS = [
     "apx_matmat_q8act", "apx_quant_act", "apx_matvec_f32", "apx_debug_block_dots",
     "apx_act_describe_async", "apx_quant_q32_async", "apx_quant_f32_async",
     "apx_matvec_async", "apx_matmat_async", "apx_act_padded_len", "apx_status_decode",
-    "apx_matvec_f32_noalloc",
+    "apx_matvec_f32_noalloc", "apx_matmat_f32", "apx_quant_f32_cols_async",
 ]
 
 NOALLOC_MAX_N_IN = 65536
@@ -88,6 +88,8 @@ _SIGS = {
     "apx_act_padded_len": (SZ, [SZ]),
     "apx_status_decode": (C.c_int, [P, U64, C.POINTER(CallStatus), EP]),
     "apx_matvec_f32_noalloc": (C.c_int, [P, U64, SZ, SZ, P, P, P, P]),
+    "apx_matmat_f32": (C.c_int, [P, U64, SZ, SZ, SZ, P, P, EP]),
+    "apx_quant_f32_cols_async": (C.c_int, [P, P, SZ, SZ, P, P, P, P]),
 }
 
 _lib = None

@@ -320,6 +320,21 @@ class Backend:
             _raise(err)
         return y[: tensor.n_out]
 
+    def matmat_f32(self, tensor: Tensor, x) -> np.ndarray:
+        """f32 boundary of the prefill contract: x is (k, n_in) f32, one token per row; the
+        result is (k, n_out) f32, row c equal to ``matvec_f32(tensor, x[c])``."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if x.ndim != 2 or x.shape[1] != tensor.n_in:
+            raise ValueError("x must be (k, n_in)")
+        k = x.shape[0]
+        y = np.empty((max(k, 1), max(tensor.n_out, 1)), dtype=np.float32)
+        err = _abi.ApxErr()
+        rc = self.lib.apx_matmat_f32(self.ctx, tensor.handle, tensor.n_out, tensor.n_in, k,
+                                     _ptr(x), _ptr(y), C.byref(err))
+        if rc:
+            _raise(err)
+        return y[:k, : tensor.n_out]
+
     def block_dots(self, tensor: Tensor, codes) -> np.ndarray:
         """The exact int32 group dots the kernels form (parity hook)."""
         codes = np.ascontiguousarray(codes, dtype=np.int8)

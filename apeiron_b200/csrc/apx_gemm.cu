@@ -1,0 +1,790 @@
+// apx_gemm.cu — exact Q8_0 prefill projection on the 5th-generation tensor cores (tcgen05).
+//
+// Contract (src/engine/kern/matmat.rs:92-134, the exact GEMM of src/engine/kern/gemm.rs:1-31,
+// 438-580): column c of the k-column projection equals matvec_q8act(W, qs[c]) bit for bit.
+// For Q8_0 every term of the sum is a scaled int32 block dot: with the f16 weight scale
+// split as d_{r,b} = m_{r,b}·2^k_{r,b} (src/engine/kern/pow2.rs:52-64) and the activation
+// scale S_{c,b} = 2^e_{c,b},
+//     y[r,c] = round_shift_32( Σ_b m_{r,b}·2^(k_{r,b}+e_{c,b}) · D_b[r,c] ),
+//     D_b[r,c] = Σ_{i<32} q_{r,b,i}·x_{c,b,i}.
+// The tensor cores form every D_b exactly (kind::i8, s32 accumulators in TMEM, one K=32
+// MMA per block).  The epilogue folds the blocks in i64, relative to the row's smallest
+// weight exponent kmin_r and the column's smallest activation exponent emin_c, the way the
+// reference's gemm_q8_0 shift-accumulates (gemm.rs:99-102 spread_limit, 470-486):
+//     acc += D_b · (M_{r,b} << s_{c,b}),   M = m·2^(k − kmin_r),   s = e − emin_c
+// which is exact while the weight spread plus the activation spread is at most 20 (|M << s| <
+// 2^31, |D·M·P| ≤ 2^50, fewer than 2^13 blocks).  y = round_shift_32(acc·2^(kmin_r+emin_c))
+// (pow2.rs:76-96 `finish`).  Columns outside those limits, outside the reference's i128
+// call bound (chart/mod.rs:362-383) or holding a code of -128 take matvec_fixed instead:
+// the checked row path, by extra CTAs of the same launch.
+//
+// Layout in HBM (built once per tensor, on its first multi-column call): the int8 codes
+// row-major, K padded to 128 bytes and rows to 128, for 2D TMA; M_{r,b} as int32 [block][row];
+// kmin per row.  Per call, the prep kernel writes the activation codes row-major per token
+// (zero for zero-scale blocks and past n_in), s as int32 [block][token], emin and a per-token
+// route (refused / GEMM / checked rows).
+//
+// Pipeline (one CTA per 128-row × 64-token tile, all of K):
+//   warp 0      TMA producer: 128-byte K slabs of W (128 rows) and of the codes (64 tokens),
+//               128B-swizzled, into a 4-stage ring (cp.async.bulk.tensor, no multicast);
+//   warp 1      TMEM owner and MMA issuer: one tcgen05.mma per 32-lane block into one of 8
+//               TMEM buffers of 64 columns; tcgen05.commit hands each buffer to the
+//               epilogue and frees the smem stage;
+//   warps 2..17 epilogue: tcgen05.ld of 32 rows × 16 tokens, buffer released, exact fold
+//               (the shift on the integer ALU, the widening multiply-add on the FMA pipe).
+// Every wait is bounded (kWaitLimit); a wait that gives up records APX_ERR_DEVICE_TIMEOUT,
+// drains what the CTA has in flight and frees its TMEM before returning.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "apx_common.cuh"
+#include "apx_kernels.h"
+#include "apx_pack.cuh"
+
+namespace apx {
+
+constexpr int kTileM = 128;
+constexpr int kTileN = 64;
+constexpr int kSlab = 128;  // K bytes per stage (4 blocks): one 128B swizzle atom per row
+constexpr int kStages = 4;
+constexpr int kBufs = 2;    // TMEM buffers of one stage's 4 blocks × kTileN columns (512 in all)
+constexpr int kBufCols = (kSlab / 32) * kTileN;
+constexpr int kEpiWarps = 8;  // 2 per SM sub-partition: 32 rows × 32 tokens each
+constexpr int kEpiTok = 32;
+constexpr int kThreads = 32 * (2 + kEpiWarps);
+constexpr int kStageA = kTileM * kSlab;           // 16 KB of weight codes
+constexpr int kStageB = kTileN * kSlab;           // 8 KB of activation codes
+constexpr int kStageM = kTileM * (kSlab / 32) * 4;  // 2 KB: M of 4 blocks × 128 rows
+constexpr int kStageS = kTileN * (kSlab / 32) * 4;  // 1 KB: s of 4 blocks × 64 tokens
+constexpr int kStageBytes = 28 * 1024;            // one stage, 1024-aligned
+constexpr int kStageTx = kStageA + kStageB + kStageM + kStageS;
+constexpr int kFallbackCtas = 32;        // extra CTAs of each launch for the checked columns
+constexpr int kSpreadLimit = 20;         // weight + activation exponent spread of the i64 fold
+constexpr int kMaxBlocks = (1 << 13) - 1;  // the i64 fold's bound on the block count
+constexpr unsigned kRouteNone = 0, kRouteGemm = 1, kRouteChecked = 2;
+
+static_assert(kStageA % 1024 == 0 && kStageB % 1024 == 0 && kStageBytes % 1024 == 0 &&
+                  kStageTx <= kStageBytes,
+              "stages keep the 1024-byte alignment of the swizzled tiles");
+
+// ---- descriptors ---------------------------------------------------------------------------
+
+// Instruction descriptor of kind::i8: D s32 (2) at bits 4-5, A and B signed 8-bit (1) at
+// bits 7-9 and 10-12, both K-major, N>>3 at bits 17-22, M>>4 at bits 24-28.
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) |
+                            ((uint32_t)(kTileN >> 3) << 17) | ((uint32_t)(kTileM >> 4) << 24);
+
+// Shared-memory matrix descriptor of a K-major operand in the 128B-swizzled layout TMA
+// writes: start address >> 4 in bits 0-13, leading byte offset 16 (>> 4) in bits 16-29,
+// 8-row groups 1024 bytes apart (stride byte offset >> 4) in bits 32-45, version 1 in bits
+// 46-47, layout type 2 (SWIZZLE_128B) in bits 61-63.  Only the start address varies.
+constexpr uint64_t kDescHi = ((uint64_t)(16 >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
+                             ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc) {
+  const uint32_t zero = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(zero), "r"(zero), "r"(zero), "r"(zero),
+      "r"(zero));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
+        "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]),
+        "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]),
+        "=r"(v[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// acc += a·b, 32×32 → 64-bit multiply-add in one instruction.
+__device__ __forceinline__ void mad_wide(long long &acc, int a, int b) {
+  asm("mad.wide.s32 %0, %1, %2, %0;" : "+l"(acc) : "r"(a), "r"(b));
+}
+
+// acc[j] += D[j]·(m << s[j]) for 32 tokens: the shift on the integer ALU, the widening
+// multiply-add on the FMA pipe.  |m << s| < 2^31 and |D| <= 2^19 by the route's limits.
+__device__ __forceinline__ void fold32(long long (&acc)[32], const uint32_t (&d)[32], int32_t m,
+                                       const int32_t *s) {
+  const int4 *sv = reinterpret_cast<const int4 *>(s);
+#pragma unroll
+  for (int j4 = 0; j4 < 8; j4++) {
+    const int4 v = sv[j4];
+    mad_wide(acc[4 * j4 + 0], (int)d[4 * j4 + 0], (int)__funnelshift_l(0u, (unsigned)m, v.x));
+    mad_wide(acc[4 * j4 + 1], (int)d[4 * j4 + 1], (int)__funnelshift_l(0u, (unsigned)m, v.y));
+    mad_wide(acc[4 * j4 + 2], (int)d[4 * j4 + 2], (int)__funnelshift_l(0u, (unsigned)m, v.z));
+    mad_wide(acc[4 * j4 + 3], (int)d[4 * j4 + 3], (int)__funnelshift_l(0u, (unsigned)m, v.w));
+  }
+}
+
+// ---- per-call workspace ------------------------------------------------------------------------
+
+struct WorkView {
+  int8_t *bcodes;    // [n_cols][kp]
+  int32_t *ptab;     // [nb][n_cols_pad] e − emin_c (0 for a zero scale or a checked column)
+  int32_t *emin;     // [n_cols_pad]
+  uint32_t *route;   // [n_cols_pad]
+  int32_t *fb;       // [0] count, [1] CTAs done, [2..] checked-route columns
+};
+
+static __host__ __device__ size_t cols_pad(size_t n_cols) {
+  return (n_cols + kTileN - 1) / kTileN * kTileN;
+}
+
+size_t gemm_work_head_bytes(size_t n_cols) { return (n_cols + 2 + 63) / 64 * 256; }
+
+static WorkView work_view(void *base, size_t n_cols, int nb) {
+  uint8_t *p = static_cast<uint8_t *>(base);
+  const size_t np = cols_pad(n_cols);
+  WorkView w;
+  w.fb = reinterpret_cast<int32_t *>(p);
+  p += gemm_work_head_bytes(n_cols);
+  w.route = reinterpret_cast<uint32_t *>(p);
+  p += np * 4;
+  w.emin = reinterpret_cast<int32_t *>(p);
+  p += np * 4;
+  w.ptab = reinterpret_cast<int32_t *>(p);
+  p += (size_t)nb * np * 4;
+  w.bcodes =
+      reinterpret_cast<int8_t *>((reinterpret_cast<uintptr_t>(p) + 255) & ~(uintptr_t)255);
+  return w;
+}
+
+size_t gemm_work_bytes(size_t n_cols, size_t n_in) {
+  const size_t nb = (n_in + 31) / 32, kp = (n_in + kSlab - 1) / kSlab * kSlab;
+  const size_t np = cols_pad(n_cols);
+  return gemm_work_head_bytes(n_cols) + 2 * np * 4 + nb * np * 4 + 256 + n_cols * kp;
+}
+
+// ---- activation prep: describe, route, B operand, P table -----------------------------------
+
+struct PrepArgs {
+  const int8_t *codes;  // caller codes, column c at c·ld
+  const uint8_t *exps;  // caller exponent bytes, column c at c·ldb
+  const ActDesc *descs; // the quantizer's descriptors (a refusal there wins), or null
+  size_t ld, ldb, n_in, kp;
+  int nb, n_cols, ks;
+  WorkView w;
+  unsigned long long *status;  // column c's refusal word at status[c·2]
+};
+
+__global__ void __launch_bounds__(256) gemm_prep_kernel(PrepArgs a) {
+  __shared__ int s_emin, s_emax, s_status;
+  __shared__ unsigned s_m128, s_route;
+  const int c = blockIdx.x;
+  const size_t np = cols_pad((size_t)a.n_cols);
+  if (c >= a.n_cols) {  // padding tokens of the last tile: P = 0
+    for (int b = threadIdx.x; b < a.nb; b += blockDim.x) a.w.ptab[(size_t)b * np + c] = 0;
+    if (threadIdx.x == 0) {
+      a.w.emin[c] = 0;
+      a.w.route[c] = kRouteNone;
+    }
+    return;
+  }
+  if (threadIdx.x == 0) {
+    s_emin = 1 << 30;
+    s_emax = -1;
+    s_status = a.descs ? a.descs[c].status : APX_OK;
+    s_m128 = 0;
+  }
+  __syncthreads();
+  if (s_status != APX_OK) {  // refused by the quantizer: its codes and exponents are not set
+    for (int b = threadIdx.x; b < a.nb; b += blockDim.x) a.w.ptab[(size_t)b * np + c] = 0;
+    if (threadIdx.x == 0) {
+      atomicMin(a.status + (size_t)c * 2, pack_status(0, (unsigned)s_status, 0));
+      a.w.emin[c] = 0;
+      a.w.route[c] = kRouteNone;
+    }
+    return;
+  }
+  const int8_t *codes = a.codes + (size_t)c * a.ld;
+  const uint8_t *exps = a.exps + (size_t)c * a.ldb;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = blockDim.x / 32;
+  // describe (QuantAct's Q32.32 image, chart/mod.rs:124-181), as the GEMV's descriptor does
+  for (int b = warp; b < a.nb; b += nw) {
+    const unsigned e = exps[b];
+    if (e == APX_EXP_ZERO) continue;
+    if (e > 62) {
+      if (lane == 0) atomicMax(&s_status, (int)APX_ERR_INVALID_ARGUMENT);
+      continue;
+    }
+    const size_t j = (size_t)b * 32 + lane;
+    const int code = j < a.n_in ? codes[j] : 0;
+    bool bad = false;
+    if (e > 56) {
+      const long long lim = 1ll << (63 - e);
+      bad = code < -lim || code > lim - 1;
+    }
+    if (__any_sync(0xFFFFFFFFu, bad) && lane == 0)
+      atomicMax(&s_status, (int)APX_ERR_FIXED_OVERFLOW);
+    if (__any_sync(0xFFFFFFFFu, code == -128) && lane == 0) atomicOr(&s_m128, 1u);
+    if (lane == 0) {
+      atomicMin(&s_emin, (int)e);
+      atomicMax(&s_emax, (int)e);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int emin = s_emax >= 0 ? s_emin : 0;
+    unsigned route = kRouteNone;
+    if (s_status != APX_OK) {
+      atomicMin(a.status + (size_t)c * 2, pack_status(0, (unsigned)s_status, 0));
+    } else if (!s_m128 && bound_ok((long long)a.n_in, Fam<kQ8_0>::top, s_emax) &&
+               (s_emax < 0 || s_emax - emin + a.ks <= kSpreadLimit)) {
+      route = kRouteGemm;
+    } else {
+      route = kRouteChecked;
+      const int slot = atomicAdd(a.w.fb, 1);
+      a.w.fb[2 + slot] = c;
+    }
+    s_emin = emin;
+    s_route = route;
+    a.w.emin[c] = emin;
+    a.w.route[c] = route;
+  }
+  __syncthreads();
+  const bool gemm = s_route == kRouteGemm;
+  const int emin = s_emin;
+  for (int b = threadIdx.x; b < a.nb; b += blockDim.x) {
+    const unsigned e = exps[b];
+    a.w.ptab[(size_t)b * np + c] = gemm && e != APX_EXP_ZERO ? (int)(e - emin) : 0;
+  }
+  // B operand row: 16 codes per thread step, zero for zero-scale blocks and past n_in
+  int8_t *dst = a.w.bcodes + (size_t)c * a.kp;
+  for (size_t j = (size_t)threadIdx.x * 16; j < a.kp; j += (size_t)blockDim.x * 16) {
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (gemm && j < a.n_in && exps[j / 32] != APX_EXP_ZERO) {
+      if (j + 16 <= a.n_in) {
+        v = *reinterpret_cast<const uint4 *>(codes + j);
+      } else {
+        uint8_t t[16];
+        for (int i = 0; i < 16; i++) t[i] = j + i < a.n_in ? (uint8_t)codes[j + i] : 0;
+        memcpy(&v, t, 16);
+      }
+    }
+    *reinterpret_cast<uint4 *>(dst + j) = v;
+  }
+}
+
+// ---- the GEMM --------------------------------------------------------------------------------
+
+struct GemmArgs {
+  const int32_t *wmul;  // [nb_pad][m_pad]
+  const int32_t *kmin;  // [m_pad]
+  WorkView w;
+  long long *out_q32;   // [n_cols][n_out] or null
+  float *out_f32;       // [n_cols][n_out] or null
+  unsigned long long *status;  // column c at status[c·2]
+  size_t n_out, m_pad;
+  int n_cols, nb, kslabs, m_tiles, tiles;
+  // checked route (matvec_fixed per row) of the columns the prep kernel listed
+  PackGeo geo;
+  const int8_t *codes;
+  const uint8_t *exps;
+  size_t ld, ldb, n_in;
+};
+
+__device__ __forceinline__ void checked_columns(const GemmArgs &g) {
+  volatile int32_t *fb = g.w.fb;
+  const long long n = fb[0];
+  const long long items = n * (long long)g.n_out;
+  const long long first = (long long)(blockIdx.x - g.tiles) * blockDim.x + threadIdx.x;
+  for (long long i = first; i < items; i += (long long)kFallbackCtas * blockDim.x) {
+    const int c = fb[2 + i / (long long)g.n_out];
+    const size_t row = (size_t)(i % (long long)g.n_out);
+    checked_row<kQ8_0>(g.geo, row, g.n_out, g.n_in, g.codes + (size_t)c * g.ld,
+                       g.exps + (size_t)c * g.ldb,
+                       g.out_q32 ? g.out_q32 + (size_t)c * g.n_out : nullptr,
+                       g.out_f32 ? g.out_f32 + (size_t)c * g.n_out : nullptr,
+                       g.status + (size_t)c * 2);
+  }
+  // every checked CTA reads the list; the last to finish resets it for the next call
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(g.w.fb + 1, 1) == kFallbackCtas - 1) {
+      g.w.fb[0] = 0;
+      g.w.fb[1] = 0;
+      __threadfence();
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_q8_0_kernel(const __grid_constant__ CUtensorMap map_w,
+                     const __grid_constant__ CUtensorMap map_x,
+                     const __grid_constant__ CUtensorMap map_m,
+                     const __grid_constant__ CUtensorMap map_s, GemmArgs g) {
+  if ((int)blockIdx.x >= g.tiles) {
+    checked_columns(g);
+    return;
+  }
+  // stage s: weight codes (16 KB, 128B-swizzled), activation codes (8 KB, swizzled),
+  // M of its 4 blocks × 128 rows (int32), shifts of its 4 blocks × 64 tokens (int32)
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
+  uint64_t *full = bars, *empty = bars + kStages, *dfull = bars + 2 * kStages;
+  uint64_t *dempty = dfull + kBufs, *mdone = dempty + kBufs;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mdone + 1);
+  int *timeout = reinterpret_cast<int *>(tmem_slot + 1);
+  auto stage_a = [&](int st) { return smem + st * kStageBytes; };
+  auto stage_b = [&](int st) { return smem + st * kStageBytes + kStageA; };
+  auto stage_m = [&](int st) {
+    return reinterpret_cast<const int32_t *>(smem + st * kStageBytes + kStageA + kStageB);
+  };
+  auto stage_s = [&](int st) {
+    return reinterpret_cast<const int32_t *>(smem + st * kStageBytes + kStageA + kStageB +
+                                             kStageM);
+  };
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int mt = (int)blockIdx.x % g.m_tiles, nt = (int)blockIdx.x / g.m_tiles;
+  const int m0 = mt * kTileM, n0 = nt * kTileN;
+
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < kStages; st++) {
+      mbar_init(full + st, 1);
+      // released by the epilogue warps: each has seen the stage's MMAs complete (dfull)
+      mbar_init(empty + st, kEpiWarps);
+    }
+    for (int b = 0; b < kBufs; b++) {
+      mbar_init(dfull + b, 1);
+      mbar_init(dempty + b, kEpiWarps);
+    }
+    mbar_init(mdone, 1);
+    *timeout = 0;
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_w)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_x)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_m)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_s)) : "memory");
+  }
+  if (warp == 1) {  // TMEM: kBufs × kBufCols columns of 32-bit accumulators
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_addr(tmem_slot)),
+                 "r"(kBufs * kBufCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---- TMA producer ----
+    if (lane == 0) {
+      int issued = 0;
+      for (int kt = 0; kt < g.kslabs; kt++) {
+        const int st = kt % kStages, use = kt / kStages;
+        if (use > 0 && !mbar_wait(empty + st, (use - 1) & 1)) {
+          atomicExch(timeout, 1);
+          break;
+        }
+        if (atomicAdd(timeout, 0)) break;
+        uint8_t *base = stage_a(st);
+        mbar_expect_tx(full + st, kStageTx);
+        tma_load_2d(base, &map_w, kt * kSlab, m0, full + st);
+        tma_load_2d(base + kStageA, &map_x, kt * kSlab, n0, full + st);
+        tma_load_2d(base + kStageA + kStageB, &map_m, m0, kt * (kSlab / 32), full + st);
+        tma_load_2d(base + kStageA + kStageB + kStageM, &map_s, n0, kt * (kSlab / 32),
+                    full + st);
+        issued++;
+      }
+      // every copy this thread started has landed before the CTA may exit
+      for (int kt = issued > kStages ? issued - kStages : 0; kt < issued; kt++)
+        mbar_wait(full + kt % kStages, (kt / kStages) & 1);
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer: a stage's 4 blocks into one TMEM buffer, one commit per stage ----
+    if (lane == 0) {
+      volatile int *vt = timeout;
+      const uint64_t a0 = kDescHi | (smem_addr(stage_a(0)) >> 4);
+      const uint64_t b0 = kDescHi | (smem_addr(stage_b(0)) >> 4);
+      for (int kt = 0; kt < g.kslabs && !*vt; kt++) {
+        const int st = kt % kStages, use = kt / kStages, buf = kt % kBufs, ub = kt / kBufs;
+        if (!mbar_wait(full + st, use & 1) ||
+            (ub > 0 && !mbar_wait(dempty + buf, (ub - 1) & 1))) {
+          atomicExch(timeout, 1);
+          break;
+        }
+        tc_fence_after();
+        // descriptor start addresses advance 16 bytes per unit: 32 bytes per block
+        const uint64_t ad = a0 + (uint64_t)(st * (kStageBytes >> 4));
+        const uint64_t bd = b0 + (uint64_t)(st * (kStageBytes >> 4));
+        const uint32_t dt = tmem + (uint32_t)(buf * kBufCols);
+        if (4 * kt + 4 <= g.nb) {
+          mma_i8(dt, ad, bd);
+          mma_i8(dt + kTileN, ad + 2, bd + 2);
+          mma_i8(dt + 2 * kTileN, ad + 4, bd + 4);
+          mma_i8(dt + 3 * kTileN, ad + 6, bd + 6);
+        } else {
+          for (int q = 0; q < g.nb - 4 * kt; q++)
+            mma_i8(dt + q * kTileN, ad + 2 * q, bd + 2 * q);
+        }
+        mma_commit(dfull + buf);
+      }
+      mma_commit(mdone);
+      if (!mbar_wait(mdone, 0)) atomicExch(timeout, 1);
+    }
+  } else {
+    // ---- epilogue: 32 rows × 32 tokens per warp, block by block; the TMEM load of block
+    // b+1 is in flight while block b is folded ----
+    const int lg = warp % 4;  // the TMEM lane quarter this warp may read
+    const int tq = (warp - 2) / 4;
+    const int rl = 32 * lg + lane;
+    const size_t row = (size_t)m0 + rl;
+    const int c0 = kEpiTok * tq;
+    const uint32_t trow = tmem + ((uint32_t)(32 * lg) << 16) + (uint32_t)c0;
+    long long acc[kEpiTok];
+#pragma unroll
+    for (int j = 0; j < kEpiTok; j++) acc[j] = 0;
+    // block b: stage kt = b/4, TMEM buffer kt % kBufs, columns (b % 4)·kTileN
+    auto tcol = [&](int b) {
+      return trow + (uint32_t)(((b >> 2) % kBufs) * kBufCols + (b & 3) * kTileN);
+    };
+    // wait for stage kt: its M / shift tables (TMA) and its dots (MMA commit)
+    auto enter = [&](int kt) {
+      if (!mbar_wait(full + kt % kStages, (kt / kStages) & 1) ||
+          !mbar_wait(dfull + kt % kBufs, (kt / kBufs) & 1))
+        return false;
+      tc_fence_after();
+      return true;
+    };
+    auto step = [&](int b, uint32_t(&cur)[kEpiTok], uint32_t(&nxt)[kEpiTok]) {
+      tmem_wait_ld();  // cur holds block b's dots
+      const int kt = b >> 2, q = b & 3, st = kt % kStages;
+      const bool stage_end = q == 3 || b == g.nb - 1;
+      if (stage_end) {  // every dot of stage kt is in registers: its TMEM buffer is free
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dempty + kt % kBufs);
+      }
+      if (b + 1 < g.nb) {
+        if (stage_end && !enter(kt + 1)) return false;
+        tmem_ld32_nowait(tcol(b + 1), nxt);
+      }
+      fold32(acc, cur, stage_m(st)[q * kTileM + rl], stage_s(st) + q * kTileN + c0);
+      if (stage_end) {  // the stage's tables are read
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + st);
+      }
+      return true;
+    };
+    bool ok = g.nb == 0 || enter(0);
+    uint32_t da[kEpiTok], db[kEpiTok];
+    if (ok && g.nb > 0) tmem_ld32_nowait(tcol(0), da);
+    for (int b = 0; ok && b < g.nb; b += 2) {
+      ok = step(b, da, db);
+      if (ok && b + 1 < g.nb) ok = step(b + 1, db, da);
+    }
+    if (!ok) atomicExch(timeout, 1);
+    if (ok && row < g.n_out) {
+      const unsigned kmin = (unsigned)g.kmin[row];
+#pragma unroll
+      for (int j = 0; j < kEpiTok; j++) {
+        const int col = n0 + c0 + j;
+        if (col >= g.n_cols || g.w.route[col] != kRouteGemm) continue;
+        Acc128 a;
+        shl128(acc[j], kmin + (unsigned)g.w.emin[col], a.lo, a.hi);
+        long long v;
+        if (!acc_round_to_i64(a, v)) {
+          atomicMin(g.status + (size_t)col * 2, pack_status(row, kKindOutputOverflow, 0));
+          continue;
+        }
+        if (g.out_q32) g.out_q32[(size_t)col * g.n_out + row] = v;
+        if (g.out_f32)
+          g.out_f32[(size_t)col * g.n_out + row] = __ll2float_rn(v) * 2.3283064365386963e-10f;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (*timeout && threadIdx.x < kTileN && n0 + (int)threadIdx.x < g.n_cols)
+    atomicMin(g.status + (size_t)(n0 + threadIdx.x) * 2,
+              pack_status(0, APX_ERR_DEVICE_TIMEOUT, 0));
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kBufs * kBufCols)
+                 : "memory");
+  }
+}
+
+// ---- the weight layout of the GEMM, from the packed units --------------------------------------
+
+// Per row: kmin = the smallest f16 exponent k of its block scales, and the largest spread.
+__global__ void gemm_row_exponents(PackGeo geo, size_t n_out, int nb, int32_t *kmin,
+                                   int *spread) {
+  const size_t row = blockIdx.x * (size_t)(blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (row >= n_out) return;
+  int lo = 1 << 30, hi = -1;
+  for (int b = lane; b < nb; b += 32) {
+    int l;
+    const uint8_t *ub = slot_unit(geo, kQ8_0, row, (size_t)b / 4, l);
+    const int bi = b % 4;
+    int m;
+    unsigned k;
+    f16_split(ub[4096 + l * 8 + 2 * bi] | (ub[4096 + l * 8 + 2 * bi + 1] << 8), m, k);
+    lo = min(lo, (int)k);
+    hi = max(hi, (int)k);
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    lo = min(lo, __shfl_xor_sync(0xFFFFFFFFu, lo, o));
+    hi = max(hi, __shfl_xor_sync(0xFFFFFFFFu, hi, o));
+  }
+  if (lane == 0) {
+    kmin[row] = nb ? lo : 0;
+    if (nb) atomicMax(spread, hi - lo);
+  }
+}
+
+// Row-major int8 codes [m_pad][kp] and M_{r,b} = m·2^(k − kmin_r) as int32 [nb_pad][m_pad];
+// zero for padding rows and blocks, and M = 0 where the spread leaves int32 (such a tensor
+// never takes the GEMM route).
+__global__ void gemm_build_layout(PackGeo geo, size_t n_out, int nb, int nb_pad, size_t m_pad,
+                                  size_t kp, const int32_t *kmin, int8_t *codes, int32_t *wmul) {
+  const size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x;  // (row, block)
+  if (idx >= m_pad * (size_t)nb_pad) return;
+  const size_t row = idx / nb_pad;
+  const int b = (int)(idx % nb_pad);
+  int32_t mul = 0;
+  uint4 c0 = make_uint4(0, 0, 0, 0), c1 = c0;
+  if (row < n_out && b < nb) {
+    int l;
+    const uint8_t *ub = slot_unit(geo, kQ8_0, row, (size_t)b / 4, l);
+    const int bi = b % 4;
+    int m;
+    unsigned k;
+    f16_split(ub[4096 + l * 8 + 2 * bi] | (ub[4096 + l * 8 + 2 * bi + 1] << 8), m, k);
+    const unsigned sh = k - (unsigned)kmin[row];
+    mul = sh <= (unsigned)kSpreadLimit ? m * (1 << sh) : 0;
+    c0 = *reinterpret_cast<const uint4 *>(ub + ((2 * bi) * 32 + l) * 16);
+    c1 = *reinterpret_cast<const uint4 *>(ub + ((2 * bi + 1) * 32 + l) * 16);
+  }
+  wmul[(size_t)b * m_pad + row] = mul;
+  uint4 *dst = reinterpret_cast<uint4 *>(codes + row * kp + 32 * (size_t)b);
+  dst[0] = c0;
+  dst[1] = c1;
+}
+
+// ---- host side ---------------------------------------------------------------------------------
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// A 2D uint8 map over `rows` rows of `inner` bytes (row stride `stride`), boxes of
+// 128 bytes × box_rows, 128-byte swizzle; reads past either extent fill zeros.
+static bool make_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t rows,
+                     uint64_t stride, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {inner, rows};
+  const cuuint64_t strides[1] = {stride};
+  const cuuint32_t box[2] = {(cuuint32_t)kSlab, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// A 2D int32 table [rows][inner] (row stride inner·4 bytes), boxes of box_inner × 4 rows
+// (one stage's blocks), no swizzle; rows past the extent fill zeros.
+static bool make_table_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t rows,
+                           uint32_t box_inner) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {inner, rows};
+  const cuuint64_t strides[1] = {inner * 4};
+  const cuuint32_t box[2] = {box_inner, (cuuint32_t)(kSlab / 32)};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_INT32, 2, const_cast<void *>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static_assert(sizeof(CUtensorMap) == sizeof(GemmLayout::map), "tensor map storage");
+
+cudaError_t build_gemm_layout(const GemvPlan &pl, const uint8_t *pack, size_t n_out,
+                              size_t n_in, GemmLayout *lay, cudaStream_t stream) {
+  *lay = GemmLayout{};
+  lay->nb = (int)((n_in + 31) / 32);
+  lay->kp = (n_in + kSlab - 1) / kSlab * kSlab;
+  lay->nb_pad = (int)(lay->kp / 32);
+  lay->m_pad = (n_out + kTileM - 1) / kTileM * kTileM;
+  const size_t codes_bytes = lay->m_pad * lay->kp;
+  const size_t mul_bytes = (size_t)lay->nb_pad * lay->m_pad * 4;
+  const size_t kmin_bytes = lay->m_pad * 4;
+  const size_t total = codes_bytes + mul_bytes + kmin_bytes + 16;
+  cudaError_t e = cudaMalloc(&lay->base, total);
+  if (e != cudaSuccess) {
+    lay->base = nullptr;
+    return e;
+  }
+  lay->codes = reinterpret_cast<int8_t *>(lay->base);
+  lay->wmul = reinterpret_cast<int32_t *>(static_cast<uint8_t *>(lay->base) + codes_bytes);
+  lay->kmin = lay->wmul + (size_t)lay->nb_pad * lay->m_pad;
+  int *spread = reinterpret_cast<int *>(lay->kmin + lay->m_pad);
+  e = cudaMemsetAsync(lay->base, 0, total, stream);
+  const PackGeo geo{pack, pl.units, pl.L};
+  if (e == cudaSuccess && n_out && lay->nb) {
+    gemm_row_exponents<<<(unsigned)((n_out + 7) / 8), 256, 0, stream>>>(geo, n_out, lay->nb,
+                                                                        lay->kmin, spread);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess && lay->nb) {
+    const size_t items = lay->m_pad * (size_t)lay->nb_pad;
+    gemm_build_layout<<<(unsigned)((items + 255) / 256), 256, 0, stream>>>(
+        geo, n_out, lay->nb, lay->nb_pad, lay->m_pad, lay->kp, lay->kmin, lay->codes,
+        lay->wmul);
+    e = cudaGetLastError();
+  }
+  int h = 0;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&h, spread, 4, cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  lay->kspread = h;
+  if (e == cudaSuccess &&
+      (!make_map(reinterpret_cast<CUtensorMap *>(lay->map), lay->codes, lay->kp, lay->m_pad,
+                 lay->kp, kTileM) ||
+       !make_table_map(reinterpret_cast<CUtensorMap *>(lay->map_m), lay->wmul, lay->m_pad,
+                       (uint64_t)lay->nb_pad, kTileM)))
+    e = cudaErrorInvalidValue;
+  if (e != cudaSuccess) {
+    cudaFree(lay->base);
+    *lay = GemmLayout{};
+  }
+  return e;
+}
+
+void free_gemm_layout(GemmLayout *lay) {
+  if (lay->base) cudaFree(lay->base);
+  *lay = GemmLayout{};
+}
+
+static size_t gemm_smem_bytes() {
+  return 1024 + (size_t)kStages * kStageBytes + (2 * kStages + 2 * kBufs + 1) * 8 + 16;
+}
+
+bool gemm_shape_ok(size_t n_in) { return n_in && (n_in + 31) / 32 <= (size_t)kMaxBlocks; }
+
+bool gemm_supported(const GemmLayout &lay) {
+  return lay.base && lay.nb > 0 && lay.nb <= kMaxBlocks && lay.kspread <= kSpreadLimit;
+}
+
+cudaError_t launch_gemm_q8_0(const GemvPlan &pl, const uint8_t *pack, const GemmLayout &lay,
+                             size_t n_out, size_t n_in, size_t n_cols, const int8_t *codes,
+                             size_t ld, const uint8_t *exps, size_t ldb, const void *descs,
+                             void *work, long long *out_q32, float *out_f32,
+                             unsigned long long *status, cudaStream_t stream) {
+  if (n_cols == 0 || n_out == 0) return cudaSuccess;
+  const WorkView w = work_view(work, n_cols, lay.nb);
+  PrepArgs pa;
+  pa.codes = codes;
+  pa.exps = exps;
+  pa.descs = static_cast<const ActDesc *>(descs);
+  pa.ld = ld;
+  pa.ldb = ldb;
+  pa.n_in = n_in;
+  pa.kp = lay.kp;
+  pa.nb = lay.nb;
+  pa.n_cols = (int)n_cols;
+  pa.ks = lay.kspread;
+  pa.w = w;
+  pa.status = status;
+  gemm_prep_kernel<<<(unsigned)cols_pad(n_cols), 256, 0, stream>>>(pa);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+
+  CUtensorMap map_x, map_s;
+  if (!make_map(&map_x, w.bcodes, lay.kp, n_cols, lay.kp, kTileN) ||
+      !make_table_map(&map_s, w.ptab, cols_pad(n_cols), (uint64_t)lay.nb, kTileN))
+    return cudaErrorInvalidValue;
+  GemmArgs a;
+  a.wmul = lay.wmul;
+  a.kmin = lay.kmin;
+  a.w = w;
+  a.out_q32 = out_q32;
+  a.out_f32 = out_f32;
+  a.status = status;
+  a.n_out = n_out;
+  a.m_pad = lay.m_pad;
+  a.n_cols = (int)n_cols;
+  a.nb = lay.nb;
+  a.kslabs = (int)(lay.kp / kSlab);
+  a.m_tiles = (int)((n_out + kTileM - 1) / kTileM);
+  a.tiles = a.m_tiles * (int)((n_cols + kTileN - 1) / kTileN);
+  a.geo = PackGeo{pack, pl.units, pl.L};
+  a.codes = codes;
+  a.exps = exps;
+  a.ld = ld;
+  a.ldb = ldb;
+  a.n_in = n_in;
+  const size_t smem = gemm_smem_bytes();
+  e = cudaFuncSetAttribute(gemm_q8_0_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem);
+  if (e != cudaSuccess) return e;
+  gemm_q8_0_kernel<<<(unsigned)(a.tiles + kFallbackCtas), kThreads, smem, stream>>>(
+      *reinterpret_cast<const CUtensorMap *>(lay.map), map_x,
+      *reinterpret_cast<const CUtensorMap *>(lay.map_m), map_s, a);
+  return cudaGetLastError();
+}
+
+}  // namespace apx

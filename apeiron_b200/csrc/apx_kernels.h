@@ -45,6 +45,44 @@ cudaError_t launch_quant_q32(const long long *x, size_t n, int8_t *codes, uint8_
                              void *desc, cudaStream_t stream);
 cudaError_t launch_quant_f32(const float *x, size_t n, int8_t *codes, uint8_t *exps, void *desc,
                              cudaStream_t stream);
+// `cols` f32 vectors, vector c at x + c·ldx, one CTA each.
+cudaError_t launch_quant_f32_cols(const float *x, size_t n, size_t ldx, int cols, int8_t *codes,
+                                  size_t ld, uint8_t *exps, size_t ldb, void *desc,
+                                  cudaStream_t stream);
+
+// The tcgen05 GEMM's view of a Q8_0 tensor (apx_gemm.cu): row-major codes for TMA, the
+// per-(block, row) integer multipliers and per-row smallest exponents, and the 2D tensor
+// maps of the codes and the multipliers (CUtensorMap, kept opaque here).
+struct GemmLayout {
+  void *base = nullptr;
+  int8_t *codes = nullptr;  // [m_pad][kp]
+  int32_t *wmul = nullptr;  // [nb_pad][m_pad]
+  int32_t *kmin = nullptr;  // [m_pad]
+  int nb = 0, nb_pad = 0;
+  size_t kp = 0, m_pad = 0;
+  int kspread = 0;  // largest exponent spread of one row's block scales
+  alignas(64) unsigned char map[128];    // the codes, 128-byte boxes × 128 rows
+  alignas(64) unsigned char map_m[128];  // wmul, 128 rows × 4 blocks
+};
+
+cudaError_t build_gemm_layout(const GemvPlan &pl, const uint8_t *pack, size_t n_out,
+                              size_t n_in, GemmLayout *lay, cudaStream_t stream);
+void free_gemm_layout(GemmLayout *lay);
+// Whether the GEMM can take a tensor of this width / this layout at all.
+bool gemm_shape_ok(size_t n_in);
+bool gemm_supported(const GemmLayout &lay);
+// Device workspace of one call (zeroed once at allocation; its list counters reset themselves).
+size_t gemm_work_bytes(size_t n_cols, size_t n_in);
+size_t gemm_work_head_bytes(size_t n_cols);
+// Exact k-column Q8_0 projection: column c's codes at codes + c·ld (16-byte aligned, ld a
+// multiple of 16, readable up to the 128-byte-padded width), exponent bytes at exps + c·ldb,
+// refusal word at status[2c] (initialised to all ones by the caller).  `descs` (one
+// ActDesc per column, or null) carries the quantizer's refusals.
+cudaError_t launch_gemm_q8_0(const GemvPlan &pl, const uint8_t *pack, const GemmLayout &lay,
+                             size_t n_out, size_t n_in, size_t n_cols, const int8_t *codes,
+                             size_t ld, const uint8_t *exps, size_t ldb, const void *descs,
+                             void *work, long long *out_q32, float *out_f32,
+                             unsigned long long *status, cudaStream_t stream);
 
 // Debug: exact int32 group dots from the repacked layout (apx_gemv.cu).
 cudaError_t launch_block_dots(const GemvPlan &pl, uint32_t type, const uint8_t *pack,

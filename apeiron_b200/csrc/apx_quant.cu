@@ -136,10 +136,20 @@ __device__ __forceinline__ bool f32_to_q32(float f, long long &out) {
   return true;
 }
 
+// One CTA per activation vector: vector c reads x at c·ldx elements and writes its codes at
+// c·ld, its exponent bytes at c·ldb and its descriptor at desc[c].
 template <bool F32>
-__global__ void quant_kernel(const void *xin, size_t n, int8_t *codes, uint8_t *exps,
-                             ActDesc *desc) {
+__global__ void quant_kernel(const void *xin, size_t n, size_t ldx, int8_t *codes, size_t ld,
+                             uint8_t *exps, size_t ldb, ActDesc *desc) {
   __shared__ DescAcc acc;
+  {
+    const size_t c = blockIdx.x;
+    xin = F32 ? (const void *)(reinterpret_cast<const float *>(xin) + c * ldx)
+              : (const void *)(reinterpret_cast<const long long *>(xin) + c * ldx);
+    codes += c * ld;
+    exps += c * ldb;
+    desc += c;
+  }
   desc_init(&acc);
   __syncthreads();
   const size_t nb = (n + 31) / 32;
@@ -202,13 +212,25 @@ cudaError_t launch_describe(const int8_t *codes, const uint8_t *exps, size_t n, 
 
 cudaError_t launch_quant_q32(const long long *x, size_t n, int8_t *codes, uint8_t *exps,
                              void *desc, cudaStream_t stream) {
-  quant_kernel<false><<<1, 1024, 0, stream>>>(x, n, codes, exps, reinterpret_cast<ActDesc *>(desc));
+  quant_kernel<false><<<1, 1024, 0, stream>>>(x, n, 0, codes, 0, exps, 0,
+                                              reinterpret_cast<ActDesc *>(desc));
   return cudaGetLastError();
 }
 
 cudaError_t launch_quant_f32(const float *x, size_t n, int8_t *codes, uint8_t *exps, void *desc,
                              cudaStream_t stream) {
-  quant_kernel<true><<<1, 1024, 0, stream>>>(x, n, codes, exps, reinterpret_cast<ActDesc *>(desc));
+  quant_kernel<true><<<1, 1024, 0, stream>>>(x, n, 0, codes, 0, exps, 0,
+                                             reinterpret_cast<ActDesc *>(desc));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quant_f32_cols(const float *x, size_t n, size_t ldx, int cols, int8_t *codes,
+                                  size_t ld, uint8_t *exps, size_t ldb, void *desc,
+                                  cudaStream_t stream) {
+  if (cols <= 0) return cudaSuccess;
+  const int threads = n <= 4096 ? 256 : 1024;
+  quant_kernel<true><<<cols, threads, 0, stream>>>(x, n, ldx, codes, ld, exps, ldb,
+                                                   reinterpret_cast<ActDesc *>(desc));
   return cudaGetLastError();
 }
 

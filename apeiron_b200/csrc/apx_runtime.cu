@@ -35,6 +35,8 @@ struct Tensor {
   size_t nonfinite_row = SIZE_MAX;  // first row holding an Inf/NaN block scale
   uint16_t nonfinite_bits = 0;
   GemvPlan plan{};
+  GemmLayout gemm;          // tcgen05 GEMM view (Q8_0), built on the first multi-column call
+  bool gemm_tried = false;
 };
 
 struct DevBuf {
@@ -113,6 +115,7 @@ struct apx_ctx {
   uint64_t next = 1;
   DevBuf dev;      // [out | status | desc | exps | codes] of the synchronous calls
   DevBuf scratch;  // device-side quantization scratch of the f32 path
+  DevBuf gwork;    // GEMM per-call workspace (its head zeroed whenever it is reallocated)
   HostBuf host;    // pinned mirror of `dev`
 };
 
@@ -292,6 +295,77 @@ int matvec_sync(apx_ctx *ctx, Tensor &t, size_t n_out, size_t n_in, const int8_t
   return rc;
 }
 
+// ---- multi-column calls on the tensor cores (Q8_0) -------------------------------------
+
+constexpr size_t kGemmMinCols = 4;  // fewer columns run as separate GEMVs
+
+// Whether a k-column call takes the tcgen05 GEMM: Q8_0, enough columns, a width the kernel
+// takes, and a weight exponent spread that leaves room for its i64 fold.  The GEMM view of
+// the tensor is built on the first such call.
+bool gemm_route(apx_ctx *ctx, Tensor &t, size_t n_out, size_t n_in, size_t k_cols) {
+  if (t.type != APX_GGML_TYPE_Q8_0 || k_cols < kGemmMinCols || n_out == 0 ||
+      !gemm_shape_ok(n_in) || !t.d_pack)
+    return false;
+  if (!t.gemm_tried) {
+    t.gemm_tried = true;
+    if (build_gemm_layout(t.plan, t.d_pack, t.n_out, t.n_in, &t.gemm, ctx->stream) !=
+        cudaSuccess)
+      cudaGetLastError();  // no GEMM view: the call runs as GEMVs
+  }
+  return gemm_supported(t.gemm);
+}
+
+cudaError_t ensure_gwork(apx_ctx *ctx, size_t n_cols, size_t n_in) {
+  const size_t need = gemm_work_bytes(n_cols, n_in);
+  if (need <= ctx->gwork.cap) return cudaSuccess;
+  cudaError_t e = ctx->gwork.ensure(need);
+  if (e == cudaSuccess) e = cudaMemset(ctx->gwork.p, 0, ctx->gwork.cap);
+  return e;
+}
+
+// Synchronous k-column projection of host activations through the GEMM: one H2D of
+// [status | exps | codes (rows padded to 128 bytes)], one D2H of [outputs | status].
+int matmat_gemm_sync(apx_ctx *ctx, Tensor &t, size_t n_out, size_t n_in, size_t k,
+                     const int8_t *codes, const uint8_t *exps, int64_t *out, apx_err *err) {
+  const size_t nb = (n_in + 31) / 32, ld = (n_in + 127) / 128 * 128;
+  const size_t out_sz = align16(k * n_out * 8), st_sz = align16(k * 16);
+  const size_t ex_sz = align16(k * nb), cd_sz = k * ld;
+  const size_t in_sz = st_sz + ex_sz + cd_sz;
+  cudaError_t e;
+  if ((e = ctx->dev.ensure(out_sz + in_sz)) != cudaSuccess) return cuda_err(err, e);
+  if ((e = ctx->host.ensure(out_sz + in_sz)) != cudaSuccess) return cuda_err(err, e);
+  if ((e = ensure_gwork(ctx, k, n_in)) != cudaSuccess) return cuda_err(err, e);
+  uint8_t *h = (uint8_t *)ctx->host.p, *d = (uint8_t *)ctx->dev.p;
+  uint8_t *hs = h + out_sz, *he = hs + st_sz, *hc = he + ex_sz;
+  std::memset(hs, 0xFF, k * 16);
+  std::memcpy(he, exps, k * nb);
+  for (size_t c = 0; c < k; c++) {
+    std::memcpy(hc + c * ld, codes + c * n_in, n_in);
+    std::memset(hc + c * ld + n_in, 0, ld - n_in);
+  }
+  uint8_t *ds = d + out_sz, *de = ds + st_sz, *dc = de + ex_sz;
+  e = cudaMemcpyAsync(ds, hs, in_sz, cudaMemcpyHostToDevice, ctx->stream);
+  if (e == cudaSuccess)
+    e = launch_gemm_q8_0(t.plan, t.d_pack, t.gemm, n_out, n_in, k, (const int8_t *)dc, ld, de,
+                         nb, nullptr, ctx->gwork.p, (long long *)d, nullptr,
+                         (unsigned long long *)ds, ctx->stream);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(h, d, out_sz + k * 16, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return cuda_err(err, e);
+  for (size_t c = 0; c < k; c++) {
+    unsigned long long word;
+    std::memcpy(&word, hs + c * 16, 8);
+    const int rc = decode_status(t, n_out, word, err);
+    if (rc != APX_OK) {
+      if (err) err->col = c;
+      return rc;
+    }
+  }
+  std::memcpy(out, h, k * n_out * 8);
+  return set_err(err, APX_OK);
+}
+
 }  // namespace
 
 namespace apx {
@@ -348,9 +422,11 @@ void apx_close(apx_ctx *ctx) {
   for (auto &kv : ctx->tensors) {
     cudaFree(kv.second.d_pack);
     if (kv.second.d_scratch) cudaFree(kv.second.d_scratch);
+    free_gemm_layout(&kv.second.gemm);
   }
   ctx->dev.release();
   ctx->scratch.release();
+  ctx->gwork.release();
   ctx->host.release();
   cudaStreamDestroy(ctx->stream);
   delete ctx;
@@ -439,6 +515,7 @@ int apx_tensor_free(apx_ctx *ctx, uint64_t handle) {
   cudaStreamSynchronize(ctx->stream);
   cudaFree(t->d_pack);
   if (t->d_scratch) cudaFree(t->d_scratch);
+  free_gemm_layout(&t->gemm);
   ctx->tensors.erase(handle);
   return APX_OK;
 }
@@ -496,6 +573,9 @@ int apx_matmat_q8act(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in, s
   if (!t) return set_err(err, APX_ERR_INVALID_ARGUMENT);
   cudaSetDevice(ctx->device);
   const size_t nb = (q_len + 31) / 32;
+  if (k_cols && check_geometry(*t, n_out, n_in, q_len, false, nullptr) == APX_OK &&
+      gemm_route(ctx, *t, n_out, n_in, k_cols))
+    return matmat_gemm_sync(ctx, *t, n_out, n_in, k_cols, codes, exps, out, err);
   for (size_t c = 0; c < k_cols; c++) {
     HostAct ha = describe_host(codes + c * q_len, q_len, exps + c * nb);
     int rc = ha.status;
@@ -581,6 +661,66 @@ int apx_matvec_f32(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in, con
   return rc;
 }
 
+int apx_matmat_f32(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in, size_t k_cols,
+                   const float *x, float *y, apx_err *err) {
+  if (!ctx || (k_cols && ((n_in && !x) || (n_out && !y))))
+    return set_err(err, APX_ERR_INVALID_ARGUMENT);
+  if (k_cols > (size_t)INT32_MAX) return set_err(err, APX_ERR_TOO_LARGE);
+  std::lock_guard<std::mutex> g(ctx->mu);
+  Tensor *t = find(ctx, tensor);
+  if (!t) return set_err(err, APX_ERR_INVALID_ARGUMENT);
+  cudaSetDevice(ctx->device);
+  int rc = check_geometry(*t, n_out, n_in, n_in, false, err);
+  if (rc != APX_OK || k_cols == 0) return rc;
+  const size_t ld = apx_act_padded_len(n_in), ldb = ld / 32;
+  const size_t y_sz = align16(k_cols * n_out * 4), st_sz = align16(k_cols * 16);
+  const size_t x_sz = align16(k_cols * n_in * 4);
+  const size_t ds_sz = align16(k_cols * sizeof(ActDesc)), ex_sz = align16(k_cols * ldb);
+  cudaError_t e;
+  if ((e = ctx->dev.ensure(y_sz + st_sz + x_sz)) != cudaSuccess) return cuda_err(err, e);
+  if ((e = ctx->host.ensure(y_sz + st_sz + x_sz)) != cudaSuccess) return cuda_err(err, e);
+  if ((e = ctx->scratch.ensure(ds_sz + ex_sz + k_cols * ld)) != cudaSuccess)
+    return cuda_err(err, e);
+  const bool gemm = gemm_route(ctx, *t, n_out, n_in, k_cols);
+  if (gemm && (e = ensure_gwork(ctx, k_cols, n_in)) != cudaSuccess) return cuda_err(err, e);
+  uint8_t *h = (uint8_t *)ctx->host.p, *d = (uint8_t *)ctx->dev.p;
+  uint8_t *sc = (uint8_t *)ctx->scratch.p;
+  uint8_t *descs = sc, *dexp = sc + ds_sz;
+  int8_t *dcod = (int8_t *)(sc + ds_sz + ex_sz);
+  std::memset(h + y_sz, 0xFF, k_cols * 16);
+  std::memcpy(h + y_sz + st_sz, x, k_cols * n_in * 4);
+  e = cudaMemcpyAsync(d + y_sz, h + y_sz, st_sz + k_cols * n_in * 4, cudaMemcpyHostToDevice,
+                      ctx->stream);
+  if (e == cudaSuccess)
+    e = launch_quant_f32_cols((const float *)(d + y_sz + st_sz), n_in, n_in, (int)k_cols, dcod,
+                              ld, dexp, ldb, descs, ctx->stream);
+  unsigned long long *status = (unsigned long long *)(d + y_sz);
+  if (e == cudaSuccess && gemm) {
+    e = launch_gemm_q8_0(t->plan, t->d_pack, t->gemm, n_out, n_in, k_cols, dcod, ld, dexp, ldb,
+                         descs, ctx->gwork.p, nullptr, (float *)d, status, ctx->stream);
+  } else {
+    for (size_t c = 0; e == cudaSuccess && c < k_cols; c++)
+      e = launch_gemv(t->plan, t->type, t->d_pack, t->d_scratch, n_out, n_in, dcod + c * ld,
+                      dexp + c * ldb, descs + c * sizeof(ActDesc), nullptr,
+                      (float *)d + c * n_out, status + 2 * c, ctx->stream);
+  }
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(h, d, y_sz + k_cols * 16, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return cuda_err(err, e);
+  for (size_t c = 0; c < k_cols; c++) {
+    unsigned long long word;
+    std::memcpy(&word, h + y_sz + c * 16, 8);
+    rc = decode_status(*t, n_out, word, err);
+    if (rc != APX_OK) {
+      if (err) err->col = c;
+      return rc;
+    }
+  }
+  std::memcpy(y, h, k_cols * n_out * 4);
+  return set_err(err, APX_OK);
+}
+
 int apx_debug_block_dots(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
                          const int8_t *codes, int32_t *dots, apx_err *err) {
   if (!ctx || !codes || !dots) return set_err(err, APX_ERR_INVALID_ARGUMENT);
@@ -637,6 +777,18 @@ int apx_quant_f32_async(apx_ctx *ctx, const float *d_x, size_t n, int8_t *d_code
   return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
 }
 
+int apx_quant_f32_cols_async(apx_ctx *ctx, const float *d_x, size_t n, size_t k_cols,
+                             int8_t *d_codes, uint8_t *d_exps, apx_act_desc *d_descs,
+                             void *stream) {
+  if (!ctx || (k_cols && (!d_descs || (n && (!d_x || !d_codes || !d_exps)))))
+    return APX_ERR_INVALID_ARGUMENT;
+  if (k_cols > (size_t)INT32_MAX) return APX_ERR_TOO_LARGE;
+  const size_t ld = apx_act_padded_len(n);
+  cudaError_t e = launch_quant_f32_cols(d_x, n, n, (int)k_cols, d_codes, ld, d_exps, ld / 32,
+                                        d_descs, (cudaStream_t)stream);
+  return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
+}
+
 int apx_matvec_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
                      const int8_t *d_codes, const uint8_t *d_exps, const apx_act_desc *d_desc,
                      int64_t *d_out_q32, float *d_out_f32, apx_call_status *d_status,
@@ -666,6 +818,17 @@ int apx_matmat_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in, s
   }
   if (!t || n_in != t->n_in || n_out > t->n_out) return APX_ERR_LAYOUT_MISMATCH;
   const size_t ld = apx_act_padded_len(n_in), ldb = ld / 32;
+  {
+    std::lock_guard<std::mutex> g(ctx->mu);
+    if (gemm_route(ctx, *t, n_out, n_in, k_cols)) {
+      if (ensure_gwork(ctx, k_cols, n_in) != cudaSuccess) return APX_ERR_OUT_OF_MEMORY;
+      cudaError_t e = launch_gemm_q8_0(t->plan, t->d_pack, t->gemm, n_out, n_in, k_cols, d_codes,
+                                       ld, d_exps, ldb, d_descs, ctx->gwork.p, (long long *)d_out_q32,
+                                       d_out_f32, (unsigned long long *)d_status,
+                                       (cudaStream_t)stream);
+      return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
+    }
+  }
   for (size_t c = 0; c < k_cols; c++) {
     cudaError_t e = launch_gemv(t->plan, t->type, t->d_pack, t->d_scratch, n_out, n_in, d_codes + c * ld,
                                 d_exps + c * ldb, d_descs + c,

@@ -161,6 +161,13 @@ APX_API int apx_quant_act(apx_ctx *ctx, const int64_t *x, size_t n, int8_t *code
 APX_API int apx_matvec_f32(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
                    const float *x, float *y, apx_err *err);
 
+/* f32 boundary of the prefill contract: k_cols columns of n_in floats (column c at
+ * x[c*n_in ..]) to column-major y[c*n_out + r]; column c of y equals apx_matvec_f32 of
+ * column c.  Q8_0 tensors with at least 4 columns run on the int8 tensor cores.  Refuses
+ * with the lowest refusing column (err->col). */
+APX_API int apx_matmat_f32(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
+                   size_t k_cols, const float *x, float *y, apx_err *err);
+
 /* Parity hook: the exact int32 group dots the kernels form, one per (row, group)
  * in group order (32-lane groups for Q8_0/Q4_K, 16-lane groups for Q6_K). */
 APX_API int apx_debug_block_dots(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
@@ -185,7 +192,17 @@ APX_API int apx_matvec_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t
                      const int8_t *d_codes, const uint8_t *d_exps,
                      const apx_act_desc *d_desc, int64_t *d_out_q32, float *d_out_f32,
                      apx_call_status *d_status, void *stream);
-/* Exact k-column projection of device activations (column-major outputs). */
+/* Device f32_to_fixed + quant_act of k_cols f32 vectors (vector c at d_x[c*n ..]);
+ * codes of column c at d_codes[c*apx_act_padded_len(n) ..], exponent bytes at
+ * d_exps[c*apx_act_padded_len(n)/32 ..], descriptor d_descs[c]. */
+APX_API int apx_quant_f32_cols_async(apx_ctx *ctx, const float *d_x, size_t n, size_t k_cols,
+                             int8_t *d_codes, uint8_t *d_exps, apx_act_desc *d_descs,
+                             void *stream);
+/* Exact k-column projection of device activations (column-major outputs), column c
+ * laid out as apx_quant_f32_cols_async writes it; d_status[c] is column c's refusal
+ * word, set to all ones by the caller.  Q8_0 tensors with at least 4 columns run on
+ * the int8 tensor cores; those calls share a context workspace, so calls on one
+ * context must not overlap in time. */
 APX_API int apx_matmat_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
                      size_t k_cols, const int8_t *d_codes, const uint8_t *d_exps,
                      const apx_act_desc *d_descs, int64_t *d_out_q32,

@@ -1,0 +1,235 @@
+"""GPU parity of the prefill contract on the int8 tensor cores (tcgen05 GEMM, Q8_0).
+
+Every multi-column Q8_0 call with at least four columns takes the GEMM; columns the GEMM's
+i64 fold cannot take exactly (a code of -128, a wide exponent spread, the reference's call
+bound failing) take the checked row path inside the same launch.  Bar: bit-exact Q32.32
+outputs against the oracle's per-column contract (src/engine/kern/matmat.rs:92-134),
+identical refusals with the lowest refusing column, and f32 outputs identical to the
+single-column f32 boundary.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from chart_inputs import random_payload, random_x
+from apeiron_b200 import chart, synth
+from apeiron_b200.chart import Backend, QuantAct
+
+pytestmark = pytest.mark.gpu
+
+Q8_0 = 8
+KIND = {1: chart.ShapeMismatch, 3: chart.ShortPayload, 4: chart.LengthOverflow,
+        6: chart.NonFiniteScale, 7: chart.FixedOverflow, 8: chart.AccumulatorOverflow,
+        9: chart.OutputOverflow}
+THREADS = os.cpu_count() or 1
+
+
+@pytest.fixture(scope="module")
+def be():
+    b = Backend(0)
+    yield b
+    b.close()
+
+
+def bench_columns(n_in, k, seed):
+    """k benchmark activations (f32 N(0,1) through f32_to_fixed and quant_act)."""
+    qs = []
+    for c in range(k):
+        x = synth.f32_to_q32(synth.activation_f32(n_in, seed + c))
+        codes, exps = synth.quant_act_np(x)
+        qs.append(QuantAct.from_exps(exps, codes))
+    return qs
+
+
+def stack(qs):
+    return (np.stack([q.codes for q in qs]), np.stack([q.scales for q in qs]))
+
+
+def check_matmat(be, raw, n_out, n_in, qs, threads=1):
+    codes, scales = stack(qs)
+    if threads > 1:
+        want = O.matmat_q8act_mt(Q8_0, raw, n_out, n_in, codes, scales, threads)
+    else:
+        want = O.matmat_q8act(Q8_0, raw, n_out, n_in, codes, scales)
+    try:
+        got = be.matmat_q8act(Q8_0, raw, n_out, n_in, qs)
+    except chart.MatvecError as e:
+        assert isinstance(want, tuple), f"GPU refused {e!r}, oracle gave values"
+        assert isinstance(e, KIND[want[1]]), (e, want)
+        assert e.col == want[5], (e.col, want)
+        return e
+    assert not isinstance(want, tuple), f"GPU gave values, oracle refused {want}"
+    assert np.array_equal(np.stack(got), want)
+    return got
+
+
+@pytest.mark.parametrize("n_out,n_in", [(4864, 896), (896, 4864)])
+def test_prefill_benchmark_shapes_512_tokens(be, n_out, n_in):
+    """The prefill configuration: 512 tokens against both Qwen2.5-0.5B FFN shapes."""
+    raw = synth.payload(Q8_0, n_out, n_in, 31 + n_out)
+    check_matmat(be, raw, n_out, n_in, bench_columns(n_in, 512, 1000), threads=THREADS)
+
+
+@pytest.mark.parametrize("n_out,n_in,k", [
+    (200, 100, 70),     # ragged K (not a multiple of 32), partial row and token tiles
+    (130, 1000, 5),
+    (1, 32, 4),
+    (129, 4000, 65),
+    (257, 96, 129),
+    (64, 15360, 8),     # the widest K one CTA's exponent table holds
+])
+def test_ragged_shapes(be, n_out, n_in, k):
+    raw = random_payload(Q8_0, n_out, n_in, 0x3000, 0x2C00, n_out * 7 + n_in)
+    qs = [_col(n_in, 17 + c, c % 5) for c in range(k)]
+    check_matmat(be, raw, n_out, n_in, qs)
+
+
+def _col(n_in, seed, shift=0):
+    c, s = O.quant_act(random_x(n_in, seed) >> shift)
+    return QuantAct.from_parts(s, c)
+
+
+def test_zero_and_sparse_columns(be):
+    """All-zero tokens, zero-scale blocks holding stray codes, and a single live block."""
+    n_out, n_in, k = 300, 640, 9
+    raw = random_payload(Q8_0, n_out, n_in, 0x3400, 0x2800, 5)
+    qs = [_col(n_in, 40 + c) for c in range(k)]
+    qs[1] = QuantAct.from_parts(np.zeros(n_in // 32, np.int64), np.zeros(n_in, np.int8))
+    s = qs[2].scales.copy()
+    s[::3] = 0                      # zero scales: their codes must not count
+    qs[2] = QuantAct.from_parts(s, qs[2].codes)
+    s = np.zeros(n_in // 32, np.int64)
+    s[7] = 1 << 20
+    qs[3] = QuantAct.from_parts(s, np.full(n_in, 127, np.int8))
+    check_matmat(be, raw, n_out, n_in, qs)
+
+
+def test_checked_route_columns(be):
+    """Columns the i64 fold does not take: a -128 code, a 25-exponent activation spread,
+    a scale of 2^56 (the reference's call bound fails); their values come from the checked
+    rows.  A bound-failing column that overflows refuses like the oracle."""
+    n_out, n_in, k = 260, 512, 8
+    raw = random_payload(Q8_0, n_out, n_in, 0x3000, 0x2C00, 9)
+    qs = [_col(n_in, 60 + c) for c in range(k)]
+    c = qs[1].codes.copy()
+    c[5] = -128
+    qs[1] = QuantAct.from_parts(qs[1].scales, c)
+    s = qs[3].scales.copy()
+    s[0] = 1 << 2
+    s[1] = 1 << 27
+    qs[3] = QuantAct.from_parts(s, qs[3].codes)
+    s = np.zeros(n_in // 32, np.int64)
+    s[4] = 1 << 56
+    c = np.zeros(n_in, np.int8)
+    c[128:132] = (1, -1, 1, 1)
+    qs[6] = QuantAct.from_parts(s, c)
+    check_matmat(be, raw, n_out, n_in, qs)
+    # the checked list resets itself: the same call again, then a plain call
+    check_matmat(be, raw, n_out, n_in, qs)
+    check_matmat(be, raw, n_out, n_in, [_col(n_in, 90 + c) for c in range(k)])
+    # a bound-failing column large enough to overflow
+    qs[5] = QuantAct.from_parts(np.full(n_in // 32, 1 << 57, np.int64), qs[5].codes // 2)
+    check_matmat(be, raw, n_out, n_in, qs)
+
+
+def test_refusals_lowest_column(be):
+    """FixedOverflow and OutputOverflow in different columns: the lowest refusing column
+    decides, and within it the first row in row order."""
+    n_out, n_in, k = 140, 256, 6
+    raw = random_payload(Q8_0, n_out, n_in, 0x7BFF, 0, 11)   # every scale 65504
+    base = [_col(n_in, 70 + c) for c in range(k)]
+    fixed = QuantAct.from_parts(np.full(n_in // 32, 1 << 60, np.int64),
+                                np.full(n_in, 127, np.int8))
+    c, s = O.quant_act(random_x(n_in, 77) << 30)
+    big = QuantAct.from_parts(s, c)
+    for pos_fixed, pos_big in [(4, 2), (1, 3), (5, 0)]:
+        qs = list(base)
+        qs[pos_fixed] = fixed
+        qs[pos_big] = big
+        e = check_matmat(be, raw, n_out, n_in, qs)
+        assert isinstance(e, chart.MatvecError) and e.col == min(pos_fixed, pos_big)
+
+
+def test_output_overflow_row_order(be):
+    """Large weights (every scale 65504) against growing activations: the GEMM's first
+    overflowing row in the lowest overflowing column, values where nothing overflows."""
+    n_out, n_in, k = 512, 1024, 4
+    raw = random_payload(Q8_0, n_out, n_in, 0x7BFF, 0, 12)
+    qs = []
+    for c, sh in enumerate([0, 10, 30, 20]):
+        cc, ss = O.quant_act(random_x(n_in, 80 + c) << sh)
+        qs.append(QuantAct.from_parts(ss, cc))
+    e = check_matmat(be, raw, n_out, n_in, qs)
+    assert isinstance(e, chart.OutputOverflow) and e.col == 2
+    check_matmat(be, raw, n_out, n_in, [qs[0], qs[1], qs[0], qs[1]])
+
+
+def test_wide_weight_spread_and_nonfinite_weights(be):
+    """Weights whose scales span subnormal to 65504 (no GEMM view: per-column GEMVs) and a
+    non-finite weight scale (column 0 refuses with its bits)."""
+    n_out, n_in, k = 96, 512, 5
+    raw = synth.payload(Q8_0, n_out, n_in, 13)
+    blk = raw.reshape(n_out, -1)[3].reshape(-1, 34)
+    blk[0, 0:2] = (0x01, 0x00)   # smallest subnormal
+    blk[1, 0:2] = (0xFF, 0x7B)   # 65504
+    check_matmat(be, raw, n_out, n_in, [_col(n_in, 85 + c) for c in range(k)])
+    raw2 = synth.payload(Q8_0, n_out, n_in, 14)
+    raw2.reshape(n_out, -1)[50].reshape(-1, 34)[2, 0:2] = (0x00, 0x7C)   # +Inf
+    e = check_matmat(be, raw2, n_out, n_in, [_col(n_in, 86 + c) for c in range(k)])
+    assert isinstance(e, chart.NonFiniteScale) and e.col == 0
+
+
+@pytest.mark.parametrize("n_out,n_in,k", [(4864, 896, 512), (896, 4864, 64), (200, 100, 7)])
+def test_f32_boundary_matches_matvec_f32(be, n_out, n_in, k):
+    """matmat_f32 (device quantizer + GEMM, f32 epilogue) equals matvec_f32 per column."""
+    raw = synth.payload(Q8_0, n_out, n_in, 21 + n_in)
+    t = be.upload(Q8_0, raw, n_out, n_in)
+    x = np.stack([synth.activation_f32(n_in, 500 + c) for c in range(k)])
+    y = be.matmat_f32(t, x)
+    for c in range(0, k, max(1, k // 16)):
+        assert np.array_equal(y[c], be.matvec_f32(t, x[c])), c
+
+
+def test_async_columns_match_sync(be):
+    """apx_quant_f32_cols_async + apx_matmat_async over device buffers (torch allocates)
+    equal the synchronous prefill call, Q32.32 and f32 outputs both."""
+    import ctypes as C
+    import torch
+
+    from apeiron_b200 import _abi
+
+    lib = be.lib
+    n_out, n_in, k = 4864, 896, 96
+    raw = synth.payload(Q8_0, n_out, n_in, 23)
+    tens = be.upload(Q8_0, raw, n_out, n_in)
+    x = np.stack([synth.activation_f32(n_in, 700 + c) for c in range(k)])
+    dev = torch.device("cuda:0")
+    dx = torch.from_numpy(x).to(dev)
+    pad = lib.apx_act_padded_len(n_in)
+    codes = torch.zeros(k * pad, dtype=torch.int8, device=dev)
+    exps = torch.full((k * pad // 32,), 0xFF, dtype=torch.uint8, device=dev)
+    descs = torch.zeros(k * 8, dtype=torch.int32, device=dev)
+    q32 = torch.zeros(k * n_out, dtype=torch.int64, device=dev)
+    f32 = torch.zeros(k * n_out, dtype=torch.float32, device=dev)
+    status = torch.full((2 * k,), -1, dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.apx_quant_f32_cols_async(be.ctx, dx.data_ptr(), n_in, k, codes.data_ptr(),
+                                        exps.data_ptr(), descs.data_ptr(), stream) == 0
+    assert lib.apx_matmat_async(be.ctx, tens.handle, n_out, n_in, k, codes.data_ptr(),
+                                exps.data_ptr(), descs.data_ptr(), q32.data_ptr(),
+                                f32.data_ptr(), status.data_ptr(), stream) == 0
+    torch.cuda.synchronize()
+    st = status.cpu().numpy()
+    for c in range(k):
+        word = _abi.CallStatus(int(st[2 * c]) & ((1 << 64) - 1), 0)
+        err = _abi.ApxErr()
+        assert lib.apx_status_decode(be.ctx, tens.handle, C.byref(word), C.byref(err)) == 0
+    qs = []
+    for c in range(k):
+        cc, ee = synth.quant_act_np(synth.f32_to_q32(x[c]))
+        qs.append(QuantAct.from_exps(ee, cc))
+    want = np.stack(be.matmat_q8act(Q8_0, tens, n_out, n_in, qs))
+    assert np.array_equal(q32.cpu().numpy().reshape(k, n_out), want)
+    assert np.array_equal(f32.cpu().numpy().reshape(k, n_out), be.matmat_f32(tens, x))
