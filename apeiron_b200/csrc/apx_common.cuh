@@ -185,24 +185,32 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
 }
 
 // Wait for phase `parity` of the barrier; false if the bounded wait gave up (after
-// kWaitLimit polls or about one second of %globaltimer, whichever comes first).
+// kWaitLimit polls or about one second of %globaltimer, whichever comes first).  A poll
+// that finds the phase open backs off with a short sleep, so that waiting warps leave the
+// issue slots to the warps they wait for (a producer or an MMA thread sharing the same
+// SM sub-partition).
+__device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; "
+      "selp.u32 %0, 1, 0, p; }"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-  uint32_t done = 0;
-  unsigned long long t0 = 0;
+  if (mbar_try(bar, parity)) return true;
+  unsigned long long t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
   for (int it = 0; it < kWaitLimit; it++) {
-    asm volatile(
-        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-        : "=r"(done)
-        : "r"(smem_addr(bar)), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if ((it & 255) == 255) {
+    __nanosleep(32);
+    if (mbar_try(bar, parity)) return true;
+    if ((it & 63) == 63) {
       unsigned long long now;
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
-      if (t0 == 0)
-        t0 = now;
-      else if (now - t0 > 1000000000ull)
-        return false;
+      if (now - t0 > 1000000000ull) return false;
     }
   }
   return false;

@@ -7,31 +7,34 @@
 // scale S_{c,b} = 2^e_{c,b},
 //     y[r,c] = round_shift_32( Σ_b m_{r,b}·2^(k_{r,b}+e_{c,b}) · D_b[r,c] ),
 //     D_b[r,c] = Σ_{i<32} q_{r,b,i}·x_{c,b,i}.
-// The tensor cores form every D_b exactly (kind::i8, s32 accumulators in TMEM, one K=32
-// MMA per block).  The epilogue folds the blocks in i64, relative to the row's smallest
-// weight exponent kmin_r and the column's smallest activation exponent emin_c, the way the
+// The tensor cores form every block's dot exactly (kind::i8, s32 accumulators in TMEM) and
+// also apply the activation's per-block power of two: with s = e − emin_c (0..3) they
+// accumulate D' = A·x + Σ_{k=1..s} 2^(k−1)·A·x = D·2^s from "planes" of the activation codes
+// (plane k holds the blocks whose s is at least k), 2^smax MMAs per block where smax is the
+// largest s of the tile's tokens.  The epilogue then folds each block with one widening
+// multiply-add, relative to the row's smallest weight exponent kmin_r, the way the
 // reference's gemm_q8_0 shift-accumulates (gemm.rs:99-102 spread_limit, 470-486):
-//     acc += D_b · (M_{r,b} << s_{c,b}),   M = m·2^(k − kmin_r),   s = e − emin_c
-// which is exact while the weight spread plus the activation spread is at most 20 (|M << s| <
-// 2^31, |D·M·P| ≤ 2^50, fewer than 2^13 blocks).  y = round_shift_32(acc·2^(kmin_r+emin_c))
-// (pow2.rs:76-96 `finish`).  Columns outside those limits, outside the reference's i128
-// call bound (chart/mod.rs:362-383) or holding a code of -128 take matvec_fixed instead:
-// the checked row path, by extra CTAs of the same launch.
+//     acc += D'_b · M_{r,b},   M = m·2^(k − kmin_r)
+// which is exact in i64 while |D'·M| < 2^(33+kspread) summed over the blocks stays below
+// 2^63.  y = round_shift_32(acc·2^(kmin_r+emin_c)) (pow2.rs:76-96 `finish`).  Columns whose
+// activation spread exceeds 3, outside the reference's i128 call bound (chart/mod.rs:
+// 362-383) or holding a code of -128 take matvec_fixed instead: the checked row path, by
+// extra CTAs of the same launch.
 //
 // Layout in HBM (built once per tensor, on its first multi-column call): the int8 codes
 // row-major, K padded to 128 bytes and rows to 128, for 2D TMA; M_{r,b} as int32 [block][row];
-// kmin per row.  Per call, the prep kernel writes the activation codes row-major per token
+// kmin per row.  Per call, the prep kernel writes the activation planes row-major per token
 // (zero for zero-scale blocks and past n_in), s as int32 [block][token], emin and a per-token
 // route (refused / GEMM / checked rows).
 //
 // Pipeline (one CTA per 128-row × 64-token tile, all of K):
-//   warp 0      TMA producer: 128-byte K slabs of W (128 rows) and of the codes (64 tokens),
-//               128B-swizzled, into a 4-stage ring (cp.async.bulk.tensor, no multicast);
-//   warp 1      TMEM owner and MMA issuer: one tcgen05.mma per 32-lane block into one of 8
-//               TMEM buffers of 64 columns; tcgen05.commit hands each buffer to the
-//               epilogue and frees the smem stage;
-//   warps 2..17 epilogue: tcgen05.ld of 32 rows × 16 tokens, buffer released, exact fold
-//               (the shift on the integer ALU, the widening multiply-add on the FMA pipe).
+//   warp 0      TMA producer: 128-byte K slabs of W (128 rows) and of the planes the slab's
+//               blocks use (64 tokens), 128B-swizzled, and the slab's M table, into a
+//               4-stage ring (cp.async.bulk.tensor, no multicast);
+//   warp 1      TMEM owner and MMA issuer: a slab's blocks into one of 2 TMEM buffers of
+//               4 × 64 columns, one tcgen05.commit per slab;
+//   warps 2..9  epilogue: tcgen05.ld of 32 rows × 32 tokens per block (the next block's
+//               load in flight during the fold), one mad.wide per output and block.
 // Every wait is bounded (kWaitLimit); a wait that gives up records APX_ERR_DEVICE_TIMEOUT,
 // drains what the CTA has in flight and frees its TMEM before returning.
 #include <cuda.h>
@@ -52,32 +55,35 @@ constexpr int kTileM = 128;
 constexpr int kTileN = 64;
 constexpr int kSlab = 128;  // K bytes per stage (4 blocks): one 128B swizzle atom per row
 constexpr int kStages = 4;
-constexpr int kBufs = 2;    // TMEM buffers of one stage's 4 blocks × kTileN columns (512 in all)
+constexpr int kBufs = 2;    // TMEM buffers of one stage: 4 blocks × kTileN columns (512 in all)
 constexpr int kBufCols = (kSlab / 32) * kTileN;
 constexpr int kEpiWarps = 8;  // 2 per SM sub-partition: 32 rows × 32 tokens each
 constexpr int kEpiTok = 32;
 constexpr int kThreads = 32 * (2 + kEpiWarps);
+constexpr int kPlanes = 4;   // activation planes x, x[s>=1], x[s>=2], x[s>=2]: shifts s <= 2
+constexpr int kMaxShift = 2;
 constexpr int kStageA = kTileM * kSlab;           // 16 KB of weight codes
-constexpr int kStageB = kTileN * kSlab;           // 8 KB of activation codes
+constexpr int kStageB = kTileN * kSlab;           // 8 KB per activation plane
 constexpr int kStageM = kTileM * (kSlab / 32) * 4;  // 2 KB: M of 4 blocks × 128 rows
-constexpr int kStageS = kTileN * (kSlab / 32) * 4;  // 1 KB: s of 4 blocks × 64 tokens
-constexpr int kStageBytes = 28 * 1024;            // one stage, 1024-aligned
-constexpr int kStageTx = kStageA + kStageB + kStageM + kStageS;
+constexpr int kStageBytes = 50 * 1024;            // one stage, 1024-aligned
 constexpr int kFallbackCtas = 32;        // extra CTAs of each launch for the checked columns
-constexpr int kSpreadLimit = 20;         // weight + activation exponent spread of the i64 fold
+constexpr int kSpreadLimit = 20;         // weight exponent spread: M stays in int32
 constexpr int kMaxBlocks = (1 << 13) - 1;  // the i64 fold's bound on the block count
 constexpr unsigned kRouteNone = 0, kRouteGemm = 1, kRouteChecked = 2;
 
 static_assert(kStageA % 1024 == 0 && kStageB % 1024 == 0 && kStageBytes % 1024 == 0 &&
-                  kStageTx <= kStageBytes,
+                  kStageA + kPlanes * kStageB + kStageM <= kStageBytes,
               "stages keep the 1024-byte alignment of the swizzled tiles");
 
 // ---- descriptors ---------------------------------------------------------------------------
 
 // Instruction descriptor of kind::i8: D s32 (2) at bits 4-5, A and B signed 8-bit (1) at
 // bits 7-9 and 10-12, both K-major, N>>3 at bits 17-22, M>>4 at bits 24-28.
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) |
-                            ((uint32_t)(kTileN >> 3) << 17) | ((uint32_t)(kTileM >> 4) << 24);
+constexpr uint32_t idesc_i8(int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(kTileM >> 4) << 24);
+}
+constexpr uint32_t kIdesc64 = idesc_i8(kTileN);  // one plane
 
 // Shared-memory matrix descriptor of a K-major operand in the 128B-swizzled layout TMA
 // writes: start address >> 4 in bits 0-13, leading byte offset 16 (>> 4) in bits 16-29,
@@ -95,13 +101,15 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
       : "memory");
 }
 
-__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc) {
+// D (+)= A·B for one 32-lane block; `accumulate` 0 overwrites D.
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
   const uint32_t zero = 0;
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(
           d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(zero), "r"(zero), "r"(zero), "r"(zero),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(zero), "r"(zero), "r"(zero),
       "r"(zero));
 }
 
@@ -123,6 +131,16 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
+        "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
@@ -140,31 +158,26 @@ __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// acc += a·b, 32×32 → 64-bit multiply-add in one instruction.
+// acc += a·b, 32×32 → 64-bit multiply-add in one instruction.  `volatile` keeps the
+// instruction as written: left free, the compiler's rewrite of a run of these into
+// separate multiplies and 64-bit adds measured about twice as slow on sm_100a.
 __device__ __forceinline__ void mad_wide(long long &acc, int a, int b) {
-  asm("mad.wide.s32 %0, %1, %2, %0;" : "+l"(acc) : "r"(a), "r"(b));
+  asm volatile("mad.wide.s32 %0, %1, %2, %0;" : "+l"(acc) : "r"(a), "r"(b));
 }
 
-// acc[j] += D[j]·(m << s[j]) for 32 tokens: the shift on the integer ALU, the widening
-// multiply-add on the FMA pipe.  |m << s| < 2^31 and |D| <= 2^19 by the route's limits.
-__device__ __forceinline__ void fold32(long long (&acc)[32], const uint32_t (&d)[32], int32_t m,
-                                       const int32_t *s) {
-  const int4 *sv = reinterpret_cast<const int4 *>(s);
+// acc[j] += D'[j]·M for the warp's tokens (D' = D·2^s formed by the tensor cores), one
+// widening multiply-add each.  |D'| <= 2^21 and |M| < 2^31.
+__device__ __forceinline__ void fold(long long (&acc)[kEpiTok], const uint32_t (&d)[kEpiTok],
+                                     int32_t m) {
 #pragma unroll
-  for (int j4 = 0; j4 < 8; j4++) {
-    const int4 v = sv[j4];
-    mad_wide(acc[4 * j4 + 0], (int)d[4 * j4 + 0], (int)__funnelshift_l(0u, (unsigned)m, v.x));
-    mad_wide(acc[4 * j4 + 1], (int)d[4 * j4 + 1], (int)__funnelshift_l(0u, (unsigned)m, v.y));
-    mad_wide(acc[4 * j4 + 2], (int)d[4 * j4 + 2], (int)__funnelshift_l(0u, (unsigned)m, v.z));
-    mad_wide(acc[4 * j4 + 3], (int)d[4 * j4 + 3], (int)__funnelshift_l(0u, (unsigned)m, v.w));
-  }
+  for (int j = 0; j < kEpiTok; j++) mad_wide(acc[j], (int)d[j], m);
 }
 
 // ---- per-call workspace ------------------------------------------------------------------------
 
 struct WorkView {
-  int8_t *bcodes;    // [n_cols][kp]
-  int32_t *ptab;     // [nb][n_cols_pad] e − emin_c (0 for a zero scale or a checked column)
+  int8_t *bcodes;    // [kPlanes][n_cols_pad][kp]: plane k holds the codes of blocks with s >= k
+  int32_t *ptab;     // [nb][n_cols_pad] s = e − emin_c (0 for a zero scale or a checked column)
   int32_t *emin;     // [n_cols_pad]
   uint32_t *route;   // [n_cols_pad]
   int32_t *fb;       // [0] count, [1] CTAs done, [2..] checked-route columns
@@ -196,7 +209,7 @@ static WorkView work_view(void *base, size_t n_cols, int nb) {
 size_t gemm_work_bytes(size_t n_cols, size_t n_in) {
   const size_t nb = (n_in + 31) / 32, kp = (n_in + kSlab - 1) / kSlab * kSlab;
   const size_t np = cols_pad(n_cols);
-  return gemm_work_head_bytes(n_cols) + 2 * np * 4 + nb * np * 4 + 256 + n_cols * kp;
+  return gemm_work_head_bytes(n_cols) + 2 * np * 4 + nb * np * 4 + 256 + kPlanes * np * kp;
 }
 
 // ---- activation prep: describe, route, B operand, P table -----------------------------------
@@ -206,7 +219,7 @@ struct PrepArgs {
   const uint8_t *exps;  // caller exponent bytes, column c at c·ldb
   const ActDesc *descs; // the quantizer's descriptors (a refusal there wins), or null
   size_t ld, ldb, n_in, kp;
-  int nb, n_cols, ks;
+  int nb, n_cols;
   WorkView w;
   unsigned long long *status;  // column c's refusal word at status[c·2]
 };
@@ -216,8 +229,11 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(PrepArgs a) {
   __shared__ unsigned s_m128, s_route;
   const int c = blockIdx.x;
   const size_t np = cols_pad((size_t)a.n_cols);
-  if (c >= a.n_cols) {  // padding tokens of the last tile: P = 0
+  if (c >= a.n_cols) {  // padding tokens of the last tile: no shift, zero planes
     for (int b = threadIdx.x; b < a.nb; b += blockDim.x) a.w.ptab[(size_t)b * np + c] = 0;
+    for (size_t j = (size_t)threadIdx.x * 16; j < a.kp; j += (size_t)blockDim.x * 16)
+      for (int k = 0; k < kPlanes; k++)
+        *reinterpret_cast<uint4 *>(a.w.bcodes + (k * np + c) * a.kp + j) = make_uint4(0, 0, 0, 0);
     if (threadIdx.x == 0) {
       a.w.emin[c] = 0;
       a.w.route[c] = kRouteNone;
@@ -233,6 +249,9 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(PrepArgs a) {
   __syncthreads();
   if (s_status != APX_OK) {  // refused by the quantizer: its codes and exponents are not set
     for (int b = threadIdx.x; b < a.nb; b += blockDim.x) a.w.ptab[(size_t)b * np + c] = 0;
+    for (size_t j = (size_t)threadIdx.x * 16; j < a.kp; j += (size_t)blockDim.x * 16)
+      for (int k = 0; k < kPlanes; k++)
+        *reinterpret_cast<uint4 *>(a.w.bcodes + (k * np + c) * a.kp + j) = make_uint4(0, 0, 0, 0);
     if (threadIdx.x == 0) {
       atomicMin(a.status + (size_t)c * 2, pack_status(0, (unsigned)s_status, 0));
       a.w.emin[c] = 0;
@@ -273,7 +292,7 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(PrepArgs a) {
     if (s_status != APX_OK) {
       atomicMin(a.status + (size_t)c * 2, pack_status(0, (unsigned)s_status, 0));
     } else if (!s_m128 && bound_ok((long long)a.n_in, Fam<kQ8_0>::top, s_emax) &&
-               (s_emax < 0 || s_emax - emin + a.ks <= kSpreadLimit)) {
+               (s_emax < 0 || s_emax - emin <= kMaxShift)) {
       route = kRouteGemm;
     } else {
       route = kRouteChecked;
@@ -292,11 +311,15 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(PrepArgs a) {
     const unsigned e = exps[b];
     a.w.ptab[(size_t)b * np + c] = gemm && e != APX_EXP_ZERO ? (int)(e - emin) : 0;
   }
-  // B operand row: 16 codes per thread step, zero for zero-scale blocks and past n_in
+  // B planes of the column: x, x[s >= 1], x[s >= 2], x[s >= 2] (x: the codes, zero for
+  // zero-scale blocks and past n_in), so that the four planes sum to x·2^s
+  const size_t plane = np * a.kp;
   int8_t *dst = a.w.bcodes + (size_t)c * a.kp;
   for (size_t j = (size_t)threadIdx.x * 16; j < a.kp; j += (size_t)blockDim.x * 16) {
     uint4 v = make_uint4(0, 0, 0, 0);
+    int sh = 0;
     if (gemm && j < a.n_in && exps[j / 32] != APX_EXP_ZERO) {
+      sh = (int)exps[j / 32] - emin;
       if (j + 16 <= a.n_in) {
         v = *reinterpret_cast<const uint4 *>(codes + j);
       } else {
@@ -305,7 +328,10 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(PrepArgs a) {
         memcpy(&v, t, 16);
       }
     }
-    *reinterpret_cast<uint4 *>(dst + j) = v;
+    const uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int k = 0; k < kPlanes; k++)
+      *reinterpret_cast<uint4 *>(dst + k * plane + j) = sh >= (k < 2 ? k : 2) ? v : z;
   }
 }
 
@@ -327,7 +353,7 @@ struct GemmArgs {
   size_t ld, ldb, n_in;
 };
 
-__device__ __forceinline__ void checked_columns(const GemmArgs &g) {
+__device__ __forceinline__ void checked_columns(const GemmArgs g) {
   volatile int32_t *fb = g.w.fb;
   const long long n = fb[0];
   const long long items = n * (long long)g.n_out;
@@ -356,14 +382,14 @@ __device__ __forceinline__ void checked_columns(const GemmArgs &g) {
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_q8_0_kernel(const __grid_constant__ CUtensorMap map_w,
                      const __grid_constant__ CUtensorMap map_x,
-                     const __grid_constant__ CUtensorMap map_m,
-                     const __grid_constant__ CUtensorMap map_s, GemmArgs g) {
+                     const __grid_constant__ CUtensorMap map_m, GemmArgs g) {
   if ((int)blockIdx.x >= g.tiles) {
     checked_columns(g);
     return;
   }
-  // stage s: weight codes (16 KB, 128B-swizzled), activation codes (8 KB, swizzled),
-  // M of its 4 blocks × 128 rows (int32), shifts of its 4 blocks × 64 tokens (int32)
+  // stage st: weight codes (16 KB, 128B-swizzled), activation planes 0..3 (8 KB each,
+  // swizzled; only the planes the stage's blocks use are loaded), M of its 4 blocks × 128
+  // rows (int32); per stage and block the largest shift of the tile's tokens
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -372,19 +398,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *dempty = dfull + kBufs, *mdone = dempty + kBufs;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mdone + 1);
   int *timeout = reinterpret_cast<int *>(tmem_slot + 1);
+  // [kStages][4] largest shift per block, 16-byte aligned for one vector read per stage
+  int *smax = reinterpret_cast<int *>((reinterpret_cast<uintptr_t>(timeout + 1) + 15) &
+                                      ~(uintptr_t)15);
   auto stage_a = [&](int st) { return smem + st * kStageBytes; };
-  auto stage_b = [&](int st) { return smem + st * kStageBytes + kStageA; };
   auto stage_m = [&](int st) {
-    return reinterpret_cast<const int32_t *>(smem + st * kStageBytes + kStageA + kStageB);
-  };
-  auto stage_s = [&](int st) {
-    return reinterpret_cast<const int32_t *>(smem + st * kStageBytes + kStageA + kStageB +
-                                             kStageM);
+    return reinterpret_cast<const int32_t *>(smem + st * kStageBytes + kStageA +
+                                             kPlanes * kStageB);
   };
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int mt = (int)blockIdx.x % g.m_tiles, nt = (int)blockIdx.x / g.m_tiles;
   const int m0 = mt * kTileM, n0 = nt * kTileN;
+  const int np = (int)cols_pad((size_t)g.n_cols);
 
   if (threadIdx.x == 0) {
     for (int st = 0; st < kStages; st++) {
@@ -401,7 +427,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_w)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_x)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_m)) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_s)) : "memory");
   }
   if (warp == 1) {  // TMEM: kBufs × kBufCols columns of 32-bit accumulators
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -416,64 +441,102 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ---- TMA producer ----
-    if (lane == 0) {
-      int issued = 0;
-      for (int kt = 0; kt < g.kslabs; kt++) {
-        const int st = kt % kStages, use = kt / kStages;
+    // ---- TMA producer (the whole warp reads the stage's shifts, lane 0 issues).  The
+    // shifts of stage kt+1 are loaded while the warp waits for stage kt's slot ----
+    int issued = 0;
+    auto load_shifts = [&](int kt, int (&v)[4]) {
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const int b = 4 * kt + q;
+        v[q] = 0;
+        if (b < g.nb) {
+          const int32_t *r = g.w.ptab + (size_t)b * np + n0;
+          v[q] = max(r[lane], r[32 + lane]);
+        }
+      }
+    };
+    int cur[4], nxt[4];
+    load_shifts(0, cur);
+    for (int kt = 0; kt < g.kslabs; kt++) {
+      const int st = kt % kStages, use = kt / kStages;
+      if (kt + 1 < g.kslabs) load_shifts(kt + 1, nxt);
+      // the largest shift of each block over the tile's 64 tokens: planes and MMAs per block
+      int sq[4], smax_stage = 0;
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        sq[q] = __reduce_max_sync(0xFFFFFFFFu, cur[q]);
+        smax_stage = max(smax_stage, sq[q]);
+      }
+      int stop = 0;
+      if (lane == 0) {
         if (use > 0 && !mbar_wait(empty + st, (use - 1) & 1)) {
           atomicExch(timeout, 1);
-          break;
+          stop = 1;
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; q++) smax[st * 4 + q] = sq[q];
+          uint8_t *base = stage_a(st);
+          const int planes = smax_stage == 0 ? 1 : (smax_stage == 1 ? 2 : 4);
+          mbar_expect_tx(full + st, kStageA + kStageM + planes * kStageB);
+          tma_load_2d(base, &map_w, kt * kSlab, m0, full + st);
+          tma_load_2d(base + kStageA + kPlanes * kStageB, &map_m, m0, kt * (kSlab / 32),
+                      full + st);
+          for (int k = 0; k < planes; k++)
+            tma_load_2d(base + kStageA + k * kStageB, &map_x, kt * kSlab, k * np + n0,
+                        full + st);
+          issued++;
         }
-        if (atomicAdd(timeout, 0)) break;
-        uint8_t *base = stage_a(st);
-        mbar_expect_tx(full + st, kStageTx);
-        tma_load_2d(base, &map_w, kt * kSlab, m0, full + st);
-        tma_load_2d(base + kStageA, &map_x, kt * kSlab, n0, full + st);
-        tma_load_2d(base + kStageA + kStageB, &map_m, m0, kt * (kSlab / 32), full + st);
-        tma_load_2d(base + kStageA + kStageB + kStageM, &map_s, n0, kt * (kSlab / 32),
-                    full + st);
-        issued++;
       }
-      // every copy this thread started has landed before the CTA may exit
+      if (__shfl_sync(0xFFFFFFFFu, stop, 0)) break;
+#pragma unroll
+      for (int q = 0; q < 4; q++) cur[q] = nxt[q];
+    }
+    // every copy this thread started has landed before the CTA may exit
+    if (lane == 0)
       for (int kt = issued > kStages ? issued - kStages : 0; kt < issued; kt++)
         mbar_wait(full + kt % kStages, (kt / kStages) & 1);
-    }
   } else if (warp == 1) {
-    // ---- MMA issuer: a stage's 4 blocks into one TMEM buffer, one commit per stage ----
+    // ---- MMA issuer: per block D' = A·x + A·x[s>=1] + A·x[s>=2] + A·x[s>=2] = D·2^s,
+    // one accumulating MMA per plane the block needs (1, 2 or 4); a stage's 4 blocks into
+    // one TMEM buffer, one commit per stage ----
     if (lane == 0) {
-      volatile int *vt = timeout;
       const uint64_t a0 = kDescHi | (smem_addr(stage_a(0)) >> 4);
-      const uint64_t b0 = kDescHi | (smem_addr(stage_b(0)) >> 4);
-      for (int kt = 0; kt < g.kslabs && !*vt; kt++) {
-        const int st = kt % kStages, use = kt / kStages, buf = kt % kBufs, ub = kt / kBufs;
-        if (!mbar_wait(full + st, use & 1) ||
-            (ub > 0 && !mbar_wait(dempty + buf, (ub - 1) & 1))) {
-          atomicExch(timeout, 1);
+      const uint64_t b0 = kDescHi | (smem_addr(stage_a(0) + kStageA) >> 4);
+      constexpr uint64_t kPlaneStep = kStageB >> 4;
+      bool ok = true;
+      for (int kt = 0; kt < g.kslabs; kt++) {
+        const int st = kt % kStages, buf = kt % kBufs;
+        if (!mbar_wait(full + st, (kt / kStages) & 1) ||
+            (kt >= kBufs && !mbar_wait(dempty + buf, ((kt / kBufs) - 1) & 1))) {
+          ok = false;
           break;
         }
         tc_fence_after();
-        // descriptor start addresses advance 16 bytes per unit: 32 bytes per block
         const uint64_t ad = a0 + (uint64_t)(st * (kStageBytes >> 4));
         const uint64_t bd = b0 + (uint64_t)(st * (kStageBytes >> 4));
-        const uint32_t dt = tmem + (uint32_t)(buf * kBufCols);
-        if (4 * kt + 4 <= g.nb) {
-          mma_i8(dt, ad, bd);
-          mma_i8(dt + kTileN, ad + 2, bd + 2);
-          mma_i8(dt + 2 * kTileN, ad + 4, bd + 4);
-          mma_i8(dt + 3 * kTileN, ad + 6, bd + 6);
-        } else {
-          for (int q = 0; q < g.nb - 4 * kt; q++)
-            mma_i8(dt + q * kTileN, ad + 2 * q, bd + 2 * q);
+        const int4 sq4 = *reinterpret_cast<const int4 *>(smax + st * 4);
+        const int sqa[4] = {sq4.x, sq4.y, sq4.z, sq4.w};
+        const int nq = min(4, g.nb - 4 * kt);
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          if (q >= nq) break;
+          const uint32_t d = tmem + (uint32_t)(buf * kBufCols + q * kTileN);
+          const uint64_t aq = ad + 2 * q, bq = bd + 2 * q;
+          mma_i8(d, aq, bq, kIdesc64, 0u);
+          if (sqa[q] >= 1) mma_i8(d, aq, bq + kPlaneStep, kIdesc64, 1u);
+          if (sqa[q] >= 2) {
+            mma_i8(d, aq, bq + 2 * kPlaneStep, kIdesc64, 1u);
+            mma_i8(d, aq, bq + 3 * kPlaneStep, kIdesc64, 1u);
+          }
         }
         mma_commit(dfull + buf);
       }
+      if (!ok) atomicExch(timeout, 1);
       mma_commit(mdone);
       if (!mbar_wait(mdone, 0)) atomicExch(timeout, 1);
     }
   } else {
-    // ---- epilogue: 32 rows × 32 tokens per warp, block by block; the TMEM load of block
-    // b+1 is in flight while block b is folded ----
+    // ---- epilogue: 32 rows × 32 tokens per warp; one wake-up per stage (4 blocks) ----
     const int lg = warp % 4;  // the TMEM lane quarter this warp may read
     const int tq = (warp - 2) / 4;
     const int rl = 32 * lg + lane;
@@ -483,62 +546,61 @@ __global__ void __launch_bounds__(kThreads, 1)
     long long acc[kEpiTok];
 #pragma unroll
     for (int j = 0; j < kEpiTok; j++) acc[j] = 0;
-    // block b: stage kt = b/4, TMEM buffer kt % kBufs, columns (b % 4)·kTileN
-    auto tcol = [&](int b) {
-      return trow + (uint32_t)(((b >> 2) % kBufs) * kBufCols + (b & 3) * kTileN);
-    };
-    // wait for stage kt: its M / shift tables (TMA) and its dots (MMA commit)
-    auto enter = [&](int kt) {
-      if (!mbar_wait(full + kt % kStages, (kt / kStages) & 1) ||
-          !mbar_wait(dfull + kt % kBufs, (kt / kBufs) & 1))
-        return false;
+    bool ok = true;
+    for (int kt = 0; kt < g.kslabs; kt++) {
+      const int st = kt % kStages, buf = kt % kBufs;
+      // the stage's M table (TMA) and its dots (MMA commit)
+      if (!mbar_wait(full + st, (kt / kStages) & 1) ||
+          !mbar_wait(dfull + buf, (kt / kBufs) & 1)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
-      return true;
-    };
-    auto step = [&](int b, uint32_t(&cur)[kEpiTok], uint32_t(&nxt)[kEpiTok]) {
-      tmem_wait_ld();  // cur holds block b's dots
-      const int kt = b >> 2, q = b & 3, st = kt % kStages;
-      const bool stage_end = q == 3 || b == g.nb - 1;
-      if (stage_end) {  // every dot of stage kt is in registers: its TMEM buffer is free
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(dempty + kt % kBufs);
+      const int nq = min(4, g.nb - 4 * kt);
+      const int32_t *sm = stage_m(st) + rl;
+      const uint32_t t = trow + (uint32_t)(buf * kBufCols);
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        if (2 * h >= nq) break;
+        uint32_t d0[kEpiTok], d1[kEpiTok];
+        const bool two = 2 * h + 1 < nq;
+        tmem_ld32_nowait(t + (uint32_t)(2 * h * kTileN), d0);
+        if (two) tmem_ld32_nowait(t + (uint32_t)((2 * h + 1) * kTileN), d1);
+        tmem_wait_ld();
+        fold(acc, d0, sm[2 * h * kTileM]);
+        if (two) fold(acc, d1, sm[(2 * h + 1) * kTileM]);
       }
-      if (b + 1 < g.nb) {
-        if (stage_end && !enter(kt + 1)) return false;
-        tmem_ld32_nowait(tcol(b + 1), nxt);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(dempty + buf);  // the dots are folded
+        mbar_arrive(empty + st);    // and the stage's table read
       }
-      fold32(acc, cur, stage_m(st)[q * kTileM + rl], stage_s(st) + q * kTileN + c0);
-      if (stage_end) {  // the stage's tables are read
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty + st);
-      }
-      return true;
-    };
-    bool ok = g.nb == 0 || enter(0);
-    uint32_t da[kEpiTok], db[kEpiTok];
-    if (ok && g.nb > 0) tmem_ld32_nowait(tcol(0), da);
-    for (int b = 0; ok && b < g.nb; b += 2) {
-      ok = step(b, da, db);
-      if (ok && b + 1 < g.nb) ok = step(b + 1, db, da);
     }
     if (!ok) atomicExch(timeout, 1);
-    if (ok && row < g.n_out) {
+    if (__all_sync(0xFFFFFFFFu, ok)) {
+      // the warp's 32 tokens: route and emin read once (lane j holds token j), then
+      // broadcast; every branch below is warp-uniform
+      const int mycol = n0 + c0 + lane;
+      const uint32_t my_route = mycol < g.n_cols ? g.w.route[mycol] : kRouteNone;
+      const int my_emin = mycol < g.n_cols ? g.w.emin[mycol] : 0;
       const unsigned kmin = (unsigned)g.kmin[row];
+      const bool live = row < g.n_out;
 #pragma unroll
       for (int j = 0; j < kEpiTok; j++) {
-        const int col = n0 + c0 + j;
-        if (col >= g.n_cols || g.w.route[col] != kRouteGemm) continue;
+        const uint32_t r = __shfl_sync(0xFFFFFFFFu, my_route, j);
+        const int e = __shfl_sync(0xFFFFFFFFu, my_emin, j);
+        if (r != kRouteGemm || !live) continue;
+        const size_t col = (size_t)(n0 + c0 + j);
         Acc128 a;
-        shl128(acc[j], kmin + (unsigned)g.w.emin[col], a.lo, a.hi);
+        shl128(acc[j], kmin + (unsigned)e, a.lo, a.hi);
         long long v;
         if (!acc_round_to_i64(a, v)) {
-          atomicMin(g.status + (size_t)col * 2, pack_status(row, kKindOutputOverflow, 0));
+          atomicMin(g.status + col * 2, pack_status(row, kKindOutputOverflow, 0));
           continue;
         }
-        if (g.out_q32) g.out_q32[(size_t)col * g.n_out + row] = v;
-        if (g.out_f32)
-          g.out_f32[(size_t)col * g.n_out + row] = __ll2float_rn(v) * 2.3283064365386963e-10f;
+        if (g.out_q32) g.out_q32[col * g.n_out + row] = v;
+        if (g.out_f32) g.out_f32[col * g.n_out + row] = __ll2float_rn(v) * 2.3283064365386963e-10f;
       }
     }
   }
@@ -720,13 +782,18 @@ void free_gemm_layout(GemmLayout *lay) {
 }
 
 static size_t gemm_smem_bytes() {
-  return 1024 + (size_t)kStages * kStageBytes + (2 * kStages + 2 * kBufs + 1) * 8 + 16;
+  return 1024 + (size_t)kStages * kStageBytes + (2 * kStages + 2 * kBufs + 1) * 8 + 32 +
+         kStages * 4 * 4;
 }
 
 bool gemm_shape_ok(size_t n_in) { return n_in && (n_in + 31) / 32 <= (size_t)kMaxBlocks; }
 
 bool gemm_supported(const GemmLayout &lay) {
-  return lay.base && lay.nb > 0 && lay.nb <= kMaxBlocks && lay.kspread <= kSpreadLimit;
+  // |D·2^s·M| < 2^(33 + kspread) per block; nb of them stay inside i64
+  int lg = 0;
+  while ((1 << lg) < lay.nb) lg++;
+  return lay.base && lay.nb > 0 && lay.nb <= kMaxBlocks && lay.kspread <= kSpreadLimit &&
+         lay.kspread <= 30 - lg;
 }
 
 cudaError_t launch_gemm_q8_0(const GemvPlan &pl, const uint8_t *pack, const GemmLayout &lay,
@@ -746,16 +813,14 @@ cudaError_t launch_gemm_q8_0(const GemvPlan &pl, const uint8_t *pack, const Gemm
   pa.kp = lay.kp;
   pa.nb = lay.nb;
   pa.n_cols = (int)n_cols;
-  pa.ks = lay.kspread;
   pa.w = w;
   pa.status = status;
   gemm_prep_kernel<<<(unsigned)cols_pad(n_cols), 256, 0, stream>>>(pa);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
 
-  CUtensorMap map_x, map_s;
-  if (!make_map(&map_x, w.bcodes, lay.kp, n_cols, lay.kp, kTileN) ||
-      !make_table_map(&map_s, w.ptab, cols_pad(n_cols), (uint64_t)lay.nb, kTileN))
+  CUtensorMap map_x;
+  if (!make_map(&map_x, w.bcodes, lay.kp, kPlanes * cols_pad(n_cols), lay.kp, kTileN))
     return cudaErrorInvalidValue;
   GemmArgs a;
   a.wmul = lay.wmul;
@@ -783,7 +848,7 @@ cudaError_t launch_gemm_q8_0(const GemvPlan &pl, const uint8_t *pack, const Gemm
   if (e != cudaSuccess) return e;
   gemm_q8_0_kernel<<<(unsigned)(a.tiles + kFallbackCtas), kThreads, smem, stream>>>(
       *reinterpret_cast<const CUtensorMap *>(lay.map), map_x,
-      *reinterpret_cast<const CUtensorMap *>(lay.map_m), map_s, a);
+      *reinterpret_cast<const CUtensorMap *>(lay.map_m), a);
   return cudaGetLastError();
 }
 

@@ -139,7 +139,7 @@ __device__ __forceinline__ bool add_checked(Acc128 &a, long long plo, long long 
 }
 
 template <uint32_t T>
-__device__ __noinline__ void checked_row(const PackGeo &g, size_t row, size_t n_out, size_t n_in,
+__device__ __noinline__ void checked_row(const PackGeo g, size_t row, size_t n_out, size_t n_in,
                                          const int8_t *codes, const uint8_t *exps,
                                          long long *out_q32, float *out_f32,
                                          unsigned long long *status) {
