@@ -173,6 +173,46 @@ __device__ __forceinline__ void fold(long long (&acc)[kEpiTok], const uint32_t (
   for (int j = 0; j < kEpiTok; j++) mad_wide(acc[j], (int)d[j], m);
 }
 
+// The finish of one output: v = round_shift_32(acc·2^s) (value.rs:10-12 on the 128-bit
+// product) with the i64 range check of chart/mod.rs:1746-1753, and its f32 image
+// F32::from_q32(v).  For s >= 32 the product has no fractional part: v = acc·2^(s−32) when
+// that fits, and f32(v·2^-32) = RN(acc)·2^(s−64) (a power-of-two scaling commutes with the
+// one rounding).  For s < 32, v = (acc + 2^(31−s)) >> (32−s), which always fits (|acc| < 2^62
+// by the route's bound), and its f32 image is RN(v)·2^-32.  One conversion either way.
+__device__ __forceinline__ bool finish_one(long long acc, unsigned s, long long &v, float &f) {
+  bool fits = true;
+  long long x;  // the integer whose rounding gives the f32 image
+  int k;        // its power-of-two scale
+  if (s >= 32) {
+    const unsigned t = s - 32;
+    v = (long long)((unsigned long long)acc << (t & 63));
+    fits = t > 63 ? acc == 0 : (acc >> (63 - t)) == (acc >> 63);
+    x = acc;
+    k = (int)s - 64;
+  } else {
+    const unsigned t = 32 - s;
+    v = (acc + (1ll << (t - 1))) >> t;
+    x = v;
+    k = -32;
+  }
+  f = __ll2float_rn(x) * __int_as_float((127 + k) << 23);
+  return fits;
+}
+
+// finish_one for the common case 32 <= s < 64 with the range check on the accumulator's
+// high word alone: acc·2^t fits i64 iff acc >> (63 − t) is 0 or -1, and for t < 32 that
+// shift reads only the high 32 bits.
+__device__ __forceinline__ bool finish_fast(long long acc, unsigned s, long long &v, float &f) {
+  if (s >= 32 && s < 64) {
+    const unsigned t = s - 32;
+    const int hi = (int)(acc >> 32);
+    v = (long long)((unsigned long long)acc << t);
+    f = __ll2float_rn(acc) * __int_as_float((int)(s + 63) << 23);  // 2^(s − 64)
+    return (hi >> (31 - t)) == (hi >> 31);
+  }
+  return finish_one(acc, s, v, f);
+}
+
 // ---- per-call workspace ------------------------------------------------------------------------
 
 struct WorkView {
@@ -401,6 +441,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // [kStages][4] largest shift per block, 16-byte aligned for one vector read per stage
   int *smax = reinterpret_cast<int *>((reinterpret_cast<uintptr_t>(timeout + 1) + 15) &
                                       ~(uintptr_t)15);
+  // per token of the tile: the finish shift emin_c, or -1 where the token is not the GEMM's
+  int *stok = smax + kStages * 4;
   auto stage_a = [&](int st) { return smem + st * kStageBytes; };
   auto stage_m = [&](int st) {
     return reinterpret_cast<const int32_t *>(smem + st * kStageBytes + kStageA +
@@ -427,6 +469,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_w)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_x)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_m)) : "memory");
+  }
+  if (threadIdx.x >= 64 && threadIdx.x < 64 + kTileN) {
+    const int c = n0 + (int)threadIdx.x - 64;
+    stok[threadIdx.x - 64] =
+        c < g.n_cols && g.w.route[c] == kRouteGemm ? g.w.emin[c] : -1;
   }
   if (warp == 1) {  // TMEM: kBufs × kBufCols columns of 32-bit accumulators
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -578,29 +625,67 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (!ok) atomicExch(timeout, 1);
-    if (__all_sync(0xFFFFFFFFu, ok)) {
-      // the warp's 32 tokens: route and emin read once (lane j holds token j), then
-      // broadcast; every branch below is warp-uniform
-      const int mycol = n0 + c0 + lane;
-      const uint32_t my_route = mycol < g.n_cols ? g.w.route[mycol] : kRouteNone;
-      const int my_emin = mycol < g.n_cols ? g.w.emin[mycol] : 0;
+    // ---- finish: acc·2^(kmin_r + emin_c) rounded to Q32.32 and to f32 ----
+    // The stage ring is idle once every epilogue warp is past its last read (named barrier
+    // 1).  Phase A: each thread rounds its 32 tokens into a [token][row] tile in shared
+    // memory.  Phase B: each warp stores whole token rows (128 rows of one token are
+    // contiguous in the output) with 16-byte stores.
+    const int ew = warp - 2;
+    const bool all_ok = __all_sync(0xFFFFFFFFu, ok);
+    asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
+    float *sf = reinterpret_cast<float *>(smem);                      // [64 tokens][128 rows]
+    long long *sv = reinterpret_cast<long long *>(smem + 32 * 1024);  // [64 tokens][128 rows]
+    if (all_ok) {
+      // 32 independent chains side by side (the conversions are long-latency)
       const unsigned kmin = (unsigned)g.kmin[row];
       const bool live = row < g.n_out;
+      uint32_t bad = 0;  // bit j: token j's output leaves i64
 #pragma unroll
       for (int j = 0; j < kEpiTok; j++) {
-        const uint32_t r = __shfl_sync(0xFFFFFFFFu, my_route, j);
-        const int e = __shfl_sync(0xFFFFFFFFu, my_emin, j);
-        if (r != kRouteGemm || !live) continue;
-        const size_t col = (size_t)(n0 + c0 + j);
-        Acc128 a;
-        shl128(acc[j], kmin + (unsigned)e, a.lo, a.hi);
+        const int e = stok[c0 + j];
         long long v;
-        if (!acc_round_to_i64(a, v)) {
-          atomicMin(g.status + col * 2, pack_status(row, kKindOutputOverflow, 0));
-          continue;
+        float f;
+        const bool fits = finish_fast(acc[j], kmin + (unsigned)e, v, f);
+        sf[(c0 + j) * kTileM + rl] = fits ? f : __int_as_float(0x7FC00000);
+        if (g.out_q32) sv[(c0 + j) * kTileM + rl] = fits ? v : 0;
+        bad |= (e >= 0 && live && !fits) ? 1u << j : 0u;
+      }
+      while (bad) {  // output overflow: rare, one refusal per token
+        const int j = __ffs(bad) - 1;
+        bad &= bad - 1;
+        atomicMin(g.status + (size_t)(n0 + c0 + j) * 2, pack_status(row, kKindOutputOverflow, 0));
+      }
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
+    if (__all_sync(0xFFFFFFFFu, all_ok)) {
+      const int rows = (int)min((size_t)kTileM, g.n_out - (size_t)m0);
+      const bool full_rows = rows == kTileM;
+      for (int tok = ew; tok < kTileN; tok += kEpiWarps) {
+        if (stok[tok] < 0) continue;  // warp-uniform
+        const size_t base = (size_t)(n0 + tok) * g.n_out + m0;
+        const int r = 4 * lane;
+        if (g.out_f32) {
+          const float4 f4 = *reinterpret_cast<const float4 *>(sf + tok * kTileM + r);
+          float *dst = g.out_f32 + base + r;
+          if (full_rows && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+            *reinterpret_cast<float4 *>(dst) = f4;
+          } else {
+            const float fv[4] = {f4.x, f4.y, f4.z, f4.w};
+            for (int u = 0; u < 4; u++)
+              if (r + u < rows) dst[u] = fv[u];
+          }
         }
-        if (g.out_q32) g.out_q32[col * g.n_out + row] = v;
-        if (g.out_f32) g.out_f32[col * g.n_out + row] = __ll2float_rn(v) * 2.3283064365386963e-10f;
+        if (g.out_q32) {
+          const long long *src = sv + tok * kTileM + r;
+          long long *dst = g.out_q32 + base + r;
+          if (full_rows && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+            reinterpret_cast<longlong2 *>(dst)[0] = reinterpret_cast<const longlong2 *>(src)[0];
+            reinterpret_cast<longlong2 *>(dst)[1] = reinterpret_cast<const longlong2 *>(src)[1];
+          } else {
+            for (int u = 0; u < 4; u++)
+              if (r + u < rows) dst[u] = src[u];
+          }
+        }
       }
     }
   }
@@ -783,7 +868,7 @@ void free_gemm_layout(GemmLayout *lay) {
 
 static size_t gemm_smem_bytes() {
   return 1024 + (size_t)kStages * kStageBytes + (2 * kStages + 2 * kBufs + 1) * 8 + 32 +
-         kStages * 4 * 4;
+         kStages * 4 * 4 + kTileN * 4;
 }
 
 bool gemm_shape_ok(size_t n_in) { return n_in && (n_in + 31) / 32 <= (size_t)kMaxBlocks; }
