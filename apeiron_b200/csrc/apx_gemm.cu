@@ -41,6 +41,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <cstring>
 #include <mutex>
@@ -216,6 +217,8 @@ __device__ __forceinline__ bool finish_fast(long long acc, unsigned s, long long
 // ---- per-call workspace ------------------------------------------------------------------------
 
 struct WorkView {
+  int *cnt;          // split-K arrival counters, one per tile (a fixed 4 KB at the start)
+  long long *part;   // split-K partial sums
   int8_t *bcodes;    // [kPlanes][n_cols_pad][kp]: plane k holds the codes of blocks with s >= k
   int32_t *ptab;     // [nb][n_cols_pad] s = e − emin_c (0 for a zero scale or a checked column)
   int32_t *emin;     // [n_cols_pad]
@@ -229,10 +232,26 @@ static __host__ __device__ size_t cols_pad(size_t n_cols) {
 
 size_t gemm_work_head_bytes(size_t n_cols) { return (n_cols + 2 + 63) / 64 * 256; }
 
-static WorkView work_view(void *base, size_t n_cols, int nb) {
+constexpr size_t kCntBytes = 4096;  // split-K counters: at most 1024 split tiles
+
+// Split K when the tiles alone leave SMs idle: the largest split that keeps one wave.
+static int gemm_ksplit(size_t tiles, int kslabs, int sm_count) {
+  if (tiles == 0 || tiles >= (size_t)sm_count || tiles > kCntBytes / 4) return 1;
+  return (int)std::max<size_t>(1, std::min<size_t>({(size_t)sm_count / tiles, (size_t)kslabs,
+                                                    (size_t)8}));
+}
+
+static size_t part_bytes(size_t tiles, int ksplit) {
+  return ksplit > 1 ? tiles * ksplit * kEpiWarps * 1024 * sizeof(long long) : 0;
+}
+
+static WorkView work_view(void *base, size_t n_cols, int nb, size_t kp, size_t tiles,
+                          int ksplit) {
   uint8_t *p = static_cast<uint8_t *>(base);
   const size_t np = cols_pad(n_cols);
   WorkView w;
+  w.cnt = reinterpret_cast<int *>(p);
+  p += kCntBytes;
   w.fb = reinterpret_cast<int32_t *>(p);
   p += gemm_work_head_bytes(n_cols);
   w.route = reinterpret_cast<uint32_t *>(p);
@@ -243,13 +262,25 @@ static WorkView work_view(void *base, size_t n_cols, int nb) {
   p += (size_t)nb * np * 4;
   w.bcodes =
       reinterpret_cast<int8_t *>((reinterpret_cast<uintptr_t>(p) + 255) & ~(uintptr_t)255);
+  p = reinterpret_cast<uint8_t *>(w.bcodes) + kPlanes * np * kp;
+  w.part = ksplit > 1 ? reinterpret_cast<long long *>(
+                            (reinterpret_cast<uintptr_t>(p) + 255) & ~(uintptr_t)255)
+                      : nullptr;
+  (void)tiles;
   return w;
 }
 
-size_t gemm_work_bytes(size_t n_cols, size_t n_in) {
+static size_t gemm_tiles(size_t n_out, size_t n_cols) {
+  return ((n_out + kTileM - 1) / kTileM) * ((n_cols + kTileN - 1) / kTileN);
+}
+
+size_t gemm_work_bytes(size_t n_cols, size_t n_in, size_t n_out, int sm_count) {
   const size_t nb = (n_in + 31) / 32, kp = (n_in + kSlab - 1) / kSlab * kSlab;
   const size_t np = cols_pad(n_cols);
-  return gemm_work_head_bytes(n_cols) + 2 * np * 4 + nb * np * 4 + 256 + kPlanes * np * kp;
+  const size_t tiles = gemm_tiles(n_out, n_cols);
+  const int ks = gemm_ksplit(tiles, (int)(kp / kSlab), sm_count);
+  return kCntBytes + gemm_work_head_bytes(n_cols) + 2 * np * 4 + nb * np * 4 + 256 +
+         kPlanes * np * kp + 256 + part_bytes(tiles, ks);
 }
 
 // ---- activation prep: describe, route, B operand, P table -----------------------------------
@@ -386,6 +417,11 @@ struct GemmArgs {
   unsigned long long *status;  // column c at status[c·2]
   size_t n_out, m_pad;
   int n_cols, nb, kslabs, m_tiles, tiles;
+  // split K: ksplit CTAs per tile, each over a contiguous range of slabs; their exact i64
+  // partial sums meet in `part`, and the last to arrive (per-tile counter) finishes
+  int ksplit;
+  long long *part;  // [tiles][ksplit][kEpiWarps][32 tokens][32 lanes]
+  int *cnt;         // [tiles], zero between calls
   // checked route (matvec_fixed per row) of the columns the prep kernel listed
   PackGeo geo;
   const int8_t *codes;
@@ -397,7 +433,8 @@ __device__ __forceinline__ void checked_columns(const GemmArgs g) {
   volatile int32_t *fb = g.w.fb;
   const long long n = fb[0];
   const long long items = n * (long long)g.n_out;
-  const long long first = (long long)(blockIdx.x - g.tiles) * blockDim.x + threadIdx.x;
+  const long long first =
+      (long long)(blockIdx.x - g.tiles * g.ksplit) * blockDim.x + threadIdx.x;
   for (long long i = first; i < items; i += (long long)kFallbackCtas * blockDim.x) {
     const int c = fb[2 + i / (long long)g.n_out];
     const size_t row = (size_t)(i % (long long)g.n_out);
@@ -423,7 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_q8_0_kernel(const __grid_constant__ CUtensorMap map_w,
                      const __grid_constant__ CUtensorMap map_x,
                      const __grid_constant__ CUtensorMap map_m, GemmArgs g) {
-  if ((int)blockIdx.x >= g.tiles) {
+  if ((int)blockIdx.x >= g.tiles * g.ksplit) {
     checked_columns(g);
     return;
   }
@@ -443,6 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                       ~(uintptr_t)15);
   // per token of the tile: the finish shift emin_c, or -1 where the token is not the GEMM's
   int *stok = smax + kStages * 4;
+  int *sflag = stok + kTileN;  // split K: this CTA is the tile's last split
   auto stage_a = [&](int st) { return smem + st * kStageBytes; };
   auto stage_m = [&](int st) {
     return reinterpret_cast<const int32_t *>(smem + st * kStageBytes + kStageA +
@@ -450,7 +488,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   };
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int mt = (int)blockIdx.x % g.m_tiles, nt = (int)blockIdx.x / g.m_tiles;
+  const int tile = (int)blockIdx.x % g.tiles, split = (int)blockIdx.x / g.tiles;
+  const int mt = tile % g.m_tiles, nt = tile / g.m_tiles;
+  // this CTA's slabs [kt0, kt0 + nk)
+  const int kt0 = (int)((long long)split * g.kslabs / g.ksplit);
+  const int nk = (int)((long long)(split + 1) * g.kslabs / g.ksplit) - kt0;
   const int m0 = mt * kTileM, n0 = nt * kTileN;
   const int np = (int)cols_pad((size_t)g.n_cols);
 
@@ -503,10 +545,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     };
     int cur[4], nxt[4];
-    load_shifts(0, cur);
-    for (int kt = 0; kt < g.kslabs; kt++) {
-      const int st = kt % kStages, use = kt / kStages;
-      if (kt + 1 < g.kslabs) load_shifts(kt + 1, nxt);
+    load_shifts(kt0, cur);
+    for (int lk = 0; lk < nk; lk++) {
+      const int kt = kt0 + lk, st = lk % kStages, use = lk / kStages;
+      if (lk + 1 < nk) load_shifts(kt + 1, nxt);
       // the largest shift of each block over the tile's 64 tokens: planes and MMAs per block
       int sq[4], smax_stage = 0;
 #pragma unroll
@@ -540,8 +582,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // every copy this thread started has landed before the CTA may exit
     if (lane == 0)
-      for (int kt = issued > kStages ? issued - kStages : 0; kt < issued; kt++)
-        mbar_wait(full + kt % kStages, (kt / kStages) & 1);
+      for (int lk = issued > kStages ? issued - kStages : 0; lk < issued; lk++)
+        mbar_wait(full + lk % kStages, (lk / kStages) & 1);
   } else if (warp == 1) {
     // ---- MMA issuer: per block D' = A·x + A·x[s>=1] + A·x[s>=2] + A·x[s>=2] = D·2^s,
     // one accumulating MMA per plane the block needs (1, 2 or 4); a stage's 4 blocks into
@@ -551,10 +593,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t b0 = kDescHi | (smem_addr(stage_a(0) + kStageA) >> 4);
       constexpr uint64_t kPlaneStep = kStageB >> 4;
       bool ok = true;
-      for (int kt = 0; kt < g.kslabs; kt++) {
-        const int st = kt % kStages, buf = kt % kBufs;
-        if (!mbar_wait(full + st, (kt / kStages) & 1) ||
-            (kt >= kBufs && !mbar_wait(dempty + buf, ((kt / kBufs) - 1) & 1))) {
+      for (int lk = 0; lk < nk; lk++) {
+        const int kt = kt0 + lk, st = lk % kStages, buf = lk % kBufs;
+        if (!mbar_wait(full + st, (lk / kStages) & 1) ||
+            (lk >= kBufs && !mbar_wait(dempty + buf, ((lk / kBufs) - 1) & 1))) {
           ok = false;
           break;
         }
@@ -594,11 +636,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int j = 0; j < kEpiTok; j++) acc[j] = 0;
     bool ok = true;
-    for (int kt = 0; kt < g.kslabs; kt++) {
-      const int st = kt % kStages, buf = kt % kBufs;
+    for (int lk = 0; lk < nk; lk++) {
+      const int kt = kt0 + lk, st = lk % kStages, buf = lk % kBufs;
       // the stage's M table (TMA) and its dots (MMA commit)
-      if (!mbar_wait(full + st, (kt / kStages) & 1) ||
-          !mbar_wait(dfull + buf, (kt / kBufs) & 1)) {
+      if (!mbar_wait(full + st, (lk / kStages) & 1) ||
+          !mbar_wait(dfull + buf, (lk / kBufs) & 1)) {
         ok = false;
         break;
       }
@@ -631,7 +673,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     // memory.  Phase B: each warp stores whole token rows (128 rows of one token are
     // contiguous in the output) with 16-byte stores.
     const int ew = warp - 2;
-    const bool all_ok = __all_sync(0xFFFFFFFFu, ok);
+    bool all_ok = __all_sync(0xFFFFFFFFu, ok);
+    if (g.ksplit > 1) {
+      // publish this split's partial sums; the last split of the tile to arrive adds the
+      // others' (exact i64 additions) and finishes, the rest are done
+      long long *mine = g.part + (((size_t)tile * g.ksplit + split) * kEpiWarps + ew) * 1024;
+#pragma unroll
+      for (int j = 0; j < kEpiTok; j++) mine[j * 32 + lane] = acc[j];
+      __threadfence();
+      asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
+      if (threadIdx.x == 64) *sflag = atomicAdd(g.cnt + tile, 1) == g.ksplit - 1;
+      asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
+      const bool last = *sflag != 0;
+      if (!last) all_ok = false;  // another split of this tile finishes
+      if (last) {
+        __threadfence();
+        for (int sp = 0; sp < g.ksplit; sp++) {
+          if (sp == split) continue;
+          const long long *other =
+              g.part + (((size_t)tile * g.ksplit + sp) * kEpiWarps + ew) * 1024;
+#pragma unroll
+          for (int j = 0; j < kEpiTok; j++) acc[j] += __ldcg(other + j * 32 + lane);
+        }
+        if (threadIdx.x == 64) g.cnt[tile] = 0;  // ready for the next call
+      }
+    }
     asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
     float *sf = reinterpret_cast<float *>(smem);                      // [64 tokens][128 rows]
     long long *sv = reinterpret_cast<long long *>(smem + 32 * 1024);  // [64 tokens][128 rows]
@@ -868,7 +934,7 @@ void free_gemm_layout(GemmLayout *lay) {
 
 static size_t gemm_smem_bytes() {
   return 1024 + (size_t)kStages * kStageBytes + (2 * kStages + 2 * kBufs + 1) * 8 + 32 +
-         kStages * 4 * 4 + kTileN * 4;
+         kStages * 4 * 4 + kTileN * 4 + 16;
 }
 
 bool gemm_shape_ok(size_t n_in) { return n_in && (n_in + 31) / 32 <= (size_t)kMaxBlocks; }
@@ -885,9 +951,11 @@ cudaError_t launch_gemm_q8_0(const GemvPlan &pl, const uint8_t *pack, const Gemm
                              size_t n_out, size_t n_in, size_t n_cols, const int8_t *codes,
                              size_t ld, const uint8_t *exps, size_t ldb, const void *descs,
                              void *work, long long *out_q32, float *out_f32,
-                             unsigned long long *status, cudaStream_t stream) {
+                             unsigned long long *status, int sm_count, cudaStream_t stream) {
   if (n_cols == 0 || n_out == 0) return cudaSuccess;
-  const WorkView w = work_view(work, n_cols, lay.nb);
+  const size_t tiles = gemm_tiles(n_out, n_cols);
+  const int ksplit = gemm_ksplit(tiles, (int)(lay.kp / kSlab), sm_count);
+  const WorkView w = work_view(work, n_cols, lay.nb, lay.kp, tiles, ksplit);
   PrepArgs pa;
   pa.codes = codes;
   pa.exps = exps;
@@ -921,6 +989,9 @@ cudaError_t launch_gemm_q8_0(const GemvPlan &pl, const uint8_t *pack, const Gemm
   a.kslabs = (int)(lay.kp / kSlab);
   a.m_tiles = (int)((n_out + kTileM - 1) / kTileM);
   a.tiles = a.m_tiles * (int)((n_cols + kTileN - 1) / kTileN);
+  a.ksplit = ksplit;
+  a.part = w.part;
+  a.cnt = w.cnt;
   a.geo = PackGeo{pack, pl.units, pl.L};
   a.codes = codes;
   a.exps = exps;
@@ -931,7 +1002,7 @@ cudaError_t launch_gemm_q8_0(const GemvPlan &pl, const uint8_t *pack, const Gemm
   e = cudaFuncSetAttribute(gemm_q8_0_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem);
   if (e != cudaSuccess) return e;
-  gemm_q8_0_kernel<<<(unsigned)(a.tiles + kFallbackCtas), kThreads, smem, stream>>>(
+  gemm_q8_0_kernel<<<(unsigned)(a.tiles * ksplit + kFallbackCtas), kThreads, smem, stream>>>(
       *reinterpret_cast<const CUtensorMap *>(lay.map), map_x,
       *reinterpret_cast<const CUtensorMap *>(lay.map_m), a);
   return cudaGetLastError();

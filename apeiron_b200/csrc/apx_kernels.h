@@ -72,7 +72,7 @@ void free_gemm_layout(GemmLayout *lay);
 bool gemm_shape_ok(size_t n_in);
 bool gemm_supported(const GemmLayout &lay);
 // Device workspace of one call (zeroed once at allocation; its list counters reset themselves).
-size_t gemm_work_bytes(size_t n_cols, size_t n_in);
+size_t gemm_work_bytes(size_t n_cols, size_t n_in, size_t n_out, int sm_count);
 size_t gemm_work_head_bytes(size_t n_cols);
 // Exact k-column Q8_0 projection: column c's codes at codes + c·ld (16-byte aligned, ld a
 // multiple of 16, readable up to the 128-byte-padded width), exponent bytes at exps + c·ldb,
@@ -82,7 +82,7 @@ cudaError_t launch_gemm_q8_0(const GemvPlan &pl, const uint8_t *pack, const Gemm
                              size_t n_out, size_t n_in, size_t n_cols, const int8_t *codes,
                              size_t ld, const uint8_t *exps, size_t ldb, const void *descs,
                              void *work, long long *out_q32, float *out_f32,
-                             unsigned long long *status, cudaStream_t stream);
+                             unsigned long long *status, int sm_count, cudaStream_t stream);
 
 // Debug: exact int32 group dots from the repacked layout (apx_gemv.cu).
 cudaError_t launch_block_dots(const GemvPlan &pl, uint32_t type, const uint8_t *pack,

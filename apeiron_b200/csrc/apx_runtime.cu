@@ -315,8 +315,8 @@ bool gemm_route(apx_ctx *ctx, Tensor &t, size_t n_out, size_t n_in, size_t k_col
   return gemm_supported(t.gemm);
 }
 
-cudaError_t ensure_gwork(apx_ctx *ctx, size_t n_cols, size_t n_in) {
-  const size_t need = gemm_work_bytes(n_cols, n_in);
+cudaError_t ensure_gwork(apx_ctx *ctx, size_t n_cols, size_t n_in, size_t n_out) {
+  const size_t need = gemm_work_bytes(n_cols, n_in, n_out, ctx->sm_count);
   if (need <= ctx->gwork.cap) return cudaSuccess;
   cudaError_t e = ctx->gwork.ensure(need);
   if (e == cudaSuccess) e = cudaMemset(ctx->gwork.p, 0, ctx->gwork.cap);
@@ -334,7 +334,7 @@ int matmat_gemm_sync(apx_ctx *ctx, Tensor &t, size_t n_out, size_t n_in, size_t 
   cudaError_t e;
   if ((e = ctx->dev.ensure(out_sz + in_sz)) != cudaSuccess) return cuda_err(err, e);
   if ((e = ctx->host.ensure(out_sz + in_sz)) != cudaSuccess) return cuda_err(err, e);
-  if ((e = ensure_gwork(ctx, k, n_in)) != cudaSuccess) return cuda_err(err, e);
+  if ((e = ensure_gwork(ctx, k, n_in, n_out)) != cudaSuccess) return cuda_err(err, e);
   uint8_t *h = (uint8_t *)ctx->host.p, *d = (uint8_t *)ctx->dev.p;
   uint8_t *hs = h + out_sz, *he = hs + st_sz, *hc = he + ex_sz;
   std::memset(hs, 0xFF, k * 16);
@@ -348,7 +348,7 @@ int matmat_gemm_sync(apx_ctx *ctx, Tensor &t, size_t n_out, size_t n_in, size_t 
   if (e == cudaSuccess)
     e = launch_gemm_q8_0(t.plan, t.d_pack, t.gemm, n_out, n_in, k, (const int8_t *)dc, ld, de,
                          nb, nullptr, ctx->gwork.p, (long long *)d, nullptr,
-                         (unsigned long long *)ds, ctx->stream);
+                         (unsigned long long *)ds, ctx->sm_count, ctx->stream);
   if (e == cudaSuccess)
     e = cudaMemcpyAsync(h, d, out_sz + k * 16, cudaMemcpyDeviceToHost, ctx->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
@@ -682,7 +682,7 @@ int apx_matmat_f32(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in, siz
   if ((e = ctx->scratch.ensure(ds_sz + ex_sz + k_cols * ld)) != cudaSuccess)
     return cuda_err(err, e);
   const bool gemm = gemm_route(ctx, *t, n_out, n_in, k_cols);
-  if (gemm && (e = ensure_gwork(ctx, k_cols, n_in)) != cudaSuccess) return cuda_err(err, e);
+  if (gemm && (e = ensure_gwork(ctx, k_cols, n_in, n_out)) != cudaSuccess) return cuda_err(err, e);
   uint8_t *h = (uint8_t *)ctx->host.p, *d = (uint8_t *)ctx->dev.p;
   uint8_t *sc = (uint8_t *)ctx->scratch.p;
   uint8_t *descs = sc, *dexp = sc + ds_sz;
@@ -697,7 +697,8 @@ int apx_matmat_f32(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in, siz
   unsigned long long *status = (unsigned long long *)(d + y_sz);
   if (e == cudaSuccess && gemm) {
     e = launch_gemm_q8_0(t->plan, t->d_pack, t->gemm, n_out, n_in, k_cols, dcod, ld, dexp, ldb,
-                         descs, ctx->gwork.p, nullptr, (float *)d, status, ctx->stream);
+                         descs, ctx->gwork.p, nullptr, (float *)d, status, ctx->sm_count,
+                         ctx->stream);
   } else {
     for (size_t c = 0; e == cudaSuccess && c < k_cols; c++)
       e = launch_gemv(t->plan, t->type, t->d_pack, t->d_scratch, n_out, n_in, dcod + c * ld,
@@ -821,11 +822,11 @@ int apx_matmat_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in, s
   {
     std::lock_guard<std::mutex> g(ctx->mu);
     if (gemm_route(ctx, *t, n_out, n_in, k_cols)) {
-      if (ensure_gwork(ctx, k_cols, n_in) != cudaSuccess) return APX_ERR_OUT_OF_MEMORY;
+      if (ensure_gwork(ctx, k_cols, n_in, n_out) != cudaSuccess) return APX_ERR_OUT_OF_MEMORY;
       cudaError_t e = launch_gemm_q8_0(t->plan, t->d_pack, t->gemm, n_out, n_in, k_cols, d_codes,
                                        ld, d_exps, ldb, d_descs, ctx->gwork.p, (long long *)d_out_q32,
                                        d_out_f32, (unsigned long long *)d_status,
-                                       (cudaStream_t)stream);
+                                       ctx->sm_count, (cudaStream_t)stream);
       return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
     }
   }
