@@ -316,6 +316,12 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(PrepArgs a) {
     s_emax = -1;
     s_status = a.descs ? a.descs[c].status : APX_OK;
     s_m128 = 0;
+    if (a.descs && s_status == APX_OK) {  // the quantizer's descriptor: no re-scan
+      const ActDesc d = a.descs[c];
+      s_emax = d.emax;
+      s_emin = d.emax >= 0 ? d.emin : 1 << 30;
+      s_m128 = d.pad[0] & 1u;
+    }
   }
   __syncthreads();
   if (s_status != APX_OK) {  // refused by the quantizer: its codes and exponents are not set
@@ -333,8 +339,9 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(PrepArgs a) {
   const int8_t *codes = a.codes + (size_t)c * a.ld;
   const uint8_t *exps = a.exps + (size_t)c * a.ldb;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = blockDim.x / 32;
-  // describe (QuantAct's Q32.32 image, chart/mod.rs:124-181), as the GEMV's descriptor does
-  for (int b = warp; b < a.nb; b += nw) {
+  // describe (QuantAct's Q32.32 image, chart/mod.rs:124-181), as the GEMV's descriptor does,
+  // unless the quantizer's descriptor came with the call
+  for (int b = warp; !a.descs && b < a.nb; b += nw) {
     const unsigned e = exps[b];
     if (e == APX_EXP_ZERO) continue;
     if (e > 62) {

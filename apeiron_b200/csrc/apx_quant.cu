@@ -18,12 +18,15 @@ __device__ __forceinline__ unsigned long long uabs64(long long v) {
   return v < 0 ? 0ull - (unsigned long long)v : (unsigned long long)v;
 }
 
-// act_scale exponent, or -1 for a zero block, or 99 when the reference returns None.
+// act_scale exponent, or -1 for a zero block, or 99 when the reference returns None: the
+// smallest e >= 0 with 127·2^e >= absmax (pow2.rs:22-39).  With bl the bit length of absmax
+// and e0 = max(0, bl − 7), 127·2^(e0−1) < 2^(bl−1) <= absmax, so e is e0 or e0 + 1; 127·2^e0
+// stays below 2^64 for every absmax <= 2^63.  No division.
 __device__ __forceinline__ int act_scale_exp(unsigned long long absmax) {
   if (absmax == 0) return -1;
-  unsigned long long need = absmax / 127ull + (absmax % 127ull != 0 ? 1ull : 0ull);
-  if (need <= 1) return 0;
-  int e = 64 - __clzll((long long)(need - 1));
+  const int bl = 64 - __clzll((long long)absmax);
+  const int e0 = bl > 7 ? bl - 7 : 0;
+  const int e = (127ull << e0) >= absmax ? e0 : e0 + 1;
   return e > 62 ? 99 : e;
 }
 
@@ -154,29 +157,40 @@ __global__ void quant_kernel(const void *xin, size_t n, size_t ldx, int8_t *code
   __syncthreads();
   const size_t nb = (n + 31) / 32;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = blockDim.x / 32;
+  // per-warp descriptor statistics, merged once at the end
+  int w_emin = 1 << 30, w_emax = -1, w_status = APX_OK;
+  unsigned w_nz = 0;
   for (size_t b = warp; b < nb; b += nw) {
     size_t j = b * 32 + lane;
     long long v = 0;
     bool ok = true;
-    if (j < n) {
-      if (F32)
-        ok = f32_to_q32(reinterpret_cast<const float *>(xin)[j], v);
-      else
-        v = reinterpret_cast<const long long *>(xin)[j];
-    }
-    if (__any_sync(0xFFFFFFFFu, !ok)) {
-      if (lane == 0) atomicMax(&acc.status, (int)APX_ERR_QUANT_REFUSED);
-      continue;
-    }
-    unsigned long long m = uabs64(v), mx = m;
+    unsigned long long mx;
+    if (F32) {
+      const float f = j < n ? reinterpret_cast<const float *>(xin)[j] : 0.0f;
+      ok = f32_to_q32(f, v);
+      if (__any_sync(0xFFFFFFFFu, !ok)) {
+        w_status = max(w_status, (int)APX_ERR_QUANT_REFUSED);
+        continue;
+      }
+      // |f| orders like round(|f|·2^32): the block absmax from the f32 bit patterns
+      const unsigned amax = __reduce_max_sync(0xFFFFFFFFu, __float_as_uint(f) & 0x7FFFFFFFu);
+      long long vm;
+      // every lane converted, so the only |f| without a positive image is 2^31 (a lane
+      // holding -2^31 = i64::MIN in Q32.32): its magnitude is 2^63
+      mx = f32_to_q32(__uint_as_float(amax), vm) ? (unsigned long long)vm : 1ull << 63;
+    } else {
+      if (j < n) v = reinterpret_cast<const long long *>(xin)[j];
+      mx = uabs64(v);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      unsigned long long t = __shfl_xor_sync(0xFFFFFFFFu, mx, o);
-      mx = t > mx ? t : mx;
+      for (int o = 16; o > 0; o >>= 1) {
+        unsigned long long t = __shfl_xor_sync(0xFFFFFFFFu, mx, o);
+        mx = t > mx ? t : mx;
+      }
     }
+    const unsigned long long m = uabs64(v);
     int e = act_scale_exp(mx);  // warp-uniform
     if (e == 99) {
-      if (lane == 0) atomicMax(&acc.status, (int)APX_ERR_QUANT_REFUSED);
+      w_status = max(w_status, (int)APX_ERR_QUANT_REFUSED);
       continue;
     }
     int code = 0;
@@ -186,20 +200,134 @@ __global__ void quant_kernel(const void *xin, size_t n, size_t ldx, int8_t *code
       code = v < 0 ? -(int)mag : (int)mag;
       bool bad = mag > 127 || !product_fits(code, e);
       if (__any_sync(0xFFFFFFFFu, bad)) {
-        if (lane == 0) atomicMax(&acc.status, (int)APX_ERR_QUANT_REFUSED);
+        w_status = max(w_status, (int)APX_ERR_QUANT_REFUSED);
         continue;
       }
-      if (lane == 0) {
-        atomicMin(&acc.emin, e);
-        atomicMax(&acc.emax, e);
-        atomicAdd(&acc.nz, 1u);
-      }
+      w_emin = min(w_emin, e);
+      w_emax = max(w_emax, e);
+      w_nz++;
     }
     if (j < n) codes[j] = (int8_t)code;
     if (lane == 0) exps[b] = e < 0 ? (uint8_t)APX_EXP_ZERO : (uint8_t)e;
   }
+  if (lane == 0) {
+    if (w_status != APX_OK) atomicMax(&acc.status, w_status);
+    if (w_emax >= 0) {
+      atomicMin(&acc.emin, w_emin);
+      atomicMax(&acc.emax, w_emax);
+      atomicAdd(&acc.nz, w_nz);
+    }
+  }
   __syncthreads();
   desc_write(&acc, desc, n);
+}
+
+// f32 vectors, bandwidth-shaped: a warp takes 128 lanes (4 blocks) per step, each thread 4
+// consecutive lanes (one 16-byte load, one 4-byte store of codes); the block absmax reduces
+// over its 8 threads on the f32 bit patterns (|f| orders like round(|f|·2^32)).  Same
+// results and descriptor as quant_kernel<true>; vector c at x + c·ldx, ldx a multiple of 4.
+__global__ void quant_f32_vec_kernel(const float *x, size_t n, size_t ldx, int8_t *codes,
+                                     size_t ld, uint8_t *exps, size_t ldb, ActDesc *desc) {
+  __shared__ DescAcc acc;
+  const size_t c = blockIdx.x;
+  x += c * ldx;
+  codes += c * ld;
+  exps += c * ldb;
+  desc_init(&acc);
+  __syncthreads();
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = blockDim.x / 32;
+  int w_emin = 1 << 30, w_emax = -1, w_status = APX_OK;
+  unsigned w_nz = 0;
+  for (size_t base = (size_t)warp * 128; base < n; base += (size_t)nw * 128) {
+    const size_t j = base + 4 * lane;  // first of this thread's 4 lanes
+    float f[4] = {0.f, 0.f, 0.f, 0.f};
+    if (j + 4 <= n) {
+      const float4 v4 = *reinterpret_cast<const float4 *>(x + j);
+      f[0] = v4.x; f[1] = v4.y; f[2] = v4.z; f[3] = v4.w;
+    } else {
+      for (int u = 0; u < 4; u++)
+        if (j + u < n) f[u] = x[j + u];
+    }
+    long long v[4];
+    bool ok = true;
+    unsigned amax = 0;
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      ok &= f32_to_q32(f[u], v[u]);
+      amax = max(amax, __float_as_uint(f[u]) & 0x7FFFFFFFu);
+    }
+    // block-level decisions: the 8 threads agree (shuffles within the 8-lane group)
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) {
+      amax = max(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+      ok &= __shfl_xor_sync(0xFFFFFFFFu, (int)ok, o) != 0;
+    }
+    int e = -1;
+    uint32_t packed = 0;
+    bool blk_ok = ok;
+    if (blk_ok) {
+      long long vm;
+      const unsigned long long mx =
+          f32_to_q32(__uint_as_float(amax), vm) ? (unsigned long long)vm : 1ull << 63;
+      e = act_scale_exp(mx);
+      if (e == 99) blk_ok = false;
+    }
+    bool bad = false;
+    if (blk_ok && e >= 0) {
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const unsigned long long m = uabs64(v[u]);
+        const unsigned long long S = 1ull << e, q = m >> e, r = m & (S - 1);
+        const unsigned long long mag = q + (2 * r >= S ? 1ull : 0ull);
+        const int code = v[u] < 0 ? -(int)mag : (int)mag;
+        bad |= mag > 127 || !product_fits(code, e);
+        packed |= ((uint32_t)(uint8_t)(int8_t)code) << (8 * u);
+      }
+    }
+    // every lane takes part in the group reductions (the branch above is group-dependent)
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) bad |= __shfl_xor_sync(0xFFFFFFFFu, (int)bad, o) != 0;
+    if (bad) blk_ok = false;
+    const bool leader = (lane & 7) == 0 && j < n;
+    if (!blk_ok) {
+      if (leader) w_status = max(w_status, (int)APX_ERR_QUANT_REFUSED);
+      continue;
+    }
+    if (j < n) {
+      if (j + 4 <= n) {
+        *reinterpret_cast<uint32_t *>(codes + j) = packed;
+      } else {
+        for (int u = 0; u < 4; u++)
+          if (j + u < n) codes[j + u] = (int8_t)(packed >> (8 * u));
+      }
+    }
+    if (leader) {
+      exps[j / 32] = e < 0 ? (uint8_t)APX_EXP_ZERO : (uint8_t)e;
+      if (e >= 0) {
+        w_emin = min(w_emin, e);
+        w_emax = max(w_emax, e);
+        w_nz++;
+      }
+    }
+  }
+  // merge the leaders' statistics
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    w_emin = min(w_emin, __shfl_xor_sync(0xFFFFFFFFu, w_emin, o));
+    w_emax = max(w_emax, __shfl_xor_sync(0xFFFFFFFFu, w_emax, o));
+    w_status = max(w_status, __shfl_xor_sync(0xFFFFFFFFu, w_status, o));
+    w_nz += __shfl_xor_sync(0xFFFFFFFFu, w_nz, o);
+  }
+  if (lane == 0) {
+    if (w_status != APX_OK) atomicMax(&acc.status, w_status);
+    if (w_emax >= 0) {
+      atomicMin(&acc.emin, w_emin);
+      atomicMax(&acc.emax, w_emax);
+      atomicAdd(&acc.nz, w_nz);
+    }
+  }
+  __syncthreads();
+  desc_write(&acc, desc + c, n);
 }
 
 cudaError_t launch_describe(const int8_t *codes, const uint8_t *exps, size_t n, int cols,
@@ -228,9 +356,17 @@ cudaError_t launch_quant_f32_cols(const float *x, size_t n, size_t ldx, int cols
                                   size_t ld, uint8_t *exps, size_t ldb, void *desc,
                                   cudaStream_t stream) {
   if (cols <= 0) return cudaSuccess;
-  const int threads = n <= 4096 ? 256 : 1024;
-  quant_kernel<true><<<cols, threads, 0, stream>>>(x, n, ldx, codes, ld, exps, ldb,
+  // 16-byte loads need 16-byte aligned vectors; the codes, 4-byte aligned rows
+  const bool vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && ldx % 4 == 0 &&
+                   (reinterpret_cast<uintptr_t>(codes) & 3) == 0 && ld % 4 == 0;
+  if (vec) {
+    quant_f32_vec_kernel<<<cols, 256, 0, stream>>>(x, n, ldx, codes, ld, exps, ldb,
                                                    reinterpret_cast<ActDesc *>(desc));
+  } else {
+    const int threads = n <= 4096 ? 256 : 1024;
+    quant_kernel<true><<<cols, threads, 0, stream>>>(x, n, ldx, codes, ld, exps, ldb,
+                                                     reinterpret_cast<ActDesc *>(desc));
+  }
   return cudaGetLastError();
 }
 
