@@ -8,16 +8,16 @@
 //     y[r,c] = round_shift_32( Σ_b m_{r,b}·2^(k_{r,b}+e_{c,b}) · D_b[r,c] ),
 //     D_b[r,c] = Σ_{i<32} q_{r,b,i}·x_{c,b,i}.
 // The tensor cores form every block's dot exactly (kind::i8, s32 accumulators in TMEM) and
-// also apply the activation's per-block power of two: with s = e − emin_c (0..3) they
-// accumulate D' = A·x + Σ_{k=1..s} 2^(k−1)·A·x = D·2^s from "planes" of the activation codes
-// (plane k holds the blocks whose s is at least k), 2^smax MMAs per block where smax is the
-// largest s of the tile's tokens.  The epilogue then folds each block with one widening
+// also apply the activation's per-block power of two: with s = e − emin_c (0..2) they
+// accumulate D' = A·x + A·x[s>=1] + 2·A·x[s>=2] = D·2^s from "planes" of the activation codes
+// (plane k holds the blocks whose s is at least k; the MMA of plane 2 is issued twice),
+// 2^smax MMAs per block where smax is the largest s of the tile's tokens.  The epilogue then folds each block with one widening
 // multiply-add, relative to the row's smallest weight exponent kmin_r, the way the
 // reference's gemm_q8_0 shift-accumulates (gemm.rs:99-102 spread_limit, 470-486):
 //     acc += D'_b · M_{r,b},   M = m·2^(k − kmin_r)
 // which is exact in i64 while |D'·M| < 2^(33+kspread) summed over the blocks stays below
 // 2^63.  y = round_shift_32(acc·2^(kmin_r+emin_c)) (pow2.rs:76-96 `finish`).  Columns whose
-// activation spread exceeds 3, outside the reference's i128 call bound (chart/mod.rs:
+// activation spread exceeds 2, outside the reference's i128 call bound (chart/mod.rs:
 // 362-383) or holding a code of -128 take matvec_fixed instead: the checked row path, by
 // extra CTAs of the same launch.
 //
@@ -30,7 +30,7 @@
 // Pipeline (one CTA per 128-row × 64-token tile, all of K):
 //   warp 0      TMA producer: 128-byte K slabs of W (128 rows) and of the planes the slab's
 //               blocks use (64 tokens), 128B-swizzled, and the slab's M table, into a
-//               4-stage ring (cp.async.bulk.tensor, no multicast);
+//               5-stage ring (cp.async.bulk.tensor, no multicast);
 //   warp 1      TMEM owner and MMA issuer: a slab's blocks into one of 2 TMEM buffers of
 //               4 × 64 columns, one tcgen05.commit per slab;
 //   warps 2..9  epilogue: tcgen05.ld of 32 rows × 32 tokens per block (the next block's
@@ -55,18 +55,18 @@ namespace apx {
 constexpr int kTileM = 128;
 constexpr int kTileN = 64;
 constexpr int kSlab = 128;  // K bytes per stage (4 blocks): one 128B swizzle atom per row
-constexpr int kStages = 4;
+constexpr int kStages = 5;
 constexpr int kBufs = 2;    // TMEM buffers of one stage: 4 blocks × kTileN columns (512 in all)
 constexpr int kBufCols = (kSlab / 32) * kTileN;
 constexpr int kEpiWarps = 8;  // 2 per SM sub-partition: 32 rows × 32 tokens each
 constexpr int kEpiTok = 32;
 constexpr int kThreads = 32 * (2 + kEpiWarps);
-constexpr int kPlanes = 4;   // activation planes x, x[s>=1], x[s>=2], x[s>=2]: shifts s <= 2
+constexpr int kPlanes = 3;   // activation planes x, x[s>=1], x[s>=2] (the last used twice): s <= 2
 constexpr int kMaxShift = 2;
 constexpr int kStageA = kTileM * kSlab;           // 16 KB of weight codes
 constexpr int kStageB = kTileN * kSlab;           // 8 KB per activation plane
 constexpr int kStageM = kTileM * (kSlab / 32) * 4;  // 2 KB: M of 4 blocks × 128 rows
-constexpr int kStageBytes = 50 * 1024;            // one stage, 1024-aligned
+constexpr int kStageBytes = 42 * 1024;            // one stage, 1024-aligned
 constexpr int kFallbackCtas = 32;        // extra CTAs of each launch for the checked columns
 constexpr int kSpreadLimit = 20;         // weight exponent spread: M stays in int32
 constexpr int kMaxBlocks = (1 << 13) - 1;  // the i64 fold's bound on the block count
@@ -389,8 +389,8 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(PrepArgs a) {
     const unsigned e = exps[b];
     a.w.ptab[(size_t)b * np + c] = gemm && e != APX_EXP_ZERO ? (int)(e - emin) : 0;
   }
-  // B planes of the column: x, x[s >= 1], x[s >= 2], x[s >= 2] (x: the codes, zero for
-  // zero-scale blocks and past n_in), so that the four planes sum to x·2^s
+  // B planes of the column: x, x[s >= 1], x[s >= 2] (x: the codes, zero for zero-scale
+  // blocks and past n_in), so that x + x[s >= 1] + 2·x[s >= 2] = x·2^s
   const size_t plane = np * a.kp;
   int8_t *dst = a.w.bcodes + (size_t)c * a.kp;
   for (size_t j = (size_t)threadIdx.x * 16; j < a.kp; j += (size_t)blockDim.x * 16) {
@@ -409,7 +409,7 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(PrepArgs a) {
     const uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
     for (int k = 0; k < kPlanes; k++)
-      *reinterpret_cast<uint4 *>(dst + k * plane + j) = sh >= (k < 2 ? k : 2) ? v : z;
+      *reinterpret_cast<uint4 *>(dst + k * plane + j) = sh >= k ? v : z;
   }
 }
 
@@ -471,7 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     checked_columns(g);
     return;
   }
-  // stage st: weight codes (16 KB, 128B-swizzled), activation planes 0..3 (8 KB each,
+  // stage st: weight codes (16 KB, 128B-swizzled), activation planes 0..2 (8 KB each,
   // swizzled; only the planes the stage's blocks use are loaded), M of its 4 blocks × 128
   // rows (int32); per stage and block the largest shift of the tile's tokens
   extern __shared__ uint8_t smem_raw[];
@@ -572,7 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int q = 0; q < 4; q++) smax[st * 4 + q] = sq[q];
           uint8_t *base = stage_a(st);
-          const int planes = smax_stage == 0 ? 1 : (smax_stage == 1 ? 2 : 4);
+          const int planes = smax_stage + 1;
           mbar_expect_tx(full + st, kStageA + kStageM + planes * kStageB);
           tma_load_2d(base, &map_w, kt * kSlab, m0, full + st);
           tma_load_2d(base + kStageA + kPlanes * kStageB, &map_m, m0, kt * (kSlab / 32),
@@ -592,8 +592,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int lk = issued > kStages ? issued - kStages : 0; lk < issued; lk++)
         mbar_wait(full + lk % kStages, (lk / kStages) & 1);
   } else if (warp == 1) {
-    // ---- MMA issuer: per block D' = A·x + A·x[s>=1] + A·x[s>=2] + A·x[s>=2] = D·2^s,
-    // one accumulating MMA per plane the block needs (1, 2 or 4); a stage's 4 blocks into
+    // ---- MMA issuer: per block D' = A·x + A·x[s>=1] + 2·A·x[s>=2] = D·2^s, 1, 2 or 4
+    // accumulating MMAs (the last plane's twice) as the block needs; a stage's 4 blocks into
     // one TMEM buffer, one commit per stage ----
     if (lane == 0) {
       const uint64_t a0 = kDescHi | (smem_addr(stage_a(0)) >> 4);
@@ -622,7 +622,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (sqa[q] >= 1) mma_i8(d, aq, bq + kPlaneStep, kIdesc64, 1u);
           if (sqa[q] >= 2) {
             mma_i8(d, aq, bq + 2 * kPlaneStep, kIdesc64, 1u);
-            mma_i8(d, aq, bq + 3 * kPlaneStep, kIdesc64, 1u);
+            mma_i8(d, aq, bq + 2 * kPlaneStep, kIdesc64, 1u);
           }
         }
         mma_commit(dfull + buf);

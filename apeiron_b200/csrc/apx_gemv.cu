@@ -182,44 +182,77 @@ __device__ __forceinline__ void fold_unit(Acc128 &acc, const UnitRegs<kQ8_0> &w,
 
 __device__ __forceinline__ unsigned byte_of(unsigned w, int i) { return (w >> (8 * i)) & 0xFFu; }
 
+// Group p's two dots (low nibbles: group 2p, high nibbles in place as 16·D: group 2p+1).
+__device__ __forceinline__ void q4k_dots(const UnitRegs<kQ4_K> &w, const int *a, int p, int &dl,
+                                         int &dh) {
+  const uint4 w0 = w.q[2 * p], w1 = w.q[2 * p + 1];
+  const int *xl = a + 16 * p, *xh = a + 16 * p + 8;
+  dl = dp4a_us(w0.x & 0x0F0F0F0Fu, xl[0], 0);
+  dl = dp4a_us(w0.y & 0x0F0F0F0Fu, xl[1], dl);
+  dl = dp4a_us(w0.z & 0x0F0F0F0Fu, xl[2], dl);
+  dl = dp4a_us(w0.w & 0x0F0F0F0Fu, xl[3], dl);
+  dl = dp4a_us(w1.x & 0x0F0F0F0Fu, xl[4], dl);
+  dl = dp4a_us(w1.y & 0x0F0F0F0Fu, xl[5], dl);
+  dl = dp4a_us(w1.z & 0x0F0F0F0Fu, xl[6], dl);
+  dl = dp4a_us(w1.w & 0x0F0F0F0Fu, xl[7], dl);
+  dh = dp4a_us(w0.x & 0xF0F0F0F0u, xh[0], 0);
+  dh = dp4a_us(w0.y & 0xF0F0F0F0u, xh[1], dh);
+  dh = dp4a_us(w0.z & 0xF0F0F0F0u, xh[2], dh);
+  dh = dp4a_us(w0.w & 0xF0F0F0F0u, xh[3], dh);
+  dh = dp4a_us(w1.x & 0xF0F0F0F0u, xh[4], dh);
+  dh = dp4a_us(w1.y & 0xF0F0F0F0u, xh[5], dh);
+  dh = dp4a_us(w1.z & 0xF0F0F0F0u, xh[6], dh);
+  dh = dp4a_us(w1.w & 0xF0F0F0F0u, xh[7], dh);
+}
+
+// er: the blocks' exponents relative to the call's smallest; xs: the blocks' Σxq.  When all
+// eight exponents are at most kQ4Narrow, each group's terms are below 975360·63·2^2 in
+// magnitude (|16·D| <= 16·32·15·127, scale <= 63) and eight of them stay below 2^31, so the
+// super-block folds in int32; otherwise in int64 (the call's spread limit keeps that exact).
+constexpr int kQ4Narrow = 2;
 __device__ __forceinline__ void fold_unit(Acc128 &acc, const UnitRegs<kQ4_K> &w, const int *a,
                                           const int *er, const long long *xs, int emin) {
   // get_scale_min_k4 (format/quant.rs:482-491) for all 8 pairs at once.
   const uint4 h = w.h;
-  unsigned sc_lo = h.y & 0x3F3F3F3Fu, mn_lo = h.z & 0x3F3F3F3Fu;
-  unsigned sc_hi = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
-  unsigned mn_hi = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
-  long long A16 = 0, B = 0;
+  const unsigned sc_lo = h.y & 0x3F3F3F3Fu, mn_lo = h.z & 0x3F3F3F3Fu;
+  const unsigned sc_hi = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+  const unsigned mn_hi = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+  const int4 e0 = reinterpret_cast<const int4 *>(er)[0], e1 = reinterpret_cast<const int4 *>(er)[1];
+  const int ev[8] = {e0.x, e0.y, e0.z, e0.w, e1.x, e1.y, e1.z, e1.w};
+  const int emax8 = max(max(max(e0.x, e0.y), max(e0.z, e0.w)), max(max(e1.x, e1.y), max(e1.z, e1.w)));
+  long long A16, B;
+  if (emax8 <= kQ4Narrow) {
+    int A32 = 0, B32 = 0;
 #pragma unroll
-  for (int p = 0; p < 4; p++) {
-    const uint4 w0 = w.q[2 * p], w1 = w.q[2 * p + 1];
-    const int *xl = a + 16 * p, *xh = a + 16 * p + 8;
-    int dl = 0, dh = 0;
-    dl = dp4a_us(w0.x & 0x0F0F0F0Fu, xl[0], dl);
-    dl = dp4a_us(w0.y & 0x0F0F0F0Fu, xl[1], dl);
-    dl = dp4a_us(w0.z & 0x0F0F0F0Fu, xl[2], dl);
-    dl = dp4a_us(w0.w & 0x0F0F0F0Fu, xl[3], dl);
-    dl = dp4a_us(w1.x & 0x0F0F0F0Fu, xl[4], dl);
-    dl = dp4a_us(w1.y & 0x0F0F0F0Fu, xl[5], dl);
-    dl = dp4a_us(w1.z & 0x0F0F0F0Fu, xl[6], dl);
-    dl = dp4a_us(w1.w & 0x0F0F0F0Fu, xl[7], dl);
-    // high nibbles in place: the dot comes out as 16·D
-    dh = dp4a_us(w0.x & 0xF0F0F0F0u, xh[0], dh);
-    dh = dp4a_us(w0.y & 0xF0F0F0F0u, xh[1], dh);
-    dh = dp4a_us(w0.z & 0xF0F0F0F0u, xh[2], dh);
-    dh = dp4a_us(w0.w & 0xF0F0F0F0u, xh[3], dh);
-    dh = dp4a_us(w1.x & 0xF0F0F0F0u, xh[4], dh);
-    dh = dp4a_us(w1.y & 0xF0F0F0F0u, xh[5], dh);
-    dh = dp4a_us(w1.z & 0xF0F0F0F0u, xh[6], dh);
-    dh = dp4a_us(w1.w & 0xF0F0F0F0u, xh[7], dh);
-    const int gl = 2 * p, gh = 2 * p + 1;
-    unsigned scl = byte_of(gl < 4 ? sc_lo : sc_hi, gl & 3);
-    unsigned sch = byte_of(gh < 4 ? sc_lo : sc_hi, gh & 3);
-    unsigned mnl = byte_of(gl < 4 ? mn_lo : mn_hi, gl & 3);
-    unsigned mnh = byte_of(gh < 4 ? mn_lo : mn_hi, gh & 3);
-    A16 += (long long)(dl << 4) * (long long)(int)(scl << er[gl]);
-    A16 += (long long)dh * (long long)(int)(sch << er[gh]);
-    B += xs[gl] * (long long)mnl + xs[gh] * (long long)mnh;
+    for (int p = 0; p < 4; p++) {
+      int dl, dh;
+      q4k_dots(w, a, p, dl, dh);
+      const int gl = 2 * p, gh = 2 * p + 1;
+      const unsigned scl = byte_of(gl < 4 ? sc_lo : sc_hi, gl & 3);
+      const unsigned sch = byte_of(gh < 4 ? sc_lo : sc_hi, gh & 3);
+      const unsigned mnl = byte_of(gl < 4 ? mn_lo : mn_hi, gl & 3);
+      const unsigned mnh = byte_of(gh < 4 ? mn_lo : mn_hi, gh & 3);
+      A32 += (dl << 4) * (int)(scl << ev[gl]) + dh * (int)(sch << ev[gh]);
+      B32 += (int)xs[gl] * (int)(mnl << ev[gl]) + (int)xs[gh] * (int)(mnh << ev[gh]);
+    }
+    A16 = A32;
+    B = B32;
+  } else {
+    A16 = 0;
+    B = 0;
+#pragma unroll
+    for (int p = 0; p < 4; p++) {
+      int dl, dh;
+      q4k_dots(w, a, p, dl, dh);
+      const int gl = 2 * p, gh = 2 * p + 1;
+      const unsigned scl = byte_of(gl < 4 ? sc_lo : sc_hi, gl & 3);
+      const unsigned sch = byte_of(gh < 4 ? sc_lo : sc_hi, gh & 3);
+      const unsigned mnl = byte_of(gl < 4 ? mn_lo : mn_hi, gl & 3);
+      const unsigned mnh = byte_of(gh < 4 ? mn_lo : mn_hi, gh & 3);
+      A16 += (long long)(dl << 4) * (long long)(int)(scl << ev[gl]);
+      A16 += (long long)dh * (long long)(int)(sch << ev[gh]);
+      B += (xs[gl] << ev[gl]) * (long long)mnl + (xs[gh] << ev[gh]) * (long long)mnh;
+    }
   }
   int md, mm;
   unsigned kd, km;
@@ -280,11 +313,16 @@ __device__ __forceinline__ bool fast_path(const ActDesc &desc, size_t n_in) {
 // family's fold reads.  Lanes load 16-byte chunks; slot s of the unit is chunks
 // [s·span/16, (s+1)·span/16).
 
+// A slot's codes are followed by 16 spare bytes, so that the L lanes of a row, which read
+// the same offset of L different slots, fall into different shared-memory banks.
+template <uint32_t T>
+__host__ __device__ constexpr int slot_ints() { return Fam<T>::span / 4 + 4; }
+
 template <uint32_t T>
 struct WarpAct {
-  int codes[4 * Fam<T>::span / 4];
+  int codes[4 * slot_ints<T>()];
   int e[4 * Fam<T>::span / 32];  // Q8_0: absolute exponent or -1; k-quants: er
-  long long xs[4 * Fam<T>::nxs];
+  long long xs[4 * Fam<T>::nxs];  // Q6_K: Σxq·2^er per 16 lanes; Q4_K: Σxq per 32 lanes
 };
 
 struct Chunk {
@@ -323,11 +361,11 @@ __device__ __forceinline__ void store_chunk(WarpAct<T> &w, Chunk s, int c, bool 
   s16 = dp4a_ss((int)v.w, 0x01010101, s16);
   const int s32 = s16 + __shfl_xor_sync(0xFFFFFFFFu, s16, 1);
   if (!in) return;
-  reinterpret_cast<uint4 *>(w.codes)[c] = v;
+  reinterpret_cast<uint4 *>(w.codes)[c + c / (Fam<T>::span / 16)] = v;  // past the slot pads
   if (T == kQ6_K) w.xs[c] = (long long)s16 << er;
   if ((c & 1) == 0) {
     w.e[c / 2] = T == kQ8_0 ? (zero ? -1 : (int)s.e) : er;
-    if (T == kQ4_K) w.xs[c / 2] = (long long)s32 << er;
+    if (T == kQ4_K) w.xs[c / 2] = s32;
   }
 }
 
@@ -410,7 +448,7 @@ __global__ void __launch_bounds__(384, 2) gemv_kernel(GemvArgs g) {
     store_chunk<T>(*w, ch0, lane, lane < nch, desc.emin);
     if (nch > 32) store_chunk<T>(*w, ch1, lane + 32, lane + 32 < nch, desc.emin);
     __syncwarp();
-    fold_unit(acc, cur, w->codes + slot * (F::span / 4), w->e + slot * (F::span / 32),
+    fold_unit(acc, cur, w->codes + slot * slot_ints<T>(), w->e + slot * (F::span / 32),
               w->xs + slot * F::nxs, desc.emin);
   }
   // the L lanes of a row combine
@@ -539,7 +577,7 @@ __global__ void __launch_bounds__(256, 2) gemv_stream_kernel(StreamArgs g) {
     if (T == kQ6_K) s_xs[j16] = (long long)s16 << er;
     if ((j16 & 1) == 0) {
       s_e[j16 / 2] = T == kQ8_0 ? (zero ? -1 : (int)ch.e) : er;
-      if (T == kQ4_K) s_xs[j16 / 2] = (long long)s32 << er;
+      if (T == kQ4_K) s_xs[j16 / 2] = s32;
     }
   }
   __syncthreads();

@@ -222,12 +222,52 @@ __global__ void quant_kernel(const void *xin, size_t n, size_t ldx, int8_t *code
   desc_write(&acc, desc, n);
 }
 
-// f32 vectors, bandwidth-shaped: a warp takes 128 lanes (4 blocks) per step, each thread 4
-// consecutive lanes (one 16-byte load, one 4-byte store of codes); the block absmax reduces
-// over its 8 threads on the f32 bit patterns (|f| orders like round(|f|·2^32)).  Same
-// results and descriptor as quant_kernel<true>; vector c at x + c·ldx, ldx a multiple of 4.
-__global__ void quant_f32_vec_kernel(const float *x, size_t n, size_t ldx, int8_t *codes,
-                                     size_t ld, uint8_t *exps, size_t ldb, ActDesc *desc) {
+// Round-half-up right shift of a value below 2^25 (0 for shifts past its bit length).
+__device__ __forceinline__ unsigned rshift_round(unsigned x, unsigned s) {
+  return s == 0 ? x : s > 25 ? 0u : (x + (1u << (s - 1))) >> s;
+}
+
+// Largest |f| bit pattern the 32-bit route takes: 127·2^24.  Below it every lane converts,
+// act_scale gives e <= 56 and every code times 2^e fits i64, so nothing refuses.
+constexpr unsigned kFastAbsMax = 0x4EFE0000u;
+
+// act_scale exponent of a block whose largest |f| has bit pattern A <= kFastAbsMax, from the
+// f32 fields: with M the 24-bit significand and E the biased exponent, round(A·2^32) is
+// M·2^(E−118) for E >= 118 (bit length E − 94, so e = E − 101 or one more when M > 127·2^17),
+// and below that a value under 2^25 formed by one rounding shift.
+__device__ __forceinline__ int fast_scale_exp(unsigned A) {
+  const unsigned E = A >> 23, M = (A & 0x7FFFFFu) | (E ? 0x800000u : 0u);
+  if (E >= 118) return (int)E - 101 + (M > 0xFE0000u ? 1 : 0);
+  const unsigned vm = rshift_round(M, 118 - (E ? E : 1));
+  if (vm == 0) return -1;
+  const int bl = 32 - __clz((int)vm);
+  const int e0 = bl > 7 ? bl - 7 : 0;
+  return (127u << e0) >= vm ? e0 : e0 + 1;
+}
+
+// Code of one lane (f32 bits) under block exponent e >= 0: round(|f|·2^32) then round by 2^e,
+// ties away from zero both times.  Where round(|f|·2^32) is exact (E >= 118) the two
+// roundings are one shift of the significand.
+__device__ __forceinline__ int fast_code(unsigned bits, int e) {
+  const unsigned b = bits & 0x7FFFFFFFu, E = b >> 23, M = (b & 0x7FFFFFu) | (E ? 0x800000u : 0u);
+  const unsigned mag = E >= 118 ? rshift_round(M, (unsigned)e + 118 - E)
+                                : rshift_round(rshift_round(M, 118 - (E ? E : 1)), (unsigned)e);
+  return (bits >> 31) ? -(int)mag : (int)mag;
+}
+
+// f32 vectors, bandwidth-shaped: a warp takes 128 lanes (4 blocks) per chunk, each thread 4
+// consecutive lanes (one 16-byte load, one 4-byte store of codes), with kQuantChunks chunks'
+// loads in flight per thread.  The block absmax reduces over its 8 threads on the f32 bit
+// patterns (|f| orders like round(|f|·2^32)).  Blocks whose absmax is at most kFastAbsMax take
+// 32-bit arithmetic on the f32 fields; a warp holding any other block takes the Q32.32 route
+// of quant_kernel for all its lanes.  Same codes, exponents and descriptor as
+// quant_kernel<true>; vector c at x + c·ldx, ldx a multiple of 4.
+constexpr int kQuantChunks = 4;
+
+__global__ void __launch_bounds__(256) quant_f32_vec_kernel(const float *x, size_t n, size_t ldx,
+                                                           int8_t *codes, size_t ld,
+                                                           uint8_t *exps, size_t ldb,
+                                                           ActDesc *desc) {
   __shared__ DescAcc acc;
   const size_t c = blockIdx.x;
   x += c * ldx;
@@ -238,75 +278,94 @@ __global__ void quant_f32_vec_kernel(const float *x, size_t n, size_t ldx, int8_
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = blockDim.x / 32;
   int w_emin = 1 << 30, w_emax = -1, w_status = APX_OK;
   unsigned w_nz = 0;
-  for (size_t base = (size_t)warp * 128; base < n; base += (size_t)nw * 128) {
-    const size_t j = base + 4 * lane;  // first of this thread's 4 lanes
-    float f[4] = {0.f, 0.f, 0.f, 0.f};
-    if (j + 4 <= n) {
-      const float4 v4 = *reinterpret_cast<const float4 *>(x + j);
-      f[0] = v4.x; f[1] = v4.y; f[2] = v4.z; f[3] = v4.w;
-    } else {
-      for (int u = 0; u < 4; u++)
-        if (j + u < n) f[u] = x[j + u];
-    }
-    long long v[4];
-    bool ok = true;
-    unsigned amax = 0;
+  const size_t chunks = (n + 127) / 128;
+  for (size_t round = 0; round * nw * kQuantChunks < chunks; round++) {
+    float4 f4[kQuantChunks];
 #pragma unroll
-    for (int u = 0; u < 4; u++) {
-      ok &= f32_to_q32(f[u], v[u]);
-      amax = max(amax, __float_as_uint(f[u]) & 0x7FFFFFFFu);
-    }
-    // block-level decisions: the 8 threads agree (shuffles within the 8-lane group)
-#pragma unroll
-    for (int o = 4; o > 0; o >>= 1) {
-      amax = max(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
-      ok &= __shfl_xor_sync(0xFFFFFFFFu, (int)ok, o) != 0;
-    }
-    int e = -1;
-    uint32_t packed = 0;
-    bool blk_ok = ok;
-    if (blk_ok) {
-      long long vm;
-      const unsigned long long mx =
-          f32_to_q32(__uint_as_float(amax), vm) ? (unsigned long long)vm : 1ull << 63;
-      e = act_scale_exp(mx);
-      if (e == 99) blk_ok = false;
-    }
-    bool bad = false;
-    if (blk_ok && e >= 0) {
-#pragma unroll
-      for (int u = 0; u < 4; u++) {
-        const unsigned long long m = uabs64(v[u]);
-        const unsigned long long S = 1ull << e, q = m >> e, r = m & (S - 1);
-        const unsigned long long mag = q + (2 * r >= S ? 1ull : 0ull);
-        const int code = v[u] < 0 ? -(int)mag : (int)mag;
-        bad |= mag > 127 || !product_fits(code, e);
-        packed |= ((uint32_t)(uint8_t)(int8_t)code) << (8 * u);
+    for (int u = 0; u < kQuantChunks; u++) {
+      const size_t j = ((round * kQuantChunks + u) * nw + warp) * 128 + 4 * lane;
+      f4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (j + 4 <= n) {
+        f4[u] = __ldg(reinterpret_cast<const float4 *>(x + j));
+      } else if (j < n) {
+        f4[u].x = x[j];
+        if (j + 1 < n) f4[u].y = x[j + 1];
+        if (j + 2 < n) f4[u].z = x[j + 2];
       }
     }
-    // every lane takes part in the group reductions (the branch above is group-dependent)
 #pragma unroll
-    for (int o = 4; o > 0; o >>= 1) bad |= __shfl_xor_sync(0xFFFFFFFFu, (int)bad, o) != 0;
-    if (bad) blk_ok = false;
-    const bool leader = (lane & 7) == 0 && j < n;
-    if (!blk_ok) {
-      if (leader) w_status = max(w_status, (int)APX_ERR_QUANT_REFUSED);
-      continue;
-    }
-    if (j < n) {
+    for (int u = 0; u < kQuantChunks; u++) {
+      const size_t cbase = ((round * kQuantChunks + u) * nw + warp) * 128;
+      if (cbase >= n) break;  // warp-uniform
+      const size_t j = cbase + 4 * lane;
+      const unsigned bits[4] = {__float_as_uint(f4[u].x), __float_as_uint(f4[u].y),
+                                __float_as_uint(f4[u].z), __float_as_uint(f4[u].w)};
+      unsigned amax = 0;
+#pragma unroll
+      for (int k = 0; k < 4; k++) amax = max(amax, bits[k] & 0x7FFFFFFFu);
+#pragma unroll
+      for (int o = 4; o > 0; o >>= 1) amax = max(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+      int e = -1;
+      uint32_t packed = 0;
+      bool blk_ok = true;
+      if (__all_sync(0xFFFFFFFFu, amax <= kFastAbsMax)) {
+        e = fast_scale_exp(amax);
+        if (e >= 0) {
+#pragma unroll
+          for (int k = 0; k < 4; k++)
+            packed |= ((uint32_t)(uint8_t)(int8_t)fast_code(bits[k], e)) << (8 * k);
+        }
+      } else {
+        // Q32.32 route (f32_to_q32, act_scale, checked product) for every lane of the warp
+        long long v[4];
+        bool ok = true;
+#pragma unroll
+        for (int k = 0; k < 4; k++) ok &= f32_to_q32(__uint_as_float(bits[k]), v[k]);
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) ok &= __shfl_xor_sync(0xFFFFFFFFu, (int)ok, o) != 0;
+        blk_ok = ok;
+        if (blk_ok) {
+          long long vm;
+          const unsigned long long mx =
+              f32_to_q32(__uint_as_float(amax), vm) ? (unsigned long long)vm : 1ull << 63;
+          e = act_scale_exp(mx);
+          if (e == 99) blk_ok = false;
+        }
+        bool bad = false;
+        if (blk_ok && e >= 0) {
+#pragma unroll
+          for (int k = 0; k < 4; k++) {
+            const unsigned long long m = uabs64(v[k]);
+            const unsigned long long S = 1ull << e, q = m >> e, r = m & (S - 1);
+            const unsigned long long mag = q + (2 * r >= S ? 1ull : 0ull);
+            const int code = v[k] < 0 ? -(int)mag : (int)mag;
+            bad |= mag > 127 || !product_fits(code, e);
+            packed |= ((uint32_t)(uint8_t)(int8_t)code) << (8 * k);
+          }
+        }
+        // every lane takes part in the group reduction (the branch above is group-dependent)
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) bad |= __shfl_xor_sync(0xFFFFFFFFu, (int)bad, o) != 0;
+        if (bad) blk_ok = false;
+      }
+      const bool leader = (lane & 7) == 0 && j < n;
+      if (!blk_ok) {
+        if (leader) w_status = max(w_status, (int)APX_ERR_QUANT_REFUSED);
+        continue;
+      }
       if (j + 4 <= n) {
         *reinterpret_cast<uint32_t *>(codes + j) = packed;
       } else {
-        for (int u = 0; u < 4; u++)
-          if (j + u < n) codes[j + u] = (int8_t)(packed >> (8 * u));
+        for (int k = 0; k < 4; k++)
+          if (j + k < n) codes[j + k] = (int8_t)(packed >> (8 * k));
       }
-    }
-    if (leader) {
-      exps[j / 32] = e < 0 ? (uint8_t)APX_EXP_ZERO : (uint8_t)e;
-      if (e >= 0) {
-        w_emin = min(w_emin, e);
-        w_emax = max(w_emax, e);
-        w_nz++;
+      if (leader) {
+        exps[j / 32] = e < 0 ? (uint8_t)APX_EXP_ZERO : (uint8_t)e;
+        if (e >= 0) {
+          w_emin = min(w_emin, e);
+          w_emax = max(w_emax, e);
+          w_nz++;
+        }
       }
     }
   }
