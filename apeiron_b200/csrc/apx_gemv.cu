@@ -402,12 +402,18 @@ __global__ void __launch_bounds__(384, 2) gemv_kernel(GemvArgs g) {
   using F = Fam<T>;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int ks = (int)(blockIdx.x % g.ksplit);
-  const size_t rt0 = (size_t)(blockIdx.x / g.ksplit) * g.R;
+  // this CTA's row tiles [rt0, rt1): an even share of the n_rt over the grid's rows of CTAs,
+  // at most R
+  // (one-wave plans keep n_rt·grid below 2^32)
+  const unsigned cta_row = blockIdx.x / g.ksplit, grid_rows = gridDim.x / g.ksplit;
+  const size_t rt0 = cta_row * (unsigned)g.n_rt / grid_rows;
+  const size_t rt1 = (cta_row + 1) * (unsigned)g.n_rt / grid_rows;
+  const int nr = (int)(rt1 - rt0);
   const int k0 = (int)((long long)g.units * ks / g.ksplit);
   const int k1 = (int)((long long)g.units * (ks + 1) / g.ksplit);
   const int r = warp / g.P, p = warp % g.P;
   const size_t rt = rt0 + r;
-  const bool active = r < g.R && rt < g.n_rt;
+  const bool active = r < nr;
   const uint8_t *base = g.pack + rt * (size_t)g.units * F::unit_bytes;
   const int L = g.L, H = 32 / L, slot = lane % L;
   const int nch = L * F::span / 16;  // chunks staged per unit: 8, 16, 32 or 64
@@ -465,7 +471,7 @@ __global__ void __launch_bounds__(384, 2) gemv_kernel(GemvArgs g) {
   __syncthreads();
   Acc128 s;
   acc_zero(s);
-  if (p == 0 && r < g.R) {
+  if (p == 0 && r < nr) {
     s = part[(r * g.P) * 32 + lane];
     for (int q = 1; q < g.P; q++) acc_add(s, part[(r * g.P + q) * 32 + lane]);
   }
@@ -481,7 +487,7 @@ __global__ void __launch_bounds__(384, 2) gemv_kernel(GemvArgs g) {
     }
     __syncthreads();
     if (threadIdx.x < (unsigned)g.R)
-      ticket[threadIdx.x] = rt0 + threadIdx.x < g.n_rt
+      ticket[threadIdx.x] = (int)threadIdx.x < nr
                                 ? atomicAdd(g.counters + rt0 + threadIdx.x, 1u)
                                 : 0u;
     __syncthreads();
@@ -747,14 +753,20 @@ GemvPlan plan_gemv(uint32_t type, size_t n_out, size_t n_in, int sm_count) {
   if (w <= 12) {
     pl.ksplit = 1;
     pl.P = w;
-    pl.R = std::max(1, std::min(12 / pl.P, (int)std::max<size_t>(1, n_rt / sm_count)));
+    // More row tiles than SMs: one CTA per SM with an even share of them (1 or 2 here), when
+    // the share fits 12 warps.  A CTA then fills half an SM's registers, so exactly one CTA of
+    // this projection and one of the next (programmatic dependent launch) sit on every SM,
+    // and the block scheduler cannot stack several CTAs of one launch on one SM.
+    const size_t share = (n_rt + sm_count - 1) / sm_count;
+    pl.R = n_rt > (size_t)sm_count && share * pl.P <= 12 ? (int)share : 1;
   } else {
     pl.ksplit = (w + 11) / 12;
     pl.P = (w + pl.ksplit - 1) / pl.ksplit;
     pl.R = 1;
   }
   if ((size_t)pl.R > n_rt) pl.R = (int)(n_rt ? n_rt : 1);
-  pl.grid = (unsigned)(((n_rt + pl.R - 1) / pl.R) * pl.ksplit);
+  const size_t rows = pl.R > 1 ? (size_t)sm_count : (n_rt + pl.R - 1) / pl.R;
+  pl.grid = (unsigned)(rows * pl.ksplit);
   pl.block = 32 * pl.R * pl.P;
   const size_t stage = (size_t)pl.R * pl.P * warp_act_bytes(type);
   const size_t red = (size_t)pl.R * pl.P * 32 * sizeof(Acc128) + 64;
