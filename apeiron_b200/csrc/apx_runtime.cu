@@ -133,6 +133,8 @@ HostAct describe_host(const int8_t *codes, size_t q_len, const uint8_t *exps) {
   int emin = 1 << 30, emax = -1;
   unsigned nz = 0, m128 = 0;
   const size_t nb = (q_len + 31) / 32;
+  // a code of -128 anywhere (one vectorised byte search): then look at the blocks it is in
+  const bool any128 = q_len && std::memchr(codes, 0x80, q_len) != nullptr;
   for (size_t b = 0; b < nb; b++) {
     unsigned e = exps[b];
     if (e == APX_EXP_ZERO) continue;
@@ -140,14 +142,16 @@ HostAct describe_host(const int8_t *codes, size_t q_len, const uint8_t *exps) {
       h.status = APX_ERR_INVALID_ARGUMENT;
       continue;
     }
-    size_t end = std::min(q_len, b * 32 + 32);
-    for (size_t j = b * 32; j < end; j++) {
-      int c = codes[j];
-      if (c == -128) m128 = 1;
-      if (e >= 57) {
-        long long lim = 1ll << (63 - e);
-        if (c < -lim || c > lim - 1) {
-          if (h.status == APX_OK) h.status = APX_ERR_FIXED_OVERFLOW;
+    if (e >= 57 || any128) {  // codes whose product with 2^e may leave i64, or a -128
+      size_t end = std::min(q_len, b * 32 + 32);
+      for (size_t j = b * 32; j < end; j++) {
+        int c = codes[j];
+        if (c == -128) m128 = 1;
+        if (e >= 57) {
+          long long lim = 1ll << (63 - e);
+          if (c < -lim || c > lim - 1) {
+            if (h.status == APX_OK) h.status = APX_ERR_FIXED_OVERFLOW;
+          }
         }
       }
     }
@@ -260,9 +264,10 @@ void scan_nonfinite(Tensor &t, const uint8_t *raw) {
 }
 
 // Synchronous single-column projection of host activations.
+// ha: the caller's describe_host of (codes, exps).
 int matvec_sync(apx_ctx *ctx, Tensor &t, size_t n_out, size_t n_in, const int8_t *codes,
-                size_t q_len, const uint8_t *exps, int64_t *out, apx_err *err) {
-  HostAct ha = describe_host(codes, q_len, exps);
+                size_t q_len, const uint8_t *exps, const HostAct &ha, int64_t *out,
+                apx_err *err) {
   const size_t nb = (q_len + 31) / 32;
   const size_t out_sz = align16(n_out * 8);
   const size_t head = 16 + 32;  // status + desc
@@ -540,7 +545,7 @@ int apx_matvec_q8act(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
   if (ha.status != APX_OK) return set_err(err, ha.status);
   int rc = check_geometry(*t, n_out, n_in, q_len, false, err);
   if (rc != APX_OK) return rc;
-  return matvec_sync(ctx, *t, n_out, n_in, codes, q_len, exps, out, err);
+  return matvec_sync(ctx, *t, n_out, n_in, codes, q_len, exps, ha, out, err);
 }
 
 int apx_matvec_q8act_chunked(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
@@ -560,7 +565,7 @@ int apx_matvec_q8act_chunked(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t
   if (rc != APX_OK) return rc;
   HostAct ha = describe_host(codes, q_len, exps);
   if (ha.status != APX_OK) return set_err(err, ha.status);
-  return matvec_sync(ctx, *t, n_out, n_in, codes, q_len, exps, out, err);
+  return matvec_sync(ctx, *t, n_out, n_in, codes, q_len, exps, ha, out, err);
 }
 
 int apx_matmat_q8act(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in, size_t k_cols,
@@ -582,7 +587,7 @@ int apx_matmat_q8act(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in, s
     if (rc == APX_OK) rc = check_geometry(*t, n_out, n_in, q_len, false, err);
     else set_err(err, rc);
     if (rc == APX_OK)
-      rc = matvec_sync(ctx, *t, n_out, n_in, codes + c * q_len, q_len, exps + c * nb,
+      rc = matvec_sync(ctx, *t, n_out, n_in, codes + c * q_len, q_len, exps + c * nb, ha,
                        out + c * n_out, err);
     if (rc != APX_OK) {
       if (err) err->col = c;

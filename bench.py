@@ -387,7 +387,7 @@ def run_ours(args, world, rank, local, pg):
     import torch
 
     from apeiron_b200 import _abi, synth
-    from apeiron_b200.chart import Backend, QuantAct
+    from apeiron_b200.chart import Backend
 
     dev = torch.device(f"cuda:{local}")
     torch.cuda.set_device(dev)
@@ -501,17 +501,33 @@ def run_ours(args, world, rank, local, pg):
     value = world * per_step * args.steps / (ms_max / 1e3) / 1e9
     assert int(status[0].item()) == -1
 
-    # e2e through the synchronous C ABI with host buffers
-    qs = [QuantAct.from_exps(a[5], a[4]) for a in acts]
-    for i in range(args.warmup):
+    # e2e through the synchronous C ABI (apx_matvec_q8act, the drop-in for matvec_q8act) with
+    # host buffers: every call copies its activation in and its Q32.32 outputs back, then
+    # returns; called through ctypes directly, as the engine's FFI binding would
+    host = [(np.ascontiguousarray(a[4], dtype=np.int8), np.ascontiguousarray(a[5], dtype=np.uint8),
+             np.empty(max(m[1], 1), dtype=np.int64)) for a, m in zip(acts, mats)]
+    herr = _abi.ApxErr()
+    hptr = C.byref(herr)
+    fn = lib.apx_matvec_q8act
+
+    def e2e_step(i):
         for m, (t, n_out, n_in) in enumerate(mats):
-            be.matvec_q8act(t, tensors[i % copies][m], n_out, n_in, qs[m])
+            hc, he, ho = host[m]
+            if fn(be.ctx, tensors[i % copies][m].handle, n_out, n_in, hc.ctypes.data, hc.size,
+                  he.ctypes.data, ho.ctypes.data, hptr):
+                raise RuntimeError(f"apx_matvec_q8act failed: code {herr.code}")
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    for m, (t, n_out, n_in) in enumerate(mats):  # the host outputs are the exact ones
+        raw = synth.payload(t, n_out, n_in, 1000 + m)
+        want = O.matvec_q8act(t, raw, n_out, n_in, acts[m][4], O.exps_to_scales(acts[m][5]))
+        assert np.array_equal(host[m][2][:n_out], want), "parity failure on the e2e path"
     barrier(pg, local)
     e_steps = min(args.steps, 2000)
     e0 = time.perf_counter()
     for i in range(e_steps):
-        for m, (t, n_out, n_in) in enumerate(mats):
-            be.matvec_q8act(t, tensors[(args.warmup + i) % copies][m], n_out, n_in, qs[m])
+        e2e_step(args.warmup + i)
     e_s = time.perf_counter() - e0
     e_s = max_over_ranks(e_s, pg, local)
     e2e = world * per_step * e_steps / e_s / 1e9
