@@ -206,6 +206,125 @@ def measure_prefill(be, lib, dev, stream, steps, warmup, pg, local, world):
     }
 
 
+SHARDED = [(12, 28672, 8192), (12, 28672, 8192), (12, 8192, 28672)]  # gate, up, down
+
+
+def measure_sharded(be, lib, dev, stream, steps, warmup, pg, rank, local, world):
+    """the Llama-3-70B-shaped Q4_K FFN decode projections, row-sharded over the
+    ranks (apeiron_b200/shard.py): each rank projects its rows of gate, up and down, and an
+    NCCL all-gather of the output slices (plus the refusal-word reduction) follows each
+    projection.  Strong scaling: the same three matrices at every N."""
+    import torch
+
+    from apeiron_b200 import shard, synth
+    from oracle import oracle as O
+
+    sp = stream.cuda_stream
+    dist = pg if world > 1 else None
+    raws = [synth.payload(t, n_out, n_in, 4000 + m) for m, (t, n_out, n_in) in enumerate(SHARDED)]
+    per_rank = sum(r.size for r in raws) / world
+    copies = max(1, int(np.ceil(3 * L2_BYTES / per_rank)))
+    shards = [[shard.RowShard(be, t, raws[m], n_out, n_in, rank, world, dist, f"cuda:{local}")
+               for m, (t, n_out, n_in) in enumerate(SHARDED)] for _ in range(copies)]
+    acts, bufs = [], []
+    for m, (t, n_out, n_in) in enumerate(SHARDED):
+        x = synth.activation_f32(n_in, 5000 + m)
+        c, e = synth.quant_act_np(synth.f32_to_q32(x))
+        pad = lib.apx_act_padded_len(n_in)
+        codes = torch.zeros(pad, dtype=torch.int8, device=dev)
+        codes[:n_in] = torch.from_numpy(c).to(dev)
+        exps = torch.full((pad // 32,), 0xFF, dtype=torch.uint8, device=dev)
+        exps[:e.size] = torch.from_numpy(e).to(dev)
+        desc = torch.zeros(8, dtype=torch.int32, device=dev)
+        with torch.cuda.stream(stream):
+            assert lib.apx_act_describe_async(be.ctx, codes.data_ptr(), exps.data_ptr(), n_in,
+                                              desc.data_ptr(), sp) == 0
+        rs = shards[0][m]
+        acts.append((codes, exps, desc, c, e))
+        bufs.append(dict(local=torch.zeros(max(rs.max_rows, 1), dtype=torch.int64, device=dev),
+                         full=torch.zeros(max(world * rs.max_rows, 1), dtype=torch.int64,
+                                          device=dev),
+                         status=torch.full((2,), -1, dtype=torch.int64, device=dev)))
+
+    def step(i):
+        for m in range(len(SHARDED)):
+            codes, exps, desc, _, _ = acts[m]
+            b = bufs[m]
+            shards[i % copies][m].matvec_async(lib, be.ctx, codes, exps, desc, b["local"],
+                                               b["full"], b["status"], sp)
+
+    # exactness before timing: the gathered Q32.32 vectors against the whole-tensor oracle
+    with torch.cuda.stream(stream):
+        step(0)
+    stream.synchronize()
+    if rank == 0:
+        for m, (t, n_out, n_in) in enumerate(SHARDED):
+            _, _, _, c, e = acts[m]
+            want = O.matvec_q8act_mt(t, raws[m], n_out, n_in, c, O.exps_to_scales(e),
+                                     os.cpu_count() or 1)
+            got = shards[0][m].assemble(bufs[m]["full"].cpu().numpy())
+            assert np.array_equal(got, want), "sharded parity failure in bench workload"
+            assert int(bufs[m]["status"][0].item()) == -1
+    del raws
+    barrier(pg, local)
+
+    with torch.cuda.stream(stream):
+        for i in range(max(warmup, 3)):
+            step(i)
+    stream.synchronize()
+    G = min(steps, 100)
+    graph = None
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(G):
+                step(i)
+    except Exception:  # collectives this build cannot capture: time the eager launches
+        graph = None
+        torch.cuda.synchronize()
+    barrier(pg, local)
+    reps = max(1, steps // G)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        if graph is not None:
+            graph.replay()
+        t0.record(stream)
+        for r in range(reps):
+            if graph is not None:
+                graph.replay()
+            else:
+                for i in range(G):
+                    step(i)
+        t1.record(stream)
+    stream.synchronize()
+    barrier(pg, local)
+    ms = max_over_ranks(t0.elapsed_time(t1), pg, local) / (reps * G)
+    for m in range(len(SHARDED)):
+        assert int(bufs[m]["status"][0].item()) == -1
+    timing = "CUDA graph" if graph is not None else "eager launches"
+    del graph  # release the captured collectives before the process group goes
+    torch.cuda.synchronize()
+    per_step = sum(gemv_bytes(*mat) for mat in SHARDED)
+    gbs = per_step / (ms / 1e3) / 1e9
+    hbm, _ = peaks()
+    return {
+        "metric": "70B FFN decode GB/s (row-sharded, NCCL all-gather)", "value": gbs,
+        "unit": "GB/s", "n_gpus": world, "ms_per_step": ms, "steps": reps * G,
+        "scaling": "strong",
+        "config": {"workload": "Llama-3-70B-shaped Q4_K FFN decode: W_gate/W_up 28672x8192, "
+                               "W_down 8192x28672, configs[4]; step = the three projections, "
+                               "each rank its rows, one all-gather of int64 output slices and "
+                               "one refusal-word all-reduce per projection",
+                   "rows_per_rank": [b - a for a, b in shards[0][0].splits],
+                   "weight_copies": copies,
+                   "l2": "rotating weight copies, >= 3x the 126 MB L2 per rank",
+                   "timing": timing,
+                   "exact": "gathered Q32.32 outputs bit-equal to the whole-tensor CPU oracle "
+                            "(checked before timing)"},
+        "hbm_frac_per_gpu": gbs / world / hbm,
+    }
+
+
 def gemv_bytes(t, n_out, n_in):
     from apeiron_b200 import synth
     qk, bb = synth.GEOM[t]
@@ -539,6 +658,10 @@ def run_ours(args, world, rank, local, pg):
     if not args.no_prefill:
         prefill = measure_prefill(be, lib, dev, stream, args.prefill_steps, args.warmup, pg,
                                   local, world)
+    sharded = None
+    if not args.no_shard:
+        sharded = measure_sharded(be, lib, dev, stream, args.shard_steps, args.warmup, pg, rank,
+                                  local, world)
     if rank != 0:
         return
     hbm, src = peaks()
@@ -574,6 +697,9 @@ def run_ours(args, world, rank, local, pg):
     if prefill is not None:
         line["prefill"] = prefill
         line["gpu_launches"] += prefill["gpu_launches_per_step"] * prefill["steps"]
+    if sharded is not None:
+        line["sharded"] = sharded
+        line["gpu_launches"] += len(SHARDED) * sharded["steps"]
     print(json.dumps(line), flush=True)
 
 
@@ -587,6 +713,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-shard", action="store_true")
+    ap.add_argument("--shard-steps", type=int, default=400)
     ap.add_argument("--prefill-steps", type=int, default=400)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

@@ -203,6 +203,18 @@ def matvec_q8act(t, raw, n_out, n_in, codes, scales):
     return _result(rc, err, out[:n_out])
 
 
+def matvec_q8act_row(t, raw, n_out, n_in, codes, scales):
+    """``matvec_q8act`` with the refusing row: (outputs, None) or (None, ApxErr)."""
+    raw = _u8(raw)
+    codes = np.ascontiguousarray(codes, dtype=np.int8)
+    scales = np.ascontiguousarray(scales, dtype=np.int64)
+    out = np.zeros(max(n_out, 1), dtype=np.int64)
+    err = ApxErr()
+    rc = lib().apxo_matvec_q8act(t, _p(raw), raw.size, n_out, n_in, _p(codes), codes.size,
+                                 _p(scales), scales.size, _p(out), C.byref(err))
+    return (None, err) if rc else (out[:n_out], None)
+
+
 def matvec_q8act_chunked(t, raw, n_out, n_in, codes, scales, chunks):
     raw = _u8(raw)
     codes = np.ascontiguousarray(codes, dtype=np.int8)
