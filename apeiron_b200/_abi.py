@@ -40,7 +40,13 @@ EXPORTS = [
     "apx_act_describe_async", "apx_quant_q32_async", "apx_quant_f32_async",
     "apx_matvec_async", "apx_matmat_async", "apx_act_padded_len", "apx_status_decode",
     "apx_matvec_f32_noalloc", "apx_matmat_f32", "apx_quant_f32_cols_async",
+    "apx_peer_alloc", "apx_peer_open", "apx_peer_close", "apx_device_read",
+    "apx_gather_publish_async",
 ]
+
+MAX_PEERS = 8
+MAX_GATHER_PROJ = 4
+PEER_HANDLE_BYTES = 64
 
 NOALLOC_MAX_N_IN = 65536
 
@@ -55,6 +61,28 @@ class ApxErr(C.Structure):
         ("col", C.c_uint64),
         ("bits", C.c_uint32),
         ("cuda_error", C.c_int32),
+    ]
+
+
+class GatherDesc(C.Structure):
+    """Mirror of ``apx_gather_desc`` (include/apeiron_cuda.h)."""
+
+    _fields_ = [
+        ("world", C.c_int),
+        ("rank", C.c_int),
+        ("nproj", C.c_int),
+        ("timeout_us", C.c_uint),
+        ("peer", C.c_void_p * MAX_PEERS),
+        ("out_off", C.c_size_t),
+        ("key_off", C.c_size_t),
+        ("flag_off", C.c_size_t),
+        ("ctr_off", C.c_size_t),
+        ("rows_off", C.c_size_t * MAX_GATHER_PROJ),
+        ("rows", C.c_size_t * MAX_GATHER_PROJ),
+        ("row0", C.c_longlong * MAX_GATHER_PROJ),
+        ("nf_key", C.c_longlong * MAX_GATHER_PROJ),
+        ("status", C.c_void_p * MAX_GATHER_PROJ),
+        ("out_status", C.c_void_p * MAX_GATHER_PROJ),
     ]
 
 
@@ -84,6 +112,11 @@ _SIGS = {
     "apx_quant_q32_async": (C.c_int, [P, P, SZ, P, P, P, P]),
     "apx_quant_f32_async": (C.c_int, [P, P, SZ, P, P, P, P]),
     "apx_matvec_async": (C.c_int, [P, U64, SZ, SZ, P, P, P, P, P, P, P]),
+    "apx_peer_alloc": (C.c_int, [P, SZ, C.POINTER(C.c_void_p), P, EP]),
+    "apx_peer_open": (C.c_int, [P, P, C.POINTER(C.c_void_p), EP]),
+    "apx_peer_close": (C.c_int, [P, P, C.c_int]),
+    "apx_device_read": (C.c_int, [P, P, P, SZ, EP]),
+    "apx_gather_publish_async": (C.c_int, [P, C.POINTER(GatherDesc), P]),
     "apx_matmat_async": (C.c_int, [P, U64, SZ, SZ, SZ, P, P, P, P, P, P, P]),
     "apx_act_padded_len": (SZ, [SZ]),
     "apx_status_decode": (C.c_int, [P, U64, C.POINTER(CallStatus), EP]),

@@ -390,6 +390,8 @@ bool tensor_launch_info(apx_ctx *ctx, uint64_t handle, uint32_t *type, const uin
   *device = ctx->device;
   return true;
 }
+
+int context_device(const apx_ctx *ctx) { return ctx->device; }
 }  // namespace apx
 
 extern "C" {

@@ -202,6 +202,16 @@ class RowShard:
             gathered[: self.rows].copy_(local_out[: self.rows])
         self.reduce_status(status)
 
+    def _key(self, w):
+        """This rank's refusal word (int64 tensor of one) as an order key: rebased to the whole
+        tensor's rows, the shard's non-finite scale folded in, "no refusal" the largest."""
+        import torch
+
+        keyed = torch.where(w == _NONE, torch.full_like(w, _I64_MAX), w + (self.r0 << _ROW_SHIFT))
+        if self.nf_word is not None:
+            keyed = torch.minimum(keyed, torch.full_like(w, self.nf_word))
+        return keyed
+
     def reduce_status(self, status) -> None:
         """In place: this rank's refusal word (int64 tensor, first entry; rows of this shard)
         becomes the first refusal over every rank in rows of the whole tensor.  The row is
@@ -210,9 +220,7 @@ class RowShard:
         import torch
 
         w = status[:1]
-        keyed = torch.where(w == _NONE, torch.full_like(w, _I64_MAX), w + (self.r0 << _ROW_SHIFT))
-        if self.nf_word is not None:
-            keyed = torch.minimum(keyed, torch.full_like(w, self.nf_word))
+        keyed = self._key(w)
         if self.world > 1 and self.dist is not None:
             self.dist.all_reduce(keyed, op=self.dist.ReduceOp.MIN, group=self.group)
         status[:1] = torch.where(keyed == _I64_MAX, torch.full_like(w, _NONE), keyed)
@@ -236,6 +244,192 @@ class RowShard:
         if kind == _abi.APX_ERR_QUANT_REFUSED:
             raise chart.QuantRefused()
         raise chart.BackendError(f"refusal word {word:#x}")
+
+
+def group_layout(shards: Sequence[RowShard]) -> Tuple[List[int], int, int]:
+    """Offsets of each projection's padded row slice in one rank's group buffer, the offset of
+    the refusal keys (one int64 per projection, after the slices) and the buffer length."""
+    offs, o = [], 0
+    for sh in shards:
+        offs.append(o)
+        o += sh.max_rows
+    return offs, o, o + len(shards)
+
+
+def matvec_group_async(shards: Sequence[RowShard], lib, ctx, acts, local, gathered, statuses,
+                       stream) -> None:
+    """Several row-sharded projections with ONE all-gather: each projection's rows into its
+    slice of `local` (int64, group_layout length), each refusal word (rebased, non-finite
+    folded) as a key after the slices, one all-gather of `local` into `gathered` (world ×
+    length, rank-major), and each `statuses[j]` (int64[2], all ones on entry) set to the first
+    refusal over the ranks.  `acts[j]` = (codes, exps, desc) device tensors of projection j;
+    all tensors on this rank's GPU, queued on the current torch stream (`stream`)."""
+    import torch
+
+    offs, k0, length = group_layout(shards)
+    for j, sh in enumerate(shards):
+        codes, exps, desc = acts[j]
+        if sh.rows:
+            rc = lib.apx_matvec_async(ctx, sh.tensor.handle, sh.rows, sh.n_in, codes.data_ptr(),
+                                      exps.data_ptr(), desc.data_ptr(),
+                                      local[offs[j]:].data_ptr(), None,
+                                      statuses[j].data_ptr(), stream)
+            if rc:
+                raise chart.BackendError(f"apx_matvec_async failed with code {rc}")
+    keys = torch.stack([sh._key(statuses[j][:1])[0] for j, sh in enumerate(shards)])
+    local[k0:k0 + len(shards)] = keys
+    sh0 = shards[0]
+    if sh0.world > 1 and sh0.dist is not None:
+        sh0.dist.all_gather_into_tensor(gathered, local, group=sh0.group)
+        first = gathered.view(sh0.world, length)[:, k0:k0 + len(shards)].min(dim=0).values
+    else:
+        gathered[:length].copy_(local)
+        first = keys
+    for j in range(len(shards)):
+        statuses[j][:1] = torch.where(first[j:j + 1] == _I64_MAX,
+                                      torch.full_like(first[j:j + 1], _NONE), first[j:j + 1])
+
+
+def assemble_group(shards: Sequence[RowShard], gathered: np.ndarray, j: int) -> np.ndarray:
+    """Projection j's whole output from a group all-gather buffer."""
+    offs, _, length = group_layout(shards)
+    sh = shards[j]
+    parts = [gathered[r * length + offs[j]: r * length + offs[j] + (b - a)]
+             for r, (a, b) in enumerate(sh.splits)]
+    return np.concatenate(parts) if parts else np.zeros(0, dtype=np.int64)
+
+
+def _align(n: int, a: int = 256) -> int:
+    return -(-n // a) * a
+
+
+class PeerGather:
+    """Row-sharded projections whose outputs move between the ranks' GPUs by peer stores
+    (apx_gather_publish_async) instead of a collective library.
+
+    Every rank allocates one gather buffer (apx_peer_alloc) and maps every other rank's
+    (CUDA IPC handles exchanged once through `dist`).  Layout, the same on every rank:
+      parity p (0, 1) at p·stride: the whole output vectors of the group's projections
+      (projection j at element base[j], 32-element aligned), then the refusal keys
+      [world][nproj]; after both parities the flags [world] and this rank's epoch counters.
+    `run` queues, on `stream`: a reset of this rank's refusal words, each projection's rows
+    written straight into this rank's buffer, and the publication that copies them into every
+    other rank's buffer and waits for everyone's.  Parities alternate per call; the epoch
+    advances on the device, so `run` may be captured in a CUDA graph (an even number of
+    calls per graph keeps the parities in step on replay).
+    """
+
+    def __init__(self, lib, ctx, shards: Sequence[RowShard], timeout_us: int = 2_000_000):
+        import ctypes as C
+
+        sh0 = shards[0]
+        if len(shards) > _abi.MAX_GATHER_PROJ or sh0.world > _abi.MAX_PEERS:
+            raise ValueError("too many projections or ranks for one gather")
+        self.lib, self.ctx, self.shards = lib, ctx, list(shards)
+        self.world, self.rank, self.dist, self.group = sh0.world, sh0.rank, sh0.dist, sh0.group
+        self.nproj = len(shards)
+        self.base, o = [], 0
+        for sh in shards:
+            self.base.append(o)
+            o += _align(max(sh.n_out, 1), 32)
+        out_bytes = _align(8 * o)
+        key_bytes = _align(8 * self.world * self.nproj)
+        self.key_rel = out_bytes
+        self.stride = out_bytes + key_bytes
+        self.flag_off = 2 * self.stride
+        self.ctr_off = self.flag_off + _align(8 * self.world)
+        total = self.ctr_off + 256
+        ptr, handle = C.c_void_p(), (C.c_ubyte * _abi.PEER_HANDLE_BYTES)()
+        err = _abi.ApxErr()
+        if lib.apx_peer_alloc(ctx, total, C.byref(ptr), handle, C.byref(err)):
+            raise chart.BackendError(f"apx_peer_alloc failed (cuda {err.cuda_error})")
+        self.local = ptr.value
+        handles = [bytes(handle)] * self.world
+        if self.world > 1 and self.dist is not None:
+            self.dist.all_gather_object(handles, bytes(handle), group=self.group)
+        self.peers, self.opened = [], []
+        for r in range(self.world):
+            if r == self.rank:
+                self.peers.append(self.local)
+                continue
+            hp, err = C.c_void_p(), _abi.ApxErr()
+            hb = (C.c_ubyte * _abi.PEER_HANDLE_BYTES).from_buffer_copy(handles[r])
+            if lib.apx_peer_open(ctx, hb, C.byref(hp), C.byref(err)):
+                raise chart.BackendError(f"apx_peer_open of rank {r} failed "
+                                         f"(cuda {err.cuda_error})")
+            self.peers.append(hp.value)
+            self.opened.append(hp.value)
+        d = _abi.GatherDesc()
+        d.world, d.rank, d.nproj, d.timeout_us = self.world, self.rank, self.nproj, timeout_us
+        for r, pv in enumerate(self.peers):
+            d.peer[r] = pv
+        d.flag_off, d.ctr_off = self.flag_off, self.ctr_off
+        for j, sh in enumerate(shards):
+            d.rows_off[j] = self.base[j] + sh.r0
+            d.rows[j] = sh.rows
+            d.row0[j] = sh.r0
+            d.nf_key[j] = sh.nf_word if sh.nf_word is not None else _I64_MAX
+        self.desc = d
+        self.calls = 0
+
+    def out_ptr(self, j: int, parity: int) -> int:
+        """Where this rank's rows of projection j go in the given parity (device address)."""
+        return self.local + parity * self.stride + 8 * (self.base[j] + self.shards[j].r0)
+
+    def run(self, acts, statuses, out_statuses, stream, shards=None) -> int:
+        """One publication of the group.  `acts[j]` = (codes, exps, desc) device tensors of
+        projection j; `statuses` an int64 tensor (nproj, 2) for this rank's refusal words;
+        `out_statuses` an int64 tensor (nproj, 2) that receives the first refusal over all
+        ranks (whole-tensor rows).  `shards` may name other uploads of the same rows (copies
+        of the weights).  Everything is queued on the current torch stream, which must be
+        `stream`.  Returns the parity written."""
+        import ctypes as C
+
+        parity = (self.calls + 1) % 2
+        statuses.fill_(-1)
+        for j, sh in enumerate(shards or self.shards):
+            codes, exps, desc = acts[j]
+            if sh.rows:
+                rc = self.lib.apx_matvec_async(self.ctx, sh.tensor.handle, sh.rows, sh.n_in,
+                                               codes.data_ptr(), exps.data_ptr(), desc.data_ptr(),
+                                               self.out_ptr(j, parity), None,
+                                               statuses[j].data_ptr(), stream)
+                if rc:
+                    raise chart.BackendError(f"apx_matvec_async failed with code {rc}")
+        d = self.desc
+        d.out_off = parity * self.stride
+        d.key_off = parity * self.stride + self.key_rel
+        for j in range(self.nproj):
+            d.status[j] = statuses[j].data_ptr()
+            d.out_status[j] = out_statuses[j].data_ptr()
+        rc = self.lib.apx_gather_publish_async(self.ctx, C.byref(d), stream)
+        if rc:
+            raise chart.BackendError(f"apx_gather_publish_async failed with code {rc}")
+        self.calls += 1
+        return parity
+
+    def read(self, j: int, parity: int) -> np.ndarray:
+        """Projection j's whole output vector from this rank's buffer (synchronous)."""
+        import ctypes as C
+
+        n = self.shards[j].n_out
+        out = np.empty(max(n, 1), dtype=np.int64)
+        err = _abi.ApxErr()
+        if n and self.lib.apx_device_read(self.ctx, self.local + parity * self.stride +
+                                          8 * self.base[j], out.ctypes.data, 8 * n,
+                                          C.byref(err)):
+            raise chart.BackendError(f"apx_device_read failed (cuda {err.cuda_error})")
+        return out[:n]
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (after every rank has stopped writing:
+        the caller synchronises its stream and the ranks meet at a barrier first)."""
+        for pv in self.opened:
+            self.lib.apx_peer_close(self.ctx, pv, 1)
+        self.opened = []
+        if self.local:
+            self.lib.apx_peer_close(self.ctx, self.local, 0)
+            self.local = 0
 
 
 def shard_projections(backend, mats: Sequence[Tuple[int, object, int, int]], rank: int,

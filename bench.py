@@ -211,9 +211,10 @@ SHARDED = [(12, 28672, 8192), (12, 28672, 8192), (12, 8192, 28672)]  # gate, up,
 
 def measure_sharded(be, lib, dev, stream, steps, warmup, pg, rank, local, world):
     """the Llama-3-70B-shaped Q4_K FFN decode projections, row-sharded over the
-    ranks (apeiron_b200/shard.py): each rank projects its rows of gate, up and down, and an
-    NCCL all-gather of the output slices (plus the refusal-word reduction) follows each
-    projection.  Strong scaling: the same three matrices at every N."""
+    ranks (apeiron_b200/shard.py): each rank projects its rows of gate, up and down straight
+    into its gather buffer, and one publication kernel per group (gate+up, down) copies them
+    into every other rank's buffer over NVLink peer stores and waits for everyone's.  Strong
+    scaling: the same three matrices at every N."""
     import torch
 
     from apeiron_b200 import shard, synth
@@ -226,8 +227,13 @@ def measure_sharded(be, lib, dev, stream, steps, warmup, pg, rank, local, world)
     copies = max(1, int(np.ceil(3 * L2_BYTES / per_rank)))
     shards = [[shard.RowShard(be, t, raws[m], n_out, n_in, rank, world, dist, f"cuda:{local}")
                for m, (t, n_out, n_in) in enumerate(SHARDED)] for _ in range(copies)]
-    acts, bufs = [], []
+    # gate and up read the same activation and gather together; down gathers alone
+    groups = [[0, 1], [2]]
+    acts = []
     for m, (t, n_out, n_in) in enumerate(SHARDED):
+        if m == 1:  # up: gate's activation
+            acts.append(acts[0])
+            continue
         x = synth.activation_f32(n_in, 5000 + m)
         c, e = synth.quant_act_np(synth.f32_to_q32(x))
         pad = lib.apx_act_padded_len(n_in)
@@ -239,32 +245,32 @@ def measure_sharded(be, lib, dev, stream, steps, warmup, pg, rank, local, world)
         with torch.cuda.stream(stream):
             assert lib.apx_act_describe_async(be.ctx, codes.data_ptr(), exps.data_ptr(), n_in,
                                               desc.data_ptr(), sp) == 0
-        rs = shards[0][m]
         acts.append((codes, exps, desc, c, e))
-        bufs.append(dict(local=torch.zeros(max(rs.max_rows, 1), dtype=torch.int64, device=dev),
-                         full=torch.zeros(max(world * rs.max_rows, 1), dtype=torch.int64,
-                                          device=dev),
-                         status=torch.full((2,), -1, dtype=torch.int64, device=dev)))
+    gathers = [shard.PeerGather(lib, be.ctx, [shards[0][m] for m in g]) for g in groups]
+    statuses = [torch.full((len(g), 2), -1, dtype=torch.int64, device=dev) for g in groups]
+    merged = [torch.full((len(g), 2), -1, dtype=torch.int64, device=dev) for g in groups]
 
     def step(i):
-        for m in range(len(SHARDED)):
-            codes, exps, desc, _, _ = acts[m]
-            b = bufs[m]
-            shards[i % copies][m].matvec_async(lib, be.ctx, codes, exps, desc, b["local"],
-                                               b["full"], b["status"], sp)
+        parities = []
+        for gi, g in enumerate(groups):
+            parities.append(gathers[gi].run([acts[m][:3] for m in g], statuses[gi], merged[gi],
+                                            sp, shards=[shards[i % copies][m] for m in g]))
+        return parities
 
-    # exactness before timing: the gathered Q32.32 vectors against the whole-tensor oracle
+    # exactness before timing: every rank's gathered Q32.32 vectors against the whole-tensor
+    # oracle, and no refusal
     with torch.cuda.stream(stream):
-        step(0)
+        parities = step(0)
     stream.synchronize()
-    if rank == 0:
-        for m, (t, n_out, n_in) in enumerate(SHARDED):
+    for gi, g in enumerate(groups):
+        for j, m in enumerate(g):
+            t, n_out, n_in = SHARDED[m]
             _, _, _, c, e = acts[m]
             want = O.matvec_q8act_mt(t, raws[m], n_out, n_in, c, O.exps_to_scales(e),
-                                     os.cpu_count() or 1)
-            got = shards[0][m].assemble(bufs[m]["full"].cpu().numpy())
+                                     max(1, (os.cpu_count() or 1) // world))
+            got = gathers[gi].read(j, parities[gi])
             assert np.array_equal(got, want), "sharded parity failure in bench workload"
-            assert int(bufs[m]["status"][0].item()) == -1
+        assert bool((merged[gi][:, 0] == -1).all().item()), "sharded refusal in bench workload"
     del raws
     barrier(pg, local)
 
@@ -299,22 +305,26 @@ def measure_sharded(be, lib, dev, stream, steps, warmup, pg, rank, local, world)
     stream.synchronize()
     barrier(pg, local)
     ms = max_over_ranks(t0.elapsed_time(t1), pg, local) / (reps * G)
-    for m in range(len(SHARDED)):
-        assert int(bufs[m]["status"][0].item()) == -1
+    for gi in range(len(groups)):
+        assert bool((merged[gi][:, 0] == -1).all().item()), "sharded refusal while timed"
     timing = "CUDA graph" if graph is not None else "eager launches"
-    del graph  # release the captured collectives before the process group goes
+    del graph
     torch.cuda.synchronize()
+    barrier(pg, local)  # no rank writes into another's gather buffer any more
+    for gth in gathers:
+        gth.close()
     per_step = sum(gemv_bytes(*mat) for mat in SHARDED)
     gbs = per_step / (ms / 1e3) / 1e9
     hbm, _ = peaks()
     return {
-        "metric": "70B FFN decode GB/s (row-sharded, NCCL all-gather)", "value": gbs,
+        "metric": "70B FFN decode GB/s (row-sharded, NVLink peer-store gather)", "value": gbs,
         "unit": "GB/s", "n_gpus": world, "ms_per_step": ms, "steps": reps * G,
         "scaling": "strong",
         "config": {"workload": "Llama-3-70B-shaped Q4_K FFN decode: W_gate/W_up 28672x8192, "
                                "W_down 8192x28672, configs[4]; step = the three projections, "
-                               "each rank its rows, one all-gather of int64 output slices and "
-                               "one refusal-word all-reduce per projection",
+                               "each rank its rows; the int64 output slices and refusal keys "
+                               "of gate+up (shared activation), then of down, published to every "
+                               "rank by peer stores (one kernel per group, bounded flag wait)",
                    "rows_per_rank": [b - a for a, b in shards[0][0].splits],
                    "weight_copies": copies,
                    "l2": "rotating weight copies, >= 3x the 126 MB L2 per rank",

@@ -243,6 +243,65 @@ APX_API int apx_matvec_f32_noalloc(apx_ctx *ctx, uint64_t tensor, size_t n_out, 
                                    const float *d_x, float *d_y, apx_call_status *d_status,
                                    void *stream);
 
+/* ---- row-sharded projections across the GPUs of one node ------------------------------
+ *
+ * A projection's rows are independent, so P processes (one per GPU) can each hold a row range
+ * of W and project it; every rank then needs the whole output vector.  These calls move it
+ * over NVLink with plain peer stores, without a collective library: each rank owns one gather
+ * buffer that every other rank maps (CUDA IPC), the projections write their rows straight into
+ * the local buffer, and apx_gather_publish_async copies them into every peer's buffer, posts
+ * this rank's refusal keys and an epoch flag, and waits (bounded) for every rank's flag.  The
+ * output area and the keys are double-buffered by epoch parity, so a rank that runs ahead
+ * never overwrites what another is still reading.  The epoch (1, 2, ...) lives in each rank's
+ * own buffer and advances on the device, so the calls can be captured in a CUDA graph and
+ * replayed.  The caller (apeiron_b200/shard.py) owns the buffer layout and alternates the
+ * parity; every rank must make the same calls in the same order. */
+
+#define APX_MAX_PEERS 8
+#define APX_MAX_GATHER_PROJ 4
+#define APX_PEER_HANDLE_BYTES 64
+
+/* A zeroed device buffer of `bytes` on ctx's GPU that other processes can map; *d_ptr gets
+ * its address, `handle` the bytes to pass to apx_peer_open in those processes. */
+APX_API int apx_peer_alloc(apx_ctx *ctx, size_t bytes, void **d_ptr,
+                           unsigned char handle[APX_PEER_HANDLE_BYTES], apx_err *err);
+/* Map another process's apx_peer_alloc buffer on ctx's GPU (peer access over NVLink). */
+APX_API int apx_peer_open(apx_ctx *ctx, const unsigned char handle[APX_PEER_HANDLE_BYTES],
+                          void **d_ptr, apx_err *err);
+/* Release a buffer: one this process allocated (opened = 0) or mapped (opened = 1). */
+APX_API int apx_peer_close(apx_ctx *ctx, void *d_ptr, int opened);
+/* Synchronous copy of `bytes` from device memory on ctx's GPU to host memory. */
+APX_API int apx_device_read(apx_ctx *ctx, const void *d_src, void *host_dst, size_t bytes,
+                            apx_err *err);
+
+/* One publication: rank `rank` of `world` makes its rows of `nproj` projections visible in
+ * every rank's gather buffer and collects every rank's refusal.  Offsets are bytes from each
+ * buffer's base (the same layout on every rank); the refusal words are this rank's
+ * apx_call_status words of the projections (device; reset to all ones here). */
+typedef struct apx_gather_desc {
+  int world, rank, nproj;
+  unsigned timeout_us;                   /* bound on the wait for the other ranks' flags  */
+  void *peer[APX_MAX_PEERS];             /* every rank's gather buffer (own one included)  */
+  size_t out_off;                        /* this parity's output area (int64 elements)     */
+  size_t key_off;                        /* this parity's keys: [world][nproj] int64       */
+  size_t flag_off;                       /* the flags: [world] uint64, epoch of each rank  */
+  size_t ctr_off;                        /* this rank's epoch and check-in count (2 uint64,
+                                            read only in its own buffer; zero at alloc)    */
+  size_t rows_off[APX_MAX_GATHER_PROJ];  /* first element of this rank's rows of proj. j   */
+  size_t rows[APX_MAX_GATHER_PROJ];      /* this rank's rows of projection j               */
+  long long row0[APX_MAX_GATHER_PROJ];   /* whole-tensor row of this rank's first row      */
+  long long nf_key[APX_MAX_GATHER_PROJ]; /* this rank's first non-finite scale as a word,
+                                            INT64_MAX for none                              */
+  apx_call_status *status[APX_MAX_GATHER_PROJ];     /* this rank's refusal words (device)  */
+  apx_call_status *out_status[APX_MAX_GATHER_PROJ]; /* the first refusal over all ranks, in
+                                                       whole-tensor rows; APX_ERR_DEVICE_TIMEOUT
+                                                       when a rank's flag did not arrive    */
+} apx_gather_desc;
+
+/* Queue the publication on `stream` after the projections that wrote this rank's rows (it
+ * waits for them on the device).  Work that follows on `stream` sees every rank's rows. */
+APX_API int apx_gather_publish_async(apx_ctx *ctx, const apx_gather_desc *gd, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

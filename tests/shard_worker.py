@@ -13,15 +13,28 @@ from oracle import oracle as O
 from apeiron_b200 import _abi, chart, shard, synth
 
 
+class Held:
+    """An uploaded shard: its bytes and geometry, and a handle for the device-path stand-in."""
+
+    def __init__(self, handle, ggml_type, raw, n_out, n_in):
+        self.handle, self.ggml_type, self.raw, self.n_out, self.n_in = \
+            handle, ggml_type, raw, n_out, n_in
+
+
 class OracleBackend:
     """`upload` / `matvec_q8act` of chart.Backend, computed by the oracle."""
 
+    def __init__(self):
+        self.held = {}
+
     def upload(self, ggml_type, raw, n_out, n_in):
-        return (ggml_type, np.array(raw, dtype=np.uint8, copy=True), n_out, n_in)
+        h = Held(len(self.held) + 1, ggml_type, np.array(raw, dtype=np.uint8, copy=True), n_out,
+                 n_in)
+        self.held[h.handle] = h
+        return h
 
     def matvec_q8act(self, ggml_type, tensor, n_out, n_in, q):
-        _, raw, _, _ = tensor
-        out, err = O.matvec_q8act_row(ggml_type, raw, n_out, n_in, q.codes, q.scales)
+        out, err = O.matvec_q8act_row(ggml_type, tensor.raw, n_out, n_in, q.codes, q.scales)
         if err is not None:
             e = _abi.ApxErr()
             for f, _ in _abi.ApxErr._fields_:
@@ -29,6 +42,30 @@ class OracleBackend:
                     setattr(e, f, getattr(err, f))
             chart._raise(e)
         return out
+
+
+class OracleLib:
+    """`apx_matvec_async` over CPU tensors (pointers are host addresses): the shard's Q32.32
+    outputs, or its refusal word, computed by the oracle."""
+
+    def __init__(self, backend):
+        self.be = backend
+
+    def apx_matvec_async(self, ctx, handle, n_out, n_in, codes, exps, desc, out, f32, status,
+                         stream):
+        import ctypes as C
+        h = self.be.held[handle]
+        c = np.ctypeslib.as_array((C.c_int8 * n_in).from_address(codes)).copy()
+        nb = (n_in + 31) // 32
+        e = np.ctypeslib.as_array((C.c_uint8 * nb).from_address(exps)).copy()
+        y, err = O.matvec_q8act_row(h.ggml_type, h.raw, n_out, n_in, c, O.exps_to_scales(e))
+        if err is None:
+            C.memmove(out, y.ctypes.data, 8 * n_out)
+        else:
+            word = np.array([(int(err.row) << 24) | (int(err.code) << 16) | (int(err.bits) & 0xFFFF)],
+                            dtype=np.uint64).view(np.int64)
+            C.memmove(status, word.ctypes.data, 8)
+        return 0
 
 
 def cases():
@@ -81,6 +118,26 @@ def run(rank, world, port, result_dir):
                 w[0] = (3 << 24) | (_abi.APX_ERR_OUTPUT_OVERFLOW << 16)
             rs.reduce_status(w)
             report[name + "/status"] = int(w[0].item())
+        # the grouped device path: the first two projections (own activations) and the two
+        # non-finite ones through one all-gather per group
+        lib = OracleLib(be)
+        cs = cases()
+        for gname, idx in (("group_ok", [0, 2]), ("group_nf", [4, 5, 1])):
+            shards = [shard.RowShard(be, cs[i][1], cs[i][2], cs[i][3], cs[i][4], rank, world,
+                                     dist, "cpu") for i in idx]
+            acts = []
+            for i in idx:
+                q = cs[i][5]
+                acts.append((torch.from_numpy(q.codes.copy()), torch.from_numpy(q.exps().copy()),
+                             torch.zeros(8, dtype=torch.int32)))
+            _, _, length = shard.group_layout(shards)
+            local = torch.zeros(length, dtype=torch.int64)
+            gathered = torch.zeros(world * length, dtype=torch.int64)
+            statuses = [torch.full((2,), -1, dtype=torch.int64) for _ in idx]
+            shard.matvec_group_async(shards, lib, None, acts, local, gathered, statuses, None)
+            g = gathered.numpy()
+            report[gname] = [(shard.assemble_group(shards, g, j).tolist(), int(statuses[j][0]))
+                             for j in range(len(idx))]
         np.save(os.path.join(result_dir, f"rank{rank}.npy"), np.array([report], dtype=object))
         dist.destroy_process_group()
     except Exception:

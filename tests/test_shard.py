@@ -101,3 +101,73 @@ def test_sharded_projections_equal_the_whole_tensor(world, tmp_path):
         want = min(cands) if cands else -1
         for rep in reports:
             assert rep[name + "/status"] == want, (name, rep[name + "/status"], want)
+    # grouped projections, one all-gather per group: outputs where the projection does not
+    # refuse, and each projection's own first refusal word
+    cs = shard_worker.cases()
+    for gname, idx in (("group_ok", [0, 2]), ("group_nf", [4, 5, 1])):
+        for rep in reports:
+            assert rep[gname] == reports[0][gname]
+        for j, i in enumerate(idx):
+            name, t, raw, n_out, n_in, q = cs[i]
+            got, word = reports[0][gname][j]
+            out, err = O.matvec_q8act_row(t, raw, n_out, n_in, q.codes, q.scales)
+            if err is None:
+                assert word == -1 and np.array_equal(np.array(got), out), (gname, name)
+            else:
+                nf = shard.first_nonfinite(t, raw, n_out, n_in)
+                want = (nf[0] << 24) | (_abi.APX_ERR_NONFINITE_SCALE << 16) | nf[1]
+                assert nf[0] == err.row and word == want, (gname, name, word, want)
+
+
+class _LayoutLib:
+    """apx_peer_alloc / apx_peer_open stand-ins that hand out fake addresses and record the
+    allocation size (no GPU)."""
+
+    def __init__(self):
+        self.size = None
+
+    def apx_peer_alloc(self, ctx, bytes_, ptr, handle, err):
+        self.size = bytes_
+        ptr._obj.value = 1 << 40
+        return 0
+
+    def apx_peer_open(self, ctx, handle, ptr, err):
+        ptr._obj.value = 2 << 40
+        return 0
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_peer_gather_layout_stays_inside_the_buffer(world):
+    """Every region a rank writes (its rows of each projection in both parities, the keys,
+    the flags, the epoch counters) lies inside the allocation, 16-byte aligned, with no two
+    regions overlapping."""
+    shapes = [(12, 28672, 64), (12, 97, 256), (8, 33, 64)]
+    be = shard_worker.OracleBackend()
+    for nproj in (1, 2, 3):
+        for rank in range(world):
+            shards = []
+            for t, n_out, n_in in shapes[:nproj]:
+                raw = np.zeros(n_out * shard.row_bytes(t, n_in), dtype=np.uint8)
+                shards.append(shard.RowShard(be, t, raw, n_out, n_in, rank, world, None, "cpu"))
+            lib = _LayoutLib()
+            g = shard.PeerGather(lib, None, shards)
+            d = g.desc
+            regions = []
+            for parity in (0, 1):
+                for j, sh in enumerate(shards):
+                    a = g.out_ptr(j, parity) - g.local
+                    assert a % 16 == 0 and d.rows_off[j] % 2 == 0
+                    regions.append((a, a + 8 * sh.rows))
+                    # every rank's rows of projection j (the peers write them here)
+                    for a0, b0 in sh.splits:
+                        lo = parity * g.stride + 8 * (g.base[j] + a0)
+                        assert lo + 8 * (b0 - a0) <= parity * g.stride + g.key_rel
+                k = parity * g.stride + g.key_rel
+                regions.append((k, k + 8 * world * nproj))
+            regions.append((g.flag_off, g.flag_off + 8 * world))
+            regions.append((g.ctr_off, g.ctr_off + 16))
+            regions.sort()
+            for (a, b), (c, e) in zip(regions, regions[1:]):
+                assert b <= c or a == b, (regions,)
+            assert regions[-1][1] <= lib.size
+            assert d.flag_off % 8 == 0 and d.ctr_off % 8 == 0
