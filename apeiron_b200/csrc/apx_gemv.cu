@@ -591,12 +591,14 @@ __global__ void __launch_bounds__(256, 2) gemv_stream_kernel(StreamArgs g) {
   // -- stream the chunk ---------------------------------------------------------------------
   Acc128 acc;
   acc_zero(acc);
-  for (long long x = x0; x < x1; x++) {
+  // the unit's row tile and K position advance with it (no division per unit)
+  long long rt = x0 / U;
+  int u = (int)(x0 - rt * U);
+  const uint8_t *next_unit = g.pack + (size_t)(x0 + 1) * F::unit_bytes;
+  for (long long x = x0; x < x1; x++, next_unit += F::unit_bytes) {
     UnitRegs<T> nxt;
     const bool more = x + 1 < x1;
-    if (more) load_unit(nxt, g.pack + (size_t)(x + 1) * F::unit_bytes, lane);
-    const long long rt = x / U;
-    const int u = (int)(x % U);
+    if (more) load_unit(nxt, next_unit, lane);
     fold_unit(acc, cur, s_codes + u * (F::span / 4), s_e + u * (F::span / 32),
               s_xs + u * F::nxs, desc.emin);
     if (u == U - 1 || !more) {
@@ -631,6 +633,10 @@ __global__ void __launch_bounds__(256, 2) gemv_stream_kernel(StreamArgs g) {
       acc_zero(acc);
     }
     if (more) cur = nxt;
+    if (++u == U) {
+      u = 0;
+      rt++;
+    }
   }
 }
 
