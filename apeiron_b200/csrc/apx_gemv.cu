@@ -530,8 +530,14 @@ struct StreamArgs {
   int kmax;           // most warps that can share a row tile
 };
 
+// Q6_K holds 53 registers of weights per unit (two with the prefetch): one CTA of 12 warps per
+// SM gives it the registers; the other families run two CTAs of 8 warps.
 template <uint32_t T>
-__global__ void __launch_bounds__(256, 2) gemv_stream_kernel(StreamArgs g) {
+__host__ __device__ constexpr int stream_threads() { return T == kQ6_K ? 384 : 256; }
+
+template <uint32_t T>
+__global__ void __launch_bounds__(stream_threads<T>(), T == kQ6_K ? 1 : 2)
+    gemv_stream_kernel(StreamArgs g) {
   extern __shared__ __align__(16) unsigned char smem[];
   using F = Fam<T>;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = blockDim.x / 32;
@@ -736,10 +742,10 @@ GemvPlan plan_gemv(uint32_t type, size_t n_out, size_t n_in, int sm_count) {
     const int span = type == kQ8_0 ? 128 : 256;
     const size_t nel = (size_t)K * span;
     pl.smem = nel + ((nel / 32 + 3) & ~(size_t)3) * 4 + nel / 16 * 8;
-    const int per_sm = pl.smem * 2 <= 200 * 1024 ? 2 : 1;
-    pl.block = 256;
+    const int per_sm = type != kQ6_K && pl.smem * 2 <= 200 * 1024 ? 2 : 1;
+    pl.block = type == kQ6_K ? 384 : 256;
     pl.grid = (unsigned)(sm_count * per_sm);
-    const long long V = (long long)pl.grid * 8;
+    const long long V = (long long)pl.grid * (pl.block / 32);
     pl.chunk = (long long)((T1 + V - 1) / V);
     pl.kmax = (int)((K + pl.chunk - 1) / pl.chunk) + 1;
     pl.R = pl.P = pl.ksplit = 1;
