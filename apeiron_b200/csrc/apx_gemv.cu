@@ -394,6 +394,7 @@ struct GemvArgs {
   unsigned *counters;   // [n_rt] arrivals of a K-split row tile (self-resetting)
   int R, P, ksplit;     // row tiles per CTA, warps per row tile, CTAs per row tile along K
   int act_bytes;        // shared bytes of the activation staging / partial sums
+  PeerRows peers;       // also store the outputs there (row-sharded gather), n = 0 otherwise
 };
 
 template <uint32_t T>
@@ -440,9 +441,11 @@ __global__ void __launch_bounds__(384, 2) gemv_kernel(GemvArgs g) {
     return;
   }
   if (!fast_path<T>(desc, g.n_in)) {
-    if (ks == 0 && p == 0 && active && slot == 0)
-      checked_row<T>(PackGeo{g.pack, g.units, L}, rt * H + lane / L, g.n_out, g.n_in, g.codes,
-                     g.exps, g.out_q32, g.out_f32, g.status);
+    if (ks == 0 && p == 0 && active && slot == 0) {
+      const RowOut o = checked_row<T>(PackGeo{g.pack, g.units, L}, rt * H + lane / L, g.n_out,
+                                      g.n_in, g.codes, g.exps, g.out_q32, g.out_f32, g.status);
+      if (o.ok) store_peers(g.peers, rt * H + lane / L, o.v);
+    }
     return;
   }
 
@@ -503,7 +506,7 @@ __global__ void __launch_bounds__(384, 2) gemv_kernel(GemvArgs g) {
     }
   }
   if (finalize && p == 0 && active && slot == 0)
-    finish_row(s, rt * H + lane / L, g.n_out, g.out_q32, g.out_f32, g.status);
+    finish_row(s, rt * H + lane / L, g.n_out, g.out_q32, g.out_f32, g.status, g.peers);
 }
 
 // ---- streaming kernel for matrices larger than one resident wave ---------------------------
@@ -528,6 +531,7 @@ struct StreamArgs {
   unsigned *counters; // [n_rt]
   long long chunk;    // C
   int kmax;           // most warps that can share a row tile
+  PeerRows peers;     // also store the outputs there (row-sharded gather), n = 0 otherwise
 };
 
 // Q6_K holds 53 registers of weights per unit (two with the prefetch): one CTA of 12 warps per
@@ -558,10 +562,13 @@ __global__ void __launch_bounds__(stream_threads<T>(), T == kQ6_K ? 1 : 2)
   }
   if (!fast_path<T>(desc, g.n_in)) {
     // the warp holding a row tile's first unit runs that tile's checked rows
-    for (long long x = x0; x < x1; x++)
-      if (x % U == 0)
-        checked_row<T>(PackGeo{g.pack, g.units, 1}, (size_t)(x / U) * 32 + lane, g.n_out,
-                       g.n_in, g.codes, g.exps, g.out_q32, g.out_f32, g.status);
+    for (long long x = x0; x < x1; x++) {
+      if (x % U != 0) continue;
+      const RowOut o = checked_row<T>(PackGeo{g.pack, g.units, 1}, (size_t)(x / U) * 32 + lane,
+                                      g.n_out, g.n_in, g.codes, g.exps, g.out_q32, g.out_f32,
+                                      g.status);
+      if (o.ok) store_peers(g.peers, (size_t)(x / U) * 32 + lane, o.v);
+    }
     return;
   }
 
@@ -613,7 +620,7 @@ __global__ void __launch_bounds__(stream_threads<T>(), T == kQ6_K ? 1 : 2)
       const long long last_v = (rt * U + U - 1) / g.chunk;
       const size_t row = (size_t)rt * 32 + lane;
       if (first_v == last_v) {
-        finish_row(acc, row, g.n_out, g.out_q32, g.out_f32, g.status);
+        finish_row(acc, row, g.n_out, g.out_q32, g.out_f32, g.status, g.peers);
       } else {
         const int k = (int)(v - first_v), count = (int)(last_v - first_v + 1);
         Acc128 *slot = g.partials + ((size_t)rt * g.kmax + k) * 32 + lane;
@@ -632,7 +639,7 @@ __global__ void __launch_bounds__(stream_threads<T>(), T == kQ6_K ? 1 : 2)
             const Acc128 *src = g.partials + ((size_t)rt * g.kmax + q) * 32 + lane;
             acc_add(s, __ldcg(&src->lo), __ldcg(&src->hi));
           }
-          finish_row(s, row, g.n_out, g.out_q32, g.out_f32, g.status);
+          finish_row(s, row, g.n_out, g.out_q32, g.out_f32, g.status, g.peers);
           if (lane == 0) g.counters[rt] = 0u;
         }
       }
@@ -731,7 +738,9 @@ static size_t warp_act_bytes(uint32_t t) {
 GemvPlan plan_gemv(uint32_t type, size_t n_out, size_t n_in, int sm_count) {
   GemvPlan pl{};
   const int K = units_per_row_tile(type, n_in);  // K-slots per row (0 for n_in = 0)
-  const size_t wave = (size_t)sm_count * 24;     // units one resident wave takes at once
+  // up to two resident waves of one unit per warp: past that the persistent streaming kernel;
+  // below it the streaming kernel's per-warp chunks would be too short to amortise its flush
+  const size_t wave = (size_t)sm_count * 48;
   const size_t T1 = (n_out + 31) / 32 * (size_t)K;
   if (T1 > wave) {
     // persistent streaming kernel: 2 CTAs of 8 warps per SM, one contiguous chunk per warp
@@ -825,7 +834,8 @@ static cudaError_t launch_cfg(Kern kern, const GemvPlan &pl, const Args &a, cuda
 cudaError_t launch_gemv(const GemvPlan &pl, uint32_t type, const uint8_t *pack, void *scratch,
                         size_t n_out, size_t n_in, const int8_t *codes, const uint8_t *exps,
                         const void *desc, long long *out_q32, float *out_f32,
-                        unsigned long long *status, cudaStream_t stream) {
+                        unsigned long long *status, cudaStream_t stream, const PeerRows *peers) {
+  const PeerRows no_peers{};
   if (n_out == 0) return cudaSuccess;
   if ((pl.pipe || pl.ksplit > 1) && !scratch) return cudaErrorInvalidValue;
   if (pl.units > 0 && !pack) return cudaErrorInvalidValue;  // a plan that reads no payload
@@ -847,6 +857,7 @@ cudaError_t launch_gemv(const GemvPlan &pl, uint32_t type, const uint8_t *pack, 
                                                pl.n_rt * (size_t)pl.kmax * 32);
     sa.chunk = pl.chunk;
     sa.kmax = pl.kmax;
+    sa.peers = peers ? *peers : no_peers;
     switch (type) {
       case kQ8_0: return launch_cfg(gemv_stream_kernel<kQ8_0>, pl, sa, stream);
       case kQ4_K: return launch_cfg(gemv_stream_kernel<kQ4_K>, pl, sa, stream);
@@ -875,6 +886,7 @@ cudaError_t launch_gemv(const GemvPlan &pl, uint32_t type, const uint8_t *pack, 
   a.P = pl.P;
   a.ksplit = pl.ksplit;
   a.act_bytes = pl.act_bytes;
+  a.peers = peers ? *peers : no_peers;
   switch (type) {
     case kQ8_0: return launch_cfg(gemv_kernel<kQ8_0>, pl, a, stream);
     case kQ4_K: return launch_cfg(gemv_kernel<kQ4_K>, pl, a, stream);

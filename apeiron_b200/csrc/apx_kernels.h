@@ -32,10 +32,17 @@ cudaError_t launch_repack(const GemvPlan &pl, const uint8_t *d_raw, uint8_t *d_p
 GemvPlan plan_gemv(uint32_t type, size_t n_out, size_t n_in, int sm_count);
 // Per-tensor device scratch of a K-split plan (partial sums + arrival counters, zeroed once).
 size_t gemv_scratch_bytes(const GemvPlan &pl);
+// Where a row-sharded projection also stores its Q32.32 outputs: this rank's rows in each
+// other rank's gather buffer (row 0 of the call at dst[i][0]); n = 0 for an ordinary call.
+struct PeerRows {
+  int n;
+  long long *dst[7];
+};
 cudaError_t launch_gemv(const GemvPlan &pl, uint32_t type, const uint8_t *pack, void *scratch,
                         size_t n_out, size_t n_in, const int8_t *codes, const uint8_t *exps,
                         const void *desc, long long *out_q32, float *out_f32,
-                        unsigned long long *status, cudaStream_t stream);
+                        unsigned long long *status, cudaStream_t stream,
+                        const PeerRows *peers = nullptr);
 
 // Activation kernels (apx_quant.cu).  `cols` activation vectors of width n laid out with
 // stride `ld` codes and `ldb` exponent bytes; one descriptor per column.

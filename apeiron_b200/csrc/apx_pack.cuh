@@ -6,6 +6,7 @@
 #pragma once
 
 #include "apx_common.cuh"
+#include "apx_kernels.h"
 
 namespace apx {
 
@@ -138,12 +139,26 @@ __device__ __forceinline__ bool add_checked(Acc128 &a, long long plo, long long 
   return !ovf;
 }
 
+// This output also into the other ranks' gather buffers (constant indices: no local copy of
+// the parameter block).
+__device__ __forceinline__ void store_peers(const PeerRows &pr, size_t row, long long v) {
+#pragma unroll
+  for (int i = 0; i < 7; i++)
+    if (i < pr.n) pr.dst[i][row] = v;
+}
+
+// matvec_fixed of one row: whether it produced an output, and the output.
+struct RowOut {
+  long long v;
+  bool ok;
+};
+
 template <uint32_t T>
-__device__ __noinline__ void checked_row(const PackGeo g, size_t row, size_t n_out, size_t n_in,
-                                         const int8_t *codes, const uint8_t *exps,
-                                         long long *out_q32, float *out_f32,
-                                         unsigned long long *status) {
-  if (row >= n_out) return;
+__device__ __noinline__ RowOut checked_row(const PackGeo g, size_t row, size_t n_out,
+                                           size_t n_in, const int8_t *codes, const uint8_t *exps,
+                                           long long *out_q32, float *out_f32,
+                                           unsigned long long *status) {
+  if (row >= n_out) return RowOut{0, false};
   Acc128 acc;
   acc_zero(acc);
   for (size_t i = 0; i < n_in; i++) {
@@ -153,21 +168,22 @@ __device__ __noinline__ void checked_row(const PackGeo g, size_t row, size_t n_o
     const long long w = weight_at<T>(g, row, i);
     if (!add_checked(acc, w * x, __mul64hi(w, x))) {
       atomicMin(status, pack_status(row, kKindAccOverflow, 0));
-      return;
+      return RowOut{0, false};
     }
   }
   long long v;
   if (!acc_round_to_i64(acc, v)) {
     atomicMin(status, pack_status(row, kKindOutputOverflow, 0));
-    return;
+    return RowOut{0, false};
   }
   if (out_q32) out_q32[row] = v;
   if (out_f32) out_f32[row] = __ll2float_rn(v) * 2.3283064365386963e-10f;
+  return RowOut{v, true};
 }
 
 __device__ __forceinline__ void finish_row(const Acc128 &s, size_t row, size_t n_out,
                                            long long *out_q32, float *out_f32,
-                                           unsigned long long *status) {
+                                           unsigned long long *status, const PeerRows &peers) {
   if (row >= n_out) return;
   long long v;
   if (!acc_round_to_i64(s, v)) {
@@ -175,6 +191,7 @@ __device__ __forceinline__ void finish_row(const Acc128 &s, size_t row, size_t n
   } else {
     if (out_q32) out_q32[row] = v;
     if (out_f32) out_f32[row] = __ll2float_rn(v) * 2.3283064365386963e-10f;
+    store_peers(peers, row, v);
   }
 }
 

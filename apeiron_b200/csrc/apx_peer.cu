@@ -1,23 +1,18 @@
 // apx_peer.cu — row shards' outputs between the GPUs of one node over NVLink peer stores.
 //
 // A row-sharded projection leaves each rank with its own rows; every rank needs the whole
-// vector.  The publication kernel below moves the rows with plain stores into the other ranks'
-// gather buffers (mapped through CUDA IPC), so the transfer is one short kernel on each rank
-// rather than a collective library call: one CTA per destination rank copies this rank's rows
-// of each projection (16-byte stores), writes this rank's refusal keys, fences at system scope
-// and releases this rank's epoch flag in the destination.  The CTA of this rank's own buffer
-// then waits, bounded in time, until every rank's flag has reached the epoch and reduces the
-// keys to the first refusal in whole-tensor row order (src/engine/chart/ffn.rs:659-661).
+// vector.  apx_matvec_gather_async runs the projection with its finish storing every output
+// row into this rank's slice of every rank's gather buffer (mapped through CUDA IPC), so the
+// transfer is spread over all SMs and overlaps the projection's tail.  The publication kernel
+// that follows (one warp; it starts once those grids have completed) writes this
+// rank's refusal keys into every buffer and releases this rank's epoch flag there, then waits,
+// bounded in time, until every rank's flag has reached the epoch in its own buffer and reduces
+// the keys to the first refusal in whole-tensor row order (src/engine/chart/ffn.rs:659-661).
 //
-// The epoch is a counter in each rank's own buffer: every CTA reads it (plus one) at its start,
-// the CTAs that write to other ranks check in on a second counter, and the CTA of the own
-// buffer stores the new epoch only after every rank's flag and every local check-in have
-// arrived.  So a replayed CUDA graph publishes fresh epochs, and no CTA of a launch can see
-// the epoch its own launch has already advanced.
-//
-// No remote atomics, no multicast: the only cross-GPU traffic is stores and the flag loads of
-// the waiting thread.  The wait gives up after gd.timeout_us and reports
-// APX_ERR_DEVICE_TIMEOUT in the merged refusal word.
+// The epoch is a counter in each rank's own buffer, read at the start of the publication and
+// advanced at its end, so a replayed CUDA graph publishes fresh epochs.  No remote atomics, no
+// multicast: the only cross-GPU traffic is stores and the flag loads of the waiting thread.
+// The wait gives up after gd.timeout_us and reports APX_ERR_DEVICE_TIMEOUT in the merged word.
 #include <cuda_runtime.h>
 
 #include <cstring>
@@ -28,6 +23,9 @@
 
 namespace apx {
 int context_device(const apx_ctx *ctx);
+bool tensor_launch_info(apx_ctx *ctx, uint64_t handle, uint32_t *type, const uint8_t **pack,
+                        void **scratch, size_t *n_out, size_t *n_in, GemvPlan *plan,
+                        int *device);
 
 namespace {
 
@@ -53,54 +51,39 @@ __device__ __forceinline__ unsigned long long now_ns() {
   return t;
 }
 
-__global__ void __launch_bounds__(512) gather_publish_kernel(const __grid_constant__
-                                                             apx_gather_desc g) {
+__global__ void __launch_bounds__(32) gather_publish_kernel(const __grid_constant__
+                                                            apx_gather_desc g) {
   pdl_launch_dependents();
-  pdl_wait();  // the projections that wrote this rank's rows and refusal words are done
-  const int q = blockIdx.x;  // destination rank
-  uint8_t *dst = static_cast<uint8_t *>(g.peer[q]);
-  uint8_t *src = static_cast<uint8_t *>(g.peer[g.rank]);
-  unsigned long long *ctr = reinterpret_cast<unsigned long long *>(src + g.ctr_off);
+  pdl_wait();  // the projections that stored this rank's rows everywhere are done
+  uint8_t *own = static_cast<uint8_t *>(g.peer[g.rank]);
+  unsigned long long *ctr = reinterpret_cast<unsigned long long *>(own + g.ctr_off);
   const unsigned long long epoch = *reinterpret_cast<volatile unsigned long long *>(ctr) + 1;
-  if (q != g.rank) {
-    for (int j = 0; j < g.nproj; j++) {
-      const size_t a = g.out_off + g.rows_off[j] * 8, n = g.rows[j] * 8;  // a: 16-aligned
-      const uint4 *s4 = reinterpret_cast<const uint4 *>(src + a);
-      uint4 *d4 = reinterpret_cast<uint4 *>(dst + a);
-      const size_t n16 = n / 16;
-      for (size_t i = threadIdx.x; i < n16; i += blockDim.x) d4[i] = s4[i];
-      if ((n & 15) && threadIdx.x == 0)
-        *reinterpret_cast<unsigned long long *>(dst + a + n16 * 16) =
-            *reinterpret_cast<const unsigned long long *>(src + a + n16 * 16);
+  const int q = threadIdx.x;  // thread q: rank q's buffer
+  if (q < g.world) {
+    uint8_t *dst = static_cast<uint8_t *>(g.peer[q]);
+    for (int j = 0; j < g.nproj; j++) {  // this rank's refusal keys
+      const unsigned long long w = g.status[j]->first;
+      long long key =
+          w == ~0ull ? kNoKey : (long long)(w + ((unsigned long long)g.row0[j] << kRowShift));
+      key = min(key, g.nf_key[j]);
+      reinterpret_cast<long long *>(dst + g.key_off)[g.rank * g.nproj + j] = key;
     }
-  }
-  if (threadIdx.x < (unsigned)g.nproj) {  // this rank's refusal keys
-    const int j = threadIdx.x;
-    const unsigned long long w = g.status[j]->first;
-    long long key = w == ~0ull ? kNoKey
-                               : (long long)(w + ((unsigned long long)g.row0[j] << kRowShift));
-    key = min(key, g.nf_key[j]);
-    reinterpret_cast<long long *>(dst + g.key_off)[g.rank * g.nproj + j] = key;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
+    // the rows the projections stored (their grids completed before this one passed its
+    // wait: their stores happen before it) and these keys precede the flag: the fence and
+    // the release are cumulative
     __threadfence_system();
     st_release_sys(reinterpret_cast<unsigned long long *>(dst + g.flag_off) + g.rank, epoch);
-    if (q != g.rank) atomicAdd(ctr + 1, 1ull);  // check in: this CTA has read the epoch
   }
-  if (q != g.rank || threadIdx.x != 0) return;
+  __syncwarp();  // every thread has read the epoch and the refusal words
+  if (q != 0) return;
 
-  // every rank's flag in this buffer and every local check-in (bounded wait), then the first
-  // refusal over the ranks
-  const unsigned long long *flags = reinterpret_cast<const unsigned long long *>(src + g.flag_off);
+  // every rank's flag in this buffer (bounded wait), then the first refusal over the ranks
+  const unsigned long long *flags = reinterpret_cast<const unsigned long long *>(own + g.flag_off);
   const unsigned long long t0 = now_ns(), limit = (unsigned long long)g.timeout_us * 1000ull;
   bool ok = true;
-  for (int r = 0; r <= g.world && ok; r++) {
-    // r < world: rank r's flag; r == world: the check-ins, (world - 1) per epoch so far
-    const unsigned long long *at = r < g.world ? flags + r : ctr + 1;
-    const unsigned long long want = r < g.world ? epoch : (unsigned long long)(g.world - 1) * epoch;
+  for (int r = 0; r < g.world && ok; r++) {
     unsigned ns = 32;
-    while (ld_acquire_sys(at) < want) {
+    while (ld_acquire_sys(flags + r) < epoch) {
       if (now_ns() - t0 > limit) {
         ok = false;
         break;
@@ -109,13 +92,14 @@ __global__ void __launch_bounds__(512) gather_publish_kernel(const __grid_consta
       if (ns < 1024) ns *= 2;
     }
   }
-  const long long *keys = reinterpret_cast<const long long *>(src + g.key_off);
+  const long long *keys = reinterpret_cast<const long long *>(own + g.key_off);
   for (int j = 0; j < g.nproj; j++) {
     long long m = kNoKey;
     for (int r = 0; ok && r < g.world; r++) m = min(m, ld_relaxed_sys(keys + r * g.nproj + j));
     g.out_status[j]->first = !ok ? pack_status(0, APX_ERR_DEVICE_TIMEOUT, 0)
                                  : (m == kNoKey ? ~0ull : (unsigned long long)m);
     g.out_status[j]->spare = 0;
+    g.status[j]->first = ~0ull;  // ready for the next projection into it
   }
   *reinterpret_cast<volatile unsigned long long *>(ctr) = epoch;
 }
@@ -183,6 +167,43 @@ APX_API int apx_device_read(apx_ctx *ctx, const void *d_src, void *host_dst, siz
   return e == cudaSuccess ? fail(err, APX_OK) : fail(err, APX_ERR_CUDA, e);
 }
 
+APX_API int apx_matvec_gather_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
+                                    const int8_t *d_codes, const uint8_t *d_exps,
+                                    const apx_act_desc *d_desc, const apx_gather_desc *gd,
+                                    int j, void *stream) {
+  if (!ctx || !gd || gd->world < 1 || gd->world > APX_MAX_PEERS || gd->rank < 0 ||
+      gd->rank >= gd->world || j < 0 || j >= gd->nproj || gd->nproj > APX_MAX_GATHER_PROJ ||
+      !gd->status[j] || n_out != gd->rows[j] || (gd->out_off & 7))
+    return APX_ERR_INVALID_ARGUMENT;
+  for (int r = 0; r < gd->world; r++)
+    if (!gd->peer[r]) return APX_ERR_INVALID_ARGUMENT;
+  uint32_t type;
+  const uint8_t *pack;
+  void *tscratch;
+  size_t t_out, t_in;
+  apx::GemvPlan plan;
+  int device;
+  if (!apx::tensor_launch_info(ctx, tensor, &type, &pack, &tscratch, &t_out, &t_in, &plan,
+                               &device))
+    return APX_ERR_INVALID_ARGUMENT;
+  if (n_in != t_in || n_out != t_out) return APX_ERR_LAYOUT_MISMATCH;
+  if (n_out == 0) return APX_OK;
+  if (!d_codes || !d_exps || !d_desc) return APX_ERR_INVALID_ARGUMENT;
+  if (cudaSetDevice(device) != cudaSuccess) return APX_ERR_CUDA;
+  auto rows_in = [&](int r) {
+    return reinterpret_cast<long long *>(static_cast<uint8_t *>(gd->peer[r]) + gd->out_off) +
+           gd->rows_off[j];
+  };
+  apx::PeerRows pr{};
+  for (int r = 0; r < gd->world; r++)
+    if (r != gd->rank) pr.dst[pr.n++] = rows_in(r);
+  const cudaError_t e =
+      apx::launch_gemv(plan, type, pack, tscratch, n_out, n_in, d_codes, d_exps, d_desc,
+                       rows_in(gd->rank), nullptr, &gd->status[j]->first,
+                       static_cast<cudaStream_t>(stream), &pr);
+  return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
+}
+
 APX_API int apx_gather_publish_async(apx_ctx *ctx, const apx_gather_desc *gd, void *stream) {
   if (!ctx || !gd || gd->world < 1 || gd->world > APX_MAX_PEERS || gd->rank < 0 ||
       gd->rank >= gd->world || gd->nproj < 1 || gd->nproj > APX_MAX_GATHER_PROJ ||
@@ -191,12 +212,11 @@ APX_API int apx_gather_publish_async(apx_ctx *ctx, const apx_gather_desc *gd, vo
   for (int r = 0; r < gd->world; r++)
     if (!gd->peer[r]) return APX_ERR_INVALID_ARGUMENT;
   for (int j = 0; j < gd->nproj; j++)
-    if ((gd->rows_off[j] & 1) || !gd->status[j] || !gd->out_status[j])
-      return APX_ERR_INVALID_ARGUMENT;  // rows start 16-byte aligned
+    if (!gd->status[j] || !gd->out_status[j]) return APX_ERR_INVALID_ARGUMENT;
   if (cudaSetDevice(apx::context_device(ctx)) != cudaSuccess) return APX_ERR_CUDA;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)gd->world);
-  cfg.blockDim = dim3(512);
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(32);
   cfg.stream = static_cast<cudaStream_t>(stream);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

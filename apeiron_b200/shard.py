@@ -312,9 +312,10 @@ class PeerGather:
       parity p (0, 1) at p·stride: the whole output vectors of the group's projections
       (projection j at element base[j], 32-element aligned), then the refusal keys
       [world][nproj]; after both parities the flags [world] and this rank's epoch counters.
-    `run` queues, on `stream`: a reset of this rank's refusal words, each projection's rows
-    written straight into this rank's buffer, and the publication that copies them into every
-    other rank's buffer and waits for everyone's.  Parities alternate per call; the epoch
+    `run` queues, on `stream`: each projection of this rank's rows, whose kernel stores every
+    output row into every rank's buffer, and the publication that posts this rank's refusal
+    keys and epoch flag everywhere, waits for everyone's and resets this rank's refusal words.  Nothing else runs between, so the next
+    projection streams its weights (programmatic dependent launch) during the publication.  Parities alternate per call; the epoch
     advances on the device, so `run` may be captured in a CUDA graph (an even number of
     calls per graph keeps the parities in step on replay).
     """
@@ -378,7 +379,8 @@ class PeerGather:
 
     def run(self, acts, statuses, out_statuses, stream, shards=None) -> int:
         """One publication of the group.  `acts[j]` = (codes, exps, desc) device tensors of
-        projection j; `statuses` an int64 tensor (nproj, 2) for this rank's refusal words;
+        projection j; `statuses` an int64 tensor (nproj, 2) for this rank's refusal words (all
+        ones before the first call; each publication resets them after reading them);
         `out_statuses` an int64 tensor (nproj, 2) that receives the first refusal over all
         ranks (whole-tensor rows).  `shards` may name other uploads of the same rows (copies
         of the weights).  Everything is queued on the current torch stream, which must be
@@ -386,22 +388,20 @@ class PeerGather:
         import ctypes as C
 
         parity = (self.calls + 1) % 2
-        statuses.fill_(-1)
-        for j, sh in enumerate(shards or self.shards):
-            codes, exps, desc = acts[j]
-            if sh.rows:
-                rc = self.lib.apx_matvec_async(self.ctx, sh.tensor.handle, sh.rows, sh.n_in,
-                                               codes.data_ptr(), exps.data_ptr(), desc.data_ptr(),
-                                               self.out_ptr(j, parity), None,
-                                               statuses[j].data_ptr(), stream)
-                if rc:
-                    raise chart.BackendError(f"apx_matvec_async failed with code {rc}")
         d = self.desc
         d.out_off = parity * self.stride
         d.key_off = parity * self.stride + self.key_rel
         for j in range(self.nproj):
             d.status[j] = statuses[j].data_ptr()
             d.out_status[j] = out_statuses[j].data_ptr()
+        for j, sh in enumerate(shards or self.shards):
+            codes, exps, desc = acts[j]
+            if sh.rows:  # this rank's rows, stored into every rank's buffer by the kernel
+                rc = self.lib.apx_matvec_gather_async(self.ctx, sh.tensor.handle, sh.rows,
+                                                      sh.n_in, codes.data_ptr(), exps.data_ptr(),
+                                                      desc.data_ptr(), C.byref(d), j, stream)
+                if rc:
+                    raise chart.BackendError(f"apx_matvec_gather_async failed with code {rc}")
         rc = self.lib.apx_gather_publish_async(self.ctx, C.byref(d), stream)
         if rc:
             raise chart.BackendError(f"apx_gather_publish_async failed with code {rc}")

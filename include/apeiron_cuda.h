@@ -248,11 +248,12 @@ APX_API int apx_matvec_f32_noalloc(apx_ctx *ctx, uint64_t tensor, size_t n_out, 
  * A projection's rows are independent, so P processes (one per GPU) can each hold a row range
  * of W and project it; every rank then needs the whole output vector.  These calls move it
  * over NVLink with plain peer stores, without a collective library: each rank owns one gather
- * buffer that every other rank maps (CUDA IPC), the projections write their rows straight into
- * the local buffer, and apx_gather_publish_async copies them into every peer's buffer, posts
- * this rank's refusal keys and an epoch flag, and waits (bounded) for every rank's flag.  The
- * output area and the keys are double-buffered by epoch parity, so a rank that runs ahead
- * never overwrites what another is still reading.  The epoch (1, 2, ...) lives in each rank's
+ * buffer that every other rank maps (CUDA IPC); apx_matvec_gather_async projects this rank's
+ * rows and its kernel stores every output row into this rank's slice of every rank's buffer;
+ * apx_gather_publish_async then posts this rank's refusal keys and an epoch flag in every
+ * buffer and waits (bounded) for every rank's flag.  The output area and the keys are
+ * double-buffered by epoch parity, so a rank that runs ahead never overwrites what another is
+ * still reading.  The epoch (1, 2, ...) lives in each rank's
  * own buffer and advances on the device, so the calls can be captured in a CUDA graph and
  * replayed.  The caller (apeiron_b200/shard.py) owns the buffer layout and alternates the
  * parity; every rank must make the same calls in the same order. */
@@ -287,7 +288,7 @@ typedef struct apx_gather_desc {
   size_t flag_off;                       /* the flags: [world] uint64, epoch of each rank  */
   size_t ctr_off;                        /* this rank's epoch and check-in count (2 uint64,
                                             read only in its own buffer; zero at alloc)    */
-  size_t rows_off[APX_MAX_GATHER_PROJ];  /* first element of this rank's rows of proj. j   */
+  size_t rows_off[APX_MAX_GATHER_PROJ];  /* element of this rank's first row of proj. j   */
   size_t rows[APX_MAX_GATHER_PROJ];      /* this rank's rows of projection j               */
   long long row0[APX_MAX_GATHER_PROJ];   /* whole-tensor row of this rank's first row      */
   long long nf_key[APX_MAX_GATHER_PROJ]; /* this rank's first non-finite scale as a word,
@@ -298,8 +299,15 @@ typedef struct apx_gather_desc {
                                                        when a rank's flag did not arrive    */
 } apx_gather_desc;
 
-/* Queue the publication on `stream` after the projections that wrote this rank's rows (it
- * waits for them on the device).  Work that follows on `stream` sees every rank's rows. */
+/* Projection j of the publication on `stream`: this rank's gd->rows[j] rows (the tensor holds
+ * exactly them) from device activations, each Q32.32 output stored into every rank's buffer at
+ * element rows_off[j] + row of the area at out_off, the refusal word into gd->status[j]. */
+APX_API int apx_matvec_gather_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
+                                    const int8_t *d_codes, const uint8_t *d_exps,
+                                    const apx_act_desc *d_desc, const apx_gather_desc *gd,
+                                    int j, void *stream);
+/* Queue the publication on `stream` after the group's apx_matvec_gather_async calls (it waits
+ * for them on the device).  Work that follows on `stream` sees every rank's rows. */
 APX_API int apx_gather_publish_async(apx_ctx *ctx, const apx_gather_desc *gd, void *stream);
 
 #ifdef __cplusplus
