@@ -395,7 +395,40 @@ struct GemvArgs {
   int R, P, ksplit;     // row tiles per CTA, warps per row tile, CTAs per row tile along K
   int act_bytes;        // shared bytes of the activation staging / partial sums
   PeerRows peers;       // also store the outputs there (row-sharded gather), n = 0 otherwise
+  GemvGroup grp;        // several tensors sharing the activation, n = 0 otherwise
 };
+
+// The group member holding the launch's row tile grt: its weights and its local row tile.
+// Constant indices throughout, so the parameter block stays in the constant bank.
+__device__ __forceinline__ void group_member(const GemvGroup &grp, size_t grt, size_t &rt,
+                                             const uint8_t *&pack) {
+#pragma unroll
+  for (int t = 0; t < kMaxGroup; t++) {
+    const size_t begin = t ? grp.rt_end[t - 1] : 0;
+    if (t < grp.n && grt >= begin && grt < grp.rt_end[t]) {
+      rt = grt - begin;
+      pack = grp.pack[t];
+    }
+  }
+}
+
+struct GroupOut {
+  size_t n_out;
+  long long *q32;
+  float *f32;
+  unsigned long long *status;
+};
+
+__device__ __forceinline__ GroupOut group_outputs(const GemvGroup &grp, size_t grt) {
+  GroupOut o{0, nullptr, nullptr, nullptr};
+#pragma unroll
+  for (int t = 0; t < kMaxGroup; t++) {
+    const size_t begin = t ? grp.rt_end[t - 1] : 0;
+    if (t < grp.n && grt >= begin && grt < grp.rt_end[t])
+      o = GroupOut{grp.n_out[t], grp.out_q32[t], grp.out_f32[t], grp.status[t]};
+  }
+  return o;
+}
 
 template <uint32_t T>
 __global__ void __launch_bounds__(384, 2) gemv_kernel(GemvArgs g) {
@@ -413,9 +446,13 @@ __global__ void __launch_bounds__(384, 2) gemv_kernel(GemvArgs g) {
   const int k0 = (int)((long long)g.units * ks / g.ksplit);
   const int k1 = (int)((long long)g.units * (ks + 1) / g.ksplit);
   const int r = warp / g.P, p = warp % g.P;
-  const size_t rt = rt0 + r;
   const bool active = r < nr;
-  const uint8_t *base = g.pack + rt * (size_t)g.units * F::unit_bytes;
+  // this warp's tensor: the launch's own, or the group member holding row tile rt0 + r (its
+  // outputs are selected again at the finish, so they hold no registers through the fold)
+  size_t rt = rt0 + r;
+  const uint8_t *pack = g.pack;
+  if (g.grp.n) group_member(g.grp, rt0 + r, rt, pack);
+  const uint8_t *base = pack + rt * (size_t)g.units * F::unit_bytes;
   const int L = g.L, H = 32 / L, slot = lane % L;
   const int nch = L * F::span / 16;  // chunks staged per unit: 8, 16, 32 or 64
 
@@ -436,14 +473,20 @@ __global__ void __launch_bounds__(384, 2) gemv_kernel(GemvArgs g) {
       ch1 = load_chunk(g.codes, g.exps, g.n_in, chunk_first<T>(k0 + p, L, lane + 32));
   }
   if (desc.status != APX_OK) {  // the activation itself is refused (chart/mod.rs:1904-1907)
-    if (blockIdx.x == 0 && threadIdx.x == 0)
-      atomicMin(g.status, pack_status(0, (unsigned)desc.status, 0));
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+      if (!g.grp.n) atomicMin(g.status, pack_status(0, (unsigned)desc.status, 0));
+#pragma unroll
+      for (int t = 0; t < kMaxGroup; t++)
+        if (t < g.grp.n) atomicMin(g.grp.status[t], pack_status(0, (unsigned)desc.status, 0));
+    }
     return;
   }
   if (!fast_path<T>(desc, g.n_in)) {
     if (ks == 0 && p == 0 && active && slot == 0) {
-      const RowOut o = checked_row<T>(PackGeo{g.pack, g.units, L}, rt * H + lane / L, g.n_out,
-                                      g.n_in, g.codes, g.exps, g.out_q32, g.out_f32, g.status);
+      GroupOut go{g.n_out, g.out_q32, g.out_f32, g.status};
+      if (g.grp.n) go = group_outputs(g.grp, rt0 + r);
+      const RowOut o = checked_row<T>(PackGeo{pack, g.units, L}, rt * H + lane / L, go.n_out,
+                                      g.n_in, g.codes, g.exps, go.q32, go.f32, go.status);
       if (o.ok) store_peers(g.peers, rt * H + lane / L, o.v);
     }
     return;
@@ -505,8 +548,11 @@ __global__ void __launch_bounds__(384, 2) gemv_kernel(GemvArgs g) {
       if (lane == 0) g.counters[rt] = 0u;  // ready for the next call
     }
   }
-  if (finalize && p == 0 && active && slot == 0)
-    finish_row(s, rt * H + lane / L, g.n_out, g.out_q32, g.out_f32, g.status, g.peers);
+  if (finalize && p == 0 && active && slot == 0) {
+    GroupOut go{g.n_out, g.out_q32, g.out_f32, g.status};
+    if (g.grp.n) go = group_outputs(g.grp, rt0 + r);
+    finish_row(s, rt * H + lane / L, go.n_out, go.q32, go.f32, go.status, g.peers);
+  }
 }
 
 // ---- streaming kernel for matrices larger than one resident wave ---------------------------
@@ -887,6 +933,37 @@ cudaError_t launch_gemv(const GemvPlan &pl, uint32_t type, const uint8_t *pack, 
   a.ksplit = pl.ksplit;
   a.act_bytes = pl.act_bytes;
   a.peers = peers ? *peers : no_peers;
+  a.grp = GemvGroup{};
+  switch (type) {
+    case kQ8_0: return launch_cfg(gemv_kernel<kQ8_0>, pl, a, stream);
+    case kQ4_K: return launch_cfg(gemv_kernel<kQ4_K>, pl, a, stream);
+    case kQ6_K: return launch_cfg(gemv_kernel<kQ6_K>, pl, a, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_gemv_group(const GemvPlan &pl, uint32_t type, const GemvGroup &grp,
+                              size_t n_in, const int8_t *codes, const uint8_t *exps,
+                              const void *desc, cudaStream_t stream) {
+  if (grp.n < 1 || grp.n > kMaxGroup || pl.pipe || pl.ksplit != 1) return cudaErrorInvalidValue;
+  GemvArgs a{};
+  a.pack = grp.pack[0];
+  a.units = pl.units;
+  a.L = pl.L;
+  a.n_rt = pl.n_rt;
+  a.n_out = grp.n_out[0];
+  a.n_in = n_in;
+  a.codes = codes;
+  a.exps = exps;
+  a.desc = reinterpret_cast<const ActDesc *>(desc);
+  a.out_q32 = grp.out_q32[0];
+  a.out_f32 = grp.out_f32[0];
+  a.status = grp.status[0];
+  a.R = pl.R;
+  a.P = pl.P;
+  a.ksplit = 1;
+  a.act_bytes = pl.act_bytes;
+  a.grp = grp;
   switch (type) {
     case kQ8_0: return launch_cfg(gemv_kernel<kQ8_0>, pl, a, stream);
     case kQ4_K: return launch_cfg(gemv_kernel<kQ4_K>, pl, a, stream);

@@ -38,6 +38,24 @@ struct PeerRows {
   int n;
   long long *dst[7];
 };
+// Up to kMaxGroup tensors of one family and width read by one launch (projections that share
+// an activation): row tile rt of the launch is row tile rt - rt_begin(t) of tensor t, where
+// rt_end holds the cumulative row-tile counts.  n = 0 for an ordinary launch.
+constexpr int kMaxGroup = 4;
+struct GemvGroup {
+  int n;
+  const uint8_t *pack[kMaxGroup];
+  size_t rt_end[kMaxGroup];
+  size_t n_out[kMaxGroup];
+  long long *out_q32[kMaxGroup];
+  float *out_f32[kMaxGroup];
+  unsigned long long *status[kMaxGroup];
+};
+// One launch over a group (every tensor planned one-wave with the same lanes per row and units
+// per row tile; `pl` planned for the concatenated row tiles, with ksplit 1).
+cudaError_t launch_gemv_group(const GemvPlan &pl, uint32_t type, const GemvGroup &grp,
+                              size_t n_in, const int8_t *codes, const uint8_t *exps,
+                              const void *desc, cudaStream_t stream);
 cudaError_t launch_gemv(const GemvPlan &pl, uint32_t type, const uint8_t *pack, void *scratch,
                         size_t n_out, size_t n_in, const int8_t *codes, const uint8_t *exps,
                         const void *desc, long long *out_q32, float *out_f32,

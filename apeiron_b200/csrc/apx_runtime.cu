@@ -814,6 +814,75 @@ int apx_matvec_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
   return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
 }
 
+static_assert(APX_MAX_GROUP == kMaxGroup, "group size in the header");
+
+int apx_matvec_group_async(apx_ctx *ctx, const uint64_t *tensors, int count, size_t n_in,
+                           const int8_t *d_codes, const uint8_t *d_exps,
+                           const apx_act_desc *d_desc, int64_t *const *d_out_q32,
+                           float *const *d_out_f32, apx_call_status *const *d_status,
+                           void *stream) {
+  if (!ctx || !tensors || count < 1 || !d_desc || !d_status) return APX_ERR_INVALID_ARGUMENT;
+  Tensor *ts[APX_MAX_GROUP];
+  bool one_launch = count <= APX_MAX_GROUP;
+  {
+    std::lock_guard<std::mutex> g(ctx->mu);
+    for (int i = 0; i < count; i++) {
+      Tensor *t = find(ctx, tensors[i]);
+      if (!t || t->n_in != n_in || !d_status[i]) return APX_ERR_LAYOUT_MISMATCH;
+      if (i < APX_MAX_GROUP) ts[i] = t;
+    }
+  }
+  // one launch when every member is a one-wave tensor of the first one's family and layout and
+  // the concatenated row tiles still plan as one wave without a K split
+  GemvPlan pl{};
+  if (one_launch) {
+    size_t n_rt = 0;
+    for (int i = 0; i < count; i++) {
+      const Tensor &t = *ts[i];
+      one_launch = one_launch && t.d_pack && t.n_out > 0 && !t.plan.pipe &&
+                   t.plan.ksplit == 1 && t.type == ts[0]->type && t.plan.L == ts[0]->plan.L &&
+                   t.plan.units == ts[0]->plan.units;
+      n_rt += t.plan.n_rt;
+    }
+    if (one_launch) {
+      pl = plan_gemv(ts[0]->type, n_rt * (size_t)(32 / ts[0]->plan.L), n_in, ctx->sm_count);
+      one_launch = !pl.pipe && pl.ksplit == 1 && pl.L == ts[0]->plan.L &&
+                   pl.units == ts[0]->plan.units && pl.n_rt == n_rt;
+    }
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  if (!one_launch) {  // one launch per tensor
+    for (int i = 0; i < count; i++) {
+      Tensor *t;
+      {
+        std::lock_guard<std::mutex> g(ctx->mu);
+        t = find(ctx, tensors[i]);
+      }
+      cudaError_t e = launch_gemv(t->plan, t->type, t->d_pack, t->d_scratch, t->n_out, n_in,
+                                  d_codes, d_exps, d_desc,
+                                  d_out_q32 ? (long long *)d_out_q32[i] : nullptr,
+                                  d_out_f32 ? d_out_f32[i] : nullptr,
+                                  (unsigned long long *)&d_status[i]->first, st);
+      if (e != cudaSuccess) return APX_ERR_CUDA;
+    }
+    return APX_OK;
+  }
+  GemvGroup grp{};
+  grp.n = count;
+  size_t end = 0;
+  for (int i = 0; i < count; i++) {
+    end += ts[i]->plan.n_rt;
+    grp.pack[i] = ts[i]->d_pack;
+    grp.rt_end[i] = end;
+    grp.n_out[i] = ts[i]->n_out;
+    grp.out_q32[i] = d_out_q32 ? (long long *)d_out_q32[i] : nullptr;
+    grp.out_f32[i] = d_out_f32 ? d_out_f32[i] : nullptr;
+    grp.status[i] = (unsigned long long *)&d_status[i]->first;
+  }
+  cudaError_t e = launch_gemv_group(pl, ts[0]->type, grp, n_in, d_codes, d_exps, d_desc, st);
+  return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
+}
+
 int apx_matmat_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in, size_t k_cols,
                      const int8_t *d_codes, const uint8_t *d_exps, const apx_act_desc *d_descs,
                      int64_t *d_out_q32, float *d_out_f32, apx_call_status *d_status,

@@ -206,6 +206,150 @@ def measure_prefill(be, lib, dev, stream, steps, warmup, pg, local, world):
     }
 
 
+# one decode step of a Qwen2.5-0.5B-shaped Q4_K_M model, every linear layer
+DECODE_LAYER = [(12, 896, 896), (12, 128, 896), (12, 128, 896), (12, 896, 896),   # q k v o
+                (12, 4864, 896), (12, 4864, 896), (12, 896, 4864)]                # gate up down
+DECODE_LAYERS = 24
+DECODE_HEAD = (14, 151936, 896)                                                   # tied lm_head
+
+
+def measure_decode_step(be, lib, dev, stream, steps, warmup, pg, local, world):
+    """the 169 projections of one decode step (24 layers of q/k/v/o/gate/up/down in
+    Q4_K, the Q6_K head) as one chain of launches replayed from a CUDA graph; every projection
+    reads a resident activation of its width (the quantizer and the nonlinear layers between
+    them are not on this path).  Replicas at N > 1."""
+    import torch
+
+    from apeiron_b200 import synth
+    from oracle import oracle as O
+
+    sp = stream.cuda_stream
+    mats = DECODE_LAYER * DECODE_LAYERS + [DECODE_HEAD]
+    per_step = sum(gemv_bytes(*m) for m in mats)
+    raws = {}
+    for i, (t, n_out, n_in) in enumerate(DECODE_LAYER + [DECODE_HEAD]):
+        raws[i] = synth.payload(t, n_out, n_in, 6000 + i)
+    wbytes = sum(raws[i % len(DECODE_LAYER)].size if i < len(mats) - 1 else raws[len(DECODE_LAYER)].size
+                 for i in range(len(mats)))
+    copies = max(2, int(np.ceil(3 * L2_BYTES / wbytes)))
+    # every layer its own upload (the same bytes per layer position: uploads are independent)
+    tensors = []
+    for c in range(copies):
+        row = []
+        for i, (t, n_out, n_in) in enumerate(mats):
+            key = len(DECODE_LAYER) if i == len(mats) - 1 else i % len(DECODE_LAYER)
+            row.append(be.upload(t, raws[key], n_out, n_in))
+        tensors.append(row)
+    acts = {}
+    for n_in in sorted({m[2] for m in mats}):
+        x = synth.activation_f32(n_in, 7000 + n_in)
+        c, e = synth.quant_act_np(synth.f32_to_q32(x))
+        pad = lib.apx_act_padded_len(n_in)
+        codes = torch.zeros(pad, dtype=torch.int8, device=dev)
+        codes[:n_in] = torch.from_numpy(c).to(dev)
+        exps = torch.full((pad // 32,), 0xFF, dtype=torch.uint8, device=dev)
+        exps[:e.size] = torch.from_numpy(e).to(dev)
+        desc = torch.zeros(8, dtype=torch.int32, device=dev)
+        with torch.cuda.stream(stream):
+            assert lib.apx_act_describe_async(be.ctx, codes.data_ptr(), exps.data_ptr(), n_in,
+                                              desc.data_ptr(), sp) == 0
+        acts[n_in] = (codes, exps, desc, c, e)
+    import ctypes as C
+
+    outs = [torch.zeros(m[1], dtype=torch.int64, device=dev) for m in mats]
+    status = torch.full((2,), -1, dtype=torch.int64, device=dev)
+    # projections that read the same activation share a launch (apx_matvec_group_async):
+    # q/k/v and gate/up of every layer; o, down and the head run alone
+    per_layer = [[0, 1, 2], [3], [4, 5], [6]]
+    launches = []  # (member indices into mats)
+    for layer in range(DECODE_LAYERS):
+        for g in per_layer:
+            launches.append([layer * len(DECODE_LAYER) + k for k in g])
+    launches.append([len(mats) - 1])
+    arrays = []  # per copy, per launch: the ctypes arrays of a grouped call
+    for c in range(copies):
+        row = []
+        for g in launches:
+            if len(g) == 1:
+                row.append(None)
+                continue
+            n = len(g)
+            row.append(((C.c_uint64 * n)(*[tensors[c][k].handle for k in g]),
+                        (C.c_void_p * n)(*[outs[k].data_ptr() for k in g]),
+                        (C.c_void_p * n)(*[status.data_ptr()] * n)))
+        arrays.append(row)
+
+    def step(i):
+        row = tensors[i % copies]
+        for li, g in enumerate(launches):
+            t, n_out, n_in = mats[g[0]]
+            codes, exps, desc, _, _ = acts[n_in]
+            if len(g) == 1:
+                k = g[0]
+                rc = lib.apx_matvec_async(be.ctx, row[k].handle, n_out, n_in, codes.data_ptr(),
+                                          exps.data_ptr(), desc.data_ptr(), outs[k].data_ptr(),
+                                          None, status.data_ptr(), sp)
+            else:
+                hs, os_, ss = arrays[i % copies][li]
+                rc = lib.apx_matvec_group_async(be.ctx, hs, len(g), n_in, codes.data_ptr(),
+                                                exps.data_ptr(), desc.data_ptr(), os_, None, ss,
+                                                sp)
+            assert rc == 0
+
+    with torch.cuda.stream(stream):
+        step(0)
+    stream.synchronize()
+    for k in list(range(len(DECODE_LAYER))) + [len(mats) - 1]:  # one layer and the head
+        t, n_out, n_in = mats[k]
+        key = len(DECODE_LAYER) if k == len(mats) - 1 else k
+        _, _, _, c, e = acts[n_in]
+        want = O.matvec_q8act_mt(t, raws[key], n_out, n_in, c, O.exps_to_scales(e),
+                                 os.cpu_count() or 1)
+        assert np.array_equal(outs[k].cpu().numpy(), want), "decode-step parity failure"
+    assert int(status[0].item()) == -1
+    G = max(2, min(steps, 20))
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=stream):
+        for i in range(G):
+            step(i)
+    with torch.cuda.stream(stream):
+        for i in range(warmup):
+            step(i)
+        gr.replay()
+    stream.synchronize()
+    barrier(pg, local)
+    reps = max(1, steps // G)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for _ in range(reps):
+            gr.replay()
+        t1.record(stream)
+    stream.synchronize()
+    barrier(pg, local)
+    ms = max_over_ranks(t0.elapsed_time(t1), pg, local) / (reps * G)
+    assert int(status[0].item()) == -1
+    del gr
+    hbm, _ = peaks()
+    gbs = world * per_step / (ms / 1e3) / 1e9
+    return {
+        "metric": "decode step GB/s (all linear layers)", "value": gbs, "unit": "GB/s",
+        "ms_per_step": ms, "steps": reps * G, "tokens_per_s": world * 1e3 / ms,
+        "scaling": "weak",
+        "config": {"workload": "Qwen2.5-0.5B-shaped Q4_K_M decode step, configs[3]: 24 layers "
+                               "x (q 896x896, k/v 128x896, o 896x896, gate/up 4864x896, down "
+                               "896x4864) Q4_K + tied lm_head 151936x896 Q6_K = 169 projections "
+                               "in 97 launches (q/k/v and gate/up of a layer share one), resident "
+                               "activations",
+                   "bytes_per_step": per_step, "weight_copies": copies,
+                   "l2": "rotating weight copies, >= 3x the 126 MB L2",
+                   "exact": "one layer's projections and the head bit-equal to the CPU oracle "
+                            "(checked before timing)"},
+        "hbm_frac": gbs / world / hbm,
+        "gpu_launches_per_step": len(launches),
+    }
+
+
 SHARDED = [(12, 28672, 8192), (12, 28672, 8192), (12, 8192, 28672)]  # gate, up, down
 
 
@@ -668,6 +812,10 @@ def run_ours(args, world, rank, local, pg):
     if not args.no_prefill:
         prefill = measure_prefill(be, lib, dev, stream, args.prefill_steps, args.warmup, pg,
                                   local, world)
+    decode = None
+    if not args.no_decode:
+        decode = measure_decode_step(be, lib, dev, stream, args.decode_steps, args.warmup, pg,
+                                     local, world)
     sharded = None
     if not args.no_shard:
         sharded = measure_sharded(be, lib, dev, stream, args.shard_steps, args.warmup, pg, rank,
@@ -707,6 +855,9 @@ def run_ours(args, world, rank, local, pg):
     if prefill is not None:
         line["prefill"] = prefill
         line["gpu_launches"] += prefill["gpu_launches_per_step"] * prefill["steps"]
+    if decode is not None:
+        line["decode_step"] = decode
+        line["gpu_launches"] += decode["gpu_launches_per_step"] * decode["steps"]
     if sharded is not None:
         line["sharded"] = sharded
         line["gpu_launches"] += len(SHARDED) * sharded["steps"]
@@ -724,6 +875,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-shard", action="store_true")
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--decode-steps", type=int, default=200)
     ap.add_argument("--shard-steps", type=int, default=400)
     ap.add_argument("--prefill-steps", type=int, default=400)
     args = ap.parse_args()

@@ -207,6 +207,17 @@ APX_API int apx_matmat_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t
                      size_t k_cols, const int8_t *d_codes, const uint8_t *d_exps,
                      const apx_act_desc *d_descs, int64_t *d_out_q32,
                      float *d_out_f32, apx_call_status *d_status, void *stream);
+/* Several projections that read the same device activation (q/k/v of a layer, gate/up of a
+ * FFN), each over its whole tensor: out[i] = matvec(tensors[i], x), refusal word in
+ * d_status[i] (all ones on entry).  Up to APX_MAX_GROUP tensors of one family whose layout
+ * allows it run as ONE launch over their concatenated row tiles; otherwise one launch each.
+ * d_out_q32 / d_out_f32 are arrays of `count` device pointers (either array may be NULL). */
+#define APX_MAX_GROUP 4
+APX_API int apx_matvec_group_async(apx_ctx *ctx, const uint64_t *tensors, int count,
+                                   size_t n_in, const int8_t *d_codes, const uint8_t *d_exps,
+                                   const apx_act_desc *d_desc, int64_t *const *d_out_q32,
+                                   float *const *d_out_f32, apx_call_status *const *d_status,
+                                   void *stream);
 /* Activation buffer length (bytes of codes) the async kernels read for width n_in. */
 APX_API size_t apx_act_padded_len(size_t n_in);
 /* Decode a refusal word (host copy of *d_status) together with the tensor's
