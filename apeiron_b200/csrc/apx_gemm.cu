@@ -180,7 +180,17 @@ __device__ __forceinline__ void fold(long long (&acc)[kEpiTok], const uint32_t (
 // that fits, and f32(v·2^-32) = RN(acc)·2^(s−64) (a power-of-two scaling commutes with the
 // one rounding).  For s < 32, v = (acc + 2^(31−s)) >> (32−s), which always fits (|acc| < 2^62
 // by the route's bound), and its f32 image is RN(v)·2^-32.  One conversion either way.
-__device__ __forceinline__ bool finish_one(long long acc, unsigned s, long long &v, float &f) {
+// The rounding's general case (s outside [32, 64)), out of line: the finish unrolls 32
+// outputs per thread, and an inlined copy of this per output would crowd the instruction cache.
+struct FinishOut {
+  long long v;
+  float f;
+  bool fits;
+};
+
+__device__ __noinline__ FinishOut finish_one(long long acc, unsigned s) {
+  long long v;
+  float f;
   bool fits = true;
   long long x;  // the integer whose rounding gives the f32 image
   int k;        // its power-of-two scale
@@ -197,7 +207,7 @@ __device__ __forceinline__ bool finish_one(long long acc, unsigned s, long long 
     k = -32;
   }
   f = __ll2float_rn(x) * __int_as_float((127 + k) << 23);
-  return fits;
+  return FinishOut{v, f, fits};
 }
 
 // finish_one for the common case 32 <= s < 64 with the range check on the accumulator's
@@ -211,7 +221,10 @@ __device__ __forceinline__ bool finish_fast(long long acc, unsigned s, long long
     f = __ll2float_rn(acc) * __int_as_float((int)(s + 63) << 23);  // 2^(s − 64)
     return (hi >> (31 - t)) == (hi >> 31);
   }
-  return finish_one(acc, s, v, f);
+  const FinishOut o = finish_one(acc, s);
+  v = o.v;
+  f = o.f;
+  return o.fits;
 }
 
 // ---- per-call workspace ------------------------------------------------------------------------
@@ -220,7 +233,6 @@ struct WorkView {
   int *cnt;          // split-K arrival counters, one per tile (a fixed 4 KB at the start)
   long long *part;   // split-K partial sums
   int8_t *bcodes;    // [kPlanes][n_cols_pad][kp]: plane k holds the codes of blocks with s >= k
-  int32_t *ptab;     // [nb][n_cols_pad] s = e − emin_c (0 for a zero scale or a checked column)
   int32_t *emin;     // [n_cols_pad]
   uint32_t *route;   // [n_cols_pad]
   int32_t *fb;       // [0] count, [1] CTAs done, [2..] checked-route columns
@@ -258,8 +270,6 @@ static WorkView work_view(void *base, size_t n_cols, int nb, size_t kp, size_t t
   p += np * 4;
   w.emin = reinterpret_cast<int32_t *>(p);
   p += np * 4;
-  w.ptab = reinterpret_cast<int32_t *>(p);
-  p += (size_t)nb * np * 4;
   w.bcodes =
       reinterpret_cast<int8_t *>((reinterpret_cast<uintptr_t>(p) + 255) & ~(uintptr_t)255);
   p = reinterpret_cast<uint8_t *>(w.bcodes) + kPlanes * np * kp;
@@ -279,8 +289,9 @@ size_t gemm_work_bytes(size_t n_cols, size_t n_in, size_t n_out, int sm_count) {
   const size_t np = cols_pad(n_cols);
   const size_t tiles = gemm_tiles(n_out, n_cols);
   const int ks = gemm_ksplit(tiles, (int)(kp / kSlab), sm_count);
-  return kCntBytes + gemm_work_head_bytes(n_cols) + 2 * np * 4 + nb * np * 4 + 256 +
-         kPlanes * np * kp + 256 + part_bytes(tiles, ks);
+  (void)nb;
+  return kCntBytes + gemm_work_head_bytes(n_cols) + 2 * np * 4 + 256 + kPlanes * np * kp + 256 +
+         part_bytes(tiles, ks);
 }
 
 // ---- activation prep: describe, route, B operand, P table -----------------------------------
@@ -301,7 +312,6 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(PrepArgs a) {
   const int c = blockIdx.x;
   const size_t np = cols_pad((size_t)a.n_cols);
   if (c >= a.n_cols) {  // padding tokens of the last tile: no shift, zero planes
-    for (int b = threadIdx.x; b < a.nb; b += blockDim.x) a.w.ptab[(size_t)b * np + c] = 0;
     for (size_t j = (size_t)threadIdx.x * 16; j < a.kp; j += (size_t)blockDim.x * 16)
       for (int k = 0; k < kPlanes; k++)
         *reinterpret_cast<uint4 *>(a.w.bcodes + (k * np + c) * a.kp + j) = make_uint4(0, 0, 0, 0);
@@ -325,7 +335,6 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(PrepArgs a) {
   }
   __syncthreads();
   if (s_status != APX_OK) {  // refused by the quantizer: its codes and exponents are not set
-    for (int b = threadIdx.x; b < a.nb; b += blockDim.x) a.w.ptab[(size_t)b * np + c] = 0;
     for (size_t j = (size_t)threadIdx.x * 16; j < a.kp; j += (size_t)blockDim.x * 16)
       for (int k = 0; k < kPlanes; k++)
         *reinterpret_cast<uint4 *>(a.w.bcodes + (k * np + c) * a.kp + j) = make_uint4(0, 0, 0, 0);
@@ -380,15 +389,14 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(PrepArgs a) {
     s_emin = emin;
     s_route = route;
     a.w.emin[c] = emin;
-    a.w.route[c] = route;
+    // a GEMM column also carries its exponent spread (0..kMaxShift): the tile's largest bounds
+    // every block's shift, so it sets the planes and MMAs per block
+    a.w.route[c] = route | (route == kRouteGemm && s_emax >= 0 ? (unsigned)(s_emax - emin) : 0u)
+                               << 8;
   }
   __syncthreads();
   const bool gemm = s_route == kRouteGemm;
   const int emin = s_emin;
-  for (int b = threadIdx.x; b < a.nb; b += blockDim.x) {
-    const unsigned e = exps[b];
-    a.w.ptab[(size_t)b * np + c] = gemm && e != APX_EXP_ZERO ? (int)(e - emin) : 0;
-  }
   // B planes of the column: x, x[s >= 1], x[s >= 2] (x: the codes, zero for zero-scale
   // blocks and past n_in), so that x + x[s >= 1] + 2·x[s >= 2] = x·2^s
   const size_t plane = np * a.kp;
@@ -488,6 +496,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // per token of the tile: the finish shift emin_c, or -1 where the token is not the GEMM's
   int *stok = smax + kStages * 4;
   int *sflag = stok + kTileN;  // split K: this CTA is the tile's last split
+  // per token of the tile: its exponent spread (the largest shift of any of its blocks)
+  int *sspread = sflag + 4;
   auto stage_a = [&](int st) { return smem + st * kStageBytes; };
   auto stage_m = [&](int st) {
     return reinterpret_cast<const int32_t *>(smem + st * kStageBytes + kStageA +
@@ -521,8 +531,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (threadIdx.x >= 64 && threadIdx.x < 64 + kTileN) {
     const int c = n0 + (int)threadIdx.x - 64;
-    stok[threadIdx.x - 64] =
-        c < g.n_cols && g.w.route[c] == kRouteGemm ? g.w.emin[c] : -1;
+    const unsigned rw = c < g.n_cols ? g.w.route[c] : kRouteNone;
+    const bool gemm_col = (rw & 0xFFu) == kRouteGemm;
+    stok[threadIdx.x - 64] = gemm_col ? g.w.emin[c] : -1;
+    sspread[threadIdx.x - 64] = gemm_col ? (int)(rw >> 8) : 0;
   }
   if (warp == 1) {  // TMEM: kBufs × kBufCols columns of 32-bit accumulators
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -537,30 +549,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ---- TMA producer (the whole warp reads the stage's shifts, lane 0 issues).  The
-    // shifts of stage kt+1 are loaded while the warp waits for stage kt's slot ----
+    // ---- TMA producer (lane 0 issues).  Every block's shift is at most the tile's largest
+    // exponent spread, read once here: planes and MMAs per block follow it ----
     int issued = 0;
-    auto load_shifts = [&](int kt, int (&v)[4]) {
-#pragma unroll
-      for (int q = 0; q < 4; q++) {
-        const int b = 4 * kt + q;
-        v[q] = 0;
-        if (b < g.nb) {
-          const int32_t *r = g.w.ptab + (size_t)b * np + n0;
-          v[q] = max(r[lane], r[32 + lane]);
-        }
-      }
-    };
-    int cur[4], nxt[4];
-    load_shifts(kt0, cur);
+    const int tile_smax = min(kMaxShift, __reduce_max_sync(0xFFFFFFFFu,
+                                                           max(sspread[lane], sspread[32 + lane])));
     for (int lk = 0; lk < nk; lk++) {
       const int kt = kt0 + lk, st = lk % kStages, use = lk / kStages;
-      if (lk + 1 < nk) load_shifts(kt + 1, nxt);
-      // the largest shift of each block over the tile's 64 tokens: planes and MMAs per block
       int sq[4], smax_stage = 0;
 #pragma unroll
       for (int q = 0; q < 4; q++) {
-        sq[q] = __reduce_max_sync(0xFFFFFFFFu, cur[q]);
+        sq[q] = 4 * kt + q < g.nb ? tile_smax : 0;
         smax_stage = max(smax_stage, sq[q]);
       }
       int stop = 0;
@@ -584,8 +583,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (__shfl_sync(0xFFFFFFFFu, stop, 0)) break;
-#pragma unroll
-      for (int q = 0; q < 4; q++) cur[q] = nxt[q];
     }
     // every copy this thread started has landed before the CTA may exit
     if (lane == 0)
@@ -642,6 +639,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     long long acc[kEpiTok];
 #pragma unroll
     for (int j = 0; j < kEpiTok; j++) acc[j] = 0;
+    // the row's finish exponent, fetched now so the finish does not wait for it
+    const unsigned kmin_row = row < g.m_pad ? (unsigned)__ldg(g.kmin + row) : 0u;
     bool ok = true;
     for (int lk = 0; lk < nk; lk++) {
       const int kt = kt0 + lk, st = lk % kStages, buf = lk % kBufs;
@@ -709,19 +708,55 @@ __global__ void __launch_bounds__(kThreads, 1)
     float *sf = reinterpret_cast<float *>(smem);                      // [64 tokens][128 rows]
     long long *sv = reinterpret_cast<long long *>(smem + 32 * 1024);  // [64 tokens][128 rows]
     if (all_ok) {
-      // 32 independent chains side by side (the conversions are long-latency)
-      const unsigned kmin = (unsigned)g.kmin[row];
+      // 32 independent chains side by side (the conversions are long-latency).  The tokens'
+      // exponents are read up front: read inside the loop, each would wait for the previous
+      // iteration's shared-memory stores.
+      const unsigned kmin = kmin_row;
       const bool live = row < g.n_out;
       uint32_t bad = 0;  // bit j: token j's output leaves i64
+      int ev[kEpiTok];
 #pragma unroll
-      for (int j = 0; j < kEpiTok; j++) {
-        const int e = stok[c0 + j];
-        long long v;
-        float f;
-        const bool fits = finish_fast(acc[j], kmin + (unsigned)e, v, f);
-        sf[(c0 + j) * kTileM + rl] = fits ? f : __int_as_float(0x7FC00000);
-        if (g.out_q32) sv[(c0 + j) * kTileM + rl] = fits ? v : 0;
-        bad |= (e >= 0 && live && !fits) ? 1u << j : 0u;
+      for (int j = 0; j < kEpiTok; j += 4) {
+        const int4 e4 = *reinterpret_cast<const int4 *>(stok + c0 + j);
+        ev[j] = e4.x;
+        ev[j + 1] = e4.y;
+        ev[j + 2] = e4.z;
+        ev[j + 3] = e4.w;
+      }
+      // Tokens off the GEMM route (e < 0) are never stored.  When every other token's shift
+      // kmin + e lies in [32, 64), the loop below has no call in it (the general case is out of
+      // line, and a call site would keep the 32 chains from interleaving).
+      int emn = 1 << 20, emx = -1;
+#pragma unroll
+      for (int j = 0; j < kEpiTok; j++)
+        if (ev[j] >= 0) {
+          emn = min(emn, ev[j]);
+          emx = max(emx, ev[j]);
+        }
+      if (emx < 0 || ((int)kmin + emn >= 32 && (int)kmin + emx < 64)) {
+#pragma unroll
+        for (int j = 0; j < kEpiTok; j++) {
+          const int e = ev[j];
+          const unsigned t = kmin + (unsigned)e - 32u;  // in [0, 32) for e >= 0
+          const int hi = (int)(acc[j] >> 32);
+          const long long v = (long long)((unsigned long long)acc[j] << (t & 31));
+          const float f = __ll2float_rn(acc[j]) * __int_as_float((int)(t + 95) << 23);
+          const bool fits = e < 0 || (hi >> (31 - (t & 31))) == (hi >> 31);
+          sf[(c0 + j) * kTileM + rl] = e >= 0 && fits ? f : __int_as_float(0x7FC00000);
+          if (g.out_q32) sv[(c0 + j) * kTileM + rl] = e >= 0 && fits ? v : 0;
+          bad |= (e >= 0 && live && !fits) ? 1u << j : 0u;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < kEpiTok; j++) {
+          const int e = ev[j];
+          long long v;
+          float f;
+          const bool fits = finish_fast(acc[j], kmin + (unsigned)e, v, f);
+          sf[(c0 + j) * kTileM + rl] = fits ? f : __int_as_float(0x7FC00000);
+          if (g.out_q32) sv[(c0 + j) * kTileM + rl] = fits ? v : 0;
+          bad |= (e >= 0 && live && !fits) ? 1u << j : 0u;
+        }
       }
       while (bad) {  // output overflow: rare, one refusal per token
         const int j = __ffs(bad) - 1;
@@ -941,7 +976,7 @@ void free_gemm_layout(GemmLayout *lay) {
 
 static size_t gemm_smem_bytes() {
   return 1024 + (size_t)kStages * kStageBytes + (2 * kStages + 2 * kBufs + 1) * 8 + 32 +
-         kStages * 4 * 4 + kTileN * 4 + 16;
+         kStages * 4 * 4 + kTileN * 4 + 16 + kTileN * 4;
 }
 
 bool gemm_shape_ok(size_t n_in) { return n_in && (n_in + 31) / 32 <= (size_t)kMaxBlocks; }
