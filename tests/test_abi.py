@@ -41,3 +41,28 @@ def test_library_loads_without_a_device(libpath):
     assert lib.apx_version().startswith(b"apeiron_b200")
     assert lib.apx_act_padded_len(896) == 1024
     assert lib.apx_act_padded_len(0) == 0
+
+
+def test_gather_desc_layout_matches_header(tmp_path):
+    """The ctypes mirror of apx_gather_desc has the C struct's size and field offsets (the
+    descriptor crosses the ABI by pointer, field for field)."""
+    import ctypes as C
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    fields = [f for f, _ in _abi.GatherDesc._fields_]
+    src = tmp_path / "probe.c"
+    src.write_text("#include <stddef.h>\n#include <stdio.h>\n#include \"apeiron_cuda.h\"\n"
+                   "int main(void) {\n  printf(\"%zu\\n\", sizeof(apx_gather_desc));\n" +
+                   "".join(f"  printf(\"%zu\\n\", offsetof(apx_gather_desc, {f}));\n"
+                           for f in fields) + "  return 0;\n}\n")
+    exe = tmp_path / "probe"
+    inc = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
+    subprocess.run([cc, "-I", inc, str(src), "-o", str(exe)], check=True)
+    out = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True,
+                                          check=True).stdout.split()]
+    assert out[0] == C.sizeof(_abi.GatherDesc)
+    assert out[1:] == [getattr(_abi.GatherDesc, f).offset for f in fields]
