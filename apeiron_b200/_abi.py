@@ -38,7 +38,7 @@ EXPORTS = [
     "apx_tensor_device_bytes", "apx_matvec_q8act", "apx_matvec_q8act_chunked",
     "apx_matmat_q8act", "apx_quant_act", "apx_matvec_f32", "apx_debug_block_dots",
     "apx_act_describe_async", "apx_quant_q32_async", "apx_quant_f32_async",
-    "apx_matvec_async", "apx_matmat_async", "apx_act_padded_len", "apx_status_decode",
+    "apx_matvec_async", "apx_matmat_async", "apx_matmat_f32_async", "apx_act_padded_len", "apx_status_decode",
     "apx_matvec_f32_noalloc", "apx_matmat_f32", "apx_quant_f32_cols_async",
     "apx_peer_alloc", "apx_peer_open", "apx_peer_close", "apx_device_read",
     "apx_gather_publish_async", "apx_matvec_gather_async", "apx_matvec_group_async",
@@ -121,6 +121,7 @@ _SIGS = {
                                           C.c_int, P]),
     "apx_matvec_group_async": (C.c_int, [P, P, C.c_int, SZ, P, P, P, P, P, P, P]),
     "apx_matmat_async": (C.c_int, [P, U64, SZ, SZ, SZ, P, P, P, P, P, P, P]),
+    "apx_matmat_f32_async": (C.c_int, [P, U64, SZ, SZ, SZ, P, SZ, P, P, P, P]),
     "apx_act_padded_len": (SZ, [SZ]),
     "apx_status_decode": (C.c_int, [P, U64, C.POINTER(CallStatus), EP]),
     "apx_matvec_f32_noalloc": (C.c_int, [P, U64, SZ, SZ, P, P, P, P]),

@@ -49,6 +49,7 @@
 #include "apx_common.cuh"
 #include "apx_kernels.h"
 #include "apx_pack.cuh"
+#include "apx_quant.cuh"
 
 namespace apx {
 
@@ -236,6 +237,8 @@ struct WorkView {
   int32_t *emin;     // [n_cols_pad]
   uint32_t *route;   // [n_cols_pad]
   int32_t *fb;       // [0] count, [1] CTAs done, [2..] checked-route columns
+  int8_t *qcodes;    // f32 path: the checked columns' codes [n_cols_pad][kp]
+  uint8_t *qexps;    // and exponent bytes [n_cols_pad][kp / 32]
 };
 
 static __host__ __device__ size_t cols_pad(size_t n_cols) {
@@ -273,6 +276,10 @@ static WorkView work_view(void *base, size_t n_cols, int nb, size_t kp, size_t t
   w.bcodes =
       reinterpret_cast<int8_t *>((reinterpret_cast<uintptr_t>(p) + 255) & ~(uintptr_t)255);
   p = reinterpret_cast<uint8_t *>(w.bcodes) + kPlanes * np * kp;
+  w.qcodes = reinterpret_cast<int8_t *>(p);
+  p += np * kp;
+  w.qexps = p;
+  p += np * (kp / 32);
   w.part = ksplit > 1 ? reinterpret_cast<long long *>(
                             (reinterpret_cast<uintptr_t>(p) + 255) & ~(uintptr_t)255)
                       : nullptr;
@@ -290,8 +297,8 @@ size_t gemm_work_bytes(size_t n_cols, size_t n_in, size_t n_out, int sm_count) {
   const size_t tiles = gemm_tiles(n_out, n_cols);
   const int ks = gemm_ksplit(tiles, (int)(kp / kSlab), sm_count);
   (void)nb;
-  return kCntBytes + gemm_work_head_bytes(n_cols) + 2 * np * 4 + 256 + kPlanes * np * kp + 256 +
-         part_bytes(tiles, ks);
+  return kCntBytes + gemm_work_head_bytes(n_cols) + 2 * np * 4 + 256 + kPlanes * np * kp +
+         np * kp + np * (kp / 32) + 256 + part_bytes(tiles, ks);
 }
 
 // ---- activation prep: describe, route, B operand, P table -----------------------------------
@@ -414,6 +421,157 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(PrepArgs a) {
         memcpy(&v, t, 16);
       }
     }
+    const uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int k = 0; k < kPlanes; k++)
+      *reinterpret_cast<uint4 *>(dst + k * plane + j) = sh >= k ? v : z;
+  }
+}
+
+// ---- fused quantize-and-prep of f32 columns (the prefill's f32 boundary) ------------------
+//
+// One CTA per column: f32_to_fixed + quant_act of the column into shared memory (the same
+// per-block arithmetic as the column quantizer, apx_quant.cuh), its descriptor, route and
+// planes, in one pass over the f32 input.  Codes and exponent bytes leave shared memory only
+// for a column the checked rows take.
+
+struct QPrepArgs {
+  const float *x;  // column c at x + c·ldx (16-byte aligned, ldx a multiple of 4)
+  size_t ldx, n_in, kp;
+  int nb, n_cols;
+  WorkView w;
+  unsigned long long *status;  // column c's refusal word at status[c·2]
+};
+
+constexpr int kQPrepChunks = 4;      // 128-lane chunks in flight per warp
+constexpr size_t kQPrepMaxIn = 16384;  // the column staged in shared memory
+
+__global__ void __launch_bounds__(256) gemm_quant_prep_kernel(QPrepArgs a) {
+  extern __shared__ __align__(16) uint8_t qsm[];
+  int8_t *scodes = reinterpret_cast<int8_t *>(qsm);  // kp bytes
+  uint8_t *sexps = qsm + a.kp;                        // kp / 32 bytes
+  __shared__ int s_emin, s_emax, s_status;
+  __shared__ unsigned s_route;
+  const int c = blockIdx.x;
+  const size_t np = cols_pad((size_t)a.n_cols);
+  if (c >= a.n_cols) {  // padding tokens of the last tile: no shift, zero planes
+    for (size_t j = (size_t)threadIdx.x * 16; j < a.kp; j += (size_t)blockDim.x * 16)
+      for (int k = 0; k < kPlanes; k++)
+        *reinterpret_cast<uint4 *>(a.w.bcodes + (k * np + c) * a.kp + j) = make_uint4(0, 0, 0, 0);
+    if (threadIdx.x == 0) {
+      a.w.emin[c] = 0;
+      a.w.route[c] = kRouteNone;
+    }
+    return;
+  }
+  if (threadIdx.x == 0) {
+    s_emin = 1 << 30;
+    s_emax = -1;
+    s_status = APX_OK;
+  }
+  __syncthreads();
+  const float *x = a.x + (size_t)c * a.ldx;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = blockDim.x / 32;
+  const size_t chunks = a.kp / 128;  // lanes past n_in read as zero: zero codes
+  int w_emin = 1 << 30, w_emax = -1, w_status = APX_OK;
+  for (size_t round = 0; round * nw * kQPrepChunks < chunks; round++) {
+    float4 f4[kQPrepChunks];
+#pragma unroll
+    for (int u = 0; u < kQPrepChunks; u++) {
+      const size_t j = ((round * kQPrepChunks + u) * nw + warp) * 128 + 4 * lane;
+      f4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (j + 4 <= a.n_in) {
+        f4[u] = __ldg(reinterpret_cast<const float4 *>(x + j));
+      } else if (j < a.n_in) {
+        f4[u].x = x[j];
+        if (j + 1 < a.n_in) f4[u].y = x[j + 1];
+        if (j + 2 < a.n_in) f4[u].z = x[j + 2];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kQPrepChunks; u++) {
+      const size_t cbase = ((round * kQPrepChunks + u) * nw + warp) * 128;
+      if (cbase >= a.kp) break;  // warp-uniform
+      const size_t j = cbase + 4 * lane;
+      uint32_t packed;
+      int e;
+      bool ok;
+      quant_quad(f4[u], packed, e, ok);
+      *reinterpret_cast<uint32_t *>(scodes + j) = ok ? packed : 0u;
+      if ((lane & 7) == 0 && j < a.n_in) {  // the block's leader
+        if (!ok) {
+          w_status = max(w_status, (int)APX_ERR_QUANT_REFUSED);
+        } else {
+          sexps[j / 32] = e < 0 ? (uint8_t)APX_EXP_ZERO : (uint8_t)e;
+          if (e >= 0) {
+            w_emin = min(w_emin, e);
+            w_emax = max(w_emax, e);
+          }
+        }
+      } else if ((lane & 7) == 0 && j / 32 < a.kp / 32) {
+        sexps[j / 32] = (uint8_t)APX_EXP_ZERO;  // a block wholly past n_in
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    w_emin = min(w_emin, __shfl_xor_sync(0xFFFFFFFFu, w_emin, o));
+    w_emax = max(w_emax, __shfl_xor_sync(0xFFFFFFFFu, w_emax, o));
+    w_status = max(w_status, __shfl_xor_sync(0xFFFFFFFFu, w_status, o));
+  }
+  if (lane == 0) {
+    if (w_status != APX_OK) atomicMax(&s_status, w_status);
+    if (w_emax >= 0) {
+      atomicMin(&s_emin, w_emin);
+      atomicMax(&s_emax, w_emax);
+    }
+  }
+  __syncthreads();
+  if (s_status != APX_OK) {  // quant_act returned None for the column
+    for (size_t j = (size_t)threadIdx.x * 16; j < a.kp; j += (size_t)blockDim.x * 16)
+      for (int k = 0; k < kPlanes; k++)
+        *reinterpret_cast<uint4 *>(a.w.bcodes + (k * np + c) * a.kp + j) = make_uint4(0, 0, 0, 0);
+    if (threadIdx.x == 0) {
+      atomicMin(a.status + (size_t)c * 2, pack_status(0, (unsigned)s_status, 0));
+      a.w.emin[c] = 0;
+      a.w.route[c] = kRouteNone;
+    }
+    return;
+  }
+  if (threadIdx.x == 0) {  // the route, as gemm_prep_kernel decides it (no code is -128 here)
+    const int emin = s_emax >= 0 ? s_emin : 0;
+    unsigned route;
+    if (bound_ok((long long)a.n_in, Fam<kQ8_0>::top, s_emax) &&
+        (s_emax < 0 || s_emax - emin <= kMaxShift)) {
+      route = kRouteGemm;
+    } else {
+      route = kRouteChecked;
+      const int slot = atomicAdd(a.w.fb, 1);
+      a.w.fb[2 + slot] = c;
+    }
+    s_emin = emin;
+    s_route = route;
+    a.w.emin[c] = emin;
+    a.w.route[c] = route | (route == kRouteGemm && s_emax >= 0 ? (unsigned)(s_emax - emin) : 0u)
+                               << 8;
+  }
+  __syncthreads();
+  const bool gemm = s_route == kRouteGemm;
+  const int emin = s_emin;
+  if (!gemm) {  // the checked rows read the column from global memory
+    for (size_t j = (size_t)threadIdx.x * 16; j < a.kp; j += (size_t)blockDim.x * 16)
+      *reinterpret_cast<uint4 *>(a.w.qcodes + (size_t)c * a.kp + j) =
+          *reinterpret_cast<const uint4 *>(scodes + j);
+    for (size_t b = threadIdx.x; b < a.kp / 32; b += blockDim.x)
+      a.w.qexps[(size_t)c * (a.kp / 32) + b] = sexps[b];
+  }
+  // planes x, x[s >= 1], x[s >= 2] (zero codes for zero blocks and past n_in already)
+  const size_t plane = np * a.kp;
+  int8_t *dst = a.w.bcodes + (size_t)c * a.kp;
+  for (size_t j = (size_t)threadIdx.x * 16; j < a.kp; j += (size_t)blockDim.x * 16) {
+    const unsigned e = sexps[j / 32];
+    const uint4 v = gemm ? *reinterpret_cast<const uint4 *>(scodes + j) : make_uint4(0, 0, 0, 0);
+    const int sh = gemm && e != APX_EXP_ZERO ? (int)e - emin : 0;
     const uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
     for (int k = 0; k < kPlanes; k++)
@@ -989,6 +1147,13 @@ bool gemm_supported(const GemmLayout &lay) {
          lay.kspread <= 30 - lg;
 }
 
+static cudaError_t launch_gemm_main(const GemvPlan &pl, const uint8_t *pack,
+                                    const GemmLayout &lay, size_t n_out, size_t n_in,
+                                    size_t n_cols, const int8_t *codes, size_t ld,
+                                    const uint8_t *exps, size_t ldb, const WorkView &w,
+                                    int ksplit, long long *out_q32, float *out_f32,
+                                    unsigned long long *status, cudaStream_t stream);
+
 cudaError_t launch_gemm_q8_0(const GemvPlan &pl, const uint8_t *pack, const GemmLayout &lay,
                              size_t n_out, size_t n_in, size_t n_cols, const int8_t *codes,
                              size_t ld, const uint8_t *exps, size_t ldb, const void *descs,
@@ -1013,7 +1178,18 @@ cudaError_t launch_gemm_q8_0(const GemvPlan &pl, const uint8_t *pack, const Gemm
   gemm_prep_kernel<<<(unsigned)cols_pad(n_cols), 256, 0, stream>>>(pa);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
+  return launch_gemm_main(pl, pack, lay, n_out, n_in, n_cols, codes, ld, exps, ldb, w, ksplit,
+                          out_q32, out_f32, status, stream);
+}
 
+// The GEMM launch after a prep: planes, routes and the checked-column list in `w`.
+static cudaError_t launch_gemm_main(const GemvPlan &pl, const uint8_t *pack,
+                                    const GemmLayout &lay, size_t n_out, size_t n_in,
+                                    size_t n_cols, const int8_t *codes, size_t ld,
+                                    const uint8_t *exps, size_t ldb, const WorkView &w,
+                                    int ksplit, long long *out_q32, float *out_f32,
+                                    unsigned long long *status, cudaStream_t stream) {
+  cudaError_t e;
   CUtensorMap map_x;
   if (!make_map(&map_x, w.bcodes, lay.kp, kPlanes * cols_pad(n_cols), lay.kp, kTileN))
     return cudaErrorInvalidValue;
@@ -1048,6 +1224,37 @@ cudaError_t launch_gemm_q8_0(const GemvPlan &pl, const uint8_t *pack, const Gemm
       *reinterpret_cast<const CUtensorMap *>(lay.map), map_x,
       *reinterpret_cast<const CUtensorMap *>(lay.map_m), a);
   return cudaGetLastError();
+}
+
+bool gemm_f32_ok(size_t n_in, const float *x, size_t ldx) {
+  const size_t kp = (n_in + kSlab - 1) / kSlab * kSlab;
+  return kp <= kQPrepMaxIn && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && ldx % 4 == 0;
+}
+
+cudaError_t launch_gemm_q8_0_f32(const GemvPlan &pl, const uint8_t *pack, const GemmLayout &lay,
+                                 size_t n_out, size_t n_in, size_t n_cols, const float *x,
+                                 size_t ldx, void *work, long long *out_q32, float *out_f32,
+                                 unsigned long long *status, int sm_count, cudaStream_t stream) {
+  if (n_cols == 0 || n_out == 0) return cudaSuccess;
+  if (!gemm_f32_ok(n_in, x, ldx)) return cudaErrorInvalidValue;
+  const size_t tiles = gemm_tiles(n_out, n_cols);
+  const int ksplit = gemm_ksplit(tiles, (int)(lay.kp / kSlab), sm_count);
+  const WorkView w = work_view(work, n_cols, lay.nb, lay.kp, tiles, ksplit);
+  QPrepArgs qa;
+  qa.x = x;
+  qa.ldx = ldx;
+  qa.n_in = n_in;
+  qa.kp = lay.kp;
+  qa.nb = lay.nb;
+  qa.n_cols = (int)n_cols;
+  qa.w = w;
+  qa.status = status;
+  const size_t smem = lay.kp + lay.kp / 32;
+  gemm_quant_prep_kernel<<<(unsigned)cols_pad(n_cols), 256, smem, stream>>>(qa);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  return launch_gemm_main(pl, pack, lay, n_out, n_in, n_cols, w.qcodes, lay.kp, w.qexps,
+                          lay.kp / 32, w, ksplit, out_q32, out_f32, status, stream);
 }
 
 }  // namespace apx

@@ -108,6 +108,14 @@ cudaError_t launch_gemm_q8_0(const GemvPlan &pl, const uint8_t *pack, const Gemm
                              size_t ld, const uint8_t *exps, size_t ldb, const void *descs,
                              void *work, long long *out_q32, float *out_f32,
                              unsigned long long *status, int sm_count, cudaStream_t stream);
+// The fused f32 prefill: f32_to_fixed + quant_act of every column and the GEMM's prep in one
+// kernel, then the GEMM.  gemm_f32_ok: the width and the input's alignment allow it.
+bool gemm_f32_ok(size_t n_in, const float *x, size_t ldx);
+cudaError_t launch_gemm_q8_0_f32(const GemvPlan &pl, const uint8_t *pack, const GemmLayout &lay,
+                                 size_t n_out, size_t n_in, size_t n_cols, const float *x,
+                                 size_t ldx, void *work, long long *out_q32, float *out_f32,
+                                 unsigned long long *status, int sm_count, cudaStream_t stream);
+
 
 // Debug: exact int32 group dots from the repacked layout (apx_gemv.cu).
 cudaError_t launch_block_dots(const GemvPlan &pl, uint32_t type, const uint8_t *pack,

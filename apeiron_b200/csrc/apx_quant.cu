@@ -11,31 +11,9 @@
 // kernel that follows on the same stream reads it.
 #include "apx_common.cuh"
 #include "apx_kernels.h"
+#include "apx_quant.cuh"
 
 namespace apx {
-
-__device__ __forceinline__ unsigned long long uabs64(long long v) {
-  return v < 0 ? 0ull - (unsigned long long)v : (unsigned long long)v;
-}
-
-// act_scale exponent, or -1 for a zero block, or 99 when the reference returns None: the
-// smallest e >= 0 with 127·2^e >= absmax (pow2.rs:22-39).  With bl the bit length of absmax
-// and e0 = max(0, bl − 7), 127·2^(e0−1) < 2^(bl−1) <= absmax, so e is e0 or e0 + 1; 127·2^e0
-// stays below 2^64 for every absmax <= 2^63.  No division.
-__device__ __forceinline__ int act_scale_exp(unsigned long long absmax) {
-  if (absmax == 0) return -1;
-  const int bl = 64 - __clzll((long long)absmax);
-  const int e0 = bl > 7 ? bl - 7 : 0;
-  const int e = (127ull << e0) >= absmax ? e0 : e0 + 1;
-  return e > 62 ? 99 : e;
-}
-
-// S·code fits i64 for S = 2^e (QuantAct::dequant's checked product).
-__device__ __forceinline__ bool product_fits(int code, int e) {
-  if (e <= 56) return true;  // 128·2^56 = 2^63: every int8 code fits except -128·2^56 = i64::MIN
-  long long lim = 1ll << (63 - e);
-  return code >= -lim && code <= lim - 1;
-}
 
 struct DescAcc {
   int emin, emax, status;
@@ -100,43 +78,6 @@ __global__ void describe_kernel(const int8_t *codes, const uint8_t *exps, size_t
   __syncthreads();
   // an invalid exponent byte outranks the overflow refusal: report it as such
   desc_write(&acc, desc + col, n);
-}
-
-// F32::to_q32 (src/engine/num/fp.rs:186-230): round(v·2^32), ties away from zero.
-__device__ __forceinline__ bool f32_to_q32(float f, long long &out) {
-  unsigned bits = __float_as_uint(f);
-  unsigned e = (bits >> 23) & 0xFFu;
-  if (e == 0xFFu) return false;
-  unsigned frac = bits & 0x007FFFFFu;
-  unsigned long long m = e == 0 ? frac : (frac | 0x00800000u);
-  bool neg = (bits & 0x80000000u) != 0;
-  unsigned ee = e == 0 ? 1 : e;
-  unsigned long long mag;
-  if (ee >= 118) {
-    unsigned k = ee - 118;
-    if (k > 40) return false;
-    if (k >= 40 && m >= (1ull << 23)) {
-      // m·2^k >= 2^63: the positive side refuses, the negative side only at exactly 2^63
-      if (neg && m == (1ull << 23)) {
-        out = (long long)(1ull << 63);
-        return true;
-      }
-      return false;
-    }
-    mag = m << k;
-  } else {
-    unsigned sh = 118 - ee;
-    mag = sh > 24 ? 0ull : (m + (1ull << (sh - 1))) >> sh;
-  }
-  const unsigned long long lim = 1ull << 63;
-  if (neg) {
-    if (mag > lim) return false;
-    out = mag == lim ? (long long)lim : -(long long)mag;
-    return true;
-  }
-  if (mag >= lim) return false;
-  out = (long long)mag;
-  return true;
 }
 
 // One CTA per activation vector: vector c reads x at c·ldx elements and writes its codes at
@@ -222,39 +163,6 @@ __global__ void quant_kernel(const void *xin, size_t n, size_t ldx, int8_t *code
   desc_write(&acc, desc, n);
 }
 
-// Round-half-up right shift of a value below 2^25 (0 for shifts past its bit length).
-__device__ __forceinline__ unsigned rshift_round(unsigned x, unsigned s) {
-  return s == 0 ? x : s > 25 ? 0u : (x + (1u << (s - 1))) >> s;
-}
-
-// Largest |f| bit pattern the 32-bit route takes: 127·2^24.  Below it every lane converts,
-// act_scale gives e <= 56 and every code times 2^e fits i64, so nothing refuses.
-constexpr unsigned kFastAbsMax = 0x4EFE0000u;
-
-// act_scale exponent of a block whose largest |f| has bit pattern A <= kFastAbsMax, from the
-// f32 fields: with M the 24-bit significand and E the biased exponent, round(A·2^32) is
-// M·2^(E−118) for E >= 118 (bit length E − 94, so e = E − 101 or one more when M > 127·2^17),
-// and below that a value under 2^25 formed by one rounding shift.
-__device__ __forceinline__ int fast_scale_exp(unsigned A) {
-  const unsigned E = A >> 23, M = (A & 0x7FFFFFu) | (E ? 0x800000u : 0u);
-  if (E >= 118) return (int)E - 101 + (M > 0xFE0000u ? 1 : 0);
-  const unsigned vm = rshift_round(M, 118 - (E ? E : 1));
-  if (vm == 0) return -1;
-  const int bl = 32 - __clz((int)vm);
-  const int e0 = bl > 7 ? bl - 7 : 0;
-  return (127u << e0) >= vm ? e0 : e0 + 1;
-}
-
-// Code of one lane (f32 bits) under block exponent e >= 0: round(|f|·2^32) then round by 2^e,
-// ties away from zero both times.  Where round(|f|·2^32) is exact (E >= 118) the two
-// roundings are one shift of the significand.
-__device__ __forceinline__ int fast_code(unsigned bits, int e) {
-  const unsigned b = bits & 0x7FFFFFFFu, E = b >> 23, M = (b & 0x7FFFFFu) | (E ? 0x800000u : 0u);
-  const unsigned mag = E >= 118 ? rshift_round(M, (unsigned)e + 118 - E)
-                                : rshift_round(rshift_round(M, 118 - (E ? E : 1)), (unsigned)e);
-  return (bits >> 31) ? -(int)mag : (int)mag;
-}
-
 // f32 vectors, bandwidth-shaped: a warp takes 128 lanes (4 blocks) per chunk, each thread 4
 // consecutive lanes (one 16-byte load, one 4-byte store of codes), with kQuantChunks chunks'
 // loads in flight per thread.  The block absmax reduces over its 8 threads on the f32 bit
@@ -298,56 +206,10 @@ __global__ void __launch_bounds__(256) quant_f32_vec_kernel(const float *x, size
       const size_t cbase = ((round * kQuantChunks + u) * nw + warp) * 128;
       if (cbase >= n) break;  // warp-uniform
       const size_t j = cbase + 4 * lane;
-      const unsigned bits[4] = {__float_as_uint(f4[u].x), __float_as_uint(f4[u].y),
-                                __float_as_uint(f4[u].z), __float_as_uint(f4[u].w)};
-      unsigned amax = 0;
-#pragma unroll
-      for (int k = 0; k < 4; k++) amax = max(amax, bits[k] & 0x7FFFFFFFu);
-#pragma unroll
-      for (int o = 4; o > 0; o >>= 1) amax = max(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
-      int e = -1;
-      uint32_t packed = 0;
-      bool blk_ok = true;
-      if (__all_sync(0xFFFFFFFFu, amax <= kFastAbsMax)) {
-        e = fast_scale_exp(amax);
-        if (e >= 0) {
-#pragma unroll
-          for (int k = 0; k < 4; k++)
-            packed |= ((uint32_t)(uint8_t)(int8_t)fast_code(bits[k], e)) << (8 * k);
-        }
-      } else {
-        // Q32.32 route (f32_to_q32, act_scale, checked product) for every lane of the warp
-        long long v[4];
-        bool ok = true;
-#pragma unroll
-        for (int k = 0; k < 4; k++) ok &= f32_to_q32(__uint_as_float(bits[k]), v[k]);
-#pragma unroll
-        for (int o = 4; o > 0; o >>= 1) ok &= __shfl_xor_sync(0xFFFFFFFFu, (int)ok, o) != 0;
-        blk_ok = ok;
-        if (blk_ok) {
-          long long vm;
-          const unsigned long long mx =
-              f32_to_q32(__uint_as_float(amax), vm) ? (unsigned long long)vm : 1ull << 63;
-          e = act_scale_exp(mx);
-          if (e == 99) blk_ok = false;
-        }
-        bool bad = false;
-        if (blk_ok && e >= 0) {
-#pragma unroll
-          for (int k = 0; k < 4; k++) {
-            const unsigned long long m = uabs64(v[k]);
-            const unsigned long long S = 1ull << e, q = m >> e, r = m & (S - 1);
-            const unsigned long long mag = q + (2 * r >= S ? 1ull : 0ull);
-            const int code = v[k] < 0 ? -(int)mag : (int)mag;
-            bad |= mag > 127 || !product_fits(code, e);
-            packed |= ((uint32_t)(uint8_t)(int8_t)code) << (8 * k);
-          }
-        }
-        // every lane takes part in the group reduction (the branch above is group-dependent)
-#pragma unroll
-        for (int o = 4; o > 0; o >>= 1) bad |= __shfl_xor_sync(0xFFFFFFFFu, (int)bad, o) != 0;
-        if (bad) blk_ok = false;
-      }
+      uint32_t packed;
+      int e;
+      bool blk_ok;
+      quant_quad(f4[u], packed, e, blk_ok);
       const bool leader = (lane & 7) == 0 && j < n;
       if (!blk_ok) {
         if (leader) w_status = max(w_status, (int)APX_ERR_QUANT_REFUSED);

@@ -116,6 +116,7 @@ struct apx_ctx {
   DevBuf dev;      // [out | status | desc | exps | codes] of the synchronous calls
   DevBuf scratch;  // device-side quantization scratch of the f32 path
   DevBuf gwork;    // GEMM per-call workspace (its head zeroed whenever it is reallocated)
+  DevBuf ascratch; // codes / exps / descriptors of apx_matmat_f32_async off the fused route
   HostBuf host;    // pinned mirror of `dev`
 };
 
@@ -698,15 +699,24 @@ int apx_matmat_f32(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in, siz
   std::memcpy(h + y_sz + st_sz, x, k_cols * n_in * 4);
   e = cudaMemcpyAsync(d + y_sz, h + y_sz, st_sz + k_cols * n_in * 4, cudaMemcpyHostToDevice,
                       ctx->stream);
-  if (e == cudaSuccess)
-    e = launch_quant_f32_cols((const float *)(d + y_sz + st_sz), n_in, n_in, (int)k_cols, dcod,
-                              ld, dexp, ldb, descs, ctx->stream);
   unsigned long long *status = (unsigned long long *)(d + y_sz);
-  if (e == cudaSuccess && gemm) {
-    e = launch_gemm_q8_0(t->plan, t->d_pack, t->gemm, n_out, n_in, k_cols, dcod, ld, dexp, ldb,
-                         descs, ctx->gwork.p, nullptr, (float *)d, status, ctx->sm_count,
-                         ctx->stream);
+  const float *dx = (const float *)(d + y_sz + st_sz);
+  if (e == cudaSuccess && gemm && gemm_f32_ok(n_in, dx, n_in)) {
+    // quantize inside the GEMM's prep kernel: one pass over the f32 columns
+    e = launch_gemm_q8_0_f32(t->plan, t->d_pack, t->gemm, n_out, n_in, k_cols, dx, n_in,
+                             ctx->gwork.p, nullptr, (float *)d, status, ctx->sm_count,
+                             ctx->stream);
+  } else if (e == cudaSuccess && gemm) {
+    e = launch_quant_f32_cols(dx, n_in, n_in, (int)k_cols, dcod, ld, dexp, ldb, descs,
+                              ctx->stream);
+    if (e == cudaSuccess)
+      e = launch_gemm_q8_0(t->plan, t->d_pack, t->gemm, n_out, n_in, k_cols, dcod, ld, dexp,
+                           ldb, descs, ctx->gwork.p, nullptr, (float *)d, status, ctx->sm_count,
+                           ctx->stream);
   } else {
+    if (e == cudaSuccess)
+      e = launch_quant_f32_cols(dx, n_in, n_in, (int)k_cols, dcod, ld, dexp, ldb, descs,
+                                ctx->stream);
     for (size_t c = 0; e == cudaSuccess && c < k_cols; c++)
       e = launch_gemv(t->plan, t->type, t->d_pack, t->d_scratch, n_out, n_in, dcod + c * ld,
                       dexp + c * ldb, descs + c * sizeof(ActDesc), nullptr,
@@ -915,6 +925,50 @@ int apx_matmat_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in, s
     if (e != cudaSuccess) return APX_ERR_CUDA;
   }
   return APX_OK;
+}
+
+int apx_matmat_f32_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
+                         size_t k_cols, const float *d_x, size_t ldx, int64_t *d_out_q32,
+                         float *d_out_f32, apx_call_status *d_status, void *stream) {
+  if (!ctx || !d_status || (k_cols && n_in && !d_x) || ldx < n_in)
+    return APX_ERR_INVALID_ARGUMENT;
+  if (k_cols > (size_t)INT32_MAX) return APX_ERR_TOO_LARGE;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  Tensor *t = find(ctx, tensor);
+  if (!t || n_in != t->n_in || n_out > t->n_out) return APX_ERR_LAYOUT_MISMATCH;
+  if (k_cols == 0) return APX_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool gemm = gemm_route(ctx, *t, n_out, n_in, k_cols);
+  if (gemm && ensure_gwork(ctx, k_cols, n_in, n_out) != cudaSuccess) return APX_ERR_OUT_OF_MEMORY;
+  cudaError_t e;
+  if (gemm && gemm_f32_ok(n_in, d_x, ldx)) {
+    e = launch_gemm_q8_0_f32(t->plan, t->d_pack, t->gemm, n_out, n_in, k_cols, d_x, ldx,
+                             ctx->gwork.p, (long long *)d_out_q32, d_out_f32,
+                             (unsigned long long *)d_status, ctx->sm_count, st);
+    return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
+  }
+  const size_t ld = apx_act_padded_len(n_in), ldb = ld / 32;
+  const size_t ds_sz = align16(k_cols * sizeof(ActDesc)), ex_sz = align16(k_cols * ldb);
+  if (ctx->ascratch.ensure(ds_sz + ex_sz + k_cols * ld) != cudaSuccess)
+    return APX_ERR_OUT_OF_MEMORY;
+  uint8_t *sc = (uint8_t *)ctx->ascratch.p;
+  const ActDesc *descs = (const ActDesc *)sc;
+  uint8_t *dexp = sc + ds_sz;
+  int8_t *dcod = (int8_t *)(sc + ds_sz + ex_sz);
+  e = launch_quant_f32_cols(d_x, n_in, ldx, (int)k_cols, dcod, ld, dexp, ldb, sc, st);
+  if (e == cudaSuccess && gemm) {
+    e = launch_gemm_q8_0(t->plan, t->d_pack, t->gemm, n_out, n_in, k_cols, dcod, ld, dexp, ldb,
+                         descs, ctx->gwork.p, (long long *)d_out_q32, d_out_f32,
+                         (unsigned long long *)d_status, ctx->sm_count, st);
+  } else {
+    for (size_t c = 0; e == cudaSuccess && c < k_cols; c++)
+      e = launch_gemv(t->plan, t->type, t->d_pack, t->d_scratch, n_out, n_in, dcod + c * ld,
+                      dexp + c * ldb, descs + c,
+                      d_out_q32 ? (long long *)d_out_q32 + c * n_out : nullptr,
+                      d_out_f32 ? d_out_f32 + c * n_out : nullptr,
+                      (unsigned long long *)&d_status[c].first, st);
+  }
+  return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
 }
 
 int apx_status_decode(apx_ctx *ctx, uint64_t tensor, const apx_call_status *status,

@@ -97,7 +97,8 @@ def cpu_prefill_baseline(seconds=10.0, tokens=64):
 
 
 def measure_prefill(be, lib, dev, stream, steps, warmup, pg, local, world):
-    """device-timed prefill steps (quantizer + exact GEMM, both shapes)."""
+    """device-timed prefill steps (f32 columns quantized inside the GEMM's prep
+    kernel, then the exact GEMM; both shapes)."""
     import torch
 
     from apeiron_b200 import synth
@@ -113,12 +114,8 @@ def measure_prefill(be, lib, dev, stream, steps, warmup, pg, local, world):
     bufs = []
     for m, (t, n_out, n_in) in enumerate(PREFILL):
         x = np.stack([synth.activation_f32(n_in, 3000 + 7 * m + c) for c in range(k)])
-        pad = lib.apx_act_padded_len(n_in)
         bufs.append(dict(
             x=x, dx=torch.from_numpy(x).to(dev),
-            codes=torch.zeros(k * pad, dtype=torch.int8, device=dev),
-            exps=torch.full((k * pad // 32,), 0xFF, dtype=torch.uint8, device=dev),
-            descs=torch.zeros(k * 8, dtype=torch.int32, device=dev),
             q32=torch.zeros(k * n_out, dtype=torch.int64, device=dev),
             f32=torch.zeros(k * n_out, dtype=torch.float32, device=dev),
             status=torch.full((2 * k,), -1, dtype=torch.int64, device=dev)))
@@ -126,14 +123,11 @@ def measure_prefill(be, lib, dev, stream, steps, warmup, pg, local, world):
     def step(i, q32=False):
         for m, (t, n_out, n_in) in enumerate(PREFILL):
             b = bufs[m]
-            assert lib.apx_quant_f32_cols_async(be.ctx, b["dx"].data_ptr(), n_in, k,
-                                                b["codes"].data_ptr(), b["exps"].data_ptr(),
-                                                b["descs"].data_ptr(), sp) == 0
-            assert lib.apx_matmat_async(be.ctx, tensors[i % copies][m].handle, n_out, n_in, k,
-                                        b["codes"].data_ptr(), b["exps"].data_ptr(),
-                                        b["descs"].data_ptr(),
-                                        b["q32"].data_ptr() if q32 else None,
-                                        b["f32"].data_ptr(), b["status"].data_ptr(), sp) == 0
+            assert lib.apx_matmat_f32_async(be.ctx, tensors[i % copies][m].handle, n_out,
+                                            n_in, k, b["dx"].data_ptr(), n_in,
+                                            b["q32"].data_ptr() if q32 else None,
+                                            b["f32"].data_ptr(), b["status"].data_ptr(),
+                                            sp) == 0
 
     # exactness of the timed configuration: every column's Q32.32 outputs of both shapes
     # against the oracle's per-column contract (threaded C port), before any timing
@@ -190,19 +184,20 @@ def measure_prefill(be, lib, dev, stream, steps, warmup, pg, local, world):
         "metric": "pp512 int8 GEMM TOPS", "value": tops, "unit": "TOPS",
         "ms_per_step": ms, "steps": reps * G, "warmup": warmup,
         "config": {"workload": "Q8_0 prefill, 512 f32 tokens x (W 4864x896, W 896x4864), "
-                               "configs[2]; step = device quant_act + exact GEMM, both shapes",
+                               "configs[2]; step = f32_to_fixed + quant_act fused into the GEMM's prep, "
+                               "then the exact GEMM, both shapes",
                    "weight_copies": copies, "l2": "rotating weight copies, > 3x the 126 MB L2",
                    "exact": "Q32.32 outputs of every column bit-equal to the CPU oracle "
                             "(checked before timing)"},
         "roofline": {"bound": "tensor", "achieved": tops, "peak": peak, "unit": "TOPS",
                      "frac": tops / peak, "peak_source": src,
-                     "note": "whole step (quantizer, prep and GEMM launches); the exact "
+                     "note": "whole step (fused quantize-prep and GEMM launches); the exact "
                              "per-block scale fold on the integer pipes bounds it, not the "
                              "tensor cores"},
         "e2e": {"value": e2e, "unit": "TOPS",
                 "h2d_bytes_per_step": sum(4 * k * n_in + 16 * k for _, _, n_in in PREFILL),
                 "d2h_bytes_per_step": sum(4 * k * n_out + 16 * k for _, n_out, _ in PREFILL)},
-        "gpu_launches_per_step": 3 * len(PREFILL),
+        "gpu_launches_per_step": 2 * len(PREFILL),
     }
 
 

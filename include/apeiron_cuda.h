@@ -207,6 +207,16 @@ APX_API int apx_matmat_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t
                      size_t k_cols, const int8_t *d_codes, const uint8_t *d_exps,
                      const apx_act_desc *d_descs, int64_t *d_out_q32,
                      float *d_out_f32, apx_call_status *d_status, void *stream);
+/* The f32 prefill on device buffers: k_cols columns of n_in floats (column c at
+ * d_x[c*ldx ..]) through f32_to_fixed + quant_act and the exact projection, column c equal
+ * to apx_matvec_f32 of column c; d_status[c] as for apx_matmat_async.  Q8_0 tensors with
+ * at least 4 columns, d_x 16-byte aligned, ldx a multiple of 4 and n_in <= 16384 quantize
+ * inside the GEMM's prep kernel; other calls quantize into a context buffer first.  Shares
+ * the context workspace as apx_matmat_async does. */
+APX_API int apx_matmat_f32_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
+                                 size_t k_cols, const float *d_x, size_t ldx,
+                                 int64_t *d_out_q32, float *d_out_f32,
+                                 apx_call_status *d_status, void *stream);
 /* Several projections that read the same device activation (q/k/v of a layer, gate/up of a
  * FFN), each over its whole tensor: out[i] = matvec(tensors[i], x), refusal word in
  * d_status[i] (all ones on entry).  Up to APX_MAX_GROUP tensors of one family whose layout

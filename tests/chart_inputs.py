@@ -50,3 +50,49 @@ def random_x(n, seed):
 
 def lcg_next(seed):
     return (seed * 6_364_136_223_846_793_005 + 1_442_695_040_888_963_407) & MASK
+
+
+def _f(bits):
+    return np.array(bits, dtype=np.uint32).view(np.float32)
+
+
+def f32_block_kinds(n, seed):
+    """f32 columns of length n for the device quantizer, each stressing one block kind of
+    f32_to_fixed + quant_act: subnormals, values that round to zero in Q32.32, values above
+    the 32-bit route's 127·2^24, -2^31 (accepted), 2^31, NaN and -inf (refused), a zero
+    column, any finite |f| < 2^31, and Q32.32 blocks beside ordinary ones."""
+    rng = np.random.default_rng(seed)
+    base = rng.standard_normal(n).astype(np.float32)
+    cols = [base.copy()]
+    cols.append((base * np.float32(1e-12)).astype(np.float32))      # tiny: rounds in Q32.32
+    sub = rng.integers(0, 1 << 23, n, dtype=np.uint32) | (rng.integers(0, 2, n, dtype=np.uint32) << 31)
+    cols.append(_f(sub))                                              # subnormals
+    big = base.copy()
+    big[::7] = np.float32(-2.14e9)                                    # above 127·2^24: code -64
+    cols.append(big)
+    lo = base.copy()
+    lo[0] = np.float32(-2147483648.0)                                 # -2^31: i64::MIN, accepted
+    cols.append(lo)
+    over = base.copy()
+    over[n // 2] = np.float32(2147483648.0)                           # 2^31: refused
+    cols.append(over)
+    nan = base.copy()
+    nan[-1] = np.float32(np.nan)
+    cols.append(nan)
+    inf = base.copy()
+    inf[n // 3] = -np.float32(np.inf)
+    cols.append(inf)
+    cols.append(np.zeros(n, dtype=np.float32))
+    edge = base.copy()
+    edge[::5] = _f([0x4EFE0000])[0]                                   # exactly 127·2^24
+    cols.append(edge)
+    above = base.copy()
+    above[n // 2] = _f([0x4EFE0001])[0]                               # one ulp above: code 64
+    cols.append(above)                                                # leaves i64, refused
+    wild = rng.integers(0, 0x4F000000, n, dtype=np.uint32) | (rng.integers(0, 2, n, dtype=np.uint32) << 31)
+    cols.append(_f(wild))                                             # any finite |f| < 2^31
+    mixed = base.copy()
+    mixed[200:232] = np.float32(1.5e9)                                # one Q32.32 block
+    mixed[40:72] = np.float32(3e-10)
+    cols.append(mixed)
+    return np.stack(cols)

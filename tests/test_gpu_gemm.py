@@ -233,3 +233,84 @@ def test_async_columns_match_sync(be):
     want = np.stack(be.matmat_q8act(Q8_0, tens, n_out, n_in, qs))
     assert np.array_equal(q32.cpu().numpy().reshape(k, n_out), want)
     assert np.array_equal(f32.cpu().numpy().reshape(k, n_out), be.matmat_f32(tens, x))
+
+
+def _oracle_f32_column(raw, n_out, n_in, col):
+    """The reference's f32 prefill of one column: f32_to_fixed, quant_act (None: refused
+    with QuantRefused), then matvec_q8act; values or ("err", code, ...)."""
+    v = [O.f32_to_q32(int(b)) for b in col.view(np.uint32)]
+    if any(t is None for t in v):
+        return ("err", 10)
+    q = O.quant_act(np.array(v, dtype=np.int64))
+    if q is None:
+        return ("err", 10)
+    codes, scales = q
+    r = O.matmat_q8act_mt(Q8_0, raw, n_out, n_in, codes[None, :], scales[None, :], THREADS)
+    return r if isinstance(r, tuple) else r[0]
+
+
+@pytest.mark.parametrize("n_out,n_in,ldx", [(256, 896, 896), (200, 200, 204),
+                                            (130, 4864, 4864), (64, 100, 100)])
+def test_f32_fused_prep_matches_oracle(be, n_out, n_in, ldx):
+    """apx_matmat_f32_async with f32_to_fixed + quant_act fused into the GEMM's prep kernel
+    (Q8_0, at least 4 columns, 16-byte aligned rows): every block kind of the device
+    quantizer beside ordinary columns, 70 columns so that the last column tile is ragged.
+    Bar: Q32.32 outputs equal to the oracle's column by column; refused columns carry the
+    oracle's refusal (QuantRefused for a column quant_act refuses); columns that take the
+    checked route inside the GEMM (Q32.32 blocks beside tiny ones) are exact too."""
+    import ctypes as C
+    import torch
+
+    from apeiron_b200 import _abi
+    from chart_inputs import f32_block_kinds
+
+    lib = be.lib
+    raw = synth.payload(Q8_0, n_out, n_in, 31 + n_in)
+    tens = be.upload(Q8_0, raw, n_out, n_in)
+    kinds = f32_block_kinds(n_in, 5 + n_in)
+    normal = np.stack([synth.activation_f32(n_in, 900 + c) for c in range(70 - len(kinds))])
+    x = np.concatenate([normal[:20], kinds, normal[20:]]).astype(np.float32)
+    k = x.shape[0]
+    xp = np.zeros((k, ldx), dtype=np.float32)
+    xp[:, :n_in] = x
+    dev = torch.device("cuda:0")
+    dx = torch.from_numpy(xp).to(dev)
+    q32 = torch.zeros(k * n_out, dtype=torch.int64, device=dev)
+    f32 = torch.zeros(k * n_out, dtype=torch.float32, device=dev)
+    status = torch.full((2 * k,), -1, dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.apx_matmat_f32_async(be.ctx, tens.handle, n_out, n_in, k, dx.data_ptr(), ldx,
+                                    q32.data_ptr(), f32.data_ptr(), status.data_ptr(),
+                                    stream) == 0
+    torch.cuda.synchronize()
+    st = status.cpu().numpy()
+    got = q32.cpu().numpy().reshape(k, n_out)
+    gotf = f32.cpu().numpy().reshape(k, n_out)
+    for c in range(k):
+        word = _abi.CallStatus(int(st[2 * c]) & ((1 << 64) - 1), 0)
+        err = _abi.ApxErr()
+        rc = lib.apx_status_decode(be.ctx, tens.handle, C.byref(word), C.byref(err))
+        want = _oracle_f32_column(raw, n_out, n_in, x[c])
+        if isinstance(want, tuple):
+            assert rc == want[1], (c, rc, want)
+            continue
+        assert rc == 0, (c, rc)
+        assert np.array_equal(got[c], want), c
+        assert np.array_equal(gotf[c], be.matvec_f32(tens, x[c])), c
+
+
+def test_f32_sync_fused_matches_unfused(be):
+    """The synchronous f32 prefill on an n_in that allows the fused prep (a multiple of 4)
+    and one that does not (quantizer kernel, then the GEMM) both equal matvec_f32."""
+    for n_in in (448, 450):
+        raw = synth.payload(Q8_0, 192, n_in, 7 + n_in)
+        t = be.upload(Q8_0, raw, 192, n_in)
+        x = np.stack([synth.activation_f32(n_in, 40 + c) for c in range(9)])
+        x[3, 17] = np.float32(np.nan)
+        with pytest.raises(chart.MatvecError) as ei:
+            be.matmat_f32(t, x)
+        assert ei.value.col == 3
+        x[3, 17] = 0.5
+        y = be.matmat_f32(t, x)
+        for c in range(9):
+            assert np.array_equal(y[c], be.matvec_f32(t, x[c])), (n_in, c)
