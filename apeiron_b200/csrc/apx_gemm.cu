@@ -7,34 +7,32 @@
 // scale S_{c,b} = 2^e_{c,b},
 //     y[r,c] = round_shift_32( Σ_b m_{r,b}·2^(k_{r,b}+e_{c,b}) · D_b[r,c] ),
 //     D_b[r,c] = Σ_{i<32} q_{r,b,i}·x_{c,b,i}.
-// The tensor cores form every block's dot exactly (kind::i8, s32 accumulators in TMEM) and
-// also apply the activation's per-block power of two: with s = e − emin_c (0..2) they
-// accumulate D' = A·x + A·x[s>=1] + 2·A·x[s>=2] = D·2^s from "planes" of the activation codes
-// (plane k holds the blocks whose s is at least k; the MMA of plane 2 is issued twice),
-// 2^smax MMAs per block where smax is the largest s of the tile's tokens.  The epilogue then folds each block with one widening
-// multiply-add, relative to the row's smallest weight exponent kmin_r, the way the
+// The tensor cores form every block's dot D_b exactly (kind::i8, one MMA per block with K = 32,
+// s32 accumulators in TMEM).  The epilogue folds each block relative to the token's smallest
+// activation exponent emin_c and the row's smallest weight exponent kmin_r, the way the
 // reference's gemm_q8_0 shift-accumulates (gemm.rs:99-102 spread_limit, 470-486):
-//     acc += D'_b · M_{r,b},   M = m·2^(k − kmin_r)
-// which is exact in i64 while |D'·M| < 2^(33+kspread) summed over the blocks stays below
-// 2^63.  y = round_shift_32(acc·2^(kmin_r+emin_c)) (pow2.rs:76-96 `finish`).  Columns whose
-// activation spread exceeds 2, outside the reference's i128 call bound (chart/mod.rs:
-// 362-383) or holding a code of -128 take matvec_fixed instead: the checked row path, by
-// extra CTAs of the same launch.
+//     acc += (D_b · 2^s) · M_{r,b},   s = e_{c,b} − emin_c,   M = m·2^(k − kmin_r)
+// one shift and one widening multiply-add per output and block.  |D| < 2^19, so D·2^s stays in
+// int32 for s <= 11, and the sum stays exact in i64 while nb terms below 2^(30 + s + kspread)
+// stay below 2^62 (gemm_max_shift bounds s per tensor).  y = round_shift_32(acc·2^(kmin_r +
+// emin_c)) (pow2.rs:76-96 `finish`).  Columns whose activation spread exceeds that bound, outside
+// the reference's i128 call bound (chart/mod.rs:362-383) or holding a code of -128 take
+// matvec_fixed instead: the checked row path, by extra CTAs of the same launch.
 //
 // Layout in HBM (built once per tensor, on its first multi-column call): the int8 codes
 // row-major, K padded to 128 bytes and rows to 128, for 2D TMA; M_{r,b} as int32 [block][row];
-// kmin per row.  Per call, the prep kernel writes the activation planes row-major per token
-// (zero for zero-scale blocks and past n_in), s as int32 [block][token], emin and a per-token
-// route (refused / GEMM / checked rows).
+// kmin per row.  Per call, the prep kernel writes the activation codes row-major per token
+// (zero for zero-scale blocks, past n_in and off the GEMM), s as int32 [block][token], emin and
+// a per-token route (refused / GEMM / checked rows).
 //
-// Pipeline (one CTA per 128-row × 64-token tile, all of K):
-//   warp 0      TMA producer: 128-byte K slabs of W (128 rows) and of the planes the slab's
-//               blocks use (64 tokens), 128B-swizzled, and the slab's M table, into a
-//               5-stage ring (cp.async.bulk.tensor, no multicast);
-//   warp 1      TMEM owner and MMA issuer: a slab's blocks into one of 2 TMEM buffers of
+// Pipeline (one CTA per 128-row × 64-token tile and K range):
+//   warp 0      TMA producer: 128-byte K slabs of W (128 rows) and of the codes (64 tokens),
+//               128B-swizzled, and the slab's M and s tables, into an 8-stage ring
+//               (cp.async.bulk.tensor, no multicast);
+//   warp 1      TMEM owner and MMA issuer: a slab's 4 blocks into one of 2 TMEM buffers of
 //               4 × 64 columns, one tcgen05.commit per slab;
-//   warps 2..9  epilogue: tcgen05.ld of 32 rows × 32 tokens per block (the next block's
-//               load in flight during the fold), one mad.wide per output and block.
+//   warps 2..9  epilogue: tcgen05.ld of 32 rows × 32 tokens per block (two blocks' loads in
+//               flight), the shift-and-fold per output and block.
 // Every wait is bounded (kWaitLimit); a wait that gives up records APX_ERR_DEVICE_TIMEOUT,
 // drains what the CTA has in flight and frees its TMEM before returning.
 #include <cuda.h>
@@ -56,25 +54,26 @@ namespace apx {
 constexpr int kTileM = 128;
 constexpr int kTileN = 64;
 constexpr int kSlab = 128;  // K bytes per stage (4 blocks): one 128B swizzle atom per row
-constexpr int kStages = 5;
+constexpr int kStages = 8;
 constexpr int kBufs = 2;    // TMEM buffers of one stage: 4 blocks × kTileN columns (512 in all)
 constexpr int kBufCols = (kSlab / 32) * kTileN;
-constexpr int kEpiWarps = 8;  // 2 per SM sub-partition: 32 rows × 32 tokens each
-constexpr int kEpiTok = 32;
+constexpr int kEpiWarps = 16;  // 4 per SM sub-partition: 32 rows × kEpiTok tokens each
+constexpr int kEpiTok = kTileN * 4 / kEpiWarps;
 constexpr int kThreads = 32 * (2 + kEpiWarps);
-constexpr int kPlanes = 3;   // activation planes x, x[s>=1], x[s>=2] (the last used twice): s <= 2
-constexpr int kMaxShift = 2;
+constexpr int kMaxShift = 11;  // s = e − emin_c <= 11: |D·2^s| < 2^30 stays in int32
 constexpr int kStageA = kTileM * kSlab;           // 16 KB of weight codes
-constexpr int kStageB = kTileN * kSlab;           // 8 KB per activation plane
+constexpr int kStageB = kTileN * kSlab;           // 8 KB of activation codes
 constexpr int kStageM = kTileM * (kSlab / 32) * 4;  // 2 KB: M of 4 blocks × 128 rows
-constexpr int kStageBytes = 42 * 1024;            // one stage, 1024-aligned
+constexpr int kStageS = kTileN * (kSlab / 32) * 4;  // 1 KB: s of 4 blocks × 64 tokens
+constexpr int kStageBytes = 27 * 1024;            // one stage, 1024-aligned
 constexpr int kFallbackCtas = 32;        // extra CTAs of each launch for the checked columns
 constexpr int kSpreadLimit = 20;         // weight exponent spread: M stays in int32
 constexpr int kMaxBlocks = (1 << 13) - 1;  // the i64 fold's bound on the block count
 constexpr unsigned kRouteNone = 0, kRouteGemm = 1, kRouteChecked = 2;
 
+static_assert(kEpiWarps % 4 == 0 && (kEpiTok == 16 || kEpiTok == 32), "epilogue split");
 static_assert(kStageA % 1024 == 0 && kStageB % 1024 == 0 && kStageBytes % 1024 == 0 &&
-                  kStageA + kPlanes * kStageB + kStageM <= kStageBytes,
+                  kStageA + kStageB + kStageM + kStageS <= kStageBytes,
               "stages keep the 1024-byte alignment of the swizzled tiles");
 
 // ---- descriptors ---------------------------------------------------------------------------
@@ -85,7 +84,7 @@ constexpr uint32_t idesc_i8(int n) {
   return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) |
          ((uint32_t)(kTileM >> 4) << 24);
 }
-constexpr uint32_t kIdesc64 = idesc_i8(kTileN);  // one plane
+constexpr uint32_t kIdesc64 = idesc_i8(kTileN);
 
 // Shared-memory matrix descriptor of a K-major operand in the 128B-swizzled layout TMA
 // writes: start address >> 4 in bits 0-13, leading byte offset 16 (>> 4) in bits 16-29,
@@ -156,6 +155,18 @@ __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&v)[3
       : "r"(taddr));
 }
 
+// This warp's kEpiTok columns of 32 TMEM lanes.
+template <int N>
+__device__ __forceinline__ void tmem_ld_tok(uint32_t taddr, uint32_t (&v)[N]);
+template <>
+__device__ __forceinline__ void tmem_ld_tok<16>(uint32_t taddr, uint32_t (&v)[16]) {
+  tmem_ld16_nowait(taddr, v);
+}
+template <>
+__device__ __forceinline__ void tmem_ld_tok<32>(uint32_t taddr, uint32_t (&v)[32]) {
+  tmem_ld32_nowait(taddr, v);
+}
+
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -167,12 +178,20 @@ __device__ __forceinline__ void mad_wide(long long &acc, int a, int b) {
   acc += (long long)a * (long long)b;
 }
 
-// acc[j] += D'[j]·M for the warp's tokens (D' = D·2^s formed by the tensor cores), one
-// widening multiply-add each.  |D'| <= 2^21 and |M| < 2^31.
+// acc[j] += (D[j]·2^s[j])·M for the warp's tokens: the block dot D from the tensor cores, the
+// token's shift s for this block from shared memory (the same 32 words for every lane: one
+// broadcast read per 4 tokens), one shift and one widening multiply-add each.  |D| < 2^19 and
+// s <= 11, so D·2^s stays in int32; |M| < 2^31.
 __device__ __forceinline__ void fold(long long (&acc)[kEpiTok], const uint32_t (&d)[kEpiTok],
-                                     int32_t m) {
+                                     const int *s, int32_t m) {
 #pragma unroll
-  for (int j = 0; j < kEpiTok; j++) mad_wide(acc[j], (int)d[j], m);
+  for (int j4 = 0; j4 < kEpiTok / 4; j4++) {
+    const int4 s4 = reinterpret_cast<const int4 *>(s)[j4];
+    mad_wide(acc[4 * j4 + 0], (int)(d[4 * j4 + 0] << s4.x), m);
+    mad_wide(acc[4 * j4 + 1], (int)(d[4 * j4 + 1] << s4.y), m);
+    mad_wide(acc[4 * j4 + 2], (int)(d[4 * j4 + 2] << s4.z), m);
+    mad_wide(acc[4 * j4 + 3], (int)(d[4 * j4 + 3] << s4.w), m);
+  }
 }
 
 // The finish of one output: v = round_shift_32(acc·2^s) (value.rs:10-12 on the 128-bit
@@ -233,7 +252,8 @@ __device__ __forceinline__ bool finish_fast(long long acc, unsigned s, long long
 struct WorkView {
   int *cnt;          // split-K arrival counters, one per tile (a fixed 4 KB at the start)
   long long *part;   // split-K partial sums
-  int8_t *bcodes;    // [kPlanes][n_cols_pad][kp]: plane k holds the codes of blocks with s >= k
+  int8_t *bcodes;    // [n_cols_pad][kp]: the GEMM columns' codes (zero elsewhere)
+  int32_t *shift;    // [kp / 32][n_cols_pad]: s = e − emin_c of block b of token c (0 elsewhere)
   int32_t *emin;     // [n_cols_pad]
   uint32_t *route;   // [n_cols_pad]
   int32_t *fb;       // [0] count, [1] CTAs done, [2..] checked-route columns
@@ -249,24 +269,37 @@ size_t gemm_work_head_bytes(size_t n_cols) { return (n_cols + 2 + 63) / 64 * 256
 
 constexpr size_t kCntBytes = 4096;  // split-K counters: at most 1024 split tiles
 
-// Split K when the tiles alone leave SMs idle: the largest split that keeps one wave.
-static int gemm_ksplit(size_t tiles, int kslabs, int sm_count) {
-  if (tiles == 0 || tiles >= (size_t)sm_count || tiles > kCntBytes / 4) return 1;
-  return (int)std::max<size_t>(1, std::min<size_t>({(size_t)sm_count / tiles, (size_t)kslabs,
-                                                    (size_t)8}));
+// The launch's work split: tiles [0, full) whole, one CTA each, in whole rounds of one CTA per
+// SM; each remaining tile over `ks` CTAs (split K) so that the short last round fills the SMs.
+// With fewer tiles than SMs every tile is split: the largest split that keeps one wave.
+struct Split {
+  int full, ks;
+  int pieces(int tiles) const { return full + (tiles - full) * ks; }
+};
+
+static Split gemm_split(size_t tiles, int kslabs, int sm_count) {
+  if (tiles == 0 || sm_count <= 0) return Split{(int)tiles, 1};
+  const size_t rem = tiles % (size_t)sm_count;
+  if (rem == 0 || rem > kCntBytes / 4) return Split{(int)tiles, 1};
+  const int ks = (int)std::min<size_t>({(size_t)sm_count / rem, (size_t)kslabs, (size_t)8});
+  if (ks <= 1) return Split{(int)tiles, 1};
+  return Split{(int)(tiles - rem), ks};
 }
 
-static size_t part_bytes(size_t tiles, int ksplit) {
-  return ksplit > 1 ? tiles * ksplit * kEpiWarps * 1024 * sizeof(long long) : 0;
+// One i64 accumulator per split tile, zero between calls (the finishing split clears it), at a
+// fixed place right after the counters: room for sm_count split tiles (a launch splits fewer).
+static size_t part_bytes(int sm_count) {
+  return (size_t)std::max(sm_count, 1) * kTileM * kTileN * sizeof(long long);
 }
 
-static WorkView work_view(void *base, size_t n_cols, int nb, size_t kp, size_t tiles,
-                          int ksplit) {
+static WorkView work_view(void *base, size_t n_cols, int nb, size_t kp, int sm_count) {
   uint8_t *p = static_cast<uint8_t *>(base);
   const size_t np = cols_pad(n_cols);
   WorkView w;
   w.cnt = reinterpret_cast<int *>(p);
   p += kCntBytes;
+  w.part = reinterpret_cast<long long *>(p);
+  p += part_bytes(sm_count);
   w.fb = reinterpret_cast<int32_t *>(p);
   p += gemm_work_head_bytes(n_cols);
   w.route = reinterpret_cast<uint32_t *>(p);
@@ -275,15 +308,14 @@ static WorkView work_view(void *base, size_t n_cols, int nb, size_t kp, size_t t
   p += np * 4;
   w.bcodes =
       reinterpret_cast<int8_t *>((reinterpret_cast<uintptr_t>(p) + 255) & ~(uintptr_t)255);
-  p = reinterpret_cast<uint8_t *>(w.bcodes) + kPlanes * np * kp;
+  p = reinterpret_cast<uint8_t *>(w.bcodes) + np * kp;
+  w.shift =
+      reinterpret_cast<int32_t *>((reinterpret_cast<uintptr_t>(p) + 255) & ~(uintptr_t)255);
+  p = reinterpret_cast<uint8_t *>(w.shift + (kp / 32) * np);
   w.qcodes = reinterpret_cast<int8_t *>(p);
   p += np * kp;
   w.qexps = p;
-  p += np * (kp / 32);
-  w.part = ksplit > 1 ? reinterpret_cast<long long *>(
-                            (reinterpret_cast<uintptr_t>(p) + 255) & ~(uintptr_t)255)
-                      : nullptr;
-  (void)tiles;
+  (void)nb;
   return w;
 }
 
@@ -291,17 +323,24 @@ static size_t gemm_tiles(size_t n_out, size_t n_cols) {
   return ((n_out + kTileM - 1) / kTileM) * ((n_cols + kTileN - 1) / kTileN);
 }
 
+// The layout of work_view: counters, split accumulators, head, route and emin, the B operand,
+// the shift table, the checked columns' codes and exponent bytes (with alignment slack).
 size_t gemm_work_bytes(size_t n_cols, size_t n_in, size_t n_out, int sm_count) {
-  const size_t nb = (n_in + 31) / 32, kp = (n_in + kSlab - 1) / kSlab * kSlab;
+  const size_t kp = (n_in + kSlab - 1) / kSlab * kSlab;
   const size_t np = cols_pad(n_cols);
-  const size_t tiles = gemm_tiles(n_out, n_cols);
-  const int ks = gemm_ksplit(tiles, (int)(kp / kSlab), sm_count);
-  (void)nb;
-  return kCntBytes + gemm_work_head_bytes(n_cols) + 2 * np * 4 + 256 + kPlanes * np * kp +
-         np * kp + np * (kp / 32) + 256 + part_bytes(tiles, ks);
+  (void)n_out;
+  return kCntBytes + part_bytes(sm_count) + gemm_work_head_bytes(n_cols) + 2 * np * 4 + 256 +
+         np * kp + 256 + (kp / 32) * np * 4 + np * kp + np * (kp / 32);
 }
 
-// ---- activation prep: describe, route, B operand, P table -----------------------------------
+// ---- activation prep: describe, route, B operand, shift table --------------------------------
+
+// A column the GEMM does not take (padding token, refused or checked): zero codes and shifts.
+__device__ __forceinline__ void zero_column(const WorkView &w, int c, size_t np, size_t kp) {
+  for (size_t j = (size_t)threadIdx.x * 16; j < kp; j += (size_t)blockDim.x * 16)
+    *reinterpret_cast<uint4 *>(w.bcodes + (size_t)c * kp + j) = make_uint4(0, 0, 0, 0);
+  for (size_t b = threadIdx.x; b < kp / 32; b += blockDim.x) w.shift[b * np + c] = 0;
+}
 
 struct PrepArgs {
   const int8_t *codes;  // caller codes, column c at c·ld
@@ -309,6 +348,7 @@ struct PrepArgs {
   const ActDesc *descs; // the quantizer's descriptors (a refusal there wins), or null
   size_t ld, ldb, n_in, kp;
   int nb, n_cols;
+  int max_shift;  // the largest spread e − emin a GEMM column may have on this tensor
   WorkView w;
   unsigned long long *status;  // column c's refusal word at status[c·2]
 };
@@ -318,10 +358,8 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(PrepArgs a) {
   __shared__ unsigned s_m128, s_route;
   const int c = blockIdx.x;
   const size_t np = cols_pad((size_t)a.n_cols);
-  if (c >= a.n_cols) {  // padding tokens of the last tile: no shift, zero planes
-    for (size_t j = (size_t)threadIdx.x * 16; j < a.kp; j += (size_t)blockDim.x * 16)
-      for (int k = 0; k < kPlanes; k++)
-        *reinterpret_cast<uint4 *>(a.w.bcodes + (k * np + c) * a.kp + j) = make_uint4(0, 0, 0, 0);
+  if (c >= a.n_cols) {  // padding tokens of the last tile: zero codes and shifts
+    zero_column(a.w, c, np, a.kp);
     if (threadIdx.x == 0) {
       a.w.emin[c] = 0;
       a.w.route[c] = kRouteNone;
@@ -342,9 +380,7 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(PrepArgs a) {
   }
   __syncthreads();
   if (s_status != APX_OK) {  // refused by the quantizer: its codes and exponents are not set
-    for (size_t j = (size_t)threadIdx.x * 16; j < a.kp; j += (size_t)blockDim.x * 16)
-      for (int k = 0; k < kPlanes; k++)
-        *reinterpret_cast<uint4 *>(a.w.bcodes + (k * np + c) * a.kp + j) = make_uint4(0, 0, 0, 0);
+    zero_column(a.w, c, np, a.kp);
     if (threadIdx.x == 0) {
       atomicMin(a.status + (size_t)c * 2, pack_status(0, (unsigned)s_status, 0));
       a.w.emin[c] = 0;
@@ -386,7 +422,7 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(PrepArgs a) {
     if (s_status != APX_OK) {
       atomicMin(a.status + (size_t)c * 2, pack_status(0, (unsigned)s_status, 0));
     } else if (!s_m128 && bound_ok((long long)a.n_in, Fam<kQ8_0>::top, s_emax) &&
-               (s_emax < 0 || s_emax - emin <= kMaxShift)) {
+               (s_emax < 0 || s_emax - emin <= a.max_shift)) {
       route = kRouteGemm;
     } else {
       route = kRouteChecked;
@@ -396,23 +432,21 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(PrepArgs a) {
     s_emin = emin;
     s_route = route;
     a.w.emin[c] = emin;
-    // a GEMM column also carries its exponent spread (0..kMaxShift): the tile's largest bounds
-    // every block's shift, so it sets the planes and MMAs per block
-    a.w.route[c] = route | (route == kRouteGemm && s_emax >= 0 ? (unsigned)(s_emax - emin) : 0u)
-                               << 8;
+    a.w.route[c] = route;
   }
   __syncthreads();
   const bool gemm = s_route == kRouteGemm;
   const int emin = s_emin;
-  // B planes of the column: x, x[s >= 1], x[s >= 2] (x: the codes, zero for zero-scale
-  // blocks and past n_in), so that x + x[s >= 1] + 2·x[s >= 2] = x·2^s
-  const size_t plane = np * a.kp;
+  // the B operand (the codes; zero for zero-scale blocks, past n_in and off the GEMM) and
+  // every block's shift s = e − emin
   int8_t *dst = a.w.bcodes + (size_t)c * a.kp;
+  for (size_t b = threadIdx.x; b < a.kp / 32; b += blockDim.x) {
+    const unsigned e = b < (size_t)a.nb ? exps[b] : APX_EXP_ZERO;
+    a.w.shift[b * np + c] = gemm && e != APX_EXP_ZERO ? (int)e - emin : 0;
+  }
   for (size_t j = (size_t)threadIdx.x * 16; j < a.kp; j += (size_t)blockDim.x * 16) {
     uint4 v = make_uint4(0, 0, 0, 0);
-    int sh = 0;
     if (gemm && j < a.n_in && exps[j / 32] != APX_EXP_ZERO) {
-      sh = (int)exps[j / 32] - emin;
       if (j + 16 <= a.n_in) {
         v = *reinterpret_cast<const uint4 *>(codes + j);
       } else {
@@ -421,10 +455,7 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(PrepArgs a) {
         memcpy(&v, t, 16);
       }
     }
-    const uint4 z = make_uint4(0, 0, 0, 0);
-#pragma unroll
-    for (int k = 0; k < kPlanes; k++)
-      *reinterpret_cast<uint4 *>(dst + k * plane + j) = sh >= k ? v : z;
+    *reinterpret_cast<uint4 *>(dst + j) = v;
   }
 }
 
@@ -439,6 +470,7 @@ struct QPrepArgs {
   const float *x;  // column c at x + c·ldx (16-byte aligned, ldx a multiple of 4)
   size_t ldx, n_in, kp;
   int nb, n_cols;
+  int max_shift;  // as PrepArgs::max_shift
   WorkView w;
   unsigned long long *status;  // column c's refusal word at status[c·2]
 };
@@ -454,10 +486,8 @@ __global__ void __launch_bounds__(256) gemm_quant_prep_kernel(QPrepArgs a) {
   __shared__ unsigned s_route;
   const int c = blockIdx.x;
   const size_t np = cols_pad((size_t)a.n_cols);
-  if (c >= a.n_cols) {  // padding tokens of the last tile: no shift, zero planes
-    for (size_t j = (size_t)threadIdx.x * 16; j < a.kp; j += (size_t)blockDim.x * 16)
-      for (int k = 0; k < kPlanes; k++)
-        *reinterpret_cast<uint4 *>(a.w.bcodes + (k * np + c) * a.kp + j) = make_uint4(0, 0, 0, 0);
+  if (c >= a.n_cols) {  // padding tokens of the last tile: zero codes and shifts
+    zero_column(a.w, c, np, a.kp);
     if (threadIdx.x == 0) {
       a.w.emin[c] = 0;
       a.w.route[c] = kRouteNone;
@@ -528,9 +558,7 @@ __global__ void __launch_bounds__(256) gemm_quant_prep_kernel(QPrepArgs a) {
   }
   __syncthreads();
   if (s_status != APX_OK) {  // quant_act returned None for the column
-    for (size_t j = (size_t)threadIdx.x * 16; j < a.kp; j += (size_t)blockDim.x * 16)
-      for (int k = 0; k < kPlanes; k++)
-        *reinterpret_cast<uint4 *>(a.w.bcodes + (k * np + c) * a.kp + j) = make_uint4(0, 0, 0, 0);
+    zero_column(a.w, c, np, a.kp);
     if (threadIdx.x == 0) {
       atomicMin(a.status + (size_t)c * 2, pack_status(0, (unsigned)s_status, 0));
       a.w.emin[c] = 0;
@@ -542,7 +570,7 @@ __global__ void __launch_bounds__(256) gemm_quant_prep_kernel(QPrepArgs a) {
     const int emin = s_emax >= 0 ? s_emin : 0;
     unsigned route;
     if (bound_ok((long long)a.n_in, Fam<kQ8_0>::top, s_emax) &&
-        (s_emax < 0 || s_emax - emin <= kMaxShift)) {
+        (s_emax < 0 || s_emax - emin <= a.max_shift)) {
       route = kRouteGemm;
     } else {
       route = kRouteChecked;
@@ -552,8 +580,7 @@ __global__ void __launch_bounds__(256) gemm_quant_prep_kernel(QPrepArgs a) {
     s_emin = emin;
     s_route = route;
     a.w.emin[c] = emin;
-    a.w.route[c] = route | (route == kRouteGemm && s_emax >= 0 ? (unsigned)(s_emax - emin) : 0u)
-                               << 8;
+    a.w.route[c] = route;
   }
   __syncthreads();
   const bool gemm = s_route == kRouteGemm;
@@ -565,17 +592,14 @@ __global__ void __launch_bounds__(256) gemm_quant_prep_kernel(QPrepArgs a) {
     for (size_t b = threadIdx.x; b < a.kp / 32; b += blockDim.x)
       a.w.qexps[(size_t)c * (a.kp / 32) + b] = sexps[b];
   }
-  // planes x, x[s >= 1], x[s >= 2] (zero codes for zero blocks and past n_in already)
-  const size_t plane = np * a.kp;
+  // the B operand (zero codes for zero blocks and past n_in already) and the shifts
   int8_t *dst = a.w.bcodes + (size_t)c * a.kp;
-  for (size_t j = (size_t)threadIdx.x * 16; j < a.kp; j += (size_t)blockDim.x * 16) {
-    const unsigned e = sexps[j / 32];
-    const uint4 v = gemm ? *reinterpret_cast<const uint4 *>(scodes + j) : make_uint4(0, 0, 0, 0);
-    const int sh = gemm && e != APX_EXP_ZERO ? (int)e - emin : 0;
-    const uint4 z = make_uint4(0, 0, 0, 0);
-#pragma unroll
-    for (int k = 0; k < kPlanes; k++)
-      *reinterpret_cast<uint4 *>(dst + k * plane + j) = sh >= k ? v : z;
+  for (size_t j = (size_t)threadIdx.x * 16; j < a.kp; j += (size_t)blockDim.x * 16)
+    *reinterpret_cast<uint4 *>(dst + j) =
+        gemm ? *reinterpret_cast<const uint4 *>(scodes + j) : make_uint4(0, 0, 0, 0);
+  for (size_t b = threadIdx.x; b < a.kp / 32; b += blockDim.x) {
+    const unsigned e = sexps[b];
+    a.w.shift[b * np + c] = gemm && e != APX_EXP_ZERO ? (int)e - emin : 0;
   }
 }
 
@@ -590,11 +614,12 @@ struct GemmArgs {
   unsigned long long *status;  // column c at status[c·2]
   size_t n_out, m_pad;
   int n_cols, nb, kslabs, m_tiles, tiles;
-  // split K: ksplit CTAs per tile, each over a contiguous range of slabs; their exact i64
-  // partial sums meet in `part`, and the last to arrive (per-tile counter) finishes
-  int ksplit;
-  long long *part;  // [tiles][ksplit][kEpiWarps][32 tokens][32 lanes]
-  int *cnt;         // [tiles], zero between calls
+  // tiles [0, full) one CTA each; every later tile over ksplit CTAs (split K), each over a
+  // contiguous range of slabs: their exact i64 partial sums meet in `part`, and the last to
+  // arrive (per split tile counter) finishes.  pieces = full + (tiles - full)·ksplit.
+  int full, ksplit, pieces;
+  long long *part;  // [tiles - full][kEpiWarps][kEpiTok tokens][32 lanes], zero between calls
+  int *cnt;         // [tiles - full], zero between calls
   // checked route (matvec_fixed per row) of the columns the prep kernel listed
   PackGeo geo;
   const int8_t *codes;
@@ -607,7 +632,7 @@ __device__ __forceinline__ void checked_columns(const GemmArgs g) {
   const long long n = fb[0];
   const long long items = n * (long long)g.n_out;
   const long long first =
-      (long long)(blockIdx.x - g.tiles * g.ksplit) * blockDim.x + threadIdx.x;
+      (long long)(blockIdx.x - g.pieces) * blockDim.x + threadIdx.x;
   for (long long i = first; i < items; i += (long long)kFallbackCtas * blockDim.x) {
     const int c = fb[2 + i / (long long)g.n_out];
     const size_t row = (size_t)(i % (long long)g.n_out);
@@ -632,14 +657,14 @@ __device__ __forceinline__ void checked_columns(const GemmArgs g) {
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_q8_0_kernel(const __grid_constant__ CUtensorMap map_w,
                      const __grid_constant__ CUtensorMap map_x,
-                     const __grid_constant__ CUtensorMap map_m, GemmArgs g) {
-  if ((int)blockIdx.x >= g.tiles * g.ksplit) {
+                     const __grid_constant__ CUtensorMap map_m,
+                     const __grid_constant__ CUtensorMap map_s, GemmArgs g) {
+  if ((int)blockIdx.x >= g.pieces) {
     checked_columns(g);
     return;
   }
-  // stage st: weight codes (16 KB, 128B-swizzled), activation planes 0..2 (8 KB each,
-  // swizzled; only the planes the stage's blocks use are loaded), M of its 4 blocks × 128
-  // rows (int32); per stage and block the largest shift of the tile's tokens
+  // stage st: weight codes (16 KB, 128B-swizzled), activation codes (8 KB, swizzled), M of
+  // its 4 blocks × 128 rows and s of its 4 blocks × 64 tokens (int32)
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -648,26 +673,34 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *dempty = dfull + kBufs, *mdone = dempty + kBufs;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mdone + 1);
   int *timeout = reinterpret_cast<int *>(tmem_slot + 1);
-  // [kStages][4] largest shift per block, 16-byte aligned for one vector read per stage
-  int *smax = reinterpret_cast<int *>((reinterpret_cast<uintptr_t>(timeout + 1) + 15) &
-                                      ~(uintptr_t)15);
   // per token of the tile: the finish shift emin_c, or -1 where the token is not the GEMM's
-  int *stok = smax + kStages * 4;
+  // (16-byte aligned for vector reads)
+  int *stok = reinterpret_cast<int *>((reinterpret_cast<uintptr_t>(timeout + 1) + 15) &
+                                      ~(uintptr_t)15);
   int *sflag = stok + kTileN;  // split K: this CTA is the tile's last split
-  // per token of the tile: its exponent spread (the largest shift of any of its blocks)
-  int *sspread = sflag + 4;
   auto stage_a = [&](int st) { return smem + st * kStageBytes; };
   auto stage_m = [&](int st) {
-    return reinterpret_cast<const int32_t *>(smem + st * kStageBytes + kStageA +
-                                             kPlanes * kStageB);
+    return reinterpret_cast<const int32_t *>(smem + st * kStageBytes + kStageA + kStageB);
+  };
+  auto stage_s = [&](int st) {
+    return reinterpret_cast<const int *>(smem + st * kStageBytes + kStageA + kStageB + kStageM);
   };
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int tile = (int)blockIdx.x % g.tiles, split = (int)blockIdx.x / g.tiles;
+  // this CTA's tile, and its share of the tile's slabs [kt0, kt0 + nk) of ks
+  int tile, split = 0, ks = 1;
+  if ((int)blockIdx.x < g.full) {
+    tile = (int)blockIdx.x;
+  } else {
+    const int i = (int)blockIdx.x - g.full, r = g.tiles - g.full;
+    tile = g.full + i % r;
+    split = i / r;
+    ks = g.ksplit;
+  }
+  const int stile = tile - g.full;  // index among the split tiles
   const int mt = tile % g.m_tiles, nt = tile / g.m_tiles;
-  // this CTA's slabs [kt0, kt0 + nk)
-  const int kt0 = (int)((long long)split * g.kslabs / g.ksplit);
-  const int nk = (int)((long long)(split + 1) * g.kslabs / g.ksplit) - kt0;
+  const int kt0 = (int)((long long)split * g.kslabs / ks);
+  const int nk = (int)((long long)(split + 1) * g.kslabs / ks) - kt0;
   const int m0 = mt * kTileM, n0 = nt * kTileN;
   const int np = (int)cols_pad((size_t)g.n_cols);
 
@@ -686,13 +719,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_w)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_x)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_m)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_s)) : "memory");
   }
   if (threadIdx.x >= 64 && threadIdx.x < 64 + kTileN) {
     const int c = n0 + (int)threadIdx.x - 64;
     const unsigned rw = c < g.n_cols ? g.w.route[c] : kRouteNone;
     const bool gemm_col = (rw & 0xFFu) == kRouteGemm;
     stok[threadIdx.x - 64] = gemm_col ? g.w.emin[c] : -1;
-    sspread[threadIdx.x - 64] = gemm_col ? (int)(rw >> 8) : 0;
   }
   if (warp == 1) {  // TMEM: kBufs × kBufCols columns of 32-bit accumulators
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -707,36 +740,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ---- TMA producer (lane 0 issues).  Every block's shift is at most the tile's largest
-    // exponent spread, read once here: planes and MMAs per block follow it ----
+    // ---- TMA producer (lane 0 issues): per slab W, the codes, M and s ----
     int issued = 0;
-    const int tile_smax = min(kMaxShift, __reduce_max_sync(0xFFFFFFFFu,
-                                                           max(sspread[lane], sspread[32 + lane])));
     for (int lk = 0; lk < nk; lk++) {
       const int kt = kt0 + lk, st = lk % kStages, use = lk / kStages;
-      int sq[4], smax_stage = 0;
-#pragma unroll
-      for (int q = 0; q < 4; q++) {
-        sq[q] = 4 * kt + q < g.nb ? tile_smax : 0;
-        smax_stage = max(smax_stage, sq[q]);
-      }
       int stop = 0;
       if (lane == 0) {
         if (use > 0 && !mbar_wait(empty + st, (use - 1) & 1)) {
           atomicExch(timeout, 1);
           stop = 1;
         } else {
-#pragma unroll
-          for (int q = 0; q < 4; q++) smax[st * 4 + q] = sq[q];
           uint8_t *base = stage_a(st);
-          const int planes = smax_stage + 1;
-          mbar_expect_tx(full + st, kStageA + kStageM + planes * kStageB);
+          mbar_expect_tx(full + st, kStageA + kStageB + kStageM + kStageS);
           tma_load_2d(base, &map_w, kt * kSlab, m0, full + st);
-          tma_load_2d(base + kStageA + kPlanes * kStageB, &map_m, m0, kt * (kSlab / 32),
+          tma_load_2d(base + kStageA, &map_x, kt * kSlab, n0, full + st);
+          tma_load_2d(base + kStageA + kStageB, &map_m, m0, kt * (kSlab / 32), full + st);
+          tma_load_2d(base + kStageA + kStageB + kStageM, &map_s, n0, kt * (kSlab / 32),
                       full + st);
-          for (int k = 0; k < planes; k++)
-            tma_load_2d(base + kStageA + k * kStageB, &map_x, kt * kSlab, k * np + n0,
-                        full + st);
           issued++;
         }
       }
@@ -747,13 +767,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int lk = issued > kStages ? issued - kStages : 0; lk < issued; lk++)
         mbar_wait(full + lk % kStages, (lk / kStages) & 1);
   } else if (warp == 1) {
-    // ---- MMA issuer: per block D' = A·x + A·x[s>=1] + 2·A·x[s>=2] = D·2^s, 1, 2 or 4
-    // accumulating MMAs (the last plane's twice) as the block needs; a stage's 4 blocks into
-    // one TMEM buffer, one commit per stage ----
+    // ---- MMA issuer: one MMA per block (its dot D, K = 32); a stage's 4 blocks into one
+    // TMEM buffer, one commit per stage ----
     if (lane == 0) {
       const uint64_t a0 = kDescHi | (smem_addr(stage_a(0)) >> 4);
       const uint64_t b0 = kDescHi | (smem_addr(stage_a(0) + kStageA) >> 4);
-      constexpr uint64_t kPlaneStep = kStageB >> 4;
       bool ok = true;
       for (int lk = 0; lk < nk; lk++) {
         const int kt = kt0 + lk, st = lk % kStages, buf = lk % kBufs;
@@ -765,20 +783,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint64_t ad = a0 + (uint64_t)(st * (kStageBytes >> 4));
         const uint64_t bd = b0 + (uint64_t)(st * (kStageBytes >> 4));
-        const int4 sq4 = *reinterpret_cast<const int4 *>(smax + st * 4);
-        const int sqa[4] = {sq4.x, sq4.y, sq4.z, sq4.w};
         const int nq = min(4, g.nb - 4 * kt);
 #pragma unroll
         for (int q = 0; q < 4; q++) {
           if (q >= nq) break;
-          const uint32_t d = tmem + (uint32_t)(buf * kBufCols + q * kTileN);
-          const uint64_t aq = ad + 2 * q, bq = bd + 2 * q;
-          mma_i8(d, aq, bq, kIdesc64, 0u);
-          if (sqa[q] >= 1) mma_i8(d, aq, bq + kPlaneStep, kIdesc64, 1u);
-          if (sqa[q] >= 2) {
-            mma_i8(d, aq, bq + 2 * kPlaneStep, kIdesc64, 1u);
-            mma_i8(d, aq, bq + 2 * kPlaneStep, kIdesc64, 1u);
-          }
+          mma_i8(tmem + (uint32_t)(buf * kBufCols + q * kTileN), ad + 2 * q, bd + 2 * q,
+                 kIdesc64, 0u);
         }
         mma_commit(dfull + buf);
       }
@@ -811,17 +821,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int nq = min(4, g.nb - 4 * kt);
       const int32_t *sm = stage_m(st) + rl;
+      const int *ss = stage_s(st) + c0;  // [4 blocks][64 tokens]: this warp's 32 tokens
       const uint32_t t = trow + (uint32_t)(buf * kBufCols);
 #pragma unroll
       for (int h = 0; h < 2; h++) {
         if (2 * h >= nq) break;
         uint32_t d0[kEpiTok], d1[kEpiTok];
         const bool two = 2 * h + 1 < nq;
-        tmem_ld32_nowait(t + (uint32_t)(2 * h * kTileN), d0);
-        if (two) tmem_ld32_nowait(t + (uint32_t)((2 * h + 1) * kTileN), d1);
+        tmem_ld_tok(t + (uint32_t)(2 * h * kTileN), d0);
+        if (two) tmem_ld_tok(t + (uint32_t)((2 * h + 1) * kTileN), d1);
         tmem_wait_ld();
-        fold(acc, d0, sm[2 * h * kTileM]);
-        if (two) fold(acc, d1, sm[(2 * h + 1) * kTileM]);
+        fold(acc, d0, ss + 2 * h * kTileN, sm[2 * h * kTileM]);
+        if (two) fold(acc, d1, ss + (2 * h + 1) * kTileN, sm[(2 * h + 1) * kTileM]);
       }
       tc_fence_before();
       __syncwarp();
@@ -838,28 +849,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     // contiguous in the output) with 16-byte stores.
     const int ew = warp - 2;
     bool all_ok = __all_sync(0xFFFFFFFFu, ok);
-    if (g.ksplit > 1) {
-      // publish this split's partial sums; the last split of the tile to arrive adds the
-      // others' (exact i64 additions) and finishes, the rest are done
-      long long *mine = g.part + (((size_t)tile * g.ksplit + split) * kEpiWarps + ew) * 1024;
+    if (ks > 1) {
+      // add this split's partial sums into the tile's accumulator in L2 (exact: i64 addition
+      // wraps, and the true sum fits); the last split of the tile to arrive reads the sum,
+      // leaves the accumulator zero for the next call and finishes, the rest are done
+      unsigned long long *sum = reinterpret_cast<unsigned long long *>(g.part) +
+                                ((size_t)stile * kEpiWarps + ew) * (kEpiTok * 32);
 #pragma unroll
-      for (int j = 0; j < kEpiTok; j++) mine[j * 32 + lane] = acc[j];
+      for (int j = 0; j < kEpiTok; j++) atomicAdd(sum + j * 32 + lane, (unsigned long long)acc[j]);
       __threadfence();
       asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
-      if (threadIdx.x == 64) *sflag = atomicAdd(g.cnt + tile, 1) == g.ksplit - 1;
+      if (threadIdx.x == 64) *sflag = atomicAdd(g.cnt + stile, 1) == ks - 1;
       asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
       const bool last = *sflag != 0;
       if (!last) all_ok = false;  // another split of this tile finishes
       if (last) {
         __threadfence();
-        for (int sp = 0; sp < g.ksplit; sp++) {
-          if (sp == split) continue;
-          const long long *other =
-              g.part + (((size_t)tile * g.ksplit + sp) * kEpiWarps + ew) * 1024;
 #pragma unroll
-          for (int j = 0; j < kEpiTok; j++) acc[j] += __ldcg(other + j * 32 + lane);
+        for (int j = 0; j < kEpiTok; j++) {
+          acc[j] = (long long)__ldcg(sum + j * 32 + lane);
+          sum[j * 32 + lane] = 0ull;
         }
-        if (threadIdx.x == 64) g.cnt[tile] = 0;  // ready for the next call
+        if (threadIdx.x == 64) g.cnt[stile] = 0;  // ready for the next call
       }
     }
     asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
@@ -1134,10 +1145,19 @@ void free_gemm_layout(GemmLayout *lay) {
 
 static size_t gemm_smem_bytes() {
   return 1024 + (size_t)kStages * kStageBytes + (2 * kStages + 2 * kBufs + 1) * 8 + 32 +
-         kStages * 4 * 4 + kTileN * 4 + 16 + kTileN * 4;
+         kTileN * 4 + 16;
 }
 
 bool gemm_shape_ok(size_t n_in) { return n_in && (n_in + 31) / 32 <= (size_t)kMaxBlocks; }
+
+// The largest activation spread s = e − emin of a GEMM column on this tensor: every term
+// |D·2^s·M| < 2^(30 + s + kspread) (|D| < 2^19, |M| < 2^(11 + kspread)), and nb <= 2^lg of
+// them stay below 2^62.  gemm_supported keeps it at 2 or more.
+static int gemm_max_shift(const GemmLayout &lay) {
+  int lg = 0;
+  while ((1 << lg) < lay.nb) lg++;
+  return std::max(0, std::min(kMaxShift, 32 - lay.kspread - lg));
+}
 
 bool gemm_supported(const GemmLayout &lay) {
   // |D·2^s·M| < 2^(33 + kspread) per block; nb of them stay inside i64
@@ -1151,7 +1171,7 @@ static cudaError_t launch_gemm_main(const GemvPlan &pl, const uint8_t *pack,
                                     const GemmLayout &lay, size_t n_out, size_t n_in,
                                     size_t n_cols, const int8_t *codes, size_t ld,
                                     const uint8_t *exps, size_t ldb, const WorkView &w,
-                                    int ksplit, long long *out_q32, float *out_f32,
+                                    Split sp, long long *out_q32, float *out_f32,
                                     unsigned long long *status, cudaStream_t stream);
 
 cudaError_t launch_gemm_q8_0(const GemvPlan &pl, const uint8_t *pack, const GemmLayout &lay,
@@ -1161,8 +1181,8 @@ cudaError_t launch_gemm_q8_0(const GemvPlan &pl, const uint8_t *pack, const Gemm
                              unsigned long long *status, int sm_count, cudaStream_t stream) {
   if (n_cols == 0 || n_out == 0) return cudaSuccess;
   const size_t tiles = gemm_tiles(n_out, n_cols);
-  const int ksplit = gemm_ksplit(tiles, (int)(lay.kp / kSlab), sm_count);
-  const WorkView w = work_view(work, n_cols, lay.nb, lay.kp, tiles, ksplit);
+  const Split ksplit = gemm_split(tiles, (int)(lay.kp / kSlab), sm_count);
+  const WorkView w = work_view(work, n_cols, lay.nb, lay.kp, sm_count);
   PrepArgs pa;
   pa.codes = codes;
   pa.exps = exps;
@@ -1175,6 +1195,7 @@ cudaError_t launch_gemm_q8_0(const GemvPlan &pl, const uint8_t *pack, const Gemm
   pa.n_cols = (int)n_cols;
   pa.w = w;
   pa.status = status;
+  pa.max_shift = gemm_max_shift(lay);
   gemm_prep_kernel<<<(unsigned)cols_pad(n_cols), 256, 0, stream>>>(pa);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
@@ -1187,11 +1208,12 @@ static cudaError_t launch_gemm_main(const GemvPlan &pl, const uint8_t *pack,
                                     const GemmLayout &lay, size_t n_out, size_t n_in,
                                     size_t n_cols, const int8_t *codes, size_t ld,
                                     const uint8_t *exps, size_t ldb, const WorkView &w,
-                                    int ksplit, long long *out_q32, float *out_f32,
+                                    Split sp, long long *out_q32, float *out_f32,
                                     unsigned long long *status, cudaStream_t stream) {
   cudaError_t e;
-  CUtensorMap map_x;
-  if (!make_map(&map_x, w.bcodes, lay.kp, kPlanes * cols_pad(n_cols), lay.kp, kTileN))
+  CUtensorMap map_x, map_s;
+  if (!make_map(&map_x, w.bcodes, lay.kp, cols_pad(n_cols), lay.kp, kTileN) ||
+      !make_table_map(&map_s, w.shift, cols_pad(n_cols), lay.kp / 32, kTileN))
     return cudaErrorInvalidValue;
   GemmArgs a;
   a.wmul = lay.wmul;
@@ -1207,7 +1229,9 @@ static cudaError_t launch_gemm_main(const GemvPlan &pl, const uint8_t *pack,
   a.kslabs = (int)(lay.kp / kSlab);
   a.m_tiles = (int)((n_out + kTileM - 1) / kTileM);
   a.tiles = a.m_tiles * (int)((n_cols + kTileN - 1) / kTileN);
-  a.ksplit = ksplit;
+  a.full = sp.full;
+  a.ksplit = sp.ks;
+  a.pieces = sp.pieces(a.tiles);
   a.part = w.part;
   a.cnt = w.cnt;
   a.geo = PackGeo{pack, pl.units, pl.L};
@@ -1220,9 +1244,9 @@ static cudaError_t launch_gemm_main(const GemvPlan &pl, const uint8_t *pack,
   e = cudaFuncSetAttribute(gemm_q8_0_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem);
   if (e != cudaSuccess) return e;
-  gemm_q8_0_kernel<<<(unsigned)(a.tiles * ksplit + kFallbackCtas), kThreads, smem, stream>>>(
+  gemm_q8_0_kernel<<<(unsigned)(a.pieces + kFallbackCtas), kThreads, smem, stream>>>(
       *reinterpret_cast<const CUtensorMap *>(lay.map), map_x,
-      *reinterpret_cast<const CUtensorMap *>(lay.map_m), a);
+      *reinterpret_cast<const CUtensorMap *>(lay.map_m), map_s, a);
   return cudaGetLastError();
 }
 
@@ -1238,8 +1262,8 @@ cudaError_t launch_gemm_q8_0_f32(const GemvPlan &pl, const uint8_t *pack, const 
   if (n_cols == 0 || n_out == 0) return cudaSuccess;
   if (!gemm_f32_ok(n_in, x, ldx)) return cudaErrorInvalidValue;
   const size_t tiles = gemm_tiles(n_out, n_cols);
-  const int ksplit = gemm_ksplit(tiles, (int)(lay.kp / kSlab), sm_count);
-  const WorkView w = work_view(work, n_cols, lay.nb, lay.kp, tiles, ksplit);
+  const Split ksplit = gemm_split(tiles, (int)(lay.kp / kSlab), sm_count);
+  const WorkView w = work_view(work, n_cols, lay.nb, lay.kp, sm_count);
   QPrepArgs qa;
   qa.x = x;
   qa.ldx = ldx;
@@ -1249,6 +1273,7 @@ cudaError_t launch_gemm_q8_0_f32(const GemvPlan &pl, const uint8_t *pack, const 
   qa.n_cols = (int)n_cols;
   qa.w = w;
   qa.status = status;
+  qa.max_shift = gemm_max_shift(lay);
   const size_t smem = lay.kp + lay.kp / 32;
   gemm_quant_prep_kernel<<<(unsigned)cols_pad(n_cols), 256, smem, stream>>>(qa);
   cudaError_t e = cudaGetLastError();
