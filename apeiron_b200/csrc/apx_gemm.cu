@@ -842,11 +842,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (!ok) atomicExch(timeout, 1);
-    // ---- finish: acc·2^(kmin_r + emin_c) rounded to Q32.32 and to f32 ----
-    // The stage ring is idle once every epilogue warp is past its last read (named barrier
-    // 1).  Phase A: each thread rounds its 32 tokens into a [token][row] tile in shared
-    // memory.  Phase B: each warp stores whole token rows (128 rows of one token are
-    // contiguous in the output) with 16-byte stores.
+    // ---- finish: acc·2^(kmin_r + emin_c) rounded to Q32.32 and to f32, stored by each thread
+    // (a split tile first meets its partial sums in L2) ----
     const int ew = warp - 2;
     bool all_ok = __all_sync(0xFFFFFFFFu, ok);
     if (ks > 1) {
@@ -873,13 +870,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (threadIdx.x == 64) g.cnt[stile] = 0;  // ready for the next call
       }
     }
-    asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
-    float *sf = reinterpret_cast<float *>(smem);                      // [64 tokens][128 rows]
-    long long *sv = reinterpret_cast<long long *>(smem + 32 * 1024);  // [64 tokens][128 rows]
     if (all_ok) {
-      // 32 independent chains side by side (the conversions are long-latency).  The tokens'
-      // exponents are read up front: read inside the loop, each would wait for the previous
-      // iteration's shared-memory stores.
+      // The outputs straight from registers: for each token the warp's 32 lanes hold 32
+      // consecutive rows, so each token's store is one coalesced segment of the column-major
+      // output (128 bytes of f32, 256 of Q32.32).  The tokens' exponents are read up front.
       const unsigned kmin = kmin_row;
       const bool live = row < g.n_out;
       uint32_t bad = 0;  // bit j: token j's output leaves i64
@@ -892,9 +886,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         ev[j + 2] = e4.z;
         ev[j + 3] = e4.w;
       }
+      float *of = g.out_f32 ? g.out_f32 + (size_t)(n0 + c0) * g.n_out + row : nullptr;
+      long long *oq = g.out_q32 ? g.out_q32 + (size_t)(n0 + c0) * g.n_out + row : nullptr;
       // Tokens off the GEMM route (e < 0) are never stored.  When every other token's shift
       // kmin + e lies in [32, 64), the loop below has no call in it (the general case is out of
-      // line, and a call site would keep the 32 chains from interleaving).
+      // line, and a call site would keep the chains from interleaving).
       int emn = 1 << 20, emx = -1;
 #pragma unroll
       for (int j = 0; j < kEpiTok; j++)
@@ -910,9 +906,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int hi = (int)(acc[j] >> 32);
           const long long v = (long long)((unsigned long long)acc[j] << (t & 31));
           const float f = __ll2float_rn(acc[j]) * __int_as_float((int)(t + 95) << 23);
-          const bool fits = e < 0 || (hi >> (31 - (t & 31))) == (hi >> 31);
-          sf[(c0 + j) * kTileM + rl] = e >= 0 && fits ? f : __int_as_float(0x7FC00000);
-          if (g.out_q32) sv[(c0 + j) * kTileM + rl] = e >= 0 && fits ? v : 0;
+          const bool fits = (hi >> (31 - (t & 31))) == (hi >> 31);
+          if (e >= 0 && live) {
+            if (of) of[(size_t)j * g.n_out] = fits ? f : __int_as_float(0x7FC00000);
+            if (oq) oq[(size_t)j * g.n_out] = fits ? v : 0;
+          }
           bad |= (e >= 0 && live && !fits) ? 1u << j : 0u;
         }
       } else {
@@ -922,8 +920,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           long long v;
           float f;
           const bool fits = finish_fast(acc[j], kmin + (unsigned)e, v, f);
-          sf[(c0 + j) * kTileM + rl] = fits ? f : __int_as_float(0x7FC00000);
-          if (g.out_q32) sv[(c0 + j) * kTileM + rl] = fits ? v : 0;
+          if (e >= 0 && live) {
+            if (of) of[(size_t)j * g.n_out] = fits ? f : __int_as_float(0x7FC00000);
+            if (oq) oq[(size_t)j * g.n_out] = fits ? v : 0;
+          }
           bad |= (e >= 0 && live && !fits) ? 1u << j : 0u;
         }
       }
@@ -931,38 +931,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int j = __ffs(bad) - 1;
         bad &= bad - 1;
         atomicMin(g.status + (size_t)(n0 + c0 + j) * 2, pack_status(row, kKindOutputOverflow, 0));
-      }
-    }
-    asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
-    if (__all_sync(0xFFFFFFFFu, all_ok)) {
-      const int rows = (int)min((size_t)kTileM, g.n_out - (size_t)m0);
-      const bool full_rows = rows == kTileM;
-      for (int tok = ew; tok < kTileN; tok += kEpiWarps) {
-        if (stok[tok] < 0) continue;  // warp-uniform
-        const size_t base = (size_t)(n0 + tok) * g.n_out + m0;
-        const int r = 4 * lane;
-        if (g.out_f32) {
-          const float4 f4 = *reinterpret_cast<const float4 *>(sf + tok * kTileM + r);
-          float *dst = g.out_f32 + base + r;
-          if (full_rows && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-            *reinterpret_cast<float4 *>(dst) = f4;
-          } else {
-            const float fv[4] = {f4.x, f4.y, f4.z, f4.w};
-            for (int u = 0; u < 4; u++)
-              if (r + u < rows) dst[u] = fv[u];
-          }
-        }
-        if (g.out_q32) {
-          const long long *src = sv + tok * kTileM + r;
-          long long *dst = g.out_q32 + base + r;
-          if (full_rows && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-            reinterpret_cast<longlong2 *>(dst)[0] = reinterpret_cast<const longlong2 *>(src)[0];
-            reinterpret_cast<longlong2 *>(dst)[1] = reinterpret_cast<const longlong2 *>(src)[1];
-          } else {
-            for (int u = 0; u < 4; u++)
-              if (r + u < rows) dst[u] = src[u];
-          }
-        }
       }
     }
   }
