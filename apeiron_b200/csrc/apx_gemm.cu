@@ -286,8 +286,8 @@ static Split gemm_split(size_t tiles, int kslabs, int sm_count) {
   return Split{(int)(tiles - rem), ks};
 }
 
-// One i64 accumulator per split tile, zero between calls (the finishing split clears it), at a
-// fixed place right after the counters: room for sm_count split tiles (a launch splits fewer).
+// The split tiles' partial sums: one tile's worth per split CTA, and a launch has at most
+// sm_count of them.
 static size_t part_bytes(int sm_count) {
   return (size_t)std::max(sm_count, 1) * kTileM * kTileN * sizeof(long long);
 }
@@ -335,6 +335,11 @@ size_t gemm_work_bytes(size_t n_cols, size_t n_in, size_t n_out, int sm_count) {
 
 // ---- activation prep: describe, route, B operand, shift table --------------------------------
 
+// The GEMM's split-K arrival counters, zero before every launch.
+__device__ __forceinline__ void zero_counters(const WorkView &w) {
+  for (int i = threadIdx.x; i < (int)(kCntBytes / 4); i += blockDim.x) w.cnt[i] = 0;
+}
+
 // A column the GEMM does not take (padding token, refused or checked): zero codes and shifts.
 __device__ __forceinline__ void zero_column(const WorkView &w, int c, size_t np, size_t kp) {
   for (size_t j = (size_t)threadIdx.x * 16; j < kp; j += (size_t)blockDim.x * 16)
@@ -358,6 +363,7 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(PrepArgs a) {
   __shared__ unsigned s_m128, s_route;
   const int c = blockIdx.x;
   const size_t np = cols_pad((size_t)a.n_cols);
+  if (c == 0) zero_counters(a.w);
   if (c >= a.n_cols) {  // padding tokens of the last tile: zero codes and shifts
     zero_column(a.w, c, np, a.kp);
     if (threadIdx.x == 0) {
@@ -486,6 +492,7 @@ __global__ void __launch_bounds__(256) gemm_quant_prep_kernel(QPrepArgs a) {
   __shared__ unsigned s_route;
   const int c = blockIdx.x;
   const size_t np = cols_pad((size_t)a.n_cols);
+  if (c == 0) zero_counters(a.w);
   if (c >= a.n_cols) {  // padding tokens of the last tile: zero codes and shifts
     zero_column(a.w, c, np, a.kp);
     if (threadIdx.x == 0) {
@@ -618,14 +625,33 @@ struct GemmArgs {
   // contiguous range of slabs: their exact i64 partial sums meet in `part`, and the last to
   // arrive (per split tile counter) finishes.  pieces = full + (tiles - full)·ksplit.
   int full, ksplit, pieces;
-  long long *part;  // [tiles - full][kEpiWarps][kEpiTok tokens][32 lanes], zero between calls
-  int *cnt;         // [tiles - full], zero between calls
+  long long *part;  // [tiles - full][ksplit][kEpiWarps][kEpiTok tokens][32 lanes]
+  int *cnt;         // [tiles - full] arrivals, zeroed by the prep kernel
   // checked route (matvec_fixed per row) of the columns the prep kernel listed
   PackGeo geo;
   const int8_t *codes;
   const uint8_t *exps;
   size_t ld, ldb, n_in;
 };
+
+// Bounded wait until *p >= target (acquire at GPU scope): kWaitLimit polls or about one
+// second, like mbar_wait; false when it gives up.
+__device__ __forceinline__ bool wait_count(const int *p, int target) {
+  unsigned long long t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (int it = 0; it < kWaitLimit; it++) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    if (v >= target) return true;
+    __nanosleep(64);
+    if ((it & 63) == 63) {
+      unsigned long long now;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+      if (now - t0 > 1000000000ull) return false;
+    }
+  }
+  return false;
+}
 
 __device__ __forceinline__ void checked_columns(const GemmArgs g) {
   volatile int32_t *fb = g.w.fb;
@@ -847,27 +873,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ew = warp - 2;
     bool all_ok = __all_sync(0xFFFFFFFFu, ok);
     if (ks > 1) {
-      // add this split's partial sums into the tile's accumulator in L2 (exact: i64 addition
-      // wraps, and the true sum fits); the last split of the tile to arrive reads the sum,
-      // leaves the accumulator zero for the next call and finishes, the rest are done
-      unsigned long long *sum = reinterpret_cast<unsigned long long *>(g.part) +
-                                ((size_t)stile * kEpiWarps + ew) * (kEpiTok * 32);
+      // Split K: every split stores its partial sums (coalesced), arrives on the tile's
+      // counter and waits (bounded) until all ks have; then the splits share the finish: split
+      // p takes the token quarters q with q % ks == p and adds the other splits' partials to
+      // its own (exact: i64 addition wraps and the true sum fits).  The splits of a launch
+      // never outnumber the SMs and a CTA fills its SM, so they are all resident together.
+      // The prep kernel zeroes the counters before every launch.
+      long long *mine =
+          g.part + (((size_t)stile * ks + split) * kEpiWarps + ew) * (kEpiTok * 32);
 #pragma unroll
-      for (int j = 0; j < kEpiTok; j++) atomicAdd(sum + j * 32 + lane, (unsigned long long)acc[j]);
+      for (int j = 0; j < kEpiTok; j++) mine[j * 32 + lane] = acc[j];
       __threadfence();
       asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
-      if (threadIdx.x == 64) *sflag = atomicAdd(g.cnt + stile, 1) == ks - 1;
+      if (threadIdx.x == 64) {
+        atomicAdd(g.cnt + stile, 1);
+        const bool all_in = wait_count(g.cnt + stile, ks);
+        if (!all_in) atomicExch(timeout, 1);
+        *sflag = all_in;
+      }
       asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
-      const bool last = *sflag != 0;
-      if (!last) all_ok = false;  // another split of this tile finishes
-      if (last) {
+      if (*sflag == 0 || tq % ks != split) {
+        all_ok = false;  // another split finishes these tokens (or the wait gave up)
+      } else {
         __threadfence();
+        for (int sp = 0; sp < ks; sp++) {
+          if (sp == split) continue;
+          const long long *other =
+              g.part + (((size_t)stile * ks + sp) * kEpiWarps + ew) * (kEpiTok * 32);
 #pragma unroll
-        for (int j = 0; j < kEpiTok; j++) {
-          acc[j] = (long long)__ldcg(sum + j * 32 + lane);
-          sum[j * 32 + lane] = 0ull;
+          for (int j = 0; j < kEpiTok; j++) acc[j] += __ldcg(other + j * 32 + lane);
         }
-        if (threadIdx.x == 64) g.cnt[stile] = 0;  // ready for the next call
       }
     }
     if (all_ok) {
