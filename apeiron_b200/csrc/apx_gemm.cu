@@ -40,6 +40,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstdint>
 #include <cstring>
 #include <mutex>
@@ -363,6 +364,7 @@ __global__ void __launch_bounds__(256) gemm_prep_kernel(PrepArgs a) {
   __shared__ unsigned s_m128, s_route;
   const int c = blockIdx.x;
   const size_t np = cols_pad((size_t)a.n_cols);
+  pdl_launch_dependents();  // the GEMM may start its weight loads now
   if (c == 0) zero_counters(a.w);
   if (c >= a.n_cols) {  // padding tokens of the last tile: zero codes and shifts
     zero_column(a.w, c, np, a.kp);
@@ -492,6 +494,7 @@ __global__ void __launch_bounds__(256) gemm_quant_prep_kernel(QPrepArgs a) {
   __shared__ unsigned s_route;
   const int c = blockIdx.x;
   const size_t np = cols_pad((size_t)a.n_cols);
+  pdl_launch_dependents();  // the GEMM may start its weight loads now
   if (c == 0) zero_counters(a.w);
   if (c >= a.n_cols) {  // padding tokens of the last tile: zero codes and shifts
     zero_column(a.w, c, np, a.kp);
@@ -686,6 +689,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                      const __grid_constant__ CUtensorMap map_m,
                      const __grid_constant__ CUtensorMap map_s, GemmArgs g) {
   if ((int)blockIdx.x >= g.pieces) {
+    pdl_wait();  // the prep kernel's list and codes
     checked_columns(g);
     return;
   }
@@ -747,12 +751,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_m)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_s)) : "memory");
   }
-  if (threadIdx.x >= 64 && threadIdx.x < 64 + kTileN) {
-    const int c = n0 + (int)threadIdx.x - 64;
-    const unsigned rw = c < g.n_cols ? g.w.route[c] : kRouteNone;
-    const bool gemm_col = (rw & 0xFFu) == kRouteGemm;
-    stok[threadIdx.x - 64] = gemm_col ? g.w.emin[c] : -1;
-  }
   if (warp == 1) {  // TMEM: kBufs × kBufCols columns of 32-bit accumulators
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_addr(tmem_slot)),
@@ -764,6 +762,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // The weight codes and their M table are the tensor's, constant since its upload: the first
+  // stages' loads of them go out before the wait for the prep kernel (programmatic dependent
+  // launch).  Everything the prep kernel writes is read after the wait.
+  constexpr uint32_t kStageTx = kStageA + kStageB + kStageM + kStageS;
+  const int pre = min(nk, kStages);
+  if (threadIdx.x == 0) {
+    for (int lk = 0; lk < pre; lk++) {
+      uint8_t *base = stage_a(lk);
+      mbar_expect_tx(full + lk, kStageTx);
+      tma_load_2d(base, &map_w, (kt0 + lk) * kSlab, m0, full + lk);
+      tma_load_2d(base + kStageA + kStageB, &map_m, m0, (kt0 + lk) * (kSlab / 32), full + lk);
+    }
+  }
+  pdl_wait();
+  if (threadIdx.x >= 64 && threadIdx.x < 64 + kTileN) {
+    const int c = n0 + (int)threadIdx.x - 64;
+    const unsigned rw = c < g.n_cols ? g.w.route[c] : kRouteNone;
+    const bool gemm_col = (rw & 0xFFu) == kRouteGemm;
+    stok[threadIdx.x - 64] = gemm_col ? g.w.emin[c] : -1;
+  }
+  __syncthreads();
 
   if (warp == 0) {
     // ---- TMA producer (lane 0 issues): per slab W, the codes, M and s ----
@@ -777,10 +796,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           stop = 1;
         } else {
           uint8_t *base = stage_a(st);
-          mbar_expect_tx(full + st, kStageA + kStageB + kStageM + kStageS);
-          tma_load_2d(base, &map_w, kt * kSlab, m0, full + st);
+          if (lk >= pre) {  // the first stages' W and M went out before the wait
+            mbar_expect_tx(full + st, kStageTx);
+            tma_load_2d(base, &map_w, kt * kSlab, m0, full + st);
+            tma_load_2d(base + kStageA + kStageB, &map_m, m0, kt * (kSlab / 32), full + st);
+          }
           tma_load_2d(base + kStageA, &map_x, kt * kSlab, n0, full + st);
-          tma_load_2d(base + kStageA + kStageB, &map_m, m0, kt * (kSlab / 32), full + st);
           tma_load_2d(base + kStageA + kStageB + kStageM, &map_s, n0, kt * (kSlab / 32),
                       full + st);
           issued++;
@@ -1247,10 +1268,24 @@ static cudaError_t launch_gemm_main(const GemvPlan &pl, const uint8_t *pack,
   e = cudaFuncSetAttribute(gemm_q8_0_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem);
   if (e != cudaSuccess) return e;
-  gemm_q8_0_kernel<<<(unsigned)(a.pieces + kFallbackCtas), kThreads, smem, stream>>>(
-      *reinterpret_cast<const CUtensorMap *>(lay.map), map_x,
-      *reinterpret_cast<const CUtensorMap *>(lay.map_m), map_s, a);
-  return cudaGetLastError();
+  // programmatic dependent launch after the prep kernel (unless APX_PDL=0)
+  static const bool pdl = [] {
+    const char *v = std::getenv("APX_PDL");
+    return !(v && v[0] == '0');
+  }();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(a.pieces + kFallbackCtas));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, gemm_q8_0_kernel,
+                            *reinterpret_cast<const CUtensorMap *>(lay.map), map_x,
+                            *reinterpret_cast<const CUtensorMap *>(lay.map_m), map_s, a);
 }
 
 bool gemm_f32_ok(size_t n_in, const float *x, size_t ldx) {
