@@ -134,6 +134,47 @@ def test_checked_route_columns(be):
     check_matmat(be, raw, n_out, n_in, qs)
 
 
+def test_activation_spreads_through_the_fold(be):
+    """GEMM columns whose block exponents lie 3..11 above their smallest: the fold shifts each
+    block's dot by s before its multiply-add (12 takes the checked rows).  Rows whose codes are
+    all -128 or all 127 against codes of ±127 make the shifted dots reach their int32 bound
+    (32·128·127·2^11 < 2^31); the other rows hold every code."""
+    n_out, n_in, k = 256, 1024, 12
+    raw = random_payload(Q8_0, n_out, n_in, 0x3000, 0, 21)
+    blk = raw.reshape(n_out, -1, 34)
+    blk[:16, :, 2:] = 0x80
+    blk[16:32, :, 2:] = 0x7F
+    rng = np.random.default_rng(21)
+    nb = n_in // 32
+    qs = []
+    for c in range(k):
+        s = np.full(nb, 1 << 8, np.int64)
+        s[rng.choice(nb, 5, replace=False)] = 1 << (8 + 3 + c % 10)   # spreads 3..12
+        if c % 3 == 2:
+            codes = rng.integers(-127, 128, n_in).astype(np.int8)
+        else:
+            codes = np.full(n_in, 127 if c % 3 else -127, np.int8)
+        qs.append(QuantAct.from_parts(s, codes))
+    check_matmat(be, raw, n_out, n_in, qs)
+
+
+def test_weight_spread_bounds_the_activation_shift(be):
+    """Rows whose block scales span 2^20 (f16 2^-14 beside 64): the i64 fold then allows an
+    activation spread of at most 32 − 20 − log2(nb) = 7 on this tensor, so columns at 6 and 7
+    take the GEMM and 8 the checked rows; all equal the oracle."""
+    n_out, n_in, k = 192, 1024, 6
+    raw = random_payload(Q8_0, n_out, n_in, 0x0400, 0, 22)
+    raw.reshape(n_out, -1, 34)[:, 1::2, 0:2] = (0x00, 0x54)
+    rng = np.random.default_rng(22)
+    nb = n_in // 32
+    qs = []
+    for spread in (6, 7, 8, 7, 6, 8):
+        s = np.full(nb, 1 << 20, np.int64)
+        s[rng.choice(nb, 3, replace=False)] = 1 << (20 + spread)
+        qs.append(QuantAct.from_parts(s, rng.integers(-127, 128, n_in).astype(np.int8)))
+    check_matmat(be, raw, n_out, n_in, qs)
+
+
 def test_refusals_lowest_column(be):
     """FixedOverflow and OutputOverflow in different columns: the lowest refusing column
     decides, and within it the first row in row order."""
