@@ -857,6 +857,11 @@ static bool pdl_enabled() {
   return on;
 }
 
+// Set while a launch is captured behind a copy (a graph edge from a copy node cannot be
+// programmatic): launches from this thread then go without the attribute.
+static thread_local bool tl_pdl_suppressed = false;
+void set_pdl_suppressed(bool on) { tl_pdl_suppressed = on; }
+
 template <typename Kern, typename Args>
 static cudaError_t launch_cfg(Kern kern, const GemvPlan &pl, const Args &a, cudaStream_t stream) {
   if (pl.smem > 48 * 1024) {
@@ -873,7 +878,7 @@ static cudaError_t launch_cfg(Kern kern, const GemvPlan &pl, const Args &a, cuda
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = pdl_enabled() && !tl_pdl_suppressed ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 

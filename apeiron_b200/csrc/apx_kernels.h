@@ -117,6 +117,9 @@ cudaError_t launch_gemm_q8_0_f32(const GemvPlan &pl, const uint8_t *pack, const 
                                  unsigned long long *status, int sm_count, cudaStream_t stream);
 
 
+// GEMV launches from the calling thread go without programmatic dependent launch while set.
+void set_pdl_suppressed(bool on);
+
 // Debug: exact int32 group dots from the repacked layout (apx_gemv.cu).
 cudaError_t launch_block_dots(const GemvPlan &pl, uint32_t type, const uint8_t *pack,
                               size_t n_out, size_t n_in, const int8_t *codes, int32_t *dots,
