@@ -22,6 +22,7 @@ APX_ERR_FIXED_OVERFLOW = 7
 APX_ERR_ACCUMULATOR_OVERFLOW = 8
 APX_ERR_OUTPUT_OVERFLOW = 9
 APX_ERR_QUANT_REFUSED = 10
+APX_ERR_SWIGLU_REFUSED = 11
 APX_ERR_INVALID_ARGUMENT = 20
 APX_ERR_LAYOUT_MISMATCH = 21
 APX_ERR_CUDA = 22
@@ -42,7 +43,9 @@ EXPORTS = [
     "apx_matvec_f32_noalloc", "apx_matmat_f32", "apx_quant_f32_cols_async",
     "apx_peer_alloc", "apx_peer_open", "apx_peer_close", "apx_device_read",
     "apx_gather_publish_async", "apx_matvec_gather_async", "apx_matvec_group_async",
+    "apx_swiglu_quant_async", "apx_ffn_status_decode",
 ]
+CARRIER_F32, CARRIER_Q32 = 0, 1
 
 MAX_PEERS = 8
 MAX_GATHER_PROJ = 4
@@ -124,6 +127,8 @@ _SIGS = {
     "apx_matmat_f32_async": (C.c_int, [P, U64, SZ, SZ, SZ, P, SZ, P, P, P, P]),
     "apx_act_padded_len": (SZ, [SZ]),
     "apx_status_decode": (C.c_int, [P, U64, C.POINTER(CallStatus), EP]),
+    "apx_swiglu_quant_async": (C.c_int, [P, P, P, SZ, C.c_int, P, P, P, P, P, P]),
+    "apx_ffn_status_decode": (C.c_int, [C.POINTER(CallStatus), EP]),
     "apx_matvec_f32_noalloc": (C.c_int, [P, U64, SZ, SZ, P, P, P, P]),
     "apx_matmat_f32": (C.c_int, [P, U64, SZ, SZ, SZ, P, P, EP]),
     "apx_quant_f32_cols_async": (C.c_int, [P, P, SZ, SZ, P, P, P, P]),

@@ -1,0 +1,278 @@
+// apx_ffn.cu — the FFN hidden activation on the device: h = SwiGLU(gate, up) under the engine's
+// carrier, then quant_act(h) for the down projection (the SwiGLU and quantization stages of
+// fused_ffn_task, src/engine/chart/ffn.rs:1577-1594), so the projections of a decode step chain
+// on the GPU without a host round trip.
+//
+// Carriers (swiglu_one_carrier, ffn.rs:246-284):
+//   F32 (the engine's default): g = from_q32(gate), u = from_q32(up) (RN(x)/2^32, fp.rs:176-178),
+//       h = to_q32(silu(g)·u) with silu(x) = x / (1 + exp(-x)) in binary32 and exp the reference's
+//       Cephes-style polynomial (mixer/f32_carrier.rs:262-375); every operation one IEEE binary32
+//       rounding (the __f*_rn intrinsics: never contracted), Overflow where h leaves Q32.32;
+//   Q32: h = round_shift_32(silu_fixed(gate)·up) (ops/silu.rs:53-100 on fixed_exp,
+//       numeric/fixed_exp.rs:1-184), Overflow where h leaves i64.
+// quant_act (chart/mod.rs:258-334) then runs per 32-lane block as in the column quantizer.
+//
+// One warp per 32-lane block, eight blocks per CTA; each CTA leaves its descriptor statistics in
+// a small workspace and a one-CTA kernel merges them into the descriptor, so no state outlives
+// the call.  The lowest refusing lane reaches the status word by atomicMin (lane in the row
+// field), which is the reference's first-refusal order.
+#include <climits>
+
+#include "apx_common.cuh"
+#include "apx_kernels.h"
+#include "apx_quant.cuh"
+
+namespace apx {
+
+typedef __int128 i128;
+
+constexpr int kFfnWarps = 8;
+constexpr int kFfnOverflow = 3;  // FfnError::Overflow (ops/ffn.rs:23-24)
+constexpr long long kOne = 1ll << 32;
+
+// ---- Q32 carrier ---------------------------------------------------------------------------
+
+// round(v / 2^32), half away from zero (fixed_exp.rs round_div_2p32).
+__device__ __forceinline__ i128 rdiv_2p32(i128 v) {
+  const i128 half = (i128)1 << 31;
+  return v >= 0 ? (v + half) >> 32 : -((-v + half) >> 32);
+}
+
+// fixed_exp: x = k·ln2 + r (k = round(x·log2 e), the product rounded at 2^64), the degree-7
+// Taylor polynomial in r by Horner with each step rounded at 2^32, then a shift by k.  The
+// constants are the reference's Q32.32 values of ln 2, 1/ln 2 and 1/i!.  false: out of range.
+__device__ bool fixed_exp_dev(long long x, long long &out) {
+  if (x < -16 * kOne || x > 21 * kOne) return false;
+  const i128 prod = (i128)x * (i128)6196328019ll;
+  const i128 sh = (prod + ((i128)1 << 63)) >> 64;
+  const long long k = (long long)sh;  // |x| <= 21·2^32: |k| <= 31
+  const long long r = x - (long long)((i128)k * (i128)2977044472ll);
+  const long long c[8] = {852176, 5965232, 35791394, 178956971, 715827883,
+                          2147483648ll, 4294967296ll, 4294967296ll};
+  i128 acc = c[0];
+#pragma unroll
+  for (int i = 1; i < 8; i++) acc = rdiv_2p32(acc * (i128)r) + c[i];
+  i128 v;
+  if (k >= 0) {
+    v = acc << k;
+  } else {
+    const int n = (int)-k;
+    v = (acc + ((i128)1 << (n - 1))) >> n;
+  }
+  if (v > (i128)LLONG_MAX || v < (i128)LLONG_MIN) return false;
+  out = (long long)v;
+  return true;
+}
+
+// silu_fixed: v >= 16 -> v, v <= -21 -> 0, else sign(v)·round(|v|·2^32 / (2^32 + e^-v)) with ties
+// upward (value.rs:5-7).  In that window the denominator is positive and the quotient at most
+// |v|, so only fixed_exp could refuse (it cannot for |v| < 21).  0 or the FfnError kind.
+__device__ int silu_fixed_dev(long long v, long long &out) {
+  if (v >= 16 * kOne) {
+    out = v;
+    return 0;
+  }
+  if (v <= -21 * kOne) {
+    out = 0;
+    return 0;
+  }
+  long long e;
+  if (!fixed_exp_dev(-v, e)) return 1;  // ExpOutOfRange
+  const long long den = kOne + e;
+  const i128 mag = v < 0 ? -(i128)v : (i128)v;
+  const i128 q = (mag * (i128)kOne + (i128)(den / 2)) / (i128)den;
+  out = (long long)(v < 0 ? -q : q);
+  return 0;
+}
+
+// ---- F32 carrier ---------------------------------------------------------------------------
+
+// exp_f32_scalar: the reference's binary32 exp (range reduction by n = rint(x·log2 e) with ln 2
+// split in two, a degree-5 polynomial, and the scale 2^n applied in two halves), one rounding
+// per operation.  The constants are its bit patterns.
+__device__ __forceinline__ float exp_ref(float x) {
+  if (x != x) return __int_as_float(0x7fc00000);
+  if (x < __int_as_float((int)0xc2b00000u)) return 0.0f;
+  if (x > __int_as_float(0x42b17218)) return __int_as_float(0x7f800000);
+  const float z = __fmul_rn(x, __int_as_float(0x3fb8aa3b));
+  const float n_flt = rintf(z);
+  const int n_int = (int)n_flt;
+  const float r = __fsub_rn(__fsub_rn(x, __fmul_rn(n_flt, __int_as_float(0x3f318000))),
+                            __fmul_rn(n_flt, __int_as_float((int)0xb95e8083u)));
+  const float r2 = __fmul_rn(r, r);
+  float p = __int_as_float(0x39506967);
+  p = __fadd_rn(__fmul_rn(p, r), __int_as_float(0x3ab743ce));
+  p = __fadd_rn(__fmul_rn(p, r), __int_as_float(0x3c088908));
+  p = __fadd_rn(__fmul_rn(p, r), __int_as_float(0x3d2aa9c1));
+  p = __fadd_rn(__fmul_rn(p, r), __int_as_float(0x3e2aaaaa));
+  p = __fadd_rn(__fmul_rn(p, r), __int_as_float(0x3f000000));
+  const float y = __fadd_rn(__fadd_rn(1.0f, r), __fmul_rn(r2, p));
+  const int n1 = n_int >> 1, n2 = n_int - n1;
+  return __fmul_rn(__fmul_rn(y, __int_as_float((n1 + 127) << 23)),
+                   __int_as_float((n2 + 127) << 23));
+}
+
+// swiglu_one under the carrier: 0 (h set) or the FfnError kind.
+__device__ int swiglu_dev(long long gate, long long up, int carrier, long long &h) {
+  if (carrier == APX_CARRIER_F32) {
+    const float g = __fmul_rn(__ll2float_rn(gate), 0x1p-32f);
+    const float u = __fmul_rn(__ll2float_rn(up), 0x1p-32f);
+    const float s = __fdiv_rn(g, __fadd_rn(1.0f, exp_ref(-g)));
+    const float prod = __fmul_rn(s, u);
+    return f32_to_q32(prod, h) ? 0 : kFfnOverflow;  // false for non-finite or out of range
+  }
+  long long s;
+  const int rc = silu_fixed_dev(gate, s);
+  if (rc) return rc;
+  const i128 v = ((i128)s * (i128)up + ((i128)1 << 31)) >> 32;  // round_shift_32
+  if (v > (i128)LLONG_MAX || v < (i128)LLONG_MIN) return kFfnOverflow;
+  h = (long long)v;
+  return 0;
+}
+
+// ---- kernels -------------------------------------------------------------------------------
+
+struct FfnArgs {
+  const long long *gate, *up;
+  long long *h;  // or null
+  int8_t *codes;
+  uint8_t *exps;
+  size_t n;
+  int carrier;
+  int4 *part;                  // per CTA: emin, emax, status, nz
+  unsigned long long *status;  // the first refusing lane
+};
+
+__global__ void __launch_bounds__(32 * kFfnWarps) swiglu_quant_kernel(FfnArgs a) {
+  __shared__ int s_emin, s_emax, s_status;
+  __shared__ unsigned s_nz;
+  if (threadIdx.x == 0) {
+    s_emin = 1 << 30;
+    s_emax = -1;
+    s_status = APX_OK;
+    s_nz = 0;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const size_t nb = (a.n + 31) / 32;
+  const size_t b = (size_t)blockIdx.x * kFfnWarps + warp;
+  if (b < nb) {  // warp-uniform
+    const size_t j = b * 32 + lane;
+    long long v = 0;
+    bool ok = true;
+    if (j < a.n) {
+      const int rc = swiglu_dev(__ldg(a.gate + j), __ldg(a.up + j), a.carrier, v);
+      if (rc) {
+        ok = false;
+        v = 0;
+        atomicMin(a.status, pack_status(j, APX_ERR_SWIGLU_REFUSED, (unsigned)rc));
+      }
+      if (a.h) a.h[j] = v;
+    }
+    // quant_act of the block: absmax, S = 2^e, codes rounded half away from zero
+    unsigned long long mx = uabs64(v);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long t = __shfl_xor_sync(0xFFFFFFFFu, mx, o);
+      mx = t > mx ? t : mx;
+    }
+    const int e = act_scale_exp(mx);  // warp-uniform
+    // a refused SwiGLU lane leaves h undefined: the activation is refused as a whole
+    int w_status = __any_sync(0xFFFFFFFFu, !ok) ? (int)APX_ERR_QUANT_REFUSED : (int)APX_OK;
+    int code = 0;
+    if (e == 99) {
+      w_status = APX_ERR_QUANT_REFUSED;
+    } else if (e >= 0) {
+      const unsigned long long m = uabs64(v);
+      const unsigned long long S = 1ull << e, q = m >> e, r = m & (S - 1);
+      const unsigned long long mag = q + (2 * r >= S ? 1ull : 0ull);
+      code = v < 0 ? -(int)mag : (int)mag;
+      if (__any_sync(0xFFFFFFFFu, mag > 127 || !product_fits(code, e)))
+        w_status = APX_ERR_QUANT_REFUSED;
+    }
+    if (j < a.n) a.codes[j] = (int8_t)code;
+    if (lane == 0) {
+      a.exps[b] = e < 0 || e == 99 ? (uint8_t)APX_EXP_ZERO : (uint8_t)e;
+      if (w_status != APX_OK) atomicMax(&s_status, w_status);
+      if (e >= 0 && e != 99) {
+        atomicMin(&s_emin, e);
+        atomicMax(&s_emax, e);
+        atomicAdd(&s_nz, 1u);
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) a.part[blockIdx.x] = make_int4(s_emin, s_emax, s_status, (int)s_nz);
+}
+
+// The descriptor from the CTAs' statistics (one CTA).
+__global__ void __launch_bounds__(256) ffn_desc_kernel(const int4 *part, int nparts, size_t n,
+                                                       ActDesc *desc) {
+  int emin = 1 << 30, emax = -1, status = APX_OK;
+  unsigned nz = 0;
+  for (int i = threadIdx.x; i < nparts; i += blockDim.x) {
+    const int4 p = part[i];
+    emin = min(emin, p.x);
+    emax = max(emax, p.y);
+    status = max(status, p.z);
+    nz += (unsigned)p.w;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    emin = min(emin, __shfl_xor_sync(0xFFFFFFFFu, emin, o));
+    emax = max(emax, __shfl_xor_sync(0xFFFFFFFFu, emax, o));
+    status = max(status, __shfl_xor_sync(0xFFFFFFFFu, status, o));
+    nz += __shfl_xor_sync(0xFFFFFFFFu, nz, o);
+  }
+  __shared__ int4 w[8];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (lane == 0) w[warp] = make_int4(emin, emax, status, (int)nz);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < (int)(blockDim.x / 32); i++) {
+      emin = min(emin, w[i].x);
+      emax = max(emax, w[i].y);
+      status = max(status, w[i].z);
+      nz += (unsigned)w[i].w;
+    }
+    ActDesc r;
+    r.status = status;
+    r.emin = emax >= 0 ? emin : 0;
+    r.emax = emax;
+    r.n_in = (int32_t)n;
+    r.nz = nz;
+    r.pad[0] = 0;  // quant_act codes are never -128
+    r.pad[1] = 0;
+    r.pad[2] = 0;
+    *desc = r;
+  }
+}
+
+size_t swiglu_work_bytes(size_t n) {
+  return ((n + 31) / 32 + kFfnWarps - 1) / kFfnWarps * sizeof(int4);
+}
+
+cudaError_t launch_swiglu_quant(const long long *gate, const long long *up, size_t n, int carrier,
+                                long long *h, int8_t *codes, uint8_t *exps, void *desc,
+                                unsigned long long *status, void *work, cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  const size_t nb = (n + 31) / 32;
+  const unsigned grid = (unsigned)((nb + kFfnWarps - 1) / kFfnWarps);
+  FfnArgs a;
+  a.gate = gate;
+  a.up = up;
+  a.h = h;
+  a.codes = codes;
+  a.exps = exps;
+  a.n = n;
+  a.carrier = carrier;
+  a.part = static_cast<int4 *>(work);
+  a.status = status;
+  swiglu_quant_kernel<<<grid, 32 * kFfnWarps, 0, stream>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  ffn_desc_kernel<<<1, 256, 0, stream>>>(a.part, (int)grid, n, static_cast<ActDesc *>(desc));
+  return cudaGetLastError();
+}
+
+}  // namespace apx

@@ -117,6 +117,13 @@ cudaError_t launch_gemm_q8_0_f32(const GemvPlan &pl, const uint8_t *pack, const 
                                  unsigned long long *status, int sm_count, cudaStream_t stream);
 
 
+// The FFN hidden activation (apx_ffn.cu): SwiGLU under the carrier, then quant_act; `work` holds
+// swiglu_work_bytes(n).
+size_t swiglu_work_bytes(size_t n);
+cudaError_t launch_swiglu_quant(const long long *gate, const long long *up, size_t n, int carrier,
+                                long long *h, int8_t *codes, uint8_t *exps, void *desc,
+                                unsigned long long *status, void *work, cudaStream_t stream);
+
 // GEMV launches from the calling thread go without programmatic dependent launch while set.
 void set_pdl_suppressed(bool on);
 

@@ -130,6 +130,7 @@ struct apx_ctx {
   DevBuf scratch;  // device-side quantization scratch of the f32 path
   DevBuf gwork;    // GEMM per-call workspace (its head zeroed whenever it is reallocated)
   DevBuf ascratch; // codes / exps / descriptors of apx_matmat_f32_async off the fused route
+  DevBuf fwork;    // per-CTA statistics of apx_swiglu_quant_async
   HostBuf host;    // pinned mirror of `dev`
 };
 
@@ -477,6 +478,7 @@ void apx_close(apx_ctx *ctx) {
   ctx->scratch.release();
   ctx->gwork.release();
   ctx->ascratch.release();
+  ctx->fwork.release();
   ctx->host.release();
   cudaStreamDestroy(ctx->stream);
   delete ctx;
@@ -1009,6 +1011,43 @@ int apx_matmat_f32_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_i
                       (unsigned long long *)&d_status[c].first, st);
   }
   return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
+}
+
+int apx_swiglu_quant_async(apx_ctx *ctx, const int64_t *d_gate, const int64_t *d_up, size_t n,
+                           int carrier, int64_t *d_h, int8_t *d_codes, uint8_t *d_exps,
+                           apx_act_desc *d_desc, apx_call_status *d_status, void *stream) {
+  if (!ctx || !d_desc || !d_status || (n && (!d_gate || !d_up || !d_codes || !d_exps)) ||
+      (carrier != APX_CARRIER_F32 && carrier != APX_CARRIER_Q32))
+    return APX_ERR_INVALID_ARGUMENT;
+  if (n > (size_t)INT32_MAX) return APX_ERR_TOO_LARGE;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  if (ctx->fwork.ensure(swiglu_work_bytes(n)) != cudaSuccess) return APX_ERR_OUT_OF_MEMORY;
+  if (n == 0) {
+    // the empty activation: an all-zero descriptor, as the quantizers write it
+    ActDesc d{};
+    d.emax = -1;
+    return cudaMemcpyAsync(d_desc, &d, sizeof d, cudaMemcpyHostToDevice, (cudaStream_t)stream) ==
+                   cudaSuccess && cudaStreamSynchronize((cudaStream_t)stream) == cudaSuccess
+               ? APX_OK
+               : APX_ERR_CUDA;
+  }
+  const cudaError_t e = launch_swiglu_quant(
+      (const long long *)d_gate, (const long long *)d_up, n, carrier, (long long *)d_h, d_codes,
+      d_exps, d_desc, (unsigned long long *)&d_status->first, ctx->fwork.p, (cudaStream_t)stream);
+  return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
+}
+
+int apx_ffn_status_decode(const apx_call_status *status, apx_err *err) {
+  if (!status) return set_err(err, APX_ERR_INVALID_ARGUMENT);
+  const unsigned long long w = status->first;
+  if (w == ~0ull) return set_err(err, APX_OK);
+  const int code = (int)((w >> 16) & 0xFF);
+  set_err(err, code);
+  if (err) {
+    err->row = w >> 24;
+    err->bits = (uint32_t)(w & 0xFFFF);
+  }
+  return code;
 }
 
 int apx_status_decode(apx_ctx *ctx, uint64_t tensor, const apx_call_status *status,

@@ -63,6 +63,7 @@ typedef enum apx_status {
   APX_ERR_ACCUMULATOR_OVERFLOW = 8, /* AccumulatorOverflow                          */
   APX_ERR_OUTPUT_OVERFLOW = 9,      /* OutputOverflow                               */
   APX_ERR_QUANT_REFUSED = 10,       /* quant_act / f32_to_fixed returned None       */
+  APX_ERR_SWIGLU_REFUSED = 11,      /* SwiGLU refused lane `row` (bits: FfnError kind, 3 = Overflow) */
   /* Backend conditions with no reference counterpart. */
   APX_ERR_INVALID_ARGUMENT = 20,    /* null pointer, unknown handle, bad size       */
   APX_ERR_LAYOUT_MISMATCH = 21,     /* call geometry differs from the upload's      */
@@ -217,6 +218,25 @@ APX_API int apx_matmat_f32_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, si
                                  size_t k_cols, const float *d_x, size_t ldx,
                                  int64_t *d_out_q32, float *d_out_f32,
                                  apx_call_status *d_status, void *stream);
+/* The FFN hidden activation between gate/up and down (replaces the SwiGLU and quantization
+ * stages of fused_ffn_task, src/engine/chart/ffn.rs:1577-1594): h_i = swiglu(gate_i, up_i) under
+ * the carrier (APX_CARRIER_F32: SiLU in binary32 with the reference's exp, the engine's default,
+ * mixer/f32_carrier.rs:262-375; APX_CARRIER_Q32: silu_fixed on fixed_exp in Q32.32,
+ * ops/silu.rs:53), then quant_act(h) into codes / exponent bytes / descriptor laid out as
+ * apx_quant_f32_async writes them (d_codes zero beyond n, as for the other quantizers).  d_h
+ * (optional) receives h.  d_status (all ones on entry) receives the lowest refusing lane
+ * (decode with apx_ffn_status_decode); the descriptor then refuses the activation, so a
+ * projection that reads it refuses too.  Shares a context workspace with the other calls of
+ * its context, which must not overlap in time. */
+#define APX_CARRIER_F32 0
+#define APX_CARRIER_Q32 1
+APX_API int apx_swiglu_quant_async(apx_ctx *ctx, const int64_t *d_gate, const int64_t *d_up,
+                                   size_t n, int carrier, int64_t *d_h, int8_t *d_codes,
+                                   uint8_t *d_exps, apx_act_desc *d_desc,
+                                   apx_call_status *d_status, void *stream);
+/* A host copy of apx_swiglu_quant_async's status word into err (APX_OK, or
+ * APX_ERR_SWIGLU_REFUSED with the lane in err->row and the FfnError kind in err->bits). */
+APX_API int apx_ffn_status_decode(const apx_call_status *status, apx_err *err);
 /* Several projections that read the same device activation (q/k/v of a layer, gate/up of a
  * FFN), each over its whole tensor: out[i] = matvec(tensors[i], x), refusal word in
  * d_status[i] (all ones on entry).  Up to APX_MAX_GROUP tensors of one family whose layout

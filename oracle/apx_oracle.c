@@ -13,6 +13,7 @@
  */
 #include "apx_oracle.h"
 
+#include <math.h>
 #include <pthread.h>
 #include <stdlib.h>
 #include <string.h>
@@ -766,3 +767,139 @@ int apxo_matmat_q8act_mt(uint32_t t, const uint8_t *raw, size_t raw_len, size_t 
                          const int64_t *scales, int threads, int64_t *out, apx_err *err) {
   return run_mt(t, raw, raw_len, n_out, n_in, k_cols, codes, scales, threads, out, err);
 }
+
+/* ---- the FFN hidden activation: SwiGLU under either carrier ----------------------------- */
+
+/* fixed_exp (src/numeric/fixed_exp.rs:1-184): e^x in Q32.32 for x in [-16, 21]: x = k·ln2 + r
+ * with k = round(x·log2(e)) (Q32.32 constants LN2 = 2977044472, 1/LN2 = 6196328019, product
+ * rounded at 2^64), the degree-7 Taylor polynomial in r by Horner with each step rounded
+ * (half away from zero) at 2^32, then a shift by k (rounded right shifts for k < 0).
+ * 0 ok, 1 OutOfRange. */
+static i128 rdiv_2p32(i128 v) {
+  const i128 half = (i128)1 << 31;
+  return v >= 0 ? (v + half) >> 32 : -((-v + half) >> 32);
+}
+
+int apxo_fixed_exp(int64_t x, int64_t *out) {
+  const int64_t one = (int64_t)1 << 32;
+  if (x < -16 * one || x > 21 * one) return 1;
+  const i128 prod = (i128)x * (i128)6196328019LL;
+  const i128 sh = (prod + ((i128)1 << 63)) >> 64;
+  if (sh > (i128)INT64_MAX || sh < (i128)INT64_MIN) return 1;
+  const int64_t k = (int64_t)sh;
+  const i128 kl = (i128)k * (i128)2977044472LL;
+  if (kl > (i128)INT64_MAX || kl < (i128)INT64_MIN) return 1;
+  const i128 r = (i128)(x - (int64_t)kl);
+  static const int64_t c[8] = {852176, 5965232, 35791394, 178956971, 715827883,
+                               2147483648LL, 4294967296LL, 4294967296LL};
+  i128 acc = c[0];
+  for (int i = 1; i < 8; i++) acc = rdiv_2p32(acc * r) + c[i];
+  i128 v;
+  if (k >= 0) {
+    if (k >= 64) return 1;
+    v = acc << k;
+  } else {
+    const uint64_t n = (uint64_t)(-k);
+    if (n >= 64) {
+      *out = 0;
+      return 0;
+    }
+    v = (acc + ((i128)1 << (n - 1))) >> n;
+  }
+  if (v > (i128)INT64_MAX || v < (i128)INT64_MIN) return 1;
+  *out = (int64_t)v;
+  return 0;
+}
+
+/* silu_fixed (src/engine/ops/silu.rs:53-100): v >= 16 -> v, v <= -21 -> 0, else
+ * sign(v)·div_round_nearest(|v|·2^32, 2^32 + fixed_exp(-v)) (value.rs:5-7, ties upward).
+ * 0 ok, else the FfnError kind (1 ExpOutOfRange, 2 ZeroDenominator, 3 Overflow). */
+int apxo_silu_fixed(int64_t v, int64_t *out) {
+  const int64_t one = (int64_t)1 << 32;
+  if (v >= 16 * one) {
+    *out = v;
+    return 0;
+  }
+  if (v <= -21 * one) {
+    *out = 0;
+    return 0;
+  }
+  int64_t e;
+  if (apxo_fixed_exp(-v, &e)) return 1;
+  int64_t den;
+  if (__builtin_add_overflow(one, e, &den)) return 3;
+  if (den <= 0) return 2;
+  const i128 mag = v < 0 ? -(i128)v : (i128)v;
+  const i128 num = mag * (i128)one;
+  const i128 q = (num + (i128)den / 2) / (i128)den;
+  const i128 sgn = v < 0 ? -q : q;
+  if (sgn > (i128)INT64_MAX || sgn < (i128)INT64_MIN) return 3;
+  *out = (int64_t)sgn;
+  return 0;
+}
+
+/* exp_f32_scalar (src/engine/mixer/f32_carrier.rs:262-324): Cephes-style binary32 exp, every
+ * operation one IEEE binary32 rounding (no contraction: this file builds with
+ * -ffp-contract=off).  Bits in, bits out. */
+static float f32_of(uint32_t b) {
+  float f;
+  memcpy(&f, &b, 4);
+  return f;
+}
+static uint32_t bits_of(float f) {
+  uint32_t b;
+  memcpy(&b, &f, 4);
+  return b;
+}
+
+static float exp_ref(float x) {
+  if (x != x) return f32_of(0x7fc00000u);
+  if (x < f32_of(0xc2b00000u)) return 0.0f;
+  if (x > f32_of(0x42b17218u)) return f32_of(0x7f800000u);
+  const float z = x * f32_of(0x3fb8aa3bu);
+  const float n_flt = rintf(z);
+  const int32_t n_int = (int32_t)n_flt;
+  const float r = (x - n_flt * f32_of(0x3f318000u)) - n_flt * f32_of(0xb95e8083u);
+  const float r2 = r * r;
+  float p = f32_of(0x39506967u);
+  p = p * r + f32_of(0x3ab743ceu);
+  p = p * r + f32_of(0x3c088908u);
+  p = p * r + f32_of(0x3d2aa9c1u);
+  p = p * r + f32_of(0x3e2aaaaau);
+  p = p * r + f32_of(0x3f000000u);
+  const float y = (1.0f + r) + (r2 * p);
+  const int32_t n1 = n_int >> 1, n2 = n_int - n1;
+  const float s1 = f32_of((uint32_t)(n1 + 127) << 23), s2 = f32_of((uint32_t)(n2 + 127) << 23);
+  return (y * s1) * s2;
+}
+
+uint32_t apxo_exp_f32(uint32_t x) { return bits_of(exp_ref(f32_of(x))); }
+
+/* silu_f32_scalar (f32_carrier.rs:372-375): x / (1 + exp(-x)). */
+uint32_t apxo_silu_f32(uint32_t x) {
+  const float f = f32_of(x);
+  return bits_of(f / (1.0f + exp_ref(-f)));
+}
+
+/* swiglu_one under a carrier (src/engine/chart/ffn.rs:246-284):
+ *   carrier 0 (F32): to_q32(silu(from_q32(gate)) · from_q32(up)), from_q32(x) = RN(x)/2^32
+ *     (fp.rs:176-178); Overflow where the product is not finite or leaves Q32.32;
+ *   carrier 1 (Q32): round_shift_32(silu_fixed(gate) · up) narrowed to i64, else Overflow.
+ * 0 ok, else the FfnError kind (3 Overflow). */
+int apxo_swiglu(int64_t gate, int64_t up, int carrier, int64_t *out) {
+  if (carrier == 0) {
+    const float g = (float)gate * 0x1p-32f, u = (float)up * 0x1p-32f;
+    const float s = g / (1.0f + exp_ref(-g));
+    const float prod = s * u;
+    if (!(prod - prod == 0.0f)) return 3;
+    return apxo_f32_to_q32(bits_of(prod), out) ? 3 : 0;
+  }
+  int64_t s;
+  const int rc = apxo_silu_fixed(gate, &s);
+  if (rc) return rc;
+  const i128 v = rs32((i128)s * (i128)up);
+  if (v > (i128)INT64_MAX || v < (i128)INT64_MIN) return 3;
+  *out = (int64_t)v;
+  return 0;
+}
+

@@ -91,6 +91,14 @@ int apxo_matmat_q8act_mt(uint32_t ggml_type, const uint8_t *raw, size_t raw_len,
                          const int8_t *codes, const int64_t *scales, int threads,
                          int64_t *out, apx_err *err);
 
+/* The FFN hidden activation (src/engine/chart/ffn.rs:246-284, ops/silu.rs:53-100,
+ * numeric/fixed_exp.rs:1-184, mixer/f32_carrier.rs:262-375). */
+int apxo_fixed_exp(int64_t x, int64_t *out);
+int apxo_silu_fixed(int64_t v, int64_t *out);
+uint32_t apxo_exp_f32(uint32_t x);
+uint32_t apxo_silu_f32(uint32_t x);
+int apxo_swiglu(int64_t gate, int64_t up, int carrier, int64_t *out);
+
 #ifdef __cplusplus
 }
 #endif

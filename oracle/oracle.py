@@ -70,6 +70,13 @@ def _declare(l):
     l.apxo_act_scale.argtypes = [C.c_uint64, C.POINTER(C.c_uint64)]
     l.apxo_finish.argtypes = [C.c_int64, C.c_uint32, C.POINTER(C.c_int64)]
     l.apxo_f32_to_q32.argtypes = [C.c_uint32, C.POINTER(C.c_int64)]
+    l.apxo_fixed_exp.argtypes = [C.c_int64, C.POINTER(C.c_int64)]
+    l.apxo_silu_fixed.argtypes = [C.c_int64, C.POINTER(C.c_int64)]
+    l.apxo_exp_f32.argtypes = [C.c_uint32]
+    l.apxo_exp_f32.restype = C.c_uint32
+    l.apxo_silu_f32.argtypes = [C.c_uint32]
+    l.apxo_silu_f32.restype = C.c_uint32
+    l.apxo_swiglu.argtypes = [C.c_int64, C.c_int64, C.c_int, C.POINTER(C.c_int64)]
     l.apxo_round_shift_32.argtypes = [C.c_int64, C.c_uint64, C.POINTER(C.c_int64),
                                       C.POINTER(C.c_uint64)]
     l.apxo_quant_act.argtypes = [P, SZ, P, P]
@@ -132,6 +139,59 @@ def round_shift_32(v: int) -> int:
     oh, ol = C.c_int64(), C.c_uint64()
     lib().apxo_round_shift_32(hi, lo, C.byref(oh), C.byref(ol))
     return (oh.value << 64) | ol.value
+
+
+# ---- the FFN hidden activation (SwiGLU) ------------------------------------------------
+
+FFN_OVERFLOW = 3     # FfnError::Overflow (ops/ffn.rs:23-24)
+CARRIER_F32, CARRIER_Q32 = 0, 1
+
+
+def fixed_exp(x: int):
+    """``fixed_exp`` (src/numeric/fixed_exp.rs:176-184): e^x in Q32.32, None out of range."""
+    v = C.c_int64()
+    return None if lib().apxo_fixed_exp(x, C.byref(v)) else v.value
+
+
+def silu_fixed(v: int):
+    """``silu_fixed`` (src/engine/ops/silu.rs:53): the Q32.32 value, or the FfnError kind as
+    ("err", kind)."""
+    o = C.c_int64()
+    rc = lib().apxo_silu_fixed(v, C.byref(o))
+    return ("err", rc) if rc else o.value
+
+
+def exp_f32(bits: int) -> int:
+    """``exp_f32_scalar`` (src/engine/mixer/f32_carrier.rs:291): binary32 bits in and out."""
+    return lib().apxo_exp_f32(bits)
+
+
+def silu_f32(bits: int) -> int:
+    """``silu_f32_scalar`` (f32_carrier.rs:372): binary32 bits in and out."""
+    return lib().apxo_silu_f32(bits)
+
+
+def swiglu(gate: int, up: int, carrier: int = CARRIER_F32):
+    """``swiglu_one_carrier`` (src/engine/chart/ffn.rs:279): h in Q32.32, or ("err", kind)."""
+    o = C.c_int64()
+    rc = lib().apxo_swiglu(gate, up, carrier, C.byref(o))
+    return ("err", rc) if rc else o.value
+
+
+def swiglu_quant(gate, up, carrier: int = CARRIER_F32):
+    """The SwiGLU and quantization stages of ``fused_ffn_task`` (chart/ffn.rs:1577-1594) over a
+    whole hidden vector: ("swiglu", lane, kind) for the lowest refusing lane, ("quant",) when
+    quant_act refuses h, else (h, codes, scales)."""
+    h = np.zeros(len(gate), dtype=np.int64)
+    for i, (g, u) in enumerate(zip(gate, up)):
+        r = swiglu(int(g), int(u), carrier)
+        if isinstance(r, tuple):
+            return ("swiglu", i, r[1])
+        h[i] = r
+    q = quant_act(h)
+    if q is None:
+        return ("quant",)
+    return (h,) + q
 
 
 # ---- activations -----------------------------------------------------------------

@@ -66,3 +66,17 @@ def test_gather_desc_layout_matches_header(tmp_path):
                                           check=True).stdout.split()]
     assert out[0] == C.sizeof(_abi.GatherDesc)
     assert out[1:] == [getattr(_abi.GatherDesc, f).offset for f in fields]
+
+
+def test_ffn_status_decode_without_a_device(libpath):
+    """apx_ffn_status_decode is host-only: all ones is OK; a SwiGLU refusal word carries the
+    lane in the row field and the FfnError kind (3 = Overflow) in the low bits."""
+    lib = _abi.load(libpath)
+    err = _abi.ApxErr()
+    ok = _abi.CallStatus((1 << 64) - 1, 0)
+    assert lib.apx_ffn_status_decode(ctypes.byref(ok), ctypes.byref(err)) == _abi.APX_OK
+    word = (1234 << 24) | (_abi.APX_ERR_SWIGLU_REFUSED << 16) | 3
+    st = _abi.CallStatus(word, 0)
+    assert lib.apx_ffn_status_decode(ctypes.byref(st), ctypes.byref(err)) == _abi.APX_ERR_SWIGLU_REFUSED
+    assert (err.code, err.row, err.bits) == (_abi.APX_ERR_SWIGLU_REFUSED, 1234, 3)
+    assert lib.apx_ffn_status_decode(None, ctypes.byref(err)) == _abi.APX_ERR_INVALID_ARGUMENT
