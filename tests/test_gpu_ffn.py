@@ -11,7 +11,7 @@ import pytest
 
 from oracle import oracle as O
 
-from apeiron_b200 import _abi
+from apeiron_b200 import _abi, synth
 from apeiron_b200.chart import Backend
 
 pytestmark = pytest.mark.gpu
@@ -110,3 +110,59 @@ def test_quant_refusal_without_swiglu_refusal(be):
     assert O.swiglu_quant(gate, up, _abi.CARRIER_Q32) == ("quant",)
     _, _, _, desc, (rc, _, _) = run(be, gate, up, _abi.CARRIER_Q32)
     assert rc == _abi.APX_OK and desc[0] == _abi.APX_ERR_QUANT_REFUSED
+
+
+@pytest.mark.parametrize("t,n_embd,n_ff,carrier", [(12, 896, 4864, _abi.CARRIER_F32),
+                                                    (8, 512, 1024, _abi.CARRIER_Q32)])
+def test_decode_ffn_chain_on_device(be, t, n_embd, n_ff, carrier):
+    """One decode FFN with nothing on the host between its stages: quant_act of x on the
+    device, gate and up as one grouped launch (Q32.32 outputs), SwiGLU + quant_act of h, then
+    the down projection reading that activation.  y equals the reference's chain
+    (matvec_q8act, swiglu_one_carrier, quant_act, matvec_q8act) computed by the oracle."""
+    import torch
+
+    lib = be.lib
+    dev = torch.device("cuda:0")
+    stream = torch.cuda.current_stream().cuda_stream
+    shapes = [(n_ff, n_embd), (n_ff, n_embd), (n_embd, n_ff)]
+    raws = [synth.payload(t, o, i, 60 + k) for k, (o, i) in enumerate(shapes)]
+    tens = [be.upload(t, r, o, i) for r, (o, i) in zip(raws, shapes)]
+    x = synth.activation_f32(n_embd, 3)
+    pad = lib.apx_act_padded_len(n_embd)
+    codes = torch.zeros(pad, dtype=torch.int8, device=dev)
+    exps = torch.full((pad // 32,), 0xFF, dtype=torch.uint8, device=dev)
+    desc = torch.zeros(8, dtype=torch.int32, device=dev)
+    dx = torch.from_numpy(x).to(dev)
+    assert lib.apx_quant_f32_async(be.ctx, dx.data_ptr(), n_embd, codes.data_ptr(),
+                                   exps.data_ptr(), desc.data_ptr(), stream) == 0
+    gu = [torch.zeros(n_ff, dtype=torch.int64, device=dev) for _ in range(2)]
+    gs = [torch.full((2,), -1, dtype=torch.int64, device=dev) for _ in range(2)]
+    handles = (C.c_uint64 * 2)(tens[0].handle, tens[1].handle)
+    optr = (C.c_void_p * 2)(*[o.data_ptr() for o in gu])
+    sptr = (C.c_void_p * 2)(*[s_.data_ptr() for s_ in gs])
+    assert lib.apx_matvec_group_async(be.ctx, handles, 2, n_embd, codes.data_ptr(),
+                                      exps.data_ptr(), desc.data_ptr(), optr, None, sptr,
+                                      stream) == 0
+    padh = lib.apx_act_padded_len(n_ff)
+    hc = torch.zeros(padh, dtype=torch.int8, device=dev)
+    he = torch.full((padh // 32,), 0xFF, dtype=torch.uint8, device=dev)
+    hd = torch.zeros(8, dtype=torch.int32, device=dev)
+    fs = torch.full((2,), -1, dtype=torch.int64, device=dev)
+    assert lib.apx_swiglu_quant_async(be.ctx, gu[0].data_ptr(), gu[1].data_ptr(), n_ff, carrier,
+                                      None, hc.data_ptr(), he.data_ptr(), hd.data_ptr(),
+                                      fs.data_ptr(), stream) == 0
+    y = torch.zeros(n_embd, dtype=torch.int64, device=dev)
+    ys = torch.full((2,), -1, dtype=torch.int64, device=dev)
+    assert lib.apx_matvec_async(be.ctx, tens[2].handle, n_embd, n_ff, hc.data_ptr(),
+                                he.data_ptr(), hd.data_ptr(), y.data_ptr(), None, ys.data_ptr(),
+                                stream) == 0
+    torch.cuda.synchronize()
+    for st in gs + [fs, ys]:
+        assert int(st[0].item()) == -1
+    c, sc = O.quant_act(synth.f32_to_q32(x))
+    g = O.matvec_q8act(t, raws[0], n_ff, n_embd, c, sc)
+    u = O.matvec_q8act(t, raws[1], n_ff, n_embd, c, sc)
+    assert np.array_equal(gu[0].cpu().numpy(), g) and np.array_equal(gu[1].cpu().numpy(), u)
+    h, hcodes, hscales = O.swiglu_quant(g, u, carrier)
+    want = O.matvec_q8act(t, raws[2], n_embd, n_ff, hcodes, hscales)
+    assert np.array_equal(y.cpu().numpy(), want)
