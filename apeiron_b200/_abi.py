@@ -31,6 +31,7 @@ APX_ERR_TOO_LARGE = 24
 APX_ERR_DEVICE_TIMEOUT = 25
 
 Q8_0, Q4_K, Q6_K = 8, 12, 14
+Q5_0 = 6  # served as Q8_0 (its codes widen exactly at upload)
 EXP_ZERO = 0xFF
 
 # Every symbol the header declares (tests/test_abi.py checks the library exports them).

@@ -29,7 +29,7 @@ import numpy as np
 from . import _abi
 
 ACT_QK = 32
-GEOM = {_abi.Q8_0: (32, 34), _abi.Q4_K: (256, 144), _abi.Q6_K: (256, 210)}
+GEOM = {_abi.Q5_0: (32, 22), _abi.Q8_0: (32, 34), _abi.Q4_K: (256, 144), _abi.Q6_K: (256, 210)}
 
 
 # ---- refusals (src/engine/ops/matvec.rs:11-48) ---------------------------------------

@@ -27,7 +27,8 @@ using namespace apx;
 namespace {
 
 struct Tensor {
-  uint32_t type = 0;
+  uint32_t type = 0;      // the family the kernels run (Q5_0 runs as Q8_0)
+  uint32_t src_type = 0;  // the uploaded ggml type: geometry and payload checks follow it
   size_t n_out = 0, n_in = 0, raw_len = 0, row_bytes = 0;
   uint8_t *d_pack = nullptr;
   size_t pack_bytes = 0;
@@ -97,6 +98,7 @@ size_t align16(size_t n) { return (n + 15) & ~(size_t)15; }
 bool geom(uint32_t t, size_t &qk, size_t &bb) {
   switch (t) {
     case APX_GGML_TYPE_Q8_0: qk = 32; bb = 34; return true;
+    case APX_GGML_TYPE_Q5_0: qk = 32; bb = 22; return true;
     case APX_GGML_TYPE_Q4_K: qk = 256; bb = 144; return true;
     case APX_GGML_TYPE_Q6_K: qk = 256; bb = 210; return true;
     default: return false;
@@ -187,7 +189,7 @@ HostAct describe_host(const int8_t *codes, size_t q_len, const uint8_t *exps) {
 int check_geometry(const Tensor &t, size_t n_out, size_t n_in, size_t q_len, bool chunked_order,
                    apx_err *err) {
   size_t qk, bb, row_bytes, need;
-  geom(t.type, qk, bb);
+  geom(t.src_type, qk, bb);
   auto shape = [&]() {
     set_err(err, APX_ERR_SHAPE_MISMATCH);
     if (err) {
@@ -280,6 +282,24 @@ void scan_nonfinite(Tensor &t, const uint8_t *raw) {
 
 // Synchronous single-column projection of host activations.
 // ha: the caller's describe_host of (codes, exps).
+// A Q5_0 block [f16 d][qh: 4 bytes][qs: 16 bytes] as the Q8_0 block [f16 d][32 int8 codes] of the
+// same weights (quant.rs:261-299 q5_0_codes): lane j < 16 is the low nibble of qs[j] with bit j of
+// qh as its fifth bit, lane 16 + j the high nibble with bit 16 + j, each offset by -16.  The
+// dequantized weights d·code are unchanged, so the Q8_0 kernels serve Q5_0 exactly.
+void widen_q5_0(const uint8_t *q5, uint8_t *q8) {
+  q8[0] = q5[0];
+  q8[1] = q5[1];
+  const uint32_t qh = (uint32_t)q5[2] | ((uint32_t)q5[3] << 8) | ((uint32_t)q5[4] << 16) |
+                      ((uint32_t)q5[5] << 24);
+  for (int j = 0; j < 16; j++) {
+    const unsigned nib = q5[6 + j];
+    const int lo = (int)((nib & 0xFu) | (((qh >> j) & 1u) << 4)) - 16;
+    const int hi = (int)((nib >> 4) | (((qh >> (16 + j)) & 1u) << 4)) - 16;
+    q8[2 + j] = (uint8_t)(int8_t)lo;
+    q8[2 + 16 + j] = (uint8_t)(int8_t)hi;
+  }
+}
+
 int matvec_sync(apx_ctx *ctx, Tensor &t, size_t n_out, size_t n_in, const int8_t *codes,
                 size_t q_len, const uint8_t *exps, const HostAct &ha, int64_t *out,
                 apx_err *err) {
@@ -508,13 +528,33 @@ int apx_tensor_upload(apx_ctx *ctx, uint32_t ggml_type, const uint8_t *raw, size
   }
   if (n_in > ((size_t)1 << 28) || n_out > ((size_t)1 << 36))
     return set_err(err, APX_ERR_TOO_LARGE);
+  // Q5_0 is served as Q8_0: its blocks widen to Q8_0 blocks of the same weights on the host
+  std::vector<uint8_t> widened;
+  uint32_t exec_type = ggml_type;
+  if (ggml_type == APX_GGML_TYPE_Q5_0) {
+    const size_t nb = (n_in + 31) / 32, wrow = nb * 34;
+    try {
+      widened.resize(n_out * wrow);
+    } catch (const std::bad_alloc &) {
+      return set_err(err, APX_ERR_OUT_OF_MEMORY);
+    }
+    for (size_t r = 0; r < n_out; r++)
+      for (size_t b = 0; b < nb; b++)
+        widen_q5_0(raw + r * row_bytes + b * 22, widened.data() + r * wrow + b * 34);
+    raw = widened.data();
+    row_bytes = wrow;
+    need = n_out * wrow;
+    exec_type = APX_GGML_TYPE_Q8_0;
+  }
   Tensor t;
-  t.type = ggml_type;
+  t.type = exec_type;
+  t.src_type = ggml_type;
   t.n_out = n_out;
   t.n_in = n_in;
   t.raw_len = raw_len;
   t.row_bytes = row_bytes;
   scan_nonfinite(t, raw);
+  ggml_type = exec_type;
   t.plan = plan_gemv(ggml_type, n_out, n_in, ctx->sm_count);
   t.pack_bytes = packed_bytes(t.plan, ggml_type);
   cudaError_t e;

@@ -10,7 +10,7 @@ and GgufField names.  `tensor_bytes` sizes a tensor as ceil(elements / block) bl
 (quant.rs:129-189) and checks it against the file's end.
 
 `ResidentModel` is the engine's one-time upload (src/engine/loader.rs:937-1020): the file is
-mapped once, and every two-dimensional tensor of a served family (Q8_0, Q4_K, Q6_K) is uploaded
+mapped once, and every two-dimensional tensor of a served family (Q5_0, Q8_0, Q4_K, Q6_K) is uploaded
 and repacked on the device, keyed by tensor index and name.  GGUF dims are (row length, rows):
 a projection's n_in is dims[0] and n_out dims[1].
 """
@@ -47,7 +47,7 @@ BLOCK_GEOM = {
     34: (256, (256 - 4 * 256 // 64) // 5 + 256 // 64 + 2),   # TQ1_0
     143: (128, (128 - 4 * 128 // 64) // 5 + 128 // 64 + 2),  # PTQ1_0
 }
-SERVED = (8, 12, 14)  # the families the device projections take (Q8_0, Q4_K, Q6_K)
+SERVED = (6, 8, 12, 14)  # the families the device projections take (Q5_0, Q8_0, Q4_K, Q6_K)
 
 # GgufField names (gguf.rs GgufField::name)
 F_KV_KEY, F_KV_TYPE, F_KV_VALUE = "kv key", "kv type", "kv value"

@@ -1,7 +1,8 @@
 /*
  * apeiron_cuda.h — C ABI of the B200 (sm_100a) backend for apeiron's integer
  * Q8-activation projection: the decode GEMV `matvec_q8act` and the prefill GEMM
- * `matmat_q8act` over GGUF Q8_0 / Q4_K / Q6_K weight payloads.
+ * `matmat_q8act` over GGUF Q8_0 / Q5_0 / Q4_K / Q6_K weight payloads (Q5_0 runs as Q8_0:
+ * its five-bit codes widen exactly at upload), and the FFN hidden activation between them.
  *
  * Every exact entry point returns, bit for bit, what the reference's CPU kernel
  * returns: `matvec_fixed(W, dequant(q))` in Q32.32 (`i64` words worth v / 2^32),
@@ -44,6 +45,7 @@ extern "C" {
 
 /* ggml type ids the backend serves (src/format/quant.rs:27-37). */
 #define APX_GGML_TYPE_Q8_0 8u
+#define APX_GGML_TYPE_Q5_0 6u  /* served as Q8_0: its codes widen exactly at upload */
 #define APX_GGML_TYPE_Q4_K 12u
 #define APX_GGML_TYPE_Q6_K 14u
 

@@ -228,6 +228,7 @@ int apxo_dequant_act(const int8_t *codes, size_t n, const int64_t *scales,
 static int geom(uint32_t t, size_t *qk, size_t *bb) {
   switch (t) {
     case APX_GGML_TYPE_Q8_0: *qk = 32; *bb = Q8_0_BYTES; return 1;
+    case APX_GGML_TYPE_Q5_0: *qk = 32; *bb = 22; return 1;
     case APX_GGML_TYPE_Q4_K: *qk = QK_K; *bb = Q4_K_BYTES; return 1;
     case APX_GGML_TYPE_Q6_K: *qk = QK_K; *bb = Q6_K_BYTES; return 1;
     default: return 0;
@@ -296,6 +297,21 @@ int apxo_dequant_row(uint32_t t, const uint8_t *row, size_t row_len, size_t n,
       if (apxo_f16_to_fixed(rd16(blk), &d)) return nonfinite(err, rd16(blk));
       for (size_t l = 0; l < take; l++) {
         if (mul_chk(d, (int8_t)blk[2 + l], &v, err)) return APX_ERR_FIXED_OVERFLOW;
+        out[pushed++] = v;
+      }
+    } else if (t == APX_GGML_TYPE_Q5_0) {
+      /* dequant_q5_0_row (num/dequant.rs:137-145, 357-390) on q5_0_codes (quant.rs:280-299):
+       * output j < 16 is the low nibble of qs[j] with qh bit j as its fifth bit, output
+       * 16 + j the high nibble with qh bit 16 + j; code - 16 times d */
+      int64_t d;
+      if (apxo_f16_to_fixed(rd16(blk), &d)) return nonfinite(err, rd16(blk));
+      const uint8_t *qh = blk + 2, *qs = blk + 6;
+      for (size_t l = 0; l < take; l++) {
+        const size_t j = l % 16;
+        const int hi = l >= 16;
+        const int bit = (qh[(hi ? 2 : 0) + j / 8] >> (j % 8)) & 1;
+        const int nib = hi ? (qs[j] >> 4) : (qs[j] & 0xF);
+        if (mul_chk(d, (int64_t)((nib | (bit << 4)) - 16), &v, err)) return APX_ERR_FIXED_OVERFLOW;
         out[pushed++] = v;
       }
     } else if (t == APX_GGML_TYPE_Q4_K) {

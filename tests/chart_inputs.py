@@ -7,7 +7,7 @@
 import numpy as np
 
 MASK = (1 << 64) - 1
-GEOM = {8: (32, 34), 12: (256, 144), 14: (256, 210)}
+GEOM = {6: (32, 22), 8: (32, 34), 12: (256, 144), 14: (256, 210)}
 
 
 def next_rand(state):
@@ -33,7 +33,7 @@ def random_payload(ggml_type, rows, n_in, d, dmin, seed):
     raw = (_stream(seed, rows * blocks * bb) & np.uint64(0xFF)).astype(np.uint8)
     for blk in range(rows * blocks):
         o = blk * bb
-        if ggml_type == 8:
+        if ggml_type in (6, 8):
             raw[o:o + 2] = (d & 0xFF, d >> 8)
         elif ggml_type == 12:
             raw[o:o + 2] = (d & 0xFF, d >> 8)
