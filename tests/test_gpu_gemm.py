@@ -355,3 +355,29 @@ def test_f32_sync_fused_matches_unfused(be):
         y = be.matmat_f32(t, x)
         for c in range(9):
             assert np.array_equal(y[c], be.matvec_f32(t, x[c])), (n_in, c)
+
+
+@pytest.mark.parametrize("t,n_out,n_in,k", [(Q8_0, 320, 450, 9), (12, 256, 512, 6),
+                                            (Q8_0, 128, 256, 3)])
+def test_f32_async_off_the_fused_route(be, t, n_out, n_in, k):
+    """apx_matmat_f32_async where the fused prep does not apply: a width that is not a multiple
+    of 4 (quantizer kernel, then the GEMM), a Q4_K tensor and a 3-column call (quantizer, then
+    one GEMV per column).  Each column equals apx_matvec_f32 of it."""
+    import torch
+
+    lib = be.lib
+    raw = synth.payload(t, n_out, n_in, 90 + n_in)
+    tens = be.upload(t, raw, n_out, n_in)
+    x = np.stack([synth.activation_f32(n_in, 300 + c) for c in range(k)])
+    dev = torch.device("cuda:0")
+    dx = torch.from_numpy(x).to(dev)
+    f32 = torch.zeros(k * n_out, dtype=torch.float32, device=dev)
+    status = torch.full((2 * k,), -1, dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.apx_matmat_f32_async(be.ctx, tens.handle, n_out, n_in, k, dx.data_ptr(), n_in,
+                                    None, f32.data_ptr(), status.data_ptr(), stream) == 0
+    torch.cuda.synchronize()
+    assert bool((status == -1).all().item())
+    y = f32.cpu().numpy().reshape(k, n_out)
+    for c in range(k):
+        assert np.array_equal(y[c], be.matvec_f32(tens, x[c])), c
