@@ -15,7 +15,9 @@ bench does the same with 256 MB of cycled copies (src/engine/chart/tests.rs:884-
            (CUDA events on the launching stream) against the measured HBM copy peak.
 
 `--impl reference` times the CPU restatement of the reference kernel (oracle/, the
-reference is Rust and cannot be built here) on all host threads, same metric.
+reference is Rust and cannot be built here) on all host threads, same metric: the
+reference's AVX2 / AVX-VNNI two-row decode cores and, for prefill, its k-column Q8_0
+AVX-VNNI GEMM (oracle/apx_oracle_x86.c), on a persistent host thread pool.
 Multi-GPU: replicas (independent decode streams per GPU, weak scaling), time = max over
 ranks.
 
@@ -66,9 +68,17 @@ PREFILL = [(8, 4864, 896), (8, 896, 4864)]
 PREFILL_TOKENS = 512
 
 
-def cpu_prefill_baseline(seconds=10.0, tokens=64):
-    """The prefill contract on the host cores: the oracle's threaded C port of matmat_q8act
-    (per-column matvec_q8act) on `tokens` of the 512 tokens of each shape, TOPS."""
+def cpu_isa():
+    from oracle import oracle as O
+
+    f = O.simd_features()
+    return "AVX-VNNI" if f["avxvnni"] else ("AVX2" if f["avx2"] else "scalar")
+
+
+def cpu_prefill_baseline(seconds=10.0, tokens=PREFILL_TOKENS):
+    """The prefill contract on the host cores: the oracle's restatement of the reference's
+    matmat_q8act, which runs the k-column Q8_0 GEMM with AVX-VNNI (kern/gemm.rs:498-580;
+    else the per-column vector rows), over `tokens` tokens of each shape, TOPS."""
     from apeiron_b200 import synth
     from oracle import oracle as O
 
@@ -86,14 +96,15 @@ def cpu_prefill_baseline(seconds=10.0, tokens=64):
     done, t0 = 0, time.perf_counter()
     while True:
         for t, raw, n_out, n_in, cs, ss in work:
-            O.matmat_q8act_mt(t, raw, n_out, n_in, cs, ss, threads)
+            r = O.matmat_q8act_mt(t, raw, n_out, n_in, cs, ss, threads, simd=True)
+            assert not isinstance(r, tuple)
         done += 1
         el = time.perf_counter() - t0
         if el >= seconds or done >= 1000:
             break
     return {"value": 2.0 * macs * done / el / 1e12, "unit": "TOPS", "cores": threads,
             "kind": "port", "sample": f"{done} passes of {tokens} tokens x both shapes "
-                                      f"({el:.1f} s), exact per-column contract"}
+                                      f"({el:.1f} s), {cpu_isa()} k-column GEMM restatement"}
 
 
 def measure_prefill(be, lib, dev, stream, steps, warmup, pg, local, world):
@@ -603,7 +614,7 @@ def cpu_passes(data, max_passes, max_seconds):
     t0 = time.perf_counter()
     while done < max_passes:
         for t, raw, n_out, n_in, c, s in data[done % len(data)]:
-            r = O.matvec_q8act_mt(t, raw, n_out, n_in, c, s, threads)
+            r = O.matvec_q8act_mt(t, raw, n_out, n_in, c, s, threads, simd=True)
             assert not isinstance(r, tuple)
             total += gemv_bytes(t, n_out, n_in)
         done += 1
@@ -618,7 +629,8 @@ def cpu_gemv_baseline(mats, seconds=10.0):
     total, done, el, threads = cpu_passes(data, 1 << 30, seconds)
     return {"value": total / el / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
             "sample": f"{done} passes of the workload over {copies} cycled host copies "
-                      f"(>= 256 MB, streamed from DRAM) in {el:.1f} s"}
+                      f"(>= 256 MB, streamed from DRAM) in {el:.1f} s, {cpu_isa()} "
+                      f"two-row decode cores"}
 
 
 def run_reference(args, world, rank, local, pg):
@@ -630,7 +642,7 @@ def run_reference(args, world, rank, local, pg):
     total, done, el, threads = cpu_passes(data, args.steps, 60.0)
     v = total / el / 1e9
     sample = (f"{done} of {args.steps} steps (capped at 60 s) over {copies} cycled host "
-              f"copies (>= 256 MB, streamed from DRAM)")
+              f"copies (>= 256 MB, streamed from DRAM), {cpu_isa()} two-row decode cores")
     line = {"metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus,
             "steps": done, "warmup": args.warmup, "ms_per_step": el * 1e3 / max(done, 1),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int64",

@@ -712,12 +712,63 @@ int apxo_block_dots(uint32_t t, const uint8_t *raw, size_t n_out, size_t n_in,
 /* ---- CPU baseline: the fused rows over contiguous row chunks on threads ------------
  * (the pool split of matvec_q8act_quant_chunked, src/engine/chart/ffn.rs:667-745). */
 
+/* The vector rows of apx_oracle_x86.c (the reference's AVX2 / AVX-VNNI row cores), one build
+ * per instruction set, and the f16 -> Q32.32 table they read (chart/portable.rs:15-79: the
+ * exact decode of every finite pattern, 1 for Inf/NaN; every finite decode is even). */
+typedef int (*x86_rows_fn)(uint32_t, const uint8_t *, size_t, size_t, size_t, size_t,
+                           const int8_t *, const int64_t *, const int32_t *, const int64_t *,
+                           int64_t *, size_t *);
+int apxo_x86_rows_avx2(uint32_t, const uint8_t *, size_t, size_t, size_t, size_t,
+                       const int8_t *, const int64_t *, const int32_t *, const int64_t *,
+                       int64_t *, size_t *);
+int apxo_x86_rows_vnni(uint32_t, const uint8_t *, size_t, size_t, size_t, size_t,
+                       const int8_t *, const int64_t *, const int32_t *, const int64_t *,
+                       int64_t *, size_t *);
+
+static int64_t f16_table[65536];
+static pthread_once_t f16_table_once = PTHREAD_ONCE_INIT;
+
+static void f16_table_build(void) {
+  for (uint32_t h = 0; h < 65536; h++) {
+    int64_t v;
+    f16_table[h] = apxo_f16_to_fixed((uint16_t)h, &v) ? 1 : v;
+  }
+}
+
+/* APXO_NO_VNNI=1 in the environment selects the AVX2 build on an AVX-VNNI host, so the tests
+ * check both builds against the scalar rows. */
+int apxo_simd_features(void) {
+  __builtin_cpu_init();
+  int f = 0;
+  if (__builtin_cpu_supports("avx2")) f |= 1;
+  const char *no_vnni = getenv("APXO_NO_VNNI");
+  if ((f & 1) && __builtin_cpu_supports("avxvnni") && !(no_vnni && no_vnni[0] == '1')) f |= 2;
+  return f;
+}
+
+static x86_rows_fn x86_rows(void) {
+  int f = apxo_simd_features();
+  if (!(f & 1)) return NULL;
+  pthread_once(&f16_table_once, f16_table_build);
+  return (f & 2) ? apxo_x86_rows_vnni : apxo_x86_rows_avx2;
+}
+
+/* The vector rows take Q8_0 on whole 32-lane blocks and Q4_K on whole super-blocks, as the
+ * reference's `tiled2` does (x86.rs:782-800); their byte dots also need every activation code
+ * in [-127, 127] (the |w|·sign(x, w) form), which quant_act guarantees. */
+static int x86_shape(uint32_t t, size_t n_in) {
+  return (t == APX_GGML_TYPE_Q8_0 && n_in % ACT_QK == 0) ||
+         (t == APX_GGML_TYPE_Q4_K && n_in % QK_K == 0);
+}
+
 typedef struct {
   uint32_t t;
   const uint8_t *raw;
   size_t row_bytes, lo, hi, n_in, k_cols, n_out;
   const int8_t *codes;
   const int64_t *scales;
+  const int32_t *xsums; /* [k_cols][n_in / 32], vector rows only */
+  x86_rows_fn vec;      /* NULL: the scalar fast rows */
   int64_t *out;
   int rc;
   size_t bad;
@@ -727,16 +778,108 @@ static void *mt_run(void *arg) {
   mt_task *a = (mt_task *)arg;
   size_t nb = (a->n_in + ACT_QK - 1) / ACT_QK;
   a->rc = 0;
-  for (size_t c = 0; c < a->k_cols && a->rc == 0; c++)
-    a->rc = fast_rows(a->t, a->raw, a->row_bytes, a->lo, a->hi, a->n_in,
-                      a->codes + c * a->n_in, a->scales + c * nb, a->out + c * a->n_out,
-                      &a->bad);
+  for (size_t c = 0; c < a->k_cols && a->rc == 0; c++) {
+    if (a->vec)
+      a->rc = a->vec(a->t, a->raw, a->row_bytes, a->lo, a->hi, a->n_in,
+                     a->codes + c * a->n_in, a->scales + c * nb,
+                     a->xsums ? a->xsums + c * nb : NULL, f16_table, a->out + c * a->n_out,
+                     &a->bad);
+    else
+      a->rc = fast_rows(a->t, a->raw, a->row_bytes, a->lo, a->hi, a->n_in,
+                        a->codes + c * a->n_in, a->scales + c * nb, a->out + c * a->n_out,
+                        &a->bad);
+  }
   return NULL;
 }
 
+/* A persistent pool of host threads, as the reference's decode runs its row chunks on a
+ * global pool started once (src/engine/chart/pool.rs): workers are created on first use (and
+ * added when a call asks for more), sleep on a condition variable between jobs and take task
+ * i of a job; the calling thread runs task 0.  One job at a time.  A forked child starts with
+ * no workers (pthread_atfork), since only the forking thread exists there. */
+#define POOL_MAX 256
+static pthread_mutex_t pool_job = PTHREAD_MUTEX_INITIALIZER;
+static pthread_mutex_t pool_mu = PTHREAD_MUTEX_INITIALIZER;
+static pthread_cond_t pool_go = PTHREAD_COND_INITIALIZER;
+static pthread_cond_t pool_done = PTHREAD_COND_INITIALIZER;
+static int pool_size, pool_pending, pool_ntasks;
+static unsigned long pool_gen;
+static void (*pool_fn)(void *, int);
+static void *pool_ctx;
+static pthread_once_t pool_fork_once = PTHREAD_ONCE_INIT;
+
+static void pool_after_fork(void) {
+  pthread_mutex_init(&pool_job, NULL);
+  pthread_mutex_init(&pool_mu, NULL);
+  pthread_cond_init(&pool_go, NULL);
+  pthread_cond_init(&pool_done, NULL);
+  pool_size = pool_pending = pool_ntasks = 0;
+  pool_fn = NULL;
+}
+
+static void pool_register_fork(void) { pthread_atfork(NULL, NULL, pool_after_fork); }
+
+static unsigned long pool_born[POOL_MAX + 1]; /* the job count when worker i was created */
+
+static void *pool_worker(void *arg) {
+  int me = (int)(intptr_t)arg;
+  pthread_mutex_lock(&pool_mu);
+  unsigned long seen = pool_born[me];
+  for (;;) {
+    while (pool_gen == seen) pthread_cond_wait(&pool_go, &pool_mu);
+    seen = pool_gen;
+    int run = me < pool_ntasks;
+    void (*fn)(void *, int) = pool_fn;
+    void *ctx = pool_ctx;
+    pthread_mutex_unlock(&pool_mu);
+    if (run) fn(ctx, me);
+    pthread_mutex_lock(&pool_mu);
+    if (--pool_pending == 0) pthread_cond_signal(&pool_done);
+  }
+  return NULL;
+}
+
+/* Runs fn(ctx, i) for i in [0, n) on the pool and the calling thread; returns when all are
+ * done. */
+static void pool_run(void (*fn)(void *, int), void *ctx, int n) {
+  pthread_once(&pool_fork_once, pool_register_fork);
+  pthread_mutex_lock(&pool_job);
+  pthread_mutex_lock(&pool_mu);
+  while (pool_size < n - 1) { /* workers 1 .. n-1 */
+    pthread_t tid;
+    pthread_attr_t at;
+    pthread_attr_init(&at);
+    pthread_attr_setdetachstate(&at, PTHREAD_CREATE_DETACHED);
+    pool_born[pool_size + 1] = pool_gen;
+    if (pthread_create(&tid, &at, pool_worker, (void *)(intptr_t)(pool_size + 1)) != 0) {
+      pthread_attr_destroy(&at);
+      break;
+    }
+    pthread_attr_destroy(&at);
+    pool_size++;
+  }
+  int workers = pool_size;
+  pool_fn = fn;
+  pool_ctx = ctx;
+  pool_ntasks = n < workers + 1 ? n : workers + 1;
+  pool_pending = workers;
+  pool_gen++;
+  pthread_cond_broadcast(&pool_go);
+  pthread_mutex_unlock(&pool_mu);
+  fn(ctx, 0);
+  for (int i = workers + 1; i < n; i++) fn(ctx, i); /* tasks no worker could take */
+  pthread_mutex_lock(&pool_mu);
+  while (pool_pending > 0) pthread_cond_wait(&pool_done, &pool_mu);
+  pool_fn = NULL;
+  pthread_mutex_unlock(&pool_mu);
+  pthread_mutex_unlock(&pool_job);
+}
+
+static void mt_item(void *ctx, int i) { mt_run(&((mt_task *)ctx)[i]); }
+
 static int run_mt(uint32_t t, const uint8_t *raw, size_t raw_len, size_t n_out,
                   size_t n_in, size_t k_cols, const int8_t *codes, const int64_t *scales,
-                  int threads, int64_t *out, apx_err *err) {
+                  int threads, int simd, int64_t *out, apx_err *err) {
   size_t nb = (n_in + ACT_QK - 1) / ACT_QK;
   clear(err);
   for (size_t c = 0; c < k_cols; c++) {
@@ -749,23 +892,35 @@ static int run_mt(uint32_t t, const uint8_t *raw, size_t raw_len, size_t n_out,
   size_t row_bytes;
   int rc = row_geometry(t, n_out, n_in, raw_len, &row_bytes, err);
   if (rc) return rc;
+  x86_rows_fn vec = simd && x86_shape(t, n_in) ? x86_rows() : NULL;
+  for (size_t i = 0; vec && i < k_cols * n_in; i++)
+    if (codes[i] == -128) vec = NULL;
+  int32_t *xsums = NULL;
+  if (vec && t == APX_GGML_TYPE_Q4_K) { /* block_xsums (chart/portable.rs:163-177) */
+    xsums = (int32_t *)malloc(k_cols * nb * sizeof(int32_t));
+    for (size_t g = 0; g < k_cols * nb; g++) {
+      int32_t s = 0;
+      for (int l = 0; l < ACT_QK; l++) s += codes[g * ACT_QK + l];
+      xsums[g] = s;
+    }
+  }
   if (threads < 1) threads = 1;
+  if (threads > POOL_MAX) threads = POOL_MAX;
   if ((size_t)threads > n_out) threads = n_out ? (int)n_out : 1;
   mt_task *tasks = (mt_task *)calloc((size_t)threads, sizeof(mt_task));
-  pthread_t *tid = (pthread_t *)calloc((size_t)threads, sizeof(pthread_t));
   size_t per = (n_out + (size_t)threads - 1) / (size_t)threads;
+  if (vec) per += per & 1; /* whole row pairs per chunk */
   for (int i = 0; i < threads; i++) {
     size_t lo = (size_t)i * per, hi = lo + per < n_out ? lo + per : n_out;
     if (lo > n_out) lo = n_out;
     tasks[i] = (mt_task){t, raw, row_bytes, lo, hi, n_in, k_cols, n_out,
-                         codes, scales, out, 0, 0};
-    pthread_create(&tid[i], NULL, mt_run, &tasks[i]);
+                         codes, scales, xsums, vec, out, 0, 0};
   }
-  for (int i = 0; i < threads; i++) pthread_join(tid[i], NULL);
+  pool_run(mt_item, tasks, threads);
   rc = 0;
   for (int i = 0; i < threads && rc == 0; i++) rc = tasks[i].rc;
   free(tasks);
-  free(tid);
+  free(xsums);
   if (rc != 0) /* any refusal: the single-threaded contract decides it */
     return apxo_matmat_q8act(t, raw, raw_len, n_out, n_in, k_cols, codes, n_in, scales,
                              out, err);
@@ -775,13 +930,150 @@ static int run_mt(uint32_t t, const uint8_t *raw, size_t raw_len, size_t n_out,
 int apxo_matvec_q8act_mt(uint32_t t, const uint8_t *raw, size_t raw_len, size_t n_out,
                          size_t n_in, const int8_t *codes, const int64_t *scales,
                          int threads, int64_t *out, apx_err *err) {
-  return run_mt(t, raw, raw_len, n_out, n_in, 1, codes, scales, threads, out, err);
+  return run_mt(t, raw, raw_len, n_out, n_in, 1, codes, scales, threads, 0, out, err);
 }
 
 int apxo_matmat_q8act_mt(uint32_t t, const uint8_t *raw, size_t raw_len, size_t n_out,
                          size_t n_in, size_t k_cols, const int8_t *codes,
                          const int64_t *scales, int threads, int64_t *out, apx_err *err) {
-  return run_mt(t, raw, raw_len, n_out, n_in, k_cols, codes, scales, threads, out, err);
+  return run_mt(t, raw, raw_len, n_out, n_in, k_cols, codes, scales, threads, 0, out, err);
+}
+
+int apxo_matvec_q8act_simd_mt(uint32_t t, const uint8_t *raw, size_t raw_len, size_t n_out,
+                              size_t n_in, const int8_t *codes, const int64_t *scales,
+                              int threads, int64_t *out, apx_err *err) {
+  return run_mt(t, raw, raw_len, n_out, n_in, 1, codes, scales, threads, 1, out, err);
+}
+
+/* ---- the prefill baseline: the k-column Q8_0 GEMM (src/engine/kern/gemm.rs:498-580) ------
+ * Its row kernel is apxo_x86_gemm_rows (apx_oracle_x86.c, AVX-VNNI build); here are the
+ * column pack (gemm.rs:131-264) and the row split over the pool. */
+int apxo_x86_gemm_rows(const uint8_t *raw, size_t row_bytes, size_t blocks, size_t lo,
+                       size_t hi, size_t k_cols, size_t n_in, const uint32_t *words,
+                       const int64_t *shift, const uint32_t *emin, const uint32_t *gspread,
+                       uint32_t limit, const int8_t *codes, const int64_t *scales,
+                       int64_t *out, size_t n_out);
+
+typedef struct {
+  const uint8_t *raw;
+  size_t row_bytes, blocks, n_out, n_in, k_cols, per;
+  const uint32_t *words, *emin, *gspread;
+  const int64_t *shift, *scales;
+  const int8_t *codes;
+  uint32_t limit;
+  int64_t *out;
+  int bail[POOL_MAX];
+} gemm_job;
+
+static void gemm_item(void *ctx, int i) {
+  gemm_job *j = (gemm_job *)ctx;
+  size_t lo = (size_t)i * j->per, hi = lo + j->per < j->n_out ? lo + j->per : j->n_out;
+  j->bail[i] = lo < hi ? apxo_x86_gemm_rows(j->raw, j->row_bytes, j->blocks, lo, hi,
+                                            j->k_cols, j->n_in, j->words, j->shift, j->emin,
+                                            j->gspread, j->limit, j->codes, j->scales, j->out,
+                                            j->n_out)
+                       : 0;
+}
+
+/* spread_limit (gemm.rs:99-102): 33 − ⌈log2 blocks⌉. */
+static uint32_t spread_limit(size_t blocks) {
+  uint32_t log = 0;
+  while (((size_t)1 << log) < blocks) log++;
+  return log >= 33 ? 0 : 33 - log;
+}
+
+/* 1 when the GEMM ran and wrote every output; 0 when the call takes the per-column rows. */
+static int gemm_q8_0_mt(const uint8_t *raw, size_t raw_len, size_t n_out, size_t n_in,
+                        size_t k_cols, const int8_t *codes, const int64_t *scales, int threads,
+                        int64_t *out) {
+  size_t blocks = n_in / ACT_QK;
+  if (n_in % ACT_QK || blocks == 0 || blocks > 512 || k_cols == 0 || n_out == 0) return 0;
+  if ((apxo_simd_features() & 3) != 3) return 0;
+  if (raw_len / Q8_0_BYTES / blocks < n_out) return 0;
+  for (size_t c = 0; c < k_cols; c++) { /* fast_columns_ok (gemm.rs:283-300) */
+    int fast = 0;
+    if (plan(APX_GGML_TYPE_Q8_0, n_in, codes + c * n_in, n_in, scales + c * blocks, blocks,
+             &fast) != 0 || !fast)
+      return 0;
+  }
+  size_t groups = (k_cols + 7) / 8;
+  uint32_t *words = (uint32_t *)malloc(groups * blocks * 64 * sizeof(uint32_t));
+  int64_t *shift = (int64_t *)calloc(groups * blocks * 8, sizeof(int64_t));
+  uint32_t *emin = (uint32_t *)calloc(groups * 8, sizeof(uint32_t));
+  uint32_t *gspread = (uint32_t *)calloc(groups, sizeof(uint32_t));
+  gemm_job *job = (gemm_job *)calloc(1, sizeof(gemm_job));
+  int ok = words && shift && emin && gspread && job;
+  for (size_t g = 0; ok && g < groups; g++) {
+    for (size_t lane = 0; lane < 8; lane++) {
+      size_t c = g * 8 + lane;
+      uint32_t e_lo = UINT32_MAX;
+      for (size_t b = 0; c < k_cols && b < blocks; b++) {
+        int64_t S = scales[c * blocks + b];
+        if (S < 0 || (S & (S - 1))) ok = 0; /* not 0 or a power of two */
+        if (S > 0 && (uint32_t)__builtin_ctzll((uint64_t)S) < e_lo)
+          e_lo = (uint32_t)__builtin_ctzll((uint64_t)S);
+      }
+      if (e_lo == UINT32_MAX) e_lo = 0;
+      emin[c] = e_lo;
+      for (size_t b = 0; b < blocks; b++) {
+        int64_t S = c < k_cols ? scales[c * blocks + b] : 0;
+        uint32_t sh = S > 0 ? (uint32_t)__builtin_ctzll((uint64_t)S) - e_lo : 0;
+        shift[(g * blocks + b) * 8 + lane] = sh;
+        if (sh > gspread[g]) gspread[g] = sh;
+        for (int q = 0; q < 8; q++) {
+          uint32_t w = 0;
+          for (int i = 0; i < 4; i++) {
+            int8_t x = S > 0 ? codes[c * n_in + b * 32 + 4 * q + i] : 0;
+            w |= (uint32_t)(uint8_t)(x + 128) << (8 * i);
+          }
+          words[((g * blocks + b) * 8 + q) * 8 + lane] = w;
+        }
+      }
+    }
+  }
+  int done = 0;
+  if (ok) {
+    if (threads < 1) threads = 1;
+    if (threads > POOL_MAX) threads = POOL_MAX;
+    if ((size_t)threads > n_out) threads = (int)n_out;
+    size_t per = (n_out + (size_t)threads - 1) / (size_t)threads;
+    per += per & 1;
+    *job = (gemm_job){raw, blocks * Q8_0_BYTES, blocks, n_out, n_in, k_cols, per, words, emin,
+                      gspread, shift, scales, codes, spread_limit(blocks), out, {0}};
+    pool_run(gemm_item, job, threads);
+    done = 1;
+    for (int i = 0; i < threads; i++) done &= !job->bail[i];
+  }
+  free(words);
+  free(shift);
+  free(emin);
+  free(gspread);
+  free(job);
+  return done;
+}
+
+extern unsigned long apxo_x86_gemm_exact_groups;
+static unsigned long gemm_calls;
+
+void apxo_gemm_counts(uint64_t *calls, uint64_t *exact_groups) {
+  *calls = __atomic_load_n(&gemm_calls, __ATOMIC_RELAXED);
+  *exact_groups = __atomic_load_n(&apxo_x86_gemm_exact_groups, __ATOMIC_RELAXED);
+}
+
+/* With AVX-VNNI, Q8_0 calls whose every column takes the fast rows run the k-column GEMM, as
+ * the reference's matmat_q8act tries gemm_q8_0 first (kern/matmat.rs:134-146); everything
+ * else (and every call the GEMM bails on) runs the vector rows per column. */
+int apxo_matmat_q8act_simd_mt(uint32_t t, const uint8_t *raw, size_t raw_len, size_t n_out,
+                              size_t n_in, size_t k_cols, const int8_t *codes,
+                              const int64_t *scales, int threads, int64_t *out,
+                              apx_err *err) {
+  if (t == APX_GGML_TYPE_Q8_0 &&
+      gemm_q8_0_mt(raw, raw_len, n_out, n_in, k_cols, codes, scales, threads, out)) {
+    __atomic_fetch_add(&gemm_calls, 1, __ATOMIC_RELAXED);
+    clear(err);
+    return 0;
+  }
+  return run_mt(t, raw, raw_len, n_out, n_in, k_cols, codes, scales, threads, 1, out, err);
 }
 
 /* ---- the FFN hidden activation: SwiGLU under either carrier ----------------------------- */

@@ -91,6 +91,25 @@ int apxo_matmat_q8act_mt(uint32_t ggml_type, const uint8_t *raw, size_t raw_len,
                          const int8_t *codes, const int64_t *scales, int threads,
                          int64_t *out, apx_err *err);
 
+/* The timed CPU baseline's vector rows (apx_oracle_x86.c, the reference's AVX2 / AVX-VNNI
+ * row cores, src/engine/chart/x86.rs:782-1200): the same results as the *_mt calls above,
+ * with Q8_0 (whole blocks) and Q4_K (whole super-blocks) rows two at a time in vector code
+ * when the CPU has AVX2; every other shape takes the scalar fast rows. */
+int apxo_matvec_q8act_simd_mt(uint32_t ggml_type, const uint8_t *raw, size_t raw_len,
+                              size_t n_out, size_t n_in, const int8_t *codes,
+                              const int64_t *scales, int threads, int64_t *out,
+                              apx_err *err);
+int apxo_matmat_q8act_simd_mt(uint32_t ggml_type, const uint8_t *raw, size_t raw_len,
+                              size_t n_out, size_t n_in, size_t k_cols,
+                              const int8_t *codes, const int64_t *scales, int threads,
+                              int64_t *out, apx_err *err);
+/* Bit 0: AVX2 (the vector rows run); bit 1: AVX-VNNI (they use vpdpbusd, and Q8_0 matmats
+ * run the k-column GEMM of src/engine/kern/gemm.rs:498-580). */
+int apxo_simd_features(void);
+/* Matmat calls the k-column GEMM completed, and (row, group) pairs it sent to the exact i128
+ * dot, since the library loaded (for the tests). */
+void apxo_gemm_counts(uint64_t *calls, uint64_t *exact_groups);
+
 /* The FFN hidden activation (src/engine/chart/ffn.rs:246-284, ops/silu.rs:53-100,
  * numeric/fixed_exp.rs:1-184, mixer/f32_carrier.rs:262-375). */
 int apxo_fixed_exp(int64_t x, int64_t *out);

@@ -1,0 +1,329 @@
+/*
+ * apx_oracle_x86.c — vector rows of the timed CPU baseline.
+ *
+ * TEST INFRASTRUCTURE ONLY (see apx_oracle.h): bench.py's cpu_baseline and `--impl reference`
+ * legs time these rows; tests/test_oracle_x86.py checks them against the scalar fused rows of
+ * apx_oracle.c.  The product library never links this file.
+ *
+ * The reference's decode rows on x86 are AVX2 cores that take two weight rows per pass and
+ * share each activation load between them (`tiled2`, `q8_0_rows2_avx2`, `q4_k_rows2_avx2`,
+ * src/engine/chart/x86.rs:782-1200).  This file restates those cores so the CPU baseline runs
+ * at the reference's own speed class instead of a scalar loop's:
+ *   - a 32-lane byte dot is |w| (unsigned) times sign(x, w) (signed), which is exact in
+ *     either instruction form: `vpmaddubsw` + `vpmaddwd` (pair sums ≤ 2·128·127 < 2^15, so no
+ *     saturation) or, with AVX-VNNI, one `vpdpbusd` (x86.rs:177-210);
+ *   - f16 block scales decode through one 65,536-entry table whose odd entries mark the
+ *     non-finite patterns (every finite decode is a multiple of 2^8), ORed into one word per
+ *     row pair and tested after the loop (chart/portable.rs:15-79);
+ *   - the folds are the scalar fast row's, in its group order, with the same exact integers:
+ *     Q8_0 `acc += d·(S·D)` (S·D fits i64 under the narrow call bound), Q4_K
+ *     `acc += S·((d·sc)·D − (dmin·m)·Σxq)` per 32-lane group.
+ * Integer sums are exact, so each row's accumulator equals the scalar fast row's bit for bit.
+ *
+ * This file is compiled twice (oracle/Makefile): with APX_X86_VNNI=0 for AVX2 and with
+ * APX_X86_VNNI=1 under -mavxvnni; apx_oracle.c picks one at run time from CPUID.
+ * Paths in comments are relative to the apeiron source tree.
+ */
+#include <immintrin.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../include/apeiron_cuda.h"
+
+typedef __int128 i128;
+
+#if APX_X86_VNNI
+#define ROWS_NAME apxo_x86_rows_vnni
+#else
+#define ROWS_NAME apxo_x86_rows_avx2
+#endif
+
+#define Q8_0_BYTES 34
+#define Q4_K_BYTES 144
+
+/* Eight i32 lane sums of w·x over 32 byte lanes (x86.rs:177-210). */
+static inline __m256i dot_lanes(__m256i w, __m256i x) {
+  __m256i u = _mm256_abs_epi8(w), s = _mm256_sign_epi8(x, w);
+#if APX_X86_VNNI
+  return _mm256_dpbusd_avx_epi32(_mm256_setzero_si256(), u, s);
+#else
+  return _mm256_madd_epi16(_mm256_maddubs_epi16(u, s), _mm256_set1_epi16(1));
+#endif
+}
+
+/* The four totals [Σp0, Σp1, Σp2, Σp3] of four lane vectors (x86.rs:148-160). */
+static inline __m128i sum4(__m256i p0, __m256i p1, __m256i p2, __m256i p3) {
+  __m256i h = _mm256_hadd_epi32(_mm256_hadd_epi32(p0, p1), _mm256_hadd_epi32(p2, p3));
+  return _mm_add_epi32(_mm256_castsi256_si128(h), _mm256_extracti128_si256(h, 1));
+}
+
+static inline int32_t sum1(__m256i p) {
+  __m128i v = _mm_add_epi32(_mm256_castsi256_si128(p), _mm256_extracti128_si256(p, 1));
+  v = _mm_hadd_epi32(v, v);
+  v = _mm_hadd_epi32(v, v);
+  return _mm_cvtsi128_si32(v);
+}
+
+static inline uint16_t word(const uint8_t *p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+static inline __m256i ld(const void *p) { return _mm256_loadu_si256((const __m256i *)p); }
+
+/* get_scale_min_k4 (src/format/quant.rs:482-491). */
+static inline void scale_min(const uint8_t *q, int j, int *s, int *m) {
+  if (j < 4) {
+    *s = q[j] & 63;
+    *m = q[j + 4] & 63;
+  } else {
+    *s = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+    *m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+  }
+}
+
+/* Two Q8_0 rows (r0, r1) of `blocks` blocks: the accumulators before rounding; returns the
+ * OR of the four scale-table entries' low bits (1 = a non-finite scale in either row). */
+static int q8_0_pair(const uint8_t *r0, const uint8_t *r1, size_t blocks, const int8_t *codes,
+                     const int64_t *S, const int64_t *tab, i128 acc[2]) {
+  i128 a0 = 0, a1 = 0;
+  int64_t bad = 0;
+  size_t b = 0;
+  for (; b + 4 <= blocks; b += 4) {
+    const uint8_t *p0 = r0 + b * Q8_0_BYTES, *p1 = r1 + b * Q8_0_BYTES;
+    const int8_t *x = codes + b * 32;
+    __m256i x0 = ld(x), x1 = ld(x + 32), x2 = ld(x + 64), x3 = ld(x + 96);
+    __m128i t0 = sum4(dot_lanes(ld(p0 + 2), x0), dot_lanes(ld(p0 + 2 + Q8_0_BYTES), x1),
+                      dot_lanes(ld(p0 + 2 + 2 * Q8_0_BYTES), x2),
+                      dot_lanes(ld(p0 + 2 + 3 * Q8_0_BYTES), x3));
+    __m128i t1 = sum4(dot_lanes(ld(p1 + 2), x0), dot_lanes(ld(p1 + 2 + Q8_0_BYTES), x1),
+                      dot_lanes(ld(p1 + 2 + 2 * Q8_0_BYTES), x2),
+                      dot_lanes(ld(p1 + 2 + 3 * Q8_0_BYTES), x3));
+    int32_t d0[4], d1[4];
+    _mm_storeu_si128((__m128i *)d0, t0);
+    _mm_storeu_si128((__m128i *)d1, t1);
+    for (int j = 0; j < 4; j++) {
+      int64_t w0 = tab[word(p0 + j * Q8_0_BYTES)], w1 = tab[word(p1 + j * Q8_0_BYTES)];
+      bad |= w0 | w1;
+      int64_t s = S[b + j];
+      a0 += (i128)w0 * (i128)(s * (int64_t)d0[j]);
+      a1 += (i128)w1 * (i128)(s * (int64_t)d1[j]);
+    }
+  }
+  for (; b < blocks; b++) {
+    const uint8_t *p0 = r0 + b * Q8_0_BYTES, *p1 = r1 + b * Q8_0_BYTES;
+    __m256i x = ld(codes + b * 32);
+    int64_t w0 = tab[word(p0)], w1 = tab[word(p1)];
+    bad |= w0 | w1;
+    int64_t s = S[b];
+    a0 += (i128)w0 * (i128)(s * (int64_t)sum1(dot_lanes(ld(p0 + 2), x)));
+    a1 += (i128)w1 * (i128)(s * (int64_t)sum1(dot_lanes(ld(p1 + 2), x)));
+  }
+  acc[0] = a0;
+  acc[1] = a1;
+  return (int)(bad & 1);
+}
+
+/* Two Q4_K rows of `sblocks` super-blocks; xsums[g] = Σ codes over 32-lane group g. */
+static int q4_k_pair(const uint8_t *r0, const uint8_t *r1, size_t sblocks, const int8_t *codes,
+                     const int64_t *S, const int32_t *xsums, const int64_t *tab, i128 acc[2]) {
+  const __m256i nib = _mm256_set1_epi8(0x0F);
+  i128 a[2] = {0, 0};
+  int64_t bad = 0;
+  for (size_t b = 0; b < sblocks; b++) {
+    const int8_t *x = codes + b * 256;
+    __m256i x0 = ld(x), x1 = ld(x + 32), x2 = ld(x + 64), x3 = ld(x + 96);
+    __m256i x4 = ld(x + 128), x5 = ld(x + 160), x6 = ld(x + 192), x7 = ld(x + 224);
+    for (int r = 0; r < 2; r++) {
+      const uint8_t *blk = (r ? r1 : r0) + b * Q4_K_BYTES;
+      int64_t d = tab[word(blk)], dmin = tab[word(blk + 2)];
+      bad |= d | dmin;
+      const uint8_t *qs = blk + 16;
+      __m256i q0 = ld(qs), q1 = ld(qs + 32), q2 = ld(qs + 64), q3 = ld(qs + 96);
+      __m128i lo = sum4(dot_lanes(_mm256_and_si256(q0, nib), x0),
+                        dot_lanes(_mm256_and_si256(q1, nib), x2),
+                        dot_lanes(_mm256_and_si256(q2, nib), x4),
+                        dot_lanes(_mm256_and_si256(q3, nib), x6));
+      __m256i h0 = _mm256_and_si256(_mm256_srli_epi16(q0, 4), nib);
+      __m256i h1 = _mm256_and_si256(_mm256_srli_epi16(q1, 4), nib);
+      __m256i h2 = _mm256_and_si256(_mm256_srli_epi16(q2, 4), nib);
+      __m256i h3 = _mm256_and_si256(_mm256_srli_epi16(q3, 4), nib);
+      __m128i hi = sum4(dot_lanes(h0, x1), dot_lanes(h1, x3), dot_lanes(h2, x5),
+                        dot_lanes(h3, x7));
+      int32_t dl[4], dh[4];
+      _mm_storeu_si128((__m128i *)dl, lo);
+      _mm_storeu_si128((__m128i *)dh, hi);
+      for (int p = 0; p < 4; p++) {
+        int sl, ml, sh, mh;
+        scale_min(blk + 4, 2 * p, &sl, &ml);
+        scale_min(blk + 4, 2 * p + 1, &sh, &mh);
+        size_t g = b * 8 + 2 * (size_t)p;
+        i128 in_lo = (i128)(d * sl) * dl[p] - (i128)(dmin * ml) * xsums[g];
+        i128 in_hi = (i128)(d * sh) * dh[p] - (i128)(dmin * mh) * xsums[g + 1];
+        a[r] += (i128)S[g] * in_lo + (i128)S[g + 1] * in_hi;
+      }
+    }
+  }
+  acc[0] = a[0];
+  acc[1] = a[1];
+  return (int)(bad & 1);
+}
+
+/* round_shift_32 then the i64 range check (src/engine/num/value.rs:10-12,
+ * chart/mod.rs:1746-1753). */
+static int finish_row(i128 acc, int64_t *out) {
+  i128 q = acc >> 32;
+  q += ((uint64_t)acc & 0xFFFFFFFFull) >= 0x80000000ull;
+  if (q > (i128)INT64_MAX || q < (i128)INT64_MIN) return 1;
+  *out = (int64_t)q;
+  return 0;
+}
+
+/* Rows [lo, hi) of a Q8_0 (n_in % 32 == 0) or Q4_K (n_in % 256 == 0) projection whose call
+ * plan chose the fast rows.  Returns 0, APX_ERR_OUTPUT_OVERFLOW with the first such row in
+ * *bad, or -1 when a block scale is non-finite (the caller then runs the contract). */
+int ROWS_NAME(uint32_t t, const uint8_t *raw, size_t row_bytes, size_t lo, size_t hi,
+              size_t n_in, const int8_t *codes, const int64_t *S, const int32_t *xsums,
+              const int64_t *tab, int64_t *out, size_t *bad) {
+  for (size_t o = lo; o < hi; o += 2) {
+    const uint8_t *r0 = raw + o * row_bytes;
+    const uint8_t *r1 = o + 1 < hi ? r0 + row_bytes : r0;
+    i128 acc[2];
+    int nf = t == APX_GGML_TYPE_Q8_0
+                 ? q8_0_pair(r0, r1, n_in / 32, codes, S, tab, acc)
+                 : q4_k_pair(r0, r1, n_in / 256, codes, S, xsums, tab, acc);
+    if (nf) {
+      *bad = o;
+      return -1;
+    }
+    for (size_t r = 0; r < 2 && o + r < hi; r++) {
+      if (finish_row(acc[r], &out[o + r])) {
+        *bad = o + r;
+        return APX_ERR_OUTPUT_OVERFLOW;
+      }
+    }
+  }
+  return 0;
+}
+
+#if APX_X86_VNNI
+/* ---- the k-column Q8_0 GEMM of the prefill baseline (src/engine/kern/gemm.rs:498-580) ----
+ *
+ * The reference's prefill runs Q8_0 projections of many tokens through `gemm_q8_0` when the
+ * host has AVX-VNNI: every weight row is read once per call and its 32-byte blocks are dotted
+ * against groups of 8 token columns with `vpdpbusd`, the activation stored as x + 128 (u8) and
+ * the weight as i8, so each lane's sum is D + 128·Σw and one subtraction of the row's
+ * 128·Σw recovers the exact block dot D.  The row's f16 scales are split as m·2^k (|m| ≤ 2047,
+ * pow2.rs:52-64) and each (row, token) accumulates `(m·D) << (k − kmin + e − emin)` in i64
+ * (|m·D| < 2^30), exact while the row's k spread plus the group's e spread stays within
+ * `33 − ⌈log2 blocks⌉` (spread_limit, gemm.rs:99-102); a (row, group) past it takes the
+ * i128 `exact_dot`.  The output is `finish(acc, kmin + emin)` (pow2.rs:76-96).  Two rows per
+ * pass share every activation load. */
+
+int apxo_f16_split(uint16_t h, int32_t *m, uint32_t *k);
+int apxo_finish(int64_t acc, uint32_t s, int64_t *out);
+int apxo_exact_dot_q8_0(const uint8_t *row, size_t blocks, const int8_t *codes,
+                        const int64_t *scales, int64_t *out);
+
+#define GEMM_MAX_BLOCKS 512
+
+/* (row, group) pairs that took the exact i128 dot, for the tests (apxo_gemm_counts). */
+unsigned long apxo_x86_gemm_exact_groups;
+
+/* A row's per-block m, k − kmin and 128·Σw (row_scales, gemm.rs:438-456); 1 on a non-finite
+ * scale. */
+static int row_scales(const uint8_t *row, size_t blocks, int32_t *m, int64_t *kd, int32_t *bsum,
+                      uint32_t *kmin_out, uint32_t *spread_out) {
+  uint32_t kmin = UINT32_MAX, kmax = 0;
+  for (size_t b = 0; b < blocks; b++) {
+    const uint8_t *blk = row + b * Q8_0_BYTES;
+    uint32_t k;
+    if (apxo_f16_split(word(blk), &m[b], &k)) return 1;
+    kd[b] = k;
+    kmin = k < kmin ? k : kmin;
+    kmax = k > kmax ? k : kmax;
+    int32_t sum = 0;
+    for (int l = 0; l < 32; l++) sum += (int8_t)blk[2 + l];
+    bsum[b] = 128 * sum;
+  }
+  for (size_t b = 0; b < blocks; b++) kd[b] -= kmin;
+  *kmin_out = kmin;
+  *spread_out = kmax - kmin;
+  return 0;
+}
+
+/* One row's 8 lanes of one block: (m·(acc − 128Σw)) << (kd + shift) added to lo/hi. */
+static inline void fold8(__m256i dots, int32_t m, int64_t kd, int32_t bsum, __m256i sh0,
+                         __m256i sh1, __m256i *lo, __m256i *hi) {
+  __m256i t = _mm256_mullo_epi32(_mm256_sub_epi32(dots, _mm256_set1_epi32(bsum)),
+                                 _mm256_set1_epi32(m));
+  __m256i kv = _mm256_set1_epi64x(kd);
+  *lo = _mm256_add_epi64(*lo, _mm256_sllv_epi64(_mm256_cvtepi32_epi64(_mm256_castsi256_si128(t)),
+                                                _mm256_add_epi64(sh0, kv)));
+  *hi = _mm256_add_epi64(*hi,
+                         _mm256_sllv_epi64(_mm256_cvtepi32_epi64(_mm256_extracti128_si256(t, 1)),
+                                           _mm256_add_epi64(sh1, kv)));
+}
+
+/* Rows [lo, hi) of the GEMM.  words: [group][block][quad][lane] u32 (4 bytes x + 128 of
+ * column 8·group + lane); shift: [group][block][lane] i64 (e − emin, 0 for zero blocks and
+ * padding lanes); emin per column; gspread per group.  out[c·n_out + o].  Returns 0, or 1 when
+ * the caller must redecide the call on the per-column path (a non-finite scale, an output
+ * outside i64, an exact dot past i128). */
+int apxo_x86_gemm_rows(const uint8_t *raw, size_t row_bytes, size_t blocks, size_t lo,
+                       size_t hi, size_t k_cols, size_t n_in, const uint32_t *words,
+                       const int64_t *shift, const uint32_t *emin, const uint32_t *gspread,
+                       uint32_t limit, const int8_t *codes, const int64_t *scales,
+                       int64_t *out, size_t n_out) {
+  int32_t ma[GEMM_MAX_BLOCKS], mb[GEMM_MAX_BLOCKS], sa[GEMM_MAX_BLOCKS], sb[GEMM_MAX_BLOCKS];
+  int64_t ka[GEMM_MAX_BLOCKS], kb[GEMM_MAX_BLOCKS];
+  size_t groups = (k_cols + 7) / 8;
+  for (size_t o = lo; o < hi; o += 2) {
+    int two = o + 1 < hi;
+    const uint8_t *ra = raw + o * row_bytes, *rb = two ? ra + row_bytes : ra;
+    uint32_t kmina, spra, kminb, sprb;
+    if (row_scales(ra, blocks, ma, ka, sa, &kmina, &spra) ||
+        row_scales(rb, blocks, mb, kb, sb, &kminb, &sprb))
+      return 1;
+    for (size_t g = 0; g < groups; g++) {
+      size_t c0 = g * 8, nc = k_cols - c0 < 8 ? k_cols - c0 : 8;
+      if (spra + gspread[g] > limit || sprb + gspread[g] > limit) {
+        __atomic_fetch_add(&apxo_x86_gemm_exact_groups, 1, __ATOMIC_RELAXED);
+        for (size_t c = c0; c < c0 + nc; c++)
+          for (int r = 0; r <= two; r++)
+            if (apxo_exact_dot_q8_0(r ? rb : ra, blocks, codes + c * n_in,
+                                    scales + c * blocks, &out[c * n_out + o + r]))
+              return 1;
+        continue;
+      }
+      const uint32_t *wg = words + g * blocks * 64;
+      const int64_t *sg = shift + g * blocks * 8;
+      __m256i a0 = _mm256_setzero_si256(), a1 = a0, b0 = a0, b1 = a0;
+      for (size_t b = 0; b < blocks; b++) {
+        const uint8_t *ca = ra + b * Q8_0_BYTES + 2, *cb = rb + b * Q8_0_BYTES + 2;
+        const uint32_t *wb = wg + b * 64;
+        __m256i da = _mm256_setzero_si256(), db = da;
+        for (int q = 0; q < 8; q++) {
+          __m256i act = ld(wb + 8 * q);
+          int32_t wa, wbq;
+          __builtin_memcpy(&wa, ca + 4 * q, 4);
+          __builtin_memcpy(&wbq, cb + 4 * q, 4);
+          da = _mm256_dpbusd_avx_epi32(da, act, _mm256_set1_epi32(wa));
+          db = _mm256_dpbusd_avx_epi32(db, act, _mm256_set1_epi32(wbq));
+        }
+        __m256i sh0 = ld(sg + b * 8), sh1 = ld(sg + b * 8 + 4);
+        fold8(da, ma[b], ka[b], sa[b], sh0, sh1, &a0, &a1);
+        fold8(db, mb[b], kb[b], sb[b], sh0, sh1, &b0, &b1);
+      }
+      int64_t la[8], lb[8];
+      _mm256_storeu_si256((__m256i *)la, a0);
+      _mm256_storeu_si256((__m256i *)(la + 4), a1);
+      _mm256_storeu_si256((__m256i *)lb, b0);
+      _mm256_storeu_si256((__m256i *)(lb + 4), b1);
+      for (size_t c = 0; c < nc; c++) {
+        if (apxo_finish(la[c], kmina + emin[c0 + c], &out[(c0 + c) * n_out + o])) return 1;
+        if (two && apxo_finish(lb[c], kminb + emin[c0 + c], &out[(c0 + c) * n_out + o + 1]))
+          return 1;
+      }
+    }
+  }
+  return 0;
+}
+#endif

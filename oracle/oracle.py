@@ -95,6 +95,10 @@ def _declare(l):
                                        C.POINTER(ApxErr)]
     l.apxo_matmat_q8act_mt.argtypes = [C.c_uint32, P, SZ, SZ, SZ, SZ, P, P, C.c_int, P,
                                        C.POINTER(ApxErr)]
+    l.apxo_matvec_q8act_simd_mt.argtypes = l.apxo_matvec_q8act_mt.argtypes
+    l.apxo_matmat_q8act_simd_mt.argtypes = l.apxo_matmat_q8act_mt.argtypes
+    l.apxo_simd_features.argtypes = []
+    l.apxo_gemm_counts.argtypes = [C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]
 
 
 def _p(a: np.ndarray):
@@ -302,25 +306,47 @@ def matmat_q8act(t, raw, n_out, n_in, codes, scales):
     return out[:k, :n_out]
 
 
-def matvec_q8act_mt(t, raw, n_out, n_in, codes, scales, threads):
+def matvec_q8act_mt(t, raw, n_out, n_in, codes, scales, threads, simd=False):
+    """The fused rows over ``threads`` row chunks; ``simd`` takes the vector rows
+    (apx_oracle_x86.c) where the shape allows, with the same results."""
     raw = _u8(raw)
+    codes = np.ascontiguousarray(codes, dtype=np.int8)
+    scales = np.ascontiguousarray(scales, dtype=np.int64)
     out = np.zeros(max(n_out, 1), dtype=np.int64)
     err = ApxErr()
-    rc = lib().apxo_matvec_q8act_mt(t, _p(raw), raw.size, n_out, n_in, _p(codes),
-                                    _p(scales), threads, _p(out), C.byref(err))
+    fn = lib().apxo_matvec_q8act_simd_mt if simd else lib().apxo_matvec_q8act_mt
+    rc = fn(t, _p(raw), raw.size, n_out, n_in, _p(codes), _p(scales), threads, _p(out),
+            C.byref(err))
     return _result(rc, err, out[:n_out])
 
 
-def matmat_q8act_mt(t, raw, n_out, n_in, codes, scales, threads):
+def matmat_q8act_mt(t, raw, n_out, n_in, codes, scales, threads, simd=False):
     raw = _u8(raw)
+    codes = np.ascontiguousarray(codes, dtype=np.int8)
+    scales = np.ascontiguousarray(scales, dtype=np.int64)
     k = codes.shape[0]
     out = np.zeros((k, n_out), dtype=np.int64)
     err = ApxErr()
-    rc = lib().apxo_matmat_q8act_mt(t, _p(raw), raw.size, n_out, n_in, k, _p(codes),
-                                    _p(scales), threads, _p(out), C.byref(err))
+    fn = lib().apxo_matmat_q8act_simd_mt if simd else lib().apxo_matmat_q8act_mt
+    rc = fn(t, _p(raw), raw.size, n_out, n_in, k, _p(codes), _p(scales), threads, _p(out),
+            C.byref(err))
     if rc:
         return ("err", err.code, err.a, err.b, err.bits, err.col)
     return out
+
+
+def gemm_counts():
+    """(matmat calls the k-column Q8_0 GEMM completed, (row, group) pairs it sent to the exact
+    i128 dot) since the library loaded."""
+    a, b = C.c_uint64(), C.c_uint64()
+    lib().apxo_gemm_counts(C.byref(a), C.byref(b))
+    return a.value, b.value
+
+
+def simd_features() -> dict:
+    """What the vector rows use on this host: {"avx2": bool, "avxvnni": bool}."""
+    f = lib().apxo_simd_features()
+    return {"avx2": bool(f & 1), "avxvnni": bool(f & 2)}
 
 
 def exact_dot_q8_0(row, blocks, codes, scales):
