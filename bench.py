@@ -623,6 +623,43 @@ def cpu_passes(data, max_passes, max_seconds):
     return total, done, time.perf_counter() - t0, threads
 
 
+def cpu_chain_baseline(mats, seed0, seconds=5.0):
+    """The CPU arm of a chain of projections (configs[3]'s decode step, configs[4]'s whole FFN):
+    every projection its own host copy, so a pass streams DRAM as the device's does, one
+    quantized activation per width, and every call the oracle's restatement of the reference's
+    pooled decode (the vector two-row cores where the width allows, else the portable fast rows
+    or the contract, as the reference picks them); GB/s of the same algorithmic bytes."""
+    from apeiron_b200 import synth
+    from oracle import oracle as O
+
+    threads = os.cpu_count() or 1
+    base = {m: synth.payload(m[0], m[1], m[2], seed0 + i) for i, m in enumerate(dict.fromkeys(mats))}
+    data = [(t, base[(t, n_out, n_in)].copy(), n_out, n_in) for t, n_out, n_in in mats]
+    acts = {}
+    for n_in in {m[2] for m in mats}:
+        c, e = synth.quant_act_np(synth.f32_to_q32(synth.activation_f32(n_in, seed0 + n_in)))
+        acts[n_in] = (c, O.exps_to_scales(e))
+    per_pass = sum(gemv_bytes(*m) for m in mats)
+
+    def one_pass():
+        for t, raw, n_out, n_in in data:
+            r = O.matvec_q8act_mt(t, raw, n_out, n_in, *acts[n_in], threads, simd=True)
+            assert not isinstance(r, tuple)
+
+    one_pass()
+    done, t0 = 0, time.perf_counter()
+    while True:
+        one_pass()
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return {"value": per_pass * done / el / 1e9, "unit": "GB/s", "cores": threads,
+            "kind": "port", "sample": f"{done} passes of all {len(mats)} projections "
+                                      f"({per_pass / 1e6:.0f} MB of distinct host copies per "
+                                      f"pass) in {el:.1f} s, {cpu_isa()} rows"}
+
+
 def cpu_gemv_baseline(mats, seconds=10.0):
     data, copies = cpu_data(mats)
     cpu_passes(data, 3, 2.0)
@@ -859,6 +896,14 @@ def run_ours(args, world, rank, local, pg):
         line["cpu_baseline"] = cpu_gemv_baseline(mats, seconds=args.cpu_seconds)
         if prefill is not None:
             prefill["cpu_baseline"] = cpu_prefill_baseline(seconds=args.cpu_seconds)
+        for obj, mats_, seed in ((decode, DECODE_LAYER * DECODE_LAYERS + [DECODE_HEAD], 6000),
+                                 (sharded, SHARDED, 4000)):
+            if obj is None:
+                continue
+            try:
+                obj["cpu_baseline"] = cpu_chain_baseline(mats_, seed, args.cpu_seconds / 2)
+            except Exception as exc:  # the device numbers stand without it
+                obj["cpu_baseline"] = {"unavailable": f"{type(exc).__name__}: {exc}"}
     if prefill is not None:
         line["prefill"] = prefill
         line["gpu_launches"] += prefill["gpu_launches_per_step"] * prefill["steps"]

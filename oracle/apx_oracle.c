@@ -769,6 +769,7 @@ typedef struct {
   const int64_t *scales;
   const int32_t *xsums; /* [k_cols][n_in / 32], vector rows only */
   x86_rows_fn vec;      /* NULL: the scalar fast rows */
+  const int64_t *xhat;  /* [k_cols][n_in] dequantized activations: the contract's rows */
   int64_t *out;
   int rc;
   size_t bad;
@@ -779,7 +780,12 @@ static void *mt_run(void *arg) {
   size_t nb = (a->n_in + ACT_QK - 1) / ACT_QK;
   a->rc = 0;
   for (size_t c = 0; c < a->k_cols && a->rc == 0; c++) {
-    if (a->vec)
+    if (a->xhat)
+      a->rc = apxo_matvec_fixed(a->t, a->raw + a->lo * a->row_bytes,
+                                (a->hi - a->lo) * a->row_bytes, a->hi - a->lo, a->n_in,
+                                a->xhat + c * a->n_in, a->n_in, a->out + c * a->n_out + a->lo,
+                                NULL);
+    else if (a->vec)
       a->rc = a->vec(a->t, a->raw, a->row_bytes, a->lo, a->hi, a->n_in,
                      a->codes + c * a->n_in, a->scales + c * nb,
                      a->xsums ? a->xsums + c * nb : NULL, f16_table, a->out + c * a->n_out,
@@ -882,17 +888,35 @@ static int run_mt(uint32_t t, const uint8_t *raw, size_t raw_len, size_t n_out,
                   int threads, int simd, int64_t *out, apx_err *err) {
   size_t nb = (n_in + ACT_QK - 1) / ACT_QK;
   clear(err);
+  /* Columns whose plan is the contract (an unfused family or width, or the call bound failing)
+   * run matvec_fixed on the dequantized activation, split over the same row chunks: the
+   * chunked caller runs every row range on the pool whatever its plan (ffn.rs:705-726). */
+  int contract_rows = 0;
   for (size_t c = 0; c < k_cols; c++) {
     int fast = 0;
     int p = plan(t, n_in, codes + c * n_in, n_in, scales + c * nb, nb, &fast);
-    if (p != 0 || !fast)
+    if (p == 2)
       return apxo_matmat_q8act(t, raw, raw_len, n_out, n_in, k_cols, codes, n_in, scales,
                                out, err);
+    if (p != 0 || !fast) contract_rows = 1;
   }
-  size_t row_bytes;
+  size_t qk, bb, row_bytes;
+  if (!geom(t, &qk, &bb))
+    return apxo_matmat_q8act(t, raw, raw_len, n_out, n_in, k_cols, codes, n_in, scales, out,
+                             err);
   int rc = row_geometry(t, n_out, n_in, raw_len, &row_bytes, err);
   if (rc) return rc;
-  x86_rows_fn vec = simd && x86_shape(t, n_in) ? x86_rows() : NULL;
+  int64_t *xhat = NULL;
+  if (contract_rows) {
+    xhat = (int64_t *)malloc((k_cols * n_in > 0 ? k_cols * n_in : 1) * sizeof(int64_t));
+    for (size_t c = 0; c < k_cols; c++)
+      if (apxo_dequant_act(codes + c * n_in, n_in, scales + c * nb, nb, xhat + c * n_in)) {
+        free(xhat);
+        return apxo_matmat_q8act(t, raw, raw_len, n_out, n_in, k_cols, codes, n_in, scales,
+                                 out, err);
+      }
+  }
+  x86_rows_fn vec = simd && !contract_rows && x86_shape(t, n_in) ? x86_rows() : NULL;
   for (size_t i = 0; vec && i < k_cols * n_in; i++)
     if (codes[i] == -128) vec = NULL;
   int32_t *xsums = NULL;
@@ -914,13 +938,14 @@ static int run_mt(uint32_t t, const uint8_t *raw, size_t raw_len, size_t n_out,
     size_t lo = (size_t)i * per, hi = lo + per < n_out ? lo + per : n_out;
     if (lo > n_out) lo = n_out;
     tasks[i] = (mt_task){t, raw, row_bytes, lo, hi, n_in, k_cols, n_out,
-                         codes, scales, xsums, vec, out, 0, 0};
+                         codes, scales, xsums, vec, xhat, out, 0, 0};
   }
   pool_run(mt_item, tasks, threads);
   rc = 0;
   for (int i = 0; i < threads && rc == 0; i++) rc = tasks[i].rc;
   free(tasks);
   free(xsums);
+  free(xhat);
   if (rc != 0) /* any refusal: the single-threaded contract decides it */
     return apxo_matmat_q8act(t, raw, raw_len, n_out, n_in, k_cols, codes, n_in, scales,
                              out, err);

@@ -183,3 +183,28 @@ def test_q8_0_gemm_refusals_fall_to_the_per_column_rows():
     want = O.matmat_q8act(Q8_0, big, n_out, n_in, c, s)
     got = O.matmat_q8act_mt(Q8_0, big, n_out, n_in, c, s, 2, simd=True)
     assert want == got and isinstance(want, tuple)
+
+
+@pytest.mark.parametrize("t,n_in", [(Q6_K, 896), (Q4_K, 300), (Q8_0, 33), (Q6_K, 300)])
+@pytest.mark.parametrize("simd", [False, True])
+def test_threaded_contract_rows_equal_single_threaded(t, n_in, simd):
+    """Widths the fused rows do not take (ragged K-quants, a ragged Q8_0 block) run the contract,
+    matvec_fixed on the dequantized activation, over the pool's row chunks, as the reference's
+    chunked caller runs every row range on its pool (chart/ffn.rs:705-726); the values equal the
+    single-threaded call, and a refusal is still redecided in row order."""
+    rows = 29
+    raw = random_payload(t, rows, n_in, 0x3800, 0x3800, 0x5150 + n_in)
+    codes, scales = O.quant_act(random_x(n_in, 31))
+    want = O.matvec_q8act(t, raw, rows, n_in, codes, scales)
+    got = O.matvec_q8act_mt(t, raw, rows, n_in, codes, scales, 4, simd=simd)
+    assert not isinstance(want, tuple) and np.array_equal(want, got)
+    cs, ss = zip(*[O.quant_act(random_x(n_in, 60 + c)) for c in range(3)])
+    mm = O.matmat_q8act(t, raw, rows, n_in, np.stack(cs), np.stack(ss))
+    assert np.array_equal(mm, O.matmat_q8act_mt(t, raw, rows, n_in, np.stack(cs),
+                                                np.stack(ss), 3, simd=simd))
+    big = random_payload(t, rows, n_in, 0x7BFF, 0x7BFF, 4)
+    c = np.full(n_in, 127, dtype=np.int8)
+    s = np.full(-(-n_in // 32), 1 << 45, dtype=np.int64)
+    want = O.matvec_q8act(t, big, rows, n_in, c, s)
+    got = O.matvec_q8act_mt(t, big, rows, n_in, c, s, 4, simd=simd)
+    assert want == got and isinstance(want, tuple)
