@@ -1078,16 +1078,157 @@ static int gemm_q8_0_mt(const uint8_t *raw, size_t raw_len, size_t n_out, size_t
 }
 
 extern unsigned long apxo_x86_gemm_exact_groups;
-static unsigned long gemm_calls;
+static unsigned long gemm_calls, q4k_calls;
+unsigned long apxo_q4k_exact_groups;
 
 void apxo_gemm_counts(uint64_t *calls, uint64_t *exact_groups) {
   *calls = __atomic_load_n(&gemm_calls, __ATOMIC_RELAXED);
   *exact_groups = __atomic_load_n(&apxo_x86_gemm_exact_groups, __ATOMIC_RELAXED);
 }
 
+void apxo_q4k_counts(uint64_t *calls, uint64_t *exact_groups) {
+  *calls = __atomic_load_n(&q4k_calls, __ATOMIC_RELAXED);
+  *exact_groups = __atomic_load_n(&apxo_q4k_exact_groups, __ATOMIC_RELAXED);
+}
+
+/* One fused row's rounded value for the vector kernels' exact fallback: 0 ok, 1 a non-finite
+ * scale, 2 an output outside i64. */
+int apxo_fast_row_value(uint32_t t, const uint8_t *row, size_t n_in, const int8_t *codes,
+                        const int64_t *S, int64_t *out) {
+  i128 acc;
+  if (fast_row(t, row, n_in, codes, S, &acc)) return 1;
+  return round_to_i64(acc, out) ? 2 : 0;
+}
+
+/* ---- the k-column Q4_K projection (chart/kcols.rs:1406-1464): the column pack
+ * (pack_cols, kcols.rs:505-614) and the row split; the rows are apx_oracle_x86.c's. */
+typedef int (*q4k_rows_fn)(const uint8_t *, size_t, size_t, size_t, size_t, size_t, size_t,
+                           const uint32_t *, const int32_t *, const int64_t *, const int64_t *,
+                           const uint32_t *, const uint32_t *, uint32_t, const int8_t *,
+                           const int64_t *, int64_t *, size_t);
+int apxo_x86_q4k_rows_avx2(const uint8_t *, size_t, size_t, size_t, size_t, size_t, size_t,
+                           const uint32_t *, const int32_t *, const int64_t *, const int64_t *,
+                           const uint32_t *, const uint32_t *, uint32_t, const int8_t *,
+                           const int64_t *, int64_t *, size_t);
+int apxo_x86_q4k_rows_vnni(const uint8_t *, size_t, size_t, size_t, size_t, size_t, size_t,
+                           const uint32_t *, const int32_t *, const int64_t *, const int64_t *,
+                           const uint32_t *, const uint32_t *, uint32_t, const int8_t *,
+                           const int64_t *, int64_t *, size_t);
+
+typedef struct {
+  q4k_rows_fn fn;
+  const uint8_t *raw;
+  size_t row_bytes, sblocks, n_out, n_in, k_cols, per;
+  const uint32_t *words, *emin, *cspread;
+  const int32_t *xs;
+  const int64_t *she, *sho, *scales;
+  const int8_t *codes;
+  uint32_t limit;
+  int64_t *out;
+  int bail[POOL_MAX];
+} q4k_job;
+
+static void q4k_item(void *ctx, int i) {
+  q4k_job *j = (q4k_job *)ctx;
+  size_t lo = (size_t)i * j->per, hi = lo + j->per < j->n_out ? lo + j->per : j->n_out;
+  j->bail[i] = lo < hi ? j->fn(j->raw, j->row_bytes, j->sblocks, lo, hi, j->k_cols, j->n_in,
+                               j->words, j->xs, j->she, j->sho, j->emin, j->cspread, j->limit,
+                               j->codes, j->scales, j->out, j->n_out)
+                       : 0;
+}
+
+/* lane_spread_limit (kcols.rs:455-462): 62 − 34 − ⌈log2 groups⌉. */
+static uint32_t lane_spread_limit(size_t groups) {
+  uint32_t log = 0;
+  while (((size_t)1 << log) < groups) log++;
+  return log >= 28 ? 0 : 28 - log;
+}
+
+/* 1 when the k-column kernel ran and wrote every output; 0 when the call takes the per-column
+ * rows (which also decide every refusal). */
+static int gemm_q4_k_mt(const uint8_t *raw, size_t raw_len, size_t n_out, size_t n_in,
+                        size_t k_cols, const int8_t *codes, const int64_t *scales, int threads,
+                        int64_t *out) {
+  size_t sblocks = n_in / QK_K, G = n_in / ACT_QK;
+  if (n_in % QK_K || sblocks == 0 || sblocks > 256 || k_cols == 0 || n_out == 0) return 0;
+  int f = apxo_simd_features();
+  if (!(f & 1)) return 0;
+  q4k_rows_fn fn = (f & 2) ? apxo_x86_q4k_rows_vnni : apxo_x86_q4k_rows_avx2;
+  if (raw_len / Q4_K_BYTES / sblocks < n_out) return 0;
+  for (size_t c = 0; c < k_cols; c++) { /* every column on its fast row, narrow bound */
+    int fast = 0;
+    if (plan(APX_GGML_TYPE_Q4_K, n_in, codes + c * n_in, n_in, scales + c * G, G, &fast) != 0 ||
+        !fast || !fast_bound_ok(n_in, 1008, scales + c * G, G, 1))
+      return 0;
+  }
+  pthread_once(&f16_table_once, f16_table_build);
+  size_t groups = (k_cols + 7) / 8;
+  uint32_t *words = (uint32_t *)calloc(groups * G * 64, sizeof(uint32_t));
+  int32_t *xs = (int32_t *)calloc(groups * G * 8, sizeof(int32_t));
+  int64_t *she = (int64_t *)calloc(groups * G * 4, sizeof(int64_t));
+  int64_t *sho = (int64_t *)calloc(groups * G * 4, sizeof(int64_t));
+  uint32_t *emin = (uint32_t *)calloc(groups * 8, sizeof(uint32_t));
+  uint32_t *cspread = (uint32_t *)calloc(groups, sizeof(uint32_t));
+  q4k_job *job = (q4k_job *)calloc(1, sizeof(q4k_job));
+  int ok = words && xs && she && sho && emin && cspread && job;
+  for (size_t c = 0; ok && c < k_cols; c++) {
+    size_t cg = c / 8, lane = c % 8;
+    uint32_t e_lo = UINT32_MAX;
+    for (size_t g = 0; g < G; g++) {
+      int64_t S = scales[c * G + g];
+      if (S < 0 || (S & (S - 1))) ok = 0;
+      if (S > 0 && (uint32_t)__builtin_ctzll((uint64_t)S) < e_lo)
+        e_lo = (uint32_t)__builtin_ctzll((uint64_t)S);
+    }
+    if (e_lo == UINT32_MAX) e_lo = 0;
+    emin[c] = e_lo;
+    for (size_t g = 0; ok && g < G; g++) {
+      int64_t S = scales[c * G + g];
+      size_t gi = cg * G + g;
+      uint32_t sh = S > 0 ? (uint32_t)__builtin_ctzll((uint64_t)S) - e_lo : 0;
+      if (sh > cspread[cg]) cspread[cg] = sh;
+      (lane & 1 ? sho : she)[gi * 4 + lane / 2] = sh;
+      int32_t sum = 0;
+      for (int q = 0; q < 8; q++) {
+        uint32_t w = 0;
+        for (int i = 0; i < 4; i++) {
+          int8_t x = S > 0 ? codes[c * n_in + g * 32 + 4 * q + i] : 0;
+          sum += x;
+          w |= (uint32_t)(uint8_t)x << (8 * i);
+        }
+        words[(gi * 8 + q) * 8 + lane] = w;
+      }
+      xs[gi * 8 + lane] = sum;
+    }
+  }
+  int done = 0;
+  if (ok) {
+    if (threads < 1) threads = 1;
+    if (threads > POOL_MAX) threads = POOL_MAX;
+    if ((size_t)threads > n_out) threads = (int)n_out;
+    size_t per = (n_out + (size_t)threads - 1) / (size_t)threads;
+    per += per & 1;
+    *job = (q4k_job){fn, raw, sblocks * Q4_K_BYTES, sblocks, n_out, n_in, k_cols, per, words,
+                     emin, cspread, xs, she, sho, scales, codes, lane_spread_limit(G), out,
+                     {0}};
+    pool_run(q4k_item, job, threads);
+    done = 1;
+    for (int i = 0; i < threads; i++) done &= !job->bail[i];
+  }
+  free(words);
+  free(xs);
+  free(she);
+  free(sho);
+  free(emin);
+  free(cspread);
+  free(job);
+  return done;
+}
+
 /* With AVX-VNNI, Q8_0 calls whose every column takes the fast rows run the k-column GEMM, as
- * the reference's matmat_q8act tries gemm_q8_0 first (kern/matmat.rs:134-146); everything
- * else (and every call the GEMM bails on) runs the vector rows per column. */
+ * the reference's matmat_q8act tries gemm_q8_0 first (kern/matmat.rs:134-146); Q4_K calls on
+ * whole super-blocks run the k-column Q4_K kernel (gemm_q4_k, matmat.rs:163-177); everything
+ * else (and every call those kernels bail on) runs the vector rows per column. */
 int apxo_matmat_q8act_simd_mt(uint32_t t, const uint8_t *raw, size_t raw_len, size_t n_out,
                               size_t n_in, size_t k_cols, const int8_t *codes,
                               const int64_t *scales, int threads, int64_t *out,
@@ -1095,6 +1236,12 @@ int apxo_matmat_q8act_simd_mt(uint32_t t, const uint8_t *raw, size_t raw_len, si
   if (t == APX_GGML_TYPE_Q8_0 &&
       gemm_q8_0_mt(raw, raw_len, n_out, n_in, k_cols, codes, scales, threads, out)) {
     __atomic_fetch_add(&gemm_calls, 1, __ATOMIC_RELAXED);
+    clear(err);
+    return 0;
+  }
+  if (t == APX_GGML_TYPE_Q4_K &&
+      gemm_q4_k_mt(raw, raw_len, n_out, n_in, k_cols, codes, scales, threads, out)) {
+    __atomic_fetch_add(&q4k_calls, 1, __ATOMIC_RELAXED);
     clear(err);
     return 0;
   }

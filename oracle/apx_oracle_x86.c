@@ -27,6 +27,7 @@
 #include <immintrin.h>
 #include <stddef.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include "../include/apeiron_cuda.h"
 
@@ -327,3 +328,175 @@ int apxo_x86_gemm_rows(const uint8_t *raw, size_t row_bytes, size_t blocks, size
   return 0;
 }
 #endif
+
+/* ---- the k-column Q4_K projection of the prefill baseline (chart/kcols.rs:1406-1464) -------
+ *
+ * The reference runs multi-column Q4_K calls (n_in % 256 == 0, every column on its fast row
+ * under the narrow bound) through one pass over each weight row: the row's nibbles are dotted
+ * against groups of 8 token columns (unsigned nibble × signed code, `vpdpbusd` or
+ * `vpmaddubsw` + `vpmaddwd`, both exact: pair sums ≤ 2·15·127), and each 32-lane group g adds
+ *     ((m_d·sc_g)·D_g) << (k_d − kmin + e_g − emin) − ((m_m·m_g)·X_g) << (k_m − kmin + e_g − emin)
+ * to the column's i64 lane (d = m_d·2^k_d, dmin = m_m·2^k_m by f16_split, X_g = Σ codes of the
+ * group).  A term is below 2^33 + 2^29 < 2^34, so G groups with every shift at most `spread`
+ * stay below 2^(34 + ⌈log2 G⌉ + spread): past lane_spread_limit (kcols.rs:455-462) a (row,
+ * column group) takes the exact i128 fast row instead.  The output is finish(acc, kmin + emin).
+ * 64-bit products come from `vpmuldq`, which reads the even 32-bit lanes, so the column shifts
+ * are kept per group in two orders: even columns (0, 2, 4, 6) and odd ones. */
+
+#if APX_X86_VNNI
+#define Q4K_NAME apxo_x86_q4k_rows_vnni
+#else
+#define Q4K_NAME apxo_x86_q4k_rows_avx2
+#endif
+
+int apxo_fast_row_value(uint32_t t, const uint8_t *row, size_t n_in, const int8_t *codes,
+                        const int64_t *S, int64_t *out);
+int apxo_f16_split(uint16_t h, int32_t *m, uint32_t *k);
+int apxo_finish(int64_t acc, uint32_t s, int64_t *out);
+
+/* (row, column group) pairs sent to the exact rows, for the tests (defined in apx_oracle.c). */
+extern unsigned long apxo_q4k_exact_groups;
+
+#define Q4K_MAX_SBLOCKS 256 /* n_in <= 65536 */
+
+static inline __m256i quad_dot(__m256i acc, __m256i w_u8, __m256i x_i8) {
+#if APX_X86_VNNI
+  return _mm256_dpbusd_avx_epi32(acc, w_u8, x_i8);
+#else
+  return _mm256_add_epi32(acc, _mm256_madd_epi16(_mm256_maddubs_epi16(w_u8, x_i8),
+                                                 _mm256_set1_epi16(1)));
+#endif
+}
+
+/* One row's per-group coefficients and weight bytes; 1 on a non-finite scale. */
+typedef struct {
+  uint8_t *w;      /* n_in unpacked nibbles, lane order */
+  int64_t *c1, *c2; /* m_d·sc_g, m_m·m_g per group */
+  int64_t *a, *b;   /* k_d − kmin, k_m − kmin per group */
+  uint32_t kmin, spread;
+} q4k_row;
+
+static int q4k_row_prep(const uint8_t *row, size_t sblocks, q4k_row *r) {
+  uint32_t kmin = UINT32_MAX, kmax = 0;
+  int32_t md[Q4K_MAX_SBLOCKS], mm[Q4K_MAX_SBLOCKS];
+  uint32_t kd[Q4K_MAX_SBLOCKS], km[Q4K_MAX_SBLOCKS];
+  for (size_t b = 0; b < sblocks; b++) {
+    const uint8_t *blk = row + b * Q4_K_BYTES;
+    if (apxo_f16_split(word(blk), &md[b], &kd[b]) || apxo_f16_split(word(blk + 2), &mm[b], &km[b]))
+      return 1;
+    uint32_t lo = kd[b] < km[b] ? kd[b] : km[b], hi = kd[b] < km[b] ? km[b] : kd[b];
+    kmin = lo < kmin ? lo : kmin;
+    kmax = hi > kmax ? hi : kmax;
+  }
+  const __m256i nib = _mm256_set1_epi8(0x0F);
+  for (size_t b = 0; b < sblocks; b++) {
+    const uint8_t *blk = row + b * Q4_K_BYTES;
+    for (int p = 0; p < 4; p++) {
+      __m256i q = ld(blk + 16 + 32 * p);
+      _mm256_storeu_si256((__m256i *)(r->w + b * 256 + 64 * p), _mm256_and_si256(q, nib));
+      _mm256_storeu_si256((__m256i *)(r->w + b * 256 + 64 * p + 32),
+                          _mm256_and_si256(_mm256_srli_epi16(q, 4), nib));
+    }
+    for (int j = 0; j < 8; j++) {
+      int sc, m;
+      scale_min(blk + 4, j, &sc, &m);
+      size_t g = b * 8 + (size_t)j;
+      r->c1[g] = (int64_t)md[b] * sc;
+      r->c2[g] = (int64_t)mm[b] * m;
+      r->a[g] = (int64_t)kd[b] - kmin;
+      r->b[g] = (int64_t)km[b] - kmin;
+    }
+  }
+  r->kmin = kmin;
+  r->spread = kmax - kmin;
+  return 0;
+}
+
+static inline void q4k_fold(__m256i d, __m256i x, const q4k_row *r, size_t g, __m256i she,
+                            __m256i sho, __m256i *ae, __m256i *ao) {
+  __m256i c1 = _mm256_set1_epi64x(r->c1[g]), c2 = _mm256_set1_epi64x(r->c2[g]);
+  __m256i a = _mm256_set1_epi64x(r->a[g]), b = _mm256_set1_epi64x(r->b[g]);
+  __m256i de = d, dodd = _mm256_srli_epi64(d, 32), xe = x, xodd = _mm256_srli_epi64(x, 32);
+  *ae = _mm256_add_epi64(*ae, _mm256_sllv_epi64(_mm256_mul_epi32(de, c1), _mm256_add_epi64(she, a)));
+  *ae = _mm256_sub_epi64(*ae, _mm256_sllv_epi64(_mm256_mul_epi32(xe, c2), _mm256_add_epi64(she, b)));
+  *ao = _mm256_add_epi64(*ao, _mm256_sllv_epi64(_mm256_mul_epi32(dodd, c1), _mm256_add_epi64(sho, a)));
+  *ao = _mm256_sub_epi64(*ao, _mm256_sllv_epi64(_mm256_mul_epi32(xodd, c2), _mm256_add_epi64(sho, b)));
+}
+
+/* Rows [lo, hi) of the k-column Q4_K projection.  words: [cgroup][g][quad][lane] u32 (four
+ * codes of column 8·cgroup + lane, zero for zero-scale groups and padding lanes); xs:
+ * [cgroup][g][lane] i32; she/sho: [cgroup][g][4] i64 (e − emin of the even / odd columns);
+ * emin per column; cspread per column group.  out[c·n_out + o].  Returns 0, or 1 when the
+ * caller must redecide the call on the per-column path. */
+int Q4K_NAME(const uint8_t *raw, size_t row_bytes, size_t sblocks, size_t lo, size_t hi,
+             size_t k_cols, size_t n_in, const uint32_t *words, const int32_t *xs,
+             const int64_t *she, const int64_t *sho, const uint32_t *emin,
+             const uint32_t *cspread, uint32_t limit, const int8_t *codes,
+             const int64_t *scales, int64_t *out, size_t n_out) {
+  size_t G = sblocks * 8, groups = (k_cols + 7) / 8;
+  uint8_t *wbuf = (uint8_t *)malloc(2 * n_in);
+  int64_t *coef = (int64_t *)malloc(8 * G * sizeof(int64_t));
+  if (!wbuf || !coef) {
+    free(wbuf);
+    free(coef);
+    return 1;
+  }
+  q4k_row rr[2];
+  for (int r = 0; r < 2; r++)
+    rr[r] = (q4k_row){wbuf + r * n_in, coef + (4 * r) * G, coef + (4 * r + 1) * G,
+                      coef + (4 * r + 2) * G, coef + (4 * r + 3) * G, 0, 0};
+  int bail = 0;
+  for (size_t o = lo; o < hi && !bail; o += 2) {
+    int two = o + 1 < hi;
+    const uint8_t *ra = raw + o * row_bytes, *rb = two ? ra + row_bytes : ra;
+    if (q4k_row_prep(ra, sblocks, &rr[0]) || q4k_row_prep(rb, sblocks, &rr[1])) {
+      bail = 1;
+      break;
+    }
+    for (size_t cg = 0; cg < groups && !bail; cg++) {
+      size_t c0 = cg * 8, nc = k_cols - c0 < 8 ? k_cols - c0 : 8;
+      if (rr[0].spread + cspread[cg] > limit || rr[1].spread + cspread[cg] > limit) {
+        __atomic_fetch_add(&apxo_q4k_exact_groups, 1, __ATOMIC_RELAXED);
+        for (size_t c = c0; c < c0 + nc && !bail; c++)
+          for (int r = 0; r <= two && !bail; r++)
+            if (apxo_fast_row_value(APX_GGML_TYPE_Q4_K, r ? rb : ra, n_in, codes + c * n_in,
+                                    scales + c * (n_in / 32), &out[c * n_out + o + r]))
+              bail = 1;
+        continue;
+      }
+      __m256i ae0 = _mm256_setzero_si256(), ao0 = ae0, ae1 = ae0, ao1 = ae0;
+      const uint32_t *wg = words + cg * G * 64;
+      for (size_t g = 0; g < G; g++) {
+        const uint32_t *wq = wg + g * 64;
+        const uint8_t *w0 = rr[0].w + g * 32, *w1 = rr[1].w + g * 32;
+        __m256i d0 = _mm256_setzero_si256(), d1 = d0;
+        for (int q = 0; q < 8; q++) {
+          __m256i x = ld(wq + 8 * q);
+          int32_t u0, u1;
+          __builtin_memcpy(&u0, w0 + 4 * q, 4);
+          __builtin_memcpy(&u1, w1 + 4 * q, 4);
+          d0 = quad_dot(d0, _mm256_set1_epi32(u0), x);
+          d1 = quad_dot(d1, _mm256_set1_epi32(u1), x);
+        }
+        size_t gi = cg * G + g;
+        __m256i xv = ld(xs + gi * 8), she_v = ld(she + gi * 4), sho_v = ld(sho + gi * 4);
+        q4k_fold(d0, xv, &rr[0], g, she_v, sho_v, &ae0, &ao0);
+        q4k_fold(d1, xv, &rr[1], g, she_v, sho_v, &ae1, &ao1);
+      }
+      int64_t e0[4], od0[4], e1[4], od1[4];
+      _mm256_storeu_si256((__m256i *)e0, ae0);
+      _mm256_storeu_si256((__m256i *)od0, ao0);
+      _mm256_storeu_si256((__m256i *)e1, ae1);
+      _mm256_storeu_si256((__m256i *)od1, ao1);
+      for (size_t c = 0; c < nc && !bail; c++) {
+        int64_t v0 = c & 1 ? od0[c / 2] : e0[c / 2], v1 = c & 1 ? od1[c / 2] : e1[c / 2];
+        if (apxo_finish(v0, rr[0].kmin + emin[c0 + c], &out[(c0 + c) * n_out + o]) ||
+            (two && apxo_finish(v1, rr[1].kmin + emin[c0 + c], &out[(c0 + c) * n_out + o + 1])))
+          bail = 1;
+      }
+    }
+  }
+  free(wbuf);
+  free(coef);
+  return bail;
+}

@@ -99,6 +99,7 @@ def _declare(l):
     l.apxo_matmat_q8act_simd_mt.argtypes = l.apxo_matmat_q8act_mt.argtypes
     l.apxo_simd_features.argtypes = []
     l.apxo_gemm_counts.argtypes = [C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]
+    l.apxo_q4k_counts.argtypes = [C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]
 
 
 def _p(a: np.ndarray):
@@ -340,6 +341,14 @@ def gemm_counts():
     i128 dot) since the library loaded."""
     a, b = C.c_uint64(), C.c_uint64()
     lib().apxo_gemm_counts(C.byref(a), C.byref(b))
+    return a.value, b.value
+
+
+def q4k_counts():
+    """(matmat calls the k-column Q4_K kernel completed, (row, column group) pairs it sent to
+    the exact rows) since the library loaded."""
+    a, b = C.c_uint64(), C.c_uint64()
+    lib().apxo_q4k_counts(C.byref(a), C.byref(b))
     return a.value, b.value
 
 

@@ -208,3 +208,62 @@ def test_threaded_contract_rows_equal_single_threaded(t, n_in, simd):
     want = O.matvec_q8act(t, big, rows, n_in, c, s)
     got = O.matvec_q8act_mt(t, big, rows, n_in, c, s, 4, simd=simd)
     assert want == got and isinstance(want, tuple)
+
+
+@pytest.mark.parametrize("n_out,n_in,k", [(37, 1536, 13), (16, 256, 8), (5, 8960, 3),
+                                          (64, 1024, 64), (1, 256, 1)])
+def test_q4_k_kcols_equals_per_column(isa, n_out, n_in, k):
+    """The k-column Q4_K kernel of the prefill baseline (chart/kcols.rs:1406-1464) equals the
+    per-column fused rows on the benchmark distribution, in both instruction forms."""
+    raw = synth.payload(Q4_K, n_out, n_in, seed=n_out + k)
+    cs, ss = [], []
+    for c in range(k):
+        q = O.quant_act(synth.f32_to_q32(synth.activation_f32(n_in, seed=700 + c)))
+        cs.append(q[0])
+        ss.append(q[1])
+    codes, scales = np.stack(cs), np.stack(ss)
+    want = O.matmat_q8act(Q4_K, raw, n_out, n_in, codes, scales)
+    assert not isinstance(want, tuple)
+    calls = O.q4k_counts()[0]
+    got = O.matmat_q8act_mt(Q4_K, raw, n_out, n_in, codes, scales, 4, simd=True)
+    assert np.array_equal(want, got)
+    assert O.q4k_counts()[0] == calls + 1
+
+
+def test_q4_k_kcols_random_headers_spreads_and_refusals(isa):
+    """Random header bytes (every sub-scale and min pattern, both signs of d and dmin), scale
+    spreads past the lane limit (exact rows per (row, group)), zero groups, an all-zero column,
+    and a non-finite scale (the call refuses as the per-column contract does)."""
+    n_out, n_in, k = 11, 512, 10
+    for seed, d, dmin in [(21, 0x3800, 0x3800), (22, 0x0001, 0x7BFF), (23, 0xBC00, 0x3C00)]:
+        raw = random_payload(Q4_K, n_out, n_in, d, dmin, seed)
+        cs, ss = [], []
+        for c in range(k):
+            x = random_x(n_in, seed * 100 + c)
+            if c % 3 == 1:
+                x[32 * (c % 16):32 * (c % 16) + 32] <<= 14
+            if c == 4:
+                x[64:128] = 0
+            if c == 7:
+                x[:] = 0
+            q = O.quant_act(x)
+            cs.append(q[0])
+            ss.append(q[1])
+        codes, scales = np.stack(cs), np.stack(ss)
+        want = O.matmat_q8act(Q4_K, raw, n_out, n_in, codes, scales)
+        calls, exact = O.q4k_counts()
+        got = O.matmat_q8act_mt(Q4_K, raw, n_out, n_in, codes, scales, 3, simd=True)
+        if isinstance(want, tuple):
+            assert want == got
+        else:
+            assert np.array_equal(want, got)
+            assert O.q4k_counts()[0] == calls + 1
+        if seed == 22:  # subnormal d against the largest dmin: spread 29 > the limit
+            assert O.q4k_counts()[1] > exact
+    bad = synth.payload(Q4_K, n_out, n_in, seed=5).reshape(n_out, -1)
+    bad[6, 144 + 2:144 + 4] = (0x00, 0xFC)  # -Inf dmin in row 6, super-block 1
+    cs, ss = zip(*[O.quant_act(random_x(n_in, 90 + c)) for c in range(3)])
+    want = O.matmat_q8act(Q4_K, bad.reshape(-1), n_out, n_in, np.stack(cs), np.stack(ss))
+    got = O.matmat_q8act_mt(Q4_K, bad.reshape(-1), n_out, n_in, np.stack(cs), np.stack(ss), 2,
+                            simd=True)
+    assert want == got and want[:2] == ("err", 6)
