@@ -267,3 +267,29 @@ def test_q4_k_kcols_random_headers_spreads_and_refusals(isa):
     got = O.matmat_q8act_mt(Q4_K, bad.reshape(-1), n_out, n_in, np.stack(cs), np.stack(ss), 2,
                             simd=True)
     assert want == got and want[:2] == ("err", 6)
+
+
+def test_pool_survives_fork():
+    """The oracle's host pool is started in this process; a forked child (which has only the
+    forking thread) starts its own workers and finishes a threaded call."""
+    import os
+    import signal
+    import time
+
+    raw = synth.payload(Q8_0, 64, 256, seed=1)
+    codes, scales = O.quant_act(random_x(256, 2))
+    want = O.matvec_q8act_mt(Q8_0, raw, 64, 256, codes, scales, 4, simd=True)
+    pid = os.fork()
+    if pid == 0:
+        got = O.matvec_q8act_mt(Q8_0, raw, 64, 256, codes, scales, 4, simd=True)
+        os._exit(0 if np.array_equal(got, want) else 1)
+    deadline = time.time() + 30
+    while time.time() < deadline:
+        done, status = os.waitpid(pid, os.WNOHANG)
+        if done:
+            assert os.WIFEXITED(status) and os.WEXITSTATUS(status) == 0
+            return
+        time.sleep(0.05)
+    os.kill(pid, signal.SIGKILL)
+    os.waitpid(pid, 0)
+    raise AssertionError("the forked child's pooled call did not finish")
