@@ -1078,8 +1078,8 @@ static int gemm_q8_0_mt(const uint8_t *raw, size_t raw_len, size_t n_out, size_t
 }
 
 extern unsigned long apxo_x86_gemm_exact_groups;
-static unsigned long gemm_calls, q4k_calls;
-unsigned long apxo_q4k_exact_groups;
+static unsigned long gemm_calls, q4k_calls, q6k_calls;
+unsigned long apxo_q4k_exact_groups, apxo_q6k_exact_groups;
 
 void apxo_gemm_counts(uint64_t *calls, uint64_t *exact_groups) {
   *calls = __atomic_load_n(&gemm_calls, __ATOMIC_RELAXED);
@@ -1091,6 +1091,18 @@ void apxo_q4k_counts(uint64_t *calls, uint64_t *exact_groups) {
   *exact_groups = __atomic_load_n(&apxo_q4k_exact_groups, __ATOMIC_RELAXED);
 }
 
+void apxo_q6k_counts(uint64_t *calls, uint64_t *exact_groups) {
+  *calls = __atomic_load_n(&q6k_calls, __ATOMIC_RELAXED);
+  *exact_groups = __atomic_load_n(&apxo_q6k_exact_groups, __ATOMIC_RELAXED);
+}
+
+/* A Q6_K super-block's 256 unsigned 6-bit codes (q, before the −32 offset). */
+void apxo_q6k_codes_u6(const uint8_t *blk, uint8_t *out) {
+  int8_t q[QK_K];
+  q6k_codes(blk, q);
+  for (int i = 0; i < QK_K; i++) out[i] = (uint8_t)(q[i] + 32);
+}
+
 /* One fused row's rounded value for the vector kernels' exact fallback: 0 ok, 1 a non-finite
  * scale, 2 an output outside i64. */
 int apxo_fast_row_value(uint32_t t, const uint8_t *row, size_t n_in, const int8_t *codes,
@@ -1100,7 +1112,7 @@ int apxo_fast_row_value(uint32_t t, const uint8_t *row, size_t n_in, const int8_
   return round_to_i64(acc, out) ? 2 : 0;
 }
 
-/* ---- the k-column Q4_K projection (chart/kcols.rs:1406-1464): the column pack
+/* ---- the k-column Q4_K and Q6_K projections (chart/kcols.rs:1406-1518): the column pack
  * (pack_cols, kcols.rs:505-614) and the row split; the rows are apx_oracle_x86.c's. */
 typedef int (*q4k_rows_fn)(const uint8_t *, size_t, size_t, size_t, size_t, size_t, size_t,
                            const uint32_t *, const int32_t *, const int64_t *, const int64_t *,
@@ -1111,6 +1123,14 @@ int apxo_x86_q4k_rows_avx2(const uint8_t *, size_t, size_t, size_t, size_t, size
                            const uint32_t *, const uint32_t *, uint32_t, const int8_t *,
                            const int64_t *, int64_t *, size_t);
 int apxo_x86_q4k_rows_vnni(const uint8_t *, size_t, size_t, size_t, size_t, size_t, size_t,
+                           const uint32_t *, const int32_t *, const int64_t *, const int64_t *,
+                           const uint32_t *, const uint32_t *, uint32_t, const int8_t *,
+                           const int64_t *, int64_t *, size_t);
+int apxo_x86_q6k_rows_avx2(const uint8_t *, size_t, size_t, size_t, size_t, size_t, size_t,
+                           const uint32_t *, const int32_t *, const int64_t *, const int64_t *,
+                           const uint32_t *, const uint32_t *, uint32_t, const int8_t *,
+                           const int64_t *, int64_t *, size_t);
+int apxo_x86_q6k_rows_vnni(const uint8_t *, size_t, size_t, size_t, size_t, size_t, size_t,
                            const uint32_t *, const int32_t *, const int64_t *, const int64_t *,
                            const uint32_t *, const uint32_t *, uint32_t, const int8_t *,
                            const int64_t *, int64_t *, size_t);
@@ -1144,27 +1164,31 @@ static uint32_t lane_spread_limit(size_t groups) {
   return log >= 28 ? 0 : 28 - log;
 }
 
-/* 1 when the k-column kernel ran and wrote every output; 0 when the call takes the per-column
- * rows (which also decide every refusal). */
-static int gemm_q4_k_mt(const uint8_t *raw, size_t raw_len, size_t n_out, size_t n_in,
-                        size_t k_cols, const int8_t *codes, const int64_t *scales, int threads,
-                        int64_t *out) {
-  size_t sblocks = n_in / QK_K, G = n_in / ACT_QK;
+/* 1 when the k-column Q4_K / Q6_K kernel ran and wrote every output; 0 when the call takes
+ * the per-column rows (which also decide every refusal).  Q6_K keeps its block sums per
+ * 16-lane group (xs), Q4_K per 32-lane group. */
+static int gemm_kq_mt(uint32_t t, const uint8_t *raw, size_t raw_len, size_t n_out, size_t n_in,
+                      size_t k_cols, const int8_t *codes, const int64_t *scales, int threads,
+                      int64_t *out) {
+  int q6 = t == APX_GGML_TYPE_Q6_K;
+  size_t sblocks = n_in / QK_K, G = n_in / ACT_QK, block_bytes = q6 ? Q6_K_BYTES : Q4_K_BYTES;
+  size_t xlanes = q6 ? 16 : 32, XG = n_in / xlanes;
   if (n_in % QK_K || sblocks == 0 || sblocks > 256 || k_cols == 0 || n_out == 0) return 0;
   int f = apxo_simd_features();
   if (!(f & 1)) return 0;
-  q4k_rows_fn fn = (f & 2) ? apxo_x86_q4k_rows_vnni : apxo_x86_q4k_rows_avx2;
-  if (raw_len / Q4_K_BYTES / sblocks < n_out) return 0;
+  q4k_rows_fn fn = q6 ? ((f & 2) ? apxo_x86_q6k_rows_vnni : apxo_x86_q6k_rows_avx2)
+                      : ((f & 2) ? apxo_x86_q4k_rows_vnni : apxo_x86_q4k_rows_avx2);
+  if (raw_len / block_bytes / sblocks < n_out) return 0;
   for (size_t c = 0; c < k_cols; c++) { /* every column on its fast row, narrow bound */
     int fast = 0;
-    if (plan(APX_GGML_TYPE_Q4_K, n_in, codes + c * n_in, n_in, scales + c * G, G, &fast) != 0 ||
-        !fast || !fast_bound_ok(n_in, 1008, scales + c * G, G, 1))
+    if (plan(t, n_in, codes + c * n_in, n_in, scales + c * G, G, &fast) != 0 || !fast ||
+        !fast_bound_ok(n_in, q6 ? 4096 : 1008, scales + c * G, G, 1))
       return 0;
   }
   pthread_once(&f16_table_once, f16_table_build);
   size_t groups = (k_cols + 7) / 8;
   uint32_t *words = (uint32_t *)calloc(groups * G * 64, sizeof(uint32_t));
-  int32_t *xs = (int32_t *)calloc(groups * G * 8, sizeof(int32_t));
+  int32_t *xs = (int32_t *)calloc(groups * XG * 8, sizeof(int32_t));
   int64_t *she = (int64_t *)calloc(groups * G * 4, sizeof(int64_t));
   int64_t *sho = (int64_t *)calloc(groups * G * 4, sizeof(int64_t));
   uint32_t *emin = (uint32_t *)calloc(groups * 8, sizeof(uint32_t));
@@ -1188,17 +1212,22 @@ static int gemm_q4_k_mt(const uint8_t *raw, size_t raw_len, size_t n_out, size_t
       uint32_t sh = S > 0 ? (uint32_t)__builtin_ctzll((uint64_t)S) - e_lo : 0;
       if (sh > cspread[cg]) cspread[cg] = sh;
       (lane & 1 ? sho : she)[gi * 4 + lane / 2] = sh;
-      int32_t sum = 0;
+      int32_t sum[2] = {0, 0};
       for (int q = 0; q < 8; q++) {
         uint32_t w = 0;
         for (int i = 0; i < 4; i++) {
           int8_t x = S > 0 ? codes[c * n_in + g * 32 + 4 * q + i] : 0;
-          sum += x;
+          sum[q / 4] += x;
           w |= (uint32_t)(uint8_t)x << (8 * i);
         }
         words[(gi * 8 + q) * 8 + lane] = w;
       }
-      xs[gi * 8 + lane] = sum;
+      if (q6) {
+        xs[(cg * XG + 2 * g) * 8 + lane] = sum[0];
+        xs[(cg * XG + 2 * g + 1) * 8 + lane] = sum[1];
+      } else {
+        xs[gi * 8 + lane] = sum[0] + sum[1];
+      }
     }
   }
   int done = 0;
@@ -1208,8 +1237,8 @@ static int gemm_q4_k_mt(const uint8_t *raw, size_t raw_len, size_t n_out, size_t
     if ((size_t)threads > n_out) threads = (int)n_out;
     size_t per = (n_out + (size_t)threads - 1) / (size_t)threads;
     per += per & 1;
-    *job = (q4k_job){fn, raw, sblocks * Q4_K_BYTES, sblocks, n_out, n_in, k_cols, per, words,
-                     emin, cspread, xs, she, sho, scales, codes, lane_spread_limit(G), out,
+    *job = (q4k_job){fn, raw, sblocks * block_bytes, sblocks, n_out, n_in, k_cols, per, words,
+                     emin, cspread, xs, she, sho, scales, codes, lane_spread_limit(XG), out,
                      {0}};
     pool_run(q4k_item, job, threads);
     done = 1;
@@ -1226,8 +1255,9 @@ static int gemm_q4_k_mt(const uint8_t *raw, size_t raw_len, size_t n_out, size_t
 }
 
 /* With AVX-VNNI, Q8_0 calls whose every column takes the fast rows run the k-column GEMM, as
- * the reference's matmat_q8act tries gemm_q8_0 first (kern/matmat.rs:134-146); Q4_K calls on
- * whole super-blocks run the k-column Q4_K kernel (gemm_q4_k, matmat.rs:163-177); everything
+ * the reference's matmat_q8act tries gemm_q8_0 first (kern/matmat.rs:134-146); Q4_K and Q6_K
+ * calls on whole super-blocks run the k-column kernels (gemm_q4_k / gemm_q6_k,
+ * matmat.rs:163-177); everything
  * else (and every call those kernels bail on) runs the vector rows per column. */
 int apxo_matmat_q8act_simd_mt(uint32_t t, const uint8_t *raw, size_t raw_len, size_t n_out,
                               size_t n_in, size_t k_cols, const int8_t *codes,
@@ -1239,9 +1269,9 @@ int apxo_matmat_q8act_simd_mt(uint32_t t, const uint8_t *raw, size_t raw_len, si
     clear(err);
     return 0;
   }
-  if (t == APX_GGML_TYPE_Q4_K &&
-      gemm_q4_k_mt(raw, raw_len, n_out, n_in, k_cols, codes, scales, threads, out)) {
-    __atomic_fetch_add(&q4k_calls, 1, __ATOMIC_RELAXED);
+  if ((t == APX_GGML_TYPE_Q4_K || t == APX_GGML_TYPE_Q6_K) &&
+      gemm_kq_mt(t, raw, raw_len, n_out, n_in, k_cols, codes, scales, threads, out)) {
+    __atomic_fetch_add(t == APX_GGML_TYPE_Q4_K ? &q4k_calls : &q6k_calls, 1, __ATOMIC_RELAXED);
     clear(err);
     return 0;
   }

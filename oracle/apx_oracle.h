@@ -112,6 +112,8 @@ void apxo_gemm_counts(uint64_t *calls, uint64_t *exact_groups);
 /* The same for the k-column Q4_K kernel (src/engine/chart/kcols.rs:1406-1464), which Q4_K
  * matmats on whole super-blocks run with AVX2. */
 void apxo_q4k_counts(uint64_t *calls, uint64_t *exact_groups);
+/* And for the k-column Q6_K kernel (kcols.rs:1466-1518). */
+void apxo_q6k_counts(uint64_t *calls, uint64_t *exact_groups);
 
 /* The FFN hidden activation (src/engine/chart/ffn.rs:246-284, ops/silu.rs:53-100,
  * numeric/fixed_exp.rs:1-184, mixer/f32_carrier.rs:262-375). */

@@ -500,3 +500,136 @@ int Q4K_NAME(const uint8_t *raw, size_t row_bytes, size_t sblocks, size_t lo, si
   free(coef);
   return bail;
 }
+
+/* ---- the k-column Q6_K projection (chart/kcols.rs:1466-1518) --------------------------------
+ *
+ * Q6_K weights are d·sc_h·(q − 32) over 16-lane groups h (q a 6-bit code, sc an int8).  Per
+ * 16-lane group the unsigned codes are dotted against the token codes (u8 × i8, exact in
+ * either instruction form: pair sums ≤ 2·63·127) and D_h = Σ q·x − 32·X_h (X_h = Σ x over the
+ * group, |D_h| < 2^16) is folded as ((m_d·sc_h)·D_h) << (k_d − kmin + e − emin), a term below
+ * 2^34, under lane_spread_limit(n_in / 16). */
+
+#if APX_X86_VNNI
+#define Q6K_NAME apxo_x86_q6k_rows_vnni
+#else
+#define Q6K_NAME apxo_x86_q6k_rows_avx2
+#endif
+
+void apxo_q6k_codes_u6(const uint8_t *blk, uint8_t *out);
+extern unsigned long apxo_q6k_exact_groups;
+
+typedef struct {
+  uint8_t *w;  /* n_in unsigned codes */
+  int64_t *c;  /* m_d·sc_h per 16-lane group */
+  int64_t *a;  /* k_d − kmin per super-block */
+  uint32_t kmin, spread;
+} q6k_row;
+
+static int q6k_row_prep(const uint8_t *row, size_t sblocks, q6k_row *r) {
+  uint32_t kmin = UINT32_MAX, kmax = 0;
+  int32_t md[Q4K_MAX_SBLOCKS];
+  uint32_t kd[Q4K_MAX_SBLOCKS];
+  for (size_t b = 0; b < sblocks; b++) {
+    if (apxo_f16_split(word(row + b * 210 + 208), &md[b], &kd[b])) return 1;
+    kmin = kd[b] < kmin ? kd[b] : kmin;
+    kmax = kd[b] > kmax ? kd[b] : kmax;
+  }
+  for (size_t b = 0; b < sblocks; b++) {
+    const uint8_t *blk = row + b * 210;
+    apxo_q6k_codes_u6(blk, r->w + b * 256);
+    for (int h = 0; h < 16; h++) r->c[b * 16 + h] = (int64_t)md[b] * (int8_t)blk[192 + h];
+    r->a[b] = (int64_t)kd[b] - kmin;
+  }
+  r->kmin = kmin;
+  r->spread = kmax - kmin;
+  return 0;
+}
+
+static inline void q6k_fold(__m256i d, __m256i x16, int64_t c, int64_t a, __m256i she,
+                            __m256i sho, __m256i *ae, __m256i *ao) {
+  d = _mm256_sub_epi32(d, _mm256_slli_epi32(x16, 5));
+  __m256i cv = _mm256_set1_epi64x(c), av = _mm256_set1_epi64x(a);
+  *ae = _mm256_add_epi64(*ae, _mm256_sllv_epi64(_mm256_mul_epi32(d, cv), _mm256_add_epi64(she, av)));
+  *ao = _mm256_add_epi64(*ao, _mm256_sllv_epi64(_mm256_mul_epi32(_mm256_srli_epi64(d, 32), cv),
+                                                _mm256_add_epi64(sho, av)));
+}
+
+/* Rows [lo, hi) of the k-column Q6_K projection; the arguments are the Q4_K kernel's, with xs
+ * per 16-lane group ([cgroup][n_in / 16][lane]). */
+int Q6K_NAME(const uint8_t *raw, size_t row_bytes, size_t sblocks, size_t lo, size_t hi,
+             size_t k_cols, size_t n_in, const uint32_t *words, const int32_t *xs,
+             const int64_t *she, const int64_t *sho, const uint32_t *emin,
+             const uint32_t *cspread, uint32_t limit, const int8_t *codes,
+             const int64_t *scales, int64_t *out, size_t n_out) {
+  size_t G = sblocks * 8, groups = (k_cols + 7) / 8;
+  uint8_t *wbuf = (uint8_t *)malloc(2 * n_in);
+  int64_t *coef = (int64_t *)malloc(2 * (16 + 1) * sblocks * sizeof(int64_t));
+  if (!wbuf || !coef) {
+    free(wbuf);
+    free(coef);
+    return 1;
+  }
+  q6k_row rr[2];
+  for (int r = 0; r < 2; r++)
+    rr[r] = (q6k_row){wbuf + r * n_in, coef + r * 17 * sblocks, coef + r * 17 * sblocks + 16 * sblocks,
+                      0, 0};
+  int bail = 0;
+  for (size_t o = lo; o < hi && !bail; o += 2) {
+    int two = o + 1 < hi;
+    const uint8_t *ra = raw + o * row_bytes, *rb = two ? ra + row_bytes : ra;
+    if (q6k_row_prep(ra, sblocks, &rr[0]) || q6k_row_prep(rb, sblocks, &rr[1])) {
+      bail = 1;
+      break;
+    }
+    for (size_t cg = 0; cg < groups && !bail; cg++) {
+      size_t c0 = cg * 8, nc = k_cols - c0 < 8 ? k_cols - c0 : 8;
+      if (rr[0].spread + cspread[cg] > limit || rr[1].spread + cspread[cg] > limit) {
+        __atomic_fetch_add(&apxo_q6k_exact_groups, 1, __ATOMIC_RELAXED);
+        for (size_t c = c0; c < c0 + nc && !bail; c++)
+          for (int r = 0; r <= two && !bail; r++)
+            if (apxo_fast_row_value(APX_GGML_TYPE_Q6_K, r ? rb : ra, n_in, codes + c * n_in,
+                                    scales + c * (n_in / 32), &out[c * n_out + o + r]))
+              bail = 1;
+        continue;
+      }
+      __m256i ae0 = _mm256_setzero_si256(), ao0 = ae0, ae1 = ae0, ao1 = ae0;
+      const uint32_t *wg = words + cg * G * 64;
+      for (size_t g = 0; g < G; g++) { /* 32-lane activation groups: two 16-lane halves */
+        size_t gi = cg * G + g;
+        __m256i she_v = ld(she + gi * 4), sho_v = ld(sho + gi * 4);
+        int64_t a0 = rr[0].a[g / 8], a1 = rr[1].a[g / 8];
+        for (int h = 0; h < 2; h++) {
+          const uint32_t *wq = wg + g * 64 + h * 32;
+          const uint8_t *w0 = rr[0].w + g * 32 + h * 16, *w1 = rr[1].w + g * 32 + h * 16;
+          __m256i d0 = _mm256_setzero_si256(), d1 = d0;
+          for (int q = 0; q < 4; q++) {
+            __m256i x = ld(wq + 8 * q);
+            int32_t u0, u1;
+            __builtin_memcpy(&u0, w0 + 4 * q, 4);
+            __builtin_memcpy(&u1, w1 + 4 * q, 4);
+            d0 = quad_dot(d0, _mm256_set1_epi32(u0), x);
+            d1 = quad_dot(d1, _mm256_set1_epi32(u1), x);
+          }
+          size_t H = 2 * g + (size_t)h;
+          __m256i x16 = ld(xs + (cg * 2 * G + H) * 8);
+          q6k_fold(d0, x16, rr[0].c[H], a0, she_v, sho_v, &ae0, &ao0);
+          q6k_fold(d1, x16, rr[1].c[H], a1, she_v, sho_v, &ae1, &ao1);
+        }
+      }
+      int64_t e0[4], od0[4], e1[4], od1[4];
+      _mm256_storeu_si256((__m256i *)e0, ae0);
+      _mm256_storeu_si256((__m256i *)od0, ao0);
+      _mm256_storeu_si256((__m256i *)e1, ae1);
+      _mm256_storeu_si256((__m256i *)od1, ao1);
+      for (size_t c = 0; c < nc && !bail; c++) {
+        int64_t v0 = c & 1 ? od0[c / 2] : e0[c / 2], v1 = c & 1 ? od1[c / 2] : e1[c / 2];
+        if (apxo_finish(v0, rr[0].kmin + emin[c0 + c], &out[(c0 + c) * n_out + o]) ||
+            (two && apxo_finish(v1, rr[1].kmin + emin[c0 + c], &out[(c0 + c) * n_out + o + 1])))
+          bail = 1;
+      }
+    }
+  }
+  free(wbuf);
+  free(coef);
+  return bail;
+}

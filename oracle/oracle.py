@@ -100,6 +100,7 @@ def _declare(l):
     l.apxo_simd_features.argtypes = []
     l.apxo_gemm_counts.argtypes = [C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]
     l.apxo_q4k_counts.argtypes = [C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]
+    l.apxo_q6k_counts.argtypes = [C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]
 
 
 def _p(a: np.ndarray):
@@ -349,6 +350,13 @@ def q4k_counts():
     the exact rows) since the library loaded."""
     a, b = C.c_uint64(), C.c_uint64()
     lib().apxo_q4k_counts(C.byref(a), C.byref(b))
+    return a.value, b.value
+
+
+def q6k_counts():
+    """The same for the k-column Q6_K kernel."""
+    a, b = C.c_uint64(), C.c_uint64()
+    lib().apxo_q6k_counts(C.byref(a), C.byref(b))
     return a.value, b.value
 
 

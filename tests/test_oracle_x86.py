@@ -269,6 +269,7 @@ def test_q4_k_kcols_random_headers_spreads_and_refusals(isa):
     assert want == got and want[:2] == ("err", 6)
 
 
+@pytest.mark.filterwarnings("ignore:This process .* is multi-threaded:DeprecationWarning")
 def test_pool_survives_fork():
     """The oracle's host pool is started in this process; a forked child (which has only the
     forking thread) starts its own workers and finishes a threaded call."""
@@ -293,3 +294,65 @@ def test_pool_survives_fork():
     os.kill(pid, signal.SIGKILL)
     os.waitpid(pid, 0)
     raise AssertionError("the forked child's pooled call did not finish")
+
+
+@pytest.mark.parametrize("n_out,n_in,k", [(37, 1536, 13), (16, 256, 8), (3, 4864, 3),
+                                          (64, 1024, 64), (1, 256, 1)])
+def test_q6_k_kcols_equals_per_column(isa, n_out, n_in, k):
+    """The k-column Q6_K kernel (chart/kcols.rs:1466-1518) equals the per-column fused rows on
+    the benchmark distribution, in both instruction forms."""
+    raw = synth.payload(Q6_K, n_out, n_in, seed=n_out + k)
+    cs, ss = [], []
+    for c in range(k):
+        q = O.quant_act(synth.f32_to_q32(synth.activation_f32(n_in, seed=800 + c)))
+        cs.append(q[0])
+        ss.append(q[1])
+    codes, scales = np.stack(cs), np.stack(ss)
+    want = O.matmat_q8act(Q6_K, raw, n_out, n_in, codes, scales)
+    assert not isinstance(want, tuple)
+    calls = O.q6k_counts()[0]
+    got = O.matmat_q8act_mt(Q6_K, raw, n_out, n_in, codes, scales, 4, simd=True)
+    assert np.array_equal(want, got)
+    assert O.q6k_counts()[0] == calls + 1
+
+
+def test_q6_k_kcols_random_bytes_spreads_and_refusals(isa):
+    """Random code and sub-scale bytes (negative sub-scales included), weight exponents from
+    subnormal to the largest (spreads past the lane limit take the exact rows), zero groups, an
+    all-zero column, and a non-finite d (the call refuses as the per-column contract does)."""
+    n_out, n_in, k = 13, 512, 10
+    for seed, d in [(31, 0x3800), (32, 0x7BFF), (33, 0xBC01)]:
+        raw = random_payload(Q6_K, n_out, n_in, d, 0, seed).reshape(n_out, -1)
+        if seed == 32:
+            raw[3, 208:210] = (0x01, 0x00)  # a subnormal d beside 65504: spread 29
+        raw = raw.reshape(-1)
+        cs, ss = [], []
+        for c in range(k):
+            x = random_x(n_in, seed * 100 + c)
+            if c % 3 == 1:
+                x[32 * (c % 16):32 * (c % 16) + 32] <<= 12
+            if c == 4:
+                x[64:128] = 0
+            if c == 7:
+                x[:] = 0
+            q = O.quant_act(x)
+            cs.append(q[0])
+            ss.append(q[1])
+        codes, scales = np.stack(cs), np.stack(ss)
+        want = O.matmat_q8act(Q6_K, raw, n_out, n_in, codes, scales)
+        calls, exact = O.q6k_counts()
+        got = O.matmat_q8act_mt(Q6_K, raw, n_out, n_in, codes, scales, 3, simd=True)
+        if isinstance(want, tuple):
+            assert want == got
+        else:
+            assert np.array_equal(want, got)
+            assert O.q6k_counts()[0] == calls + 1
+        if seed == 32:
+            assert O.q6k_counts()[1] > exact
+    bad = synth.payload(Q6_K, n_out, n_in, seed=6).reshape(n_out, -1)
+    bad[9, 210 + 208:210 + 210] = (0x00, 0x7E)  # NaN d in row 9, super-block 1
+    cs, ss = zip(*[O.quant_act(random_x(n_in, 95 + c)) for c in range(3)])
+    want = O.matmat_q8act(Q6_K, bad.reshape(-1), n_out, n_in, np.stack(cs), np.stack(ss))
+    got = O.matmat_q8act_mt(Q6_K, bad.reshape(-1), n_out, n_in, np.stack(cs), np.stack(ss), 2,
+                            simd=True)
+    assert want == got and want[:2] == ("err", 6)
