@@ -69,10 +69,21 @@ PREFILL_TOKENS = 512
 
 
 def cpu_isa():
+    """The vector form the CPU arm runs in, and the host CPU's model name."""
     from oracle import oracle as O
 
     f = O.simd_features()
-    return "AVX-VNNI" if f["avxvnni"] else ("AVX2" if f["avx2"] else "scalar")
+    isa = "AVX-VNNI" if f["avxvnni"] else ("AVX2" if f["avx2"] else "scalar")
+    model = "unknown CPU"
+    try:
+        with open("/proc/cpuinfo") as fh:
+            for ln in fh:
+                if ln.startswith("model name"):
+                    model = ln.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return f"{isa} on {model}"
 
 
 def cpu_prefill_baseline(seconds=10.0, tokens=PREFILL_TOKENS):
@@ -104,7 +115,7 @@ def cpu_prefill_baseline(seconds=10.0, tokens=PREFILL_TOKENS):
             break
     return {"value": 2.0 * macs * done / el / 1e12, "unit": "TOPS", "cores": threads,
             "kind": "port", "sample": f"{done} passes of {tokens} tokens x both shapes "
-                                      f"({el:.1f} s), {cpu_isa()} k-column GEMM restatement"}
+                                      f"({el:.1f} s), k-column GEMM restatement, {cpu_isa()}"}
 
 
 def measure_prefill(be, lib, dev, stream, steps, warmup, pg, local, world):
@@ -657,7 +668,7 @@ def cpu_chain_baseline(mats, seed0, seconds=5.0):
     return {"value": per_pass * done / el / 1e9, "unit": "GB/s", "cores": threads,
             "kind": "port", "sample": f"{done} passes of all {len(mats)} projections "
                                       f"({per_pass / 1e6:.0f} MB of distinct host copies per "
-                                      f"pass) in {el:.1f} s, {cpu_isa()} rows"}
+                                      f"pass) in {el:.1f} s, {cpu_isa()}"}
 
 
 def cpu_gemv_baseline(mats, seconds=10.0):
@@ -666,8 +677,8 @@ def cpu_gemv_baseline(mats, seconds=10.0):
     total, done, el, threads = cpu_passes(data, 1 << 30, seconds)
     return {"value": total / el / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
             "sample": f"{done} passes of the workload over {copies} cycled host copies "
-                      f"(>= 256 MB, streamed from DRAM) in {el:.1f} s, {cpu_isa()} "
-                      f"two-row decode cores"}
+                      f"(>= 256 MB, streamed from DRAM) in {el:.1f} s, two-row "
+                      f"decode cores, {cpu_isa()}"}
 
 
 def run_reference(args, world, rank, local, pg):
@@ -679,7 +690,7 @@ def run_reference(args, world, rank, local, pg):
     total, done, el, threads = cpu_passes(data, args.steps, 60.0)
     v = total / el / 1e9
     sample = (f"{done} of {args.steps} steps (capped at 60 s) over {copies} cycled host "
-              f"copies (>= 256 MB, streamed from DRAM), {cpu_isa()} two-row decode cores")
+              f"copies (>= 256 MB, streamed from DRAM), two-row decode cores, {cpu_isa()}")
     line = {"metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus,
             "steps": done, "warmup": args.warmup, "ms_per_step": el * 1e3 / max(done, 1),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int64",
