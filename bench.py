@@ -68,6 +68,15 @@ PREFILL = [(8, 4864, 896), (8, 896, 4864)]
 PREFILL_TOKENS = 512
 
 
+def host_threads():
+    """The host threads this process may run on (its CPU affinity set, which a container's
+    cpuset can make smaller than the machine's count)."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 def cpu_isa():
     """The vector form the CPU arm runs in, and the host CPU's model name."""
     from oracle import oracle as O
@@ -93,7 +102,7 @@ def cpu_prefill_baseline(seconds=10.0, tokens=PREFILL_TOKENS):
     from apeiron_b200 import synth
     from oracle import oracle as O
 
-    threads = os.cpu_count() or 1
+    threads = host_threads()
     work = []
     for m, (t, n_out, n_in) in enumerate(PREFILL):
         raw = synth.payload(t, n_out, n_in, 2000 + m)
@@ -161,7 +170,7 @@ def measure_prefill(be, lib, dev, stream, steps, warmup, pg, local, world):
         cs, es = zip(*(synth.quant_act_np(synth.f32_to_q32(bufs[m]["x"][c])) for c in range(k)))
         want = O.matmat_q8act_mt(t, raws[m], n_out, n_in, np.stack(cs),
                                  np.stack([O.exps_to_scales(e) for e in es]),
-                                 os.cpu_count() or 1)
+                                 host_threads())
         got = bufs[m]["q32"].cpu().numpy().reshape(k, n_out)
         assert np.array_equal(got, want), "prefill parity failure in bench workload"
         assert bool((bufs[m]["status"] == -1).all().item())
@@ -321,7 +330,7 @@ def measure_decode_step(be, lib, dev, stream, steps, warmup, pg, local, world):
         key = len(DECODE_LAYER) if k == len(mats) - 1 else k
         _, _, _, c, e = acts[n_in]
         want = O.matvec_q8act_mt(t, raws[key], n_out, n_in, c, O.exps_to_scales(e),
-                                 os.cpu_count() or 1)
+                                 host_threads())
         assert np.array_equal(outs[k].cpu().numpy(), want), "decode-step parity failure"
     assert int(status[0].item()) == -1
     G = max(2, min(steps, 20))
@@ -428,7 +437,7 @@ def measure_sharded(be, lib, dev, stream, steps, warmup, pg, rank, local, world)
             t, n_out, n_in = SHARDED[m]
             _, _, _, c, e = acts[m]
             want = O.matvec_q8act_mt(t, raws[m], n_out, n_in, c, O.exps_to_scales(e),
-                                     max(1, (os.cpu_count() or 1) // world))
+                                     max(1, (host_threads()) // world))
             got = gathers[gi].read(j, parities[gi])
             assert np.array_equal(got, want), "sharded parity failure in bench workload"
         assert bool((merged[gi][:, 0] == -1).all().item()), "sharded refusal in bench workload"
@@ -620,7 +629,7 @@ def cpu_passes(data, max_passes, max_seconds):
     chunked decode, src/engine/chart/ffn.rs:667-745) on every host thread."""
     from oracle import oracle as O
 
-    threads = os.cpu_count() or 1
+    threads = host_threads()
     total = done = 0
     t0 = time.perf_counter()
     while done < max_passes:
@@ -643,7 +652,7 @@ def cpu_chain_baseline(mats, seed0, seconds=5.0):
     from apeiron_b200 import synth
     from oracle import oracle as O
 
-    threads = os.cpu_count() or 1
+    threads = host_threads()
     base = {m: synth.payload(m[0], m[1], m[2], seed0 + i) for i, m in enumerate(dict.fromkeys(mats))}
     data = [(t, base[(t, n_out, n_in)].copy(), n_out, n_in) for t, n_out, n_in in mats]
     acts = {}
