@@ -356,3 +356,33 @@ def test_q6_k_kcols_random_bytes_spreads_and_refusals(isa):
     got = O.matmat_q8act_mt(Q6_K, bad.reshape(-1), n_out, n_in, np.stack(cs), np.stack(ss), 2,
                             simd=True)
     assert want == got and want[:2] == ("err", 6)
+
+
+@pytest.mark.parametrize("t", [Q8_0, Q4_K, Q6_K])
+def test_vector_paths_on_degenerate_shapes(t):
+    """No rows, one row with more threads than rows, and zero-width activations: the vector
+    paths return what the single-threaded rows return."""
+    qk = 32 if t == Q8_0 else 256
+    for rows, n_in, threads in [(0, qk, 4), (1, qk, 16), (3, 2 * qk, 64), (2, 0, 2)]:
+        raw = synth.payload(t, max(rows, 1), max(n_in, 1), seed=rows + n_in)
+        if rows == 0:
+            raw = raw[:0]
+        if n_in == 0:
+            raw = raw[:0]
+        codes, scales = O.quant_act(random_x(n_in, 3)) if n_in else (
+            np.zeros(0, np.int8), np.zeros(0, np.int64))
+        want = O.matvec_q8act(t, raw, rows, n_in, codes, scales)
+        got = O.matvec_q8act_mt(t, raw, rows, n_in, codes, scales, threads, simd=True)
+        if isinstance(want, tuple):
+            assert want == got
+        else:
+            assert np.array_equal(want, got)
+        k = 3
+        cs = np.stack([codes] * k)
+        ss = np.stack([scales] * k)
+        want = O.matmat_q8act(t, raw, rows, n_in, cs, ss)
+        got = O.matmat_q8act_mt(t, raw, rows, n_in, cs, ss, threads, simd=True)
+        if isinstance(want, tuple):
+            assert want == got
+        else:
+            assert np.array_equal(np.asarray(want).reshape(k, rows), got)
