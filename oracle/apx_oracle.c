@@ -480,6 +480,24 @@ static int fast_row(uint32_t t, const uint8_t *row, size_t n_in, const int8_t *c
       for (int l = 0; l < 32; l++) dot += (int32_t)q[l] * (int32_t)x[l];
       acc += (i128)S[g] * ((i128)d * (i128)dot);
     }
+  } else if (t == APX_GGML_TYPE_Q5_0) {
+    /* Q5_0Decoder (chart/mod.rs:630-712): one pure 32-lane group per block, w = d·(c − 16)
+     * with c the five-bit code (qs nibble, qh bit as the fifth bit; quant.rs:280-299). */
+    for (size_t g = 0; g < groups; g++) {
+      const uint8_t *blk = row + g * 22;
+      int64_t d;
+      if (apxo_f16_to_fixed(rd16(blk), &d)) return 1;
+      const uint8_t *qh = blk + 2, *qs = blk + 6;
+      const int8_t *x = codes + g * ACT_QK;
+      int32_t dot = 0;
+      for (int l = 0; l < 32; l++) {
+        const int j = l % 16, hi = l >= 16;
+        const int bit = (qh[(hi ? 2 : 0) + j / 8] >> (j % 8)) & 1;
+        const int nib = hi ? (qs[j] >> 4) : (qs[j] & 0xF);
+        dot += ((nib | (bit << 4)) - 16) * (int32_t)x[l];
+      }
+      acc += (i128)S[g] * ((i128)d * (i128)dot);
+    }
   } else if (t == APX_GGML_TYPE_Q4_K) {
     for (size_t g = 0; g < groups; g += 2) {
       size_t pp = g / 2, b = pp / 4, p = pp % 4;
@@ -539,6 +557,8 @@ static int plan(uint32_t t, size_t n_in, const int8_t *codes, size_t q_len,
   *fast = 0;
   if (t == APX_GGML_TYPE_Q8_0 && n_in % 32 == 0)
     *fast = fast_bound_ok(n_in, 128, scales, n_scales, 1);
+  else if (t == APX_GGML_TYPE_Q5_0 && n_in % 32 == 0)
+    *fast = fast_bound_ok(n_in, 16, scales, n_scales, 1);
   else if (t == APX_GGML_TYPE_Q4_K && n_in % 64 == 0)
     *fast = fast_bound_ok(n_in, 1008, scales, n_scales, 0);
   else if (t == APX_GGML_TYPE_Q6_K && n_in % 256 == 0)

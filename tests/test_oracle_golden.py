@@ -15,7 +15,7 @@ from oracle import oracle as O
 import populations as pop
 from chart_inputs import random_payload, random_x, lcg_next
 
-Q8_0, Q4_K, Q6_K = 8, 12, 14
+Q5_0, Q8_0, Q4_K, Q6_K = 6, 8, 12, 14
 I64_MIN, I64_MAX = -(1 << 63), (1 << 63) - 1
 HERE = os.path.dirname(os.path.abspath(__file__))
 
@@ -211,7 +211,7 @@ def _fused_equals_fixed(t, raw, rows, n_in, x):
     return a
 
 
-@pytest.mark.parametrize("t", [Q8_0, Q4_K, Q6_K])
+@pytest.mark.parametrize("t", [Q8_0, Q5_0, Q4_K, Q6_K])
 def test_fused_rows_equal_contract_on_random_payloads(t):
     """chart/tests.rs:224-271 (`chart_matches_fixed_on_random_payloads_for_every_family`)."""
     seed = 0x123456789ABCDEF0
@@ -223,7 +223,7 @@ def test_fused_rows_equal_contract_on_random_payloads(t):
         _fused_equals_fixed(t, raw, rows, n_in, x)
 
 
-@pytest.mark.parametrize("t", [Q8_0, Q4_K, Q6_K])
+@pytest.mark.parametrize("t", [Q8_0, Q5_0, Q4_K, Q6_K])
 def test_fused_rows_equal_contract_on_extremes_and_ragged(t):
     """chart/tests.rs:273-334: +-127 codes against 0x7BFF scales; ragged widths."""
     raw = random_payload(t, 2, 256, 0x7BFF, 0x7BFF, 0x51FF0000 + t)
@@ -279,7 +279,7 @@ def test_short_payload_and_shape_order():
     assert r == ("err", 3, 3 * 68, 2 * 68, 0)
 
 
-@pytest.mark.parametrize("t", [Q8_0, Q4_K, Q6_K])
+@pytest.mark.parametrize("t", [Q8_0, Q5_0, Q4_K, Q6_K])
 def test_matmat_and_threads_equal_per_column(t):
     """kern/matmat.rs:92-134: column c equals the per-column call; the threaded CPU
     baseline equals the single-threaded rows."""
@@ -306,3 +306,20 @@ def test_block_dots_rebuild_the_q8_0_value():
             acc += O.f16_to_fixed(h) * int(scales[b]) * int(dots[r, b])
         want = O.exact_dot_q8_0(raw[r * 136:(r + 1) * 136], 4, codes, scales)
         assert O.round_shift_32(acc) == want
+
+
+def test_q5_0_fused_rows_take_the_fast_path_and_equal_the_contract():
+    """The Q5_0 fused row (chart/mod.rs:630-712: one pure group per block, w = d·(c − 16))
+    against matvec_fixed on the dequantized activation, on whole-block widths under the narrow
+    bound (top 16) and on ragged widths, which take the contract."""
+    for rows, n_in, seed in [(7, 64, 1), (3, 896, 2), (5, 4864, 3), (4, 33, 4), (2, 300, 5)]:
+        raw = random_payload(Q5_0, rows, n_in, 0x3800, 0, 0x5000 + seed)
+        for xs in (random_x(n_in, seed), random_x(n_in, seed) << 20):
+            _fused_equals_fixed(Q5_0, raw, rows, n_in, xs)
+    raw = random_payload(Q5_0, 3, 64, 0x7BFF, 0, 77)
+    codes = np.array([127 if j % 3 else -127 for j in range(64)], dtype=np.int8)
+    for s in (1, 1 << 40):
+        scales = np.full(2, s, dtype=np.int64)
+        a = O.matvec_q8act(Q5_0, raw, 3, 64, codes, scales)
+        b = O.matvec_fixed(Q5_0, raw, 3, 64, O.dequant_act(codes, scales))
+        assert (a == b) if isinstance(a, tuple) else np.array_equal(a, b)
