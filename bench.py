@@ -715,6 +715,18 @@ def run_reference(args, world, rank, local, pg):
                            "unit": "TOPS", "cpu_baseline": pre,
                            "e2e": {"value": pre["value"], "unit": "TOPS",
                                    "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    for key, skip, metric, mats_, seed in (
+            ("decode_step", args.no_decode, "decode step GB/s (all linear layers)",
+             DECODE_LAYER * DECODE_LAYERS + [DECODE_HEAD], 6000),
+            ("sharded", args.no_shard, "70B FFN decode GB/s (one host)", SHARDED, 4000)):
+        if skip:
+            continue
+        try:
+            cb = cpu_chain_baseline(mats_, seed, args.cpu_seconds / 2)
+            line[key] = {"metric": metric, "value": cb["value"], "unit": "GB/s",
+                         "cpu_baseline": cb}
+        except Exception as exc:  # the headline line stands without it
+            line[key] = {"unavailable": f"{type(exc).__name__}: {exc}"}
     print(json.dumps(line), flush=True)
 
 
