@@ -1274,9 +1274,82 @@ static int gemm_kq_mt(uint32_t t, const uint8_t *raw, size_t raw_len, size_t n_o
   return done;
 }
 
+int apxo_x86_q8_0_kcols_avx2(const uint8_t *, size_t, size_t, size_t, size_t, size_t,
+                             const int8_t *, const int64_t *, const int64_t *, int64_t *,
+                             size_t);
+int apxo_x86_q8_0_kcols_vnni(const uint8_t *, size_t, size_t, size_t, size_t, size_t,
+                             const int8_t *, const int64_t *, const int64_t *, int64_t *,
+                             size_t);
+static unsigned long kcols_calls;
+
+void apxo_kcols_counts(uint64_t *calls) {
+  *calls = __atomic_load_n(&kcols_calls, __ATOMIC_RELAXED);
+}
+
+typedef struct {
+  int (*fn)(const uint8_t *, size_t, size_t, size_t, size_t, size_t, const int8_t *,
+            const int64_t *, const int64_t *, int64_t *, size_t);
+  const uint8_t *raw;
+  size_t row_bytes, n_out, n_in, k_cols, per;
+  const int8_t *codes;
+  const int64_t *scales;
+  int64_t *out;
+  int bail[POOL_MAX];
+} kcols_job;
+
+static void kcols_item(void *ctx, int i) {
+  kcols_job *j = (kcols_job *)ctx;
+  size_t lo = (size_t)i * j->per, hi = lo + j->per < j->n_out ? lo + j->per : j->n_out;
+  j->bail[i] = lo < hi ? j->fn(j->raw, j->row_bytes, lo, hi, j->n_in, j->k_cols, j->codes,
+                               j->scales, f16_table, j->out, j->n_out)
+                       : 0;
+}
+
+/* The Q8_0 columns in runs of 16 over one pass of each row (pooled_q8_0, kern/matmat.rs:
+ * 198-206), what the reference runs when its GEMM does not; 1 when it wrote every output. */
+static int q8_0_kcols_mt(const uint8_t *raw, size_t raw_len, size_t n_out, size_t n_in,
+                         size_t k_cols, const int8_t *codes, const int64_t *scales, int threads,
+                         int64_t *out) {
+  size_t blocks = n_in / ACT_QK;
+  if (n_in % ACT_QK || blocks == 0 || k_cols == 0 || n_out == 0) return 0;
+  x86_rows_fn vec = x86_rows(); /* AVX2 present; builds the f16 table */
+  if (!vec) return 0;
+  if (raw_len / Q8_0_BYTES / blocks < n_out) return 0;
+  for (size_t c = 0; c < k_cols; c++) {
+    int fast = 0;
+    if (plan(APX_GGML_TYPE_Q8_0, n_in, codes + c * n_in, n_in, scales + c * blocks, blocks,
+             &fast) != 0 || !fast)
+      return 0;
+  }
+  for (size_t i = 0; i < k_cols * n_in; i++)
+    if (codes[i] == -128) return 0;
+  kcols_job *job = (kcols_job *)calloc(1, sizeof(kcols_job));
+  if (!job) return 0;
+  if (threads < 1) threads = 1;
+  if (threads > POOL_MAX) threads = POOL_MAX;
+  if ((size_t)threads > n_out) threads = (int)n_out;
+  size_t per = (n_out + (size_t)threads - 1) / (size_t)threads;
+  job->fn = (apxo_simd_features() & 2) ? apxo_x86_q8_0_kcols_vnni : apxo_x86_q8_0_kcols_avx2;
+  job->raw = raw;
+  job->row_bytes = blocks * Q8_0_BYTES;
+  job->n_out = n_out;
+  job->n_in = n_in;
+  job->k_cols = k_cols;
+  job->per = per;
+  job->codes = codes;
+  job->scales = scales;
+  job->out = out;
+  pool_run(kcols_item, job, threads);
+  int done = 1;
+  for (int i = 0; i < threads; i++) done &= !job->bail[i];
+  free(job);
+  return done;
+}
+
 /* With AVX-VNNI, Q8_0 calls whose every column takes the fast rows run the k-column GEMM, as
- * the reference's matmat_q8act tries gemm_q8_0 first (kern/matmat.rs:134-146); Q4_K and Q6_K
- * calls on whole super-blocks run the k-column kernels (gemm_q4_k / gemm_q6_k,
+ * the reference's matmat_q8act tries gemm_q8_0 first (kern/matmat.rs:134-146); Q8_0 calls the GEMM
+ * does not take (no AVX-VNNI) run their columns in runs of 16 per row pass (pooled_q8_0); Q4_K
+ * and Q6_K calls on whole super-blocks run the k-column kernels (gemm_q4_k / gemm_q6_k,
  * matmat.rs:163-177); everything
  * else (and every call those kernels bail on) runs the vector rows per column. */
 int apxo_matmat_q8act_simd_mt(uint32_t t, const uint8_t *raw, size_t raw_len, size_t n_out,
@@ -1286,6 +1359,12 @@ int apxo_matmat_q8act_simd_mt(uint32_t t, const uint8_t *raw, size_t raw_len, si
   if (t == APX_GGML_TYPE_Q8_0 &&
       gemm_q8_0_mt(raw, raw_len, n_out, n_in, k_cols, codes, scales, threads, out)) {
     __atomic_fetch_add(&gemm_calls, 1, __ATOMIC_RELAXED);
+    clear(err);
+    return 0;
+  }
+  if (t == APX_GGML_TYPE_Q8_0 && k_cols > 1 &&
+      q8_0_kcols_mt(raw, raw_len, n_out, n_in, k_cols, codes, scales, threads, out)) {
+    __atomic_fetch_add(&kcols_calls, 1, __ATOMIC_RELAXED);
     clear(err);
     return 0;
   }

@@ -114,6 +114,9 @@ void apxo_gemm_counts(uint64_t *calls, uint64_t *exact_groups);
 void apxo_q4k_counts(uint64_t *calls, uint64_t *exact_groups);
 /* And for the k-column Q6_K kernel (kcols.rs:1466-1518). */
 void apxo_q6k_counts(uint64_t *calls, uint64_t *exact_groups);
+/* Matmat calls the Q8_0 column runs of 16 (kern/matmat.rs:198-206, the path without AVX-VNNI)
+ * completed. */
+void apxo_kcols_counts(uint64_t *calls);
 
 /* The FFN hidden activation (src/engine/chart/ffn.rs:246-284, ops/silu.rs:53-100,
  * numeric/fixed_exp.rs:1-184, mixer/f32_carrier.rs:262-375). */

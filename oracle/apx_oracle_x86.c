@@ -633,3 +633,59 @@ int Q6K_NAME(const uint8_t *raw, size_t row_bytes, size_t sblocks, size_t lo, si
   free(coef);
   return bail;
 }
+
+/* ---- the k-column Q8_0 rows without AVX-VNNI (kern/matmat.rs:198-206, pooled_q8_0) ----------
+ *
+ * Without AVX-VNNI the reference's matmat_q8act runs Q8_0 columns in runs of at most 16 over
+ * one pass of each weight row (`q8_0_row_kcols_avx2`): a block's codes and scale are read once
+ * and dotted against every column of the run (|w| · sign(x, w), `vpmaddubsw` + `vpmaddwd`),
+ * each column folding `acc += d·(S·D)` in i128, the fast row's arithmetic. */
+
+#if APX_X86_VNNI
+#define KCOLS_NAME apxo_x86_q8_0_kcols_vnni
+#else
+#define KCOLS_NAME apxo_x86_q8_0_kcols_avx2
+#endif
+
+#define KCOLS_RUN 16
+
+/* Rows [lo, hi) against k_cols columns (codes [c][n_in], S [c][n_in / 32]) in runs of 16;
+ * out[c·n_out + o].  Returns 0, or 1 when the caller must redecide the call (a non-finite
+ * scale or an output outside i64). */
+int KCOLS_NAME(const uint8_t *raw, size_t row_bytes, size_t lo, size_t hi, size_t n_in,
+               size_t k_cols, const int8_t *codes, const int64_t *S, const int64_t *tab,
+               int64_t *out, size_t n_out) {
+  size_t blocks = n_in / 32;
+  for (size_t o = lo; o < hi; o++) {
+    const uint8_t *row = raw + o * row_bytes;
+    for (size_t c0 = 0; c0 < k_cols; c0 += KCOLS_RUN) {
+      size_t nc = k_cols - c0 < KCOLS_RUN ? k_cols - c0 : KCOLS_RUN;
+      i128 acc[KCOLS_RUN] = {0};
+      int64_t bad = 0;
+      for (size_t b = 0; b < blocks; b++) {
+        const uint8_t *blk = row + b * Q8_0_BYTES;
+        int64_t d = tab[word(blk)];
+        bad |= d;
+        __m256i w = ld(blk + 2);
+        size_t c = 0;
+        for (; c + 4 <= nc; c += 4) {
+          const int8_t *x = codes + (c0 + c) * n_in + b * 32;
+          int32_t dots[4];
+          _mm_storeu_si128((__m128i *)dots,
+                           sum4(dot_lanes(w, ld(x)), dot_lanes(w, ld(x + n_in)),
+                                dot_lanes(w, ld(x + 2 * n_in)), dot_lanes(w, ld(x + 3 * n_in))));
+          for (int j = 0; j < 4; j++)
+            acc[c + j] += (i128)d * (i128)(S[(c0 + c + j) * blocks + b] * (int64_t)dots[j]);
+        }
+        for (; c < nc; c++) {
+          int32_t dot = sum1(dot_lanes(w, ld(codes + (c0 + c) * n_in + b * 32)));
+          acc[c] += (i128)d * (i128)(S[(c0 + c) * blocks + b] * (int64_t)dot);
+        }
+      }
+      if (bad & 1) return 1;
+      for (size_t c = 0; c < nc; c++)
+        if (finish_row(acc[c], &out[(c0 + c) * n_out + o])) return 1;
+    }
+  }
+  return 0;
+}

@@ -101,6 +101,7 @@ def _declare(l):
     l.apxo_gemm_counts.argtypes = [C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]
     l.apxo_q4k_counts.argtypes = [C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]
     l.apxo_q6k_counts.argtypes = [C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]
+    l.apxo_kcols_counts.argtypes = [C.POINTER(C.c_uint64)]
 
 
 def _p(a: np.ndarray):
@@ -358,6 +359,13 @@ def q6k_counts():
     a, b = C.c_uint64(), C.c_uint64()
     lib().apxo_q6k_counts(C.byref(a), C.byref(b))
     return a.value, b.value
+
+
+def kcols_counts() -> int:
+    """Matmat calls the Q8_0 column runs of 16 completed (the path without AVX-VNNI)."""
+    a = C.c_uint64()
+    lib().apxo_kcols_counts(C.byref(a))
+    return a.value
 
 
 def simd_features() -> dict:

@@ -386,3 +386,27 @@ def test_vector_paths_on_degenerate_shapes(t):
             assert want == got
         else:
             assert np.array_equal(np.asarray(want).reshape(k, rows), got)
+
+
+@pytest.mark.parametrize("n_out,n_in,k", [(37, 896, 13), (8, 4864, 40), (3, 32, 2)])
+def test_q8_0_matmat_without_vnni_runs_column_runs(isa, n_out, n_in, k):
+    """Without AVX-VNNI (the AVX2 build) Q8_0 matmats run their columns in runs of 16 per row
+    pass (kern/matmat.rs:198-206); with it, the GEMM.  Both equal the per-column rows."""
+    raw = synth.payload(Q8_0, n_out, n_in, seed=k)
+    cs, ss = zip(*[O.quant_act(synth.f32_to_q32(synth.activation_f32(n_in, seed=40 + c)))
+                   for c in range(k)])
+    codes, scales = np.stack(cs), np.stack(ss)
+    want = O.matmat_q8act(Q8_0, raw, n_out, n_in, codes, scales)
+    runs, gemms = O.kcols_counts(), O.gemm_counts()[0]
+    got = O.matmat_q8act_mt(Q8_0, raw, n_out, n_in, codes, scales, 3, simd=True)
+    assert np.array_equal(want, got)
+    if isa == "avx2":
+        assert O.kcols_counts() == runs + 1 and O.gemm_counts()[0] == gemms
+    else:
+        assert O.gemm_counts()[0] == gemms + 1
+    # a refusal (an output past i64) is redecided by the per-column contract
+    big = random_payload(Q8_0, n_out, n_in, 0x7BFF, 0x7BFF, 3)
+    c = np.full((k, n_in), 127, dtype=np.int8)
+    s = np.full((k, n_in // 32), 1 << 40, dtype=np.int64)
+    assert O.matmat_q8act(Q8_0, big, n_out, n_in, c, s) == \
+        O.matmat_q8act_mt(Q8_0, big, n_out, n_in, c, s, 3, simd=True)
