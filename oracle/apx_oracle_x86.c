@@ -122,9 +122,12 @@ static int q8_0_pair(const uint8_t *r0, const uint8_t *r1, size_t blocks, const 
   return (int)(bad & 1);
 }
 
-/* Two Q4_K rows of `sblocks` super-blocks; xsums[g] = Σ codes over 32-lane group g. */
-static int q4_k_pair(const uint8_t *r0, const uint8_t *r1, size_t sblocks, const int8_t *codes,
-                     const int64_t *S, const int32_t *xsums, const int64_t *tab, i128 acc[2]) {
+/* Two Q4_K rows of `sblocks` whole super-blocks and then `tail` 64-lane windows of the next
+ * one (a width that is a multiple of 64 but not of 256, as the reference's single-row core
+ * takes it window by window, chart/mod.rs:719-838); xsums[g] = Σ codes over 32-lane group g. */
+static int q4_k_pair(const uint8_t *r0, const uint8_t *r1, size_t sblocks, int tail,
+                     const int8_t *codes, const int64_t *S, const int32_t *xsums,
+                     const int64_t *tab, i128 acc[2]) {
   const __m256i nib = _mm256_set1_epi8(0x0F);
   i128 a[2] = {0, 0};
   int64_t bad = 0;
@@ -162,6 +165,28 @@ static int q4_k_pair(const uint8_t *r0, const uint8_t *r1, size_t sblocks, const
       }
     }
   }
+  if (tail > 0) {
+    const size_t b = sblocks;
+    const int8_t *x = codes + b * 256;
+    for (int r = 0; r < 2; r++) {
+      const uint8_t *blk = (r ? r1 : r0) + b * Q4_K_BYTES;
+      int64_t d = tab[word(blk)], dmin = tab[word(blk + 2)];
+      bad |= d | dmin;
+      for (int p = 0; p < tail; p++) {
+        __m256i q = ld(blk + 16 + 32 * p);
+        int32_t dl = sum1(dot_lanes(_mm256_and_si256(q, nib), ld(x + 64 * p)));
+        int32_t dh = sum1(dot_lanes(_mm256_and_si256(_mm256_srli_epi16(q, 4), nib),
+                                    ld(x + 64 * p + 32)));
+        int sl, ml, sh, mh;
+        scale_min(blk + 4, 2 * p, &sl, &ml);
+        scale_min(blk + 4, 2 * p + 1, &sh, &mh);
+        size_t g = b * 8 + 2 * (size_t)p;
+        i128 in_lo = (i128)(d * sl) * dl - (i128)(dmin * ml) * xsums[g];
+        i128 in_hi = (i128)(d * sh) * dh - (i128)(dmin * mh) * xsums[g + 1];
+        a[r] += (i128)S[g] * in_lo + (i128)S[g + 1] * in_hi;
+      }
+    }
+  }
   acc[0] = a[0];
   acc[1] = a[1];
   return (int)(bad & 1);
@@ -177,7 +202,7 @@ static int finish_row(i128 acc, int64_t *out) {
   return 0;
 }
 
-/* Rows [lo, hi) of a Q8_0 (n_in % 32 == 0) or Q4_K (n_in % 256 == 0) projection whose call
+/* Rows [lo, hi) of a Q8_0 (n_in % 32 == 0) or Q4_K (n_in % 64 == 0) projection whose call
  * plan chose the fast rows.  Returns 0, APX_ERR_OUTPUT_OVERFLOW with the first such row in
  * *bad, or -1 when a block scale is non-finite (the caller then runs the contract). */
 int ROWS_NAME(uint32_t t, const uint8_t *raw, size_t row_bytes, size_t lo, size_t hi,
@@ -189,7 +214,8 @@ int ROWS_NAME(uint32_t t, const uint8_t *raw, size_t row_bytes, size_t lo, size_
     i128 acc[2];
     int nf = t == APX_GGML_TYPE_Q8_0
                  ? q8_0_pair(r0, r1, n_in / 32, codes, S, tab, acc)
-                 : q4_k_pair(r0, r1, n_in / 256, codes, S, xsums, tab, acc);
+                 : q4_k_pair(r0, r1, n_in / 256, (int)(n_in % 256) / 64, codes, S, xsums,
+                             tab, acc);
     if (nf) {
       *bad = o;
       return -1;

@@ -39,7 +39,8 @@ def _both(t, raw, rows, n_in, codes, scales, threads):
 
 
 @pytest.mark.parametrize("t,n_in", [(Q8_0, 32), (Q8_0, 96), (Q8_0, 896), (Q8_0, 4864),
-                                    (Q4_K, 256), (Q4_K, 1536), (Q4_K, 896), (Q6_K, 512)])
+                                    (Q4_K, 256), (Q4_K, 1536), (Q4_K, 896), (Q4_K, 64),
+                                    (Q4_K, 320), (Q4_K, 448), (Q6_K, 512)])
 @pytest.mark.parametrize("rows,threads", [(1, 1), (3, 1), (37, 3), (64, 8)])
 def test_vector_rows_equal_scalar_rows(isa, t, n_in, rows, threads):
     raw = synth.payload(t, rows, n_in, seed=rows * 1000 + n_in)
