@@ -1,5 +1,5 @@
 /*
- * apx_oracle_x86.c — vector rows of the timed CPU baseline.
+ * apx_oracle_x86.c — vector kernels of the timed CPU baseline.
  *
  * TEST INFRASTRUCTURE ONLY (see apx_oracle.h): bench.py's cpu_baseline and `--impl reference`
  * legs time these rows; tests/test_oracle_x86.py checks them against the scalar fused rows of
@@ -19,6 +19,13 @@
  *     Q8_0 `acc += d·(S·D)` (S·D fits i64 under the narrow call bound), Q4_K
  *     `acc += S·((d·sc)·D − (dmin·m)·Σxq)` per 32-lane group.
  * Integer sums are exact, so each row's accumulator equals the scalar fast row's bit for bit.
+ *
+ * The multi-column (prefill) kernels follow, each in its own section: the k-column Q8_0 GEMM
+ * (AVX-VNNI build only, kern/gemm.rs:498-580), the k-column Q4_K and Q6_K kernels
+ * (chart/kcols.rs:1406-1518) and the Q8_0 column runs of 16 the reference uses without AVX-VNNI
+ * (kern/matmat.rs:198-206).  Every one of them reports a case it cannot finish exactly (a
+ * non-finite scale, an output outside i64) to its caller, which redecides the call on the
+ * per-column rows, so refusals are always the contract's.
  *
  * This file is compiled twice (oracle/Makefile): with APX_X86_VNNI=0 for AVX2 and with
  * APX_X86_VNNI=1 under -mavxvnni; apx_oracle.c picks one at run time from CPUID.
