@@ -199,6 +199,60 @@ static int q4_k_pair(const uint8_t *r0, const uint8_t *r1, size_t sblocks, int t
   return (int)(bad & 1);
 }
 
+/* The 256 codes q − 32 of a Q6_K super-block in lane order, 8 vectors of 32 (quant.rs:574-599:
+ * low nibbles of ql with two bits of qh above them). */
+static inline void q6_k_codes8(const uint8_t *blk, __m256i w[8]) {
+  const __m256i m4 = _mm256_set1_epi8(0x0F), m2 = _mm256_set1_epi8(0x03);
+  const __m256i off = _mm256_set1_epi8(32);
+  for (int n = 0; n < 2; n++) {
+    __m256i l0 = ld(blk + 64 * n), l1 = ld(blk + 64 * n + 32), h = ld(blk + 128 + 32 * n);
+    __m256i h0 = _mm256_slli_epi16(_mm256_and_si256(h, m2), 4);
+    __m256i h1 = _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(h, 2), m2), 4);
+    __m256i h2 = _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(h, 4), m2), 4);
+    __m256i h3 = _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(h, 6), m2), 4);
+    w[4 * n + 0] = _mm256_sub_epi8(_mm256_or_si256(_mm256_and_si256(l0, m4), h0), off);
+    w[4 * n + 1] = _mm256_sub_epi8(_mm256_or_si256(_mm256_and_si256(l1, m4), h1), off);
+    w[4 * n + 2] = _mm256_sub_epi8(
+        _mm256_or_si256(_mm256_and_si256(_mm256_srli_epi16(l0, 4), m4), h2), off);
+    w[4 * n + 3] = _mm256_sub_epi8(
+        _mm256_or_si256(_mm256_and_si256(_mm256_srli_epi16(l1, 4), m4), h3), off);
+  }
+}
+
+/* Two Q6_K rows of `sblocks` super-blocks (the reference's Q6_K core, x86.rs:713-780): per
+ * 32-lane activation group c, `acc += S_c·(d·(sc_2c·D_2c + sc_2c+1·D_2c+1))` over the two
+ * 16-lane halves, the halves' dots being the low and high 128 bits of one lane vector. */
+static int q6_k_pair(const uint8_t *r0, const uint8_t *r1, size_t sblocks, const int8_t *codes,
+                     const int64_t *S, const int64_t *tab, i128 acc[2]) {
+  i128 a[2] = {0, 0};
+  int64_t bad = 0;
+  for (size_t b = 0; b < sblocks; b++) {
+    const int8_t *x = codes + b * 256;
+    __m256i xv[8];
+    for (int c = 0; c < 8; c++) xv[c] = ld(x + 32 * c);
+    for (int r = 0; r < 2; r++) {
+      const uint8_t *blk = (r ? r1 : r0) + b * 210;
+      int64_t d = tab[word(blk + 208)];
+      bad |= d;
+      __m256i w[8];
+      q6_k_codes8(blk, w);
+      for (int c = 0; c < 8; c++) {
+        __m256i p = dot_lanes(w[c], xv[c]);
+        __m128i lo = _mm256_castsi256_si128(p), hi = _mm256_extracti128_si256(p, 1);
+        __m128i t = _mm_hadd_epi32(lo, hi);
+        t = _mm_hadd_epi32(t, t); /* [D_lo, D_hi, D_lo, D_hi] */
+        int32_t dlo = _mm_cvtsi128_si32(t), dhi = _mm_extract_epi32(t, 1);
+        int64_t gd = (int64_t)(int8_t)blk[192 + 2 * c] * dlo +
+                     (int64_t)(int8_t)blk[192 + 2 * c + 1] * dhi;
+        a[r] += (i128)S[b * 8 + (size_t)c] * ((i128)d * gd);
+      }
+    }
+  }
+  acc[0] = a[0];
+  acc[1] = a[1];
+  return (int)(bad & 1);
+}
+
 /* round_shift_32 then the i64 range check (src/engine/num/value.rs:10-12,
  * chart/mod.rs:1746-1753). */
 static int finish_row(i128 acc, int64_t *out) {
@@ -209,7 +263,8 @@ static int finish_row(i128 acc, int64_t *out) {
   return 0;
 }
 
-/* Rows [lo, hi) of a Q8_0 (n_in % 32 == 0) or Q4_K (n_in % 64 == 0) projection whose call
+/* Rows [lo, hi) of a Q8_0 (n_in % 32 == 0), Q4_K (n_in % 64 == 0) or Q6_K (n_in % 256 == 0)
+ * projection whose call
  * plan chose the fast rows.  Returns 0, APX_ERR_OUTPUT_OVERFLOW with the first such row in
  * *bad, or -1 when a block scale is non-finite (the caller then runs the contract). */
 int ROWS_NAME(uint32_t t, const uint8_t *raw, size_t row_bytes, size_t lo, size_t hi,
@@ -219,10 +274,10 @@ int ROWS_NAME(uint32_t t, const uint8_t *raw, size_t row_bytes, size_t lo, size_
     const uint8_t *r0 = raw + o * row_bytes;
     const uint8_t *r1 = o + 1 < hi ? r0 + row_bytes : r0;
     i128 acc[2];
-    int nf = t == APX_GGML_TYPE_Q8_0
-                 ? q8_0_pair(r0, r1, n_in / 32, codes, S, tab, acc)
-                 : q4_k_pair(r0, r1, n_in / 256, (int)(n_in % 256) / 64, codes, S, xsums,
-                             tab, acc);
+    int nf = t == APX_GGML_TYPE_Q8_0   ? q8_0_pair(r0, r1, n_in / 32, codes, S, tab, acc)
+             : t == APX_GGML_TYPE_Q6_K ? q6_k_pair(r0, r1, n_in / 256, codes, S, tab, acc)
+                                       : q4_k_pair(r0, r1, n_in / 256, (int)(n_in % 256) / 64,
+                                                   codes, S, xsums, tab, acc);
     if (nf) {
       *bad = o;
       return -1;

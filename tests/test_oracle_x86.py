@@ -52,7 +52,7 @@ def test_vector_rows_equal_scalar_rows(isa, t, n_in, rows, threads):
     assert np.array_equal(out, ref)
 
 
-@pytest.mark.parametrize("t", [Q8_0, Q4_K])
+@pytest.mark.parametrize("t", [Q8_0, Q4_K, Q6_K])
 def test_vector_rows_on_random_bytes_and_extremes(isa, t):
     """Random header bytes (every Q4_K scale/min pattern), the largest finite scales against
     +-127 codes, and spread activation exponents."""
@@ -67,16 +67,16 @@ def test_vector_rows_on_random_bytes_and_extremes(isa, t):
     _both(t, raw, 2, 256, codes, np.ones(8, dtype=np.int64), 1)
 
 
-@pytest.mark.parametrize("t", [Q8_0, Q4_K])
+@pytest.mark.parametrize("t", [Q8_0, Q4_K, Q6_K])
 def test_vector_rows_refusals(isa, t):
     """A non-finite block scale and an output past i64 refuse exactly as the scalar rows do
     (both redecided by the single-threaded contract)."""
     n_in, rows = 256, 6
     raw = random_payload(t, rows, n_in, 0x3800, 0x3800, 77 + t)
-    qk, bb = (32, 34) if t == Q8_0 else (256, 144)
+    qk, bb, at = {Q8_0: (32, 34, 0), Q4_K: (256, 144, 0), Q6_K: (256, 210, 208)}[t]
     row_bytes = (n_in // qk) * bb
     bad = raw.copy()
-    bad[3 * row_bytes:3 * row_bytes + 2] = (0x01, 0x7C)  # row 3, block 0: NaN
+    bad[3 * row_bytes + at:3 * row_bytes + at + 2] = (0x01, 0x7C)  # row 3, block 0: NaN
     codes, scales = O.quant_act(random_x(n_in, 5))
     r = _both(t, bad, rows, n_in, codes, scales, 2)
     assert r[:2] == ("err", 6) and r[4] == 0x7C01
