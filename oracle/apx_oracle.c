@@ -773,14 +773,14 @@ static x86_rows_fn x86_rows(void) {
   return (f & 2) ? apxo_x86_rows_vnni : apxo_x86_rows_avx2;
 }
 
-/* The vector rows take Q8_0 on whole 32-lane blocks, Q4_K on whole 64-lane windows and Q6_K
+/* The vector rows take Q8_0 and Q5_0 on whole 32-lane blocks, Q4_K on whole 64-lane windows and Q6_K
  * on whole super-blocks, the widths the reference's AVX2 rows take (`tiled2` for whole
  * super-blocks, x86.rs:782-800, the single-row cores otherwise, chart/mod.rs:719-938); their
  * byte dots also
  * need every activation code in [-127, 127] (the |w|·sign(x, w) form), which quant_act
  * guarantees. */
 static int x86_shape(uint32_t t, size_t n_in) {
-  return (t == APX_GGML_TYPE_Q8_0 && n_in % ACT_QK == 0) ||
+  return ((t == APX_GGML_TYPE_Q8_0 || t == APX_GGML_TYPE_Q5_0) && n_in % ACT_QK == 0) ||
          (t == APX_GGML_TYPE_Q4_K && n_in % 64 == 0) ||
          (t == APX_GGML_TYPE_Q6_K && n_in % QK_K == 0);
 }

@@ -253,6 +253,44 @@ static int q6_k_pair(const uint8_t *r0, const uint8_t *r1, size_t sblocks, const
   return (int)(bad & 1);
 }
 
+/* The 32 weights c − 16 of a Q5_0 block (quant.rs:280-299): lane j < 16 the low nibble of qs[j],
+ * lane 16 + j the high one, each with qh bit j (resp. 16 + j) as its fifth bit. */
+static inline __m256i q5_0_codes(const uint8_t *blk) {
+  const __m128i qs = _mm_loadu_si128((const __m128i *)(blk + 6));
+  const __m128i m4 = _mm_set1_epi8(0x0F);
+  __m256i nib = _mm256_set_m128i(_mm_and_si128(_mm_srli_epi16(qs, 4), m4), _mm_and_si128(qs, m4));
+  uint32_t qh;
+  __builtin_memcpy(&qh, blk + 2, 4);
+  /* byte j of the lane vector takes qh byte j / 8, then its bit j % 8 */
+  const __m256i spread = _mm256_setr_epi8(0, 0, 0, 0, 0, 0, 0, 0, 1, 1, 1, 1, 1, 1, 1, 1, 2, 2, 2,
+                                          2, 2, 2, 2, 2, 3, 3, 3, 3, 3, 3, 3, 3);
+  const __m256i bits = _mm256_set1_epi64x((long long)0x8040201008040201ull);
+  __m256i hb = _mm256_shuffle_epi8(_mm256_set1_epi32((int)qh), spread);
+  hb = _mm256_cmpeq_epi8(_mm256_and_si256(hb, bits), bits);
+  __m256i c = _mm256_or_si256(nib, _mm256_and_si256(hb, _mm256_set1_epi8(0x10)));
+  return _mm256_sub_epi8(c, _mm256_set1_epi8(16));
+}
+
+/* Two Q5_0 rows of `blocks` blocks (q5_0_rows2_avx2, x86.rs:957-1058): per block
+ * `acc += d·(S·D)` with D the exact dot of c − 16 against the codes. */
+static int q5_0_pair(const uint8_t *r0, const uint8_t *r1, size_t blocks, const int8_t *codes,
+                     const int64_t *S, const int64_t *tab, i128 acc[2]) {
+  i128 a0 = 0, a1 = 0;
+  int64_t bad = 0;
+  for (size_t b = 0; b < blocks; b++) {
+    const uint8_t *p0 = r0 + b * 22, *p1 = r1 + b * 22;
+    __m256i x = ld(codes + b * 32);
+    int64_t w0 = tab[word(p0)], w1 = tab[word(p1)];
+    bad |= w0 | w1;
+    int64_t s = S[b];
+    a0 += (i128)w0 * (i128)(s * (int64_t)sum1(dot_lanes(q5_0_codes(p0), x)));
+    a1 += (i128)w1 * (i128)(s * (int64_t)sum1(dot_lanes(q5_0_codes(p1), x)));
+  }
+  acc[0] = a0;
+  acc[1] = a1;
+  return (int)(bad & 1);
+}
+
 /* round_shift_32 then the i64 range check (src/engine/num/value.rs:10-12,
  * chart/mod.rs:1746-1753). */
 static int finish_row(i128 acc, int64_t *out) {
@@ -263,8 +301,8 @@ static int finish_row(i128 acc, int64_t *out) {
   return 0;
 }
 
-/* Rows [lo, hi) of a Q8_0 (n_in % 32 == 0), Q4_K (n_in % 64 == 0) or Q6_K (n_in % 256 == 0)
- * projection whose call
+/* Rows [lo, hi) of a Q8_0 or Q5_0 (n_in % 32 == 0), Q4_K (n_in % 64 == 0) or Q6_K
+ * (n_in % 256 == 0) projection whose call
  * plan chose the fast rows.  Returns 0, APX_ERR_OUTPUT_OVERFLOW with the first such row in
  * *bad, or -1 when a block scale is non-finite (the caller then runs the contract). */
 int ROWS_NAME(uint32_t t, const uint8_t *raw, size_t row_bytes, size_t lo, size_t hi,
@@ -275,6 +313,7 @@ int ROWS_NAME(uint32_t t, const uint8_t *raw, size_t row_bytes, size_t lo, size_
     const uint8_t *r1 = o + 1 < hi ? r0 + row_bytes : r0;
     i128 acc[2];
     int nf = t == APX_GGML_TYPE_Q8_0   ? q8_0_pair(r0, r1, n_in / 32, codes, S, tab, acc)
+             : t == APX_GGML_TYPE_Q5_0 ? q5_0_pair(r0, r1, n_in / 32, codes, S, tab, acc)
              : t == APX_GGML_TYPE_Q6_K ? q6_k_pair(r0, r1, n_in / 256, codes, S, tab, acc)
                                        : q4_k_pair(r0, r1, n_in / 256, (int)(n_in % 256) / 64,
                                                    codes, S, xsums, tab, acc);

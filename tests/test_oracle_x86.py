@@ -12,6 +12,7 @@ from chart_inputs import random_payload, random_x
 from apeiron_b200 import synth
 
 Q8_0, Q4_K, Q6_K = O.Q8_0, O.Q4_K, O.Q6_K
+Q5_0 = 6
 
 pytestmark = pytest.mark.skipif(not O.simd_features()["avx2"], reason="host has no AVX2")
 
@@ -411,3 +412,20 @@ def test_q8_0_matmat_without_vnni_runs_column_runs(isa, n_out, n_in, k):
     s = np.full((k, n_in // 32), 1 << 40, dtype=np.int64)
     assert O.matmat_q8act(Q8_0, big, n_out, n_in, c, s) == \
         O.matmat_q8act_mt(Q8_0, big, n_out, n_in, c, s, 3, simd=True)
+
+
+@pytest.mark.parametrize("n_in", [32, 64, 896, 4864])
+def test_q5_0_vector_rows_equal_scalar_rows(isa, n_in):
+    """The Q5_0 vector rows (the fifth bit spread from qh into each lane, c − 16 against the codes)
+    equal the scalar fused row and the contract, on random payloads (every qh/qs pattern) and on
+    the largest finite scales."""
+    for rows, threads, d, seed in [(1, 1, 0x3800, 1), (37, 3, 0x3800, 2), (9, 4, 0x7BFF, 3),
+                                   (5, 2, 0xB800, 4)]:
+        raw = random_payload(Q5_0, rows, n_in, d, 0, seed + n_in)
+        codes, scales = O.quant_act(random_x(n_in, seed) << (seed * 5))
+        out = _both(Q5_0, raw, rows, n_in, codes, scales, threads)
+        ref = O.matvec_fixed(Q5_0, raw, rows, n_in, O.dequant_act(codes, scales))
+        if isinstance(out, tuple):
+            assert out[:2] == ref[:2]
+        else:
+            assert np.array_equal(out, ref)
