@@ -87,6 +87,7 @@ class GatherDesc(C.Structure):
         ("nf_key", C.c_longlong * MAX_GATHER_PROJ),
         ("status", C.c_void_p * MAX_GATHER_PROJ),
         ("out_status", C.c_void_p * MAX_GATHER_PROJ),
+        ("bytes", C.c_size_t),
     ]
 
 

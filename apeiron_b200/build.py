@@ -15,7 +15,8 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libapeiron_cuda.so")
-SOURCES = ["apx_runtime.cu", "apx_gemv.cu", "apx_quant.cu", "apx_gemm.cu", "apx_ffn.cu", "apx_noalloc.cu",
+SOURCES = ["apx_runtime.cu", "apx_gemv.cu", "apx_quant.cu", "apx_gemm.cu", "apx_lgemm.cu", "apx_ffn.cu",
+           "apx_noalloc.cu",
            "apx_peer.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -49,6 +49,7 @@
 #include "apx_kernels.h"
 #include "apx_pack.cuh"
 #include "apx_quant.cuh"
+#include "apx_tc.cuh"
 
 namespace apx {
 
@@ -94,68 +95,6 @@ constexpr uint32_t kIdesc64 = idesc_i8(kTileN);
 constexpr uint64_t kDescHi = ((uint64_t)(16 >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
                              ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
-                                            uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
-      : "memory");
-}
-
-// D (+)= A·B for one 32-lane block; `accumulate` 0 overwrites D.
-__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
-                                       uint32_t idesc, uint32_t accumulate) {
-  const uint32_t zero = 0;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(
-          d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(zero), "r"(zero), "r"(zero),
-      "r"(zero));
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t *bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          smem_addr(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&v)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-      "%14,%15}, [%16];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
-        "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-      : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&v)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
-        "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]),
-        "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
-        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]),
-        "=r"(v[31])
-      : "r"(taddr));
-}
-
 // This warp's kEpiTok columns of 32 TMEM lanes.
 template <int N>
 __device__ __forceinline__ void tmem_ld_tok(uint32_t taddr, uint32_t (&v)[N]);
@@ -166,10 +105,6 @@ __device__ __forceinline__ void tmem_ld_tok<16>(uint32_t taddr, uint32_t (&v)[16
 template <>
 __device__ __forceinline__ void tmem_ld_tok<32>(uint32_t taddr, uint32_t (&v)[32]) {
   tmem_ld32_nowait(taddr, v);
-}
-
-__device__ __forceinline__ void tmem_wait_ld() {
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 // acc += a·b, a 32×32 → 64-bit product added to a 64-bit sum.  Written in C++ so the compiler
@@ -193,59 +128,6 @@ __device__ __forceinline__ void fold(long long (&acc)[kEpiTok], const uint32_t (
     mad_wide(acc[4 * j4 + 2], (int)(d[4 * j4 + 2] << s4.z), m);
     mad_wide(acc[4 * j4 + 3], (int)(d[4 * j4 + 3] << s4.w), m);
   }
-}
-
-// The finish of one output: v = round_shift_32(acc·2^s) (value.rs:10-12 on the 128-bit
-// product) with the i64 range check of chart/mod.rs:1746-1753, and its f32 image
-// F32::from_q32(v).  For s >= 32 the product has no fractional part: v = acc·2^(s−32) when
-// that fits, and f32(v·2^-32) = RN(acc)·2^(s−64) (a power-of-two scaling commutes with the
-// one rounding).  For s < 32, v = (acc + 2^(31−s)) >> (32−s), which always fits (|acc| < 2^62
-// by the route's bound), and its f32 image is RN(v)·2^-32.  One conversion either way.
-// The rounding's general case (s outside [32, 64)), out of line: the finish unrolls 32
-// outputs per thread, and an inlined copy of this per output would crowd the instruction cache.
-struct FinishOut {
-  long long v;
-  float f;
-  bool fits;
-};
-
-__device__ __noinline__ FinishOut finish_one(long long acc, unsigned s) {
-  long long v;
-  float f;
-  bool fits = true;
-  long long x;  // the integer whose rounding gives the f32 image
-  int k;        // its power-of-two scale
-  if (s >= 32) {
-    const unsigned t = s - 32;
-    v = (long long)((unsigned long long)acc << (t & 63));
-    fits = t > 63 ? acc == 0 : (acc >> (63 - t)) == (acc >> 63);
-    x = acc;
-    k = (int)s - 64;
-  } else {
-    const unsigned t = 32 - s;
-    v = (acc + (1ll << (t - 1))) >> t;
-    x = v;
-    k = -32;
-  }
-  f = __ll2float_rn(x) * __int_as_float((127 + k) << 23);
-  return FinishOut{v, f, fits};
-}
-
-// finish_one for the common case 32 <= s < 64 with the range check on the accumulator's
-// high word alone: acc·2^t fits i64 iff acc >> (63 − t) is 0 or -1, and for t < 32 that
-// shift reads only the high 32 bits.
-__device__ __forceinline__ bool finish_fast(long long acc, unsigned s, long long &v, float &f) {
-  if (s >= 32 && s < 64) {
-    const unsigned t = s - 32;
-    const int hi = (int)(acc >> 32);
-    v = (long long)((unsigned long long)acc << t);
-    f = __ll2float_rn(acc) * __int_as_float((int)(s + 63) << 23);  // 2^(s − 64)
-    return (hi >> (31 - t)) == (hi >> 31);
-  }
-  const FinishOut o = finish_one(acc, s);
-  v = o.v;
-  f = o.f;
-  return o.fits;
 }
 
 // ---- per-call workspace ------------------------------------------------------------------------
@@ -1062,20 +944,6 @@ __global__ void gemm_build_layout(PackGeo geo, size_t n_out, int nb, int nb_pad,
 }
 
 // ---- host side ---------------------------------------------------------------------------------
-
-static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void *p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
 
 // A 2D uint8 map over `rows` rows of `inner` bytes (row stride `stride`), boxes of
 // 128 bytes × box_rows, 128-byte swizzle; reads past either extent fill zeros.

@@ -10,7 +10,9 @@
 //
 // The array is a file-scope __device__ variable: every GPU that loads the library holds its
 // APX_NOALLOC_SCRATCH_BYTES until the process exits.  Its address is looked up once per
-// device (cudaGetSymbolAddress, with that device current) on the first call on that device.
+// device (cudaGetSymbolAddress, with that device current) on the first call on that device and
+// kept for the life of the process: a host application that resets a device (cudaDeviceReset)
+// invalidates it, as it invalidates every context, stream and tensor of this library there.
 #include <cuda_runtime.h>
 
 #include <cstring>
@@ -72,10 +74,16 @@ extern "C" APX_API int apx_matvec_f32_noalloc(apx_ctx *ctx, uint64_t tensor, siz
                                &device))
     return APX_ERR_INVALID_ARGUMENT;
   if (n_in != t_in || n_out > t_out) return APX_ERR_LAYOUT_MISMATCH;
-  cudaError_t e = cudaSetDevice(device);
+  // the launches need the context's device current; the caller's current device is restored
+  int prev = -1;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e == cudaSuccess && prev != device) e = cudaSetDevice(device);
   void *base = nullptr;
   if (e == cudaSuccess) e = scratch_address(device, &base);
-  if (e != cudaSuccess) return APX_ERR_CUDA;
+  if (e != cudaSuccess) {
+    if (prev >= 0 && prev != device) cudaSetDevice(prev);
+    return APX_ERR_CUDA;
+  }
   unsigned char *s = static_cast<unsigned char *>(base);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // the refusal word must start at all ones (no refusal); the scratch itself is fully
@@ -88,5 +96,6 @@ extern "C" APX_API int apx_matvec_f32_noalloc(apx_ctx *ctx, uint64_t tensor, siz
     e = apx::launch_gemv(plan, type, pack, tscratch, n_out, n_in,
                          reinterpret_cast<const int8_t *>(s + kCodesOff), s + kExpsOff,
                          s + kDescOff, nullptr, d_y, &d_status->first, st);
+  if (prev >= 0 && prev != device) cudaSetDevice(prev);
   return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
 }

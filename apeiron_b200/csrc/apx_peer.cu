@@ -167,6 +167,13 @@ APX_API int apx_device_read(apx_ctx *ctx, const void *d_src, void *host_dst, siz
   return e == cudaSuccess ? fail(err, APX_OK) : fail(err, APX_ERR_CUDA, e);
 }
 
+namespace {
+// [off, off + len) inside a buffer of `bytes` (no wrap-around).
+bool inside(size_t off, size_t len, size_t bytes) { return off <= bytes && len <= bytes - off; }
+// len = a·b without overflow.
+bool mul_ok(size_t a, size_t b, size_t &len) { return !__builtin_mul_overflow(a, b, &len); }
+}  // namespace
+
 APX_API int apx_matvec_gather_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
                                     const int8_t *d_codes, const uint8_t *d_exps,
                                     const apx_act_desc *d_desc, const apx_gather_desc *gd,
@@ -175,6 +182,12 @@ APX_API int apx_matvec_gather_async(apx_ctx *ctx, uint64_t tensor, size_t n_out,
       gd->rank >= gd->world || j < 0 || j >= gd->nproj || gd->nproj > APX_MAX_GATHER_PROJ ||
       !gd->status[j] || n_out != gd->rows[j] || (gd->out_off & 7))
     return APX_ERR_INVALID_ARGUMENT;
+  {  // this projection's rows of the output area lie inside every rank's buffer
+    size_t first, len;
+    if (!mul_ok(gd->rows_off[j], 8, first) || !mul_ok(gd->rows[j], 8, len) ||
+        !inside(gd->out_off, first, gd->bytes) || !inside(gd->out_off + first, len, gd->bytes))
+      return APX_ERR_INVALID_ARGUMENT;
+  }
   for (int r = 0; r < gd->world; r++)
     if (!gd->peer[r]) return APX_ERR_INVALID_ARGUMENT;
   uint32_t type;
@@ -213,6 +226,12 @@ APX_API int apx_gather_publish_async(apx_ctx *ctx, const apx_gather_desc *gd, vo
     if (!gd->peer[r]) return APX_ERR_INVALID_ARGUMENT;
   for (int j = 0; j < gd->nproj; j++)
     if (!gd->status[j] || !gd->out_status[j]) return APX_ERR_INVALID_ARGUMENT;
+  // the keys ([world][nproj] int64), the flags ([world] uint64) and this rank's epoch and
+  // check-in count (2 uint64) lie inside every rank's buffer
+  if (!inside(gd->key_off, 8 * (size_t)gd->world * (size_t)gd->nproj, gd->bytes) ||
+      !inside(gd->flag_off, 8 * (size_t)gd->world, gd->bytes) ||
+      !inside(gd->ctr_off, 16, gd->bytes))
+    return APX_ERR_INVALID_ARGUMENT;
   if (cudaSetDevice(apx::context_device(ctx)) != cudaSuccess) return APX_ERR_CUDA;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1);

@@ -36,8 +36,10 @@ struct Tensor {
   size_t nonfinite_row = SIZE_MAX;  // first row holding an Inf/NaN block scale
   uint16_t nonfinite_bits = 0;
   GemvPlan plan{};
-  GemmLayout gemm;          // tcgen05 GEMM view (Q8_0), built on the first multi-column call
+  GemmLayout gemm;          // tcgen05 fold GEMM view (Q8_0), built when the digit planes fail
   bool gemm_tried = false;
+  LimbLayout limb;          // tcgen05 digit-plane view, built on the first multi-column call
+  bool limb_tried = false;
   // The synchronous GEMV call as one CUDA graph [H2D, GEMV, D2H], captured on the context's
   // staging buffers for one (n_out, q_len) and rebuilt when they change.
   cudaGraphExec_t sync_exec = nullptr;
@@ -48,6 +50,7 @@ struct Tensor {
     cudaFree(d_pack);
     if (d_scratch) cudaFree(d_scratch);
     free_gemm_layout(&gemm);
+    free_limb_layout(&limb);
     if (sync_exec) cudaGraphExecDestroy(sync_exec);
     sync_exec = nullptr;
   }
@@ -130,7 +133,8 @@ struct apx_ctx {
   uint64_t next = 1;
   DevBuf dev;      // [out | status | desc | exps | codes] of the synchronous calls
   DevBuf scratch;  // device-side quantization scratch of the f32 path
-  DevBuf gwork;    // GEMM per-call workspace (its head zeroed whenever it is reallocated)
+  DevBuf gwork;    // fold GEMM per-call workspace (its head zeroed whenever it is reallocated)
+  DevBuf lwork;    // digit-plane GEMM per-call workspace (no state kept between calls)
   DevBuf ascratch; // codes / exps / descriptors of apx_matmat_f32_async off the fused route
   DevBuf fwork;    // per-CTA statistics of apx_swiglu_quant_async
   HostBuf host;    // pinned mirror of `dev`
@@ -367,13 +371,13 @@ int matvec_sync(apx_ctx *ctx, Tensor &t, size_t n_out, size_t n_in, const int8_t
   return rc;
 }
 
-// ---- multi-column calls on the tensor cores (Q8_0) -------------------------------------
+// ---- multi-column calls on the tensor cores ---------------------------------------------------
 
 constexpr size_t kGemmMinCols = 4;  // fewer columns run as separate GEMVs
 
-// Whether a k-column call takes the tcgen05 GEMM: Q8_0, enough columns, a width the kernel
-// takes, and a weight exponent spread that leaves room for its i64 fold.  The GEMM view of
-// the tensor is built on the first such call.
+// Whether a Q8_0 k-column call can take the fold GEMM (apx_gemm.cu): enough columns, a width the
+// kernel takes, and a weight exponent spread that leaves room for its i64 fold.  Its view of the
+// tensor is built on the first such call.
 bool gemm_route(apx_ctx *ctx, Tensor &t, size_t n_out, size_t n_in, size_t k_cols) {
   if (t.type != APX_GGML_TYPE_Q8_0 || k_cols < kGemmMinCols || n_out == 0 ||
       !gemm_shape_ok(n_in) || !t.d_pack)
@@ -387,17 +391,67 @@ bool gemm_route(apx_ctx *ctx, Tensor &t, size_t n_out, size_t n_in, size_t k_col
   return gemm_supported(t.gemm);
 }
 
-cudaError_t ensure_gwork(apx_ctx *ctx, size_t n_cols, size_t n_in, size_t n_out) {
-  const size_t need = gemm_work_bytes(n_cols, n_in, n_out, ctx->sm_count);
-  if (need <= ctx->gwork.cap) return cudaSuccess;
-  cudaError_t e = ctx->gwork.ensure(need);
-  if (e == cudaSuccess) e = cudaMemset(ctx->gwork.p, 0, ctx->gwork.cap);
+// The tensor-core route of a k-column call: the digit-plane GEMM (apx_lgemm.cu) for every family
+// whose weights fit four digits, else the fold GEMM for Q8_0, else one GEMV per column.
+enum TcRoute { kTcNone = 0, kTcLimb = 1, kTcFold = 2 };
+
+TcRoute tc_route(apx_ctx *ctx, Tensor &t, size_t n_out, size_t n_in, size_t k_cols) {
+  if (k_cols < kGemmMinCols || n_out == 0 || !t.d_pack) return kTcNone;
+  if (limb_shape_ok(n_in)) {
+    if (!t.limb_tried) {
+      t.limb_tried = true;
+      if (build_limb_layout(t.plan, t.type, t.d_pack, t.n_out, t.n_in, &t.limb, ctx->stream) !=
+          cudaSuccess)
+        cudaGetLastError();  // no digit planes: the next route
+    }
+    if (t.limb.ok) return kTcLimb;
+  }
+  return gemm_route(ctx, t, n_out, n_in, k_cols) ? kTcFold : kTcNone;
+}
+
+// The route's own workspace: the fold GEMM keeps self-resetting counters in a layout of its
+// own, so the two never share one buffer.
+cudaError_t ensure_gwork(apx_ctx *ctx, TcRoute route, size_t n_cols, size_t n_in, size_t n_out) {
+  DevBuf &b = route == kTcLimb ? ctx->lwork : ctx->gwork;
+  const size_t need = route == kTcLimb ? limb_work_bytes(n_cols, n_in, n_out, ctx->sm_count)
+                                       : gemm_work_bytes(n_cols, n_in, n_out, ctx->sm_count);
+  if (need <= b.cap) return cudaSuccess;
+  cudaError_t e = b.ensure(need);
+  if (e == cudaSuccess) e = cudaMemset(b.p, 0, b.cap);
   return e;
+}
+
+// One tensor-core k-column launch of device codes (column c at codes + c·ld) on the route.
+cudaError_t launch_tc(apx_ctx *ctx, Tensor &t, TcRoute route, size_t n_out, size_t n_in,
+                      size_t k, const int8_t *codes, size_t ld, const uint8_t *exps, size_t ldb,
+                      const void *descs, long long *out_q32, float *out_f32,
+                      unsigned long long *status, cudaStream_t stream) {
+  if (route == kTcLimb)
+    return launch_limb_gemm(t.plan, t.type, t.d_pack, t.limb, n_out, n_in, k, codes, ld, exps,
+                            ldb, descs, ctx->lwork.p, out_q32, out_f32, status, ctx->sm_count,
+                            stream);
+  return launch_gemm_q8_0(t.plan, t.d_pack, t.gemm, n_out, n_in, k, codes, ld, exps, ldb, descs,
+                          ctx->gwork.p, out_q32, out_f32, status, ctx->sm_count, stream);
+}
+
+// The fused f32 route (quantization inside the GEMM's prep kernel), when the input allows it.
+bool tc_f32_ok(TcRoute route, size_t n_in, const float *x, size_t ldx) {
+  return route == kTcLimb ? limb_f32_ok(n_in, x, ldx) : gemm_f32_ok(n_in, x, ldx);
+}
+
+cudaError_t launch_tc_f32(apx_ctx *ctx, Tensor &t, TcRoute route, size_t n_out, size_t n_in,
+                          size_t k, const float *x, size_t ldx, long long *out_q32,
+                          float *out_f32, unsigned long long *status, cudaStream_t stream) {
+  if (route == kTcLimb)
+    return launch_limb_gemm_f32(t.plan, t.type, t.d_pack, t.limb, n_out, n_in, k, x, ldx,
+                                ctx->lwork.p, out_q32, out_f32, status, ctx->sm_count, stream);
+  return launch_gemm_q8_0_f32(t.plan, t.d_pack, t.gemm, n_out, n_in, k, x, ldx, ctx->gwork.p,
+                              out_q32, out_f32, status, ctx->sm_count, stream);
 }
 
 // Synchronous k-column projection of host activations through the GEMM: one H2D of
 // [status | exps | codes (rows padded to 128 bytes)], one D2H of [outputs | status].
-int matmat_gemm_sync(apx_ctx *ctx, Tensor &t, size_t n_out, size_t n_in, size_t k,
+int matmat_gemm_sync(apx_ctx *ctx, Tensor &t, TcRoute route, size_t n_out, size_t n_in, size_t k,
                      const int8_t *codes, const uint8_t *exps, int64_t *out, apx_err *err) {
   const size_t nb = (n_in + 31) / 32, ld = (n_in + 127) / 128 * 128;
   const size_t out_sz = align16(k * n_out * 8), st_sz = align16(k * 16);
@@ -406,7 +460,7 @@ int matmat_gemm_sync(apx_ctx *ctx, Tensor &t, size_t n_out, size_t n_in, size_t 
   cudaError_t e;
   if ((e = ctx->dev.ensure(out_sz + in_sz)) != cudaSuccess) return cuda_err(err, e);
   if ((e = ctx->host.ensure(out_sz + in_sz)) != cudaSuccess) return cuda_err(err, e);
-  if ((e = ensure_gwork(ctx, k, n_in, n_out)) != cudaSuccess) return cuda_err(err, e);
+  if ((e = ensure_gwork(ctx, route, k, n_in, n_out)) != cudaSuccess) return cuda_err(err, e);
   uint8_t *h = (uint8_t *)ctx->host.p, *d = (uint8_t *)ctx->dev.p;
   uint8_t *hs = h + out_sz, *he = hs + st_sz, *hc = he + ex_sz;
   std::memset(hs, 0xFF, k * 16);
@@ -418,9 +472,8 @@ int matmat_gemm_sync(apx_ctx *ctx, Tensor &t, size_t n_out, size_t n_in, size_t 
   uint8_t *ds = d + out_sz, *de = ds + st_sz, *dc = de + ex_sz;
   e = cudaMemcpyAsync(ds, hs, in_sz, cudaMemcpyHostToDevice, ctx->stream);
   if (e == cudaSuccess)
-    e = launch_gemm_q8_0(t.plan, t.d_pack, t.gemm, n_out, n_in, k, (const int8_t *)dc, ld, de,
-                         nb, nullptr, ctx->gwork.p, (long long *)d, nullptr,
-                         (unsigned long long *)ds, ctx->sm_count, ctx->stream);
+    e = launch_tc(ctx, t, route, n_out, n_in, k, (const int8_t *)dc, ld, de, nb, nullptr,
+                  (long long *)d, nullptr, (unsigned long long *)ds, ctx->stream);
   if (e == cudaSuccess)
     e = cudaMemcpyAsync(h, d, out_sz + k * 16, cudaMemcpyDeviceToHost, ctx->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
@@ -497,6 +550,7 @@ void apx_close(apx_ctx *ctx) {
   ctx->dev.release();
   ctx->scratch.release();
   ctx->gwork.release();
+  ctx->lwork.release();
   ctx->ascratch.release();
   ctx->fwork.release();
   ctx->host.release();
@@ -614,7 +668,13 @@ size_t apx_tensor_device_bytes(apx_ctx *ctx, uint64_t handle) {
   if (!ctx) return 0;
   std::lock_guard<std::mutex> g(ctx->mu);
   Tensor *t = find(ctx, handle);
-  return t ? t->pack_bytes : 0;
+  if (!t) return 0;
+  // the repacked payload, plus the tensor-core views once a multi-column call has built them
+  size_t n = t->pack_bytes;
+  if (t->limb.ok) n += 4 * t->limb.m_pad * t->limb.kp + 4 * t->limb.m_pad;
+  if (t->gemm.base)
+    n += t->gemm.m_pad * t->gemm.kp + (size_t)t->gemm.nb_pad * t->gemm.m_pad * 4 + t->gemm.m_pad * 4;
+  return n;
 }
 
 int apx_matvec_q8act(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in,
@@ -663,9 +723,11 @@ int apx_matmat_q8act(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in, s
   if (!t) return set_err(err, APX_ERR_INVALID_ARGUMENT);
   cudaSetDevice(ctx->device);
   const size_t nb = (q_len + 31) / 32;
-  if (k_cols && check_geometry(*t, n_out, n_in, q_len, false, nullptr) == APX_OK &&
-      gemm_route(ctx, *t, n_out, n_in, k_cols))
-    return matmat_gemm_sync(ctx, *t, n_out, n_in, k_cols, codes, exps, out, err);
+  if (k_cols && check_geometry(*t, n_out, n_in, q_len, false, nullptr) == APX_OK) {
+    const TcRoute route = tc_route(ctx, *t, n_out, n_in, k_cols);
+    if (route != kTcNone)
+      return matmat_gemm_sync(ctx, *t, route, n_out, n_in, k_cols, codes, exps, out, err);
+  }
   for (size_t c = 0; c < k_cols; c++) {
     HostAct ha = describe_host(codes + c * q_len, q_len, exps + c * nb);
     int rc = ha.status;
@@ -771,8 +833,10 @@ int apx_matmat_f32(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in, siz
   if ((e = ctx->host.ensure(y_sz + st_sz + x_sz)) != cudaSuccess) return cuda_err(err, e);
   if ((e = ctx->scratch.ensure(ds_sz + ex_sz + k_cols * ld)) != cudaSuccess)
     return cuda_err(err, e);
-  const bool gemm = gemm_route(ctx, *t, n_out, n_in, k_cols);
-  if (gemm && (e = ensure_gwork(ctx, k_cols, n_in, n_out)) != cudaSuccess) return cuda_err(err, e);
+  const TcRoute route = tc_route(ctx, *t, n_out, n_in, k_cols);
+  const bool gemm = route != kTcNone;
+  if (gemm && (e = ensure_gwork(ctx, route, k_cols, n_in, n_out)) != cudaSuccess)
+    return cuda_err(err, e);
   uint8_t *h = (uint8_t *)ctx->host.p, *d = (uint8_t *)ctx->dev.p;
   uint8_t *sc = (uint8_t *)ctx->scratch.p;
   uint8_t *descs = sc, *dexp = sc + ds_sz;
@@ -783,18 +847,16 @@ int apx_matmat_f32(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in, siz
                       ctx->stream);
   unsigned long long *status = (unsigned long long *)(d + y_sz);
   const float *dx = (const float *)(d + y_sz + st_sz);
-  if (e == cudaSuccess && gemm && gemm_f32_ok(n_in, dx, n_in)) {
+  if (e == cudaSuccess && gemm && tc_f32_ok(route, n_in, dx, n_in)) {
     // quantize inside the GEMM's prep kernel: one pass over the f32 columns
-    e = launch_gemm_q8_0_f32(t->plan, t->d_pack, t->gemm, n_out, n_in, k_cols, dx, n_in,
-                             ctx->gwork.p, nullptr, (float *)d, status, ctx->sm_count,
-                             ctx->stream);
+    e = launch_tc_f32(ctx, *t, route, n_out, n_in, k_cols, dx, n_in, nullptr, (float *)d, status,
+                      ctx->stream);
   } else if (e == cudaSuccess && gemm) {
     e = launch_quant_f32_cols(dx, n_in, n_in, (int)k_cols, dcod, ld, dexp, ldb, descs,
                               ctx->stream);
     if (e == cudaSuccess)
-      e = launch_gemm_q8_0(t->plan, t->d_pack, t->gemm, n_out, n_in, k_cols, dcod, ld, dexp,
-                           ldb, descs, ctx->gwork.p, nullptr, (float *)d, status, ctx->sm_count,
-                           ctx->stream);
+      e = launch_tc(ctx, *t, route, n_out, n_in, k_cols, dcod, ld, dexp, ldb, descs, nullptr,
+                    (float *)d, status, ctx->stream);
   } else {
     if (e == cudaSuccess)
       e = launch_quant_f32_cols(dx, n_in, n_in, (int)k_cols, dcod, ld, dexp, ldb, descs,
@@ -989,12 +1051,13 @@ int apx_matmat_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_in, s
   const size_t ld = apx_act_padded_len(n_in), ldb = ld / 32;
   {
     std::lock_guard<std::mutex> g(ctx->mu);
-    if (gemm_route(ctx, *t, n_out, n_in, k_cols)) {
-      if (ensure_gwork(ctx, k_cols, n_in, n_out) != cudaSuccess) return APX_ERR_OUT_OF_MEMORY;
-      cudaError_t e = launch_gemm_q8_0(t->plan, t->d_pack, t->gemm, n_out, n_in, k_cols, d_codes,
-                                       ld, d_exps, ldb, d_descs, ctx->gwork.p, (long long *)d_out_q32,
-                                       d_out_f32, (unsigned long long *)d_status,
-                                       ctx->sm_count, (cudaStream_t)stream);
+    const TcRoute route = tc_route(ctx, *t, n_out, n_in, k_cols);
+    if (route != kTcNone) {
+      if (ensure_gwork(ctx, route, k_cols, n_in, n_out) != cudaSuccess)
+        return APX_ERR_OUT_OF_MEMORY;
+      cudaError_t e = launch_tc(ctx, *t, route, n_out, n_in, k_cols, d_codes, ld, d_exps, ldb,
+                                d_descs, (long long *)d_out_q32, d_out_f32,
+                                (unsigned long long *)d_status, (cudaStream_t)stream);
       return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
     }
   }
@@ -1020,13 +1083,14 @@ int apx_matmat_f32_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_i
   if (!t || n_in != t->n_in || n_out > t->n_out) return APX_ERR_LAYOUT_MISMATCH;
   if (k_cols == 0) return APX_OK;
   cudaStream_t st = (cudaStream_t)stream;
-  const bool gemm = gemm_route(ctx, *t, n_out, n_in, k_cols);
-  if (gemm && ensure_gwork(ctx, k_cols, n_in, n_out) != cudaSuccess) return APX_ERR_OUT_OF_MEMORY;
+  const TcRoute route = tc_route(ctx, *t, n_out, n_in, k_cols);
+  const bool gemm = route != kTcNone;
+  if (gemm && ensure_gwork(ctx, route, k_cols, n_in, n_out) != cudaSuccess)
+    return APX_ERR_OUT_OF_MEMORY;
   cudaError_t e;
-  if (gemm && gemm_f32_ok(n_in, d_x, ldx)) {
-    e = launch_gemm_q8_0_f32(t->plan, t->d_pack, t->gemm, n_out, n_in, k_cols, d_x, ldx,
-                             ctx->gwork.p, (long long *)d_out_q32, d_out_f32,
-                             (unsigned long long *)d_status, ctx->sm_count, st);
+  if (gemm && tc_f32_ok(route, n_in, d_x, ldx)) {
+    e = launch_tc_f32(ctx, *t, route, n_out, n_in, k_cols, d_x, ldx, (long long *)d_out_q32,
+                      d_out_f32, (unsigned long long *)d_status, st);
     return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
   }
   const size_t ld = apx_act_padded_len(n_in), ldb = ld / 32;
@@ -1039,9 +1103,8 @@ int apx_matmat_f32_async(apx_ctx *ctx, uint64_t tensor, size_t n_out, size_t n_i
   int8_t *dcod = (int8_t *)(sc + ds_sz + ex_sz);
   e = launch_quant_f32_cols(d_x, n_in, ldx, (int)k_cols, dcod, ld, dexp, ldb, sc, st);
   if (e == cudaSuccess && gemm) {
-    e = launch_gemm_q8_0(t->plan, t->d_pack, t->gemm, n_out, n_in, k_cols, dcod, ld, dexp, ldb,
-                         descs, ctx->gwork.p, (long long *)d_out_q32, d_out_f32,
-                         (unsigned long long *)d_status, ctx->sm_count, st);
+    e = launch_tc(ctx, *t, route, n_out, n_in, k_cols, dcod, ld, dexp, ldb, descs,
+                  (long long *)d_out_q32, d_out_f32, (unsigned long long *)d_status, st);
   } else {
     for (size_t c = 0; e == cudaSuccess && c < k_cols; c++)
       e = launch_gemv(t->plan, t->type, t->d_pack, t->d_scratch, n_out, n_in, dcod + c * ld,

@@ -364,7 +364,7 @@ class PeerGather:
         d.world, d.rank, d.nproj, d.timeout_us = self.world, self.rank, self.nproj, timeout_us
         for r, pv in enumerate(self.peers):
             d.peer[r] = pv
-        d.flag_off, d.ctr_off = self.flag_off, self.ctr_off
+        d.flag_off, d.ctr_off, d.bytes = self.flag_off, self.ctr_off, total
         for j, sh in enumerate(shards):
             d.rows_off[j] = self.base[j] + sh.r0
             d.rows[j] = sh.rows

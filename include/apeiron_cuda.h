@@ -126,7 +126,9 @@ APX_API int apx_tensor_upload(apx_ctx *ctx, uint32_t ggml_type, const uint8_t *r
                       apx_err *err);
 /* Release an uploaded tensor. */
 APX_API int apx_tensor_free(apx_ctx *ctx, uint64_t handle);
-/* Device bytes held by an uploaded tensor (repacked payload + row metadata). */
+/* Device bytes held by an uploaded tensor: the repacked payload and row metadata, plus the
+ * tensor-core views a multi-column call builds (the weight digit planes: 4 bytes per weight;
+ * or the Q8_0 fold view). */
 APX_API size_t apx_tensor_device_bytes(apx_ctx *ctx, uint64_t handle);
 
 /* ---- synchronous drop-in entry points (host buffers) ----------------------------- */
@@ -277,7 +279,9 @@ APX_API int apx_status_decode(apx_ctx *ctx, uint64_t tensor, const apx_call_stat
  * which every GPU that loads the library holds until the process exits.
  *   - n_in above APX_NOALLOC_MAX_N_IN is refused with APX_ERR_TOO_LARGE.
  *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress);
- *     make that first call before any stream capture.
+ *     make that first call before any stream capture.  The address is kept until the process
+ *     exits: a cudaDeviceReset of that device invalidates it (with every context on it).
+ *   - The caller's current device is left as it was.
  *   - Every call on a device shares the one array and it keeps the last call's contents:
  *     calls whose kernels overlap on the GPU (other streams, other host threads) race.
  *     Serialise them on one stream.
@@ -340,6 +344,9 @@ typedef struct apx_gather_desc {
   apx_call_status *out_status[APX_MAX_GATHER_PROJ]; /* the first refusal over all ranks, in
                                                        whole-tensor rows; APX_ERR_DEVICE_TIMEOUT
                                                        when a rank's flag did not arrive    */
+  size_t bytes;                          /* size of every rank's gather buffer: the rows, keys,
+                                            flags and counters of the offsets above must lie
+                                            inside it (else APX_ERR_INVALID_ARGUMENT)        */
 } apx_gather_desc;
 
 /* Projection j of the publication on `stream`: this rank's gd->rows[j] rows (the tensor holds

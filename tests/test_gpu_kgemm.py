@@ -1,0 +1,186 @@
+"""GPU parity of the prefill contract on the digit-plane tensor-core GEMM, every family.
+
+Multi-column calls (four columns or more) take the digit-plane GEMM (apx_lgemm.cu) whenever the
+tensor's weights, over their row's smallest scale exponent, fit four balanced base-256 digits:
+Q4_K and Q6_K (the k-column projections the reference runs as gemm_q4_k / gemm_q6_k,
+src/engine/chart/kcols.rs:1406-1518, dispatched from matmat_q8act, src/engine/kern/matmat.rs:
+158-174) and Q8_0 (gemm_q8_0, src/engine/kern/gemm.rs:498-580).  A Q8_0 tensor whose weights
+need more digits keeps the per-block fold GEMM (apx_gemm.cu).  Bar: bit-exact Q32.32 outputs
+against the oracle's per-column contract (matmat.rs:92-134), identical refusals with the lowest
+refusing column, f32 outputs identical to the single-column f32 boundary.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from chart_inputs import random_payload, random_x
+from apeiron_b200 import chart, synth
+from apeiron_b200.chart import Backend, QuantAct
+
+pytestmark = pytest.mark.gpu
+
+Q8_0, Q4_K, Q6_K = 8, 12, 14
+KIND = {1: chart.ShapeMismatch, 3: chart.ShortPayload, 4: chart.LengthOverflow,
+        6: chart.NonFiniteScale, 7: chart.FixedOverflow, 8: chart.AccumulatorOverflow,
+        9: chart.OutputOverflow}
+THREADS = os.cpu_count() or 1
+
+
+@pytest.fixture(scope="module")
+def be():
+    b = Backend(0)
+    yield b
+    b.close()
+
+
+def bench_columns(n_in, k, seed):
+    """k benchmark activations (f32 N(0,1) through f32_to_fixed and quant_act)."""
+    qs = []
+    for c in range(k):
+        x = synth.f32_to_q32(synth.activation_f32(n_in, seed + c))
+        codes, exps = synth.quant_act_np(x)
+        qs.append(QuantAct.from_exps(exps, codes))
+    return qs
+
+
+def _col(n_in, seed, shift=0):
+    c, s = O.quant_act(random_x(n_in, seed) >> shift)
+    return QuantAct.from_parts(s, c)
+
+
+def device_bytes(be, t):
+    return be.lib.apx_tensor_device_bytes(be.ctx, t.handle)
+
+
+def digit_plane_bytes(n_out, n_in):
+    m_pad, kp = -(-n_out // 128) * 128, -(-n_in // 64) * 64
+    return 4 * m_pad * kp + 4 * m_pad
+
+
+def check_matmat(be, t, raw, n_out, n_in, qs, threads=1, simd=False):
+    """GPU matmat against the oracle's per-column contract; returns the GPU refusal or values."""
+    codes = np.stack([q.codes for q in qs])
+    scales = np.stack([q.scales for q in qs])
+    if threads > 1:
+        want = O.matmat_q8act_mt(t, raw, n_out, n_in, codes, scales, threads, simd=simd)
+    else:
+        want = O.matmat_q8act(t, raw, n_out, n_in, codes, scales)
+    try:
+        got = be.matmat_q8act(t, raw, n_out, n_in, qs)
+    except chart.MatvecError as e:
+        assert isinstance(want, tuple), f"GPU refused {e!r}, oracle gave values"
+        assert isinstance(e, KIND[want[1]]), (e, want)
+        assert e.col == want[5], (e.col, want)
+        return e
+    assert not isinstance(want, tuple), f"GPU gave values, oracle refused {want}"
+    got = np.stack(got)
+    if not np.array_equal(got, want):
+        bad = np.argwhere(got != want)
+        c, r = bad[0]
+        raise AssertionError(f"{len(bad)} outputs differ; first col {c} row {r}: "
+                             f"gpu {got[c, r]} oracle {want[c, r]}")
+    return got
+
+
+def run_and_check_route(be, t, raw, n_out, n_in, qs, **kw):
+    tensor = be._tensor(t, raw, n_out, n_in)
+    before = device_bytes(be, tensor)
+    out = check_matmat(be, t, raw, n_out, n_in, qs, **kw)
+    grown = device_bytes(be, tensor) - before
+    return out, grown
+
+
+@pytest.mark.parametrize("t,n_out,n_in,k", [
+    (Q4_K, 1536, 1024, 70),    # whole super-blocks, partial token tile
+    (Q4_K, 300, 896, 9),       # 896 wide (the 0.5B FFN width): ragged super-block, fast rows
+    (Q4_K, 130, 1000, 5),      # a width outside the fast rows: the contract's values
+    (Q6_K, 640, 512, 64),
+    (Q6_K, 257, 896, 33),      # ragged rows and width
+    (Q8_0, 4864, 896, 512),    # configs[2]: 512 tokens on both Qwen2.5-0.5B FFN shapes
+    (Q8_0, 896, 4864, 512),
+    (Q8_0, 200, 100, 70),      # ragged K (not a multiple of 32)
+])
+def test_digit_plane_gemm_equals_oracle(be, t, n_out, n_in, k):
+    raw = synth.payload(t, n_out, n_in, 17 + n_out + t)
+    qs = bench_columns(n_in, k, 400 + n_in)
+    _, grown = run_and_check_route(be, t, raw, n_out, n_in, qs, threads=THREADS)
+    assert grown == digit_plane_bytes(n_out, n_in), "the call did not take the digit planes"
+
+
+@pytest.mark.parametrize("n_out,n_in", [(28672, 8192), (8192, 28672)])
+def test_llama70b_ffn_prefill_512_tokens(be, n_out, n_in):
+    """configs[4]'s prefill: 512 tokens through the Llama-3-70B-shaped Q4_K FFN matrices, checked
+    column by column against the oracle's k-column Q4_K kernel (tested equal to the scalar
+    contract rows in test_oracle_x86.py)."""
+    raw = synth.payload(Q4_K, n_out, n_in, 70 + n_out)
+    qs = bench_columns(n_in, 512, 9000)
+    _, grown = run_and_check_route(be, Q4_K, raw, n_out, n_in, qs, threads=THREADS, simd=True)
+    assert grown == digit_plane_bytes(n_out, n_in)
+
+
+def test_kquant_mixed_routes(be):
+    """Zero columns, zero-scale blocks, an activation spread of 7 (the GEMM's last) and of 9 and
+    a bound-failing scale (both on the checked rows), in one Q4_K and one Q6_K call."""
+    for t in (Q4_K, Q6_K):
+        n_out, n_in, k = 384, 768, 12
+        raw = synth.payload(t, n_out, n_in, 5 + t)
+        qs = [_col(n_in, 60 + c) for c in range(k)]
+        qs[1] = QuantAct.from_parts(np.zeros(n_in // 32, np.int64), np.zeros(n_in, np.int8))
+        s = qs[2].scales.copy()
+        s[::3] = 0
+        qs[2] = QuantAct.from_parts(s, qs[2].codes)
+        for c, spread in ((3, 7), (4, 9)):
+            s = qs[c].scales.copy()
+            s[0] = s[1] << spread
+            qs[c] = QuantAct.from_parts(s, qs[c].codes)
+        s = qs[5].scales.copy()
+        s[4] = 1 << 56
+        c5 = qs[5].codes.copy()
+        c5[4 * 32:5 * 32] = np.clip(c5[4 * 32:5 * 32], -1, 1)
+        qs[5] = QuantAct.from_parts(s, c5)
+        check_matmat(be, t, raw, n_out, n_in, qs)
+
+
+def test_kquant_refusals(be):
+    """OutputOverflow in row order, a non-finite scale before or after it, and the lowest refusing
+    column, as the oracle reports them."""
+    n_out, n_in, k = 260, 512, 6
+    raw = random_payload(Q4_K, n_out, n_in, 0x7BFF, 0x7800, 11)
+    big = [QuantAct.from_parts(np.full(n_in // 32, 1 << 40, np.int64),
+                               np.full(n_in, 127 - c, np.int8)) for c in range(k)]
+    check_matmat(be, Q4_K, raw, n_out, n_in, [_col(n_in, 3 + c) for c in range(2)] + big[:2])
+    raw2 = raw.copy()
+    raw2[7 * 2 * 144 + 2: 7 * 2 * 144 + 4] = (0x00, 0x7C)  # row 7's dmin = +Inf
+    check_matmat(be, Q4_K, raw2, n_out, n_in, [_col(n_in, 3 + c) for c in range(k)])
+    check_matmat(be, Q4_K, raw2, n_out, n_in, [_col(n_in, 3 + c) for c in range(3)] + big[:3])
+    raw6 = random_payload(Q6_K, n_out, n_in, 0x7BFF, 0, 13)
+    check_matmat(be, Q6_K, raw6, n_out, n_in, [_col(n_in, 30 + c) for c in range(3)] + big[:3])
+
+
+def test_q8_0_wide_weight_spread_keeps_fold_gemm(be):
+    """Q8_0 rows whose block scales span 2^-24 .. 1.75 (exponent spread 14) need more than four
+    digits: the tensor gets no digit planes and the per-block fold GEMM serves it, bit-exact."""
+    n_out, n_in, k = 256, 1024, 16
+    raw = synth.payload(Q8_0, n_out, n_in, 41).reshape(-1, 34).copy()
+    rng = np.random.default_rng(3)
+    f16 = np.where(rng.random(raw.shape[0]) < 0.5, 2.0 ** -24, 1.75)
+    raw[:, 0:2] = f16.astype(np.float16).view(np.uint8).reshape(-1, 2)
+    raw = raw.reshape(-1)
+    qs = bench_columns(n_in, k, 77)
+    _, grown = run_and_check_route(be, Q8_0, raw, n_out, n_in, qs)
+    assert grown != digit_plane_bytes(n_out, n_in) and grown > 0
+
+
+@pytest.mark.parametrize("t,n_out,n_in,k", [(Q4_K, 1536, 1536, 40), (Q6_K, 512, 1024, 9),
+                                            (Q8_0, 896, 4864, 24)])
+def test_f32_prefill_equals_single_column(be, t, n_out, n_in, k):
+    """apx_matmat_f32 on the digit planes (fused quantize-prep) equals apx_matvec_f32 per token."""
+    raw = synth.payload(t, n_out, n_in, 90 + t)
+    tensor = be.upload(t, raw, n_out, n_in)
+    x = np.stack([synth.activation_f32(n_in, 500 + c) for c in range(k)])
+    got = be.matmat_f32(tensor, x)
+    want = np.stack([be.matvec_f32(tensor, x[c]) for c in range(k)])
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    tensor.free()

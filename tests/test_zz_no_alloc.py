@@ -8,6 +8,9 @@ output is the exact Q32.32 projection rounded once to f32), so the tolerance her
 the same as the other f32-path tests.  Two calls in a row with different activations check
 that the shared array carries nothing from one call into the next.
 
+Refusals must match too: an activation the quantizer refuses (NaN, Inf, |x| >= 2^31), a row
+with a non-finite weight scale, and a call over the first n_out < n rows of the tensor.
+
 This file is collected last (test_zz_*), so a run that stops at the first failure has run
 every other test before it; it also passes alone in a fresh process.
 """
@@ -52,6 +55,80 @@ def test_noalloc_matches_the_allocating_entry_point(ggml_type, n_out, n_in):
             torch.cuda.synchronize(dev)
             assert _decode(be, tensor, status) == _abi.APX_OK
             assert np.array_equal(dy.cpu().numpy(), want)
+    finally:
+        be.close()
+
+
+def _both(be, tensor, n_out, n_in, x):
+    """(rc, row, y) of apx_matvec_f32 and of apx_matvec_f32_noalloc on the same input."""
+    import torch
+
+    err = _abi.ApxErr()
+    y = np.full(max(n_out, 1), np.nan, dtype=np.float32)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rc = be.lib.apx_matvec_f32(be.ctx, tensor.handle, n_out, n_in,
+                               x.ctypes.data_as(C.c_void_p), y.ctypes.data_as(C.c_void_p),
+                               C.byref(err))
+    want = (rc, err.row if rc else None, y[:n_out] if rc == 0 else None)
+    dev = torch.device("cuda:0")
+    dx = torch.from_numpy(x).to(dev)
+    dy = torch.full((max(n_out, 1),), float("nan"), dtype=torch.float32, device=dev)
+    status = torch.zeros(2, dtype=torch.int64, device=dev)
+    assert be.lib.apx_matvec_f32_noalloc(be.ctx, tensor.handle, n_out, n_in, dx.data_ptr(),
+                                         dy.data_ptr(), status.data_ptr(),
+                                         torch.cuda.current_stream(dev).cuda_stream) == 0
+    torch.cuda.synchronize(dev)
+    st = _abi.CallStatus(int(status[0].item()) & ((1 << 64) - 1),
+                         int(status[1].item()) & ((1 << 64) - 1))
+    err2 = _abi.ApxErr()
+    rc2 = be.lib.apx_status_decode(be.ctx, tensor.handle, C.byref(st), C.byref(err2))
+    got = (rc2, err2.row if rc2 else None, dy.cpu().numpy()[:n_out] if rc2 == 0 else None)
+    return want, got
+
+
+def _same(want, got):
+    assert want[0] == got[0] and want[1] == got[1], (want[:2], got[:2])
+    if want[0] == _abi.APX_OK:
+        assert np.array_equal(want[2].view(np.uint32), got[2].view(np.uint32))
+
+
+def test_noalloc_refusals_and_partial_rows_match():
+    """A refusing activation (NaN, +Inf, 2^31), a call over the first rows only, and a row whose
+    block scale is Inf: the same result or refusal as apx_matvec_f32, twice in a row."""
+    be = Backend(0)
+    try:
+        n_out, n_in = 300, 1024
+        raw = synth.payload(8, n_out, n_in, 77)
+        tensor = be.upload(8, raw, n_out, n_in)
+        x = synth.activation_f32(n_in, 5)
+        for bad in (np.nan, np.inf, 2.0 ** 31):
+            xb = x.copy()
+            xb[700] = bad
+            want, got = _both(be, tensor, n_out, n_in, xb)
+            assert want[0] == _abi.APX_ERR_QUANT_REFUSED
+            _same(want, got)
+            _same(*_both(be, tensor, n_out, n_in, x))  # the next call is unaffected
+        for rows in (1, 31, 257):
+            _same(*_both(be, tensor, rows, n_in, synth.activation_f32(n_in, rows)))
+        raw2 = raw.copy()
+        raw2[(41 * (n_in // 32) + 3) * 34: (41 * (n_in // 32) + 3) * 34 + 2] = (0x00, 0x7C)
+        t2 = be.upload(8, raw2, n_out, n_in)
+        want, got = _both(be, t2, n_out, n_in, x)
+        assert want[0] == _abi.APX_ERR_NONFINITE_SCALE and want[1] == 41
+        _same(want, got)
+        _same(*_both(be, t2, 41, n_in, x))  # the rows before it project
+    finally:
+        be.close()
+
+
+def test_noalloc_at_its_widest_activation():
+    """n_in = APX_NOALLOC_MAX_N_IN: the codes end exactly at the end of the fixed array."""
+    be = Backend(0)
+    try:
+        n_out, n_in = 96, _abi.NOALLOC_MAX_N_IN
+        tensor = be.upload(8, synth.payload(8, n_out, n_in, 8), n_out, n_in)
+        for seed in (1, 2):
+            _same(*_both(be, tensor, n_out, n_in, synth.activation_f32(n_in, seed)))
     finally:
         be.close()
 
