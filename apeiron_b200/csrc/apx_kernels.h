@@ -118,22 +118,24 @@ cudaError_t launch_gemm_q8_0_f32(const GemvPlan &pl, const uint8_t *pack, const 
 
 // The digit-plane GEMM's view of a Q8_0 / Q4_K / Q6_K tensor (apx_lgemm.cu): every weight
 // W'[r,i] = w_{r,i} / 2^kmin_r (its Q32.32 value over the row's smallest scale exponent, an
-// integer) as four balanced base-256 int8 digits [4][m_pad][kp], kmin per row, and the 3D tensor
-// map of the digits.  ok = false when some weight needs more digits (the tensor then has no such view).
+// integer) as three or four balanced base-256 int8 digits [digits][m_pad][kp], kmin per row, and
+// the 3D tensor map of the digits.  ok = false when some weight needs more than four digits
+// (the tensor then has no such view).
 struct LimbLayout {
   void *base = nullptr;
-  int8_t *planes = nullptr;  // [4][m_pad][kp]
+  int8_t *planes = nullptr;  // [digits][m_pad][kp]
   int32_t *kmin = nullptr;   // [m_pad]
   size_t kp = 0, m_pad = 0;
+  int digits = 0;  // 3 when every weight fits three digits, else 4
   bool ok = false;
-  alignas(64) unsigned char map[128];  // the digits, 64-byte boxes × 128 rows × 4 planes
+  alignas(64) unsigned char map[128];  // the digits, 64-byte boxes × 128 rows × `digits` planes
 };
 
 bool limb_shape_ok(size_t n_in);
 cudaError_t build_limb_layout(const GemvPlan &pl, uint32_t type, const uint8_t *pack,
                               size_t n_out, size_t n_in, LimbLayout *lay, cudaStream_t stream);
 void free_limb_layout(LimbLayout *lay);
-// Device workspace of one call (zeroed once at allocation; its counters reset themselves).
+// Device workspace of one call (nothing in it outlives the call).
 size_t limb_work_bytes(size_t n_cols, size_t n_in, size_t n_out, int sm_count);
 // Exact k-column projection on the digit planes: the arguments of launch_gemm_q8_0 plus the
 // family (the checked columns' rows and the call bound follow it).

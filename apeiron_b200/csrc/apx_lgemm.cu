@@ -15,12 +15,13 @@
 //     X'[c,i] = x_i · 2^(e_b − emin_c),
 // and y[r,c] = round_shift_32(acc) with the i64 range check (chart/mod.rs:1746-1753).
 //
-// Digit planes.  W' is written once per tensor as four balanced base-256 digits (each in
-// [−128, 127], W' = Σ_j 256^j·w_j) and X' per call as two (|X'| <= 128·2^7 = 2^14).  Every digit
-// pair is one ordinary int8 GEMM over the whole K on the tensor cores (tcgen05.mma kind::i8,
-// s32 accumulators in TMEM); pairs of equal weight 256^(j+l) share an accumulator, so five
-// accumulators p = 0..4 hold A_p = Σ_{j+l=p} Σ_i w_j[i]·x_l[i], and the exact combine
-// T = Σ_p 256^p·A_p runs once per output instead of once per block.  Bounds:
+// Digit planes.  W' is written once per tensor as D = 3 or 4 balanced base-256 digits (each in
+// [−128, 127], W' = Σ_j 256^j·w_j; three when every weight of the tensor fits, as the benchmark's
+// Q8_0 weights do) and X' per call as two (|X'| <= 128·2^7 = 2^14).  Every digit pair is one
+// ordinary int8 GEMM over the whole K on the tensor cores (tcgen05.mma kind::i8, s32 accumulators
+// in TMEM); pairs of equal weight 256^(j+l) share an accumulator, so D + 1 accumulators
+// p = 0..D hold A_p = Σ_{j+l=p} Σ_i w_j[i]·x_l[i], and the exact combine T = Σ_p 256^p·A_p runs
+// once per output instead of once per block.  Bounds:
 //   |w_j·x_l| <= 128·128 (l = 0) and 128·64 (l = 1), two pairs per accumulator: |A_p| <=
 //   24576·K < 2^31 for K <= 65536;
 //   |W'| < 2^31 and |X'| <= 2^14, so |T| < K·2^45 < 2^62 for K <= 65536 (the finish's bound);
@@ -29,17 +30,20 @@
 //   exceeds 7 or whose scales fail the reference's call bound (chart/mod.rs:362-383) takes the
 //   checked rows (matvec_fixed), as the bound-failing columns of the reference do.
 //
-// Layout in HBM: the weight digits as [4][m_pad][kp] int8 (rows padded to 128, K to 64), kmin
+// Layout in HBM: the weight digits as [D][m_pad][kp] int8 (rows padded to 128, K to 64), kmin
 // per row; per call the activation digits [2][n_pad][kp], emin and a route per token.
 //
-// Kernel: one CTA per SM (stream-K: every CTA takes an equal run of the (tile, K stage) space;
-// a tile of 128 rows × 64 tokens split between CTAs meets its partial sums in global memory and
-// the last to arrive finishes it — no waiting).  Warp 0 issues TMA (3D boxes, 64-byte swizzle,
-// no multicast) of the stage's 4 weight digit tiles and 2 activation digit tiles into a 5-stage
-// ring; warp 1 owns TMEM and issues 8 MMAs per 32-lane block; warps 2..9 drain the five
-// accumulators into i64 sums (T = 256·T + A_p), release TMEM to the next tile's MMAs, and finish
-// and store from registers.  Every wait is bounded; a wait that gives up reports
-// APX_ERR_DEVICE_TIMEOUT for the call's columns, drains what is in flight and frees TMEM.
+// Kernel: one CTA per SM; a tile is 128 rows × N tokens (N = 128 with three weight digits: four
+// accumulators fill TMEM's 512 columns; 96 with four: five accumulators).  Whole tiles go in
+// data-parallel waves (the CTAs of a wave share each weight row tile through L2); the tiles left
+// over are split evenly in K-contiguous runs (stream-K), a split tile meeting its partial sums in
+// global memory where the last CTA to arrive finishes it — no waiting.  Warp 0 issues TMA (3D
+// boxes, 64-byte swizzle, no multicast) of a stage's D weight digit tiles and 2 activation digit
+// tiles into a 5-stage ring; warp 1 owns TMEM and issues 2·D MMAs per 32-lane block; warps 2..17
+// drain the accumulators into i64 sums (T = 256·T + A_p), release TMEM to the next tile's MMAs,
+// and finish and store from registers; at the end the same CTAs take the checked columns' rows.
+// Every wait is bounded; a wait that gives up reports APX_ERR_DEVICE_TIMEOUT for the call's
+// columns, drains what is in flight and frees TMEM.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -59,30 +63,35 @@ namespace apx {
 namespace {
 
 constexpr int kLM = 128;        // weight rows per tile (MMA M)
-constexpr int kLN = 64;         // tokens per tile (MMA N)
 constexpr int kLK = 64;         // K bytes per stage: two 32-lane blocks, one 64-byte swizzle row
 constexpr int kLStages = 5;
-constexpr int kWDig = 4, kXDig = 2, kAccs = kWDig + kXDig - 1;
-constexpr int kLEpiWarps = 8;   // 2 per TMEM lane quarter: 32 rows × 32 tokens each
+constexpr int kXDig = 2;        // activation digits
+constexpr int kLEpiWarps = 16;  // 4 per TMEM lane quarter: 32 rows × N/4 tokens each
 constexpr int kLThreads = 32 * (2 + kLEpiWarps);
 constexpr int kLMaxShift = 7;   // X' = x·2^s with |x| <= 128 stays within two digits
 constexpr size_t kLMaxK = 65536;
-constexpr int kLTileW = kLM * kLK;                  // 8 KB: one weight digit tile
-constexpr int kLTileX = kLN * kLK;                  // 4 KB: one activation digit tile
-constexpr int kLStageBytes = kWDig * kLTileW + kXDig * kLTileX;  // 40 KB
-constexpr int kLFallbackCtas = 32;  // extra CTAs of each launch for the checked columns
+constexpr int kLTileW = kLM * kLK;  // 8 KB: one weight digit tile
+constexpr int kLNMin = 64, kLNMax = 128;  // token tile widths (workspace bounds)
 constexpr int kLMinIters = 4;       // stages per stream-K CTA at least
 constexpr unsigned kRouteNone = 0, kRouteGemm = 1, kRouteChecked = 2;
-constexpr long long kPartSlot = (long long)kLEpiWarps * 32 * 32;  // i64 per partial tile
+constexpr long long kPartSlot = (long long)kLM * kLNMax;  // i64 per partial tile
 
-static_assert(kLStageBytes % 1024 == 0 && kLTileW % 1024 == 0 && kLTileX % 1024 == 0,
-              "stages keep the alignment of the swizzled tiles");
-static_assert(kAccs * kLN <= 512, "the accumulators fit in TMEM");
-
-// Instruction descriptor of kind::i8: D s32 (2) at bits 4-5, A and B signed 8-bit (1) at bits
-// 7-9 and 10-12, both K-major, N>>3 at bits 17-22, M>>4 at bits 24-28.
-constexpr uint32_t kLIdesc = (2u << 4) | (1u << 7) | (1u << 10) |
-                             ((uint32_t)(kLN >> 3) << 17) | ((uint32_t)(kLM >> 4) << 24);
+// The kernel's shape for D weight digits and N-token tiles.
+template <int D, int N>
+struct LShape {
+  static constexpr int kAcc = D + kXDig - 1;        // accumulators (TMEM: kAcc·N columns)
+  static constexpr int kTileX = N * kLK;            // one activation digit tile
+  static constexpr int kStage = D * kLTileW + kXDig * kTileX;
+  static constexpr int kEpt = N / 4;                // tokens per epilogue warp
+  // Instruction descriptor of kind::i8: D s32 (2) at bits 4-5, A and B signed 8-bit (1) at
+  // bits 7-9 and 10-12, both K-major, N>>3 at bits 17-22, M>>4 at bits 24-28.
+  static constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) |
+                                     ((uint32_t)(N >> 3) << 17) | ((uint32_t)(kLM >> 4) << 24);
+  static_assert(kAcc * N <= 512, "the accumulators fit in TMEM");
+  static_assert(kStage % 1024 == 0 && kTileX % 1024 == 0, "stages keep the swizzle alignment");
+  static_assert(kLStages * kStage + 4096 <= 227 * 1024, "the ring fits in shared memory");
+  static_assert(kEpt % 8 == 0 && N % 16 == 0 && N <= kLNMax && N >= kLNMin, "tile shape");
+};
 
 // Shared-memory matrix descriptor of a K-major operand in the 64-byte-swizzled layout TMA writes:
 // start address >> 4 in bits 0-13, leading byte offset 16 (>> 4, unused for swizzled K-major)
@@ -91,14 +100,6 @@ constexpr uint32_t kLIdesc = (2u << 4) | (1u << 7) | (1u << 10) |
 // the second 32-lane block of a stage starts 32 bytes further.
 constexpr uint64_t kLDescHi = ((uint64_t)(16 >> 4) << 16) | ((uint64_t)(512 >> 4) << 32) |
                               ((uint64_t)1 << 46) | ((uint64_t)4 << 61);
-
-// The eight digit pairs (j, l) in issue order, accumulator j + l; `init` marks the first pair
-// of each accumulator (it overwrites on the first block of a tile).
-struct Pair {
-  int j, l, init;
-};
-__device__ constexpr Pair kPairs[8] = {{0, 0, 1}, {1, 0, 1}, {0, 1, 0}, {2, 0, 1},
-                                       {1, 1, 0}, {3, 0, 1}, {2, 1, 0}, {3, 1, 1}};
 
 // bar.red.or over the epilogue warps (named barrier 1): every warp learns whether any of them
 // saw `v`, so all take the same branch.
@@ -172,11 +173,12 @@ __global__ void limb_row_kmin(PackGeo geo, size_t n_out, size_t n_in, int32_t *k
   if (lane == 0) kmin[row] = lo == (1 << 30) ? 0 : lo;
 }
 
-// W'[row, 32g .. 32g+31] (zero past n_in and n_out) as four digit planes; *bad = 1 where a value
-// needs more than four digits.  One thread per (row, 32-lane group).
+// W'[row, 32g .. 32g+31] (zero past n_in and n_out) as four digit planes; bit 0 of *flags where
+// a value needs more than four digits, bit 1 where one needs the fourth.  One thread per (row,
+// 32-lane group).
 template <uint32_t T>
 __global__ void limb_build_planes(PackGeo geo, size_t n_out, size_t n_in, size_t m_pad, size_t kp,
-                                  const int32_t *kmin, int8_t *planes, int *bad) {
+                                  const int32_t *kmin, int8_t *planes, int *flags) {
   const size_t groups = kp / 32;
   const size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (idx >= m_pad * groups) return;
@@ -186,7 +188,7 @@ __global__ void limb_build_planes(PackGeo geo, size_t n_out, size_t n_in, size_t
   for (int j = 0; j < 4; j++)
 #pragma unroll
     for (int q = 0; q < 8; q++) pl[j][q] = 0;
-  bool ok = true;
+  bool ok = true, need4 = false;
   if (row < n_out && g * 32 < n_in) {
     const int km = kmin[row];
     long long w[32];
@@ -257,11 +259,13 @@ __global__ void limb_build_planes(PackGeo geo, size_t n_out, size_t n_in, size_t
       uint32_t d;
       if (g * 32 + t >= n_in) w[t] = 0;
       ok = digits4(w[t], d) && ok;
+      need4 = need4 || (d >> 24) != 0;
 #pragma unroll
       for (int j = 0; j < 4; j++) pl[j][t / 4] |= ((d >> (8 * j)) & 0xFFu) << (8 * (t % 4));
     }
   }
-  if (!ok) atomicOr(bad, 1);
+  const int f = (ok ? 0 : 1) | (need4 ? 2 : 0);
+  if (f) atomicOr(flags, f);
 #pragma unroll
   for (int j = 0; j < 4; j++) {
     uint4 *dst = reinterpret_cast<uint4 *>(planes + ((size_t)j * m_pad + row) * kp + g * 32);
@@ -273,7 +277,8 @@ __global__ void limb_build_planes(PackGeo geo, size_t n_out, size_t n_in, size_t
 // ---- per-call workspace --------------------------------------------------------------------------
 
 // Nothing in it outlives a call: the prep kernel zeroes the tile counters and writes every
-// column's route, emin and digits before the GEMM reads them.
+// column's route, emin and digits before the GEMM reads them.  Regions are sized for the
+// narrowest token tile (most tiles) and the widest (most padding columns).
 struct LWork {
   int *cnt;          // [tiles] arrivals of the tiles split between CTAs (zeroed by the prep)
   long long *part;   // [2·sm_count][kPartSlot] partial sums of split tiles
@@ -284,21 +289,23 @@ struct LWork {
   uint8_t *qexps;    // and exponent bytes [n_pad][kp / 32]
 };
 
-__host__ __device__ size_t lpad_cols(size_t n) { return (n + kLN - 1) / kLN * kLN; }
 size_t lpad_k(size_t n_in) { return (n_in + kLK - 1) / kLK * kLK; }
-size_t ltiles(size_t n_out, size_t n_cols) {
-  return ((n_out + kLM - 1) / kLM) * ((n_cols + kLN - 1) / kLN);
+size_t lpad_n(size_t n, int nt) { return (n + nt - 1) / nt * nt; }
+size_t ltiles(size_t n_out, size_t n_cols, int nt) {
+  return ((n_out + kLM - 1) / kLM) * ((n_cols + nt - 1) / nt);
 }
 size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
 
 size_t lwork_bytes(size_t n_cols, size_t n_in, size_t n_out, int sm_count) {
-  const size_t np = lpad_cols(n_cols), kp = lpad_k(n_in), tiles = ltiles(n_out, n_cols);
+  const size_t np = lpad_n(n_cols, kLNMax), kp = lpad_k(n_in);
+  const size_t tiles = ltiles(n_out, n_cols, kLNMin);
   return align256(tiles * 4) + align256((size_t)2 * std::max(sm_count, 1) * kPartSlot * 8) +
          align256(np * 4) * 2 + 2 * np * kp + align256(np * kp) + align256(np * (kp / 32)) + 256;
 }
 
 LWork lwork_view(void *base, size_t n_cols, size_t n_in, size_t n_out, int sm_count) {
-  const size_t np = lpad_cols(n_cols), kp = lpad_k(n_in), tiles = ltiles(n_out, n_cols);
+  const size_t np = lpad_n(n_cols, kLNMax), kp = lpad_k(n_in);
+  const size_t tiles = ltiles(n_out, n_cols, kLNMin);
   uint8_t *p = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(base) + 255) & ~(uintptr_t)255);
   LWork w;
@@ -348,6 +355,7 @@ struct LPrepArgs {
   const ActDesc *descs;  // the quantizer's descriptors (a refusal there wins), or null
   const float *x;        // f32 path: column c at x + c·ldx
   size_t ld, ldb, ldx, n_in, kp;
+  size_t np;  // columns padded to the GEMM's token tile: the digit planes' rows
   int nb, n_cols, tiles;
   long long top;  // the family's call-bound constant (chart/mod.rs:1697-1706)
   LWork w;
@@ -382,7 +390,7 @@ __global__ void __launch_bounds__(256) limb_prep_kernel(LPrepArgs a) {
   __shared__ int s_emin, s_emax, s_status;
   __shared__ unsigned s_route;
   const int c = blockIdx.x;
-  const size_t np = lpad_cols((size_t)a.n_cols);
+  const size_t np = a.np;
   lprep_common_start(a);
   if (c >= a.n_cols) {
     lzero_column(a, c, np);
@@ -478,7 +486,7 @@ __global__ void __launch_bounds__(256) limb_quant_prep_kernel(LPrepArgs a) {
   __shared__ int s_emin, s_emax, s_status;
   __shared__ unsigned s_route;
   const int c = blockIdx.x;
-  const size_t np = lpad_cols((size_t)a.n_cols);
+  const size_t np = a.np;
   lprep_common_start(a);
   if (c >= a.n_cols) {
     lzero_column(a, c, np);
@@ -597,10 +605,16 @@ struct LArgs {
   float *out_f32;        // [n_cols][n_out] or null
   unsigned long long *status;  // column c at status[c·2]
   size_t n_out;
-  int n_cols, kstages, n_tiles, tiles;
-  long long iters;  // tiles · kstages: the stream-K space, tile-major (tile = mt·n_tiles + nt)
-  int G;            // stream-K CTAs; CTA b takes [b·iters/G, (b+1)·iters/G)
-  // checked route (matvec_fixed per row) of the columns the prep kernel listed
+  int n_cols, kstages, n_tiles, tiles;  // tile = mt·n_tiles + nt
+  // Work split over G CTAs (one per SM at most): `waves` data-parallel waves of whole tiles (CTA
+  // b takes tiles b, b + G, ...: the CTAs of a wave share weight row tiles, so each row tile's
+  // digits stream from HBM once), then the remaining tiles' (tile, stage) space, sk_iters long,
+  // split evenly in K-contiguous runs over the first Gs CTAs (stream-K: CTA b < Gs takes
+  // [b·sk_iters/Gs, (b+1)·sk_iters/Gs); Gs <= sk_iters, so no run is empty and every CTA between
+  // a split tile's first and last owner contributes to it).
+  int G, waves, Gs;
+  long long sk_iters;
+  // checked route (matvec_fixed per row) of the columns the prep kernel routed there
   PackGeo geo;
   const int8_t *codes;
   const uint8_t *exps;
@@ -608,53 +622,79 @@ struct LArgs {
 };
 
 __device__ __forceinline__ long long lstart(const LArgs &g, int b) {
-  return (long long)b * g.iters / g.G;
+  return b >= g.Gs ? g.sk_iters : (long long)b * g.sk_iters / g.Gs;
 }
-// The stream-K CTA whose run holds iteration `it`.
+// The CTA whose stream-K run holds iteration `it` of the remaining tiles.
 __device__ __forceinline__ int lowner(const LArgs &g, long long it) {
-  return (int)(((it + 1) * (long long)g.G - 1) / g.iters);
+  return (int)(((it + 1) * (long long)g.Gs - 1) / g.sk_iters);
 }
-
-// The checked rows (matvec_fixed per row) of every column the prep kernel routed there: the
-// extra CTAs walk the columns in order and split each one's rows between their threads.
-template <uint32_t T>
-__device__ __forceinline__ void lchecked_columns(const LArgs &g) {
-  const size_t first = (size_t)(blockIdx.x - g.G) * blockDim.x + threadIdx.x;
-  const size_t stride = (size_t)kLFallbackCtas * blockDim.x;
-  for (int c = 0; c < g.n_cols; c++) {
-    if (__ldg(g.w.route + c) != kRouteChecked) continue;  // uniform over the CTA
-    for (size_t row = first; row < g.n_out; row += stride)
-      checked_row<T>(g.geo, row, g.n_out, g.n_in, g.codes + (size_t)c * g.ld,
-                     g.exps + (size_t)c * g.ldb,
-                     g.out_q32 ? g.out_q32 + (size_t)c * g.n_out : nullptr,
-                     g.out_f32 ? g.out_f32 + (size_t)c * g.n_out : nullptr,
-                     g.status + (size_t)c * 2);
+// CTA b's local iteration i (its waves' stages first, then its stream-K run from s0): tile, stage.
+__device__ __forceinline__ void lat(const LArgs &g, int b, long long s0, int i, int &tile,
+                                    int &ks) {
+  const int dp = g.waves * g.kstages;
+  if (i < dp) {
+    tile = b + (i / g.kstages) * g.G;
+    ks = i % g.kstages;
+  } else {
+    const long long it = s0 + (i - dp);
+    tile = g.waves * g.G + (int)(it / g.kstages);
+    ks = (int)(it % g.kstages);
   }
 }
 
+// The checked rows (matvec_fixed per row) of every column the prep kernel routed there, by the
+// GEMM's CTAs once their tiles are done: they read the routes a CTA-width at a time (one load
+// per thread), gather that chunk's checked columns in shared memory and split each one's rows
+// between all their threads.
 template <uint32_t T>
+__device__ __forceinline__ void lchecked_columns(const LArgs &g) {
+  __shared__ int s_cols[kLThreads];
+  __shared__ int s_n;
+  const size_t first = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const size_t stride = (size_t)g.G * blockDim.x;
+  for (int base = 0; base < g.n_cols; base += blockDim.x) {
+    if (threadIdx.x == 0) s_n = 0;
+    __syncthreads();
+    const int c = base + (int)threadIdx.x;
+    if (c < g.n_cols && __ldg(g.w.route + c) == kRouteChecked) s_cols[atomicAdd(&s_n, 1)] = c;
+    __syncthreads();
+    for (int i = 0; i < s_n; i++) {
+      const int cc = s_cols[i];
+      for (size_t row = first; row < g.n_out; row += stride)
+        checked_row<T>(g.geo, row, g.n_out, g.n_in, g.codes + (size_t)cc * g.ld,
+                       g.exps + (size_t)cc * g.ldb,
+                       g.out_q32 ? g.out_q32 + (size_t)cc * g.n_out : nullptr,
+                       g.out_f32 ? g.out_f32 + (size_t)cc * g.n_out : nullptr,
+                       g.status + (size_t)cc * 2);
+    }
+    __syncthreads();
+  }
+}
+
+// 18 warps, one CTA per SM: the warps spread 5/5/4/4 over the SM's four 16,384-register
+// sub-partitions, which caps them at 96 registers each.
+template <uint32_t T, int D, int N>
 __global__ void __launch_bounds__(kLThreads, 1)
     limb_gemm_kernel(const __grid_constant__ CUtensorMap map_w,
                      const __grid_constant__ CUtensorMap map_x, LArgs g) {
-  if ((int)blockIdx.x >= g.G) {
-    pdl_wait();  // the prep kernel's routes and codes
-    lchecked_columns<T>(g);
-    return;
-  }
+  using S = LShape<D, N>;
+  constexpr int kAcc = S::kAcc, kEpt = S::kEpt, kStage = S::kStage;
   extern __shared__ uint8_t lsmem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(lsmem_raw) + 1023) & ~(uintptr_t)1023);
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kLStages * kLStageBytes);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kLStages * kStage);
   uint64_t *full = bars, *empty = bars + kLStages;
   uint64_t *tfull = bars + 2 * kLStages, *tempty = tfull + 1, *mdone = tfull + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mdone + 1);
   int *timeout = reinterpret_cast<int *>(tmem_slot + 1);
   int *slast = timeout + 1;  // split tile: this CTA arrived last
+  int *tok_e = slast + 3;    // [N]: the tile's token exponents emin_c, -1 off the GEMM route
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int b = (int)blockIdx.x;
-  const long long it0 = lstart(g, b), it1 = lstart(g, b + 1);
-  const int nit = (int)(it1 - it0);
+  const long long s0 = lstart(g, b), s1 = lstart(g, b + 1);
+  const int dp = g.waves * g.kstages;
+  const int nit = dp + (int)(s1 - s0);
 
   if (threadIdx.x == 0) {
     for (int st = 0; st < kLStages; st++) {
@@ -668,7 +708,7 @@ __global__ void __launch_bounds__(kLThreads, 1)
     prefetch_map(&map_w);
     prefetch_map(&map_x);
   }
-  if (warp == 1) {  // TMEM: kAccs × kLN columns of 32-bit accumulators (a 512-column allocation)
+  if (warp == 1) {  // TMEM: kAcc × N columns of 32-bit accumulators (a 512-column allocation)
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_addr(tmem_slot)),
                  "r"(512)
@@ -679,28 +719,28 @@ __global__ void __launch_bounds__(kLThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  auto stage_w = [&](int st) { return smem + st * kLStageBytes; };
-  auto stage_x = [&](int st) { return smem + st * kLStageBytes + kWDig * kLTileW; };
+  auto stage_w = [&](int st) { return smem + st * kStage; };
+  auto stage_x = [&](int st) { return smem + st * kStage + D * kLTileW; };
   // The weight digits are the tensor's, constant since the layout was built: the first stages'
   // loads of them go out before the wait for the prep kernel (programmatic dependent launch).
   // Everything the prep kernel writes is read after the wait.
   const int pre = min(nit, kLStages);
   if (threadIdx.x == 0) {
     for (int i = 0; i < pre; i++) {
-      const long long it = it0 + i;
-      const int tile = (int)(it / g.kstages), ks = (int)(it % g.kstages);
-      mbar_expect_tx(full + i, kLStageBytes);
+      int tile, ks;
+      lat(g, b, s0, i, tile, ks);
+      mbar_expect_tx(full + i, kStage);
       tma_load_3d(stage_w(i), &map_w, ks * kLK, (tile / g.n_tiles) * kLM, 0, full + i);
     }
   }
   pdl_wait();
 
   if (warp == 0) {
-    // ---- TMA producer (lane 0): per stage the 4 weight digit tiles and the 2 activation ones
+    // ---- TMA producer (lane 0): per stage the D weight digit tiles and the 2 activation ones
     int issued = 0;
     for (int i = 0; i < nit; i++) {
-      const long long it = it0 + i;
-      const int tile = (int)(it / g.kstages), ks = (int)(it % g.kstages);
+      int tile, ks;
+      lat(g, b, s0, i, tile, ks);
       const int st = i % kLStages, use = i / kLStages;
       int stop = 0;
       if (lane == 0) {
@@ -709,10 +749,10 @@ __global__ void __launch_bounds__(kLThreads, 1)
           stop = 1;
         } else {
           if (i >= pre) {
-            mbar_expect_tx(full + st, kLStageBytes);
+            mbar_expect_tx(full + st, kStage);
             tma_load_3d(stage_w(st), &map_w, ks * kLK, (tile / g.n_tiles) * kLM, 0, full + st);
           }
-          tma_load_3d(stage_x(st), &map_x, ks * kLK, (tile % g.n_tiles) * kLN, 0, full + st);
+          tma_load_3d(stage_x(st), &map_x, ks * kLK, (tile % g.n_tiles) * N, 0, full + st);
           issued++;
         }
       }
@@ -720,21 +760,23 @@ __global__ void __launch_bounds__(kLThreads, 1)
     }
     // every copy this thread started has landed before the CTA may exit
     if (lane == 0) {
-      for (int i = max(issued, pre) > kLStages ? max(issued, pre) - kLStages : 0;
-           i < max(issued, pre); i++)
+      const int last = max(issued, pre);
+      for (int i = last > kLStages ? last - kLStages : 0; i < last; i++)
         mbar_wait(full + i % kLStages, (i / kLStages) & 1);
     }
   } else if (warp == 1) {
-    // ---- MMA issuer (lane 0): 8 MMAs per 32-lane block, one commit per stage (frees it) and
-    // one per tile piece (its accumulators are complete) ----
+    // ---- MMA issuer (lane 0): 2·D MMAs per 32-lane block, one commit per stage (frees it) and
+    // one per tile piece (its accumulators are complete).  Accumulator p takes the pairs
+    // (p, 0) and (p − 1, 1); the first of them on a piece's first block overwrites it. ----
     if (lane == 0) {
       const uint64_t w0 = kLDescHi | (smem_addr(stage_w(0)) >> 4);
       const uint64_t x0 = kLDescHi | (smem_addr(stage_x(0)) >> 4);
       bool ok = true;
       int i = 0, piece = 0;
-      for (long long it = it0; ok && it < it1; piece++) {
-        const int ks0 = (int)(it % g.kstages);
-        const int nk = (int)min((long long)(g.kstages - ks0), it1 - it);
+      for (int pi = 0; ok && pi < nit; piece++) {
+        int tile, ks0;
+        lat(g, b, s0, pi, tile, ks0);
+        const int nk = min(g.kstages - ks0, nit - pi);
         if (piece > 0 && !mbar_wait(tempty, (piece - 1) & 1)) {
           ok = false;
           break;
@@ -747,69 +789,89 @@ __global__ void __launch_bounds__(kLThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint64_t wd = w0 + (uint64_t)(st * (kLStageBytes >> 4));
-          const uint64_t xd = x0 + (uint64_t)(st * (kLStageBytes >> 4));
+          const uint64_t wd = w0 + (uint64_t)(st * (kStage >> 4));
+          const uint64_t xd = x0 + (uint64_t)(st * (kStage >> 4));
 #pragma unroll
           for (int q = 0; q < kLK / 32; q++) {
+            const bool first = k == 0 && q == 0;
 #pragma unroll
-            for (int pp = 0; pp < 8; pp++) {
-              const Pair pr = kPairs[pp];
-              const uint32_t accumulate = (k == 0 && q == 0 && pr.init) ? 0u : 1u;
-              mma_i8(tmem + (uint32_t)((pr.j + pr.l) * kLN),
-                     wd + (uint64_t)(pr.j * (kLTileW >> 4) + 2 * q),
-                     xd + (uint64_t)(pr.l * (kLTileX >> 4) + 2 * q), kLIdesc, accumulate);
+            for (int p = 0; p < kAcc; p++) {
+              const uint32_t acc = tmem + (uint32_t)(p * N);
+              if (p < D)  // (p, 0)
+                mma_i8(acc, wd + (uint64_t)(p * (kLTileW >> 4) + 2 * q),
+                       xd + (uint64_t)(2 * q), S::kIdesc, first ? 0u : 1u);
+              if (p >= 1)  // (p − 1, 1)
+                mma_i8(acc, wd + (uint64_t)((p - 1) * (kLTileW >> 4) + 2 * q),
+                       xd + (uint64_t)((S::kTileX >> 4) + 2 * q), S::kIdesc,
+                       (first && p == D) ? 0u : 1u);
             }
           }
           mma_commit(empty + st);
         }
         if (!ok) break;
         mma_commit(tfull);
-        it += nk;
+        pi += nk;
       }
       if (!ok) atomicExch(timeout, 1);
       mma_commit(mdone);
       if (!mbar_wait(mdone, 0)) atomicExch(timeout, 1);
     }
   } else {
-    // ---- epilogue: 32 rows × 32 tokens per warp ----
+    // ---- epilogue: 32 rows × kEpt tokens per warp ----
     const int ew = warp - 2;
     const int lq = warp % 4;  // the TMEM lane quarter this warp may read
-    const int th = ew / 4;    // token half
+    const int tq = ew / 4;    // token quarter
     const int rl = 32 * lq + lane;
-    const uint32_t trow = tmem + ((uint32_t)(32 * lq) << 16) + (uint32_t)(32 * th);
+    const uint32_t trow = tmem + ((uint32_t)(32 * lq) << 16) + (uint32_t)(kEpt * tq);
     int piece = 0;
-    for (long long it = it0; it < it1; piece++) {
-      const int tile = (int)(it / g.kstages), ks0 = (int)(it % g.kstages);
-      const int nk = (int)min((long long)(g.kstages - ks0), it1 - it);
+    for (int pi = 0; pi < nit; piece++) {
+      int tile, ks0;
+      lat(g, b, s0, pi, tile, ks0);
+      const int nk = min(g.kstages - ks0, nit - pi);
       const int mt = tile / g.n_tiles, nt = tile % g.n_tiles;
-      const bool got = mbar_wait(tfull, piece & 1);
+      const bool got = mbar_wait_long(tfull, piece & 1);
+      // every epilogue warp is done with the previous piece (tok_e included) past this barrier
       if (epi_any(!got)) {
         if (lane == 0) atomicExch(timeout, 1);
         break;
       }
       tc_fence_after();
-      // drain: T = Σ_p 256^p·A_p by Horner from the top accumulator
-      long long acc[32];
+      if (ew == 0)
+        for (int t = lane; t < N; t += 32) {
+          const int c = nt * N + t;
+          tok_e[t] = c < g.n_cols && __ldg(g.w.route + c) == kRouteGemm ? __ldg(g.w.emin + c)
+                                                                          : -1;
+        }
+      // drain: T = Σ_p 256^p·A_p by Horner from the top accumulator, up to 16 columns per wait
+      long long acc[kEpt];
+      constexpr int kChunk = kEpt % 16 == 0 ? 16 : 8;
 #pragma unroll
-      for (int p = kAccs - 1; p >= 0; p--) {
-        uint32_t v[32];
-        tmem_ld32_nowait(trow + (uint32_t)(p * kLN), v);
-        tmem_wait_ld();
+      for (int p = kAcc - 1; p >= 0; p--) {
 #pragma unroll
-        for (int j = 0; j < 32; j++)
-          acc[j] = p == kAccs - 1 ? (long long)(int)v[j] : acc[j] * 256 + (long long)(int)v[j];
+        for (int c = 0; c < kEpt / kChunk; c++) {
+          uint32_t v[kChunk];
+#pragma unroll
+          for (int h = 0; h < kChunk / 8; h++)
+            tmem_ld8_nowait(trow + (uint32_t)(p * N + kChunk * c + 8 * h), v, h);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < kChunk; j++)
+            acc[kChunk * c + j] = p == kAcc - 1 ? (long long)(int)v[j]
+                                                : acc[kChunk * c + j] * 256 + (long long)(int)v[j];
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty);  // the next piece's MMAs may overwrite TMEM
-      const long long tbeg = (long long)tile * g.kstages;
       bool finish = ks0 == 0 && nk == g.kstages;  // this CTA holds the whole tile
       if (!finish) {
-        // split tile: store the partial sums, arrive; the last to arrive adds the others'
-        const int slot = 2 * b + (it == it0 ? 0 : 1);
-        long long *mine = g.w.part + (size_t)slot * kPartSlot + (size_t)ew * 1024;
+        // split tile (stream-K): store the partial sums, arrive; the last to arrive adds the
+        // others'.  Slot 2b holds CTA b's first run piece, 2b + 1 its last.
+        const long long tbeg = (long long)(tile - g.waves * g.G) * g.kstages;
+        const int slot = 2 * b + (pi == dp ? 0 : 1);
+        long long *mine = g.w.part + (size_t)slot * kPartSlot + (size_t)ew * (kEpt * 32);
 #pragma unroll
-        for (int j = 0; j < 32; j++) mine[j * 32 + lane] = acc[j];
+        for (int j = 0; j < kEpt; j++) mine[j * 32 + lane] = acc[j];
         __threadfence();
         epi_sync();
         const int bf = lowner(g, tbeg), bl = lowner(g, tbeg + g.kstages - 1);
@@ -826,11 +888,14 @@ __global__ void __launch_bounds__(kLThreads, 1)
           for (int b2 = bf; b2 <= bl; b2++) {
             if (b2 == b) continue;
             const int slot2 = 2 * b2 + ((b2 == bf && lstart(g, b2) < tbeg) ? 1 : 0);
-            const long long *other = g.w.part + (size_t)slot2 * kPartSlot + (size_t)ew * 1024;
+            const long long *other =
+                g.w.part + (size_t)slot2 * kPartSlot + (size_t)ew * (kEpt * 32);
 #pragma unroll
-            for (int j = 0; j < 32; j++) acc[j] += __ldcg(other + j * 32 + lane);
+            for (int j = 0; j < kEpt; j++) acc[j] += __ldcg(other + j * 32 + lane);
           }
         }
+      } else {
+        epi_sync();  // tok_e is written
       }
       if (finish) {
         // y = round_shift_32(T·2^(kmin_r + emin_c)) and its f32 image, stored from registers:
@@ -838,49 +903,50 @@ __global__ void __launch_bounds__(kLThreads, 1)
         const size_t row = (size_t)mt * kLM + rl;
         const bool live = row < g.n_out;
         const unsigned kmin = live ? (unsigned)__ldg(g.kmin + row) : 0u;
-        const int c0 = nt * kLN + 32 * th;
-        int ev[32];
-        int emn = 1 << 20, emx = -1;
-#pragma unroll
-        for (int j = 0; j < 32; j++) {
-          const int c = c0 + j;
-          const bool on = c < g.n_cols && __ldg(g.w.route + c) == kRouteGemm;
-          ev[j] = on ? __ldg(g.w.emin + c) : -1;
-          if (ev[j] >= 0) {
-            emn = min(emn, ev[j]);
-            emx = max(emx, ev[j]);
-          }
-        }
+        const int t0 = kEpt * tq, c0 = nt * N + t0;
         float *of = g.out_f32 ? g.out_f32 + (size_t)c0 * g.n_out + row : nullptr;
         long long *oq = g.out_q32 ? g.out_q32 + (size_t)c0 * g.n_out + row : nullptr;
+        // the tokens' exponents: when every live token's shift kmin + e lies in [32, 64) the
+        // loop has no call in it (the general case is out of line)
+        int emn = 1 << 20, emx = -1;
+#pragma unroll
+        for (int j = 0; j < kEpt; j++) {
+          const int e = tok_e[t0 + j];
+          if (e >= 0) {
+            emn = min(emn, e);
+            emx = max(emx, e);
+          }
+        }
         uint32_t bad = 0;  // bit j: token j's output leaves i64
         if (emx < 0 || ((int)kmin + emn >= 32 && (int)kmin + emx < 64)) {
+          // v = T·2^t, t = kmin + e − 32 in [0, 32), its f32 image RN(T)·2^(t − 32)
 #pragma unroll
-          for (int j = 0; j < 32; j++) {
-            const int e = ev[j];
-            const unsigned t = kmin + (unsigned)e - 32u;  // in [0, 32) for e >= 0
+          for (int j = 0; j < kEpt; j++) {
+            const int e = tok_e[t0 + j];
+            const unsigned t = kmin + (unsigned)e - 32u;
             const int hi = (int)(acc[j] >> 32);
-            const long long v = (long long)((unsigned long long)acc[j] << (t & 31));
-            const float f = __ll2float_rn(acc[j]) * __int_as_float((int)(t + 95) << 23);
             const bool fits = (hi >> (31 - (t & 31))) == (hi >> 31);
             if (e >= 0 && live) {
-              if (of) of[(size_t)j * g.n_out] = fits ? f : __int_as_float(0x7FC00000);
-              if (oq) oq[(size_t)j * g.n_out] = fits ? v : 0;
+              if (of)
+                *of = fits ? __ll2float_rn(acc[j]) * __int_as_float((int)(t + 95) << 23)
+                           : __int_as_float(0x7FC00000);
+              if (oq) *oq = fits ? (long long)((unsigned long long)acc[j] << (t & 31)) : 0;
             }
             bad |= (e >= 0 && live && !fits) ? 1u << j : 0u;
+            if (of) of += g.n_out;
+            if (oq) oq += g.n_out;
           }
         } else {
 #pragma unroll
-          for (int j = 0; j < 32; j++) {
-            const int e = ev[j];
+          for (int j = 0; j < kEpt; j++) {
+            const int e = tok_e[t0 + j];
+            if (e < 0 || !live) continue;
             long long v;
             float f;
             const bool fits = finish_fast(acc[j], kmin + (unsigned)e, v, f);
-            if (e >= 0 && live) {
-              if (of) of[(size_t)j * g.n_out] = fits ? f : __int_as_float(0x7FC00000);
-              if (oq) oq[(size_t)j * g.n_out] = fits ? v : 0;
-            }
-            bad |= (e >= 0 && live && !fits) ? 1u << j : 0u;
+            if (of) of[(size_t)j * g.n_out] = fits ? f : __int_as_float(0x7FC00000);
+            if (oq) oq[(size_t)j * g.n_out] = fits ? v : 0;
+            bad |= fits ? 0u : 1u << j;
           }
         }
         while (bad) {  // output overflow: rare, one refusal per token
@@ -889,7 +955,7 @@ __global__ void __launch_bounds__(kLThreads, 1)
           atomicMin(g.status + (size_t)(c0 + j) * 2, pack_status(row, kKindOutputOverflow, 0));
         }
       }
-      it += nk;
+      pi += nk;
     }
   }
   tc_fence_before();
@@ -902,6 +968,7 @@ __global__ void __launch_bounds__(kLThreads, 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512)
                  : "memory");
   }
+  lchecked_columns<T>(g);  // the routes and codes are the prep kernel's (read after its wait)
 }
 
 // ---- host side ---------------------------------------------------------------------------------
@@ -922,23 +989,28 @@ bool make_plane_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+template <int D, int N>
 size_t limb_smem_bytes() {
-  return 1024 + (size_t)kLStages * kLStageBytes + (2 * kLStages + 3) * 8 + 16;
+  return 1024 + (size_t)kLStages * LShape<D, N>::kStage + (2 * kLStages + 3) * 8 + 32 + N * 4;
 }
 
 long long family_top(uint32_t type) {
   return type == kQ8_0 ? Fam<kQ8_0>::top : type == kQ4_K ? Fam<kQ4_K>::top : Fam<kQ6_K>::top;
 }
 
-template <uint32_t T>
+// The token tile of a tensor with D weight digits: four accumulators of N = 128 tokens fill
+// TMEM; with five, 96 tokens.
+int tile_tokens(int digits) { return digits <= 3 ? 128 : 96; }
+
+template <uint32_t T, int D, int N>
 cudaError_t launch_main(const GemvPlan &pl, const uint8_t *pack, const LimbLayout &lay,
                         size_t n_out, size_t n_in, size_t n_cols, const int8_t *codes, size_t ld,
                         const uint8_t *exps, size_t ldb, const LWork &w, long long *out_q32,
                         float *out_f32, unsigned long long *status, int sm_count,
                         cudaStream_t stream) {
   CUtensorMap map_x;
-  const size_t np = lpad_cols(n_cols);
-  if (!make_plane_map(&map_x, w.xp, lay.kp, np, kXDig, kLN)) return cudaErrorInvalidValue;
+  const size_t np = lpad_n(n_cols, N);
+  if (!make_plane_map(&map_x, w.xp, lay.kp, np, kXDig, N)) return cudaErrorInvalidValue;
   LArgs a;
   a.kmin = lay.kmin;
   a.w = w;
@@ -948,33 +1020,53 @@ cudaError_t launch_main(const GemvPlan &pl, const uint8_t *pack, const LimbLayou
   a.n_out = n_out;
   a.n_cols = (int)n_cols;
   a.kstages = (int)(lay.kp / kLK);
-  a.n_tiles = (int)(np / kLN);
-  a.tiles = (int)ltiles(n_out, n_cols);
-  a.iters = (long long)a.tiles * a.kstages;
+  a.n_tiles = (int)(np / N);
+  a.tiles = (int)ltiles(n_out, n_cols, N);
+  const long long iters = (long long)a.tiles * a.kstages;
   a.G = (int)std::max<long long>(
-      1, std::min<long long>(sm_count, (a.iters + kLMinIters - 1) / kLMinIters));
+      1, std::min<long long>(sm_count, (iters + kLMinIters - 1) / kLMinIters));
+  // Waves keep each weight row tile's digits streaming from HBM once; digit planes that sit in
+  // L2 anyway (up to 64 MB) gain nothing from them, and an even split of all the work spares
+  // such a call a long tail of one extra short round.
+  const bool l2_resident = (size_t)D * lay.m_pad * lay.kp <= ((size_t)64 << 20);
+  a.waves = l2_resident ? 0 : a.tiles / a.G;
+  a.sk_iters = (long long)(a.tiles - a.waves * a.G) * a.kstages;
+  a.Gs = (int)std::min<long long>(a.G, (a.sk_iters + kLMinIters - 1) / kLMinIters);
   a.geo = PackGeo{pack, pl.units, pl.L};
   a.codes = codes;
   a.exps = exps;
   a.ld = ld;
   a.ldb = ldb;
   a.n_in = n_in;
-  cudaError_t e = cudaFuncSetAttribute(limb_gemm_kernel<T>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)limb_smem_bytes());
+  const size_t smem = limb_smem_bytes<D, N>();
+  cudaError_t e = cudaFuncSetAttribute(limb_gemm_kernel<T, D, N>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(a.G + kLFallbackCtas));
+  cfg.gridDim = dim3((unsigned)a.G);
   cfg.blockDim = dim3(kLThreads);
-  cfg.dynamicSmemBytes = limb_smem_bytes();
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, limb_gemm_kernel<T>,
+  return cudaLaunchKernelEx(&cfg, limb_gemm_kernel<T, D, N>,
                             *reinterpret_cast<const CUtensorMap *>(lay.map), map_x, a);
+}
+
+template <uint32_t T>
+cudaError_t launch_family(const GemvPlan &pl, const uint8_t *pack, const LimbLayout &lay,
+                          size_t n_out, size_t n_in, size_t n_cols, const int8_t *codes,
+                          size_t ld, const uint8_t *exps, size_t ldb, const LWork &w,
+                          long long *out_q32, float *out_f32, unsigned long long *status,
+                          int sm_count, cudaStream_t stream) {
+  if (lay.digits == 3)
+    return launch_main<T, 3, 128>(pl, pack, lay, n_out, n_in, n_cols, codes, ld, exps, ldb, w,
+                                  out_q32, out_f32, status, sm_count, stream);
+  return launch_main<T, 4, 96>(pl, pack, lay, n_out, n_in, n_cols, codes, ld, exps, ldb, w,
+                               out_q32, out_f32, status, sm_count, stream);
 }
 
 cudaError_t launch_main_any(uint32_t type, const GemvPlan &pl, const uint8_t *pack,
@@ -984,14 +1076,14 @@ cudaError_t launch_main_any(uint32_t type, const GemvPlan &pl, const uint8_t *pa
                             unsigned long long *status, int sm_count, cudaStream_t stream) {
   switch (type) {
     case kQ8_0:
-      return launch_main<kQ8_0>(pl, pack, lay, n_out, n_in, n_cols, codes, ld, exps, ldb, w,
-                                out_q32, out_f32, status, sm_count, stream);
+      return launch_family<kQ8_0>(pl, pack, lay, n_out, n_in, n_cols, codes, ld, exps, ldb, w,
+                                  out_q32, out_f32, status, sm_count, stream);
     case kQ4_K:
-      return launch_main<kQ4_K>(pl, pack, lay, n_out, n_in, n_cols, codes, ld, exps, ldb, w,
-                                out_q32, out_f32, status, sm_count, stream);
+      return launch_family<kQ4_K>(pl, pack, lay, n_out, n_in, n_cols, codes, ld, exps, ldb, w,
+                                  out_q32, out_f32, status, sm_count, stream);
     case kQ6_K:
-      return launch_main<kQ6_K>(pl, pack, lay, n_out, n_in, n_cols, codes, ld, exps, ldb, w,
-                                out_q32, out_f32, status, sm_count, stream);
+      return launch_family<kQ6_K>(pl, pack, lay, n_out, n_in, n_cols, codes, ld, exps, ldb, w,
+                                  out_q32, out_f32, status, sm_count, stream);
     default:
       return cudaErrorInvalidValue;
   }
@@ -999,16 +1091,29 @@ cudaError_t launch_main_any(uint32_t type, const GemvPlan &pl, const uint8_t *pa
 
 LPrepArgs prep_args(uint32_t type, const LimbLayout &lay, size_t n_out, size_t n_in,
                     size_t n_cols, const LWork &w, unsigned long long *status) {
+  const int nt = tile_tokens(lay.digits);
   LPrepArgs pa{};
   pa.n_in = n_in;
   pa.kp = lay.kp;
+  pa.np = lpad_n(n_cols, nt);
   pa.nb = (int)((n_in + 31) / 32);
   pa.n_cols = (int)n_cols;
-  pa.tiles = (int)ltiles(n_out, n_cols);
+  pa.tiles = (int)ltiles(n_out, n_cols, nt);
   pa.top = family_top(type);
   pa.w = w;
   pa.status = status;
   return pa;
+}
+
+// The prep kernels run right before the GEMM on the same SMs: giving them the GEMM's carveout
+// (the most shared memory) spares the SMs a reconfiguration between the two launches.
+bool set_prep_carveout() {
+  cudaFuncSetAttribute(limb_prep_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                       cudaSharedmemCarveoutMaxShared);
+  cudaFuncSetAttribute(limb_quant_prep_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                       cudaSharedmemCarveoutMaxShared);
+  cudaGetLastError();  // a hint: a refusal leaves the default
+  return true;
 }
 
 }  // namespace
@@ -1026,60 +1131,82 @@ cudaError_t build_limb_layout(const GemvPlan &pl, uint32_t type, const uint8_t *
   *lay = LimbLayout{};
   if (!limb_shape_ok(n_in) || n_out == 0 || (type != kQ8_0 && type != kQ4_K && type != kQ6_K))
     return cudaErrorInvalidValue;
-  lay->kp = lpad_k(n_in);
-  lay->m_pad = (n_out + kLM - 1) / kLM * kLM;
-  const size_t planes_bytes = (size_t)kWDig * lay->m_pad * lay->kp;
-  const size_t total = planes_bytes + lay->m_pad * 4 + 16;
-  cudaError_t e = cudaMalloc(&lay->base, total);
-  if (e != cudaSuccess) {
-    lay->base = nullptr;
-    return e;
-  }
-  lay->planes = reinterpret_cast<int8_t *>(lay->base);
-  lay->kmin = reinterpret_cast<int32_t *>(static_cast<uint8_t *>(lay->base) + planes_bytes);
-  int *bad = reinterpret_cast<int *>(lay->kmin + lay->m_pad);
-  e = cudaMemsetAsync(lay->kmin, 0, lay->m_pad * 4 + 16, stream);
+  const size_t kp = lpad_k(n_in), m_pad = (n_out + kLM - 1) / kLM * kLM;
+  // four planes first; a tensor whose weights all fit three digits then keeps three
+  const size_t plane = m_pad * kp;
+  void *base = nullptr;
+  cudaError_t e = cudaMalloc(&base, 4 * plane + m_pad * 4 + 16);
+  if (e != cudaSuccess) return e;
+  int8_t *planes = reinterpret_cast<int8_t *>(base);
+  int32_t *kmin = reinterpret_cast<int32_t *>(planes + 4 * plane);
+  int *flags = reinterpret_cast<int *>(kmin + m_pad);
+  e = cudaMemsetAsync(kmin, 0, m_pad * 4 + 16, stream);
   const PackGeo geo{pack, pl.units, pl.L};
-  const size_t items = lay->m_pad * (lay->kp / 32);
+  const size_t items = m_pad * (kp / 32);
   const unsigned rows_grid = (unsigned)((n_out + 7) / 8);
   const unsigned items_grid = (unsigned)((items + 127) / 128);
   if (e == cudaSuccess) {
     switch (type) {
       case kQ8_0:
-        limb_row_kmin<kQ8_0><<<rows_grid, 256, 0, stream>>>(geo, n_out, n_in, lay->kmin);
-        limb_build_planes<kQ8_0><<<items_grid, 128, 0, stream>>>(
-            geo, n_out, n_in, lay->m_pad, lay->kp, lay->kmin, lay->planes, bad);
+        limb_row_kmin<kQ8_0><<<rows_grid, 256, 0, stream>>>(geo, n_out, n_in, kmin);
+        limb_build_planes<kQ8_0><<<items_grid, 128, 0, stream>>>(geo, n_out, n_in, m_pad, kp,
+                                                                 kmin, planes, flags);
         break;
       case kQ4_K:
-        limb_row_kmin<kQ4_K><<<rows_grid, 256, 0, stream>>>(geo, n_out, n_in, lay->kmin);
-        limb_build_planes<kQ4_K><<<items_grid, 128, 0, stream>>>(
-            geo, n_out, n_in, lay->m_pad, lay->kp, lay->kmin, lay->planes, bad);
+        limb_row_kmin<kQ4_K><<<rows_grid, 256, 0, stream>>>(geo, n_out, n_in, kmin);
+        limb_build_planes<kQ4_K><<<items_grid, 128, 0, stream>>>(geo, n_out, n_in, m_pad, kp,
+                                                                 kmin, planes, flags);
         break;
       default:
-        limb_row_kmin<kQ6_K><<<rows_grid, 256, 0, stream>>>(geo, n_out, n_in, lay->kmin);
-        limb_build_planes<kQ6_K><<<items_grid, 128, 0, stream>>>(
-            geo, n_out, n_in, lay->m_pad, lay->kp, lay->kmin, lay->planes, bad);
+        limb_row_kmin<kQ6_K><<<rows_grid, 256, 0, stream>>>(geo, n_out, n_in, kmin);
+        limb_build_planes<kQ6_K><<<items_grid, 128, 0, stream>>>(geo, n_out, n_in, m_pad, kp,
+                                                                 kmin, planes, flags);
         break;
     }
     e = cudaGetLastError();
   }
-  int h = 1;
-  if (e == cudaSuccess) e = cudaMemcpyAsync(&h, bad, 4, cudaMemcpyDeviceToHost, stream);
+  int f = 1;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&f, flags, 4, cudaMemcpyDeviceToHost, stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
-  if (e == cudaSuccess &&
-      !make_plane_map(reinterpret_cast<CUtensorMap *>(lay->map), lay->planes, lay->kp,
-                      lay->m_pad, kWDig, kLM))
-    e = cudaErrorInvalidValue;
-  if (e != cudaSuccess) {
-    cudaFree(lay->base);
-    *lay = LimbLayout{};
+  if (e != cudaSuccess || (f & 1)) {  // a weight needs more than four digits: no digit planes
+    cudaFree(base);
     return e;
   }
-  lay->ok = h == 0;
-  if (!lay->ok) {  // some weight needs more than four digits: no digit planes for this tensor
-    cudaFree(lay->base);
-    *lay = LimbLayout{};
+  int digits = 4;
+  if (!(f & 2)) {  // every fourth digit is zero: keep planes 0..2 and kmin in a smaller buffer
+    void *b3 = nullptr;
+    if (cudaMalloc(&b3, 3 * plane + m_pad * 4 + 16) == cudaSuccess) {
+      e = cudaMemcpyAsync(b3, planes, 3 * plane, cudaMemcpyDeviceToDevice, stream);
+      if (e == cudaSuccess)
+        e = cudaMemcpyAsync(static_cast<int8_t *>(b3) + 3 * plane, kmin, m_pad * 4,
+                            cudaMemcpyDeviceToDevice, stream);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+      if (e != cudaSuccess) {
+        cudaFree(b3);
+        cudaFree(base);
+        return e;
+      }
+      cudaFree(base);
+      base = b3;
+      planes = static_cast<int8_t *>(b3);
+      kmin = reinterpret_cast<int32_t *>(planes + 3 * plane);
+      digits = 3;
+    } else {
+      cudaGetLastError();  // keep the four planes
+    }
   }
+  if (!make_plane_map(reinterpret_cast<CUtensorMap *>(lay->map), planes, kp, m_pad,
+                      (uint32_t)digits, kLM)) {
+    cudaFree(base);
+    return cudaErrorInvalidValue;
+  }
+  lay->base = base;
+  lay->planes = planes;
+  lay->kmin = kmin;
+  lay->kp = kp;
+  lay->m_pad = m_pad;
+  lay->digits = digits;
+  lay->ok = true;
   return cudaSuccess;
 }
 
@@ -1102,7 +1229,9 @@ cudaError_t launch_limb_gemm(const GemvPlan &pl, uint32_t type, const uint8_t *p
   pa.descs = static_cast<const ActDesc *>(descs);
   pa.ld = ld;
   pa.ldb = ldb;
-  limb_prep_kernel<<<(unsigned)lpad_cols(n_cols), 256, 0, stream>>>(pa);
+  static const bool carve = set_prep_carveout();
+  (void)carve;
+  limb_prep_kernel<<<(unsigned)pa.np, 256, 0, stream>>>(pa);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   return launch_main_any(type, pl, pack, lay, n_out, n_in, n_cols, codes, ld, exps, ldb, w,
@@ -1126,7 +1255,9 @@ cudaError_t launch_limb_gemm_f32(const GemvPlan &pl, uint32_t type, const uint8_
   pa.x = x;
   pa.ldx = ldx;
   const size_t smem = lay.kp + lay.kp / 32 + 16;
-  limb_quant_prep_kernel<<<(unsigned)lpad_cols(n_cols), 256, smem, stream>>>(pa);
+  static const bool carve = set_prep_carveout();
+  (void)carve;
+  limb_quant_prep_kernel<<<(unsigned)pa.np, 256, smem, stream>>>(pa);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   return launch_main_any(type, pl, pack, lay, n_out, n_in, n_cols, w.qcodes, lay.kp, w.qexps,

@@ -671,7 +671,8 @@ size_t apx_tensor_device_bytes(apx_ctx *ctx, uint64_t handle) {
   if (!t) return 0;
   // the repacked payload, plus the tensor-core views once a multi-column call has built them
   size_t n = t->pack_bytes;
-  if (t->limb.ok) n += 4 * t->limb.m_pad * t->limb.kp + 4 * t->limb.m_pad;
+  if (t->limb.ok)
+    n += (size_t)t->limb.digits * t->limb.m_pad * t->limb.kp + 4 * t->limb.m_pad;
   if (t->gemm.base)
     n += t->gemm.m_pad * t->gemm.kp + (size_t)t->gemm.nb_pad * t->gemm.m_pad * 4 + t->gemm.m_pad * 4;
   return n;

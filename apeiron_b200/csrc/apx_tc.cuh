@@ -74,6 +74,25 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
+// mbar_wait for waits that usually last microseconds (a whole tile's MMAs): a longer back-off
+// leaves the issue slots to the producer and MMA threads sharing the sub-partitions.  Bounded
+// like mbar_wait (about one second).
+__device__ __forceinline__ bool mbar_wait_long(uint64_t *bar, uint32_t parity) {
+  if (mbar_try(bar, parity)) return true;
+  unsigned long long t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (int it = 0; it < kWaitLimit; it++) {
+    __nanosleep(256);
+    if (mbar_try(bar, parity)) return true;
+    if ((it & 15) == 15) {
+      unsigned long long now;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+      if (now - t0 > 1000000000ull) return false;
+    }
+  }
+  return false;
+}
+
 // ---- TMEM loads (32 lanes × n columns of 32-bit words per warp) --------------------------------
 
 __device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&v)[16]) {
@@ -96,6 +115,16 @@ __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&v)[3
         "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
         "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]),
         "=r"(v[31])
+      : "r"(taddr));
+}
+
+// 8 columns into v[8h .. 8h + 7] (h a compile-time index after unrolling).
+template <int N>
+__device__ __forceinline__ void tmem_ld8_nowait(uint32_t taddr, uint32_t (&v)[N], int h) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+      : "=r"(v[8 * h + 0]), "=r"(v[8 * h + 1]), "=r"(v[8 * h + 2]), "=r"(v[8 * h + 3]),
+        "=r"(v[8 * h + 4]), "=r"(v[8 * h + 5]), "=r"(v[8 * h + 6]), "=r"(v[8 * h + 7])
       : "r"(taddr));
 }
 

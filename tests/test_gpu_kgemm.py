@@ -55,8 +55,10 @@ def device_bytes(be, t):
 
 
 def digit_plane_bytes(n_out, n_in):
+    """Device bytes a digit-plane view adds: three or four int8 planes (three when every scaled
+    weight of the tensor fits three digits) and one kmin word per row."""
     m_pad, kp = -(-n_out // 128) * 128, -(-n_in // 64) * 64
-    return 4 * m_pad * kp + 4 * m_pad
+    return {d * m_pad * kp + 4 * m_pad for d in (3, 4)}
 
 
 def check_matmat(be, t, raw, n_out, n_in, qs, threads=1, simd=False):
@@ -106,7 +108,7 @@ def test_digit_plane_gemm_equals_oracle(be, t, n_out, n_in, k):
     raw = synth.payload(t, n_out, n_in, 17 + n_out + t)
     qs = bench_columns(n_in, k, 400 + n_in)
     _, grown = run_and_check_route(be, t, raw, n_out, n_in, qs, threads=THREADS)
-    assert grown == digit_plane_bytes(n_out, n_in), "the call did not take the digit planes"
+    assert grown in digit_plane_bytes(n_out, n_in), "the call did not take the digit planes"
 
 
 @pytest.mark.parametrize("n_out,n_in", [(28672, 8192), (8192, 28672)])
@@ -117,7 +119,7 @@ def test_llama70b_ffn_prefill_512_tokens(be, n_out, n_in):
     raw = synth.payload(Q4_K, n_out, n_in, 70 + n_out)
     qs = bench_columns(n_in, 512, 9000)
     _, grown = run_and_check_route(be, Q4_K, raw, n_out, n_in, qs, threads=THREADS, simd=True)
-    assert grown == digit_plane_bytes(n_out, n_in)
+    assert grown in digit_plane_bytes(n_out, n_in)
 
 
 def test_kquant_mixed_routes(be):
@@ -170,7 +172,7 @@ def test_q8_0_wide_weight_spread_keeps_fold_gemm(be):
     raw = raw.reshape(-1)
     qs = bench_columns(n_in, k, 77)
     _, grown = run_and_check_route(be, Q8_0, raw, n_out, n_in, qs)
-    assert grown != digit_plane_bytes(n_out, n_in) and grown > 0
+    assert grown not in digit_plane_bytes(n_out, n_in) and grown > 0
 
 
 @pytest.mark.parametrize("t,n_out,n_in,k", [(Q4_K, 1536, 1536, 40), (Q6_K, 512, 1024, 9),
