@@ -44,7 +44,8 @@ EXPORTS = [
     "apx_matvec_f32_noalloc", "apx_matmat_f32", "apx_quant_f32_cols_async",
     "apx_peer_alloc", "apx_peer_open", "apx_peer_close", "apx_device_read",
     "apx_gather_publish_async", "apx_matvec_gather_async", "apx_matvec_group_async",
-    "apx_swiglu_quant_async", "apx_ffn_status_decode",
+    "apx_swiglu_quant_async", "apx_swiglu_quant_cols_async", "apx_act_describe_cols_async",
+    "apx_ffn_status_decode",
 ]
 CARRIER_F32, CARRIER_Q32 = 0, 1
 
@@ -130,6 +131,8 @@ _SIGS = {
     "apx_act_padded_len": (SZ, [SZ]),
     "apx_status_decode": (C.c_int, [P, U64, C.POINTER(CallStatus), EP]),
     "apx_swiglu_quant_async": (C.c_int, [P, P, P, SZ, C.c_int, P, P, P, P, P, P]),
+    "apx_swiglu_quant_cols_async": (C.c_int, [P, P, P, SZ, SZ, C.c_int, P, P, P, P, P, P]),
+    "apx_act_describe_cols_async": (C.c_int, [P, P, P, SZ, SZ, P, P]),
     "apx_ffn_status_decode": (C.c_int, [C.POINTER(CallStatus), EP]),
     "apx_matvec_f32_noalloc": (C.c_int, [P, U64, SZ, SZ, P, P, P, P]),
     "apx_matmat_f32": (C.c_int, [P, U64, SZ, SZ, SZ, P, P, EP]),

@@ -16,6 +16,7 @@
 // a small workspace and a one-CTA kernel merges them into the descriptor, so no state outlives
 // the call.  The lowest refusing lane reaches the status word by atomicMin (lane in the row
 // field), which is the reference's first-refusal order.
+#include <algorithm>
 #include <climits>
 
 #include "apx_common.cuh"
@@ -132,12 +133,14 @@ __device__ int swiglu_dev(long long gate, long long up, int carrier, long long &
 
 // ---- kernels -------------------------------------------------------------------------------
 
+// Column c (blockIdx.y) of a multi-column call: gate, up and h at c·ldg, codes at c·ldc, exponent
+// bytes at c·lde, the status word at status[2c], CTA statistics at part[c·gridDim.x + x].
 struct FfnArgs {
   const long long *gate, *up;
   long long *h;  // or null
   int8_t *codes;
   uint8_t *exps;
-  size_t n;
+  size_t n, ldg, ldc, lde;
   int carrier;
   int4 *part;                  // per CTA: emin, emax, status, nz
   unsigned long long *status;  // the first refusing lane
@@ -153,6 +156,15 @@ __global__ void __launch_bounds__(32 * kFfnWarps) swiglu_quant_kernel(FfnArgs a)
     s_nz = 0;
   }
   __syncthreads();
+  const size_t col = blockIdx.y;
+  if (col) {  // this CTA's column of a multi-column call
+    a.gate += col * a.ldg;
+    a.up += col * a.ldg;
+    if (a.h) a.h += col * a.ldg;
+    a.codes += col * a.ldc;
+    a.exps += col * a.lde;
+    a.status += col * 2;
+  }
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const size_t nb = (a.n + 31) / 32;
   const size_t b = (size_t)blockIdx.x * kFfnWarps + warp;
@@ -202,12 +214,15 @@ __global__ void __launch_bounds__(32 * kFfnWarps) swiglu_quant_kernel(FfnArgs a)
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) a.part[blockIdx.x] = make_int4(s_emin, s_emax, s_status, (int)s_nz);
+  if (threadIdx.x == 0)
+    a.part[col * gridDim.x + blockIdx.x] = make_int4(s_emin, s_emax, s_status, (int)s_nz);
 }
 
-// The descriptor from the CTAs' statistics (one CTA).
+// The descriptor from the CTAs' statistics (one CTA per column).
 __global__ void __launch_bounds__(256) ffn_desc_kernel(const int4 *part, int nparts, size_t n,
                                                        ActDesc *desc) {
+  part += (size_t)blockIdx.x * nparts;
+  desc += blockIdx.x;
   int emin = 1 << 30, emax = -1, status = APX_OK;
   unsigned nz = 0;
   for (int i = threadIdx.x; i < nparts; i += blockDim.x) {
@@ -248,14 +263,23 @@ __global__ void __launch_bounds__(256) ffn_desc_kernel(const int4 *part, int npa
   }
 }
 
-size_t swiglu_work_bytes(size_t n) {
-  return ((n + 31) / 32 + kFfnWarps - 1) / kFfnWarps * sizeof(int4);
+size_t swiglu_work_bytes(size_t n, size_t cols) {
+  return ((n + 31) / 32 + kFfnWarps - 1) / kFfnWarps * sizeof(int4) * std::max<size_t>(cols, 1);
 }
 
 cudaError_t launch_swiglu_quant(const long long *gate, const long long *up, size_t n, int carrier,
                                 long long *h, int8_t *codes, uint8_t *exps, void *desc,
                                 unsigned long long *status, void *work, cudaStream_t stream) {
-  if (n == 0) return cudaSuccess;
+  return launch_swiglu_quant_cols(gate, up, n, 1, 0, carrier, h, codes, 0, exps, 0, desc, status,
+                                  work, stream);
+}
+
+cudaError_t launch_swiglu_quant_cols(const long long *gate, const long long *up, size_t n,
+                                     size_t cols, size_t ldg, int carrier, long long *h,
+                                     int8_t *codes, size_t ldc, uint8_t *exps, size_t lde,
+                                     void *desc, unsigned long long *status, void *work,
+                                     cudaStream_t stream) {
+  if (n == 0 || cols == 0) return cudaSuccess;
   const size_t nb = (n + 31) / 32;
   const unsigned grid = (unsigned)((nb + kFfnWarps - 1) / kFfnWarps);
   FfnArgs a;
@@ -265,13 +289,17 @@ cudaError_t launch_swiglu_quant(const long long *gate, const long long *up, size
   a.codes = codes;
   a.exps = exps;
   a.n = n;
+  a.ldg = ldg;
+  a.ldc = ldc;
+  a.lde = lde;
   a.carrier = carrier;
   a.part = static_cast<int4 *>(work);
   a.status = status;
-  swiglu_quant_kernel<<<grid, 32 * kFfnWarps, 0, stream>>>(a);
+  swiglu_quant_kernel<<<dim3(grid, (unsigned)cols), 32 * kFfnWarps, 0, stream>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  ffn_desc_kernel<<<1, 256, 0, stream>>>(a.part, (int)grid, n, static_cast<ActDesc *>(desc));
+  ffn_desc_kernel<<<(unsigned)cols, 256, 0, stream>>>(a.part, (int)grid, n,
+                                                        static_cast<ActDesc *>(desc));
   return cudaGetLastError();
 }
 

@@ -127,6 +127,7 @@ struct LimbLayout {
   int32_t *kmin = nullptr;   // [m_pad]
   size_t kp = 0, m_pad = 0;
   int digits = 0;  // 3 when every weight fits three digits, else 4
+  int wbits = 0;   // bit length of the largest |W'|
   bool ok = false;
   alignas(64) unsigned char map[128];  // the digits, 64-byte boxes × 128 rows × `digits` planes
 };
@@ -154,10 +155,17 @@ cudaError_t launch_limb_gemm_f32(const GemvPlan &pl, uint32_t type, const uint8_
 
 // The FFN hidden activation (apx_ffn.cu): SwiGLU under the carrier, then quant_act; `work` holds
 // swiglu_work_bytes(n).
-size_t swiglu_work_bytes(size_t n);
+size_t swiglu_work_bytes(size_t n, size_t cols = 1);
 cudaError_t launch_swiglu_quant(const long long *gate, const long long *up, size_t n, int carrier,
                                 long long *h, int8_t *codes, uint8_t *exps, void *desc,
                                 unsigned long long *status, void *work, cudaStream_t stream);
+// `cols` columns in one launch: gate/up/h of column c at c·ldg, codes at c·ldc, exponent bytes at
+// c·lde, descriptor desc[c], status word at status[2c]; `work` holds swiglu_work_bytes(n, cols).
+cudaError_t launch_swiglu_quant_cols(const long long *gate, const long long *up, size_t n,
+                                     size_t cols, size_t ldg, int carrier, long long *h,
+                                     int8_t *codes, size_t ldc, uint8_t *exps, size_t lde,
+                                     void *desc, unsigned long long *status, void *work,
+                                     cudaStream_t stream);
 
 // GEMV launches from the calling thread go without programmatic dependent launch while set.
 void set_pdl_suppressed(bool on);

@@ -65,15 +65,19 @@ namespace {
 constexpr int kLM = 128;        // weight rows per tile (MMA M)
 constexpr int kLK = 64;         // K bytes per stage: two 32-lane blocks, one 64-byte swizzle row
 constexpr int kLStages = 5;
-constexpr int kXDig = 2;        // activation digits
+constexpr int kXDig = 2;        // activation digits per pass over K
+constexpr int kXPlanes = 3;     // activation digit planes written (the third for a second pass)
 constexpr int kLEpiWarps = 16;  // 4 per TMEM lane quarter: 32 rows × N/4 tokens each
 constexpr int kLThreads = 32 * (2 + kLEpiWarps);
 constexpr int kLMaxShift = 7;   // X' = x·2^s with |x| <= 128 stays within two digits
+constexpr int kLMaxShift3 = 15; // ... and within three
 constexpr size_t kLMaxK = 65536;
 constexpr int kLTileW = kLM * kLK;  // 8 KB: one weight digit tile
 constexpr int kLNMin = 64, kLNMax = 128;  // token tile widths (workspace bounds)
 constexpr int kLMinIters = 4;       // stages per stream-K CTA at least
-constexpr unsigned kRouteNone = 0, kRouteGemm = 1, kRouteChecked = 2;
+// A column's route: refused, the GEMM with two activation digits, the checked rows, or the GEMM
+// with three (a tile holding such a column runs a second pass over K for the third digit).
+constexpr unsigned kRouteNone = 0, kRouteGemm = 1, kRouteChecked = 2, kRouteGemm3 = 3;
 constexpr long long kPartSlot = (long long)kLM * kLNMax;  // i64 per partial tile
 
 // The kernel's shape for D weight digits and N-token tiles.
@@ -173,9 +177,9 @@ __global__ void limb_row_kmin(PackGeo geo, size_t n_out, size_t n_in, int32_t *k
   if (lane == 0) kmin[row] = lo == (1 << 30) ? 0 : lo;
 }
 
-// W'[row, 32g .. 32g+31] (zero past n_in and n_out) as four digit planes; bit 0 of *flags where
-// a value needs more than four digits, bit 1 where one needs the fourth.  One thread per (row,
-// 32-lane group).
+// W'[row, 32g .. 32g+31] (zero past n_in and n_out) as four digit planes; bit 0 of flags[0] where
+// a value needs more than four digits, bit 1 where one needs the fourth; flags[1] the largest bit
+// length of |W'|.  One thread per (row, 32-lane group).
 template <uint32_t T>
 __global__ void limb_build_planes(PackGeo geo, size_t n_out, size_t n_in, size_t m_pad, size_t kp,
                                   const int32_t *kmin, int8_t *planes, int *flags) {
@@ -189,6 +193,7 @@ __global__ void limb_build_planes(PackGeo geo, size_t n_out, size_t n_in, size_t
 #pragma unroll
     for (int q = 0; q < 8; q++) pl[j][q] = 0;
   bool ok = true, need4 = false;
+  int wb = 0;  // bit length of the largest |W'|
   if (row < n_out && g * 32 < n_in) {
     const int km = kmin[row];
     long long w[32];
@@ -260,12 +265,15 @@ __global__ void limb_build_planes(PackGeo geo, size_t n_out, size_t n_in, size_t
       if (g * 32 + t >= n_in) w[t] = 0;
       ok = digits4(w[t], d) && ok;
       need4 = need4 || (d >> 24) != 0;
+      const unsigned long long mag = w[t] < 0 ? 0ull - (unsigned long long)w[t] : (unsigned long long)w[t];
+      wb = max(wb, mag ? 64 - __clzll((long long)mag) : 0);
 #pragma unroll
       for (int j = 0; j < 4; j++) pl[j][t / 4] |= ((d >> (8 * j)) & 0xFFu) << (8 * (t % 4));
     }
   }
   const int f = (ok ? 0 : 1) | (need4 ? 2 : 0);
   if (f) atomicOr(flags, f);
+  if (wb) atomicMax(flags + 1, wb);
 #pragma unroll
   for (int j = 0; j < 4; j++) {
     uint4 *dst = reinterpret_cast<uint4 *>(planes + ((size_t)j * m_pad + row) * kp + g * 32);
@@ -278,13 +286,13 @@ __global__ void limb_build_planes(PackGeo geo, size_t n_out, size_t n_in, size_t
 
 // Nothing in it outlives a call: the prep kernel zeroes the tile counters and writes every
 // column's route, emin and digits before the GEMM reads them.  Regions are sized for the
-// narrowest token tile (most tiles) and the widest (most padding columns).
+// narrowest token tile (most tiles) and the most padding columns any tile width gives.
 struct LWork {
   int *cnt;          // [tiles] arrivals of the tiles split between CTAs (zeroed by the prep)
   long long *part;   // [2·sm_count][kPartSlot] partial sums of split tiles
   uint32_t *route;   // [n_pad]: refused / GEMM / checked rows
   int32_t *emin;     // [n_pad]
-  int8_t *xp;        // [2][n_pad][kp]: the activation digits (zero off the GEMM)
+  int8_t *xp;        // [3][n_pad][kp]: the activation digits (zero off the GEMM)
   int8_t *qcodes;    // f32 path: the checked columns' codes [n_pad][kp]
   uint8_t *qexps;    // and exponent bytes [n_pad][kp / 32]
 };
@@ -296,15 +304,19 @@ size_t ltiles(size_t n_out, size_t n_cols, int nt) {
 }
 size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
 
+// Columns padded to the widest any token tile pads them (96 or 128 tokens).
+size_t lpad_max(size_t n_cols) { return std::max(lpad_n(n_cols, 96), lpad_n(n_cols, 128)); }
+
 size_t lwork_bytes(size_t n_cols, size_t n_in, size_t n_out, int sm_count) {
-  const size_t np = lpad_n(n_cols, kLNMax), kp = lpad_k(n_in);
+  const size_t np = lpad_max(n_cols), kp = lpad_k(n_in);
   const size_t tiles = ltiles(n_out, n_cols, kLNMin);
   return align256(tiles * 4) + align256((size_t)2 * std::max(sm_count, 1) * kPartSlot * 8) +
-         align256(np * 4) * 2 + 2 * np * kp + align256(np * kp) + align256(np * (kp / 32)) + 256;
+         align256(np * 4) * 2 + kXPlanes * np * kp + align256(np * kp) + align256(np * (kp / 32)) +
+         256;
 }
 
 LWork lwork_view(void *base, size_t n_cols, size_t n_in, size_t n_out, int sm_count) {
-  const size_t np = lpad_n(n_cols, kLNMax), kp = lpad_k(n_in);
+  const size_t np = lpad_max(n_cols), kp = lpad_k(n_in);
   const size_t tiles = ltiles(n_out, n_cols, kLNMin);
   uint8_t *p = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(base) + 255) & ~(uintptr_t)255);
@@ -318,7 +330,7 @@ LWork lwork_view(void *base, size_t n_cols, size_t n_in, size_t n_out, int sm_co
   w.emin = reinterpret_cast<int32_t *>(p);
   p += align256(np * 4);
   w.xp = reinterpret_cast<int8_t *>(p);
-  p += 2 * np * kp;
+  p += kXPlanes * np * kp;
   w.qcodes = reinterpret_cast<int8_t *>(p);
   p += align256(np * kp);
   w.qexps = p;
@@ -327,26 +339,40 @@ LWork lwork_view(void *base, size_t n_cols, size_t n_in, size_t n_out, int sm_co
 
 // ---- activation prep: routes and digit planes --------------------------------------------------
 
-// 16 codes of one 32-lane block times 2^s as balanced base-256 digits (|x·2^s| <= 2^14).
-__device__ __forceinline__ void x_digits16(uint4 v, int s, uint4 &lo, uint4 &hi) {
+// 16 codes of one 32-lane block times 2^s (s <= 15: |x·2^s| <= 2^22) as three balanced base-256
+// digits; the third is zero for s <= 7.
+__device__ __forceinline__ void x_digits16(uint4 v, int s, uint4 &lo, uint4 &mid, uint4 &hi) {
   const uint32_t in[4] = {v.x, v.y, v.z, v.w};
-  uint32_t o0[4], o1[4];
+  uint32_t o0[4], o1[4], o2[4];
 #pragma unroll
   for (int q = 0; q < 4; q++) {
-    uint32_t a = 0, b = 0;
+    uint32_t a = 0, b = 0, c = 0;
 #pragma unroll
     for (int t = 0; t < 4; t++) {
       const int x = (int)(signed char)((in[q] >> (8 * t)) & 0xFFu) * (1 << s);
       const int d0 = (signed char)(x & 0xFF);
-      const int d1 = (x - d0) >> 8;
+      const int r1 = (x - d0) >> 8;
+      const int d1 = (signed char)(r1 & 0xFF);
+      const int d2 = (r1 - d1) >> 8;
       a |= ((uint32_t)d0 & 0xFFu) << (8 * t);
       b |= ((uint32_t)d1 & 0xFFu) << (8 * t);
+      c |= ((uint32_t)d2 & 0xFFu) << (8 * t);
     }
     o0[q] = a;
     o1[q] = b;
+    o2[q] = c;
   }
   lo = make_uint4(o0[0], o0[1], o0[2], o0[3]);
-  hi = make_uint4(o1[0], o1[1], o1[2], o1[3]);
+  mid = make_uint4(o1[0], o1[1], o1[2], o1[3]);
+  hi = make_uint4(o2[0], o2[1], o2[2], o2[3]);
+}
+
+// The three digit planes' 16 bytes of column c at element j.
+__device__ __forceinline__ void store_xdigits(int8_t *xp, size_t np, size_t kp, int c, size_t j,
+                                              uint4 d0, uint4 d1, uint4 d2) {
+  *reinterpret_cast<uint4 *>(xp + (size_t)c * kp + j) = d0;
+  *reinterpret_cast<uint4 *>(xp + (np + c) * kp + j) = d1;
+  *reinterpret_cast<uint4 *>(xp + (2 * np + c) * kp + j) = d2;
 }
 
 struct LPrepArgs {
@@ -358,15 +384,15 @@ struct LPrepArgs {
   size_t np;  // columns padded to the GEMM's token tile: the digit planes' rows
   int nb, n_cols, tiles;
   long long top;  // the family's call-bound constant (chart/mod.rs:1697-1706)
+  int smax3;      // the largest activation spread of the three-digit route on this tensor
   LWork w;
   unsigned long long *status;  // column c's refusal word at status[c·2]
 };
 
 __device__ __forceinline__ void lzero_column(const LPrepArgs &a, int c, size_t np) {
-  for (size_t j = (size_t)threadIdx.x * 16; j < a.kp; j += (size_t)blockDim.x * 16) {
-    *reinterpret_cast<uint4 *>(a.w.xp + (size_t)c * a.kp + j) = make_uint4(0, 0, 0, 0);
-    *reinterpret_cast<uint4 *>(a.w.xp + (np + c) * a.kp + j) = make_uint4(0, 0, 0, 0);
-  }
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  for (size_t j = (size_t)threadIdx.x * 16; j < a.kp; j += (size_t)blockDim.x * 16)
+    store_xdigits(a.w.xp, np, a.kp, c, j, z, z, z);
 }
 
 __device__ __forceinline__ void lprep_common_start(const LPrepArgs &a) {
@@ -375,13 +401,16 @@ __device__ __forceinline__ void lprep_common_start(const LPrepArgs &a) {
     for (int i = threadIdx.x; i < a.tiles; i += blockDim.x) a.w.cnt[i] = 0;
 }
 
-// Route of a described column: GEMM when the reference's call bound holds and the activation
-// spread fits two digits; otherwise the checked rows (the GEMM's extra CTAs find the column by
-// its route).
+// Route of a described column: the GEMM when the reference's call bound holds and the activation
+// spread fits two digits (three up to the tensor's smax3); otherwise the checked rows (the GEMM's
+// CTAs find the column by its route).
 __device__ __forceinline__ unsigned lroute(const LPrepArgs &a, int emin, int emax) {
-  return bound_ok((long long)a.n_in, a.top, emax) && (emax < 0 || emax - emin <= kLMaxShift)
-             ? kRouteGemm
-             : kRouteChecked;
+  if (!bound_ok((long long)a.n_in, a.top, emax)) return kRouteChecked;
+  if (emax < 0 || emax - emin <= kLMaxShift) return kRouteGemm;
+  return emax - emin <= a.smax3 ? kRouteGemm3 : kRouteChecked;
+}
+__device__ __forceinline__ bool on_gemm(unsigned route) {
+  return route == kRouteGemm || route == kRouteGemm3;
 }
 
 // One CTA per column (padding columns of the last tile included): describe (unless the
@@ -450,10 +479,10 @@ __global__ void __launch_bounds__(256) limb_prep_kernel(LPrepArgs a) {
     a.w.route[c] = route;
   }
   __syncthreads();
-  const bool gemm = s_route == kRouteGemm;
+  const bool gemm = on_gemm(s_route);
   const int emin = s_emin;
   for (size_t j = (size_t)threadIdx.x * 16; j < a.kp; j += (size_t)blockDim.x * 16) {
-    uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
+    uint4 lo = make_uint4(0, 0, 0, 0), mid = lo, hi = lo;
     if (gemm && j < a.n_in) {
       const unsigned e = exps[j / 32];
       if (e != APX_EXP_ZERO) {
@@ -465,11 +494,10 @@ __global__ void __launch_bounds__(256) limb_prep_kernel(LPrepArgs a) {
           for (int i = 0; i < 16; i++) t[i] = j + i < a.n_in ? (uint8_t)codes[j + i] : 0;
           memcpy(&v, t, 16);
         }
-        x_digits16(v, (int)e - emin, lo, hi);
+        x_digits16(v, (int)e - emin, lo, mid, hi);
       }
     }
-    *reinterpret_cast<uint4 *>(a.w.xp + (size_t)c * a.kp + j) = lo;
-    *reinterpret_cast<uint4 *>(a.w.xp + (np + c) * a.kp + j) = hi;
+    store_xdigits(a.w.xp, np, a.kp, c, j, lo, mid, hi);
   }
 }
 
@@ -577,7 +605,7 @@ __global__ void __launch_bounds__(256) limb_quant_prep_kernel(LPrepArgs a) {
     a.w.route[c] = route;
   }
   __syncthreads();
-  const bool gemm = s_route == kRouteGemm;
+  const bool gemm = on_gemm(s_route);
   const int emin = s_emin;
   if (!gemm) {  // the checked rows read the column from global memory
     for (size_t j = (size_t)threadIdx.x * 16; j < a.kp; j += (size_t)blockDim.x * 16)
@@ -587,12 +615,11 @@ __global__ void __launch_bounds__(256) limb_quant_prep_kernel(LPrepArgs a) {
       a.w.qexps[(size_t)c * (a.kp / 32) + b] = sexps[b];
   }
   for (size_t j = (size_t)threadIdx.x * 16; j < a.kp; j += (size_t)blockDim.x * 16) {
-    uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
+    uint4 lo = make_uint4(0, 0, 0, 0), mid = lo, hi = lo;
     const unsigned e = sexps[j / 32];
     if (gemm && e != APX_EXP_ZERO)
-      x_digits16(*reinterpret_cast<const uint4 *>(scodes + j), (int)e - emin, lo, hi);
-    *reinterpret_cast<uint4 *>(a.w.xp + (size_t)c * a.kp + j) = lo;
-    *reinterpret_cast<uint4 *>(a.w.xp + (np + c) * a.kp + j) = hi;
+      x_digits16(*reinterpret_cast<const uint4 *>(scodes + j), (int)e - emin, lo, mid, hi);
+    store_xdigits(a.w.xp, np, a.kp, c, j, lo, mid, hi);
   }
 }
 
@@ -656,7 +683,7 @@ __device__ __forceinline__ void lchecked_columns(const LArgs &g) {
     if (threadIdx.x == 0) s_n = 0;
     __syncthreads();
     const int c = base + (int)threadIdx.x;
-    if (c < g.n_cols && __ldg(g.w.route + c) == kRouteChecked) s_cols[atomicAdd(&s_n, 1)] = c;
+    if (c < g.n_cols && __ldcg(g.w.route + c) == kRouteChecked) s_cols[atomicAdd(&s_n, 1)] = c;
     __syncthreads();
     for (int i = 0; i < s_n; i++) {
       const int cc = s_cols[i];
@@ -722,96 +749,133 @@ __global__ void __launch_bounds__(kLThreads, 1)
   auto stage_w = [&](int st) { return smem + st * kStage; };
   auto stage_x = [&](int st) { return smem + st * kStage + D * kLTileW; };
   // The weight digits are the tensor's, constant since the layout was built: the first stages'
-  // loads of them go out before the wait for the prep kernel (programmatic dependent launch).
-  // Everything the prep kernel writes is read after the wait.
-  const int pre = min(nit, kLStages);
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < pre; i++) {
-      int tile, ks;
-      lat(g, b, s0, i, tile, ks);
-      mbar_expect_tx(full + i, kStage);
-      tma_load_3d(stage_w(i), &map_w, ks * kLK, (tile / g.n_tiles) * kLM, 0, full + i);
-    }
+  // loads of them (the first piece's first pass) go out before the wait for the prep kernel
+  // (programmatic dependent launch).  Everything the prep kernel writes is read after the wait.
+  int pre;
+  {
+    int tile0, ks00;
+    lat(g, b, s0, 0, tile0, ks00);
+    pre = nit > 0 ? min(min(g.kstages - ks00, nit), kLStages) : 0;
+    if (threadIdx.x == 0)
+      for (int i = 0; i < pre; i++) {
+        mbar_expect_tx(full + i, kStage);
+        tma_load_3d(stage_w(i), &map_w, (ks00 + i) * kLK, (tile0 / g.n_tiles) * kLM, 0,
+                    full + i);
+      }
   }
   pdl_wait();
+  // Whether token tile nt holds a column of the three-digit route (a second pass over K for the
+  // third activation digit), read by a whole warp: the same answer in every role.
+  auto needs3 = [&](int nt) {
+    bool any = false;
+    for (int t = lane; t < N; t += 32) {
+      const int c = nt * N + t;
+      any = any || (c < g.n_cols && __ldcg(g.w.route + c) == kRouteGemm3);
+    }
+    return __any_sync(0xFFFFFFFFu, any);
+  };
 
   if (warp == 0) {
-    // ---- TMA producer (lane 0): per stage the D weight digit tiles and the 2 activation ones
-    int issued = 0;
-    for (int i = 0; i < nit; i++) {
-      int tile, ks;
-      lat(g, b, s0, i, tile, ks);
-      const int st = i % kLStages, use = i / kLStages;
-      int stop = 0;
-      if (lane == 0) {
-        if (use > 0 && !mbar_wait(empty + st, (use - 1) & 1)) {
-          atomicExch(timeout, 1);
-          stop = 1;
-        } else {
-          if (i >= pre) {
-            mbar_expect_tx(full + st, kStage);
-            tma_load_3d(stage_w(st), &map_w, ks * kLK, (tile / g.n_tiles) * kLM, 0, full + st);
+    // ---- TMA producer (lane 0): per stage the D weight digit tiles and 2 activation digit tiles
+    // (digits 0 and 1 on a piece's first pass; digit 2 and a zero plane on its second) ----
+    int i = 0, issued = 0;
+    bool stop = false;
+    for (int pi = 0; !stop && pi < nit;) {
+      int tile, ks0;
+      lat(g, b, s0, pi, tile, ks0);
+      const int nk = min(g.kstages - ks0, nit - pi);
+      const int passes = needs3(tile % g.n_tiles) ? 2 : 1;
+      for (int pass = 0; !stop && pass < passes; pass++) {
+        for (int k = 0; k < nk; k++, i++) {
+          const int st = i % kLStages, use = i / kLStages;
+          int bad = 0;
+          if (lane == 0) {
+            if (use > 0 && !mbar_wait(empty + st, (use - 1) & 1)) {
+              atomicExch(timeout, 1);
+              bad = 1;
+            } else {
+              if (i >= pre) {
+                mbar_expect_tx(full + st, kStage);
+                tma_load_3d(stage_w(st), &map_w, (ks0 + k) * kLK, (tile / g.n_tiles) * kLM, 0,
+                            full + st);
+              }
+              tma_load_3d(stage_x(st), &map_x, (ks0 + k) * kLK, (tile % g.n_tiles) * N,
+                          pass == 0 ? 0 : 2, full + st);
+              issued = i + 1;
+            }
           }
-          tma_load_3d(stage_x(st), &map_x, ks * kLK, (tile % g.n_tiles) * N, 0, full + st);
-          issued++;
+          if (__shfl_sync(0xFFFFFFFFu, bad, 0)) {
+            stop = true;
+            break;
+          }
         }
       }
-      if (__shfl_sync(0xFFFFFFFFu, stop, 0)) break;
+      pi += nk;
     }
     // every copy this thread started has landed before the CTA may exit
     if (lane == 0) {
       const int last = max(issued, pre);
-      for (int i = last > kLStages ? last - kLStages : 0; i < last; i++)
-        mbar_wait(full + i % kLStages, (i / kLStages) & 1);
+      for (int j = last > kLStages ? last - kLStages : 0; j < last; j++)
+        mbar_wait(full + j % kLStages, (j / kLStages) & 1);
     }
   } else if (warp == 1) {
-    // ---- MMA issuer (lane 0): 2·D MMAs per 32-lane block, one commit per stage (frees it) and
-    // one per tile piece (its accumulators are complete).  Accumulator p takes the pairs
-    // (p, 0) and (p − 1, 1); the first of them on a piece's first block overwrites it. ----
-    if (lane == 0) {
-      const uint64_t w0 = kLDescHi | (smem_addr(stage_w(0)) >> 4);
-      const uint64_t x0 = kLDescHi | (smem_addr(stage_x(0)) >> 4);
-      bool ok = true;
-      int i = 0, piece = 0;
-      for (int pi = 0; ok && pi < nit; piece++) {
-        int tile, ks0;
-        lat(g, b, s0, pi, tile, ks0);
-        const int nk = min(g.kstages - ks0, nit - pi);
-        if (piece > 0 && !mbar_wait(tempty, (piece - 1) & 1)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        for (int k = 0; k < nk; k++, i++) {
-          const int st = i % kLStages;
-          if (!mbar_wait(full + st, (i / kLStages) & 1)) {
-            ok = false;
-            break;
-          }
+    // ---- MMA issuer (lane 0): a piece's first pass takes 2·D MMAs per 32-lane block into D + 1
+    // accumulators (accumulator p the pairs (p, 0) and (p − 1, 1)); a second pass, for a tile with
+    // a three-digit column, D MMAs (weight digit p against activation digit 2 into accumulator
+    // p).  One commit per stage (frees it) and one per pass (its accumulators are complete). ----
+    const uint64_t w0 = kLDescHi | (smem_addr(stage_w(0)) >> 4);
+    const uint64_t x0 = kLDescHi | (smem_addr(stage_x(0)) >> 4);
+    int ok = 1;
+    int i = 0, npass = 0;
+    for (int pi = 0; ok && pi < nit;) {
+      int tile, ks0;
+      lat(g, b, s0, pi, tile, ks0);
+      const int nk = min(g.kstages - ks0, nit - pi);
+      const int passes = needs3(tile % g.n_tiles) ? 2 : 1;
+      for (int pass = 0; ok && pass < passes; pass++, npass++) {
+        if (lane == 0) {
+          if (npass > 0 && !mbar_wait(tempty, (npass - 1) & 1)) ok = 0;
           tc_fence_after();
-          const uint64_t wd = w0 + (uint64_t)(st * (kStage >> 4));
-          const uint64_t xd = x0 + (uint64_t)(st * (kStage >> 4));
-#pragma unroll
-          for (int q = 0; q < kLK / 32; q++) {
-            const bool first = k == 0 && q == 0;
-#pragma unroll
-            for (int p = 0; p < kAcc; p++) {
-              const uint32_t acc = tmem + (uint32_t)(p * N);
-              if (p < D)  // (p, 0)
-                mma_i8(acc, wd + (uint64_t)(p * (kLTileW >> 4) + 2 * q),
-                       xd + (uint64_t)(2 * q), S::kIdesc, first ? 0u : 1u);
-              if (p >= 1)  // (p − 1, 1)
-                mma_i8(acc, wd + (uint64_t)((p - 1) * (kLTileW >> 4) + 2 * q),
-                       xd + (uint64_t)((S::kTileX >> 4) + 2 * q), S::kIdesc,
-                       (first && p == D) ? 0u : 1u);
+          for (int k = 0; ok && k < nk; k++, i++) {
+            const int st = i % kLStages;
+            if (!mbar_wait(full + st, (i / kLStages) & 1)) {
+              ok = 0;
+              break;
             }
+            tc_fence_after();
+            const uint64_t wd = w0 + (uint64_t)(st * (kStage >> 4));
+            const uint64_t xd = x0 + (uint64_t)(st * (kStage >> 4));
+#pragma unroll
+            for (int q = 0; q < kLK / 32; q++) {
+              const bool first = k == 0 && q == 0;
+              if (pass == 0) {
+#pragma unroll
+                for (int p = 0; p < kAcc; p++) {
+                  const uint32_t acc = tmem + (uint32_t)(p * N);
+                  if (p < D)  // (p, 0)
+                    mma_i8(acc, wd + (uint64_t)(p * (kLTileW >> 4) + 2 * q),
+                           xd + (uint64_t)(2 * q), S::kIdesc, first ? 0u : 1u);
+                  if (p >= 1)  // (p − 1, 1)
+                    mma_i8(acc, wd + (uint64_t)((p - 1) * (kLTileW >> 4) + 2 * q),
+                           xd + (uint64_t)((S::kTileX >> 4) + 2 * q), S::kIdesc,
+                           (first && p == D) ? 0u : 1u);
+                }
+              } else {
+#pragma unroll
+                for (int p = 0; p < D; p++)  // (p, 2): the stage's first activation tile
+                  mma_i8(tmem + (uint32_t)(p * N), wd + (uint64_t)(p * (kLTileW >> 4) + 2 * q),
+                         xd + (uint64_t)(2 * q), S::kIdesc, first ? 0u : 1u);
+              }
+            }
+            mma_commit(empty + st);
           }
-          mma_commit(empty + st);
+          if (ok) mma_commit(tfull);
         }
-        if (!ok) break;
-        mma_commit(tfull);
-        pi += nk;
+        ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
       }
+      pi += nk;
+    }
+    if (lane == 0) {
       if (!ok) atomicExch(timeout, 1);
       mma_commit(mdone);
       if (!mbar_wait(mdone, 0)) atomicExch(timeout, 1);
@@ -823,46 +887,75 @@ __global__ void __launch_bounds__(kLThreads, 1)
     const int tq = ew / 4;    // token quarter
     const int rl = 32 * lq + lane;
     const uint32_t trow = tmem + ((uint32_t)(32 * lq) << 16) + (uint32_t)(kEpt * tq);
-    int piece = 0;
-    for (int pi = 0; pi < nit; piece++) {
+    constexpr int kChunk = kEpt % 16 == 0 ? 16 : 8;
+    int npass = 0;
+    bool failed = false;
+    for (int pi = 0; !failed && pi < nit;) {
       int tile, ks0;
       lat(g, b, s0, pi, tile, ks0);
       const int nk = min(g.kstages - ks0, nit - pi);
       const int mt = tile / g.n_tiles, nt = tile % g.n_tiles;
-      const bool got = mbar_wait_long(tfull, piece & 1);
-      // every epilogue warp is done with the previous piece (tok_e included) past this barrier
-      if (epi_any(!got)) {
-        if (lane == 0) atomicExch(timeout, 1);
-        break;
-      }
-      tc_fence_after();
-      if (ew == 0)
-        for (int t = lane; t < N; t += 32) {
-          const int c = nt * N + t;
-          tok_e[t] = c < g.n_cols && __ldg(g.w.route + c) == kRouteGemm ? __ldg(g.w.emin + c)
-                                                                          : -1;
-        }
-      // drain: T = Σ_p 256^p·A_p by Horner from the top accumulator, up to 16 columns per wait
+      const bool two = needs3(nt);
       long long acc[kEpt];
-      constexpr int kChunk = kEpt % 16 == 0 ? 16 : 8;
-#pragma unroll
-      for (int p = kAcc - 1; p >= 0; p--) {
-#pragma unroll
-        for (int c = 0; c < kEpt / kChunk; c++) {
-          uint32_t v[kChunk];
-#pragma unroll
-          for (int h = 0; h < kChunk / 8; h++)
-            tmem_ld8_nowait(trow + (uint32_t)(p * N + kChunk * c + 8 * h), v, h);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < kChunk; j++)
-            acc[kChunk * c + j] = p == kAcc - 1 ? (long long)(int)v[j]
-                                                : acc[kChunk * c + j] * 256 + (long long)(int)v[j];
+      for (int pass = 0; pass < (two ? 2 : 1); pass++, npass++) {
+        const bool got = mbar_wait_long(tfull, npass & 1);
+        // every epilogue warp is done with the previous piece (tok_e included) past this barrier
+        if (epi_any(!got)) {
+          if (lane == 0) atomicExch(timeout, 1);
+          failed = true;
+          break;
         }
+        tc_fence_after();
+        if (pass == 0) {
+          if (ew == 0)
+            for (int t = lane; t < N; t += 32) {
+              const int c = nt * N + t;
+              // coherent loads: the prep kernel wrote these while this grid was already
+              // resident (programmatic dependent launch), so the read-only path could serve a
+              // stale line
+              tok_e[t] = c < g.n_cols && on_gemm(__ldcg(g.w.route + c)) ? __ldcg(g.w.emin + c)
+                                                                          : -1;
+            }
+          // drain: T = Σ_p 256^p·A_p by Horner from the top accumulator, up to 16 columns per
+          // wait
+#pragma unroll
+          for (int p = kAcc - 1; p >= 0; p--) {
+#pragma unroll
+            for (int c = 0; c < kEpt / kChunk; c++) {
+              uint32_t v[kChunk];
+#pragma unroll
+              for (int h = 0; h < kChunk / 8; h++)
+                tmem_ld8_nowait(trow + (uint32_t)(p * N + kChunk * c + 8 * h), v, h);
+              tmem_wait_ld();
+#pragma unroll
+              for (int j = 0; j < kChunk; j++)
+                acc[kChunk * c + j] = p == kAcc - 1
+                                          ? (long long)(int)v[j]
+                                          : acc[kChunk * c + j] * 256 + (long long)(int)v[j];
+            }
+          }
+        } else {
+          // the third digit's pass: T += Σ_p 2^(16 + 8p)·A_p
+#pragma unroll
+          for (int p = 0; p < D; p++) {
+#pragma unroll
+            for (int c = 0; c < kEpt / kChunk; c++) {
+              uint32_t v[kChunk];
+#pragma unroll
+              for (int h = 0; h < kChunk / 8; h++)
+                tmem_ld8_nowait(trow + (uint32_t)(p * N + kChunk * c + 8 * h), v, h);
+              tmem_wait_ld();
+#pragma unroll
+              for (int j = 0; j < kChunk; j++)
+                acc[kChunk * c + j] += (long long)(int)v[j] * (1ll << (16 + 8 * p));
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tempty);  // the next pass's MMAs may overwrite TMEM
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(tempty);  // the next piece's MMAs may overwrite TMEM
+      if (failed) break;
       bool finish = ks0 == 0 && nk == g.kstages;  // this CTA holds the whole tile
       if (!finish) {
         // split tile (stream-K): store the partial sums, arrive; the last to arrive adds the
@@ -974,15 +1067,15 @@ __global__ void __launch_bounds__(kLThreads, 1)
 // ---- host side ---------------------------------------------------------------------------------
 
 // A 3D int8 map over `planes` planes of `rows` rows of `inner` bytes (rows `inner` bytes apart,
-// planes rows·inner apart), boxes of 64 bytes × box_rows × planes, 64-byte swizzle; reads past
-// an extent fill zeros.
+// planes rows·inner apart), boxes of 64 bytes × box_rows × box_planes, 64-byte swizzle; reads
+// past an extent (a plane past the last one included) fill zeros.
 bool make_plane_map(CUtensorMap *map, const void *base, uint64_t inner, uint64_t rows,
-                    uint32_t planes, uint32_t box_rows) {
+                    uint32_t planes, uint32_t box_planes, uint32_t box_rows) {
   auto fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[3] = {inner, rows, planes};
   const cuuint64_t strides[2] = {inner, inner * rows};
-  const cuuint32_t box[3] = {(cuuint32_t)kLK, box_rows, planes};
+  const cuuint32_t box[3] = {(cuuint32_t)kLK, box_rows, box_planes};
   const cuuint32_t estr[3] = {1, 1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box,
             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
@@ -1001,6 +1094,7 @@ long long family_top(uint32_t type) {
 // The token tile of a tensor with D weight digits: four accumulators of N = 128 tokens fill
 // TMEM; with five, 96 tokens.
 int tile_tokens(int digits) { return digits <= 3 ? 128 : 96; }
+static_assert(kLNMax == 128, "lpad_max covers every token tile width");
 
 template <uint32_t T, int D, int N>
 cudaError_t launch_main(const GemvPlan &pl, const uint8_t *pack, const LimbLayout &lay,
@@ -1010,7 +1104,7 @@ cudaError_t launch_main(const GemvPlan &pl, const uint8_t *pack, const LimbLayou
                         cudaStream_t stream) {
   CUtensorMap map_x;
   const size_t np = lpad_n(n_cols, N);
-  if (!make_plane_map(&map_x, w.xp, lay.kp, np, kXDig, N)) return cudaErrorInvalidValue;
+  if (!make_plane_map(&map_x, w.xp, lay.kp, np, kXPlanes, kXDig, N)) return cudaErrorInvalidValue;
   LArgs a;
   a.kmin = lay.kmin;
   a.w = w;
@@ -1089,6 +1183,16 @@ cudaError_t launch_main_any(uint32_t type, const GemvPlan &pl, const uint8_t *pa
   }
 }
 
+// The largest activation spread s of the three-digit route on a tensor whose weights have
+// wbits bits: every sum T = Σ W'·X' and each of its two passes' parts stay below 2^61 when
+// kp·2^(wbits + 8 + s) <= 2^61 (|W'| < 2^wbits, |X'| <= 2^(7 + s), and the parts' digits add at
+// most one more bit), so the finish's i64 bound holds; at most 15 (three digits).
+int three_digit_limit(const LimbLayout &lay) {
+  int lg = 0;
+  while (((size_t)1 << lg) < lay.kp) lg++;
+  return std::min(kLMaxShift3, 53 - lay.wbits - lg);
+}
+
 LPrepArgs prep_args(uint32_t type, const LimbLayout &lay, size_t n_out, size_t n_in,
                     size_t n_cols, const LWork &w, unsigned long long *status) {
   const int nt = tile_tokens(lay.digits);
@@ -1100,6 +1204,7 @@ LPrepArgs prep_args(uint32_t type, const LimbLayout &lay, size_t n_out, size_t n
   pa.n_cols = (int)n_cols;
   pa.tiles = (int)ltiles(n_out, n_cols, nt);
   pa.top = family_top(type);
+  pa.smax3 = three_digit_limit(lay);
   pa.w = w;
   pa.status = status;
   return pa;
@@ -1165,9 +1270,10 @@ cudaError_t build_limb_layout(const GemvPlan &pl, uint32_t type, const uint8_t *
     }
     e = cudaGetLastError();
   }
-  int f = 1;
-  if (e == cudaSuccess) e = cudaMemcpyAsync(&f, flags, 4, cudaMemcpyDeviceToHost, stream);
+  int fl[2] = {1, 0};
+  if (e == cudaSuccess) e = cudaMemcpyAsync(fl, flags, 8, cudaMemcpyDeviceToHost, stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  const int f = fl[0];
   if (e != cudaSuccess || (f & 1)) {  // a weight needs more than four digits: no digit planes
     cudaFree(base);
     return e;
@@ -1196,7 +1302,7 @@ cudaError_t build_limb_layout(const GemvPlan &pl, uint32_t type, const uint8_t *
     }
   }
   if (!make_plane_map(reinterpret_cast<CUtensorMap *>(lay->map), planes, kp, m_pad,
-                      (uint32_t)digits, kLM)) {
+                      (uint32_t)digits, (uint32_t)digits, kLM)) {
     cudaFree(base);
     return cudaErrorInvalidValue;
   }
@@ -1206,6 +1312,7 @@ cudaError_t build_limb_layout(const GemvPlan &pl, uint32_t type, const uint8_t *
   lay->kp = kp;
   lay->m_pad = m_pad;
   lay->digits = digits;
+  lay->wbits = fl[1];
   lay->ok = true;
   return cudaSuccess;
 }

@@ -1141,6 +1141,51 @@ int apx_swiglu_quant_async(apx_ctx *ctx, const int64_t *d_gate, const int64_t *d
   return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
 }
 
+int apx_swiglu_quant_cols_async(apx_ctx *ctx, const int64_t *d_gate, const int64_t *d_up,
+                                size_t n, size_t k_cols, int carrier, int64_t *d_h,
+                                int8_t *d_codes, uint8_t *d_exps, apx_act_desc *d_descs,
+                                apx_call_status *d_status, void *stream) {
+  if (!ctx || (k_cols && (!d_descs || !d_status ||
+                          (n && (!d_gate || !d_up || !d_codes || !d_exps)))) ||
+      (carrier != APX_CARRIER_F32 && carrier != APX_CARRIER_Q32))
+    return APX_ERR_INVALID_ARGUMENT;
+  if (n > (size_t)INT32_MAX || k_cols > 65535) return APX_ERR_TOO_LARGE;
+  if (k_cols == 0) return APX_OK;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  if (n == 0) {  // empty activations: all-zero descriptors, as the quantizers write them
+    std::vector<ActDesc> d(k_cols);
+    for (auto &x : d) {
+      x = ActDesc{};
+      x.emax = -1;
+    }
+    return cudaMemcpyAsync(d_descs, d.data(), k_cols * sizeof(ActDesc), cudaMemcpyHostToDevice,
+                           (cudaStream_t)stream) == cudaSuccess &&
+                   cudaStreamSynchronize((cudaStream_t)stream) == cudaSuccess
+               ? APX_OK
+               : APX_ERR_CUDA;
+  }
+  if (ctx->fwork.ensure(swiglu_work_bytes(n, k_cols)) != cudaSuccess) return APX_ERR_OUT_OF_MEMORY;
+  const size_t ld = apx_act_padded_len(n);
+  const cudaError_t e = launch_swiglu_quant_cols(
+      (const long long *)d_gate, (const long long *)d_up, n, k_cols, n, carrier,
+      (long long *)d_h, d_codes, ld, d_exps, ld / 32, d_descs,
+      (unsigned long long *)&d_status->first, ctx->fwork.p, (cudaStream_t)stream);
+  return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
+}
+
+int apx_act_describe_cols_async(apx_ctx *ctx, const int8_t *d_codes, const uint8_t *d_exps,
+                                size_t n_in, size_t k_cols, apx_act_desc *d_descs,
+                                void *stream) {
+  if (!ctx || (k_cols && (!d_descs || (n_in && (!d_codes || !d_exps)))))
+    return APX_ERR_INVALID_ARGUMENT;
+  if (k_cols > (size_t)INT32_MAX) return APX_ERR_TOO_LARGE;
+  if (k_cols == 0) return APX_OK;
+  const size_t ld = apx_act_padded_len(n_in);
+  cudaError_t e = launch_describe(d_codes, d_exps, n_in, (int)k_cols, ld, ld / 32, d_descs,
+                                  (cudaStream_t)stream);
+  return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
+}
+
 int apx_ffn_status_decode(const apx_call_status *status, apx_err *err) {
   if (!status) return set_err(err, APX_ERR_INVALID_ARGUMENT);
   const unsigned long long w = status->first;

@@ -505,6 +505,357 @@ def measure_sharded(be, lib, dev, stream, steps, warmup, pg, rank, local, world)
     }
 
 
+PREFILL70 = [(12, 28672, 8192), (12, 28672, 8192), (12, 8192, 28672)]  # gate, up, down
+
+
+def cpu_prefill70_baseline(seconds=10.0, tokens=64):
+    """configs[4]'s prefill on the host cores: the oracle's restatement of the reference's
+    k-column Q4_K kernel (chart/kcols.rs:1406-1518, what matmat_q8act runs for multi-column Q4_K
+    calls) over `tokens` tokens of the 28672x8192 gate matrix, TOPS."""
+    from apeiron_b200 import synth
+    from oracle import oracle as O
+
+    threads = host_threads()
+    t, n_out, n_in = PREFILL70[0]
+    raw = synth.payload(t, n_out, n_in, 4000)
+    cs, ss = [], []
+    for c in range(tokens):
+        cc, ee = synth.quant_act_np(synth.f32_to_q32(synth.activation_f32(n_in, 8000 + c)))
+        cs.append(cc)
+        ss.append(O.exps_to_scales(ee))
+    cs, ss = np.stack(cs), np.stack(ss)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        r = O.matmat_q8act_mt(t, raw, n_out, n_in, cs, ss, threads, simd=True)
+        assert not isinstance(r, tuple)
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or done >= 100:
+            break
+    macs = tokens * n_out * n_in * done
+    return {"value": 2.0 * macs / el / 1e12, "unit": "TOPS", "cores": threads, "kind": "port",
+            "sample": f"{done} passes of {tokens} tokens x W 28672x8192 Q4_K ({el:.1f} s), "
+                      f"k-column Q4_K restatement, {cpu_isa()}"}
+
+
+def measure_prefill70(be, lib, dev, stream, steps, warmup, pg, rank, local, world):
+    """configs[4]'s prefill: the Llama-3-70B-shaped Q4_K projections over 512 f32 tokens each
+    (x ~ N(0,1)): gate and up (W 28672x8192) on one 512-token input, down (W 8192x28672) on its
+    own, each through the f32 prefill entry (fused quantize + digit-plane tensor-core GEMM).  At
+    N > 1 every rank holds a 32-row-aligned slice of each matrix's rows (apeiron_b200/shard.py
+    row_split) and an NCCL all-gather of every projection's f32 output slices gives each rank
+    the whole outputs.  Strong scaling.
+
+    Before timing, the FFN chain these projections make is checked on the device against the
+    oracle's chain for 4 tokens: gate and up, SwiGLU + quant_act of every token's hidden vector
+    in one launch (at N > 1 an all-gather of the hidden codes), down reading those codes."""
+    import torch
+
+    from apeiron_b200 import shard, synth
+    from oracle import oracle as O
+
+    sp = stream.cuda_stream
+    k = PREFILL_TOKENS
+    dist = pg if world > 1 else None
+    raws = [synth.payload(t, n_out, n_in, 4000 + m) for m, (t, n_out, n_in) in enumerate(PREFILL70)]
+    shards = [shard.RowShard(be, t, raws[m], n_out, n_in, rank, world, dist, f"cuda:{local}")
+              for m, (t, n_out, n_in) in enumerate(PREFILL70)]
+    n_embd, n_ff = PREFILL70[0][2], PREFILL70[0][1]
+    rg, rd = shards[0].rows, shards[2].rows
+    for sh in shards:  # equal slices: all-gathers of equal-sized chunks
+        assert all(b - a == sh.rows for a, b in sh.splits)
+    assert rg % 256 == 0, "hidden slices must fill whole padded activation blocks"
+    x = np.stack([synth.activation_f32(n_embd, 8000 + c) for c in range(k)])
+    xd_h = np.stack([synth.activation_f32(n_ff, 8600 + c) for c in range(k)])
+    dx = torch.from_numpy(x).to(dev)
+    dxd = torch.from_numpy(xd_h).to(dev)
+    q32 = lambda n: torch.zeros(n, dtype=torch.int64, device=dev)
+    st = lambda: torch.full((2 * k,), -1, dtype=torch.int64, device=dev)
+    thr = max(1, host_threads() // world)
+    r0, g0 = shards[2].r0, shards[0].r0
+
+    # ---- the FFN chain, exactness only ----
+    gate_s, up_s = q32(k * rg), q32(k * rg)
+    sg, su, sf, sy = st(), st(), st(), st()
+    hc = torch.zeros(k * n_ff, dtype=torch.int8, device=dev)
+    he = torch.full((k * n_ff // 32,), 0xFF, dtype=torch.uint8, device=dev)
+    hd = torch.zeros(8 * k, dtype=torch.int32, device=dev)
+    yq_s = q32(k * rd)
+    with torch.cuda.stream(stream):
+        assert lib.apx_matmat_f32_async(be.ctx, shards[0].tensor.handle, rg, n_embd, k,
+                                        dx.data_ptr(), n_embd, gate_s.data_ptr(), None,
+                                        sg.data_ptr(), sp) == 0
+        assert lib.apx_matmat_f32_async(be.ctx, shards[1].tensor.handle, rg, n_embd, k,
+                                        dx.data_ptr(), n_embd, up_s.data_ptr(), None,
+                                        su.data_ptr(), sp) == 0
+        if world == 1:
+            assert lib.apx_swiglu_quant_cols_async(be.ctx, gate_s.data_ptr(), up_s.data_ptr(), rg,
+                                                   k, 0, None, hc.data_ptr(), he.data_ptr(),
+                                                   hd.data_ptr(), sf.data_ptr(), sp) == 0
+        else:
+            hc_s = torch.zeros(k * rg, dtype=torch.int8, device=dev)
+            he_s = torch.full((k * rg // 32,), 0xFF, dtype=torch.uint8, device=dev)
+            hd_s = torch.zeros(8 * k, dtype=torch.int32, device=dev)
+            hc_g = torch.zeros(world * k * rg, dtype=torch.int8, device=dev)
+            he_g = torch.zeros(world * k * rg // 32, dtype=torch.uint8, device=dev)
+            assert lib.apx_swiglu_quant_cols_async(be.ctx, gate_s.data_ptr(), up_s.data_ptr(), rg,
+                                                   k, 0, None, hc_s.data_ptr(), he_s.data_ptr(),
+                                                   hd_s.data_ptr(), sf.data_ptr(), sp) == 0
+            pg.all_gather_into_tensor(hc_g, hc_s)
+            pg.all_gather_into_tensor(he_g, he_s)
+            # [rank][token][slice] -> [token][rank][slice]: every token's whole h
+            hc.view(k, world, rg).copy_(hc_g.view(world, k, rg).transpose(0, 1))
+            he.view(k, world, rg // 32).copy_(he_g.view(world, k, rg // 32).transpose(0, 1))
+            assert lib.apx_act_describe_cols_async(be.ctx, hc.data_ptr(), he.data_ptr(), n_ff, k,
+                                                   hd.data_ptr(), sp) == 0
+        assert lib.apx_matmat_async(be.ctx, shards[2].tensor.handle, rd, n_ff, k, hc.data_ptr(),
+                                    he.data_ptr(), hd.data_ptr(), yq_s.data_ptr(), None,
+                                    sy.data_ptr(), sp) == 0
+    stream.synchronize()
+    for s_ in (sg, su, sf, sy):
+        assert bool((s_[0::2] == -1).all().item()), "refusal in the prefill chain"
+    ys = yq_s.cpu().numpy().reshape(k, rd)
+    gq, uq = gate_s.cpu().numpy().reshape(k, rg), up_s.cpu().numpy().reshape(k, rg)
+    hcn, hen = hc.cpu().numpy().reshape(k, n_ff), he.cpu().numpy().reshape(k, n_ff // 32)
+    for c in (0, 1, k // 2, k - 1):
+        cx, sx = O.quant_act(synth.f32_to_q32(x[c]))
+        g = O.matvec_q8act_mt(12, raws[0], n_ff, n_embd, cx, sx, thr, simd=True)
+        u = O.matvec_q8act_mt(12, raws[1], n_ff, n_embd, cx, sx, thr, simd=True)
+        assert np.array_equal(gq[c], g[g0:g0 + rg]), f"gate parity failure, token {c}"
+        assert np.array_equal(uq[c], u[g0:g0 + rg]), f"up parity failure, token {c}"
+        _, hcodes, hscales = O.swiglu_quant(g, u, 0)
+        assert np.array_equal(hcn[c], hcodes), f"h codes parity failure, token {c}"
+        assert np.array_equal(hen[c], O.scales_to_exps(hscales)), f"h exponents, token {c}"
+        want = O.matvec_q8act_mt(12, raws[2], n_embd, n_ff, hcodes, hscales, thr, simd=True)
+        if not np.array_equal(ys[c], want[r0:r0 + rd]):
+            bad = np.nonzero(ys[c] != want[r0:r0 + rd])[0]
+            raise AssertionError(f"prefill chain parity failure, token {c}: {bad.size} rows, "
+                                 f"first {bad[0]} gpu {ys[c][bad[0]]} oracle {want[r0 + bad[0]]}")
+    del gate_s, up_s, hc, he, yq_s
+
+    # ---- the timed step: the three projections (+ all-gathers of their output slices) ----
+    ins = [(dx, n_embd), (dx, n_embd), (dxd, n_ff)]
+    rows = [sh.rows for sh in shards]
+    y_s = [torch.zeros(k * r, dtype=torch.float32, device=dev) for r in rows]
+    yq = [q32(k * r) for r in rows]
+    y_g = ([torch.zeros(world * k * r, dtype=torch.float32, device=dev) for r in rows]
+           if world > 1 else y_s)
+    sts = [st() for _ in rows]
+
+    def step(check=False):
+        for m in range(3):
+            xin, n_in = ins[m]
+            assert lib.apx_matmat_f32_async(be.ctx, shards[m].tensor.handle, rows[m], n_in, k,
+                                            xin.data_ptr(), n_in,
+                                            yq[m].data_ptr() if check else None,
+                                            y_s[m].data_ptr(), sts[m].data_ptr(), sp) == 0
+            if world > 1:
+                pg.all_gather_into_tensor(y_g[m], y_s[m])
+
+    with torch.cuda.stream(stream):
+        step(check=True)
+    stream.synchronize()
+    for m, (t, n_out, n_in) in enumerate(PREFILL70):
+        assert bool((sts[m][0::2] == -1).all().item()), f"refusal in projection {m}"
+        got = yq[m].cpu().numpy().reshape(k, rows[m])
+        gf = y_g[m].cpu().numpy().reshape(world, k, rows[m])
+        xs = x if m < 2 else xd_h
+        sr0 = shards[m].r0
+        for c in ((0, k - 1) if m < 2 else (0, k // 3, k - 1)):
+            cx, sx = O.quant_act(synth.f32_to_q32(xs[c]))
+            want = O.matvec_q8act_mt(t, raws[m], n_out, n_in, cx, sx, thr, simd=True)
+            assert np.array_equal(got[c], want[sr0:sr0 + rows[m]]), \
+                f"projection {m} parity failure, token {c}"
+            wf = (want.astype(np.float64) / 4294967296.0).astype(np.float32)
+            whole = np.concatenate([gf[r, c] for r in range(world)])
+            assert np.allclose(whole, wf, rtol=1e-6, atol=0), f"projection {m} f32, token {c}"
+    del raws, yq
+    barrier(pg, local)
+    with torch.cuda.stream(stream):
+        for _ in range(max(warmup, 3)):
+            step()
+    stream.synchronize()
+    barrier(pg, local)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for _ in range(steps):
+            step()
+        t1.record(stream)
+    stream.synchronize()
+    barrier(pg, local)
+    ms = max_over_ranks(t0.elapsed_time(t1), pg, local) / steps
+    for m in range(3):
+        assert bool((sts[m][0::2] == -1).all().item()), "refusal while timed"
+    macs = sum(k * n_out * n_in for _, n_out, n_in in PREFILL70)
+    tops = 2.0 * macs / (ms / 1e3) / 1e12
+
+    # e2e: pinned host inputs copied in, assembled outputs copied out, every step
+    hx = [torch.from_numpy(x).pin_memory(), torch.from_numpy(xd_h).pin_memory()]
+    hy = [torch.empty(y_g[m].numel(), dtype=torch.float32).pin_memory() for m in range(3)]
+
+    def e2e_step():
+        dx.copy_(hx[0], non_blocking=True)
+        dxd.copy_(hx[1], non_blocking=True)
+        step()
+        for m in range(3):
+            hy[m].copy_(y_g[m], non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            e2e_step()
+    stream.synchronize()
+    barrier(pg, local)
+    e_steps = max(3, steps // 2)
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for _ in range(e_steps):
+            e2e_step()
+        t1.record(stream)
+    stream.synchronize()
+    barrier(pg, local)
+    e_ms = max_over_ranks(t0.elapsed_time(t1), pg, local) / e_steps
+    peak, src = int8_peak()
+    return {
+        "metric": "70B FFN pp512 int8 TOPS (gate/up/down projections, row-sharded)",
+        "value": tops, "unit": "TOPS", "n_gpus": world, "ms_per_step": ms, "steps": steps,
+        "warmup": warmup, "scaling": "strong",
+        "config": {"workload": "Llama-3-70B-shaped Q4_K FFN prefill, configs[4]: 512 f32 tokens "
+                               "(N(0,1)) through gate and up (W 28672x8192) and 512 through down "
+                               "(W 8192x28672), each by the f32 prefill entry (quantize + digit-"
+                               "plane tensor-core GEMM); at N > 1 row shards and an NCCL all-"
+                               "gather of every projection's f32 output slices (assembled "
+                               "outputs [rank][token][row slice] on every rank)",
+                   "rows_per_rank": {"gate_up": rg, "down": rd},
+                   "l2": "digit planes of the three matrices (2.8 GB at N = 1) exceed the 126 MB "
+                         "L2: every step streams them from HBM",
+                   "exact": "2-3 tokens of every projection bit-equal (Q32.32) to the oracle, and "
+                            "the FFN chain (gate, up, SwiGLU + quant_act, down) bit-equal for 4 "
+                            "tokens, checked before timing"},
+        "roofline": {"bound": "tensor", "achieved": tops / world, "peak": peak, "unit": "TOPS",
+                     "frac": tops / world / peak, "peak_source": src,
+                     "note": "algorithmic int8 ops per GPU; these Q4_K rows need four weight "
+                             "digits (27-bit integer weights), so the GEMM runs 8 int8 MMAs "
+                             "(4 weight x 2 activation digits) per algorithmic op: the tensor "
+                             "pipe's own rate is 8x this"},
+        "gpu_launches_per_step": 6,
+        "e2e": {"value": 2.0 * macs / (e_ms / 1e3) / 1e12, "unit": "TOPS", "ms_per_step": e_ms,
+                "h2d_bytes_per_step": int(x.nbytes + xd_h.nbytes),
+                "d2h_bytes_per_step": int(sum(4 * y_g[m].numel() for m in range(3))),
+                "note": "pinned host inputs -> device, the three projections (+ gathers), the "
+                        "assembled f32 outputs -> pinned host, per step; CUDA events on the "
+                        "stream, max over ranks"},
+    }
+
+
+def measure_gemv(be, lib, dev, stream, mat, steps, warmup, pg, local, world, seed=1100):
+    """One projection's decode GEMV (configs[0]: Q8_0 4864x896) on its own: device-timed GB/s
+    of algorithmic bytes over rotating weight copies (3x the L2), back-to-back launches replayed
+    from a CUDA graph, checked against the oracle first; e2e through apx_matvec_q8act with host
+    buffers (every copy's synchronous call warmed first)."""
+    import ctypes as C
+
+    import torch
+
+    from apeiron_b200 import _abi, synth
+    from oracle import oracle as O
+
+    sp = stream.cuda_stream
+    t, n_out, n_in = mat
+    raw = synth.payload(t, n_out, n_in, seed)
+    copies = max(4, int(np.ceil(3 * L2_BYTES / raw.size)))
+    tensors = [be.upload(t, raw, n_out, n_in) for _ in range(copies)]
+    x = synth.activation_f32(n_in, seed + 1)
+    c, e = synth.quant_act_np(synth.f32_to_q32(x))
+    pad = lib.apx_act_padded_len(n_in)
+    codes = torch.zeros(pad, dtype=torch.int8, device=dev)
+    codes[:n_in] = torch.from_numpy(c).to(dev)
+    exps = torch.full((pad // 32,), 0xFF, dtype=torch.uint8, device=dev)
+    exps[:e.size] = torch.from_numpy(e).to(dev)
+    desc = torch.zeros(8, dtype=torch.int32, device=dev)
+    out = torch.zeros(n_out, dtype=torch.int64, device=dev)
+    status = torch.full((2,), -1, dtype=torch.int64, device=dev)
+    with torch.cuda.stream(stream):
+        assert lib.apx_act_describe_async(be.ctx, codes.data_ptr(), exps.data_ptr(), n_in,
+                                          desc.data_ptr(), sp) == 0
+
+    def launch(i):
+        assert lib.apx_matvec_async(be.ctx, tensors[i % copies].handle, n_out, n_in,
+                                    codes.data_ptr(), exps.data_ptr(), desc.data_ptr(),
+                                    out.data_ptr(), None, status.data_ptr(), sp) == 0
+
+    with torch.cuda.stream(stream):
+        launch(0)
+    stream.synchronize()
+    want = O.matvec_q8act(t, raw, n_out, n_in, c, O.exps_to_scales(e))
+    assert np.array_equal(out.cpu().numpy(), want), "configs[0] parity failure"
+    G = max(64, min(steps, 1000))
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=stream):
+        for i in range(G):
+            launch(i)
+    with torch.cuda.stream(stream):
+        for i in range(max(warmup, 3)):
+            launch(i)
+        gr.replay()
+    stream.synchronize()
+    barrier(pg, local)
+    reps = max(1, steps // G)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for _ in range(reps):
+            gr.replay()
+        t1.record(stream)
+    stream.synchronize()
+    barrier(pg, local)
+    ms = max_over_ranks(t0.elapsed_time(t1), pg, local) / (reps * G)
+    assert int(status[0].item()) == -1
+    del gr
+    nbytes = gemv_bytes(*mat)
+    gbs = world * nbytes / (ms / 1e3) / 1e9
+    # e2e: the synchronous drop-in with host buffers, every rotating copy warmed first
+    hc, he = np.ascontiguousarray(c, dtype=np.int8), np.ascontiguousarray(e, dtype=np.uint8)
+    ho = np.empty(n_out, dtype=np.int64)
+    err = _abi.ApxErr()
+    for i in range(copies):
+        assert lib.apx_matvec_q8act(be.ctx, tensors[i].handle, n_out, n_in, hc.ctypes.data, n_in,
+                                    he.ctypes.data, ho.ctypes.data, C.byref(err)) == 0
+    assert np.array_equal(ho, want)
+    n_e = 2000
+    e0 = time.perf_counter()
+    for i in range(n_e):
+        lib.apx_matvec_q8act(be.ctx, tensors[i % copies].handle, n_out, n_in, hc.ctypes.data,
+                             n_in, he.ctypes.data, ho.ctypes.data, C.byref(err))
+    e_s = max_over_ranks(time.perf_counter() - e0, pg, local)
+    hbm, src = peaks()
+    return {
+        "metric": "Q8_0 decode GEMV GB/s", "value": gbs, "unit": "GB/s", "ms_per_step": ms,
+        "steps": reps * G, "scaling": "weak",
+        "config": {"workload": "Q8_0 GEMV 4864x896 (Qwen2.5-0.5B FFN up), configs[0]; step = one "
+                               "launch, resident activation",
+                   "weight_copies": copies, "l2": "rotating weight copies, 3x the 126 MB L2",
+                   "exact": "Q32.32 outputs bit-equal to the CPU oracle (checked before timing)"},
+        "roofline": {"bound": "hbm", "achieved": gbs / world, "peak": hbm, "unit": "GB/s",
+                     "frac": gbs / world / hbm, "kernel": f"gemv_kernel<Q8_0> {n_out}x{n_in}",
+                     "algorithmic_bytes": nbytes, "peak_source": src,
+                     "note": "back-to-back launches under programmatic dependent launch"},
+        "e2e": {"value": world * nbytes * n_e / e_s / 1e9, "unit": "GB/s",
+                "h2d_bytes_per_step": 16 + 32 + ((-(-n_in // 32) + 15) // 16) * 16 +
+                                      ((n_in + 15) // 16) * 16,
+                "d2h_bytes_per_step": ((8 * n_out + 15) // 16) * 16 + 16},
+        "gpu_launches_per_step": 1,
+    }
+
+
+def gemv_config(name):
+    """The headline's `config`: the workload alone, identical for both arms."""
+    return {"workload": name,
+            "l2": "every step streams its weights from memory (rotating copies larger than the "
+                  "last-level cache)",
+            "exact": "Q32.32 outputs bit-equal to the CPU oracle (checked before timing)"}
+
+
 def gemv_bytes(t, n_out, n_in):
     from apeiron_b200 import synth
     qk, bb = synth.GEOM[t]
@@ -624,15 +975,16 @@ def cpu_data(mats, min_bytes=256 << 20):
             for _ in range(copies)], copies
 
 
-def cpu_passes(data, max_passes, max_seconds):
+def cpu_passes(data, max_passes, max_seconds, min_seconds=0.0):
     """Timed passes of the oracle's threaded fused rows (restating the reference's AVX2
-    chunked decode, src/engine/chart/ffn.rs:667-745) on every host thread."""
+    chunked decode, src/engine/chart/ffn.rs:667-745) on every host thread: at least
+    `max_passes` passes or `min_seconds`, whichever is longer, and at most `max_seconds`."""
     from oracle import oracle as O
 
     threads = host_threads()
     total = done = 0
     t0 = time.perf_counter()
-    while done < max_passes:
+    while done < max_passes or time.perf_counter() - t0 < min_seconds:
         for t, raw, n_out, n_in, c, s in data[done % len(data)]:
             r = O.matvec_q8act_mt(t, raw, n_out, n_in, c, s, threads, simd=True)
             assert not isinstance(r, tuple)
@@ -696,15 +1048,19 @@ def run_reference(args, world, rank, local, pg):
     name, mats = WORKLOADS[args.config]
     data, copies = cpu_data(mats)
     cpu_passes(data, args.warmup, 10.0)
-    total, done, el, threads = cpu_passes(data, args.steps, 60.0)
+    # a timed window of at least 5 s whatever --steps is (a few ms per step on the host)
+    total, done, el, threads = cpu_passes(data, args.steps, 60.0, min_seconds=5.0)
     v = total / el / 1e9
-    sample = (f"{done} of {args.steps} steps (capped at 60 s) over {copies} cycled host "
-              f"copies (>= 256 MB, streamed from DRAM), two-row decode cores, {cpu_isa()}")
+    sample = (f"{done} steps in {el:.1f} s (at least {args.steps} and 5 s, at most 60 s) over "
+              f"{copies} cycled host copies (>= 256 MB, streamed from DRAM), two-row decode "
+              f"cores, {cpu_isa()}")
     line = {"metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus,
             "steps": done, "warmup": args.warmup, "ms_per_step": el * 1e3 / max(done, 1),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int64",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": name, "parallelism": f"{threads} host threads"},
+            "config": gemv_config(name),
+            "arm": {"weight_copies": copies, "l2": "cycled host copies >= 256 MB",
+                    "parallelism": f"{threads} host threads"},
             "cpu_baseline": {"value": v, "unit": "GB/s", "cores": threads, "kind": "port",
                              "sample": sample},
             "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0,
@@ -715,6 +1071,15 @@ def run_reference(args, world, rank, local, pg):
                            "unit": "TOPS", "cpu_baseline": pre,
                            "e2e": {"value": pre["value"], "unit": "TOPS",
                                    "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if not args.no_gemv0:
+        g0 = cpu_gemv_baseline(WORKLOADS[1][1], seconds=min(10.0, args.cpu_seconds))
+        line["gemv_q8_0"] = {"metric": "Q8_0 decode GEMV GB/s", "value": g0["value"],
+                             "unit": "GB/s", "cpu_baseline": g0}
+    if not args.no_prefill70:
+        p70 = cpu_prefill70_baseline(seconds=min(20.0, args.cpu_seconds * 2))
+        line["prefill_70b"] = {
+            "metric": "70B FFN pp512 int8 TOPS (gate/up/down projections, row-sharded)",
+            "value": p70["value"], "unit": "TOPS", "cpu_baseline": p70}
     for key, skip, metric, mats_, seed in (
             ("decode_step", args.no_decode, "decode step GB/s (all linear layers)",
              DECODE_LAYER * DECODE_LAYERS + [DECODE_HEAD], 6000),
@@ -794,14 +1159,14 @@ def run_ours(args, world, rank, local, pg):
 
     # The timed steps are replayed from CUDA graphs (captured once, untimed), so the device
     # time is the kernels' and not the Python launch loop's.
-    def capture(first, count, only_first=False):
+    def capture(first, count, only=None):
         gr = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gr, stream=stream):
             for i in range(first, first + count):
-                if only_first:
-                    t, n_out, n_in = mats[0]
-                    codes, exps, desc, out, _, _ = acts[0]
-                    assert lib.apx_matvec_async(be.ctx, tensors[i % copies][0].handle, n_out,
+                if only is not None:
+                    t, n_out, n_in = mats[only]
+                    codes, exps, desc, out, _, _ = acts[only]
+                    assert lib.apx_matvec_async(be.ctx, tensors[i % copies][only].handle, n_out,
                                                 n_in, codes.data_ptr(), exps.data_ptr(),
                                                 desc.data_ptr(), out.data_ptr(), None,
                                                 status.data_ptr(), sp) == 0
@@ -813,7 +1178,7 @@ def run_ours(args, world, rank, local, pg):
     g_main = capture(0, G)
     g_rem = capture(0, args.steps % G) if args.steps % G else None
     n_k = min(max(args.steps, 64), 1000)
-    g_kernel = capture(0, n_k, only_first=True)
+    g_kernels = [capture(0, n_k, only=m) for m in range(len(mats))]
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
             step(i)
@@ -835,15 +1200,17 @@ def run_ours(args, world, rank, local, pg):
     stream.synchronize()
     barrier(pg, local)
     ms = t0.elapsed_time(t1)
-    # the dominant kernel alone, n_k back-to-back launches over the rotating copies
-    k0e, k1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        g_kernel.replay()
-        k0e.record(stream)
-        g_kernel.replay()
-        k1e.record(stream)
-    stream.synchronize()
-    kms = k0e.elapsed_time(k1e) / n_k
+    # each projection's kernel alone, n_k back-to-back launches over the rotating copies
+    kms = []
+    for g_kernel in g_kernels:
+        k0e, k1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            g_kernel.replay()
+            k0e.record(stream)
+            g_kernel.replay()
+            k1e.record(stream)
+        stream.synchronize()
+        kms.append(k0e.elapsed_time(k1e) / n_k)
     clk = clocks.stop()
     clk["timed_region_ms"] = ms
     ms_max = max_over_ranks(ms, pg, local)
@@ -866,7 +1233,9 @@ def run_ours(args, world, rank, local, pg):
                   he.ctypes.data, ho.ctypes.data, hptr):
                 raise RuntimeError(f"apx_matvec_q8act failed: code {herr.code}")
 
-    for i in range(args.warmup):
+    # every rotating copy once first: each tensor's synchronous call builds its cached graph on
+    # its first call, so the timed loop measures the steady state
+    for i in range(max(args.warmup, copies)):
         e2e_step(i)
     for m, (t, n_out, n_in) in enumerate(mats):  # the host outputs are the exact ones
         raw = synth.payload(t, n_out, n_in, 1000 + m)
@@ -884,10 +1253,18 @@ def run_ours(args, world, rank, local, pg):
               for _, _, n_in in mats)
     d2h = sum(((8 * n_out + 15) // 16) * 16 + 16 for _, n_out, _ in mats)
 
+    gemv0 = None
+    if not args.no_gemv0:
+        gemv0 = measure_gemv(be, lib, dev, stream, WORKLOADS[1][1][0], args.steps, args.warmup,
+                             pg, local, world)
     prefill = None
     if not args.no_prefill:
         prefill = measure_prefill(be, lib, dev, stream, args.prefill_steps, args.warmup, pg,
                                   local, world)
+    prefill70 = None
+    if not args.no_prefill70:
+        prefill70 = measure_prefill70(be, lib, dev, stream, args.prefill70_steps, args.warmup, pg,
+                                      rank, local, world)
     decode = None
     if not args.no_decode:
         decode = measure_decode_step(be, lib, dev, stream, args.decode_steps, args.warmup, pg,
@@ -899,35 +1276,47 @@ def run_ours(args, world, rank, local, pg):
     if rank != 0:
         return
     hbm, src = peaks()
-    t0m = mats[0]
+    # the roofline of the slowest kernel per byte of the step (the one that bounds it)
+    rates = [gemv_bytes(*m) / (kms[i] / 1e3) / 1e9 for i, m in enumerate(mats)]
+    slow = int(np.argmin(rates))
+    t0m = mats[slow]
     kbytes = gemv_bytes(*t0m)
-    achieved = kbytes / (kms / 1e3) / 1e9
+    achieved = rates[slow]
     traffic = None
     prof = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(prof):
         traffic = json.load(open(prof)).get(f"{t0m[0]}:{t0m[1]}x{t0m[2]}")
+    fam = {8: "Q8_0", 12: "Q4_K", 14: "Q6_K"}
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
-        "config": {"workload": name, "weight_copies": copies,
-                   "l2": "rotating weight copies, 3x the 126 MB L2",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                   "exact": "Q32.32 outputs bit-equal to the CPU oracle (checked before timing)"},
+        "config": gemv_config(name),
+        "arm": {"weight_copies": copies, "l2": "rotating device copies, 3x the 126 MB L2",
+                "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "traffic": traffic,
-                     "kernel": f"gemv_kernel<Q4_K> {t0m[1]}x{t0m[2]}",
+                     "kernel": f"gemv_kernel<{fam[t0m[0]]}> {t0m[1]}x{t0m[2]} (the step's slower "
+                               f"kernel per byte)",
+                     "share_of_step": kms[slow] / sum(kms),
+                     "kernels": [{"shape": f"{m[1]}x{m[2]}", "us": kms[i] * 1e3,
+                                  "gbs": rates[i], "frac": rates[i] / hbm}
+                                 for i, m in enumerate(mats)],
                      "algorithmic_bytes": kbytes, "peak_source": src},
         "e2e": {"value": e2e, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": len(mats) * args.steps,
-        "kernel_us": kms * 1e3,
+        "kernel_us": kms[slow] * 1e3,
         "clocks": clk,
     }
     if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_gemv_baseline(mats, seconds=args.cpu_seconds)
+        if gemv0 is not None:
+            gemv0["cpu_baseline"] = cpu_gemv_baseline(WORKLOADS[1][1], seconds=args.cpu_seconds / 2)
         if prefill is not None:
             prefill["cpu_baseline"] = cpu_prefill_baseline(seconds=args.cpu_seconds)
+        if prefill70 is not None:
+            prefill70["cpu_baseline"] = cpu_prefill70_baseline(seconds=args.cpu_seconds)
         for obj, mats_, seed in ((decode, DECODE_LAYER * DECODE_LAYERS + [DECODE_HEAD], 6000),
                                  (sharded, SHARDED, 4000)):
             if obj is None:
@@ -936,9 +1325,15 @@ def run_ours(args, world, rank, local, pg):
                 obj["cpu_baseline"] = cpu_chain_baseline(mats_, seed, args.cpu_seconds / 2)
             except Exception as exc:  # the device numbers stand without it
                 obj["cpu_baseline"] = {"unavailable": f"{type(exc).__name__}: {exc}"}
+    if gemv0 is not None:
+        line["gemv_q8_0"] = gemv0
+        line["gpu_launches"] += gemv0["steps"]
     if prefill is not None:
         line["prefill"] = prefill
         line["gpu_launches"] += prefill["gpu_launches_per_step"] * prefill["steps"]
+    if prefill70 is not None:
+        line["prefill_70b"] = prefill70
+        line["gpu_launches"] += prefill70["gpu_launches_per_step"] * prefill70["steps"]
     if decode is not None:
         line["decode_step"] = decode
         line["gpu_launches"] += decode["gpu_launches_per_step"] * decode["steps"]
@@ -959,6 +1354,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-shard", action="store_true")
+    ap.add_argument("--no-gemv0", action="store_true")
+    ap.add_argument("--no-prefill70", action="store_true")
+    ap.add_argument("--prefill70-steps", type=int, default=10)
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--decode-steps", type=int, default=200)
     ap.add_argument("--shard-steps", type=int, default=400)

@@ -238,6 +238,24 @@ APX_API int apx_swiglu_quant_async(apx_ctx *ctx, const int64_t *d_gate, const in
                                    size_t n, int carrier, int64_t *d_h, int8_t *d_codes,
                                    uint8_t *d_exps, apx_act_desc *d_desc,
                                    apx_call_status *d_status, void *stream);
+/* apx_swiglu_quant_async over k_cols columns in one launch (the prefill side of the FFN: the
+ * hidden activation of every token between the gate/up and down projections): column c of gate,
+ * up and d_h (optional) at c*n (the column-major outputs of apx_matmat_async), codes at
+ * d_codes[c*apx_act_padded_len(n) ..], exponent bytes at d_exps[c*apx_act_padded_len(n)/32 ..],
+ * descriptor d_descs[c], status word d_status[c] (all ones on entry) — the layout
+ * apx_quant_f32_cols_async writes, which apx_matmat_async reads.  Each column equals
+ * apx_swiglu_quant_async of that column. */
+APX_API int apx_swiglu_quant_cols_async(apx_ctx *ctx, const int64_t *d_gate, const int64_t *d_up,
+                                        size_t n, size_t k_cols, int carrier, int64_t *d_h,
+                                        int8_t *d_codes, uint8_t *d_exps, apx_act_desc *d_descs,
+                                        apx_call_status *d_status, void *stream);
+/* apx_act_describe_async over k_cols device columns laid out as apx_quant_f32_cols_async writes
+ * them (codes of column c at d_codes[c*apx_act_padded_len(n_in) ..], exponent bytes at
+ * d_exps[c*apx_act_padded_len(n_in)/32 ..]): for activations assembled on the device, e.g. the
+ * slices of a row-sharded hidden activation gathered from every rank. */
+APX_API int apx_act_describe_cols_async(apx_ctx *ctx, const int8_t *d_codes,
+                                        const uint8_t *d_exps, size_t n_in, size_t k_cols,
+                                        apx_act_desc *d_descs, void *stream);
 /* A host copy of apx_swiglu_quant_async's status word into err (APX_OK, or
  * APX_ERR_SWIGLU_REFUSED with the lane in err->row and the FfnError kind in err->bits). */
 APX_API int apx_ffn_status_decode(const apx_call_status *status, apx_err *err);

@@ -30,3 +30,9 @@ def test_cpu_prefill_baseline_small():
 
 def test_cpu_isa_names_the_vector_form():
     assert bench.cpu_isa().split(" on ")[0] in ("AVX-VNNI", "AVX2", "scalar")
+
+
+def test_cpu_prefill70_baseline_small():
+    d = bench.cpu_prefill70_baseline(seconds=0.2, tokens=8)
+    _check(d, "TOPS")
+    assert "8 tokens" in d["sample"]

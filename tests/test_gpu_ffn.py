@@ -166,3 +166,103 @@ def test_decode_ffn_chain_on_device(be, t, n_embd, n_ff, carrier):
     h, hcodes, hscales = O.swiglu_quant(g, u, carrier)
     want = O.matvec_q8act(t, raws[2], n_embd, n_ff, hcodes, hscales)
     assert np.array_equal(y.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("n,k,carrier", [(4864, 9, _abi.CARRIER_F32), (1000, 5, _abi.CARRIER_Q32),
+                                         (96, 3, _abi.CARRIER_F32)])
+def test_swiglu_columns_equal_single_column(be, n, k, carrier):
+    """apx_swiglu_quant_cols_async over k columns (one launch) equals apx_swiglu_quant_async of
+    every column: h, codes, exponent bytes, descriptor and status word, refusing columns
+    included."""
+    import torch
+
+    lib = be.lib
+    dev = torch.device("cuda:0")
+    stream = torch.cuda.current_stream().cuda_stream
+    cols = [hidden(n, 100 + c) for c in range(k)]
+    if k > 2:  # one column with a lane the carrier refuses, one whose h quant_act refuses
+        cols[1][0][5], cols[1][1][5] = 16 * ONE, (1 << 62)
+        cols[2][0][40], cols[2][1][40] = 16 * ONE, (1 << 59) - (1 << 50)
+    gate = np.concatenate([c[0] for c in cols])
+    up = np.concatenate([c[1] for c in cols])
+    pad = lib.apx_act_padded_len(n)
+    dg, du = torch.from_numpy(gate).to(dev), torch.from_numpy(up).to(dev)
+    h = torch.zeros(k * n, dtype=torch.int64, device=dev)
+    codes = torch.zeros(k * pad, dtype=torch.int8, device=dev)
+    exps = torch.full((k * pad // 32,), 0xEE, dtype=torch.uint8, device=dev)
+    descs = torch.zeros(8 * k, dtype=torch.int32, device=dev)
+    status = torch.full((2 * k,), -1, dtype=torch.int64, device=dev)
+    assert lib.apx_swiglu_quant_cols_async(be.ctx, dg.data_ptr(), du.data_ptr(), n, k, carrier,
+                                           h.data_ptr(), codes.data_ptr(), exps.data_ptr(),
+                                           descs.data_ptr(), status.data_ptr(), stream) == 0
+    torch.cuda.synchronize()
+    hh, cc, ee = h.cpu().numpy(), codes.cpu().numpy(), exps.cpu().numpy()
+    dd, ss = descs.cpu().numpy(), status.cpu().numpy()
+    nb = -(-n // 32)
+    for c in range(k):
+        h1, c1, e1, d1, _ = run(be, cols[c][0], cols[c][1], carrier)
+        st1 = torch.full((2,), -1, dtype=torch.int64, device=dev)
+        # the single-column call's raw status word, for an exact comparison
+        g1, u1 = torch.from_numpy(cols[c][0]).to(dev), torch.from_numpy(cols[c][1]).to(dev)
+        tmp_c = torch.zeros(pad, dtype=torch.int8, device=dev)
+        tmp_e = torch.full((pad // 32,), 0xEE, dtype=torch.uint8, device=dev)
+        tmp_d = torch.zeros(8, dtype=torch.int32, device=dev)
+        assert lib.apx_swiglu_quant_async(be.ctx, g1.data_ptr(), u1.data_ptr(), n, carrier, None,
+                                          tmp_c.data_ptr(), tmp_e.data_ptr(), tmp_d.data_ptr(),
+                                          st1.data_ptr(), stream) == 0
+        torch.cuda.synchronize()
+        assert np.array_equal(hh[c * n:(c + 1) * n], h1), c
+        assert np.array_equal(cc[c * pad:c * pad + n], c1[:n]), c
+        assert np.array_equal(ee[c * pad // 32:c * pad // 32 + nb], e1[:nb]), c
+        assert np.array_equal(dd[8 * c:8 * c + 8], d1), c
+        assert ss[2 * c] == int(st1[0].item()), c
+
+
+def test_prefill_ffn_chain_on_device(be):
+    """A prefill FFN over 48 tokens with nothing on the host between its stages: gate and up on
+    the tensor cores (Q32.32 outputs, column-major), SwiGLU + quant_act of every token's h in
+    one launch, then the down projection of all tokens reading those codes.  Every token's y
+    equals the reference's chain computed by the oracle."""
+    import torch
+
+    lib = be.lib
+    dev = torch.device("cuda:0")
+    stream = torch.cuda.current_stream().cuda_stream
+    t, n_embd, n_ff, k, carrier = 12, 1024, 2816, 48, _abi.CARRIER_F32
+    shapes = [(n_ff, n_embd), (n_ff, n_embd), (n_embd, n_ff)]
+    raws = [synth.payload(t, o, i, 80 + j) for j, (o, i) in enumerate(shapes)]
+    tens = [be.upload(t, r, o, i) for r, (o, i) in zip(raws, shapes)]
+    x = np.stack([synth.activation_f32(n_embd, 30 + c) for c in range(k)])
+    dx = torch.from_numpy(x).to(dev)
+    gu = [torch.zeros(k * n_ff, dtype=torch.int64, device=dev) for _ in range(2)]
+    gs = [torch.full((2 * k,), -1, dtype=torch.int64, device=dev) for _ in range(2)]
+    for j in range(2):
+        assert lib.apx_matmat_f32_async(be.ctx, tens[j].handle, n_ff, n_embd, k, dx.data_ptr(),
+                                        n_embd, gu[j].data_ptr(), None, gs[j].data_ptr(),
+                                        stream) == 0
+    padh = lib.apx_act_padded_len(n_ff)
+    hc = torch.zeros(k * padh, dtype=torch.int8, device=dev)
+    he = torch.full((k * padh // 32,), 0xFF, dtype=torch.uint8, device=dev)
+    hd = torch.zeros(8 * k, dtype=torch.int32, device=dev)
+    fs = torch.full((2 * k,), -1, dtype=torch.int64, device=dev)
+    assert lib.apx_swiglu_quant_cols_async(be.ctx, gu[0].data_ptr(), gu[1].data_ptr(), n_ff, k,
+                                           carrier, None, hc.data_ptr(), he.data_ptr(),
+                                           hd.data_ptr(), fs.data_ptr(), stream) == 0
+    y = torch.zeros(k * n_embd, dtype=torch.int64, device=dev)
+    ys = torch.full((2 * k,), -1, dtype=torch.int64, device=dev)
+    assert lib.apx_matmat_async(be.ctx, tens[2].handle, n_embd, n_ff, k, hc.data_ptr(),
+                                he.data_ptr(), hd.data_ptr(), y.data_ptr(), None, ys.data_ptr(),
+                                stream) == 0
+    torch.cuda.synchronize()
+    for st in gs + [fs, ys]:
+        assert bool((st[0::2] == -1).all().item())
+    g_all, u_all = gu[0].cpu().numpy().reshape(k, n_ff), gu[1].cpu().numpy().reshape(k, n_ff)
+    y_all = y.cpu().numpy().reshape(k, n_embd)
+    for c in range(k):
+        cx, sx = O.quant_act(synth.f32_to_q32(x[c]))
+        g = O.matvec_q8act(t, raws[0], n_ff, n_embd, cx, sx)
+        u = O.matvec_q8act(t, raws[1], n_ff, n_embd, cx, sx)
+        assert np.array_equal(g_all[c], g) and np.array_equal(u_all[c], u), c
+        _, hcodes, hscales = O.swiglu_quant(g, u, carrier)
+        want = O.matvec_q8act(t, raws[2], n_embd, n_ff, hcodes, hscales)
+        assert np.array_equal(y_all[c], want), c

@@ -186,3 +186,53 @@ def test_f32_prefill_equals_single_column(be, t, n_out, n_in, k):
     want = np.stack([be.matvec_f32(tensor, x[c]) for c in range(k)])
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
     tensor.free()
+
+
+@pytest.mark.parametrize("t,n_out,n_in,k,e0,spread", [
+    (Q4_K, 512, 2816, 8, 34, 4), (Q4_K, 256, 28672, 8, 34, 4), (Q8_0, 384, 1024, 6, 40, 4),
+    (Q6_K, 256, 1024, 5, 30, 4),
+    (Q4_K, 384, 2816, 100, 30, 9),    # spreads 8..9: the third activation digit's second pass
+    (Q8_0, 300, 1024, 70, 30, 14),    # up to 14
+    (Q6_K, 256, 1024, 9, 20, 12),
+])
+def test_device_descriptors_and_large_exponents(be, t, n_out, n_in, k, e0, spread):
+    """apx_matmat_async with descriptors computed on the device (apx_act_describe_cols_async), on
+    activations whose scales are 2^e0 .. 2^(e0 + spread) (hidden activations of an FFN, whose
+    spread exceeds two activation digits for some tokens), against the oracle column by column;
+    a few tokens with a narrow spread ride in the same tiles."""
+    import torch
+
+    lib = be.lib
+    dev = torch.device("cuda:0")
+    stream = torch.cuda.current_stream().cuda_stream
+    raw = synth.payload(t, n_out, n_in, 5 + n_in)
+    tensor = be._tensor(t, raw, n_out, n_in)
+    rng = np.random.default_rng(e0)
+    nb = n_in // 32
+    pad = lib.apx_act_padded_len(n_in)
+    codes = np.zeros((k, pad), np.int8)
+    exps = np.full((k, pad // 32), 0xFF, np.uint8)
+    for c in range(k):
+        codes[c, :n_in] = rng.integers(-127, 128, n_in)
+        exps[c, :nb] = e0 + rng.integers(0, 5 if c % 3 == 0 else spread + 1, nb)
+        exps[c, 0] = e0  # the spread is reached
+    dc, de = torch.from_numpy(codes).to(dev), torch.from_numpy(exps).to(dev)
+    dd = torch.zeros(8 * k, dtype=torch.int32, device=dev)
+    y = torch.zeros(k * n_out, dtype=torch.int64, device=dev)
+    ys = torch.full((2 * k,), -1, dtype=torch.int64, device=dev)
+    assert lib.apx_act_describe_cols_async(be.ctx, dc.data_ptr(), de.data_ptr(), n_in, k,
+                                           dd.data_ptr(), stream) == 0
+    assert lib.apx_matmat_async(be.ctx, tensor.handle, n_out, n_in, k, dc.data_ptr(),
+                                de.data_ptr(), dd.data_ptr(), y.data_ptr(), None, ys.data_ptr(),
+                                stream) == 0
+    torch.cuda.synchronize()
+    got = y.cpu().numpy().reshape(k, n_out)
+    sc = [O.exps_to_scales(exps[c, :nb]) for c in range(k)]
+    want = O.matmat_q8act(t, raw, n_out, n_in, codes[:, :n_in], np.stack(sc))
+    if isinstance(want, tuple):
+        assert int(ys[0::2].min().item()) != -1
+        return
+    assert bool((ys[0::2] == -1).all().item())
+    bad = np.argwhere(got != want)
+    assert bad.size == 0, (f"{len(bad)} differ; first col {bad[0][0]} row {bad[0][1]}: gpu "
+                           f"{got[tuple(bad[0])]} oracle {want[tuple(bad[0])]}")
