@@ -40,13 +40,14 @@ EXPORTS = [
     "apx_tensor_device_bytes", "apx_matvec_q8act", "apx_matvec_q8act_chunked",
     "apx_matmat_q8act", "apx_quant_act", "apx_matvec_f32", "apx_debug_block_dots",
     "apx_act_describe_async", "apx_quant_q32_async", "apx_quant_f32_async",
-    "apx_matvec_async", "apx_matmat_async", "apx_matmat_f32_async", "apx_act_padded_len", "apx_status_decode",
+    "apx_matvec_async", "apx_matmat_async", "apx_matmat_f32_async", "apx_act_padded_len", "apx_status_decode", "apx_status_decode_rows",
     "apx_matvec_f32_noalloc", "apx_matmat_f32", "apx_quant_f32_cols_async",
     "apx_peer_alloc", "apx_peer_open", "apx_peer_close", "apx_device_read",
     "apx_gather_publish_async", "apx_matvec_gather_async", "apx_matvec_group_async",
     "apx_swiglu_quant_async", "apx_swiglu_quant_cols_async", "apx_act_describe_cols_async",
-    "apx_ffn_status_decode",
+    "apx_ffn_status_decode", "apx_plan_create", "apx_plan_run_async", "apx_plan_destroy",
 ]
+PLAN_GATE, PLAN_UP = 0, 1
 CARRIER_F32, CARRIER_Q32 = 0, 1
 
 MAX_PEERS = 8
@@ -97,6 +98,23 @@ class CallStatus(C.Structure):
 
 
 P = C.c_void_p
+class PlanAct(C.Structure):
+    _fields_ = [("d_codes", C.c_void_p), ("d_exps", C.c_void_p), ("d_desc", C.c_void_p),
+                ("ffn", C.c_int32), ("reserved", C.c_int32)]
+
+
+class PlanProj(C.Structure):
+    _fields_ = [("tensor", C.c_uint64), ("n_out", C.c_size_t), ("n_in", C.c_size_t),
+                ("act", C.c_int32), ("ffn", C.c_int32), ("role", C.c_int32),
+                ("reserved", C.c_int32), ("d_out_q32", C.c_void_p), ("d_out_f32", C.c_void_p),
+                ("d_status", C.c_void_p)]
+
+
+class PlanFfn(C.Structure):
+    _fields_ = [("carrier", C.c_int32), ("out_act", C.c_int32), ("d_h", C.c_void_p),
+                ("d_status", C.c_void_p)]
+
+
 SZ = C.c_size_t
 U64 = C.c_uint64
 EP = C.POINTER(ApxErr)
@@ -130,10 +148,15 @@ _SIGS = {
     "apx_matmat_f32_async": (C.c_int, [P, U64, SZ, SZ, SZ, P, SZ, P, P, P, P]),
     "apx_act_padded_len": (SZ, [SZ]),
     "apx_status_decode": (C.c_int, [P, U64, C.POINTER(CallStatus), EP]),
+    "apx_status_decode_rows": (C.c_int, [P, U64, SZ, C.POINTER(CallStatus), EP]),
     "apx_swiglu_quant_async": (C.c_int, [P, P, P, SZ, C.c_int, P, P, P, P, P, P]),
     "apx_swiglu_quant_cols_async": (C.c_int, [P, P, P, SZ, SZ, C.c_int, P, P, P, P, P, P]),
     "apx_act_describe_cols_async": (C.c_int, [P, P, P, SZ, SZ, P, P]),
     "apx_ffn_status_decode": (C.c_int, [C.POINTER(CallStatus), EP]),
+    "apx_plan_create": (P, [P, C.POINTER(PlanProj), SZ, C.POINTER(PlanAct), SZ,
+                            C.POINTER(PlanFfn), SZ, EP]),
+    "apx_plan_run_async": (C.c_int, [P, P]),
+    "apx_plan_destroy": (None, [P]),
     "apx_matvec_f32_noalloc": (C.c_int, [P, U64, SZ, SZ, P, P, P, P]),
     "apx_matmat_f32": (C.c_int, [P, U64, SZ, SZ, SZ, P, P, EP]),
     "apx_quant_f32_cols_async": (C.c_int, [P, P, SZ, SZ, P, P, P, P]),

@@ -17,7 +17,7 @@ CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libapeiron_cuda.so")
 SOURCES = ["apx_runtime.cu", "apx_gemv.cu", "apx_quant.cu", "apx_gemm.cu", "apx_lgemm.cu", "apx_ffn.cu",
            "apx_noalloc.cu",
-           "apx_peer.cu"]
+           "apx_peer.cu", "apx_plan.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

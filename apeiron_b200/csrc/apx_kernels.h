@@ -5,6 +5,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <vector>
 
 namespace apx {
 
@@ -167,8 +168,52 @@ cudaError_t launch_swiglu_quant_cols(const long long *gate, const long long *up,
                                      void *desc, unsigned long long *status, void *work,
                                      cudaStream_t stream);
 
+// Step plans (apx_plan.cu): the projections of a decode step, and the FFNs among them whose
+// finish runs SwiGLU + quant_act, in one persistent launch.  All projections of one plan share a
+// family; each reads its tensor in the tensor's own repacked layout (plan = its GemvPlan).
+constexpr int kPlanMaxProj = 4096, kPlanMaxFfn = 64;
+struct PlanCtl {  // zero between launches (the launch's last warp resets it)
+  unsigned queue, exit, abort, pad;
+  unsigned ready[kPlanMaxFfn];   // blocks of the FFN's h quantized
+  unsigned flag[kPlanMaxFfn];    // the FFN's descriptor published
+  int stats[kPlanMaxFfn][4];     // 63 - emin (max), emax + 1 (max), status (max), nz (sum)
+};
+struct PlanSpec {
+  struct Proj {
+    uint32_t type;
+    const uint8_t *pack;
+    GemvPlan plan;
+    size_t n_out, n_in;
+    int act, ffn, role;  // ffn: -1 or the FFN this projection feeds as gate (0) or up (1)
+    long long *out_q32;
+    float *out_f32;
+    unsigned long long *status;
+  };
+  struct Act {
+    const int8_t *codes;
+    const uint8_t *exps;
+    const void *desc;  // ActDesc
+    int ffn;           // -1: ready when the launch starts; else the FFN that writes it
+  };
+  struct Ffn {
+    int carrier, out_act;
+    long long *h;                // or null
+    unsigned long long *status;  // the first refusing SwiGLU lane
+    bool refused;                // gate or up holds a non-finite scale below the width
+  };
+  std::vector<Proj> projs;
+  std::vector<Act> acts;
+  std::vector<Ffn> ffns;
+};
+struct PlanHost;
+int plan_build(const PlanSpec &s, int sm_count, PlanHost **out);  // an APX_ERR_* code
+cudaError_t plan_run(const PlanHost &h, cudaStream_t stream, bool pdl);
+void plan_free(PlanHost *h);
+
 // GEMV launches from the calling thread go without programmatic dependent launch while set.
 void set_pdl_suppressed(bool on);
+// Whether a launch from this thread may carry programmatic dependent launch now.
+bool pdl_allowed();
 
 // Debug: exact int32 group dots from the repacked layout (apx_gemv.cu).
 cudaError_t launch_block_dots(const GemvPlan &pl, uint32_t type, const uint8_t *pack,

@@ -1,0 +1,848 @@
+// apx_plan.cu — the projections of a decode step in one persistent launch.
+//
+// A plan lists projections (a tensor, its activation, its outputs) in dependency order, and
+// optionally FFNs: a gate and an up projection of one activation whose finish runs SwiGLU and
+// quant_act (the SwiGLU and quantization stages of fused_ffn_task,
+// src/engine/chart/ffn.rs:1577-1594) into an activation a later projection reads (down).  One
+// launch of a persistent grid runs the whole list; each projection's outputs, refusals and
+// rounding are those of apx_matvec_async on the same inputs (matvec_q8act,
+// chart/mod.rs:1887-1925), each FFN's those of apx_swiglu_quant_async.
+//
+// Work.  Every projection's row tiles are cut into pieces of at most kPlanPiece units of the
+// tensor's repacked layout (fewer for a short plan); the pieces of all projections form one
+// queue, and warp v of the V in the grid takes pieces v, v + V, v + 2V, ... in order (no shared
+// counter: a counter on one address serialises every warp's take).  A warp streams its pieces'
+// units through a ring in shared memory (1D bulk copies, two units in flight while one folds; the
+// first piece's copies start before the wait for the previous kernel) and folds each exactly as
+// the one-wave GEMV kernel does; a row tile of one piece finishes in the warp, a row tile of
+// several through partial sums in the plan's scratch and a self-resetting arrival counter (the
+// last to arrive finishes it).
+//
+// Hand-off.  The finish of a gate or up row tile (32 rows: one quant_act block of h) counts on a
+// per-block counter; the second of the two runs SwiGLU under the carrier and quant_act for the
+// block and adds the block's exponent statistics to the FFN's; the last block publishes the
+// descriptor and raises the FFN's flag.  A warp that takes a piece reading that activation waits
+// on the flag first, with a bound (about one second) after which the projection refuses with
+// APX_ERR_DEVICE_TIMEOUT.  The host queues each reader of an FFN two grid-rounds (2V pieces)
+// after the FFN's last piece when other work can fill the gap, so the flag is usually up when a
+// warp gets there.  A warp waits only at the start of a piece with nothing unfinished, and every
+// piece a wait depends on sits earlier in the queue: by induction on queue position the earliest
+// waiting piece's producers belong to warps that reach them, since the grid is sized to be
+// co-resident.  The last CTA out resets the counters and flags for the next launch.
+#include <algorithm>
+#include <climits>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "apx_common.cuh"
+#include "apx_kernels.h"
+#include "apx_pack.cuh"
+#include "apx_quant.cuh"
+#include "apx_swiglu.cuh"
+#include "apx_unit.cuh"
+
+namespace apx {
+
+namespace {
+
+constexpr int kPlanPiece = 8;  // units per piece at most
+
+struct PlanProjD {
+  const uint8_t *pack;
+  long long *out_q32;
+  float *out_f32;
+  unsigned long long *status;
+  Acc128 *part;   // [n_rt][npieces][32] when npieces > 1
+  unsigned *cnt;  // [n_rt] arrivals (self-resetting) when npieces > 1
+  size_t n_out, n_in;
+  int n_rt, U, L, plen, npieces, piece0;
+  int act, ffn;  // activation read; FFN fed (-1 for none)
+};
+
+struct PlanActD {
+  const int8_t *codes;
+  const uint8_t *exps;
+  const ActDesc *desc;
+  int ffn;  // the FFN of this launch that writes it, or -1 (ready when the launch starts)
+  int pad;
+};
+
+struct PlanFfnD {
+  const long long *gate, *up;  // the gate and up projections' Q32.32 outputs
+  const unsigned long long *gate_status, *up_status;
+  long long *h;  // or null
+  int8_t *codes;
+  uint8_t *exps;
+  ActDesc *desc;
+  unsigned long long *status;  // the first refusing SwiGLU lane
+  unsigned *pair;              // [n_rt] row tiles of the block done (self-resetting)
+  size_t n;
+  int n_rt, carrier, refused;  // refused: a non-finite weight row below n (found at upload)
+  int pad;
+};
+
+struct PlanArgs {
+  const PlanProjD *proj;
+  const PlanActD *act;
+  const PlanFfnD *ffn;
+  PlanCtl *ctl;
+  int n_proj, n_ffn, total, V;
+};
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Chunk c of an activation written in this launch: L2-coherent loads (the read-only path could
+// hold a line from before the writer's store).
+__device__ __forceinline__ Chunk load_chunk_cg(const int8_t *codes, const uint8_t *exps,
+                                               size_t n_in, size_t j) {
+  Chunk s{make_uint4(0, 0, 0, 0), APX_EXP_ZERO};
+  if (j < n_in) {
+    s.e = __ldcg(exps + j / 32);
+    if (j + 16 <= n_in && ((reinterpret_cast<uintptr_t>(codes + j) & 15) == 0)) {
+      s.v = __ldcg(reinterpret_cast<const uint4 *>(codes + j));
+    } else {
+      unsigned t[4] = {0, 0, 0, 0};
+      for (int i = 0; i < 16; i++)
+        if (j + i < n_in) t[i / 4] |= ((unsigned)(uint8_t)__ldcg(codes + j + i)) << (8 * (i % 4));
+      s.v = make_uint4(t[0], t[1], t[2], t[3]);
+    }
+  }
+  return s;
+}
+
+struct Piece {
+  int j, rt, q, u0, u1;
+};
+
+__device__ __forceinline__ Piece decode_piece(const PlanArgs &g, const int *p0, int x) {
+  int lo = 0, hi = g.n_proj - 1;  // the last projection whose first piece is <= x
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) / 2;
+    if (p0[mid] <= x) lo = mid;
+    else hi = mid - 1;
+  }
+  const PlanProjD &P = g.proj[lo];
+  const int local = x - p0[lo], np = P.npieces, plen = P.plen;
+  Piece pc;
+  pc.j = lo;
+  pc.rt = local / np;
+  pc.q = local % np;
+  pc.u0 = pc.q * plen;
+  pc.u1 = min(P.U, pc.u0 + plen);
+  return pc;
+}
+
+template <uint32_t T>
+__device__ __forceinline__ const uint8_t *unit_ptr(const PlanProjD &P, int rt, int u) {
+  return P.pack + ((size_t)rt * P.U + u) * (size_t)Fam<T>::unit_bytes;
+}
+
+// SwiGLU + quant_act of block rt of FFN f (lane = row), its statistics, and — for the last
+// block — the descriptor and the flag.  Mirrors swiglu_quant_kernel and ffn_desc_kernel.
+__device__ void ffn_block(const PlanArgs &g, int f, int rt, int lane) {
+  const PlanFfnD &F = g.ffn[f];
+  const size_t row = (size_t)rt * 32 + lane;
+  long long v = 0;
+  bool ok = true;
+  if (row < F.n) {
+    const int rc = swiglu_dev(__ldcg(F.gate + row), __ldcg(F.up + row), F.carrier, v);
+    if (rc) {
+      ok = false;
+      v = 0;
+      atomicMin(F.status, pack_status(row, APX_ERR_SWIGLU_REFUSED, (unsigned)rc));
+    }
+    if (F.h) F.h[row] = v;
+  }
+  unsigned long long mx = uabs64(v);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long t = __shfl_xor_sync(0xFFFFFFFFu, mx, o);
+    mx = t > mx ? t : mx;
+  }
+  const int e = act_scale_exp(mx);
+  int w_status = __any_sync(0xFFFFFFFFu, !ok) ? (int)APX_ERR_QUANT_REFUSED : (int)APX_OK;
+  int code = 0;
+  if (e == 99) {
+    w_status = APX_ERR_QUANT_REFUSED;
+  } else if (e >= 0) {
+    const unsigned long long m = uabs64(v);
+    const unsigned long long S = 1ull << e, qq = m >> e, r = m & (S - 1);
+    const unsigned long long mag = qq + (2 * r >= S ? 1ull : 0ull);
+    code = v < 0 ? -(int)mag : (int)mag;
+    if (__any_sync(0xFFFFFFFFu, mag > 127 || !product_fits(code, e)))
+      w_status = APX_ERR_QUANT_REFUSED;
+  }
+  if (row < F.n) F.codes[row] = (int8_t)code;
+  if (lane == 0) F.exps[rt] = e < 0 || e == 99 ? (uint8_t)APX_EXP_ZERO : (uint8_t)e;
+  __threadfence();  // every lane's stores before the block counts
+  __syncwarp();
+  int *st = g.ctl->stats[f];
+  if (lane == 0) {
+    // one address per statistic and FFN: an atomic only where it can change the value
+    if (w_status != APX_OK) atomicMax(st + 2, w_status);
+    if (e >= 0 && e != 99) {
+      if (__ldcg(st + 0) < 63 - e) atomicMax(st + 0, 63 - e);
+      if (__ldcg(st + 1) < e + 1) atomicMax(st + 1, e + 1);
+      atomicAdd(st + 3, 1);
+    }
+    __threadfence();
+    const unsigned done = atomicAdd(&g.ctl->ready[f], 1u);
+    if (done == (unsigned)F.n_rt - 1) {
+      // every block is in: every row tile of gate and up has finished (its outputs and its
+      // refusals were stored before its count), so their status words are final too
+      __threadfence();
+      const int nemin = atomicAdd(st + 0, 0), emax1 = atomicAdd(st + 1, 0);
+      int status = atomicAdd(st + 2, 0);
+      const unsigned nz = (unsigned)atomicAdd(st + 3, 0);
+      if (F.refused || __ldcg(F.gate_status) != ~0ull || __ldcg(F.up_status) != ~0ull)
+        status = max(status, (int)APX_ERR_QUANT_REFUSED);  // h is undefined where they refused
+      ActDesc d;
+      d.status = status;
+      d.emax = emax1 - 1;
+      d.emin = emax1 > 0 ? 63 - nemin : 0;
+      d.n_in = (int32_t)F.n;
+      d.nz = nz;
+      d.pad[0] = 0;  // quant_act codes are never -128
+      d.pad[1] = 0;
+      d.pad[2] = 0;
+      *F.desc = d;
+      __threadfence();
+      atomicExch(&g.ctl->flag[f], 1u);
+    }
+  }
+}
+
+// Wait for FFN f's descriptor: about one second at most, and none at all once a wait of this
+// launch has given up (the launch's later readers then refuse at once).
+__device__ __forceinline__ bool wait_flag(const PlanArgs &g, int f) {
+  if (ld_acquire(&g.ctl->flag[f])) return true;
+  unsigned long long t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (int it = 0; it < kWaitLimit; it++) {
+    __nanosleep(128);
+    if (ld_acquire(&g.ctl->flag[f])) return true;
+    if ((it & 15) == 15) {
+      if (ld_acquire(&g.ctl->abort)) return false;
+      unsigned long long now;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+      if (now - t0 > 1000000000ull) break;
+    }
+  }
+  atomicExch(&g.ctl->abort, 1u);
+  return false;
+}
+
+// Launch shape per family: warps per CTA, CTAs per SM, weight ring slots per warp.  Each warp
+// streams its units through a ring of kSlots unit buffers in shared memory, filled by 1D bulk
+// copies (cp.async.bulk, no multicast) that complete on one mbarrier per slot: kSlots - 1 units
+// in flight while one folds.
+template <uint32_t T>
+struct PlanShape {
+  static constexpr int kWarps = T == kQ6_K ? 8 : 6;
+  static constexpr int kCtas = T == kQ6_K ? 1 : 2;
+  static constexpr int kSlots = 3;
+  static constexpr int kUnit = Fam<T>::unit_bytes;
+  static constexpr int kThreads = 32 * kWarps;
+  static_assert(kUnit % 16 == 0, "bulk copies move whole 16-byte chunks");
+};
+
+template <uint32_t T>
+__host__ __device__ constexpr size_t plan_ring_bytes() {
+  return (size_t)PlanShape<T>::kWarps * PlanShape<T>::kSlots * PlanShape<T>::kUnit;
+}
+template <uint32_t T>
+__host__ __device__ constexpr size_t plan_fixed_smem() {  // ring, barriers, activation slots
+  return plan_ring_bytes<T>() + (size_t)PlanShape<T>::kWarps * PlanShape<T>::kSlots * 8 +
+         (size_t)2 * PlanShape<T>::kWarps * sizeof(WarpAct<T>);
+}
+
+// The order-fence between this thread's reads of a ring slot and the bulk copy that refills it.
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// One warp's stream of units: the units of its current piece, then those of the piece it took
+// next.  k_issue / k_fold count units copied / folded; unit k sits in slot k % kSlots, and its
+// copy completes phase (k / kSlots) & 1 of that slot's barrier.
+template <uint32_t T>
+struct UnitStream {
+  uint8_t *ring;   // this warp's kSlots buffers
+  uint64_t *bars;  // their barriers
+  int k_issue, k_fold;
+  int nxt_on;      // the issue cursor is in the next piece
+  int iu;          // the issue cursor's unit
+
+  // Copy units ahead while slots are free: the rest of `pc`, then `pn` when it exists.
+  __device__ __forceinline__ void top_up(const PlanArgs &g, const Piece &pc, const Piece &pn,
+                                         bool have_next, int lane) {
+    constexpr int S = PlanShape<T>::kSlots;
+    while (k_issue - k_fold < S) {
+      const Piece &p = nxt_on ? pn : pc;
+      if (iu >= p.u1) {
+        if (nxt_on || !have_next) break;
+        nxt_on = 1;
+        iu = pn.u0;
+        continue;
+      }
+      if (lane == 0) {
+        const int s = k_issue % S;
+        mbar_expect_tx(bars + s, PlanShape<T>::kUnit);
+        bulk_g2s(ring + (size_t)s * PlanShape<T>::kUnit, unit_ptr<T>(g.proj[p.j], p.rt, iu),
+                 PlanShape<T>::kUnit, bars + s);
+      }
+      iu++;
+      k_issue++;
+    }
+  }
+
+  // The next unit's slot, once its copy has landed (bounded: false when the wait gave up).
+  __device__ __forceinline__ bool wait_front(uint8_t *&slot) {
+    constexpr int S = PlanShape<T>::kSlots;
+    const int s = k_fold % S;
+    slot = ring + (size_t)s * PlanShape<T>::kUnit;
+    return mbar_wait(bars + s, (uint32_t)((k_fold / S) & 1));
+  }
+
+  // Hand the front slot back after the warp read it: the next copy may refill it.
+  __device__ __forceinline__ void release_front() {
+    fence_proxy_async();
+    __syncwarp();
+    k_fold++;
+  }
+
+  // The piece the stream moves on to: the issue cursor leaves the finished piece.
+  __device__ __forceinline__ void advance(const Piece &next) {
+    if (nxt_on) {
+      nxt_on = 0;
+    } else {
+      iu = next.u0;
+    }
+  }
+};
+
+template <uint32_t T>
+__global__ void __launch_bounds__(PlanShape<T>::kThreads, PlanShape<T>::kCtas)
+    plan_kernel(PlanArgs g) {
+  using F = Fam<T>;
+  using SH = PlanShape<T>;
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + plan_ring_bytes<T>()) + warp * SH::kSlots;
+  WarpAct<T> *wa = reinterpret_cast<WarpAct<T> *>(smem + plan_ring_bytes<T>() +
+                                                  (size_t)SH::kWarps * SH::kSlots * 8) +
+                   2 * warp;
+  int *s_p0 = reinterpret_cast<int *>(smem + plan_fixed_smem<T>());
+  for (int i = threadIdx.x; i < g.n_proj; i += blockDim.x) s_p0[i] = g.proj[i].piece0;
+  if (lane == 0)
+    for (int s = 0; s < SH::kSlots; s++) mbar_init(bars + s, 1);
+  __syncthreads();
+  // the first pieces go one per CTA before any CTA takes a second, so a short plan spreads
+  // over every SM
+  const int v = warp * (int)gridDim.x + (int)blockIdx.x;
+
+  pdl_launch_dependents();
+  UnitStream<T> us{smem + (size_t)warp * SH::kSlots * SH::kUnit, bars, 0, 0, 0, 0};
+  int x = v < g.total ? v : -1;
+  Piece pc{0, 0, 0, 0, 0}, pn{0, 0, 0, 0, 0};
+  if (x >= 0) {  // the first piece is static: its weights stream in before the wait
+    pc = decode_piece(g, s_p0, x);
+    us.iu = pc.u0;
+    us.top_up(g, pc, pn, false, lane);
+  }
+  pdl_wait();
+
+  const Chunk zero_chunk{make_uint4(0, 0, 0, 0), APX_EXP_ZERO};
+  auto fetch = [&](const PlanProjD &Q, const PlanActD &B, int u, Chunk &a0, Chunk &a1) {
+    const int nq = Q.L * F::span / 16;
+    a0 = zero_chunk;
+    a1 = zero_chunk;
+    if (B.ffn >= 0) {
+      if (lane < nq) a0 = load_chunk_cg(B.codes, B.exps, Q.n_in, chunk_first<T>(u, Q.L, lane));
+      if (lane + 32 < nq)
+        a1 = load_chunk_cg(B.codes, B.exps, Q.n_in, chunk_first<T>(u, Q.L, lane + 32));
+    } else {
+      if (lane < nq) a0 = load_chunk(B.codes, B.exps, Q.n_in, chunk_first<T>(u, Q.L, lane));
+      if (lane + 32 < nq)
+        a1 = load_chunk(B.codes, B.exps, Q.n_in, chunk_first<T>(u, Q.L, lane + 32));
+    }
+  };
+  Chunk c0 = zero_chunk, c1 = zero_chunk;
+  bool act_pre = false;  // c0/c1 already hold the current piece's first activation chunk
+
+  while (x >= 0) {
+    const PlanProjD &P = g.proj[pc.j];
+    const int L = P.L, H = 32 / L, slot = lane % L;
+    const int nch = L * F::span / 16;
+    const PlanActD &A = g.act[P.act];
+    const bool produced = A.ffn >= 0;
+    bool ready = true;
+    if (produced) {  // before taking the next piece: a waiting warp holds no later work
+      int r = 1;
+      if (lane == 0) r = wait_flag(g, A.ffn) ? 1 : 0;
+      ready = __shfl_sync(0xFFFFFFFFu, r, 0) != 0;
+      __syncwarp();  // every lane's reads of the activation come after the acquire
+    }
+    ActDesc desc;
+    if (produced) {
+      const int4 d0 = __ldcg(reinterpret_cast<const int4 *>(A.desc));
+      const int4 d1 = __ldcg(reinterpret_cast<const int4 *>(A.desc) + 1);
+      memcpy(&desc, &d0, 16);
+      memcpy(reinterpret_cast<char *>(&desc) + 16, &d1, 16);
+    } else {
+      desc = *A.desc;
+    }
+    // the next piece of this warp's sequence: its weights follow this piece's through the ring
+    const int xn = x + g.V < g.total ? x + g.V : -1;
+    if (xn >= 0) pn = decode_piece(g, s_p0, xn);
+    us.top_up(g, pc, pn, xn >= 0, lane);
+
+    const bool fast = ready && desc.status == APX_OK && fast_path<T>(desc, P.n_in);
+    if (fast && !act_pre) fetch(P, A, pc.u0, c0, c1);
+    bool next_pre = false, copies_ok = true;
+    Acc128 acc;
+    acc_zero(acc);
+    for (int u = pc.u0; u < pc.u1; u++) {
+      uint8_t *sl;
+      const bool got = us.wait_front(sl);
+      copies_ok = copies_ok && got;
+      UnitRegs<T> w;
+      if (fast) load_unit_smem(w, sl, lane);
+      us.release_front();
+      us.top_up(g, pc, pn, xn >= 0, lane);
+      if (!fast) continue;  // the slot is consumed all the same
+      WarpAct<T> &wb = wa[u & 1];
+      store_chunk<T>(wb, c0, lane, lane < nch, desc.emin);
+      if (nch > 32) store_chunk<T>(wb, c1, lane + 32, lane + 32 < nch, desc.emin);
+      __syncwarp();
+      if (u + 1 < pc.u1) {
+        fetch(P, A, u + 1, c0, c1);
+      } else if (xn >= 0) {  // the next piece's first chunk, when its activation is ready now
+        const PlanProjD &Q = g.proj[pn.j];
+        const PlanActD &B = g.act[Q.act];
+        int r = 1;
+        if (B.ffn >= 0 && lane == 0) r = ld_acquire(&g.ctl->flag[B.ffn]) ? 1 : 0;
+        r = __shfl_sync(0xFFFFFFFFu, r, 0);
+        __syncwarp();
+        if (r) {
+          fetch(Q, B, pn.u0, c0, c1);
+          next_pre = true;
+        }
+      }
+      fold_unit(acc, w, wb.codes + slot * slot_ints<T>(), wb.e + slot * (F::span / 32),
+                wb.xs + slot * F::nxs, desc.emin);
+    }
+    const bool lead = pc.q == 0;  // the piece that speaks for its row tile off the fast path
+    bool done = false;            // this warp completed the row tile
+    if (!copies_ok) {             // a weight copy did not land in time
+      if (lane == 0) {
+        atomicExch(&g.ctl->abort, 1u);
+        atomicMin(P.status, pack_status(0, APX_ERR_DEVICE_TIMEOUT, 0));
+      }
+      done = lead;
+    } else if (!ready) {
+      if (lead && lane == 0) atomicMin(P.status, pack_status(0, APX_ERR_DEVICE_TIMEOUT, 0));
+      done = lead;
+    } else if (desc.status != APX_OK) {  // the activation is refused (chart/mod.rs:1904-1907)
+      if (lead && pc.rt == 0 && lane == 0)
+        atomicMin(P.status, pack_status(0, (unsigned)desc.status, 0));
+      done = lead;
+    } else if (!fast) {
+      if (lead && slot == 0)
+        checked_row<T>(PackGeo{P.pack, P.U, L}, (size_t)pc.rt * H + lane / L, P.n_out, P.n_in,
+                       A.codes, A.exps, P.out_q32, P.out_f32, P.status);
+      done = lead;
+    } else {
+      for (int o = 1; o < L; o <<= 1) {  // the L lanes of a row combine
+        const unsigned long long lo = __shfl_xor_sync(0xFFFFFFFFu, acc.lo, o);
+        const unsigned long long hi = __shfl_xor_sync(0xFFFFFFFFu, acc.hi, o);
+        acc_add(acc, lo, hi);
+      }
+      bool fin = P.npieces == 1;
+      if (!fin) {
+        Acc128 *dst = P.part + ((size_t)pc.rt * P.npieces + pc.q) * 32 + lane;
+        dst->lo = acc.lo;
+        dst->hi = acc.hi;
+        __threadfence();
+        __syncwarp();
+        unsigned ticket = 0;
+        if (lane == 0) ticket = atomicAdd(P.cnt + pc.rt, 1u);
+        ticket = __shfl_sync(0xFFFFFFFFu, ticket, 0);
+        fin = ticket == (unsigned)P.npieces - 1;
+        if (fin) {
+          __threadfence();
+          acc_zero(acc);
+          for (int qq = 0; qq < P.npieces; qq++) {
+            const Acc128 *src = P.part + ((size_t)pc.rt * P.npieces + qq) * 32 + lane;
+            acc_add(acc, __ldcg(&src->lo), __ldcg(&src->hi));
+          }
+          if (lane == 0) P.cnt[pc.rt] = 0u;  // ready for the next launch
+        }
+      }
+      if (fin && slot == 0)
+        finish_row(acc, (size_t)pc.rt * H + lane / L, P.n_out, P.out_q32, P.out_f32, P.status,
+                   PeerRows{});
+      done = fin;
+    }
+    // -- the FFN hand-off: the second of a block's gate and up row tiles runs its SwiGLU --
+    if (done && P.ffn >= 0) {
+      __threadfence();
+      __syncwarp();
+      unsigned old = 0;
+      if (lane == 0) old = atomicAdd(g.ffn[P.ffn].pair + pc.rt, 1u);
+      old = __shfl_sync(0xFFFFFFFFu, old, 0);
+      if (old == 1) {
+        if (lane == 0) g.ffn[P.ffn].pair[pc.rt] = 0u;  // ready for the next launch
+        __threadfence();
+        ffn_block(g, P.ffn, pc.rt, lane);
+      }
+    }
+    if (!copies_ok) break;  // the ring's phases are lost: this warp stops
+    if (xn >= 0) us.advance(pn);
+    x = xn;
+    pc = pn;
+    act_pre = next_pre;
+  }
+
+  // no copy may land in this CTA's shared memory after it exits
+  while (us.k_fold < us.k_issue) {
+    uint8_t *sl;
+    us.wait_front(sl);
+    us.k_fold++;
+  }
+  // the last CTA out resets the launch's counters and flags
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (atomicAdd(&g.ctl->exit, 1u) == gridDim.x - 1) {
+      g.ctl->queue = 0u;
+      g.ctl->abort = 0u;
+      for (int f = 0; f < g.n_ffn; f++) {
+        g.ctl->ready[f] = 0u;
+        g.ctl->flag[f] = 0u;
+        for (int k = 0; k < 4; k++) g.ctl->stats[f][k] = 0;
+      }
+      __threadfence();
+      g.ctl->exit = 0u;
+    }
+  }
+}
+
+}  // namespace
+
+
+// ---- host ---------------------------------------------------------------------------------------
+
+struct PlanHost {
+  uint32_t type = 0;
+  int n_proj = 0, n_ffn = 0, total = 0;
+  unsigned grid = 0;
+  int block = 0;
+  size_t smem = 0;
+  void *dev = nullptr;  // records, control block and scratch in one allocation
+  PlanProjD *proj = nullptr;
+  PlanActD *act = nullptr;
+  PlanFfnD *ffn = nullptr;
+  PlanCtl *ctl = nullptr;
+};
+
+namespace {
+
+size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+template <uint32_t T>
+cudaError_t plan_geometry(int n_proj, int sm_count, unsigned &grid, int &block, size_t &smem) {
+  block = PlanShape<T>::kThreads;
+  smem = plan_fixed_smem<T>() + (((size_t)n_proj * 4 + 15) & ~(size_t)15);
+  cudaError_t e = cudaFuncSetAttribute(plan_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, plan_kernel<T>, block, smem);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) return cudaErrorInvalidConfiguration;
+  per_sm = std::min(per_sm, PlanShape<T>::kCtas);
+  grid = (unsigned)(sm_count * per_sm);  // co-resident: every wait ends
+  return cudaSuccess;
+}
+
+template <uint32_t T>
+cudaError_t plan_launch(const PlanHost &h, const PlanArgs &a, cudaStream_t stream, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(h.grid);
+  cfg.blockDim = dim3(h.block);
+  cfg.dynamicSmemBytes = h.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, plan_kernel<T>, a);
+}
+
+// Records of one plan, checked: the FFNs' gate and up projections (index per FFN), and for every
+// projection the FFN whose activation it reads (-1 for a resident one).
+int plan_check(const PlanSpec &s, std::vector<int> &gate, std::vector<int> &up,
+               std::vector<int> &reads) {
+  const int n_proj = (int)s.projs.size(), n_act = (int)s.acts.size(), n_ffn = (int)s.ffns.size();
+  if (n_proj < 1 || n_proj > kPlanMaxProj || n_ffn > kPlanMaxFfn) return APX_ERR_INVALID_ARGUMENT;
+  const uint32_t type = s.projs[0].type;
+  for (const PlanSpec::Act &x : s.acts)
+    if (!x.codes || !x.exps || !x.desc || x.ffn < -1 || x.ffn >= n_ffn)
+      return APX_ERR_INVALID_ARGUMENT;
+  reads.assign(n_proj, -1);
+  for (int i = 0; i < n_proj; i++) {
+    const PlanSpec::Proj &p = s.projs[i];
+    if (p.type != type || !p.pack || p.n_out == 0 || p.n_in == 0 || p.act < 0 ||
+        p.act >= n_act || p.ffn < -1 || p.ffn >= n_ffn || !p.status || p.plan.L < 1 ||
+        p.plan.units < 1)
+      return APX_ERR_INVALID_ARGUMENT;
+    reads[i] = s.acts[p.act].ffn;
+  }
+  gate.assign(n_ffn, -1);
+  up.assign(n_ffn, -1);
+  for (int i = 0; i < n_proj; i++) {
+    const PlanSpec::Proj &p = s.projs[i];
+    if (p.ffn < 0) continue;
+    if (p.role != 0 && p.role != 1) return APX_ERR_INVALID_ARGUMENT;
+    int &slot = p.role == 0 ? gate[p.ffn] : up[p.ffn];
+    if (slot != -1) return APX_ERR_INVALID_ARGUMENT;
+    slot = i;
+  }
+  for (int f = 0; f < n_ffn; f++) {
+    const PlanSpec::Ffn &x = s.ffns[f];
+    if (gate[f] < 0 || up[f] < 0 || x.out_act < 0 || x.out_act >= n_act ||
+        s.acts[x.out_act].ffn != f)
+      return APX_ERR_INVALID_ARGUMENT;
+    const PlanSpec::Proj &pg = s.projs[gate[f]], &pu = s.projs[up[f]];
+    if (pg.n_out != pu.n_out || pg.n_in != pu.n_in || pg.act != pu.act || pg.plan.L != 1 ||
+        pu.plan.L != 1 || !pg.out_q32 || !pu.out_q32)
+      return APX_ERR_INVALID_ARGUMENT;
+    // readers of the FFN's activation come after both of its projections, at its width
+    for (int i = 0; i < n_proj; i++)
+      if (reads[i] == f && (i <= std::max(gate[f], up[f]) || s.projs[i].n_in != pg.n_out))
+        return APX_ERR_INVALID_ARGUMENT;
+  }
+  return APX_OK;
+}
+
+}  // namespace
+
+int plan_build(const PlanSpec &s, int sm_count, PlanHost **out) {
+  *out = nullptr;
+  std::vector<int> gate, up, reads;
+  int rc = plan_check(s, gate, up, reads);
+  if (rc != APX_OK) return rc;
+  const int n_proj = (int)s.projs.size(), n_act = (int)s.acts.size(), n_ffn = (int)s.ffns.size();
+  const uint32_t type = s.projs[0].type;
+  unsigned grid = 0;
+  int block = 0;
+  size_t smem = 0;
+  cudaError_t e;
+  switch (type) {
+    case kQ8_0: e = plan_geometry<kQ8_0>(n_proj, sm_count, grid, block, smem); break;
+    case kQ4_K: e = plan_geometry<kQ4_K>(n_proj, sm_count, grid, block, smem); break;
+    case kQ6_K: e = plan_geometry<kQ6_K>(n_proj, sm_count, grid, block, smem); break;
+    default: return APX_ERR_INVALID_ARGUMENT;
+  }
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return APX_ERR_CUDA;
+  }
+  const long long V = (long long)grid * (block / 32);
+
+  // Pieces: at most kPlanPiece units, fewer when the plan is short, so that every warp of the
+  // grid gets about two.
+  std::vector<int> n_rt(n_proj), npieces(n_proj), plen(n_proj);
+  long long units = 0;
+  for (int i = 0; i < n_proj; i++) {
+    const PlanSpec::Proj &p = s.projs[i];
+    const int H = 32 / p.plan.L;
+    n_rt[i] = (int)((p.n_out + H - 1) / H);
+    units += (long long)n_rt[i] * p.plan.units;
+  }
+  const int plen_t = (int)std::max<long long>(1, std::min<long long>(kPlanPiece, units / (2 * V)));
+  long long total = 0;
+  for (int i = 0; i < n_proj; i++) {
+    const int U = s.projs[i].plan.units;
+    npieces[i] = (U + plen_t - 1) / plen_t;
+    plen[i] = (U + npieces[i] - 1) / npieces[i];
+    npieces[i] = (U + plen[i] - 1) / plen[i];
+    total += (long long)n_rt[i] * npieces[i];
+  }
+  if (total > INT_MAX / 2) return APX_ERR_TOO_LARGE;
+
+  // Queue order: the given order, except that a projection reading an FFN's activation waits
+  // until two grid-rounds of pieces (2V) have been queued after that FFN's last piece, when
+  // other work is there to fill the gap: the activation is then (nearly) ready when a warp
+  // takes it.
+  std::vector<int> order, pending;
+  std::vector<long long> ready_at(n_ffn, -1);
+  std::vector<int> producers_left(n_ffn, 2);
+  long long emitted = 0;
+  auto emit = [&](int i) {
+    order.push_back(i);
+    emitted += (long long)n_rt[i] * npieces[i];
+    const int f = s.projs[i].ffn;
+    if (f >= 0 && --producers_left[f] == 0) ready_at[f] = emitted + 2 * V;
+  };
+  auto flush = [&](bool all) {
+    for (bool moved = true; moved;) {
+      moved = false;
+      for (size_t k = 0; k < pending.size(); k++) {
+        const int f = reads[pending[k]];
+        if (all || (ready_at[f] >= 0 && ready_at[f] <= emitted)) {
+          const int i = pending[k];
+          pending.erase(pending.begin() + (long)k);
+          emit(i);
+          moved = true;
+          break;
+        }
+      }
+    }
+  };
+  for (int i = 0; i < n_proj; i++) {
+    const int f = reads[i];
+    if (f >= 0 && (ready_at[f] < 0 || ready_at[f] > emitted)) pending.push_back(i);
+    else emit(i);
+    flush(false);
+  }
+  flush(true);
+
+  // device records, in queue order
+  std::vector<PlanProjD> pd(n_proj);
+  std::vector<size_t> part_off(n_proj, 0), cnt_off(n_proj, 0), pair_off(n_ffn, 0);
+  size_t scratch = 0;
+  long long first = 0;
+  for (int q = 0; q < n_proj; q++) {
+    const int i = order[q];
+    const PlanSpec::Proj &p = s.projs[i];
+    PlanProjD &d = pd[q];
+    d = PlanProjD{};
+    d.pack = p.pack;
+    d.out_q32 = p.out_q32;
+    d.out_f32 = p.out_f32;
+    d.status = p.status;
+    d.n_out = p.n_out;
+    d.n_in = p.n_in;
+    d.L = p.plan.L;
+    d.U = p.plan.units;
+    d.n_rt = n_rt[i];
+    d.npieces = npieces[i];
+    d.plen = plen[i];
+    d.piece0 = (int)first;
+    d.act = p.act;
+    d.ffn = p.ffn;
+    first += (long long)n_rt[i] * npieces[i];
+    if (d.npieces > 1) {
+      part_off[q] = scratch;
+      scratch += al256((size_t)d.n_rt * d.npieces * 32 * sizeof(Acc128));
+      cnt_off[q] = scratch;
+      scratch += al256((size_t)d.n_rt * 4);
+    }
+  }
+  std::vector<PlanActD> ad(n_act);
+  for (int a = 0; a < n_act; a++) {
+    const PlanSpec::Act &x = s.acts[a];
+    ad[a] = PlanActD{x.codes, x.exps, static_cast<const ActDesc *>(x.desc), x.ffn, 0};
+  }
+  std::vector<PlanFfnD> fd(n_ffn);
+  for (int f = 0; f < n_ffn; f++) {
+    const PlanSpec::Ffn &x = s.ffns[f];
+    const PlanSpec::Proj &pg = s.projs[gate[f]], &pu = s.projs[up[f]];
+    PlanFfnD &d = fd[f];
+    d = PlanFfnD{};
+    d.gate = pg.out_q32;
+    d.up = pu.out_q32;
+    d.gate_status = pg.status;
+    d.up_status = pu.status;
+    d.h = x.h;
+    d.codes = const_cast<int8_t *>(s.acts[x.out_act].codes);
+    d.exps = const_cast<uint8_t *>(s.acts[x.out_act].exps);
+    d.desc = static_cast<ActDesc *>(const_cast<void *>(s.acts[x.out_act].desc));
+    d.status = x.status;
+    d.n = pg.n_out;
+    d.n_rt = (int)((pg.n_out + 31) / 32);
+    d.carrier = x.carrier;
+    d.refused = x.refused ? 1 : 0;
+    pair_off[f] = scratch;
+    scratch += al256((size_t)d.n_rt * 4);
+  }
+
+  auto *h = new (std::nothrow) PlanHost;
+  if (!h) return APX_ERR_OUT_OF_MEMORY;
+  h->type = type;
+  h->n_proj = n_proj;
+  h->n_ffn = n_ffn;
+  h->total = (int)total;
+  h->grid = grid;
+  h->block = block;
+  h->smem = smem;
+  const size_t o_proj = 0, o_act = al256(n_proj * sizeof(PlanProjD));
+  const size_t o_ffn = o_act + al256(std::max(n_act, 1) * sizeof(PlanActD));
+  const size_t o_ctl = o_ffn + al256(std::max(n_ffn, 1) * sizeof(PlanFfnD));
+  const size_t o_scr = o_ctl + al256(sizeof(PlanCtl));
+  const size_t bytes = o_scr + scratch;
+  if (cudaMalloc(&h->dev, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    delete h;
+    return APX_ERR_OUT_OF_MEMORY;
+  }
+  uint8_t *base = static_cast<uint8_t *>(h->dev);
+  for (int q = 0; q < n_proj; q++)
+    if (pd[q].npieces > 1) {
+      pd[q].part = reinterpret_cast<Acc128 *>(base + o_scr + part_off[q]);
+      pd[q].cnt = reinterpret_cast<unsigned *>(base + o_scr + cnt_off[q]);
+    }
+  for (int f = 0; f < n_ffn; f++)
+    fd[f].pair = reinterpret_cast<unsigned *>(base + o_scr + pair_off[f]);
+  h->proj = reinterpret_cast<PlanProjD *>(base + o_proj);
+  h->act = reinterpret_cast<PlanActD *>(base + o_act);
+  h->ffn = reinterpret_cast<PlanFfnD *>(base + o_ffn);
+  h->ctl = reinterpret_cast<PlanCtl *>(base + o_ctl);
+  e = cudaMemset(h->dev, 0, bytes);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(h->proj, pd.data(), n_proj * sizeof(PlanProjD), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && n_act)
+    e = cudaMemcpy(h->act, ad.data(), n_act * sizeof(PlanActD), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && n_ffn)
+    e = cudaMemcpy(h->ffn, fd.data(), n_ffn * sizeof(PlanFfnD), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    plan_free(h);
+    return APX_ERR_CUDA;
+  }
+  *out = h;
+  return APX_OK;
+}
+
+cudaError_t plan_run(const PlanHost &h, cudaStream_t stream, bool pdl) {
+  PlanArgs a;
+  a.proj = h.proj;
+  a.act = h.act;
+  a.ffn = h.ffn;
+  a.ctl = h.ctl;
+  a.n_proj = h.n_proj;
+  a.n_ffn = h.n_ffn;
+  a.total = h.total;
+  a.V = (int)h.grid * (h.block / 32);
+  switch (h.type) {
+    case kQ8_0: return plan_launch<kQ8_0>(h, a, stream, pdl);
+    case kQ4_K: return plan_launch<kQ4_K>(h, a, stream, pdl);
+    case kQ6_K: return plan_launch<kQ6_K>(h, a, stream, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+void plan_free(PlanHost *h) {
+  if (!h) return;
+  if (h->dev) cudaFree(h->dev);
+  delete h;
+}
+
+}  // namespace apx

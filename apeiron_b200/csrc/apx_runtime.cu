@@ -16,6 +16,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <new>
 #include <unordered_map>
 #include <vector>
 
@@ -1207,5 +1208,129 @@ int apx_status_decode(apx_ctx *ctx, uint64_t tensor, const apx_call_status *stat
   if (!t) return set_err(err, APX_ERR_INVALID_ARGUMENT);
   return decode_status(*t, t->n_out, status->first, err);
 }
+
+int apx_status_decode_rows(apx_ctx *ctx, uint64_t tensor, size_t n_out,
+                           const apx_call_status *status, apx_err *err) {
+  if (!ctx || !status) return set_err(err, APX_ERR_INVALID_ARGUMENT);
+  std::lock_guard<std::mutex> g(ctx->mu);
+  Tensor *t = find(ctx, tensor);
+  if (!t || n_out > t->n_out) return set_err(err, APX_ERR_INVALID_ARGUMENT);
+  return decode_status(*t, n_out, status->first, err);
+}
+
+// ---- step plans ------------------------------------------------------------------------------
+
+struct apx_plan {
+  apx_ctx *ctx = nullptr;
+  PlanHost *host = nullptr;
+  std::vector<void *> own;  // the gate / up Q32.32 outputs the caller did not provide
+  ~apx_plan() {
+    plan_free(host);
+    for (void *p : own) cudaFree(p);
+  }
+};
+
+apx_plan *apx_plan_create(apx_ctx *ctx, const apx_plan_proj *projs, size_t n_proj,
+                          const apx_plan_act *acts, size_t n_act, const apx_plan_ffn *ffns,
+                          size_t n_ffn, apx_err *err) {
+  set_err(err, APX_OK);
+  if (!ctx || !projs || n_proj == 0 || (n_act && !acts) || (n_ffn && !ffns) || n_act == 0 ||
+      n_proj > (size_t)kPlanMaxProj || n_ffn > (size_t)kPlanMaxFfn || n_act > (size_t)INT32_MAX) {
+    set_err(err, APX_ERR_INVALID_ARGUMENT);
+    return nullptr;
+  }
+  auto *plan = new (std::nothrow) apx_plan;
+  if (!plan) {
+    set_err(err, APX_ERR_OUT_OF_MEMORY);
+    return nullptr;
+  }
+  plan->ctx = ctx;
+  PlanSpec s;
+  int rc = APX_OK;
+  {
+    std::lock_guard<std::mutex> g(ctx->mu);
+    for (size_t i = 0; i < n_proj && rc == APX_OK; i++) {
+      const apx_plan_proj &q = projs[i];
+      Tensor *t = find(ctx, q.tensor);
+      if (!t || !t->d_pack || q.n_in != t->n_in || q.n_out > t->n_out) {
+        rc = APX_ERR_LAYOUT_MISMATCH;
+        break;
+      }
+      PlanSpec::Proj p;
+      p.type = t->type;
+      p.pack = t->d_pack;
+      p.plan = t->plan;
+      p.n_out = q.n_out;
+      p.n_in = q.n_in;
+      p.act = q.act;
+      p.ffn = q.ffn;
+      p.role = q.role;
+      p.out_q32 = (long long *)q.d_out_q32;
+      p.out_f32 = q.d_out_f32;
+      p.status = q.d_status ? (unsigned long long *)&q.d_status->first : nullptr;
+      if (q.ffn >= 0 && !p.out_q32 && q.n_out) {  // SwiGLU reads gate and up in Q32.32
+        void *buf = nullptr;
+        if (cudaMalloc(&buf, q.n_out * sizeof(long long)) != cudaSuccess) {
+          cudaGetLastError();
+          rc = APX_ERR_OUT_OF_MEMORY;
+          break;
+        }
+        plan->own.push_back(buf);
+        p.out_q32 = static_cast<long long *>(buf);
+      }
+      s.projs.push_back(p);
+    }
+    for (size_t f = 0; f < n_ffn && rc == APX_OK; f++) {
+      PlanSpec::Ffn x;
+      x.carrier = ffns[f].carrier;
+      x.out_act = ffns[f].out_act;
+      x.h = (long long *)ffns[f].d_h;
+      x.status = ffns[f].d_status ? (unsigned long long *)&ffns[f].d_status->first : nullptr;
+      x.refused = false;
+      if ((x.carrier != APX_CARRIER_F32 && x.carrier != APX_CARRIER_Q32) || !x.status) {
+        rc = APX_ERR_INVALID_ARGUMENT;
+        break;
+      }
+      for (size_t i = 0; i < n_proj; i++)  // a non-finite weight row leaves h undefined
+        if (projs[i].ffn == (int32_t)f) {
+          const Tensor *t = find(ctx, projs[i].tensor);
+          x.refused = x.refused || (t && t->nonfinite_row < projs[i].n_out);
+        }
+      s.ffns.push_back(x);
+    }
+  }
+  for (size_t a = 0; a < n_act && rc == APX_OK; a++) {
+    const apx_plan_act &x = acts[a];
+    s.acts.push_back(PlanSpec::Act{x.d_codes, x.d_exps, x.d_desc, x.ffn});
+    if (x.ffn >= 0 && (size_t)x.ffn < n_ffn && x.d_codes && x.d_exps) {
+      // the FFN writes codes [0, n) and exponent bytes [0, ceil(n/32)): the rest of the
+      // padded buffers reads as zero blocks
+      size_t n = 0;
+      for (size_t i = 0; i < n_proj; i++)
+        if (projs[i].ffn == x.ffn) n = projs[i].n_out;
+      const size_t pad = apx_act_padded_len(n), nb = (n + 31) / 32;
+      if (cudaMemset(x.d_codes + n, 0, pad - n) != cudaSuccess ||
+          cudaMemset(x.d_exps + nb, 0xFF, pad / 32 - nb) != cudaSuccess) {
+        cudaGetLastError();
+        rc = APX_ERR_CUDA;
+      }
+    }
+  }
+  if (rc == APX_OK) rc = plan_build(s, ctx->sm_count, &plan->host);
+  if (rc != APX_OK) {
+    delete plan;
+    set_err(err, rc);
+    return nullptr;
+  }
+  return plan;
+}
+
+int apx_plan_run_async(apx_plan *plan, void *stream) {
+  if (!plan || !plan->host) return APX_ERR_INVALID_ARGUMENT;
+  const cudaError_t e = plan_run(*plan->host, (cudaStream_t)stream, pdl_allowed());
+  return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
+}
+
+void apx_plan_destroy(apx_plan *plan) { delete plan; }
 
 }  // extern "C"

@@ -241,12 +241,16 @@ DECODE_HEAD = (14, 151936, 896)                                                 
 
 def measure_decode_step(be, lib, dev, stream, steps, warmup, pg, local, world):
     """the 169 projections of one decode step (24 layers of q/k/v/o/gate/up/down in
-    Q4_K, the Q6_K head) as one chain of launches replayed from a CUDA graph; every projection
-    reads a resident activation of its width (the quantizer and the nonlinear layers between
-    them are not on this path).  Replicas at N > 1."""
+    Q4_K, the Q6_K head) as two launches replayed from a CUDA graph: one step plan
+    (apx_plan_run_async) for the 168 layer projections and the head on its own.  q/k/v/o and
+    gate/up read resident activations of their width (attention and the residual stream are
+    not on this path); each layer's down reads the hidden activation its FFN produces on the
+    device (SwiGLU + quant_act in the gate/up finish).  Replicas at N > 1."""
+    import ctypes as C
+
     import torch
 
-    from apeiron_b200 import synth
+    from apeiron_b200 import _abi, synth
     from oracle import oracle as O
 
     sp = stream.cuda_stream
@@ -255,84 +259,85 @@ def measure_decode_step(be, lib, dev, stream, steps, warmup, pg, local, world):
     raws = {}
     for i, (t, n_out, n_in) in enumerate(DECODE_LAYER + [DECODE_HEAD]):
         raws[i] = synth.payload(t, n_out, n_in, 6000 + i)
-    wbytes = sum(raws[i % len(DECODE_LAYER)].size if i < len(mats) - 1 else raws[len(DECODE_LAYER)].size
+    nl = len(DECODE_LAYER)
+    wbytes = sum(raws[i % nl].size if i < len(mats) - 1 else raws[nl].size
                  for i in range(len(mats)))
     copies = max(2, int(np.ceil(3 * L2_BYTES / wbytes)))
-    # every layer its own upload (the same bytes per layer position: uploads are independent)
-    tensors = []
+    tensors = []  # [copy][projection]: every layer its own upload
     for c in range(copies):
-        row = []
-        for i, (t, n_out, n_in) in enumerate(mats):
-            key = len(DECODE_LAYER) if i == len(mats) - 1 else i % len(DECODE_LAYER)
-            row.append(be.upload(t, raws[key], n_out, n_in))
-        tensors.append(row)
-    acts = {}
-    for n_in in sorted({m[2] for m in mats}):
-        x = synth.activation_f32(n_in, 7000 + n_in)
-        c, e = synth.quant_act_np(synth.f32_to_q32(x))
-        pad = lib.apx_act_padded_len(n_in)
-        codes = torch.zeros(pad, dtype=torch.int8, device=dev)
-        codes[:n_in] = torch.from_numpy(c).to(dev)
-        exps = torch.full((pad // 32,), 0xFF, dtype=torch.uint8, device=dev)
-        exps[:e.size] = torch.from_numpy(e).to(dev)
-        desc = torch.zeros(8, dtype=torch.int32, device=dev)
-        with torch.cuda.stream(stream):
-            assert lib.apx_act_describe_async(be.ctx, codes.data_ptr(), exps.data_ptr(), n_in,
-                                              desc.data_ptr(), sp) == 0
-        acts[n_in] = (codes, exps, desc, c, e)
-    import ctypes as C
-
+        tensors.append([be.upload(t, raws[nl if i == len(mats) - 1 else i % nl], n_out, n_in)
+                        for i, (t, n_out, n_in) in enumerate(mats)])
+    n_embd, n_ff = DECODE_LAYER[0][2], DECODE_LAYER[4][1]
+    x = synth.activation_f32(n_embd, 7000 + n_embd)
+    cx, ex = synth.quant_act_np(synth.f32_to_q32(x))
+    pad = lib.apx_act_padded_len(n_embd)
+    codes = torch.zeros(pad, dtype=torch.int8, device=dev)
+    codes[:n_embd] = torch.from_numpy(cx).to(dev)
+    exps = torch.full((pad // 32,), 0xFF, dtype=torch.uint8, device=dev)
+    exps[:ex.size] = torch.from_numpy(ex).to(dev)
+    desc = torch.zeros(8, dtype=torch.int32, device=dev)
+    with torch.cuda.stream(stream):
+        assert lib.apx_act_describe_async(be.ctx, codes.data_ptr(), exps.data_ptr(), n_embd,
+                                          desc.data_ptr(), sp) == 0
+    hpad = lib.apx_act_padded_len(n_ff)
+    hs = [(torch.zeros(hpad, dtype=torch.int8, device=dev),
+           torch.full((hpad // 32,), 0xFF, dtype=torch.uint8, device=dev),
+           torch.zeros(8, dtype=torch.int32, device=dev)) for _ in range(DECODE_LAYERS)]
     outs = [torch.zeros(m[1], dtype=torch.int64, device=dev) for m in mats]
-    status = torch.full((2,), -1, dtype=torch.int64, device=dev)
-    # projections that read the same activation share a launch (apx_matvec_group_async):
-    # q/k/v and gate/up of every layer; o, down and the head run alone
-    per_layer = [[0, 1, 2], [3], [4, 5], [6]]
-    launches = []  # (member indices into mats)
-    for layer in range(DECODE_LAYERS):
-        for g in per_layer:
-            launches.append([layer * len(DECODE_LAYER) + k for k in g])
-    launches.append([len(mats) - 1])
-    arrays = []  # per copy, per launch: the ctypes arrays of a grouped call
+    statuses = torch.full((len(mats) + DECODE_LAYERS, 2), -1, dtype=torch.int64, device=dev)
+    acts = [_abi.PlanAct(codes.data_ptr(), exps.data_ptr(), desc.data_ptr(), -1, 0)]
+    acts += [_abi.PlanAct(h[0].data_ptr(), h[1].data_ptr(), h[2].data_ptr(), layer, 0)
+             for layer, h in enumerate(hs)]
+    ffns = (_abi.PlanFfn * DECODE_LAYERS)(*[
+        _abi.PlanFfn(0, 1 + layer, None, statuses[len(mats) + layer].data_ptr())
+        for layer in range(DECODE_LAYERS)])
+    plans = []
     for c in range(copies):
-        row = []
-        for g in launches:
-            if len(g) == 1:
-                row.append(None)
-                continue
-            n = len(g)
-            row.append(((C.c_uint64 * n)(*[tensors[c][k].handle for k in g]),
-                        (C.c_void_p * n)(*[outs[k].data_ptr() for k in g]),
-                        (C.c_void_p * n)(*[status.data_ptr()] * n)))
-        arrays.append(row)
+        projs = []
+        for i, (t, n_out, n_in) in enumerate(mats[:-1]):
+            layer, k = divmod(i, nl)
+            ffn, role = (layer, k - 4) if k in (4, 5) else (-1, 0)
+            projs.append(_abi.PlanProj(tensors[c][i].handle, n_out, n_in,
+                                       1 + layer if k == 6 else 0, ffn, role, 0,
+                                       outs[i].data_ptr(), None, statuses[i].data_ptr()))
+        err = _abi.ApxErr()
+        pl = lib.apx_plan_create(be.ctx, (_abi.PlanProj * len(projs))(*projs), len(projs),
+                                 (_abi.PlanAct * len(acts))(*acts), len(acts), ffns,
+                                 DECODE_LAYERS, C.byref(err))
+        assert pl, f"apx_plan_create failed: {err.code}"
+        plans.append(pl)
+    head = len(mats) - 1
 
     def step(i):
-        row = tensors[i % copies]
-        for li, g in enumerate(launches):
-            t, n_out, n_in = mats[g[0]]
-            codes, exps, desc, _, _ = acts[n_in]
-            if len(g) == 1:
-                k = g[0]
-                rc = lib.apx_matvec_async(be.ctx, row[k].handle, n_out, n_in, codes.data_ptr(),
-                                          exps.data_ptr(), desc.data_ptr(), outs[k].data_ptr(),
-                                          None, status.data_ptr(), sp)
-            else:
-                hs, os_, ss = arrays[i % copies][li]
-                rc = lib.apx_matvec_group_async(be.ctx, hs, len(g), n_in, codes.data_ptr(),
-                                                exps.data_ptr(), desc.data_ptr(), os_, None, ss,
-                                                sp)
-            assert rc == 0
+        assert lib.apx_plan_run_async(plans[i % copies], sp) == 0
+        t, n_out, n_in = mats[head]
+        assert lib.apx_matvec_async(be.ctx, tensors[i % copies][head].handle, n_out, n_in,
+                                    codes.data_ptr(), exps.data_ptr(), desc.data_ptr(),
+                                    outs[head].data_ptr(), None, statuses[head].data_ptr(),
+                                    sp) == 0
 
     with torch.cuda.stream(stream):
         step(0)
     stream.synchronize()
-    for k in list(range(len(DECODE_LAYER))) + [len(mats) - 1]:  # one layer and the head
-        t, n_out, n_in = mats[k]
-        key = len(DECODE_LAYER) if k == len(mats) - 1 else k
-        _, _, _, c, e = acts[n_in]
-        want = O.matvec_q8act_mt(t, raws[key], n_out, n_in, c, O.exps_to_scales(e),
-                                 host_threads())
-        assert np.array_equal(outs[k].cpu().numpy(), want), "decode-step parity failure"
-    assert int(status[0].item()) == -1
+    assert bool((statuses == -1).all().item()), "refusal in the decode step"
+    # exactness: layer 0's projections (down through the device FFN chain) and the head
+    thr = host_threads()
+    sc = O.exps_to_scales(ex)
+    ys = {}
+    for k in range(4):
+        t, n_out, n_in = DECODE_LAYER[k]
+        ys[k] = O.matvec_q8act_mt(t, raws[k], n_out, n_in, cx, sc, thr)
+        assert np.array_equal(outs[k].cpu().numpy(), ys[k]), f"decode-step parity {k}"
+    g = O.matvec_q8act_mt(12, raws[4], n_ff, n_embd, cx, sc, thr)
+    u = O.matvec_q8act_mt(12, raws[5], n_ff, n_embd, cx, sc, thr)
+    assert np.array_equal(outs[4].cpu().numpy(), g) and np.array_equal(outs[5].cpu().numpy(), u)
+    _, hcodes, hscales = O.swiglu_quant(g, u, 0)
+    assert np.array_equal(hs[0][0].cpu().numpy()[:n_ff], hcodes), "decode-step h codes"
+    y = O.matvec_q8act_mt(12, raws[6], n_embd, n_ff, hcodes, hscales, thr)
+    assert np.array_equal(outs[6].cpu().numpy(), y), "decode-step down (FFN chain) parity"
+    t, n_out, n_in = DECODE_HEAD
+    want = O.matvec_q8act_mt(t, raws[nl], n_out, n_in, cx, sc, thr)
+    assert np.array_equal(outs[head].cpu().numpy(), want), "decode-step head parity"
     G = max(2, min(steps, 20))
     gr = torch.cuda.CUDAGraph()
     with torch.cuda.graph(gr, stream=stream):
@@ -354,10 +359,33 @@ def measure_decode_step(be, lib, dev, stream, steps, warmup, pg, local, world):
     stream.synchronize()
     barrier(pg, local)
     ms = max_over_ranks(t0.elapsed_time(t1), pg, local) / (reps * G)
-    assert int(status[0].item()) == -1
+    assert bool((statuses == -1).all().item()), "refusal while timed"
+    # the plan alone and the head alone, back to back (the step's kernels)
+    parts = {}
+    for name, fn in (("plan", lambda i: lib.apx_plan_run_async(plans[i % copies], sp)),
+                     ("head", lambda i: lib.apx_matvec_async(
+                         be.ctx, tensors[i % copies][head].handle, mats[head][1], mats[head][2],
+                         codes.data_ptr(), exps.data_ptr(), desc.data_ptr(),
+                         outs[head].data_ptr(), None, statuses[head].data_ptr(), sp))):
+        g2 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g2, stream=stream):
+            for i in range(G):
+                assert fn(i) == 0
+        with torch.cuda.stream(stream):
+            g2.replay()
+            t0.record(stream)
+            g2.replay()
+            t1.record(stream)
+        stream.synchronize()
+        parts[name] = t0.elapsed_time(t1) / G
+        del g2
     del gr
+    for pl in plans:
+        lib.apx_plan_destroy(pl)
     hbm, _ = peaks()
     gbs = world * per_step / (ms / 1e3) / 1e9
+    plan_bytes = sum(gemv_bytes(*m) for m in mats[:-1])
+    head_bytes = gemv_bytes(*mats[head])
     return {
         "metric": "decode step GB/s (all linear layers)", "value": gbs, "unit": "GB/s",
         "ms_per_step": ms, "steps": reps * G, "tokens_per_s": world * 1e3 / ms,
@@ -365,14 +393,23 @@ def measure_decode_step(be, lib, dev, stream, steps, warmup, pg, local, world):
         "config": {"workload": "Qwen2.5-0.5B-shaped Q4_K_M decode step, configs[3]: 24 layers "
                                "x (q 896x896, k/v 128x896, o 896x896, gate/up 4864x896, down "
                                "896x4864) Q4_K + tied lm_head 151936x896 Q6_K = 169 projections "
-                               "in 97 launches (q/k/v and gate/up of a layer share one), resident "
-                               "activations",
+                               "in 2 launches: one step plan (168 layer projections; each "
+                               "layer's down reads the hidden activation its FFN's SwiGLU + "
+                               "quant_act produces on the device) and the head; q/k/v/o/gate/up "
+                               "read resident activations",
                    "bytes_per_step": per_step, "weight_copies": copies,
                    "l2": "rotating weight copies, >= 3x the 126 MB L2",
-                   "exact": "one layer's projections and the head bit-equal to the CPU oracle "
-                            "(checked before timing)"},
+                   "exact": "layer 0's q/k/v/o/gate/up, its h codes and its down output (the "
+                            "device FFN chain) and the head bit-equal to the CPU oracle (checked "
+                            "before timing)"},
         "hbm_frac": gbs / world / hbm,
-        "gpu_launches_per_step": len(launches),
+        "kernels": [{"kernel": "plan_kernel<Q4_K> (168 projections, 24 FFNs)",
+                     "us": parts["plan"] * 1e3, "gbs": plan_bytes / (parts["plan"] / 1e3) / 1e9,
+                     "frac": plan_bytes / (parts["plan"] / 1e3) / 1e9 / hbm},
+                    {"kernel": "gemv_stream_kernel<Q6_K> (head 151936x896)",
+                     "us": parts["head"] * 1e3, "gbs": head_bytes / (parts["head"] / 1e3) / 1e9,
+                     "frac": head_bytes / (parts["head"] / 1e3) / 1e9 / hbm}],
+        "gpu_launches_per_step": 2,
     }
 
 

@@ -273,9 +273,69 @@ APX_API int apx_matvec_group_async(apx_ctx *ctx, const uint64_t *tensors, int co
 /* Activation buffer length (bytes of codes) the async kernels read for width n_in. */
 APX_API size_t apx_act_padded_len(size_t n_in);
 /* Decode a refusal word (host copy of *d_status) together with the tensor's
- * upload-time findings into err; returns err->code. */
+ * upload-time findings into err; returns err->code.  For a call over all of the tensor's
+ * rows; a call over its first n_out rows decodes with apx_status_decode_rows. */
 APX_API int apx_status_decode(apx_ctx *ctx, uint64_t tensor, const apx_call_status *status,
                       apx_err *err);
+/* apx_status_decode for a call that projected the tensor's first n_out rows: an Inf/NaN
+ * block scale found at upload counts only when its row is below n_out (the rows the call
+ * computed), as apx_matvec_q8act decides for the same n_out. */
+APX_API int apx_status_decode_rows(apx_ctx *ctx, uint64_t tensor, size_t n_out,
+                                   const apx_call_status *status, apx_err *err);
+
+/* ---- step plans: the projections of a decode step in one launch -------------------- */
+/* A plan lists projections in dependency order, each reading one activation record, and
+ * optionally FFNs: the gate and up projections of one activation (role APX_PLAN_GATE /
+ * APX_PLAN_UP) whose finish runs SwiGLU + quant_act into an activation record that later
+ * projections (down) read.  apx_plan_run_async runs the whole plan as one persistent launch;
+ * every projection's outputs and refusal word are those of apx_matvec_async on the same inputs,
+ * every FFN's activation and refusal word those of apx_swiglu_quant_async on the gate and up
+ * outputs.  The plan replaces the per-projection calls of a decode step's projection schedule
+ * (step_proj_sched, src/engine/step.rs:1458; ffn_q8act_prepared_into, chart/ffn.rs:1609): same
+ * results, one launch, each projection's weights streaming while earlier ones finish.
+ *
+ * All tensors of a plan share a family (Q5_0 counts as Q8_0).  Records hold device pointers
+ * that must stay valid while the plan exists; activation buffers follow apx_act_padded_len.
+ * Status words (projections and FFNs) are set to all ones by the caller before each run.  A
+ * projection reading an FFN's activation comes after both of that FFN's projections; it waits
+ * for the activation on the device (bounded: about one second, then APX_ERR_DEVICE_TIMEOUT).
+ * Runs of one plan must not overlap in time (the plan owns its counters and scratch). */
+typedef struct apx_plan apx_plan;
+#define APX_PLAN_GATE 0
+#define APX_PLAN_UP 1
+typedef struct apx_plan_act {
+  int8_t *d_codes;      /* apx_act_padded_len(n) code bytes */
+  uint8_t *d_exps;      /* apx_act_padded_len(n) / 32 exponent bytes */
+  apx_act_desc *d_desc; /* its descriptor */
+  int32_t ffn;          /* -1: written before the run; else the FFN that writes it (the plan
+                         * then sets the pad bytes past n once, at creation) */
+  int32_t reserved;
+} apx_plan_act;
+typedef struct apx_plan_proj {
+  uint64_t tensor;
+  size_t n_out, n_in;        /* the first n_out rows (decode with apx_status_decode_rows) */
+  int32_t act;               /* the activation record it reads */
+  int32_t ffn;               /* -1, or the FFN it feeds */
+  int32_t role;              /* APX_PLAN_GATE or APX_PLAN_UP when ffn >= 0 */
+  int32_t reserved;
+  int64_t *d_out_q32;        /* optional (an FFN's gate and up get plan-owned ones) */
+  float *d_out_f32;          /* optional */
+  apx_call_status *d_status; /* required */
+} apx_plan_proj;
+typedef struct apx_plan_ffn {
+  int32_t carrier;           /* APX_CARRIER_F32 or APX_CARRIER_Q32 */
+  int32_t out_act;           /* the activation record it writes */
+  int64_t *d_h;              /* optional: h in Q32.32 */
+  apx_call_status *d_status; /* the first refusing SwiGLU lane (apx_ffn_status_decode) */
+} apx_plan_ffn;
+/* NULL with err set on failure: APX_ERR_LAYOUT_MISMATCH (a tensor or width), APX_ERR_
+ * INVALID_ARGUMENT (records: families differ, an FFN without one gate and one up of equal
+ * shape and activation, a reader before its FFN, more than 4096 projections or 64 FFNs). */
+APX_API apx_plan *apx_plan_create(apx_ctx *ctx, const apx_plan_proj *projs, size_t n_proj,
+                                  const apx_plan_act *acts, size_t n_act,
+                                  const apx_plan_ffn *ffns, size_t n_ffn, apx_err *err);
+APX_API int apx_plan_run_async(apx_plan *plan, void *stream);
+APX_API void apx_plan_destroy(apx_plan *plan);
 
 /* ---- allocation-free entry point ------------------------------------------------ */
 
@@ -291,8 +351,8 @@ APX_API int apx_status_decode(apx_ctx *ctx, uint64_t tensor, const apx_call_stat
  *
  * Same result as apx_matvec_f32 (f32_to_fixed + quant_act on the device, the exact
  * projection, one rounding to f32), on device buffers: d_x holds n_in floats, d_y receives
- * n_out floats, *d_status the refusal word (decode with apx_status_decode after the stream
- * has finished).  The call is asynchronous on `stream` and allocates nothing: the quantized
+ * n_out floats, *d_status the refusal word (decode with apx_status_decode_rows for the same
+ * n_out after the stream has finished).  The call is asynchronous on `stream` and allocates nothing: the quantized
  * activation is staged in one array of APX_NOALLOC_SCRATCH_BYTES compiled into the library,
  * which every GPU that loads the library holds until the process exits.
  *   - n_in above APX_NOALLOC_MAX_N_IN is refused with APX_ERR_TOO_LARGE.

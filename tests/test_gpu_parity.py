@@ -303,6 +303,56 @@ def test_async_device_path_matches_sync(be):
     assert np.array_equal(out.cpu().numpy(), want)
 
 
+def test_async_short_rows_decode(be):
+    """A call over the first n_out rows of a tensor with an Inf block scale in a later row
+    projects those rows (apx_matvec_q8act decides the same for that n_out):
+    apx_status_decode_rows merges the upload-time finding only below n_out."""
+    import ctypes as C
+    import torch
+
+    from apeiron_b200 import _abi
+
+    lib = be.lib
+    t, n_out, n_in = Q8_0, 512, 1024
+    raw = synth.payload(t, n_out, n_in, 31).copy()
+    bad_row = 200
+    off = (bad_row * (n_in // 32) + 5) * 34
+    raw[off:off + 2] = (0x00, 0x7C)  # +Inf scale
+    tens = be.upload(t, raw, n_out, n_in)
+    x = synth.activation_f32(n_in, 32)
+    c, e = synth.quant_act_np(synth.f32_to_q32(x))
+    dev = torch.device("cuda:0")
+    pad = lib.apx_act_padded_len(n_in)
+    codes = torch.zeros(pad, dtype=torch.int8, device=dev)
+    codes[:n_in] = torch.from_numpy(c).to(dev)
+    exps = torch.full((pad // 32,), 0xFF, dtype=torch.uint8, device=dev)
+    exps[:e.size] = torch.from_numpy(e).to(dev)
+    desc = torch.zeros(8, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.apx_act_describe_async(be.ctx, codes.data_ptr(), exps.data_ptr(), n_in,
+                                      desc.data_ptr(), stream) == 0
+    for rows in (bad_row, bad_row + 1, n_out):
+        out = torch.zeros(rows, dtype=torch.int64, device=dev)
+        status = torch.full((2,), -1, dtype=torch.int64, device=dev)
+        assert lib.apx_matvec_async(be.ctx, tens.handle, rows, n_in, codes.data_ptr(),
+                                    exps.data_ptr(), desc.data_ptr(), out.data_ptr(), None,
+                                    status.data_ptr(), stream) == 0
+        torch.cuda.synchronize()
+        st = _abi.CallStatus(int(status[0].item()) & ((1 << 64) - 1), 0)
+        err = _abi.ApxErr()
+        rc = lib.apx_status_decode_rows(be.ctx, tens.handle, rows, C.byref(st), C.byref(err))
+        if rows <= bad_row:
+            assert rc == _abi.APX_OK
+            want = O.matvec_q8act(t, raw[:rows * (n_in // 32) * 34], rows, n_in, c,
+                                  O.exps_to_scales(e))
+            assert np.array_equal(out.cpu().numpy(), want)
+        else:
+            assert rc == _abi.APX_ERR_NONFINITE_SCALE and err.row == bad_row
+    err = _abi.ApxErr()
+    assert lib.apx_status_decode_rows(be.ctx, tens.handle, n_out + 1, C.byref(st),
+                                      C.byref(err)) == _abi.APX_ERR_INVALID_ARGUMENT
+
+
 # ---- matrices beyond one resident wave: the persistent streaming kernel --------------------
 
 @pytest.mark.parametrize("t,n_out,n_in", [

@@ -81,7 +81,8 @@ def _both(be, tensor, n_out, n_in, x):
     st = _abi.CallStatus(int(status[0].item()) & ((1 << 64) - 1),
                          int(status[1].item()) & ((1 << 64) - 1))
     err2 = _abi.ApxErr()
-    rc2 = be.lib.apx_status_decode(be.ctx, tensor.handle, C.byref(st), C.byref(err2))
+    rc2 = be.lib.apx_status_decode_rows(be.ctx, tensor.handle, n_out, C.byref(st),
+                                        C.byref(err2))
     got = (rc2, err2.row if rc2 else None, dy.cpu().numpy()[:n_out] if rc2 == 0 else None)
     return want, got
 
