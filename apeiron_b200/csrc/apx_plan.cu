@@ -23,9 +23,9 @@
 // block and adds the block's exponent statistics to the FFN's; the last block publishes the
 // descriptor and raises the FFN's flag.  A warp that takes a piece reading that activation waits
 // on the flag first, with a bound (about one second) after which the projection refuses with
-// APX_ERR_DEVICE_TIMEOUT.  The host queues each reader of an FFN two grid-rounds (2V pieces)
-// after the FFN's last piece when other work can fill the gap, so the flag is usually up when a
-// warp gets there.  A warp waits only at the start of a piece with nothing unfinished, and every
+// APX_ERR_DEVICE_TIMEOUT.  The host queues projections by dependency level, an FFN's producers
+// ahead of the level's other work and its readers in the next level, so the flag is usually up
+// when a warp gets there.  A warp waits only at the start of a piece with nothing unfinished, and every
 // piece a wait depends on sits earlier in the queue: by induction on queue position the earliest
 // waiting piece's producers belong to warps that reach them, since the grid is sized to be
 // co-resident.  The last CTA out resets the counters and flags for the next launch.
@@ -240,12 +240,14 @@ __device__ __forceinline__ bool wait_flag(const PlanArgs &g, int f) {
 // Launch shape per family: warps per CTA, CTAs per SM, weight ring slots per warp.  Each warp
 // streams its units through a ring of kSlots unit buffers in shared memory, filled by 1D bulk
 // copies (cp.async.bulk, no multicast) that complete on one mbarrier per slot: kSlots - 1 units
-// in flight while one folds.
+// in flight while one folds.  Measured on B200 over a decode step's 168 projections: sixteen
+// warps per SM with two slots each beat twelve with three (the fold is issue-bound: warps hide
+// its latency better than deeper rings hide HBM's) and eight or six with five or seven slots.
 template <uint32_t T>
 struct PlanShape {
-  static constexpr int kWarps = T == kQ6_K ? 8 : 6;
+  static constexpr int kWarps = 8;
   static constexpr int kCtas = T == kQ6_K ? 1 : 2;
-  static constexpr int kSlots = 3;
+  static constexpr int kSlots = T == kQ6_K ? 3 : 2;
   static constexpr int kUnit = Fam<T>::unit_bytes;
   static constexpr int kThreads = 32 * kWarps;
   static_assert(kUnit % 16 == 0, "bulk copies move whole 16-byte chunks");
@@ -410,11 +412,11 @@ __global__ void __launch_bounds__(PlanShape<T>::kThreads, PlanShape<T>::kCtas)
       uint8_t *sl;
       const bool got = us.wait_front(sl);
       copies_ok = copies_ok && got;
-      UnitRegs<T> w;
-      if (fast) load_unit_smem(w, sl, lane);
-      us.release_front();
-      us.top_up(g, pc, pn, xn >= 0, lane);
-      if (!fast) continue;  // the slot is consumed all the same
+      if (!fast) {  // the slot is consumed all the same
+        us.release_front();
+        us.top_up(g, pc, pn, xn >= 0, lane);
+        continue;
+      }
       WarpAct<T> &wb = wa[u & 1];
       store_chunk<T>(wb, c0, lane, lane < nch, desc.emin);
       if (nch > 32) store_chunk<T>(wb, c1, lane + 32, lane + 32 < nch, desc.emin);
@@ -433,8 +435,10 @@ __global__ void __launch_bounds__(PlanShape<T>::kThreads, PlanShape<T>::kCtas)
           next_pre = true;
         }
       }
-      fold_unit(acc, w, wb.codes + slot * slot_ints<T>(), wb.e + slot * (F::span / 32),
-                wb.xs + slot * F::nxs, desc.emin);
+      fold_unit_smem<T>(acc, sl, lane, wb.codes + slot * slot_ints<T>(),
+                        wb.e + slot * (F::span / 32), wb.xs + slot * F::nxs, desc.emin);
+      us.release_front();  // the fold has read the slot: the next copy may refill it
+      us.top_up(g, pc, pn, xn >= 0, lane);
     }
     const bool lead = pc.q == 0;  // the piece that speaks for its row tile off the fast path
     bool done = false;            // this warp completed the row tile
@@ -677,42 +681,24 @@ int plan_build(const PlanSpec &s, int sm_count, PlanHost **out) {
   }
   if (total > INT_MAX / 2) return APX_ERR_TOO_LARGE;
 
-  // Queue order: the given order, except that a projection reading an FFN's activation waits
-  // until two grid-rounds of pieces (2V) have been queued after that FFN's last piece, when
-  // other work is there to fill the gap: the activation is then (nearly) ready when a warp
-  // takes it.
-  std::vector<int> order, pending;
-  std::vector<long long> ready_at(n_ffn, -1);
-  std::vector<int> producers_left(n_ffn, 2);
-  long long emitted = 0;
-  auto emit = [&](int i) {
-    order.push_back(i);
-    emitted += (long long)n_rt[i] * npieces[i];
+  // Queue order by dependency level: a projection reading a resident activation has level 0,
+  // one reading FFN f's activation the level of f's gate and up plus one.  Within a level the
+  // FFN producers (gate / up) go first and the other projections after them, each group in the
+  // given order: by the time a warp reaches a level's readers, every FFN they read had the whole
+  // level's other work to finish in.
+  std::vector<int> level(n_proj, 0), ffn_level(n_ffn, -1);
+  for (int i = 0; i < n_proj; i++) {  // producers come before their readers (plan_check)
+    level[i] = reads[i] < 0 ? 0 : ffn_level[reads[i]] + 1;
     const int f = s.projs[i].ffn;
-    if (f >= 0 && --producers_left[f] == 0) ready_at[f] = emitted + 2 * V;
-  };
-  auto flush = [&](bool all) {
-    for (bool moved = true; moved;) {
-      moved = false;
-      for (size_t k = 0; k < pending.size(); k++) {
-        const int f = reads[pending[k]];
-        if (all || (ready_at[f] >= 0 && ready_at[f] <= emitted)) {
-          const int i = pending[k];
-          pending.erase(pending.begin() + (long)k);
-          emit(i);
-          moved = true;
-          break;
-        }
-      }
-    }
-  };
-  for (int i = 0; i < n_proj; i++) {
-    const int f = reads[i];
-    if (f >= 0 && (ready_at[f] < 0 || ready_at[f] > emitted)) pending.push_back(i);
-    else emit(i);
-    flush(false);
+    if (f >= 0) ffn_level[f] = std::max(ffn_level[f], level[i]);
   }
-  flush(true);
+  std::vector<int> order(n_proj);
+  for (int i = 0; i < n_proj; i++) order[i] = i;
+  std::stable_sort(order.begin(), order.end(), [&](int a0, int b0) {
+    const int ka = 2 * level[a0] + (s.projs[a0].ffn >= 0 ? 0 : 1);
+    const int kb = 2 * level[b0] + (s.projs[b0].ffn >= 0 ? 0 : 1);
+    return ka < kb;
+  });
 
   // device records, in queue order
   std::vector<PlanProjD> pd(n_proj);

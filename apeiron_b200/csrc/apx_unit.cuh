@@ -72,12 +72,51 @@ __device__ __forceinline__ void load_unit_smem(UnitRegs<kQ6_K> &w, const uint8_t
   w.d = *reinterpret_cast<const unsigned short *>(ub + 6656 + lane * 2);
 }
 
-__device__ __forceinline__ void fold_unit(Acc128 &acc, const UnitRegs<kQ8_0> &w, const int *a,
-                                          const int *eabs, const long long *, int) {
+// Two views of a unit for the folds: its registers, loaded beforehand (RegView), or its copy in
+// shared memory, each chunk read where the fold uses it (SmemView: fewer live registers).
+template <uint32_t T>
+struct RegView {
+  const UnitRegs<T> &w;
+  __device__ __forceinline__ uint4 chunk(int c) const { return w.q[c]; }
+};
+template <uint32_t T>
+struct SmemView {
+  const uint8_t *ub;
+  int lane;
+  __device__ __forceinline__ uint4 chunk(int c) const {
+    return *reinterpret_cast<const uint4 *>(ub + (c * 32 + lane) * 16);
+  }
+};
+__device__ __forceinline__ uint2 q8_scales(const RegView<kQ8_0> &v) { return v.w.s; }
+__device__ __forceinline__ uint2 q8_scales(const SmemView<kQ8_0> &v) {
+  return *reinterpret_cast<const uint2 *>(v.ub + 4096 + v.lane * 8);
+}
+__device__ __forceinline__ uint4 q4_head(const RegView<kQ4_K> &v) { return v.w.h; }
+__device__ __forceinline__ uint4 q4_head(const SmemView<kQ4_K> &v) {
+  return *reinterpret_cast<const uint4 *>(v.ub + 4096 + v.lane * 16);
+}
+__device__ __forceinline__ unsigned q6_word(const RegView<kQ6_K> &v, int k) {
+  return reinterpret_cast<const unsigned *>(v.w.q)[k];
+}
+__device__ __forceinline__ unsigned q6_word(const SmemView<kQ6_K> &v, int k) {
+  return *reinterpret_cast<const unsigned *>(v.ub + ((k / 4) * 32 + v.lane) * 16 + (k % 4) * 4);
+}
+__device__ __forceinline__ uint4 q6_scales(const RegView<kQ6_K> &v) { return v.w.sc; }
+__device__ __forceinline__ uint4 q6_scales(const SmemView<kQ6_K> &v) {
+  return *reinterpret_cast<const uint4 *>(v.ub + 6144 + v.lane * 16);
+}
+__device__ __forceinline__ unsigned q6_d(const RegView<kQ6_K> &v) { return v.w.d; }
+__device__ __forceinline__ unsigned q6_d(const SmemView<kQ6_K> &v) {
+  return *reinterpret_cast<const unsigned short *>(v.ub + 6656 + v.lane * 2);
+}
+
+template <class V>
+__device__ __forceinline__ void fold_q8_0(Acc128 &acc, const V &w, const int *a,
+                                          const int *eabs) {
 #pragma unroll
   for (int bi = 0; bi < 4; bi++) {
     const int *x = a + bi * 8;
-    const uint4 q0 = w.q[2 * bi], q1 = w.q[2 * bi + 1];
+    const uint4 q0 = w.chunk(2 * bi), q1 = w.chunk(2 * bi + 1);
     int d = 0;
     d = dp4a_ss((int)q0.x, x[0], d);
     d = dp4a_ss((int)q0.y, x[1], d);
@@ -87,7 +126,8 @@ __device__ __forceinline__ void fold_unit(Acc128 &acc, const UnitRegs<kQ8_0> &w,
     d = dp4a_ss((int)q1.y, x[5], d);
     d = dp4a_ss((int)q1.z, x[6], d);
     d = dp4a_ss((int)q1.w, x[7], d);
-    unsigned bits = ((bi < 2 ? w.s.x : w.s.y) >> (16 * (bi & 1))) & 0xFFFFu;
+    const uint2 sv = q8_scales(w);
+    unsigned bits = ((bi < 2 ? sv.x : sv.y) >> (16 * (bi & 1))) & 0xFFFFu;
     int m;
     unsigned k;
     f16_split(bits, m, k);
@@ -95,13 +135,18 @@ __device__ __forceinline__ void fold_unit(Acc128 &acc, const UnitRegs<kQ8_0> &w,
     if (e >= 0) acc_add_shl(acc, (long long)(m * d), k + (unsigned)e);
   }
 }
+__device__ __forceinline__ void fold_unit(Acc128 &acc, const UnitRegs<kQ8_0> &w, const int *a,
+                                          const int *eabs, const long long *, int) {
+  fold_q8_0(acc, RegView<kQ8_0>{w}, a, eabs);
+}
 
 __device__ __forceinline__ unsigned byte_of(unsigned w, int i) { return (w >> (8 * i)) & 0xFFu; }
 
 // Group p's two dots (low nibbles: group 2p, high nibbles in place as 16·D: group 2p+1).
-__device__ __forceinline__ void q4k_dots(const UnitRegs<kQ4_K> &w, const int *a, int p, int &dl,
+template <class V>
+__device__ __forceinline__ void q4k_dots(const V &w, const int *a, int p, int &dl,
                                          int &dh) {
-  const uint4 w0 = w.q[2 * p], w1 = w.q[2 * p + 1];
+  const uint4 w0 = w.chunk(2 * p), w1 = w.chunk(2 * p + 1);
   const int *xl = a + 16 * p, *xh = a + 16 * p + 8;
   dl = dp4a_us(w0.x & 0x0F0F0F0Fu, xl[0], 0);
   dl = dp4a_us(w0.y & 0x0F0F0F0Fu, xl[1], dl);
@@ -126,10 +171,11 @@ __device__ __forceinline__ void q4k_dots(const UnitRegs<kQ4_K> &w, const int *a,
 // magnitude (|16·D| <= 16·32·15·127, scale <= 63) and eight of them stay below 2^31, so the
 // super-block folds in int32; otherwise in int64 (the call's spread limit keeps that exact).
 constexpr int kQ4Narrow = 2;
-__device__ __forceinline__ void fold_unit(Acc128 &acc, const UnitRegs<kQ4_K> &w, const int *a,
-                                          const int *er, const long long *xs, int emin) {
+template <class V>
+__device__ __forceinline__ void fold_q4_k(Acc128 &acc, const V &w, const int *a, const int *er,
+                                          const long long *xs, int emin) {
   // get_scale_min_k4 (format/quant.rs:482-491) for all 8 pairs at once.
-  const uint4 h = w.h;
+  const uint4 h = q4_head(w);
   const unsigned sc_lo = h.y & 0x3F3F3F3Fu, mn_lo = h.z & 0x3F3F3F3Fu;
   const unsigned sc_hi = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
   const unsigned mn_hi = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
@@ -177,10 +223,15 @@ __device__ __forceinline__ void fold_unit(Acc128 &acc, const UnitRegs<kQ4_K> &w,
   acc_add_shl(acc, (long long)md * A16, kd + (unsigned)emin - 4u);
   acc_sub_shl(acc, (long long)mm * B, km + (unsigned)emin);
 }
+__device__ __forceinline__ void fold_unit(Acc128 &acc, const UnitRegs<kQ4_K> &w, const int *a,
+                                          const int *er, const long long *xs, int emin) {
+  fold_q4_k(acc, RegView<kQ4_K>{w}, a, er, xs, emin);
+}
 
-__device__ __forceinline__ void fold_unit(Acc128 &acc, const UnitRegs<kQ6_K> &wr, const int *a,
-                                          const int *er, const long long *xs16, int emin) {
-  const unsigned *w = reinterpret_cast<const unsigned *>(wr.q);  // ql words 0..31, qh 32..47
+template <class V>
+__device__ __forceinline__ void fold_q6_k(Acc128 &acc, const V &wr, const int *a, const int *er,
+                                          const long long *xs16, int emin) {
+  // ql words 0..31, qh words 32..47
   int du[16];
 #pragma unroll
   for (int g = 0; g < 16; g++) du[g] = 0;
@@ -188,7 +239,8 @@ __device__ __forceinline__ void fold_unit(Acc128 &acc, const UnitRegs<kQ6_K> &wr
   for (int n = 0; n < 2; n++) {
 #pragma unroll
     for (int j = 0; j < 8; j++) {
-      unsigned ql0 = w[16 * n + j], ql1 = w[16 * n + 8 + j], qh = w[32 + 8 * n + j];
+      unsigned ql0 = q6_word(wr, 16 * n + j), ql1 = q6_word(wr, 16 * n + 8 + j),
+               qh = q6_word(wr, 32 + 8 * n + j);
       unsigned u1 = (ql0 & 0x0F0F0F0Fu) | ((qh << 4) & 0x30303030u);
       unsigned u2 = (ql1 & 0x0F0F0F0Fu) | ((qh << 2) & 0x30303030u);
       unsigned u3 = ((ql0 >> 4) & 0x0F0F0F0Fu) | (qh & 0x30303030u);
@@ -200,7 +252,8 @@ __device__ __forceinline__ void fold_unit(Acc128 &acc, const UnitRegs<kQ6_K> &wr
       du[g + 6] = dp4a_us(u4, a[32 * n + 24 + j], du[g + 6]);
     }
   }
-  const unsigned scw[4] = {wr.sc.x, wr.sc.y, wr.sc.z, wr.sc.w};
+  const uint4 scv = q6_scales(wr);
+  const unsigned scw[4] = {scv.x, scv.y, scv.z, scv.w};
   long long A = 0, B = 0;
 #pragma unroll
   for (int g = 0; g < 16; g++) {
@@ -211,8 +264,22 @@ __device__ __forceinline__ void fold_unit(Acc128 &acc, const UnitRegs<kQ6_K> &wr
   long long Tv = A - 32 * B;  // codes are u - 32 (format/quant.rs:574-599)
   int md;
   unsigned kd;
-  f16_split(wr.d, md, kd);
+  f16_split(q6_d(wr), md, kd);
   acc_add_shl(acc, (long long)md * Tv, kd + (unsigned)emin);
+}
+__device__ __forceinline__ void fold_unit(Acc128 &acc, const UnitRegs<kQ6_K> &wr, const int *a,
+                                          const int *er, const long long *xs16, int emin) {
+  fold_q6_k(acc, RegView<kQ6_K>{wr}, a, er, xs16, emin);
+}
+
+// The fold of a unit read from its copy in shared memory.
+template <uint32_t T>
+__device__ __forceinline__ void fold_unit_smem(Acc128 &acc, const uint8_t *ub, int lane,
+                                               const int *a, const int *er, const long long *xs,
+                                               int emin) {
+  if (T == kQ8_0) fold_q8_0(acc, SmemView<kQ8_0>{ub, lane}, a, er);
+  else if (T == kQ4_K) fold_q4_k(acc, SmemView<kQ4_K>{ub, lane}, a, er, xs, emin);
+  else fold_q6_k(acc, SmemView<kQ6_K>{ub, lane}, a, er, xs, emin);
 }
 
 

@@ -395,8 +395,9 @@ def measure_decode_step(be, lib, dev, stream, steps, warmup, pg, local, world):
                                "896x4864) Q4_K + tied lm_head 151936x896 Q6_K = 169 projections "
                                "in 2 launches: one step plan (168 layer projections; each "
                                "layer's down reads the hidden activation its FFN's SwiGLU + "
-                               "quant_act produces on the device) and the head; q/k/v/o/gate/up "
-                               "read resident activations",
+                               "quant_act produces on the device; the plan queues by dependency "
+                               "level: gate/up, then q/k/v/o, then down) and the head; "
+                               "q/k/v/o/gate/up read resident activations",
                    "bytes_per_step": per_step, "weight_copies": copies,
                    "l2": "rotating weight copies, >= 3x the 126 MB L2",
                    "exact": "layer 0's q/k/v/o/gate/up, its h codes and its down output (the "
