@@ -45,9 +45,10 @@ EXPORTS = [
     "apx_peer_alloc", "apx_peer_open", "apx_peer_close", "apx_device_read",
     "apx_gather_publish_async", "apx_matvec_gather_async", "apx_matvec_group_async",
     "apx_swiglu_quant_async", "apx_swiglu_quant_cols_async", "apx_act_describe_cols_async",
-    "apx_ffn_status_decode", "apx_plan_create", "apx_plan_run_async", "apx_plan_destroy",
+    "apx_ffn_status_decode", "apx_ctx_set_gemm_route", "apx_plan_create", "apx_plan_run_async", "apx_plan_destroy",
 ]
 PLAN_GATE, PLAN_UP = 0, 1
+GEMM_AUTO, GEMM_DIGITS, GEMM_FOLD = 0, 1, 2
 CARRIER_F32, CARRIER_Q32 = 0, 1
 
 MAX_PEERS = 8
@@ -156,6 +157,7 @@ _SIGS = {
     "apx_plan_create": (P, [P, C.POINTER(PlanProj), SZ, C.POINTER(PlanAct), SZ,
                             C.POINTER(PlanFfn), SZ, EP]),
     "apx_plan_run_async": (C.c_int, [P, P]),
+    "apx_ctx_set_gemm_route": (C.c_int, [P, C.c_int]),
     "apx_plan_destroy": (None, [P]),
     "apx_matvec_f32_noalloc": (C.c_int, [P, U64, SZ, SZ, P, P, P, P]),
     "apx_matmat_f32": (C.c_int, [P, U64, SZ, SZ, SZ, P, P, EP]),

@@ -138,6 +138,7 @@ struct apx_ctx {
   DevBuf lwork;    // digit-plane GEMM per-call workspace (no state kept between calls)
   DevBuf ascratch; // codes / exps / descriptors of apx_matmat_f32_async off the fused route
   DevBuf fwork;    // per-CTA statistics of apx_swiglu_quant_async
+  int gemm_route = APX_GEMM_AUTO;  // apx_ctx_set_gemm_route
   HostBuf host;    // pinned mirror of `dev`
 };
 
@@ -392,12 +393,23 @@ bool gemm_route(apx_ctx *ctx, Tensor &t, size_t n_out, size_t n_in, size_t k_col
   return gemm_supported(t.gemm);
 }
 
-// The tensor-core route of a k-column call: the digit-plane GEMM (apx_lgemm.cu) for every family
-// whose weights fit four digits, else the fold GEMM for Q8_0, else one GEMV per column.
+// The tensor-core route of a k-column call: a Q8_0 call below kFoldMaxMacs on the fold GEMM
+// (apx_gemm.cu); otherwise the digit-plane GEMM (apx_lgemm.cu) for every family whose weights
+// fit four digits, else the fold GEMM for Q8_0, else one GEMV per column.
 enum TcRoute { kTcNone = 0, kTcLimb = 1, kTcFold = 2 };
+
+// Below this many multiply-adds a Q8_0 call runs faster on the per-block fold GEMM than on the
+// digit planes (B200, 512 tokens: 4864x896 38.6 vs 47.2 us, 896x4864 37.5 vs 59.7 us; above it
+// 8192x8192 277 vs 222 us, 28672x8192 918 vs 697 us): the fold's work per MMA is one int8 dot
+// against the digit planes' six, but its exact per-block epilogue grows with the call.
+constexpr double kFoldMaxMacs = 6e9;
 
 TcRoute tc_route(apx_ctx *ctx, Tensor &t, size_t n_out, size_t n_in, size_t k_cols) {
   if (k_cols < kGemmMinCols || n_out == 0 || !t.d_pack) return kTcNone;
+  const bool small = (double)n_out * (double)n_in * (double)k_cols < kFoldMaxMacs;
+  if (t.type == kQ8_0 && ctx->gemm_route != APX_GEMM_DIGITS &&
+      (small || ctx->gemm_route == APX_GEMM_FOLD) && gemm_route(ctx, t, n_out, n_in, k_cols))
+    return kTcFold;
   if (limb_shape_ok(n_in)) {
     if (!t.limb_tried) {
       t.limb_tried = true;
@@ -1207,6 +1219,14 @@ int apx_status_decode(apx_ctx *ctx, uint64_t tensor, const apx_call_status *stat
   Tensor *t = find(ctx, tensor);
   if (!t) return set_err(err, APX_ERR_INVALID_ARGUMENT);
   return decode_status(*t, t->n_out, status->first, err);
+}
+
+int apx_ctx_set_gemm_route(apx_ctx *ctx, int route) {
+  if (!ctx || (route != APX_GEMM_AUTO && route != APX_GEMM_DIGITS && route != APX_GEMM_FOLD))
+    return APX_ERR_INVALID_ARGUMENT;
+  std::lock_guard<std::mutex> g(ctx->mu);
+  ctx->gemm_route = route;
+  return APX_OK;
 }
 
 int apx_status_decode_rows(apx_ctx *ctx, uint64_t tensor, size_t n_out,

@@ -105,6 +105,15 @@ typedef struct apx_call_status {
 
 /* ---- context ---------------------------------------------------------------- */
 
+/* Which tensor-core GEMM a Q8_0 multi-column call takes.  APX_GEMM_AUTO (the default): the
+ * per-block fold GEMM below 6e9 multiply-adds per call (faster there on B200), the digit-plane
+ * GEMM above; APX_GEMM_DIGITS / APX_GEMM_FOLD: that GEMM whenever the tensor has its view.  The
+ * results are the same bits on every route; K-quant tensors always take the digit planes. */
+#define APX_GEMM_AUTO 0
+#define APX_GEMM_DIGITS 1
+#define APX_GEMM_FOLD 2
+APX_API int apx_ctx_set_gemm_route(apx_ctx *ctx, int route);
+
 /* Open a backend context on CUDA device `device`.  Returns NULL on failure. */
 APX_API apx_ctx *apx_open(int device, apx_err *err);
 /* Free every device buffer the context owns. */

@@ -16,7 +16,7 @@ import pytest
 
 from oracle import oracle as O
 from chart_inputs import random_payload, random_x
-from apeiron_b200 import chart, synth
+from apeiron_b200 import _abi, chart, synth
 from apeiron_b200.chart import Backend, QuantAct
 
 pytestmark = pytest.mark.gpu
@@ -31,6 +31,9 @@ THREADS = os.cpu_count() or 1
 @pytest.fixture(scope="module")
 def be():
     b = Backend(0)
+    # this module is about the digit-plane GEMM: Q8_0 calls of every size take it (by default
+    # the small ones run the per-block fold GEMM, tested in test_gpu_gemm.py)
+    assert b.lib.apx_ctx_set_gemm_route(b.ctx, _abi.GEMM_DIGITS) == 0
     yield b
     b.close()
 
@@ -236,3 +239,23 @@ def test_device_descriptors_and_large_exponents(be, t, n_out, n_in, k, e0, sprea
     bad = np.argwhere(got != want)
     assert bad.size == 0, (f"{len(bad)} differ; first col {bad[0][0]} row {bad[0][1]}: gpu "
                            f"{got[tuple(bad[0])]} oracle {want[tuple(bad[0])]}")
+
+
+def test_auto_route_by_call_size(be):
+    """APX_GEMM_AUTO: a small Q8_0 call runs the per-block fold GEMM (the tensor gains its fold
+    view, not digit planes), a K-quant call the digit planes; both bit-exact; a bad route code is
+    refused."""
+    assert be.lib.apx_ctx_set_gemm_route(be.ctx, 7) == _abi.APX_ERR_INVALID_ARGUMENT
+    assert be.lib.apx_ctx_set_gemm_route(be.ctx, _abi.GEMM_AUTO) == 0
+    try:
+        n_out, n_in, k = 896, 4864, 64
+        raw = synth.payload(Q8_0, n_out, n_in, 123)
+        _, grown = run_and_check_route(be, Q8_0, raw, n_out, n_in, bench_columns(n_in, k, 5),
+                                       threads=THREADS)
+        assert grown > 0 and grown not in digit_plane_bytes(n_out, n_in)
+        raw = synth.payload(Q4_K, n_out, n_in, 124)
+        _, grown = run_and_check_route(be, Q4_K, raw, n_out, n_in, bench_columns(n_in, 8, 6),
+                                       threads=THREADS)
+        assert grown in digit_plane_bytes(n_out, n_in)
+    finally:
+        assert be.lib.apx_ctx_set_gemm_route(be.ctx, _abi.GEMM_DIGITS) == 0
