@@ -42,12 +42,14 @@ EXPORTS = [
     "apx_act_describe_async", "apx_quant_q32_async", "apx_quant_f32_async",
     "apx_matvec_async", "apx_matmat_async", "apx_matmat_f32_async", "apx_act_padded_len", "apx_status_decode", "apx_status_decode_rows",
     "apx_matvec_f32_noalloc", "apx_matmat_f32", "apx_quant_f32_cols_async",
-    "apx_peer_alloc", "apx_peer_open", "apx_peer_close", "apx_device_read",
+    "apx_peer_alloc", "apx_peer_open", "apx_peer_close", "apx_device_read", "apx_device_write",
     "apx_gather_publish_async", "apx_matvec_gather_async", "apx_matvec_group_async",
     "apx_swiglu_quant_async", "apx_swiglu_quant_cols_async", "apx_act_describe_cols_async",
     "apx_ffn_status_decode", "apx_ctx_set_gemm_route", "apx_plan_create", "apx_plan_run_async", "apx_plan_destroy",
 ]
 PLAN_GATE, PLAN_UP = 0, 1
+PLAN_MAX_PEERS = 7
+PLAN_ACT_UNPADDED = 1
 GEMM_AUTO, GEMM_DIGITS, GEMM_FOLD = 0, 1, 2
 CARRIER_F32, CARRIER_Q32 = 0, 1
 
@@ -91,6 +93,8 @@ class GatherDesc(C.Structure):
         ("status", C.c_void_p * MAX_GATHER_PROJ),
         ("out_status", C.c_void_p * MAX_GATHER_PROJ),
         ("bytes", C.c_size_t),
+        ("desc_off", C.c_size_t),
+        ("merged_off", C.c_size_t),
     ]
 
 
@@ -101,7 +105,7 @@ class CallStatus(C.Structure):
 P = C.c_void_p
 class PlanAct(C.Structure):
     _fields_ = [("d_codes", C.c_void_p), ("d_exps", C.c_void_p), ("d_desc", C.c_void_p),
-                ("ffn", C.c_int32), ("reserved", C.c_int32)]
+                ("ffn", C.c_int32), ("flags", C.c_int32)]
 
 
 class PlanProj(C.Structure):
@@ -113,7 +117,10 @@ class PlanProj(C.Structure):
 
 class PlanFfn(C.Structure):
     _fields_ = [("carrier", C.c_int32), ("out_act", C.c_int32), ("d_h", C.c_void_p),
-                ("d_status", C.c_void_p)]
+                ("d_status", C.c_void_p), ("n_peers", C.c_int32), ("reserved", C.c_int32),
+                ("d_peer_codes", C.c_void_p * PLAN_MAX_PEERS),
+                ("d_peer_exps", C.c_void_p * PLAN_MAX_PEERS),
+                ("d_peer_desc", C.c_void_p * PLAN_MAX_PEERS)]
 
 
 SZ = C.c_size_t
@@ -141,6 +148,7 @@ _SIGS = {
     "apx_peer_open": (C.c_int, [P, P, C.POINTER(C.c_void_p), EP]),
     "apx_peer_close": (C.c_int, [P, P, C.c_int]),
     "apx_device_read": (C.c_int, [P, P, P, SZ, EP]),
+    "apx_device_write": (C.c_int, [P, P, P, SZ, EP]),
     "apx_gather_publish_async": (C.c_int, [P, C.POINTER(GatherDesc), P]),
     "apx_matvec_gather_async": (C.c_int, [P, U64, SZ, SZ, P, P, P, C.POINTER(GatherDesc),
                                           C.c_int, P]),

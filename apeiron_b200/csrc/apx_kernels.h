@@ -200,6 +200,10 @@ struct PlanSpec {
     long long *h;                // or null
     unsigned long long *status;  // the first refusing SwiGLU lane
     bool refused;                // gate or up holds a non-finite scale below the width
+    int n_peers;                 // copies of the quantized blocks and the descriptor
+    int8_t *peer_codes[7];
+    uint8_t *peer_exps[7];
+    void *peer_desc[7];          // ActDesc
   };
   std::vector<Proj> projs;
   std::vector<Act> acts;

@@ -101,6 +101,29 @@ __global__ void __launch_bounds__(32) gather_publish_kernel(const __grid_constan
     g.out_status[j]->spare = 0;
     g.status[j]->first = ~0ull;  // ready for the next projection into it
   }
+  if (g.desc_off) {  // the ranks' slice descriptors of a sharded activation, merged
+    const ActDesc *sl = reinterpret_cast<const ActDesc *>(own + g.desc_off);
+    int status = APX_OK, emin = 1 << 30, emax = -1, n = 0;
+    unsigned nz = 0;
+    for (int r = 0; r < g.world; r++) {
+      const ActDesc d = sl[r];  // stored before rank r's flag, read after its acquire
+      status = max(status, d.status);
+      if (d.emax >= 0) {
+        emin = min(emin, d.emin);
+        emax = max(emax, d.emax);
+      }
+      nz += d.nz;
+      n += d.n_in;
+    }
+    ActDesc m;
+    m.status = ok ? status : (int)APX_ERR_DEVICE_TIMEOUT;
+    m.emin = emax >= 0 ? emin : 0;
+    m.emax = emax;
+    m.n_in = n;
+    m.nz = nz;
+    m.pad[0] = m.pad[1] = m.pad[2] = 0;  // quant_act codes are never -128
+    *reinterpret_cast<ActDesc *>(own + g.merged_off) = m;
+  }
   *reinterpret_cast<volatile unsigned long long *>(ctr) = epoch;
 }
 
@@ -167,6 +190,14 @@ APX_API int apx_device_read(apx_ctx *ctx, const void *d_src, void *host_dst, siz
   return e == cudaSuccess ? fail(err, APX_OK) : fail(err, APX_ERR_CUDA, e);
 }
 
+APX_API int apx_device_write(apx_ctx *ctx, void *d_dst, const void *host_src, size_t bytes,
+                             apx_err *err) {
+  if (!ctx || (bytes && (!d_dst || !host_src))) return fail(err, APX_ERR_INVALID_ARGUMENT);
+  cudaError_t e = cudaSetDevice(apx::context_device(ctx));
+  if (e == cudaSuccess && bytes) e = cudaMemcpy(d_dst, host_src, bytes, cudaMemcpyHostToDevice);
+  return e == cudaSuccess ? fail(err, APX_OK) : fail(err, APX_ERR_CUDA, e);
+}
+
 namespace {
 // [off, off + len) inside a buffer of `bytes` (no wrap-around).
 bool inside(size_t off, size_t len, size_t bytes) { return off <= bytes && len <= bytes - off; }
@@ -228,7 +259,10 @@ APX_API int apx_gather_publish_async(apx_ctx *ctx, const apx_gather_desc *gd, vo
     if (!gd->status[j] || !gd->out_status[j]) return APX_ERR_INVALID_ARGUMENT;
   // the keys ([world][nproj] int64), the flags ([world] uint64) and this rank's epoch and
   // check-in count (2 uint64) lie inside every rank's buffer
-  if (!inside(gd->key_off, 8 * (size_t)gd->world * (size_t)gd->nproj, gd->bytes) ||
+  if ((gd->desc_off && (gd->desc_off % 16 || gd->merged_off % 16 ||
+                        !inside(gd->desc_off, sizeof(apx_act_desc) * (size_t)gd->world, gd->bytes) ||
+                        !inside(gd->merged_off, sizeof(apx_act_desc), gd->bytes))) ||
+      !inside(gd->key_off, 8 * (size_t)gd->world * (size_t)gd->nproj, gd->bytes) ||
       !inside(gd->flag_off, 8 * (size_t)gd->world, gd->bytes) ||
       !inside(gd->ctr_off, 16, gd->bytes))
     return APX_ERR_INVALID_ARGUMENT;

@@ -18,10 +18,11 @@
 // several through partial sums in the plan's scratch and a self-resetting arrival counter (the
 // last to arrive finishes it).
 //
-// Hand-off.  The finish of a gate or up row tile (32 rows: one quant_act block of h) counts on a
-// per-block counter; the second of the two runs SwiGLU under the carrier and quant_act for the
-// block and adds the block's exponent statistics to the FFN's; the last block publishes the
-// descriptor and raises the FFN's flag.  A warp that takes a piece reading that activation waits
+// Hand-off.  The finish of a gate or up row tile counts on the counter of its 32-row block of h
+// (one quant_act block: L row tiles of 32/L rows in each projection); the last of the block's
+// row tiles runs SwiGLU under the carrier and quant_act for the block and adds the block's
+// exponent statistics to the FFN's; the last block publishes the descriptor and raises the
+// FFN's flag.  A warp that takes a piece reading that activation waits
 // on the flag first, with a bound (about one second) after which the projection refuses with
 // APX_ERR_DEVICE_TIMEOUT.  The host queues projections by dependency level, an FFN's producers
 // ahead of the level's other work and its readers in the next level, so the flag is usually up
@@ -79,7 +80,10 @@ struct PlanFfnD {
   unsigned *pair;              // [n_rt] row tiles of the block done (self-resetting)
   size_t n;
   int n_rt, carrier, refused;  // refused: a non-finite weight row below n (found at upload)
-  int pad;
+  int n_peers;                 // row shards: where else the blocks and the descriptor go
+  int8_t *peer_codes[7];
+  uint8_t *peer_exps[7];
+  ActDesc *peer_desc[7];
 };
 
 struct PlanArgs {
@@ -177,8 +181,14 @@ __device__ void ffn_block(const PlanArgs &g, int f, int rt, int lane) {
     if (__any_sync(0xFFFFFFFFu, mag > 127 || !product_fits(code, e)))
       w_status = APX_ERR_QUANT_REFUSED;
   }
+  const uint8_t eb = e < 0 || e == 99 ? (uint8_t)APX_EXP_ZERO : (uint8_t)e;
   if (row < F.n) F.codes[row] = (int8_t)code;
-  if (lane == 0) F.exps[rt] = e < 0 || e == 99 ? (uint8_t)APX_EXP_ZERO : (uint8_t)e;
+  if (lane == 0) F.exps[rt] = eb;
+#pragma unroll 1
+  for (int p = 0; p < F.n_peers; p++) {  // row shards: the block into the other ranks' buffers
+    if (row < F.n) F.peer_codes[p][row] = (int8_t)code;
+    if (lane == 0) F.peer_exps[p][rt] = eb;
+  }
   __threadfence();  // every lane's stores before the block counts
   __syncwarp();
   int *st = g.ctl->stats[f];
@@ -211,6 +221,7 @@ __device__ void ffn_block(const PlanArgs &g, int f, int rt, int lane) {
       d.pad[1] = 0;
       d.pad[2] = 0;
       *F.desc = d;
+      for (int p = 0; p < F.n_peers; p++) *F.peer_desc[p] = d;
       __threadfence();
       atomicExch(&g.ctl->flag[f], 1u);
     }
@@ -492,17 +503,20 @@ __global__ void __launch_bounds__(PlanShape<T>::kThreads, PlanShape<T>::kCtas)
                    PeerRows{});
       done = fin;
     }
-    // -- the FFN hand-off: the second of a block's gate and up row tiles runs its SwiGLU --
+    // -- the FFN hand-off: a 32-row block of h covers L row tiles of gate and of up; the last
+    // of them to finish runs the block's SwiGLU --
     if (done && P.ffn >= 0) {
+      const int blk = pc.rt / L;
+      const int need = 2 * (min(P.n_rt, (blk + 1) * L) - blk * L);
       __threadfence();
       __syncwarp();
       unsigned old = 0;
-      if (lane == 0) old = atomicAdd(g.ffn[P.ffn].pair + pc.rt, 1u);
+      if (lane == 0) old = atomicAdd(g.ffn[P.ffn].pair + blk, 1u);
       old = __shfl_sync(0xFFFFFFFFu, old, 0);
-      if (old == 1) {
-        if (lane == 0) g.ffn[P.ffn].pair[pc.rt] = 0u;  // ready for the next launch
+      if (old == (unsigned)need - 1) {
+        if (lane == 0) g.ffn[P.ffn].pair[blk] = 0u;  // ready for the next launch
         __threadfence();
-        ffn_block(g, P.ffn, pc.rt, lane);
+        ffn_block(g, P.ffn, blk, lane);
       }
     }
     if (!copies_ok) break;  // the ring's phases are lost: this warp stops
@@ -621,11 +635,13 @@ int plan_check(const PlanSpec &s, std::vector<int> &gate, std::vector<int> &up,
   for (int f = 0; f < n_ffn; f++) {
     const PlanSpec::Ffn &x = s.ffns[f];
     if (gate[f] < 0 || up[f] < 0 || x.out_act < 0 || x.out_act >= n_act ||
-        s.acts[x.out_act].ffn != f)
+        s.acts[x.out_act].ffn != f || x.n_peers < 0 || x.n_peers > 7)
       return APX_ERR_INVALID_ARGUMENT;
+    for (int p = 0; p < x.n_peers; p++)
+      if (!x.peer_codes[p] || !x.peer_exps[p] || !x.peer_desc[p]) return APX_ERR_INVALID_ARGUMENT;
     const PlanSpec::Proj &pg = s.projs[gate[f]], &pu = s.projs[up[f]];
-    if (pg.n_out != pu.n_out || pg.n_in != pu.n_in || pg.act != pu.act || pg.plan.L != 1 ||
-        pu.plan.L != 1 || !pg.out_q32 || !pu.out_q32)
+    if (pg.n_out != pu.n_out || pg.n_in != pu.n_in || pg.act != pu.act ||
+        pg.plan.L != pu.plan.L || !pg.out_q32 || !pu.out_q32)
       return APX_ERR_INVALID_ARGUMENT;
     // readers of the FFN's activation come after both of its projections, at its width
     for (int i = 0; i < n_proj; i++)
@@ -756,6 +772,12 @@ int plan_build(const PlanSpec &s, int sm_count, PlanHost **out) {
     d.n_rt = (int)((pg.n_out + 31) / 32);
     d.carrier = x.carrier;
     d.refused = x.refused ? 1 : 0;
+    d.n_peers = x.n_peers;
+    for (int p = 0; p < x.n_peers; p++) {
+      d.peer_codes[p] = x.peer_codes[p];
+      d.peer_exps[p] = x.peer_exps[p];
+      d.peer_desc[p] = static_cast<ActDesc *>(x.peer_desc[p]);
+    }
     pair_off[f] = scratch;
     scratch += al256((size_t)d.n_rt * 4);
   }

@@ -1307,6 +1307,16 @@ apx_plan *apx_plan_create(apx_ctx *ctx, const apx_plan_proj *projs, size_t n_pro
       x.h = (long long *)ffns[f].d_h;
       x.status = ffns[f].d_status ? (unsigned long long *)&ffns[f].d_status->first : nullptr;
       x.refused = false;
+      x.n_peers = ffns[f].n_peers;
+      if (x.n_peers < 0 || x.n_peers > APX_PLAN_MAX_PEERS) {
+        rc = APX_ERR_INVALID_ARGUMENT;
+        break;
+      }
+      for (int p = 0; p < x.n_peers; p++) {
+        x.peer_codes[p] = ffns[f].d_peer_codes[p];
+        x.peer_exps[p] = ffns[f].d_peer_exps[p];
+        x.peer_desc[p] = ffns[f].d_peer_desc[p];
+      }
       if ((x.carrier != APX_CARRIER_F32 && x.carrier != APX_CARRIER_Q32) || !x.status) {
         rc = APX_ERR_INVALID_ARGUMENT;
         break;
@@ -1322,7 +1332,8 @@ apx_plan *apx_plan_create(apx_ctx *ctx, const apx_plan_proj *projs, size_t n_pro
   for (size_t a = 0; a < n_act && rc == APX_OK; a++) {
     const apx_plan_act &x = acts[a];
     s.acts.push_back(PlanSpec::Act{x.d_codes, x.d_exps, x.d_desc, x.ffn});
-    if (x.ffn >= 0 && (size_t)x.ffn < n_ffn && x.d_codes && x.d_exps) {
+    if (x.ffn >= 0 && (size_t)x.ffn < n_ffn && x.d_codes && x.d_exps &&
+        !(x.flags & APX_PLAN_ACT_UNPADDED)) {
       // the FFN writes codes [0, n) and exponent bytes [0, ceil(n/32)): the rest of the
       // padded buffers reads as zero blocks
       size_t n = 0;

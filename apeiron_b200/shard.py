@@ -432,6 +432,154 @@ class PeerGather:
             self.local = 0
 
 
+class _Ptr:
+    """A device address where torch tensors are expected (``.data_ptr()``)."""
+
+    def __init__(self, addr: int):
+        self.addr = addr
+
+    def data_ptr(self) -> int:
+        return self.addr
+
+
+class HiddenGather:
+    """The quantized hidden activation h of a row-sharded FFN, assembled on every rank.
+
+    Rank r's step plan (apx_plan_*) runs gate and up on its rows with SwiGLU + quant_act in
+    their finish (h rows g0..g1, whole 32-row blocks), storing each block's codes and exponent
+    byte, and its slice's descriptor, into every rank's buffer here; `publish` then posts the
+    gate/up refusal keys and an epoch flag everywhere, waits (bounded) for every rank's, and
+    merges the ranks' slice descriptors into the descriptor of the whole h, which the down
+    projection reads.  Only the int8 codes and exponent bytes cross NVLink (n_ff + n_ff/32
+    bytes per step over all ranks), not the int64 gate and up outputs.
+
+    Layout, the same on every rank, parity p (0, 1) at p·stride: codes [padded n_ff], exponent
+    bytes [padded n_ff / 32], slice descriptors [world] × 32 B, the merged descriptor, the keys
+    [world][2]; after both parities the flags [world] and this rank's epoch counters.  Parities
+    alternate per publication (an even number per CUDA graph keeps them in step on replay).
+    """
+
+    def __init__(self, lib, ctx, gate: RowShard, up: RowShard, timeout_us: int = 2_000_000):
+        import ctypes as C
+
+        if gate.splits != up.splits or gate.n_out != up.n_out or gate.world > _abi.MAX_PEERS:
+            raise ValueError("gate and up must share their row split")
+        if any(a % 32 for a, _ in gate.splits):
+            raise ValueError("hidden slices must start on 32-row blocks")
+        self.lib, self.ctx, self.gate, self.up = lib, ctx, gate, up
+        self.world, self.rank, self.dist, self.group = gate.world, gate.rank, gate.dist, gate.group
+        self.n = gate.n_out
+        pad = int(lib.apx_act_padded_len(self.n))
+        self.codes_rel = 0
+        self.exps_rel = _align(pad)
+        self.desc_rel = self.exps_rel + _align(pad // 32)
+        self.merged_rel = self.desc_rel + 32 * self.world
+        self.key_rel = _align(self.merged_rel + 32)
+        self.stride = _align(self.key_rel + 8 * self.world * 2)
+        self.flag_off = 2 * self.stride
+        self.ctr_off = self.flag_off + _align(8 * self.world)
+        total = self.ctr_off + 256
+        ptr, handle = C.c_void_p(), (C.c_ubyte * _abi.PEER_HANDLE_BYTES)()
+        err = _abi.ApxErr()
+        if lib.apx_peer_alloc(ctx, total, C.byref(ptr), handle, C.byref(err)):
+            raise chart.BackendError(f"apx_peer_alloc failed (cuda {err.cuda_error})")
+        self.local = ptr.value
+        # exponent bytes past n read as zero blocks in both parities
+        ff = np.full(pad // 32 - self.n // 32, 0xFF, dtype=np.uint8)
+        for par in (0, 1):
+            if ff.size and lib.apx_device_write(ctx, self.local + par * self.stride +
+                                                self.exps_rel + self.n // 32, ff.ctypes.data,
+                                                ff.size, C.byref(err)):
+                raise chart.BackendError("apx_device_write failed")
+        handles = [bytes(handle)] * self.world
+        if self.world > 1 and self.dist is not None:
+            self.dist.all_gather_object(handles, bytes(handle), group=self.group)
+        self.peers, self.opened = [], []
+        for r in range(self.world):
+            if r == self.rank:
+                self.peers.append(self.local)
+                continue
+            hp, err = C.c_void_p(), _abi.ApxErr()
+            hb = (C.c_ubyte * _abi.PEER_HANDLE_BYTES).from_buffer_copy(handles[r])
+            if lib.apx_peer_open(ctx, hb, C.byref(hp), C.byref(err)):
+                raise chart.BackendError(f"apx_peer_open of rank {r} failed "
+                                         f"(cuda {err.cuda_error})")
+            self.peers.append(hp.value)
+            self.opened.append(hp.value)
+        d = _abi.GatherDesc()
+        d.world, d.rank, d.nproj, d.timeout_us = self.world, self.rank, 2, timeout_us
+        for r, pv in enumerate(self.peers):
+            d.peer[r] = pv
+        d.flag_off, d.ctr_off, d.bytes = self.flag_off, self.ctr_off, total
+        for j, sh in enumerate((gate, up)):
+            d.row0[j] = sh.r0
+            d.nf_key[j] = sh.nf_word if sh.nf_word is not None else _I64_MAX
+        self.desc = d
+        self.calls = 0
+
+    def next_parity(self) -> int:
+        return (self.calls + 1) % 2
+
+    def slice_dest(self, parity: int, r: int):
+        """(codes, exps, descriptor slot) of this rank's slice in rank r's buffer."""
+        base = self.peers[r] + parity * self.stride
+        g0 = self.gate.r0
+        return (base + self.codes_rel + g0, base + self.exps_rel + g0 // 32,
+                base + self.desc_rel + 32 * self.rank)
+
+    def activation(self, parity: int):
+        """The whole h in this rank's buffer: (codes, exps, merged descriptor) addresses."""
+        base = self.local + parity * self.stride
+        return (_Ptr(base + self.codes_rel), _Ptr(base + self.exps_rel),
+                _Ptr(base + self.merged_rel))
+
+    def publish(self, statuses, out_statuses, stream) -> int:
+        """Queue the publication of the next parity: `statuses` (2, 2) int64, the gate and up
+        refusal words the plan wrote (reset by the publication), `out_statuses` (2, 2) the
+        first refusal of each over all ranks.  Returns the parity."""
+        import ctypes as C
+
+        parity = self.next_parity()
+        d = self.desc
+        base = parity * self.stride
+        d.key_off = base + self.key_rel
+        d.desc_off = base + self.desc_rel
+        d.merged_off = base + self.merged_rel
+        d.out_off = base
+        for j in range(2):
+            d.status[j] = statuses[j].data_ptr()
+            d.out_status[j] = out_statuses[j].data_ptr()
+        rc = self.lib.apx_gather_publish_async(self.ctx, C.byref(d), stream)
+        if rc:
+            raise chart.BackendError(f"apx_gather_publish_async failed with code {rc}")
+        self.calls += 1
+        return parity
+
+    def read(self, parity: int):
+        """(codes, exponent bytes, merged descriptor words) of the whole h (synchronous)."""
+        import ctypes as C
+
+        codes = np.empty(self.n, dtype=np.int8)
+        exps = np.empty(self.n // 32, dtype=np.uint8)
+        desc = np.empty(8, dtype=np.int32)
+        err = _abi.ApxErr()
+        base = self.local + parity * self.stride
+        for addr, arr in ((base + self.codes_rel, codes), (base + self.exps_rel, exps),
+                          (base + self.merged_rel, desc)):
+            if self.lib.apx_device_read(self.ctx, addr, arr.ctypes.data, arr.nbytes,
+                                        C.byref(err)):
+                raise chart.BackendError("apx_device_read failed")
+        return codes, exps, desc
+
+    def close(self) -> None:
+        for pv in self.opened:
+            self.lib.apx_peer_close(self.ctx, pv, 1)
+        self.opened = []
+        if self.local:
+            self.lib.apx_peer_close(self.ctx, self.local, 0)
+            self.local = 0
+
+
 def shard_projections(backend, mats: Sequence[Tuple[int, object, int, int]], rank: int,
                       world: int, dist=None, device: str = "cpu", group=None) -> List[RowShard]:
     """Row shards of several projections (ggml_type, raw, n_out, n_in), one per matrix."""

@@ -418,14 +418,19 @@ SHARDED = [(12, 28672, 8192), (12, 28672, 8192), (12, 8192, 28672)]  # gate, up,
 
 
 def measure_sharded(be, lib, dev, stream, steps, warmup, pg, rank, local, world):
-    """the Llama-3-70B-shaped Q4_K FFN decode projections, row-sharded over the
-    ranks (apeiron_b200/shard.py): each rank projects its rows of gate, up and down straight
-    into its gather buffer, and one publication kernel per group (gate+up, down) copies them
-    into every other rank's buffer over NVLink peer stores and waits for everyone's.  Strong
-    scaling: the same three matrices at every N."""
+    """configs[4] decode: the Llama-3-70B-shaped Q4_K FFN as a chain, row-sharded over the
+    ranks (apeiron_b200/shard.py).  Each rank holds the same row range of gate and up and a row
+    range of down.  Per step: one step plan (apx_plan_run_async) runs this rank's gate and up
+    rows with SwiGLU + quant_act in their finish, storing each 32-row block of h (int8 codes
+    and an exponent byte) and its slice's descriptor into every rank's buffer by NVLink peer
+    stores; a publication (flags, bounded wait) makes every rank's slice visible and merges the
+    descriptors; down projects this rank's rows from the whole h with its outputs stored into
+    every rank's buffer; a second publication.  Strong scaling: the same FFN at every N."""
+    import ctypes as C
+
     import torch
 
-    from apeiron_b200 import shard, synth
+    from apeiron_b200 import _abi, shard, synth
     from oracle import oracle as O
 
     sp = stream.cuda_stream
@@ -435,111 +440,135 @@ def measure_sharded(be, lib, dev, stream, steps, warmup, pg, rank, local, world)
     copies = max(1, int(np.ceil(3 * L2_BYTES / per_rank)))
     shards = [[shard.RowShard(be, t, raws[m], n_out, n_in, rank, world, dist, f"cuda:{local}")
                for m, (t, n_out, n_in) in enumerate(SHARDED)] for _ in range(copies)]
-    # gate and up read the same activation and gather together; down gathers alone
-    groups = [[0, 1], [2]]
-    acts = []
-    for m, (t, n_out, n_in) in enumerate(SHARDED):
-        if m == 1:  # up: gate's activation
-            acts.append(acts[0])
-            continue
-        x = synth.activation_f32(n_in, 5000 + m)
-        c, e = synth.quant_act_np(synth.f32_to_q32(x))
-        pad = lib.apx_act_padded_len(n_in)
-        codes = torch.zeros(pad, dtype=torch.int8, device=dev)
-        codes[:n_in] = torch.from_numpy(c).to(dev)
-        exps = torch.full((pad // 32,), 0xFF, dtype=torch.uint8, device=dev)
-        exps[:e.size] = torch.from_numpy(e).to(dev)
-        desc = torch.zeros(8, dtype=torch.int32, device=dev)
-        with torch.cuda.stream(stream):
-            assert lib.apx_act_describe_async(be.ctx, codes.data_ptr(), exps.data_ptr(), n_in,
-                                              desc.data_ptr(), sp) == 0
-        acts.append((codes, exps, desc, c, e))
-    gathers = [shard.PeerGather(lib, be.ctx, [shards[0][m] for m in g]) for g in groups]
-    statuses = [torch.full((len(g), 2), -1, dtype=torch.int64, device=dev) for g in groups]
-    merged = [torch.full((len(g), 2), -1, dtype=torch.int64, device=dev) for g in groups]
+    n_ff, n_embd = SHARDED[0][1], SHARDED[0][2]
+    x = synth.activation_f32(n_embd, 5000)
+    cx, ex = synth.quant_act_np(synth.f32_to_q32(x))
+    pad = lib.apx_act_padded_len(n_embd)
+    codes = torch.zeros(pad, dtype=torch.int8, device=dev)
+    codes[:n_embd] = torch.from_numpy(cx).to(dev)
+    exps = torch.full((pad // 32,), 0xFF, dtype=torch.uint8, device=dev)
+    exps[:ex.size] = torch.from_numpy(ex).to(dev)
+    desc = torch.zeros(8, dtype=torch.int32, device=dev)
+    with torch.cuda.stream(stream):
+        assert lib.apx_act_describe_async(be.ctx, codes.data_ptr(), exps.data_ptr(), n_embd,
+                                          desc.data_ptr(), sp) == 0
+    stream.synchronize()
+    hg = shard.HiddenGather(lib, be.ctx, shards[0][0], shards[0][1])
+    yg = shard.PeerGather(lib, be.ctx, [shards[0][2]])
+    st_gu = torch.full((2, 2), -1, dtype=torch.int64, device=dev)
+    merged_gu = torch.full((2, 2), -1, dtype=torch.int64, device=dev)
+    st_y = torch.full((1, 2), -1, dtype=torch.int64, device=dev)
+    merged_y = torch.full((1, 2), -1, dtype=torch.int64, device=dev)
+    ffn_st = torch.full((2,), -1, dtype=torch.int64, device=dev)
+    peers = [q for q in range(world) if q != rank]
+    plans = []  # [copy][parity]
+    for c in range(copies):
+        row = []
+        for par in (0, 1):
+            gsh, ush = shards[c][0], shards[c][1]
+            oc, oe, od = hg.slice_dest(par, rank)
+            acts = (_abi.PlanAct * 2)(
+                _abi.PlanAct(codes.data_ptr(), exps.data_ptr(), desc.data_ptr(), -1, 0),
+                _abi.PlanAct(oc, oe, od, 0, _abi.PLAN_ACT_UNPADDED))
+            projs = (_abi.PlanProj * 2)(
+                _abi.PlanProj(gsh.tensor.handle, gsh.rows, n_embd, 0, 0, _abi.PLAN_GATE, 0,
+                              None, None, st_gu[0].data_ptr()),
+                _abi.PlanProj(ush.tensor.handle, ush.rows, n_embd, 0, 0, _abi.PLAN_UP, 0,
+                              None, None, st_gu[1].data_ptr()))
+            f = _abi.PlanFfn(0, 1, None, ffn_st.data_ptr())
+            f.n_peers = len(peers)
+            for i, q in enumerate(peers):
+                f.d_peer_codes[i], f.d_peer_exps[i], f.d_peer_desc[i] = hg.slice_dest(par, q)
+            err = _abi.ApxErr()
+            pl = lib.apx_plan_create(be.ctx, projs, 2, acts, 2, (_abi.PlanFfn * 1)(f), 1,
+                                     C.byref(err))
+            assert pl, f"apx_plan_create failed: {err.code}"
+            row.append(pl)
+        plans.append(row)
 
     def step(i):
-        parities = []
-        for gi, g in enumerate(groups):
-            parities.append(gathers[gi].run([acts[m][:3] for m in g], statuses[gi], merged[gi],
-                                            sp, shards=[shards[i % copies][m] for m in g]))
-        return parities
+        par = hg.next_parity()
+        assert lib.apx_plan_run_async(plans[i % copies][par], sp) == 0
+        assert hg.publish(st_gu, merged_gu, sp) == par
+        ypar = yg.run([hg.activation(par)], st_y, merged_y, sp, shards=[shards[i % copies][2]])
+        return par, ypar
 
-    # exactness before timing: every rank's gathered Q32.32 vectors against the whole-tensor
-    # oracle, and no refusal
+    # exactness before timing: every rank's whole h and gathered y against the oracle's chain
     with torch.cuda.stream(stream):
-        parities = step(0)
+        par, ypar = step(0)
     stream.synchronize()
-    for gi, g in enumerate(groups):
-        for j, m in enumerate(g):
-            t, n_out, n_in = SHARDED[m]
-            _, _, _, c, e = acts[m]
-            want = O.matvec_q8act_mt(t, raws[m], n_out, n_in, c, O.exps_to_scales(e),
-                                     max(1, (host_threads()) // world))
-            got = gathers[gi].read(j, parities[gi])
-            assert np.array_equal(got, want), "sharded parity failure in bench workload"
-        assert bool((merged[gi][:, 0] == -1).all().item()), "sharded refusal in bench workload"
+    thr = max(1, host_threads() // world)
+    sc = O.exps_to_scales(ex)
+    g = O.matvec_q8act_mt(12, raws[0], n_ff, n_embd, cx, sc, thr, simd=True)
+    u = O.matvec_q8act_mt(12, raws[1], n_ff, n_embd, cx, sc, thr, simd=True)
+    _, hcodes, hscales = O.swiglu_quant(g, u, 0)
+    hc, he, hd = hg.read(par)
+    assert np.array_equal(hc, hcodes), "sharded h codes parity failure"
+    assert np.array_equal(he, O.scales_to_exps(hscales)), "sharded h exponents parity failure"
+    want = O.matvec_q8act_mt(12, raws[2], n_embd, n_ff, hcodes, hscales, thr, simd=True)
+    assert np.array_equal(yg.read(0, ypar), want), "sharded FFN chain parity failure"
+    for w in (merged_gu, merged_y):
+        assert bool((w[:, 0] == -1).all().item()), "sharded refusal in bench workload"
+    assert int(ffn_st[0].item()) == -1
     del raws
     barrier(pg, local)
 
     with torch.cuda.stream(stream):
-        for i in range(max(warmup, 3)):
-            step(i)
+        for i in range(max(warmup, 3) + 1):  # an even number of calls: parities in step
+            step(1 + i)
     stream.synchronize()
-    G = min(steps, 100)
-    graph = None
-    try:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            for i in range(G):
-                step(i)
-    except Exception:  # collectives this build cannot capture: time the eager launches
-        graph = None
-        torch.cuda.synchronize()
+    G = min(steps, 100) // 2 * 2 or 2
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(G):
+            step(i)
     barrier(pg, local)
     reps = max(1, steps // G)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
-        if graph is not None:
-            graph.replay()
+        graph.replay()
         t0.record(stream)
-        for r in range(reps):
-            if graph is not None:
-                graph.replay()
-            else:
-                for i in range(G):
-                    step(i)
+        for _ in range(reps):
+            graph.replay()
         t1.record(stream)
     stream.synchronize()
     barrier(pg, local)
     ms = max_over_ranks(t0.elapsed_time(t1), pg, local) / (reps * G)
-    for gi in range(len(groups)):
-        assert bool((merged[gi][:, 0] == -1).all().item()), "sharded refusal while timed"
-    timing = "CUDA graph" if graph is not None else "eager launches"
+    for w in (merged_gu, merged_y):
+        assert bool((w[:, 0] == -1).all().item()), "sharded refusal while timed"
     del graph
     torch.cuda.synchronize()
-    barrier(pg, local)  # no rank writes into another's gather buffer any more
-    for gth in gathers:
-        gth.close()
+    barrier(pg, local)  # no rank writes into another's buffers any more
+    for row in plans:
+        for pl in row:
+            lib.apx_plan_destroy(pl)
+    hg.close()
+    yg.close()
     per_step = sum(gemv_bytes(*mat) for mat in SHARDED)
     gbs = per_step / (ms / 1e3) / 1e9
     hbm, _ = peaks()
     return {
-        "metric": "70B FFN decode GB/s (row-sharded, NVLink peer-store gather)", "value": gbs,
-        "unit": "GB/s", "n_gpus": world, "ms_per_step": ms, "steps": reps * G,
+        "metric": "70B FFN decode GB/s (row-sharded FFN chain, NVLink peer-store exchange)",
+        "value": gbs, "unit": "GB/s", "n_gpus": world, "ms_per_step": ms, "steps": reps * G,
         "scaling": "strong",
-        "config": {"workload": "Llama-3-70B-shaped Q4_K FFN decode: W_gate/W_up 28672x8192, "
-                               "W_down 8192x28672, configs[4]; step = the three projections, "
-                               "each rank its rows; the int64 output slices and refusal keys "
-                               "of gate+up (shared activation), then of down, published to every "
-                               "rank by peer stores (one kernel per group, bounded flag wait)",
-                   "rows_per_rank": [b - a for a, b in shards[0][0].splits],
+        "config": {"workload": "Llama-3-70B-shaped Q4_K FFN decode, configs[4]: W_gate/W_up "
+                               "28672x8192, W_down 8192x28672; step = gate and up of this "
+                               "rank's rows with SwiGLU + quant_act in one step plan, h's int8 "
+                               "codes and exponent bytes (and each slice's descriptor) stored "
+                               "into every rank's buffer, a publication, down of this rank's "
+                               "rows from the whole h with its outputs stored into every rank's "
+                               "buffer, a second publication: 4 launches",
+                   "rows_per_rank": {"gate_up": shards[0][0].rows, "down": shards[0][2].rows},
+                   "nvlink_bytes_per_rank": (shards[0][0].rows + shards[0][0].rows // 32 + 32)
+                                            * (world - 1) + 8 * shards[0][2].rows * (world - 1),
                    "weight_copies": copies,
                    "l2": "rotating weight copies, >= 3x the 126 MB L2 per rank",
-                   "timing": timing,
-                   "exact": "gathered Q32.32 outputs bit-equal to the whole-tensor CPU oracle "
-                            "(checked before timing)"},
+                   "timing": "CUDA graph",
+                   "exact": "every rank's whole h and gathered y bit-equal to the CPU oracle's "
+                            "chain (matvec_q8act, swiglu_quant, matvec_q8act), checked before "
+                            "timing"},
         "hbm_frac_per_gpu": gbs / world / hbm,
+        "gpu_launches_per_step": 4,
     }
 
 
@@ -1121,7 +1150,7 @@ def run_reference(args, world, rank, local, pg):
     for key, skip, metric, mats_, seed in (
             ("decode_step", args.no_decode, "decode step GB/s (all linear layers)",
              DECODE_LAYER * DECODE_LAYERS + [DECODE_HEAD], 6000),
-            ("sharded", args.no_shard, "70B FFN decode GB/s (one host)", SHARDED, 4000)):
+            ("sharded", args.no_shard, "70B FFN decode GB/s (row-sharded FFN chain)", SHARDED, 4000)):
         if skip:
             continue
         try:
@@ -1377,7 +1406,7 @@ def run_ours(args, world, rank, local, pg):
         line["gpu_launches"] += decode["gpu_launches_per_step"] * decode["steps"]
     if sharded is not None:
         line["sharded"] = sharded
-        line["gpu_launches"] += len(SHARDED) * sharded["steps"]
+        line["gpu_launches"] += sharded["gpu_launches_per_step"] * sharded["steps"]
     print(json.dumps(line), flush=True)
 
 

@@ -312,13 +312,16 @@ APX_API int apx_status_decode_rows(apx_ctx *ctx, uint64_t tensor, size_t n_out,
 typedef struct apx_plan apx_plan;
 #define APX_PLAN_GATE 0
 #define APX_PLAN_UP 1
+#define APX_PLAN_MAX_PEERS 7
+#define APX_PLAN_ACT_UNPADDED 1 /* apx_plan_act.flags: an FFN's slice inside a larger buffer */
 typedef struct apx_plan_act {
   int8_t *d_codes;      /* apx_act_padded_len(n) code bytes */
   uint8_t *d_exps;      /* apx_act_padded_len(n) / 32 exponent bytes */
   apx_act_desc *d_desc; /* its descriptor */
   int32_t ffn;          /* -1: written before the run; else the FFN that writes it (the plan
-                         * then sets the pad bytes past n once, at creation) */
-  int32_t reserved;
+                         * then sets the pad bytes past n once, at creation, unless flags
+                         * holds APX_PLAN_ACT_UNPADDED) */
+  int32_t flags;
 } apx_plan_act;
 typedef struct apx_plan_proj {
   uint64_t tensor;
@@ -336,6 +339,16 @@ typedef struct apx_plan_ffn {
   int32_t out_act;           /* the activation record it writes */
   int64_t *d_h;              /* optional: h in Q32.32 */
   apx_call_status *d_status; /* the first refusing SwiGLU lane (apx_ffn_status_decode) */
+  /* Row shards: copies of every quantized block of h and of the descriptor also go to
+   * n_peers other places (other GPUs' buffers, mapped with apx_peer_open): codes at
+   * d_peer_codes[i][row], exponent bytes at d_peer_exps[i][row / 32], the descriptor of this
+   * slice to d_peer_desc[i].  A publication (apx_gather_publish_async with desc_off) makes
+   * them visible and merges the slices' descriptors. */
+  int32_t n_peers;
+  int32_t reserved;
+  int8_t *d_peer_codes[APX_PLAN_MAX_PEERS];
+  uint8_t *d_peer_exps[APX_PLAN_MAX_PEERS];
+  apx_act_desc *d_peer_desc[APX_PLAN_MAX_PEERS];
 } apx_plan_ffn;
 /* NULL with err set on failure: APX_ERR_LAYOUT_MISMATCH (a tensor or width), APX_ERR_
  * INVALID_ARGUMENT (records: families differ, an FFN without one gate and one up of equal
@@ -408,6 +421,9 @@ APX_API int apx_peer_close(apx_ctx *ctx, void *d_ptr, int opened);
 /* Synchronous copy of `bytes` from device memory on ctx's GPU to host memory. */
 APX_API int apx_device_read(apx_ctx *ctx, const void *d_src, void *host_dst, size_t bytes,
                             apx_err *err);
+/* Synchronous copy of `bytes` from host memory to device memory on ctx's GPU. */
+APX_API int apx_device_write(apx_ctx *ctx, void *d_dst, const void *host_src, size_t bytes,
+                             apx_err *err);
 
 /* One publication: rank `rank` of `world` makes its rows of `nproj` projections visible in
  * every rank's gather buffer and collects every rank's refusal.  Offsets are bytes from each
@@ -434,6 +450,12 @@ typedef struct apx_gather_desc {
   size_t bytes;                          /* size of every rank's gather buffer: the rows, keys,
                                             flags and counters of the offsets above must lie
                                             inside it (else APX_ERR_INVALID_ARGUMENT)        */
+  size_t desc_off;                       /* 0, or this parity's [world] apx_act_desc: each
+                                            rank's descriptor of its slice of a sharded
+                                            activation (stored by an apx_plan_ffn's peer
+                                            destinations); after the wait the publication
+                                            merges them into one descriptor at merged_off   */
+  size_t merged_off;                     /* (16-byte aligned, as desc_off)                  */
 } apx_gather_desc;
 
 /* Projection j of the publication on `stream`: this rank's gd->rows[j] rows (the tensor holds

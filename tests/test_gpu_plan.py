@@ -224,6 +224,8 @@ def _separate_chain(be, k, n_embd, n_ff, carrier):
     (Q4_K, 896, 4864, 1, 1),
     (Q8_0, 1024, 2816, 3, 0),
     (Q4_K, 2048, 5632, 1, 0),
+    (Q4_K, 8192, 1024, 1, 0),   # gate/up in 8-row tiles (L = 4): four per block of h
+    (Q8_0, 4096, 1000, 1, 1),   # L = 4 and a ragged last block of h (one 8-row tile)
 ])
 def test_plan_ffn_chain_equals_separate_calls(be, t, n_embd, n_ff, layers, carrier):
     lib, ctx = be.lib, be.ctx
