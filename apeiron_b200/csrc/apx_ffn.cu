@@ -30,6 +30,15 @@ constexpr int kFfnWarps = 8;
 
 // ---- kernels -------------------------------------------------------------------------------
 
+// Row shards: copies of a one-column call's codes, exponent bytes and descriptor at n other places
+// (other GPUs' buffers), element 0 of the call at codes[i][0] / exps[i][0].
+struct ShardDests {
+  int n;
+  int8_t *codes[7];
+  uint8_t *exps[7];
+  ActDesc *desc[7];
+};
+
 // Column c (blockIdx.y) of a multi-column call: gate, up and h at c·ldg, codes at c·ldc, exponent
 // bytes at c·lde, the status word at status[2c], CTA statistics at part[c·gridDim.x + x].
 struct FfnArgs {
@@ -41,6 +50,7 @@ struct FfnArgs {
   int carrier;
   int4 *part;                  // per CTA: emin, emax, status, nz
   unsigned long long *status;  // the first refusing lane
+  ShardDests dst;              // one-column calls: where else the codes and exponents go
 };
 
 __global__ void __launch_bounds__(32 * kFfnWarps) swiglu_quant_kernel(FfnArgs a) {
@@ -99,9 +109,15 @@ __global__ void __launch_bounds__(32 * kFfnWarps) swiglu_quant_kernel(FfnArgs a)
       if (__any_sync(0xFFFFFFFFu, mag > 127 || !product_fits(code, e)))
         w_status = APX_ERR_QUANT_REFUSED;
     }
+    const uint8_t eb = e < 0 || e == 99 ? (uint8_t)APX_EXP_ZERO : (uint8_t)e;
     if (j < a.n) a.codes[j] = (int8_t)code;
+#pragma unroll 1
+    for (int i = 0; i < a.dst.n; i++) {
+      if (j < a.n) a.dst.codes[i][j] = (int8_t)code;
+      if (lane == 0) a.dst.exps[i][b] = eb;
+    }
     if (lane == 0) {
-      a.exps[b] = e < 0 || e == 99 ? (uint8_t)APX_EXP_ZERO : (uint8_t)e;
+      a.exps[b] = eb;
       if (w_status != APX_OK) atomicMax(&s_status, w_status);
       if (e >= 0 && e != 99) {
         atomicMin(&s_emin, e);
@@ -117,7 +133,7 @@ __global__ void __launch_bounds__(32 * kFfnWarps) swiglu_quant_kernel(FfnArgs a)
 
 // The descriptor from the CTAs' statistics (one CTA per column).
 __global__ void __launch_bounds__(256) ffn_desc_kernel(const int4 *part, int nparts, size_t n,
-                                                       ActDesc *desc) {
+                                                       ActDesc *desc, ShardDests dst) {
   part += (size_t)blockIdx.x * nparts;
   desc += blockIdx.x;
   int emin = 1 << 30, emax = -1, status = APX_OK;
@@ -157,6 +173,7 @@ __global__ void __launch_bounds__(256) ffn_desc_kernel(const int4 *part, int npa
     r.pad[1] = 0;
     r.pad[2] = 0;
     *desc = r;
+    for (int i = 0; i < dst.n; i++) *dst.desc[i] = r;
   }
 }
 
@@ -166,16 +183,17 @@ size_t swiglu_work_bytes(size_t n, size_t cols) {
 
 cudaError_t launch_swiglu_quant(const long long *gate, const long long *up, size_t n, int carrier,
                                 long long *h, int8_t *codes, uint8_t *exps, void *desc,
-                                unsigned long long *status, void *work, cudaStream_t stream) {
+                                unsigned long long *status, void *work, cudaStream_t stream,
+                                const SwigluDests *dests) {
   return launch_swiglu_quant_cols(gate, up, n, 1, 0, carrier, h, codes, 0, exps, 0, desc, status,
-                                  work, stream);
+                                  work, stream, dests);
 }
 
 cudaError_t launch_swiglu_quant_cols(const long long *gate, const long long *up, size_t n,
                                      size_t cols, size_t ldg, int carrier, long long *h,
                                      int8_t *codes, size_t ldc, uint8_t *exps, size_t lde,
                                      void *desc, unsigned long long *status, void *work,
-                                     cudaStream_t stream) {
+                                     cudaStream_t stream, const SwigluDests *dests) {
   if (n == 0 || cols == 0) return cudaSuccess;
   const size_t nb = (n + 31) / 32;
   const unsigned grid = (unsigned)((nb + kFfnWarps - 1) / kFfnWarps);
@@ -192,11 +210,21 @@ cudaError_t launch_swiglu_quant_cols(const long long *gate, const long long *up,
   a.carrier = carrier;
   a.part = static_cast<int4 *>(work);
   a.status = status;
+  a.dst = ShardDests{};
+  if (dests) {
+    if (cols != 1 || dests->n < 0 || dests->n > 7) return cudaErrorInvalidValue;
+    a.dst.n = dests->n;
+    for (int i = 0; i < dests->n; i++) {
+      a.dst.codes[i] = dests->codes[i];
+      a.dst.exps[i] = dests->exps[i];
+      a.dst.desc[i] = static_cast<ActDesc *>(dests->desc[i]);
+    }
+  }
   swiglu_quant_kernel<<<dim3(grid, (unsigned)cols), 32 * kFfnWarps, 0, stream>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   ffn_desc_kernel<<<(unsigned)cols, 256, 0, stream>>>(a.part, (int)grid, n,
-                                                        static_cast<ActDesc *>(desc));
+                                                        static_cast<ActDesc *>(desc), a.dst);
   return cudaGetLastError();
 }
 

@@ -157,16 +157,24 @@ cudaError_t launch_limb_gemm_f32(const GemvPlan &pl, uint32_t type, const uint8_
 // The FFN hidden activation (apx_ffn.cu): SwiGLU under the carrier, then quant_act; `work` holds
 // swiglu_work_bytes(n).
 size_t swiglu_work_bytes(size_t n, size_t cols = 1);
+// Row shards: where else a one-column call's codes, exponent bytes and descriptor go.
+struct SwigluDests {
+  int n;
+  int8_t *codes[7];
+  uint8_t *exps[7];
+  void *desc[7];  // ActDesc
+};
 cudaError_t launch_swiglu_quant(const long long *gate, const long long *up, size_t n, int carrier,
                                 long long *h, int8_t *codes, uint8_t *exps, void *desc,
-                                unsigned long long *status, void *work, cudaStream_t stream);
+                                unsigned long long *status, void *work, cudaStream_t stream,
+                                const SwigluDests *dests = nullptr);
 // `cols` columns in one launch: gate/up/h of column c at c·ldg, codes at c·ldc, exponent bytes at
 // c·lde, descriptor desc[c], status word at status[2c]; `work` holds swiglu_work_bytes(n, cols).
 cudaError_t launch_swiglu_quant_cols(const long long *gate, const long long *up, size_t n,
                                      size_t cols, size_t ldg, int carrier, long long *h,
                                      int8_t *codes, size_t ldc, uint8_t *exps, size_t lde,
                                      void *desc, unsigned long long *status, void *work,
-                                     cudaStream_t stream);
+                                     cudaStream_t stream, const SwigluDests *dests = nullptr);
 
 // Step plans (apx_plan.cu): the projections of a decode step, and the FFNs among them whose
 // finish runs SwiGLU + quant_act, in one persistent launch.  All projections of one plan share a

@@ -1154,6 +1154,34 @@ int apx_swiglu_quant_async(apx_ctx *ctx, const int64_t *d_gate, const int64_t *d
   return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
 }
 
+int apx_swiglu_quant_shard_async(apx_ctx *ctx, const int64_t *d_gate, const int64_t *d_up,
+                                 size_t n, int carrier, int64_t *d_h, int8_t *d_codes,
+                                 uint8_t *d_exps, apx_act_desc *d_desc, int n_peers,
+                                 int8_t *const *d_peer_codes, uint8_t *const *d_peer_exps,
+                                 apx_act_desc *const *d_peer_desc, apx_call_status *d_status,
+                                 void *stream) {
+  if (!ctx || !d_desc || !d_status || n == 0 || !d_gate || !d_up || !d_codes || !d_exps ||
+      (carrier != APX_CARRIER_F32 && carrier != APX_CARRIER_Q32) || n_peers < 0 ||
+      n_peers > APX_PLAN_MAX_PEERS || (n_peers && (!d_peer_codes || !d_peer_exps || !d_peer_desc)))
+    return APX_ERR_INVALID_ARGUMENT;
+  if (n > (size_t)INT32_MAX) return APX_ERR_TOO_LARGE;
+  SwigluDests dests{};
+  dests.n = n_peers;
+  for (int i = 0; i < n_peers; i++) {
+    if (!d_peer_codes[i] || !d_peer_exps[i] || !d_peer_desc[i]) return APX_ERR_INVALID_ARGUMENT;
+    dests.codes[i] = d_peer_codes[i];
+    dests.exps[i] = d_peer_exps[i];
+    dests.desc[i] = d_peer_desc[i];
+  }
+  std::lock_guard<std::mutex> g(ctx->mu);
+  if (ctx->fwork.ensure(swiglu_work_bytes(n)) != cudaSuccess) return APX_ERR_OUT_OF_MEMORY;
+  const cudaError_t e = launch_swiglu_quant(
+      (const long long *)d_gate, (const long long *)d_up, n, carrier, (long long *)d_h, d_codes,
+      d_exps, d_desc, (unsigned long long *)&d_status->first, ctx->fwork.p, (cudaStream_t)stream,
+      &dests);
+  return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
+}
+
 int apx_swiglu_quant_cols_async(apx_ctx *ctx, const int64_t *d_gate, const int64_t *d_up,
                                 size_t n, size_t k_cols, int carrier, int64_t *d_h,
                                 int8_t *d_codes, uint8_t *d_exps, apx_act_desc *d_descs,

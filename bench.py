@@ -461,36 +461,34 @@ def measure_sharded(be, lib, dev, stream, steps, warmup, pg, rank, local, world)
     merged_y = torch.full((1, 2), -1, dtype=torch.int64, device=dev)
     ffn_st = torch.full((2,), -1, dtype=torch.int64, device=dev)
     peers = [q for q in range(world) if q != rank]
-    plans = []  # [copy][parity]
-    for c in range(copies):
-        row = []
-        for par in (0, 1):
-            gsh, ush = shards[c][0], shards[c][1]
-            oc, oe, od = hg.slice_dest(par, rank)
-            acts = (_abi.PlanAct * 2)(
-                _abi.PlanAct(codes.data_ptr(), exps.data_ptr(), desc.data_ptr(), -1, 0),
-                _abi.PlanAct(oc, oe, od, 0, _abi.PLAN_ACT_UNPADDED))
-            projs = (_abi.PlanProj * 2)(
-                _abi.PlanProj(gsh.tensor.handle, gsh.rows, n_embd, 0, 0, _abi.PLAN_GATE, 0,
-                              None, None, st_gu[0].data_ptr()),
-                _abi.PlanProj(ush.tensor.handle, ush.rows, n_embd, 0, 0, _abi.PLAN_UP, 0,
-                              None, None, st_gu[1].data_ptr()))
-            f = _abi.PlanFfn(0, 1, None, ffn_st.data_ptr())
-            f.n_peers = len(peers)
-            for i, q in enumerate(peers):
-                f.d_peer_codes[i], f.d_peer_exps[i], f.d_peer_desc[i] = hg.slice_dest(par, q)
-            err = _abi.ApxErr()
-            pl = lib.apx_plan_create(be.ctx, projs, 2, acts, 2, (_abi.PlanFfn * 1)(f), 1,
-                                     C.byref(err))
-            assert pl, f"apx_plan_create failed: {err.code}"
-            row.append(pl)
-        plans.append(row)
+    gq = torch.zeros(shards[0][0].rows, dtype=torch.int64, device=dev)
+    uq = torch.zeros(shards[0][1].rows, dtype=torch.int64, device=dev)
+    gu_handles = [(C.c_uint64 * 2)(row[0].tensor.handle, row[1].tensor.handle) for row in shards]
+    gu_outs = (C.c_void_p * 2)(gq.data_ptr(), uq.data_ptr())
+    gu_st = (C.c_void_p * 2)(st_gu[0].data_ptr(), st_gu[1].data_ptr())
+    dests = []  # per parity: this rank's slice in its own buffer and in every peer's
+    for par in (0, 1):
+        own = hg.slice_dest(par, rank)
+        ps = [hg.slice_dest(par, q) for q in peers]
+        n = max(len(ps), 1)
+        dests.append((own, len(ps), (C.c_void_p * n)(*[p[0] for p in ps]),
+                      (C.c_void_p * n)(*[p[1] for p in ps]),
+                      (C.c_void_p * n)(*[p[2] for p in ps])))
 
     def step(i):
+        row = shards[i % copies]
         par = hg.next_parity()
-        assert lib.apx_plan_run_async(plans[i % copies][par], sp) == 0
+        # gate and up of this rank's rows (Q32.32: the SwiGLU's inputs), one launch when their
+        # layouts allow
+        assert lib.apx_matvec_group_async(be.ctx, gu_handles[i % copies], 2, n_embd,
+                                          codes.data_ptr(), exps.data_ptr(), desc.data_ptr(),
+                                          gu_outs, None, gu_st, sp) == 0
+        (oc, oe, od), npeer, pc, pe, pd = dests[par]
+        assert lib.apx_swiglu_quant_shard_async(be.ctx, gq.data_ptr(), uq.data_ptr(), row[0].rows,
+                                                0, None, oc, oe, od, npeer, pc, pe, pd,
+                                                ffn_st.data_ptr(), sp) == 0
         assert hg.publish(st_gu, merged_gu, sp) == par
-        ypar = yg.run([hg.activation(par)], st_y, merged_y, sp, shards=[shards[i % copies][2]])
+        ypar = yg.run([hg.activation(par)], st_y, merged_y, sp, shards=[row[2]])
         return par, ypar
 
     # exactness before timing: every rank's whole h and gathered y against the oracle's chain
@@ -539,9 +537,6 @@ def measure_sharded(be, lib, dev, stream, steps, warmup, pg, rank, local, world)
     del graph
     torch.cuda.synchronize()
     barrier(pg, local)  # no rank writes into another's buffers any more
-    for row in plans:
-        for pl in row:
-            lib.apx_plan_destroy(pl)
     hg.close()
     yg.close()
     per_step = sum(gemv_bytes(*mat) for mat in SHARDED)
@@ -553,11 +548,11 @@ def measure_sharded(be, lib, dev, stream, steps, warmup, pg, rank, local, world)
         "scaling": "strong",
         "config": {"workload": "Llama-3-70B-shaped Q4_K FFN decode, configs[4]: W_gate/W_up "
                                "28672x8192, W_down 8192x28672; step = gate and up of this "
-                               "rank's rows with SwiGLU + quant_act in one step plan, h's int8 "
-                               "codes and exponent bytes (and each slice's descriptor) stored "
-                               "into every rank's buffer, a publication, down of this rank's "
-                               "rows from the whole h with its outputs stored into every rank's "
-                               "buffer, a second publication: 4 launches",
+                               "rank's rows (GEMV, one launch when their layouts allow), SwiGLU "
+                               "+ quant_act of the slice storing h's int8 codes and exponent "
+                               "bytes (and the slice's descriptor) into every rank's buffer, a "
+                               "publication, down of this rank's rows from the whole h with its "
+                               "outputs stored into every rank's buffer, a second publication",
                    "rows_per_rank": {"gate_up": shards[0][0].rows, "down": shards[0][2].rows},
                    "nvlink_bytes_per_rank": (shards[0][0].rows + shards[0][0].rows // 32 + 32)
                                             * (world - 1) + 8 * shards[0][2].rows * (world - 1),
@@ -568,7 +563,10 @@ def measure_sharded(be, lib, dev, stream, steps, warmup, pg, rank, local, world)
                             "chain (matvec_q8act, swiglu_quant, matvec_q8act), checked before "
                             "timing"},
         "hbm_frac_per_gpu": gbs / world / hbm,
-        "gpu_launches_per_step": 4,
+        # gate and up share one launch when both plan as one resident wave (the GEMV planner:
+        # row tiles x K-slots within two waves of 148 SMs x 48 units), as at N = 8
+        "gpu_launches_per_step": 6 if shards[0][0].rows // 32 * (n_embd // 256) <= 148 * 48
+                                 else 7,
     }
 
 

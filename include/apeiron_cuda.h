@@ -292,6 +292,20 @@ APX_API int apx_status_decode(apx_ctx *ctx, uint64_t tensor, const apx_call_stat
 APX_API int apx_status_decode_rows(apx_ctx *ctx, uint64_t tensor, size_t n_out,
                                    const apx_call_status *status, apx_err *err);
 
+/* apx_swiglu_quant_async for one slice of a row-sharded FFN's h: the codes, exponent bytes and
+ * descriptor also go to n_peers other places (other GPUs' buffers, mapped with apx_peer_open),
+ * element 0 of the slice at d_peer_codes[i][0] / d_peer_exps[i][0]; a publication
+ * (apx_gather_publish_async with desc_off) makes them visible and merges the slices'
+ * descriptors.  n_peers <= APX_PLAN_MAX_PEERS. */
+APX_API int apx_swiglu_quant_shard_async(apx_ctx *ctx, const int64_t *d_gate,
+                                         const int64_t *d_up, size_t n, int carrier,
+                                         int64_t *d_h, int8_t *d_codes, uint8_t *d_exps,
+                                         apx_act_desc *d_desc, int n_peers,
+                                         int8_t *const *d_peer_codes,
+                                         uint8_t *const *d_peer_exps,
+                                         apx_act_desc *const *d_peer_desc,
+                                         apx_call_status *d_status, void *stream);
+
 /* ---- step plans: the projections of a decode step in one launch -------------------- */
 /* A plan lists projections in dependency order, each reading one activation record, and
  * optionally FFNs: the gate and up projections of one activation (role APX_PLAN_GATE /

@@ -266,3 +266,84 @@ def test_prefill_ffn_chain_on_device(be):
         _, hcodes, hscales = O.swiglu_quant(g, u, carrier)
         want = O.matvec_q8act(t, raws[2], n_embd, n_ff, hcodes, hscales)
         assert np.array_equal(y_all[c], want), c
+
+
+@pytest.mark.parametrize("n,peers", [(4864, 3), (1000, 7), (64, 1)])
+def test_swiglu_shard_copies_equal_single_call(be, n, peers):
+    """apx_swiglu_quant_shard_async: the slice's codes, exponent bytes and descriptor, and every
+    copy of them, equal apx_swiglu_quant_async's (device buffers on this GPU stand in for the
+    other ranks'); a bad peer count is refused."""
+    import torch
+
+    lib = be.lib
+    dev = torch.device("cuda:0")
+    gate, up = hidden(n, 77 + n)
+    h0, c0, e0, d0, s0 = run(be, gate, up, _abi.CARRIER_F32)
+    dg = torch.from_numpy(gate).to(dev)
+    du = torch.from_numpy(up).to(dev)
+    pad = max(lib.apx_act_padded_len(n), 32)
+    bufs = [(torch.zeros(pad, dtype=torch.int8, device=dev),
+             torch.full((pad // 32,), 0xEE, dtype=torch.uint8, device=dev),
+             torch.zeros(8, dtype=torch.int32, device=dev)) for _ in range(peers + 1)]
+    own, rest = bufs[0], bufs[1:]
+    pc = (C.c_void_p * peers)(*[b[0].data_ptr() for b in rest])
+    pe = (C.c_void_p * peers)(*[b[1].data_ptr() for b in rest])
+    pd = (C.c_void_p * peers)(*[b[2].data_ptr() for b in rest])
+    status = torch.full((2,), -1, dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.apx_swiglu_quant_shard_async(be.ctx, dg.data_ptr(), du.data_ptr(), n, 0, None,
+                                            own[0].data_ptr(), own[1].data_ptr(),
+                                            own[2].data_ptr(), peers, pc, pe, pd,
+                                            status.data_ptr(), stream) == 0
+    torch.cuda.synchronize()
+    nb = (n + 31) // 32
+    for b in bufs:
+        assert np.array_equal(b[0].cpu().numpy()[:n], c0[:n])
+        assert np.array_equal(b[1].cpu().numpy()[:nb], e0[:nb])
+        assert np.array_equal(b[2].cpu().numpy(), d0)
+    assert lib.apx_swiglu_quant_shard_async(be.ctx, dg.data_ptr(), du.data_ptr(), n, 0, None,
+                                            own[0].data_ptr(), own[1].data_ptr(),
+                                            own[2].data_ptr(), 8, pc, pe, pd,
+                                            status.data_ptr(), stream) == \
+        _abi.APX_ERR_INVALID_ARGUMENT
+
+
+def test_hidden_gather_one_rank_merges_descriptor(be):
+    """shard.HiddenGather at world 1: the slice stored by apx_swiglu_quant_shard_async into the
+    gather buffer, one publication (flags, keys, the descriptor merge), and the whole h read
+    back equal to apx_swiglu_quant_async's, parity after parity."""
+    import torch
+
+    from apeiron_b200 import shard
+
+    lib = be.lib
+    dev = torch.device("cuda:0")
+    n, n_in = 4096, 512
+    raw = synth.payload(12, n, n_in, 5)
+    gsh = shard.RowShard(be, 12, raw, n, n_in, 0, 1, None, "cuda:0")
+    ush = shard.RowShard(be, 12, raw, n, n_in, 0, 1, None, "cuda:0")
+    hg = shard.HiddenGather(lib, be.ctx, gsh, ush)
+    st = torch.full((2, 2), -1, dtype=torch.int64, device=dev)
+    merged = torch.full((2, 2), -1, dtype=torch.int64, device=dev)
+    fst = torch.full((2,), -1, dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+    try:
+        for step in range(4):
+            gate, up = hidden(n, 300 + step)
+            _, c0, e0, d0, _ = run(be, gate, up, _abi.CARRIER_F32)
+            dg = torch.from_numpy(gate).to(dev)
+            du = torch.from_numpy(up).to(dev)
+            par = hg.next_parity()
+            oc, oe, od = hg.slice_dest(par, 0)
+            assert lib.apx_swiglu_quant_shard_async(be.ctx, dg.data_ptr(), du.data_ptr(), n, 0,
+                                                    None, oc, oe, od, 0, None, None, None,
+                                                    fst.data_ptr(), stream) == 0
+            assert hg.publish(st, merged, stream) == par
+            torch.cuda.synchronize()
+            codes, exps, desc = hg.read(par)
+            assert np.array_equal(codes, c0[:n]) and np.array_equal(exps, e0[:n // 32])
+            assert np.array_equal(desc, d0), (desc, d0)
+            assert bool((merged[:, 0] == -1).all().item())
+    finally:
+        torch.cuda.synchronize()
+        hg.close()
