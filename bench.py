@@ -1408,6 +1408,61 @@ def run_ours(args, world, rank, local, pg):
     print(json.dumps(line), flush=True)
 
 
+def gemm_probe(args):
+    """One k-column shape through the f32 prefill entry (apx_matmat_f32_async), its first token
+    checked against the oracle, then `--steps` calls back to back (rotating two weight copies,
+    CUDA events); prints one JSON line.  A small single-GPU case for ncu captures of the
+    tensor-core GEMM."""
+    import torch
+
+    from apeiron_b200 import synth
+    from apeiron_b200.chart import Backend
+    from oracle import oracle as O
+
+    t, n_out, n_in, k = (int(v) for v in args.gemm_probe.split(","))
+    dev = torch.device("cuda:0")
+    be = Backend(0)
+    lib = be.lib
+    stream = torch.cuda.Stream(device=dev)
+    sp = stream.cuda_stream
+    raws = [synth.payload(t, n_out, n_in, 600 + c) for c in range(2)]
+    tens = [be.upload(t, r, n_out, n_in) for r in raws]
+    x = np.stack([synth.activation_f32(n_in, 700 + c) for c in range(k)])
+    dx = torch.from_numpy(x).to(dev)
+    yq = torch.zeros(k * n_out, dtype=torch.int64, device=dev)
+    y = torch.zeros(k * n_out, dtype=torch.float32, device=dev)
+    st = torch.full((2 * k,), -1, dtype=torch.int64, device=dev)
+
+    def call(i, q=False):
+        assert lib.apx_matmat_f32_async(be.ctx, tens[i % 2].handle, n_out, n_in, k, dx.data_ptr(),
+                                        n_in, yq.data_ptr() if q else None, y.data_ptr(),
+                                        st.data_ptr(), sp) == 0
+
+    with torch.cuda.stream(stream):
+        call(0, q=True)
+    stream.synchronize()
+    c, e = O.quant_act(synth.f32_to_q32(x[0]))
+    want = O.matvec_q8act_mt(t, raws[0], n_out, n_in, c, e, host_threads(), simd=True)
+    assert np.array_equal(yq.cpu().numpy()[:n_out], want), "gemm probe parity failure"
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            call(i)
+    stream.synchronize()
+    steps = min(args.steps, 200)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for i in range(steps):
+            call(i)
+        t1.record(stream)
+    stream.synchronize()
+    assert bool((st[0::2] == -1).all().item())
+    us = t0.elapsed_time(t1) / steps * 1e3
+    print(json.dumps({"probe": "gemm", "type": t, "n_out": n_out, "n_in": n_in, "tokens": k,
+                      "us_per_call": us, "tops": 2.0 * k * n_out * n_in / us / 1e6}), flush=True)
+    be.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1426,8 +1481,14 @@ def main():
     ap.add_argument("--decode-steps", type=int, default=200)
     ap.add_argument("--shard-steps", type=int, default=400)
     ap.add_argument("--prefill-steps", type=int, default=400)
+    ap.add_argument("--gemm-probe", default=None,
+                    help="TYPE,N_OUT,N_IN,TOKENS: time one prefill shape alone and exit (a small "
+                         "case for profilers)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.gemm_probe:
+        gemm_probe(args)
+        return
     world, rank, local, pg = dist_setup(args.gpus)
     try:
         if args.impl == "reference":
