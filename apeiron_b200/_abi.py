@@ -44,7 +44,7 @@ EXPORTS = [
     "apx_matvec_f32_noalloc", "apx_matmat_f32", "apx_quant_f32_cols_async",
     "apx_peer_alloc", "apx_peer_open", "apx_peer_close", "apx_device_read", "apx_device_write",
     "apx_gather_publish_async", "apx_matvec_gather_async", "apx_matvec_group_async",
-    "apx_swiglu_quant_async", "apx_swiglu_quant_cols_async", "apx_swiglu_quant_shard_async", "apx_act_describe_cols_async",
+    "apx_swiglu_quant_async", "apx_swiglu_quant_cols_async", "apx_swiglu_quant_shard_async", "apx_matmat_f32_group_async", "apx_act_describe_cols_async",
     "apx_ffn_status_decode", "apx_ctx_set_gemm_route", "apx_plan_create", "apx_plan_run_async", "apx_plan_destroy",
 ]
 PLAN_GATE, PLAN_UP = 0, 1
@@ -162,6 +162,7 @@ _SIGS = {
     "apx_swiglu_quant_cols_async": (C.c_int, [P, P, P, SZ, SZ, C.c_int, P, P, P, P, P, P]),
     "apx_swiglu_quant_shard_async": (C.c_int, [P, P, P, SZ, C.c_int, P, P, P, P, C.c_int, P, P,
                                                P, P, P]),
+    "apx_matmat_f32_group_async": (C.c_int, [P, P, C.c_int, SZ, SZ, P, SZ, P, P, P, P]),
     "apx_act_describe_cols_async": (C.c_int, [P, P, P, SZ, SZ, P, P]),
     "apx_ffn_status_decode": (C.c_int, [C.POINTER(CallStatus), EP]),
     "apx_plan_create": (P, [P, C.POINTER(PlanProj), SZ, C.POINTER(PlanAct), SZ,

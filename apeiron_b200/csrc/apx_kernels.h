@@ -154,6 +154,21 @@ cudaError_t launch_limb_gemm_f32(const GemvPlan &pl, uint32_t type, const uint8_
                                  float *out_f32, unsigned long long *status, int sm_count,
                                  cudaStream_t stream);
 
+// Several tensors of one family, each with digit planes of the same digit count, reading one
+// activation (q/k/v; gate/up): one quantize-and-digits prep, then each member's GEMM over it.
+struct LimbMember {
+  const GemvPlan *pl;
+  const uint8_t *pack;
+  const LimbLayout *lay;
+  size_t n_out;
+  long long *out_q32;
+  float *out_f32;
+  unsigned long long *status;
+};
+cudaError_t launch_limb_gemm_f32_group(uint32_t type, const LimbMember *m, int count,
+                                       size_t n_in, size_t n_cols, const float *x, size_t ldx,
+                                       void *work, int sm_count, cudaStream_t stream);
+
 // The FFN hidden activation (apx_ffn.cu): SwiGLU under the carrier, then quant_act; `work` holds
 // swiglu_work_bytes(n).
 size_t swiglu_work_bytes(size_t n, size_t cols = 1);

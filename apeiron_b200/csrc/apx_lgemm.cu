@@ -387,7 +387,16 @@ struct LPrepArgs {
   int smax3;      // the largest activation spread of the three-digit route on this tensor
   LWork w;
   unsigned long long *status;  // column c's refusal word at status[c·2]
+  unsigned long long *status_more[3];  // a group's other members' refusal words
+  int n_more;
 };
+
+// An activation refusal goes to every member of the call.
+__device__ __forceinline__ void prep_refuse(const LPrepArgs &a, int c, int kind) {
+  atomicMin(a.status + (size_t)c * 2, pack_status(0, (unsigned)kind, 0));
+  for (int m = 0; m < a.n_more; m++)
+    atomicMin(a.status_more[m] + (size_t)c * 2, pack_status(0, (unsigned)kind, 0));
+}
 
 __device__ __forceinline__ void lzero_column(const LPrepArgs &a, int c, size_t np) {
   const uint4 z = make_uint4(0, 0, 0, 0);
@@ -470,7 +479,7 @@ __global__ void __launch_bounds__(256) limb_prep_kernel(LPrepArgs a) {
     const int emin = s_emax >= 0 ? s_emin : 0;
     unsigned route = kRouteNone;
     if (s_status != APX_OK)
-      atomicMin(a.status + (size_t)c * 2, pack_status(0, (unsigned)s_status, 0));
+      prep_refuse(a, c, s_status);
     else
       route = lroute(a, emin, s_emax);
     s_emin = emin;
@@ -590,7 +599,7 @@ __global__ void __launch_bounds__(256) limb_quant_prep_kernel(LPrepArgs a) {
   if (s_status != APX_OK) {  // quant_act returned None for the column
     lzero_column(a, c, np);
     if (threadIdx.x == 0) {
-      atomicMin(a.status + (size_t)c * 2, pack_status(0, (unsigned)s_status, 0));
+      prep_refuse(a, c, s_status);
       a.w.emin[c] = 0;
       a.w.route[c] = kRouteNone;
     }
@@ -1207,6 +1216,7 @@ LPrepArgs prep_args(uint32_t type, const LimbLayout &lay, size_t n_out, size_t n
   pa.smax3 = three_digit_limit(lay);
   pa.w = w;
   pa.status = status;
+  pa.n_more = 0;
   return pa;
 }
 
@@ -1369,6 +1379,44 @@ cudaError_t launch_limb_gemm_f32(const GemvPlan &pl, uint32_t type, const uint8_
   if (e != cudaSuccess) return e;
   return launch_main_any(type, pl, pack, lay, n_out, n_in, n_cols, w.qcodes, lay.kp, w.qexps,
                          lay.kp / 32, w, out_q32, out_f32, status, sm_count, stream);
+}
+
+cudaError_t launch_limb_gemm_f32_group(uint32_t type, const LimbMember *m, int count,
+                                       size_t n_in, size_t n_cols, const float *x, size_t ldx,
+                                       void *work, int sm_count, cudaStream_t stream) {
+  if (count < 1 || count > 4) return cudaErrorInvalidValue;
+  if (n_cols == 0) return cudaSuccess;
+  size_t n_out_max = 0;
+  int smax3 = kLMaxShift3, tiles = 0;
+  for (int i = 0; i < count; i++) {
+    const LimbLayout &lay = *m[i].lay;
+    if (!lay.ok || lay.digits != m[0].lay->digits || lay.kp != m[0].lay->kp || m[i].n_out == 0)
+      return cudaErrorInvalidValue;
+    n_out_max = std::max(n_out_max, m[i].n_out);
+    smax3 = std::min(smax3, three_digit_limit(lay));
+  }
+  if (!limb_f32_ok(n_in, x, ldx)) return cudaErrorInvalidValue;
+  // one view of the workspace for every member: sized for the most rows
+  const LWork w = lwork_view(work, n_cols, n_in, n_out_max, sm_count);
+  LPrepArgs pa = prep_args(type, *m[0].lay, n_out_max, n_in, n_cols, w, m[0].status);
+  pa.smax3 = smax3;  // a column takes the three-digit route only where every member allows it
+  for (int i = 0; i < count; i++)
+    tiles = std::max(tiles, (int)ltiles(m[i].n_out, n_cols, tile_tokens(m[i].lay->digits)));
+  pa.tiles = tiles;
+  pa.n_more = count - 1;
+  for (int i = 1; i < count; i++) pa.status_more[i - 1] = m[i].status;
+  pa.x = x;
+  pa.ldx = ldx;
+  const size_t smem = m[0].lay->kp + m[0].lay->kp / 32 + 16;
+  static const bool carve = set_prep_carveout();
+  (void)carve;
+  limb_quant_prep_kernel<<<(unsigned)pa.np, 256, smem, stream>>>(pa);
+  cudaError_t e = cudaGetLastError();
+  for (int i = 0; e == cudaSuccess && i < count; i++)
+    e = launch_main_any(type, *m[i].pl, m[i].pack, *m[i].lay, m[i].n_out, n_in, n_cols, w.qcodes,
+                        m[i].lay->kp, w.qexps, m[i].lay->kp / 32, w, m[i].out_q32,
+                        m[i].out_f32, m[i].status, sm_count, stream);
+  return e;
 }
 
 }  // namespace apx

@@ -1154,6 +1154,70 @@ int apx_swiglu_quant_async(apx_ctx *ctx, const int64_t *d_gate, const int64_t *d
   return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
 }
 
+int apx_matmat_f32_group_async(apx_ctx *ctx, const uint64_t *tensors, int count, size_t n_in,
+                               size_t k_cols, const float *d_x, size_t ldx,
+                               int64_t *const *d_out_q32, float *const *d_out_f32,
+                               apx_call_status *const *d_status, void *stream) {
+  if (!ctx || !tensors || count < 1 || count > APX_MAX_GROUP || !d_status ||
+      (k_cols && n_in && !d_x) || ldx < n_in)
+    return APX_ERR_INVALID_ARGUMENT;
+  for (int i = 0; i < count; i++)
+    if (!d_status[i]) return APX_ERR_INVALID_ARGUMENT;
+  if (k_cols > (size_t)INT32_MAX) return APX_ERR_TOO_LARGE;
+  if (k_cols == 0) return APX_OK;
+  bool grouped = true;
+  {
+    std::lock_guard<std::mutex> g(ctx->mu);
+    Tensor *ts[APX_MAX_GROUP];
+    size_t n_out_max = 0;
+    for (int i = 0; i < count; i++) {
+      ts[i] = find(ctx, tensors[i]);
+      if (!ts[i] || ts[i]->n_in != n_in) return APX_ERR_LAYOUT_MISMATCH;
+      n_out_max = std::max(n_out_max, ts[i]->n_out);
+    }
+    // one prep over the activation when every member runs the digit-plane GEMM alike
+    for (int i = 0; grouped && i < count; i++) {
+      Tensor &t = *ts[i];
+      grouped = t.type == ts[0]->type && k_cols >= kGemmMinCols && t.d_pack && t.n_out &&
+                limb_shape_ok(n_in);
+      if (grouped && !t.limb_tried) {
+        t.limb_tried = true;
+        if (build_limb_layout(t.plan, t.type, t.d_pack, t.n_out, t.n_in, &t.limb, ctx->stream) !=
+            cudaSuccess)
+          cudaGetLastError();
+      }
+      grouped = grouped && t.limb.ok && t.limb.digits == ts[0]->limb.digits;
+    }
+    grouped = grouped && limb_f32_ok(n_in, d_x, ldx) &&
+              ensure_gwork(ctx, kTcLimb, k_cols, n_in, n_out_max) == cudaSuccess;
+    if (grouped) {
+      LimbMember m[APX_MAX_GROUP];
+      for (int i = 0; i < count; i++)
+        m[i] = LimbMember{&ts[i]->plan, ts[i]->d_pack, &ts[i]->limb, ts[i]->n_out,
+                          d_out_q32 ? (long long *)d_out_q32[i] : nullptr,
+                          d_out_f32 ? d_out_f32[i] : nullptr,
+                          (unsigned long long *)d_status[i]};
+      const cudaError_t e = launch_limb_gemm_f32_group(ts[0]->type, m, count, n_in, k_cols, d_x,
+                                                       ldx, ctx->lwork.p, ctx->sm_count,
+                                                       (cudaStream_t)stream);
+      return e == cudaSuccess ? APX_OK : APX_ERR_CUDA;
+    }
+  }
+  // otherwise each member on its own route
+  for (int i = 0; i < count; i++) {
+    Tensor *t;
+    {
+      std::lock_guard<std::mutex> g(ctx->mu);
+      t = find(ctx, tensors[i]);
+    }
+    const int rc = apx_matmat_f32_async(ctx, tensors[i], t->n_out, n_in, k_cols, d_x, ldx,
+                                        d_out_q32 ? d_out_q32[i] : nullptr,
+                                        d_out_f32 ? d_out_f32[i] : nullptr, d_status[i], stream);
+    if (rc != APX_OK) return rc;
+  }
+  return APX_OK;
+}
+
 int apx_swiglu_quant_shard_async(apx_ctx *ctx, const int64_t *d_gate, const int64_t *d_up,
                                  size_t n, int carrier, int64_t *d_h, int8_t *d_codes,
                                  uint8_t *d_exps, apx_act_desc *d_desc, int n_peers,

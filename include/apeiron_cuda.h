@@ -292,6 +292,18 @@ APX_API int apx_status_decode(apx_ctx *ctx, uint64_t tensor, const apx_call_stat
 APX_API int apx_status_decode_rows(apx_ctx *ctx, uint64_t tensor, size_t n_out,
                                    const apx_call_status *status, apx_err *err);
 
+/* The prefill of several tensors reading one activation (q/k/v; gate/up: gemm_q8_0_group,
+ * src/engine/kern/gemm.rs:818, for every family): member i's whole rows, k_cols f32 columns of
+ * d_x as apx_matmat_f32_async takes them, outputs d_out_q32[i] / d_out_f32[i] (either array may
+ * be NULL, or hold NULL) and refusal words d_status[i][c] (all ones on entry).  When every
+ * member has digit planes of one family and digit count, the activation is quantized into its
+ * digits once and each member's GEMM reads them; otherwise the members run one by one.  Each
+ * member's results equal its own apx_matmat_f32_async.  count <= APX_MAX_GROUP. */
+APX_API int apx_matmat_f32_group_async(apx_ctx *ctx, const uint64_t *tensors, int count,
+                                       size_t n_in, size_t k_cols, const float *d_x, size_t ldx,
+                                       int64_t *const *d_out_q32, float *const *d_out_f32,
+                                       apx_call_status *const *d_status, void *stream);
+
 /* apx_swiglu_quant_async for one slice of a row-sharded FFN's h: the codes, exponent bytes and
  * descriptor also go to n_peers other places (other GPUs' buffers, mapped with apx_peer_open),
  * element 0 of the slice at d_peer_codes[i][0] / d_peer_exps[i][0]; a publication

@@ -259,3 +259,60 @@ def test_auto_route_by_call_size(be):
         assert grown in digit_plane_bytes(n_out, n_in)
     finally:
         assert be.lib.apx_ctx_set_gemm_route(be.ctx, _abi.GEMM_DIGITS) == 0
+
+
+@pytest.mark.parametrize("members,n_in,k", [
+    ([(Q8_0, 896), (Q8_0, 128), (Q8_0, 128)], 896, 64),      # q/k/v of the 0.5B model
+    ([(Q4_K, 1536), (Q4_K, 256), (Q4_K, 256)], 1536, 40),
+    ([(Q6_K, 2048), (Q6_K, 2048)], 1024, 17),                # gate/up
+    ([(Q4_K, 512), (Q8_0, 512)], 1024, 8),                   # families differ: member by member
+])
+def test_grouped_prefill_equals_members(be, members, n_in, k):
+    """apx_matmat_f32_group_async: one quantize-and-digits prep for the shared activation, then
+    every member's GEMM; each member's Q32.32 and f32 outputs and refusal words equal its own
+    apx_matmat_f32_async, a token holding a NaN is refused for every member, and member 0
+    equals the oracle."""
+    import ctypes as C
+
+    import torch
+
+    lib = be.lib
+    dev = torch.device("cuda:0")
+    stream = torch.cuda.current_stream().cuda_stream
+    raws = [synth.payload(t, n_out, n_in, 800 + i) for i, (t, n_out) in enumerate(members)]
+    tens = [be.upload(t, raws[i], n_out, n_in) for i, (t, n_out) in enumerate(members)]
+    x = np.stack([synth.activation_f32(n_in, 900 + c) for c in range(k)])
+    x[k // 2, 7] = np.nan
+    dx = torch.from_numpy(x).to(dev)
+    count = len(members)
+
+    def outs():
+        return ([torch.zeros(k * n, dtype=torch.int64, device=dev) for _, n in members],
+                [torch.zeros(k * n, dtype=torch.float32, device=dev) for _, n in members],
+                [torch.full((2 * k,), -1, dtype=torch.int64, device=dev) for _ in members])
+
+    gq, gf, gs = outs()
+    P = lambda ts: (C.c_void_p * count)(*[t.data_ptr() for t in ts])
+    assert lib.apx_matmat_f32_group_async(be.ctx, (C.c_uint64 * count)(*[t.handle for t in tens]),
+                                          count, n_in, k, dx.data_ptr(), n_in, P(gq), P(gf), P(gs),
+                                          stream) == 0
+    sq, sf, ss = outs()
+    for i, (t, n_out) in enumerate(members):
+        assert lib.apx_matmat_f32_async(be.ctx, tens[i].handle, n_out, n_in, k, dx.data_ptr(),
+                                        n_in, sq[i].data_ptr(), sf[i].data_ptr(),
+                                        ss[i].data_ptr(), stream) == 0
+    torch.cuda.synchronize()
+    for i in range(count):
+        assert np.array_equal(gs[i].cpu().numpy(), ss[i].cpu().numpy()), i
+        words = gs[i].cpu().numpy()[0::2]
+        assert words[k // 2] != -1 and (np.delete(words, k // 2) == -1).all(), i
+        ok = [c for c in range(k) if c != k // 2]
+        q = gq[i].cpu().numpy().reshape(k, -1)
+        assert np.array_equal(q[ok], sq[i].cpu().numpy().reshape(k, -1)[ok]), i
+        f = gf[i].cpu().numpy().reshape(k, -1)
+        assert np.array_equal(f[ok].view(np.uint32),
+                              sf[i].cpu().numpy().reshape(k, -1)[ok].view(np.uint32)), i
+    t0, n0 = members[0]
+    c0, s0 = O.quant_act(synth.f32_to_q32(x[0]))
+    want = O.matvec_q8act_mt(t0, raws[0], n0, n_in, c0, s0, THREADS, simd=True)
+    assert np.array_equal(gq[0].cpu().numpy()[:n0], want)
