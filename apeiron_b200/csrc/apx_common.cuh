@@ -216,4 +216,29 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
   return false;
 }
 
+// ---- thread-block clusters ------------------------------------------------------------------
+// The CTAs of a cluster are co-scheduled, and each can store into the others' shared memory
+// (distributed shared memory).  barrier.cluster completes when every non-exited thread of the
+// cluster has arrived: a hardware barrier like __syncthreads, not a poll.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The address of `p` (in this CTA's shared memory) in the shared memory of cluster CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_map(const void *p, unsigned rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_acc(uint32_t addr, unsigned long long lo,
+                                               unsigned long long hi) {
+  asm volatile("st.shared::cluster.v2.u64 [%0], {%1, %2};" ::"r"(addr), "l"(lo), "l"(hi)
+               : "memory");
+}
+
 }  // namespace apx

@@ -115,6 +115,7 @@ struct GemvArgs {
   Acc128 *partials;     // [n_rt][ksplit][32] partial sums of a K-split row tile
   unsigned *counters;   // [n_rt] arrivals of a K-split row tile (self-resetting)
   int R, P, ksplit;     // row tiles per CTA, warps per row tile, CTAs per row tile along K
+  int cluster;          // > 1: the ksplit CTAs of a row tile are one cluster (R = 1)
   int act_bytes;        // shared bytes of the activation staging / partial sums
   PeerRows peers;       // also store the outputs there (row-sharded gather), n = 0 otherwise
   GemvGroup grp;        // several tensors sharing the activation, n = 0 otherwise
@@ -177,6 +178,9 @@ __global__ void __launch_bounds__(384, 2) gemv_kernel(GemvArgs g) {
   const uint8_t *base = pack + rt * (size_t)g.units * F::unit_bytes;
   const int L = g.L, H = 32 / L, slot = lane % L;
   const int nch = L * F::span / 16;  // chunks staged per unit: 8, 16, 32 or 64
+  // a cluster's CTAs store into CTA 0's shared memory at the end: each arrives here, and
+  // waits there for the others, so that none is written before it has started
+  if (g.cluster > 1) cluster_arrive_relaxed();
 
   pdl_launch_dependents();
   // weights first, straight into registers: they depend on nothing the previous kernel
@@ -203,7 +207,10 @@ __global__ void __launch_bounds__(384, 2) gemv_kernel(GemvArgs g) {
     }
     return;
   }
-  if (!fast_path<T>(desc, g.n_in)) {
+  // the fast fold within the family's spread limit, the wide one beyond it while the call
+  // bound holds, the checked rows otherwise
+  const bool wide = !fast_path<T>(desc, g.n_in);
+  if (wide && !wide_path<T>(desc, g.n_in)) {
     if (ks == 0 && p == 0 && active && slot == 0) {
       GroupOut go{g.n_out, g.out_q32, g.out_f32, g.status};
       if (g.grp.n) go = group_outputs(g.grp, rt0 + r);
@@ -219,11 +226,15 @@ __global__ void __launch_bounds__(384, 2) gemv_kernel(GemvArgs g) {
   Acc128 acc;
   acc_zero(acc);
   if (first) {
-    store_chunk<T>(*w, ch0, lane, lane < nch, desc.emin);
-    if (nch > 32) store_chunk<T>(*w, ch1, lane + 32, lane + 32 < nch, desc.emin);
+    store_chunk<T>(*w, ch0, lane, lane < nch, desc.emin, wide);
+    if (nch > 32) store_chunk<T>(*w, ch1, lane + 32, lane + 32 < nch, desc.emin, wide);
     __syncwarp();
-    fold_unit(acc, cur, w->codes + slot * slot_ints<T>(), w->e + slot * (F::span / 32),
-              w->xs + slot * F::nxs, desc.emin);
+    if (wide)
+      fold_unit_wide(acc, cur, w->codes + slot * slot_ints<T>(), w->e + slot * (F::span / 32),
+                     w->xs + slot * F::nxs, desc.emin);
+    else
+      fold_unit(acc, cur, w->codes + slot * slot_ints<T>(), w->e + slot * (F::span / 32),
+                w->xs + slot * F::nxs, desc.emin);
   }
   // the L lanes of a row combine
   for (int o = 1; o < L; o <<= 1) {
@@ -244,7 +255,20 @@ __global__ void __launch_bounds__(384, 2) gemv_kernel(GemvArgs g) {
     for (int q = 1; q < g.P; q++) acc_add(s, part[(r * g.P + q) * 32 + lane]);
   }
   bool finalize = ks == 0;
-  if (g.ksplit > 1) {
+  if (g.cluster > 1) {
+    // the row tile's CTAs are one cluster (R = 1): each stores its partial into CTA 0's shared
+    // memory, and CTA 0 sums them once the cluster barrier has seen every store
+    Acc128 *slots = reinterpret_cast<Acc128 *>(smem + g.act_bytes);  // [ksplit][32]
+    cluster_wait_acquire();  // every CTA of the cluster has started
+    if (p == 0 && active) st_cluster_acc(cluster_map(slots + ks * 32 + lane, 0), s.lo, s.hi);
+    cluster_arrive_release();
+    if (ks != 0) return;
+    cluster_wait_acquire();
+    if (p == 0 && active) {
+      acc_zero(s);
+      for (int q = 0; q < g.ksplit; q++) acc_add(s, slots[q * 32 + lane]);
+    }
+  } else if (g.ksplit > 1) {
     // last-arriving CTA of the row tile sums the others' partials (threadfence reduction)
     unsigned *ticket = reinterpret_cast<unsigned *>(part + g.R * g.P * 32);
     if (p == 0 && active) {
@@ -328,7 +352,8 @@ __global__ void __launch_bounds__(stream_threads<T>(), T == kQ6_K ? 1 : 2)
       atomicMin(g.status, pack_status(0, (unsigned)desc.status, 0));
     return;
   }
-  if (!fast_path<T>(desc, g.n_in)) {
+  const bool wide = !fast_path<T>(desc, g.n_in);  // as in gemv_kernel
+  if (wide && !wide_path<T>(desc, g.n_in)) {
     // the warp holding a row tile's first unit runs that tile's checked rows
     for (long long x = x0; x < x1; x++) {
       if (x % U != 0) continue;
@@ -361,7 +386,7 @@ __global__ void __launch_bounds__(stream_threads<T>(), T == kQ6_K ? 1 : 2)
     const int s32 = s16 + __shfl_xor_sync(0xFFFFFFFFu, s16, 1);
     if (!in) continue;
     reinterpret_cast<uint4 *>(s_codes)[j16] = val;
-    if (T == kQ6_K) s_xs[j16] = (long long)s16 << er;
+    if (T == kQ6_K) s_xs[j16] = wide ? (long long)s16 : (long long)s16 << er;
     if ((j16 & 1) == 0) {
       s_e[j16 / 2] = T == kQ8_0 ? (zero ? -1 : (int)ch.e) : er;
       if (T == kQ4_K) s_xs[j16 / 2] = s32;
@@ -380,8 +405,12 @@ __global__ void __launch_bounds__(stream_threads<T>(), T == kQ6_K ? 1 : 2)
     UnitRegs<T> nxt;
     const bool more = x + 1 < x1;
     if (more) load_unit(nxt, next_unit, lane);
-    fold_unit(acc, cur, s_codes + u * (F::span / 4), s_e + u * (F::span / 32),
-              s_xs + u * F::nxs, desc.emin);
+    if (wide)
+      fold_unit_wide(acc, cur, s_codes + u * (F::span / 4), s_e + u * (F::span / 32),
+                     s_xs + u * F::nxs, desc.emin);
+    else
+      fold_unit(acc, cur, s_codes + u * (F::span / 4), s_e + u * (F::span / 32),
+                s_xs + u * F::nxs, desc.emin);
     if (u == U - 1 || !more) {
       // flush this warp's share of row tile rt
       const long long first_v = (rt * U) / g.chunk;
@@ -503,6 +532,15 @@ static size_t warp_act_bytes(uint32_t t) {
                     : (t == kQ4_K ? sizeof(WarpAct<kQ4_K>) : sizeof(WarpAct<kQ6_K>));
 }
 
+// The most CTAs of a K split that run as one cluster (8, the portable cluster size).
+static int max_cluster_split() {
+  static const int v = [] {
+    const char *e = std::getenv("APX_GEMV_CLUSTER_MAX");  // 0 or 1: scratch splits only
+    return e ? std::max(0, std::min(8, atoi(e))) : 8;
+  }();
+  return v;
+}
+
 GemvPlan plan_gemv(uint32_t type, size_t n_out, size_t n_in, int sm_count) {
   GemvPlan pl{};
   const int K = units_per_row_tile(type, n_in);  // K-slots per row (0 for n_in = 0)
@@ -555,18 +593,24 @@ GemvPlan plan_gemv(uint32_t type, size_t n_out, size_t n_in, int sm_count) {
   }
   if ((size_t)pl.R > n_rt) pl.R = (int)(n_rt ? n_rt : 1);
   const size_t rows = pl.R > 1 ? (size_t)sm_count : (n_rt + pl.R - 1) / pl.R;
+  // A K split of up to 8 CTAs runs as one thread-block cluster per row tile: the partial sums
+  // meet in CTA 0's shared memory instead of global scratch and an arrival counter.  (Splitting
+  // row tiles over clusters only to even out the CTAs per SM was slower on the configs[0] and
+  // configs[1] shapes: 608 CTAs of 2 warps 3.08 us against 152 of 7 warps 2.69 us.)
+  pl.cluster = pl.ksplit > 1 && pl.ksplit <= max_cluster_split() ? pl.ksplit : 0;
   pl.grid = (unsigned)(rows * pl.ksplit);
   pl.block = 32 * pl.R * pl.P;
   const size_t stage = (size_t)pl.R * pl.P * warp_act_bytes(type);
   const size_t red = (size_t)pl.R * pl.P * 32 * sizeof(Acc128) + 64;
   pl.act_bytes = (int)((std::max(stage, red) + 15) & ~(size_t)15);
-  pl.smem = pl.act_bytes;
+  // a cluster's partial sums: [ksplit][32] in CTA 0's shared memory, after the staging
+  pl.smem = pl.act_bytes + (pl.cluster ? (size_t)pl.cluster * 32 * sizeof(Acc128) : 0);
   return pl;
 }
 
 size_t gemv_scratch_bytes(const GemvPlan &pl) {
   if (pl.pipe) return pl.n_rt * (size_t)pl.kmax * 32 * sizeof(Acc128) + pl.n_rt * sizeof(unsigned);
-  if (pl.ksplit <= 1) return 0;
+  if (pl.ksplit <= 1 || pl.cluster > 1) return 0;
   return pl.n_rt * (size_t)pl.ksplit * 32 * sizeof(Acc128) + pl.n_rt * sizeof(unsigned);
 }
 
@@ -597,11 +641,22 @@ static cudaError_t launch_cfg(Kern kern, const GemvPlan &pl, const Args &a, cuda
   cfg.blockDim = dim3(pl.block);
   cfg.dynamicSmemBytes = pl.smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (pdl_enabled() && !tl_pdl_suppressed) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    n++;
+  }
+  if (!pl.pipe && pl.cluster > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = (unsigned)pl.cluster;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    n++;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() && !tl_pdl_suppressed ? 1 : 0;
+  cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
@@ -611,7 +666,7 @@ cudaError_t launch_gemv(const GemvPlan &pl, uint32_t type, const uint8_t *pack, 
                         unsigned long long *status, cudaStream_t stream, const PeerRows *peers) {
   const PeerRows no_peers{};
   if (n_out == 0) return cudaSuccess;
-  if ((pl.pipe || pl.ksplit > 1) && !scratch) return cudaErrorInvalidValue;
+  if ((pl.pipe || (pl.ksplit > 1 && pl.cluster <= 1)) && !scratch) return cudaErrorInvalidValue;
   if (pl.units > 0 && !pack) return cudaErrorInvalidValue;  // a plan that reads no payload
   if (pl.pipe) {
     StreamArgs sa;
@@ -652,13 +707,15 @@ cudaError_t launch_gemv(const GemvPlan &pl, uint32_t type, const uint8_t *pack, 
   a.out_q32 = out_q32;
   a.out_f32 = out_f32;
   a.status = status;
-  a.partials = reinterpret_cast<Acc128 *>(scratch);
-  a.counters = pl.ksplit > 1 ? reinterpret_cast<unsigned *>(
-                                   reinterpret_cast<Acc128 *>(scratch) + pl.n_rt * pl.ksplit * 32)
-                             : nullptr;
+  const bool global_split = pl.ksplit > 1 && pl.cluster <= 1;
+  a.partials = global_split ? reinterpret_cast<Acc128 *>(scratch) : nullptr;
+  a.counters = global_split ? reinterpret_cast<unsigned *>(reinterpret_cast<Acc128 *>(scratch) +
+                                                           pl.n_rt * pl.ksplit * 32)
+                            : nullptr;
   a.R = pl.R;
   a.P = pl.P;
   a.ksplit = pl.ksplit;
+  a.cluster = pl.cluster > 1 ? pl.cluster : 1;
   a.act_bytes = pl.act_bytes;
   a.peers = peers ? *peers : no_peers;
   a.grp = GemvGroup{};
@@ -673,7 +730,8 @@ cudaError_t launch_gemv(const GemvPlan &pl, uint32_t type, const uint8_t *pack, 
 cudaError_t launch_gemv_group(const GemvPlan &pl, uint32_t type, const GemvGroup &grp,
                               size_t n_in, const int8_t *codes, const uint8_t *exps,
                               const void *desc, cudaStream_t stream) {
-  if (grp.n < 1 || grp.n > kMaxGroup || pl.pipe || pl.ksplit != 1) return cudaErrorInvalidValue;
+  if (grp.n < 1 || grp.n > kMaxGroup || pl.pipe || (pl.ksplit != 1 && pl.cluster != pl.ksplit))
+    return cudaErrorInvalidValue;  // a K split only through a cluster: no scratch here
   GemvArgs a{};
   a.pack = grp.pack[0];
   a.units = pl.units;
@@ -689,7 +747,8 @@ cudaError_t launch_gemv_group(const GemvPlan &pl, uint32_t type, const GemvGroup
   a.status = grp.status[0];
   a.R = pl.R;
   a.P = pl.P;
-  a.ksplit = 1;
+  a.ksplit = pl.ksplit;
+  a.cluster = pl.cluster > 1 ? pl.cluster : 1;
   a.act_bytes = pl.act_bytes;
   a.grp = grp;
   switch (type) {

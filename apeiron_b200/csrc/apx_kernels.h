@@ -15,6 +15,8 @@ struct GemvPlan {
   size_t n_rt;     // row tiles
   int R, P;        // row tiles per CTA, warps per row tile
   int ksplit;      // CTAs per row tile along K
+  int cluster;     // ksplit when those CTAs form a thread-block cluster (their partial sums
+                   // meet in distributed shared memory), else 0: scratch and arrival counters
   bool pipe;       // persistent streaming kernel (matrices beyond one resident wave)
   long long chunk; // streaming: units per warp
   int kmax;        // streaming: most warps sharing one row tile

@@ -414,7 +414,12 @@ __global__ void __launch_bounds__(PlanShape<T>::kThreads, PlanShape<T>::kCtas)
     if (xn >= 0) pn = decode_piece(g, s_p0, xn);
     us.top_up(g, pc, pn, xn >= 0, lane);
 
-    const bool fast = ready && desc.status == APX_OK && fast_path<T>(desc, P.n_in);
+    // the fold: the fast one within the family's spread limit, the wide one beyond it while
+    // the call bound holds; other activations take the checked rows
+    const bool ok = ready && desc.status == APX_OK;
+    const bool narrow = ok && fast_path<T>(desc, P.n_in);
+    const bool wide = ok && !narrow && wide_path<T>(desc, P.n_in);
+    const bool fast = narrow || wide;
     if (fast && !act_pre) fetch(P, A, pc.u0, c0, c1);
     bool next_pre = false, copies_ok = true;
     Acc128 acc;
@@ -429,8 +434,8 @@ __global__ void __launch_bounds__(PlanShape<T>::kThreads, PlanShape<T>::kCtas)
         continue;
       }
       WarpAct<T> &wb = wa[u & 1];
-      store_chunk<T>(wb, c0, lane, lane < nch, desc.emin);
-      if (nch > 32) store_chunk<T>(wb, c1, lane + 32, lane + 32 < nch, desc.emin);
+      store_chunk<T>(wb, c0, lane, lane < nch, desc.emin, wide);
+      if (nch > 32) store_chunk<T>(wb, c1, lane + 32, lane + 32 < nch, desc.emin, wide);
       __syncwarp();
       if (u + 1 < pc.u1) {
         fetch(P, A, u + 1, c0, c1);
@@ -447,7 +452,7 @@ __global__ void __launch_bounds__(PlanShape<T>::kThreads, PlanShape<T>::kCtas)
         }
       }
       fold_unit_smem<T>(acc, sl, lane, wb.codes + slot * slot_ints<T>(),
-                        wb.e + slot * (F::span / 32), wb.xs + slot * F::nxs, desc.emin);
+                        wb.e + slot * (F::span / 32), wb.xs + slot * F::nxs, desc.emin, wide);
       us.release_front();  // the fold has read the slot: the next copy may refill it
       us.top_up(g, pc, pn, xn >= 0, lane);
     }

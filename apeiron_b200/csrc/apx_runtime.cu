@@ -1008,13 +1008,14 @@ int apx_matvec_group_async(apx_ctx *ctx, const uint64_t *tensors, int count, siz
     for (int i = 0; i < count; i++) {
       const Tensor &t = *ts[i];
       one_launch = one_launch && t.d_pack && t.n_out > 0 && !t.plan.pipe &&
-                   t.plan.ksplit == 1 && t.type == ts[0]->type && t.plan.L == ts[0]->plan.L &&
+                   t.type == ts[0]->type && t.plan.L == ts[0]->plan.L &&
                    t.plan.units == ts[0]->plan.units;
       n_rt += t.plan.n_rt;
     }
     if (one_launch) {
       pl = plan_gemv(ts[0]->type, n_rt * (size_t)(32 / ts[0]->plan.L), n_in, ctx->sm_count);
-      one_launch = !pl.pipe && pl.ksplit == 1 && pl.L == ts[0]->plan.L &&
+      one_launch = !pl.pipe && (pl.ksplit == 1 || pl.cluster == pl.ksplit) &&
+                   pl.L == ts[0]->plan.L &&
                    pl.units == ts[0]->plan.units && pl.n_rt == n_rt;
     }
   }

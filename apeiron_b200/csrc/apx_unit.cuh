@@ -171,17 +171,16 @@ __device__ __forceinline__ void q4k_dots(const V &w, const int *a, int p, int &d
 // magnitude (|16·D| <= 16·32·15·127, scale <= 63) and eight of them stay below 2^31, so the
 // super-block folds in int32; otherwise in int64 (the call's spread limit keeps that exact).
 constexpr int kQ4Narrow = 2;
+// ev: the eight group exponents relative to `ebase`, each in [0, emax8], emax8 <= es_limit.
 template <class V>
-__device__ __forceinline__ void fold_q4_k(Acc128 &acc, const V &w, const int *a, const int *er,
-                                          const long long *xs, int emin) {
+__device__ __forceinline__ void fold_q4_k_ev(Acc128 &acc, const V &w, const int *a,
+                                             const int (&ev)[8], int emax8, const long long *xs,
+                                             int ebase) {
   // get_scale_min_k4 (format/quant.rs:482-491) for all 8 pairs at once.
   const uint4 h = q4_head(w);
   const unsigned sc_lo = h.y & 0x3F3F3F3Fu, mn_lo = h.z & 0x3F3F3F3Fu;
   const unsigned sc_hi = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
   const unsigned mn_hi = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
-  const int4 e0 = reinterpret_cast<const int4 *>(er)[0], e1 = reinterpret_cast<const int4 *>(er)[1];
-  const int ev[8] = {e0.x, e0.y, e0.z, e0.w, e1.x, e1.y, e1.z, e1.w};
-  const int emax8 = max(max(max(e0.x, e0.y), max(e0.z, e0.w)), max(max(e1.x, e1.y), max(e1.z, e1.w)));
   long long A16, B;
   if (emax8 <= kQ4Narrow) {
     int A32 = 0, B32 = 0;
@@ -220,17 +219,34 @@ __device__ __forceinline__ void fold_q4_k(Acc128 &acc, const V &w, const int *a,
   unsigned kd, km;
   f16_split(h.x & 0xFFFFu, md, kd);
   f16_split(h.x >> 16, mm, km);
-  acc_add_shl(acc, (long long)md * A16, kd + (unsigned)emin - 4u);
-  acc_sub_shl(acc, (long long)mm * B, km + (unsigned)emin);
+  acc_add_shl(acc, (long long)md * A16, kd + (unsigned)ebase - 4u);
+  acc_sub_shl(acc, (long long)mm * B, km + (unsigned)ebase);
+}
+__device__ __forceinline__ void load_ev8(const int *er, int (&ev)[8]) {
+  const int4 e0 = reinterpret_cast<const int4 *>(er)[0], e1 = reinterpret_cast<const int4 *>(er)[1];
+  ev[0] = e0.x; ev[1] = e0.y; ev[2] = e0.z; ev[3] = e0.w;
+  ev[4] = e1.x; ev[5] = e1.y; ev[6] = e1.z; ev[7] = e1.w;
+}
+template <class V>
+__device__ __forceinline__ void fold_q4_k(Acc128 &acc, const V &w, const int *a, const int *er,
+                                          const long long *xs, int emin) {
+  int ev[8];
+  load_ev8(er, ev);
+  const int emax8 = max(max(max(ev[0], ev[1]), max(ev[2], ev[3])),
+                        max(max(ev[4], ev[5]), max(ev[6], ev[7])));
+  fold_q4_k_ev(acc, w, a, ev, emax8, xs, emin);
 }
 __device__ __forceinline__ void fold_unit(Acc128 &acc, const UnitRegs<kQ4_K> &w, const int *a,
                                           const int *er, const long long *xs, int emin) {
   fold_q4_k(acc, RegView<kQ4_K>{w}, a, er, xs, emin);
 }
 
-template <class V>
-__device__ __forceinline__ void fold_q6_k(Acc128 &acc, const V &wr, const int *a, const int *er,
-                                          const long long *xs16, int emin) {
+// ev: the eight 32-element blocks' exponents relative to `ebase`, each at most es_limit; xs16
+// the 16-element groups' Σxq, already shifted by their block's ev unless kShiftXs.
+template <bool kShiftXs, class V>
+__device__ __forceinline__ void fold_q6_k_ev(Acc128 &acc, const V &wr, const int *a,
+                                             const int (&ev)[8], const long long *xs16,
+                                             int ebase) {
   // ql words 0..31, qh words 32..47
   int du[16];
 #pragma unroll
@@ -258,30 +274,156 @@ __device__ __forceinline__ void fold_q6_k(Acc128 &acc, const V &wr, const int *a
 #pragma unroll
   for (int g = 0; g < 16; g++) {
     int sc = (int)(signed char)byte_of(scw[g / 4], g % 4);
-    A += (long long)du[g] * (long long)(sc * (1 << er[g / 2]));
-    B += xs16[g] * (long long)sc;
+    A += (long long)du[g] * (long long)(sc * (1 << ev[g / 2]));
+    B += (kShiftXs ? xs16[g] << ev[g / 2] : xs16[g]) * (long long)sc;
   }
   long long Tv = A - 32 * B;  // codes are u - 32 (format/quant.rs:574-599)
   int md;
   unsigned kd;
   f16_split(q6_d(wr), md, kd);
-  acc_add_shl(acc, (long long)md * Tv, kd + (unsigned)emin);
+  acc_add_shl(acc, (long long)md * Tv, kd + (unsigned)ebase);
+}
+template <class V>
+__device__ __forceinline__ void fold_q6_k(Acc128 &acc, const V &wr, const int *a, const int *er,
+                                          const long long *xs16, int emin) {
+  int ev[8];
+  load_ev8(er, ev);
+  fold_q6_k_ev<false>(acc, wr, a, ev, xs16, emin);
 }
 __device__ __forceinline__ void fold_unit(Acc128 &acc, const UnitRegs<kQ6_K> &wr, const int *a,
                                           const int *er, const long long *xs16, int emin) {
   fold_q6_k(acc, RegView<kQ6_K>{wr}, a, er, xs16, emin);
 }
 
+// The wide folds: each group's term goes into the 128-bit accumulator with its own shift, so any
+// activation exponent spread folds exactly whenever the call-level bound holds (every partial
+// sum is then inside i128, chart/mod.rs:362-383).  The fast folds above sum a super-block's
+// groups in i64 first, which needs the spread within the family's es_limit.  er and xs as the
+// staging writes them with `wide` set (Q6_K's Σxq unshifted).
+template <class V>
+__device__ __forceinline__ void fold_q4_k_wide(Acc128 &acc, const V &w, const int *a,
+                                               const int *er, const long long *xs, int emin) {
+  // Within one super-block the spread is usually small even when the call's is not: the
+  // fast fold then runs on exponents relative to the super-block's own smallest.
+  int ev[8];
+  load_ev8(er, ev);
+  const int lo = min(min(min(ev[0], ev[1]), min(ev[2], ev[3])), min(min(ev[4], ev[5]), min(ev[6], ev[7])));
+  const int hi = max(max(max(ev[0], ev[1]), max(ev[2], ev[3])), max(max(ev[4], ev[5]), max(ev[6], ev[7])));
+  if (hi - lo <= Fam<kQ4_K>::es_limit) {
+#pragma unroll
+    for (int i = 0; i < 8; i++) ev[i] -= lo;
+    fold_q4_k_ev(acc, w, a, ev, hi - lo, xs, emin + lo);
+    return;
+  }
+  const uint4 h = q4_head(w);
+  const unsigned sc_lo = h.y & 0x3F3F3F3Fu, mn_lo = h.z & 0x3F3F3F3Fu;
+  const unsigned sc_hi = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+  const unsigned mn_hi = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+  int md, mm;
+  unsigned kd, km;
+  f16_split(h.x & 0xFFFFu, md, kd);
+  f16_split(h.x >> 16, mm, km);
+#pragma unroll
+  for (int p = 0; p < 4; p++) {
+    int dl, dh;
+    q4k_dots(w, a, p, dl, dh);
+    const int gl = 2 * p, gh = 2 * p + 1;
+    const long long scl = byte_of(gl < 4 ? sc_lo : sc_hi, gl & 3);
+    const long long sch = byte_of(gh < 4 ? sc_lo : sc_hi, gh & 3);
+    const long long mnl = byte_of(gl < 4 ? mn_lo : mn_hi, gl & 3);
+    const long long mnh = byte_of(gh < 4 ? mn_lo : mn_hi, gh & 3);
+    // the low nibbles' dot is scaled by 16 to share the high nibbles' shift (kd + e - 4)
+    acc_add_shl(acc, (long long)md * ((long long)(dl << 4) * scl),
+                kd + (unsigned)(emin + er[gl]) - 4u);
+    acc_add_shl(acc, (long long)md * ((long long)dh * sch), kd + (unsigned)(emin + er[gh]) - 4u);
+    acc_sub_shl(acc, (long long)mm * (xs[gl] * mnl), km + (unsigned)(emin + er[gl]));
+    acc_sub_shl(acc, (long long)mm * (xs[gh] * mnh), km + (unsigned)(emin + er[gh]));
+  }
+}
+
+template <class V>
+__device__ __forceinline__ void fold_q6_k_wide(Acc128 &acc, const V &wr, const int *a,
+                                               const int *er, const long long *xs16, int emin) {
+  int ev[8];  // as in fold_q4_k_wide: the fast fold relative to the super-block's smallest
+  load_ev8(er, ev);
+  const int lo = min(min(min(ev[0], ev[1]), min(ev[2], ev[3])), min(min(ev[4], ev[5]), min(ev[6], ev[7])));
+  const int hi = max(max(max(ev[0], ev[1]), max(ev[2], ev[3])), max(max(ev[4], ev[5]), max(ev[6], ev[7])));
+  if (hi - lo <= Fam<kQ6_K>::es_limit) {
+#pragma unroll
+    for (int i = 0; i < 8; i++) ev[i] -= lo;
+    fold_q6_k_ev<true>(acc, wr, a, ev, xs16, emin + lo);
+    return;
+  }
+  int du[16];
+#pragma unroll
+  for (int g = 0; g < 16; g++) du[g] = 0;
+#pragma unroll
+  for (int n = 0; n < 2; n++) {
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      unsigned ql0 = q6_word(wr, 16 * n + j), ql1 = q6_word(wr, 16 * n + 8 + j),
+               qh = q6_word(wr, 32 + 8 * n + j);
+      unsigned u1 = (ql0 & 0x0F0F0F0Fu) | ((qh << 4) & 0x30303030u);
+      unsigned u2 = (ql1 & 0x0F0F0F0Fu) | ((qh << 2) & 0x30303030u);
+      unsigned u3 = ((ql0 >> 4) & 0x0F0F0F0Fu) | (qh & 0x30303030u);
+      unsigned u4 = ((ql1 >> 4) & 0x0F0F0F0Fu) | ((qh >> 2) & 0x30303030u);
+      const int g = 8 * n + j / 4;
+      du[g] = dp4a_us(u1, a[32 * n + j], du[g]);
+      du[g + 2] = dp4a_us(u2, a[32 * n + 8 + j], du[g + 2]);
+      du[g + 4] = dp4a_us(u3, a[32 * n + 16 + j], du[g + 4]);
+      du[g + 6] = dp4a_us(u4, a[32 * n + 24 + j], du[g + 6]);
+    }
+  }
+  const uint4 scv = q6_scales(wr);
+  const unsigned scw[4] = {scv.x, scv.y, scv.z, scv.w};
+  int md;
+  unsigned kd;
+  f16_split(q6_d(wr), md, kd);
+#pragma unroll
+  for (int g = 0; g < 16; g++) {
+    const long long sc = (signed char)byte_of(scw[g / 4], g % 4);
+    const long long t = (long long)du[g] * sc - 32 * xs16[g] * sc;  // codes are u - 32
+    acc_add_shl(acc, (long long)md * t, kd + (unsigned)(emin + er[g / 2]));
+  }
+}
+
 // The fold of a unit read from its copy in shared memory.
 template <uint32_t T>
 __device__ __forceinline__ void fold_unit_smem(Acc128 &acc, const uint8_t *ub, int lane,
                                                const int *a, const int *er, const long long *xs,
-                                               int emin) {
-  if (T == kQ8_0) fold_q8_0(acc, SmemView<kQ8_0>{ub, lane}, a, er);
+                                               int emin, bool wide = false) {
+  if (T == kQ8_0) fold_q8_0(acc, SmemView<kQ8_0>{ub, lane}, a, er);  // per block already
+  else if (T == kQ4_K && wide) fold_q4_k_wide(acc, SmemView<kQ4_K>{ub, lane}, a, er, xs, emin);
   else if (T == kQ4_K) fold_q4_k(acc, SmemView<kQ4_K>{ub, lane}, a, er, xs, emin);
+  else if (wide) fold_q6_k_wide(acc, SmemView<kQ6_K>{ub, lane}, a, er, xs, emin);
   else fold_q6_k(acc, SmemView<kQ6_K>{ub, lane}, a, er, xs, emin);
 }
 
+// The same from the unit's registers.
+__device__ __forceinline__ void fold_unit_wide(Acc128 &acc, const UnitRegs<kQ8_0> &w,
+                                               const int *a, const int *eabs, const long long *,
+                                               int) {
+  fold_q8_0(acc, RegView<kQ8_0>{w}, a, eabs);
+}
+__device__ __forceinline__ void fold_unit_wide(Acc128 &acc, const UnitRegs<kQ4_K> &w,
+                                               const int *a, const int *er, const long long *xs,
+                                               int emin) {
+  fold_q4_k_wide(acc, RegView<kQ4_K>{w}, a, er, xs, emin);
+}
+__device__ __forceinline__ void fold_unit_wide(Acc128 &acc, const UnitRegs<kQ6_K> &w,
+                                               const int *a, const int *er, const long long *xs,
+                                               int emin) {
+  fold_q6_k_wide(acc, RegView<kQ6_K>{w}, a, er, xs, emin);
+}
+
+
+// The wide folds' condition: the call-level bound, and no code of -128 (those activations take
+// the checked rows, as the fast path's do).
+template <uint32_t T>
+__device__ __forceinline__ bool wide_path(const ActDesc &desc, size_t n_in) {
+  return desc.status == APX_OK && bound_ok((long long)n_in, Fam<T>::top, desc.emax) &&
+         !(desc.pad[0] & 1u);
+}
 
 template <uint32_t T>
 __device__ __forceinline__ bool fast_path(const ActDesc &desc, size_t n_in) {
@@ -334,7 +476,8 @@ __device__ __forceinline__ Chunk load_chunk(const int8_t *codes, const uint8_t *
 // Stage chunk c (of the staged region) with its sums; every lane of the warp calls this
 // for the same c-round (the pair sum is a shuffle).
 template <uint32_t T>
-__device__ __forceinline__ void store_chunk(WarpAct<T> &w, Chunk s, int c, bool in, int emin) {
+__device__ __forceinline__ void store_chunk(WarpAct<T> &w, Chunk s, int c, bool in, int emin,
+                                            bool wide = false) {
   const bool zero = s.e == APX_EXP_ZERO;
   const uint4 v = zero ? make_uint4(0, 0, 0, 0) : s.v;
   const int er = zero ? 0 : (int)s.e - emin;
@@ -345,7 +488,7 @@ __device__ __forceinline__ void store_chunk(WarpAct<T> &w, Chunk s, int c, bool 
   const int s32 = s16 + __shfl_xor_sync(0xFFFFFFFFu, s16, 1);
   if (!in) return;
   reinterpret_cast<uint4 *>(w.codes)[c + c / (Fam<T>::span / 16)] = v;  // past the slot pads
-  if (T == kQ6_K) w.xs[c] = (long long)s16 << er;
+  if (T == kQ6_K) w.xs[c] = wide ? (long long)s16 : (long long)s16 << er;
   if ((c & 1) == 0) {
     w.e[c / 2] = T == kQ8_0 ? (zero ? -1 : (int)s.e) : er;
     if (T == kQ4_K) w.xs[c / 2] = s32;
