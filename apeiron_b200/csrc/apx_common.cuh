@@ -216,6 +216,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
   return false;
 }
 
+// A release/acquire fence at GPU scope: with a relaxed atomic after it (writer) or before it
+// (reader) it orders the writer's earlier stores before the reader's later loads, which is all
+// the hand-offs through arrival counters need.  Lighter than __threadfence (sequentially
+// consistent).
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+
 // ---- thread-block clusters ------------------------------------------------------------------
 // The CTAs of a cluster are co-scheduled, and each can store into the others' shared memory
 // (distributed shared memory).  barrier.cluster completes when every non-exited thread of the

@@ -423,13 +423,14 @@ __global__ void __launch_bounds__(stream_threads<T>(), T == kQ6_K ? 1 : 2)
         Acc128 *slot = g.partials + ((size_t)rt * g.kmax + k) * 32 + lane;
         slot->lo = acc.lo;
         slot->hi = acc.hi;
-        __threadfence();
-        __syncwarp();
+        __syncwarp();  // the lanes' stores, then lane 0's release fence and arrival
+        fence_acq_rel_gpu();
         unsigned ticket = 0;
         if (lane == 0) ticket = atomicAdd(g.counters + rt, 1u);
         ticket = __shfl_sync(0xFFFFFFFFu, ticket, 0);
         if (ticket == (unsigned)(count - 1)) {
-          __threadfence();
+          fence_acq_rel_gpu();  // lane 0's acquire, then the lanes' loads
+          __syncwarp();
           Acc128 s;
           acc_zero(s);
           for (int q = 0; q < count; q++) {

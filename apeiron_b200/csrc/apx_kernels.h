@@ -201,7 +201,7 @@ struct PlanCtl {  // zero between launches (the launch's last warp resets it)
   unsigned queue, exit, abort, pad;
   unsigned ready[kPlanMaxFfn];   // blocks of the FFN's h quantized
   unsigned flag[kPlanMaxFfn];    // the FFN's descriptor published
-  int stats[kPlanMaxFfn][4];     // 63 - emin (max), emax + 1 (max), status (max), nz (sum)
+  int stats[kPlanMaxFfn][4];     // [2]: the FFN's refusal (max); the rest spare
 };
 struct PlanSpec {
   struct Proj {

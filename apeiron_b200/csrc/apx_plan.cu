@@ -32,6 +32,7 @@
 // co-resident.  The last CTA out resets the counters and flags for the next launch.
 #include <algorithm>
 #include <climits>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <vector>
@@ -54,11 +55,20 @@ struct PlanProjD {
   long long *out_q32;
   float *out_f32;
   unsigned long long *status;
-  Acc128 *part;   // [n_rt][npieces][32] when npieces > 1
+  Acc128 *part;   // [n_rt][npieces][1 + paired][32] when npieces > 1
   unsigned *cnt;  // [n_rt] arrivals (self-resetting) when npieces > 1
   size_t n_out, n_in;
   int n_rt, U, L, plen, npieces, piece0;
   int act, ffn;  // activation read; FFN fed (-1 for none)
+  // An FFN's gate and up as one record (paired = 1): a piece streams gate unit u (pack) and
+  // up unit u (pack2) in turn over one staged activation chunk, and the warp that finishes a
+  // row tile holds both outputs of its 32-row block of h, so it runs the block's SwiGLU at
+  // once.  Virtual unit 2u + 0 / 1 is gate / up unit u.
+  int paired;
+  const uint8_t *pack2;
+  long long *out2_q32;
+  float *out2_f32;
+  unsigned long long *status2;
 };
 
 struct PlanActD {
@@ -136,14 +146,16 @@ __device__ __forceinline__ Piece decode_piece(const PlanArgs &g, const int *p0, 
   pc.j = lo;
   pc.rt = local / np;
   pc.q = local % np;
-  pc.u0 = pc.q * plen;
-  pc.u1 = min(P.U, pc.u0 + plen);
+  pc.u0 = (pc.q * plen) << P.paired;  // virtual units: 2u + 0 / 1 in a paired record
+  pc.u1 = min(P.U, pc.q * plen + plen) << P.paired;
   return pc;
 }
 
+// The weights of (virtual) unit u of row tile rt.
 template <uint32_t T>
 __device__ __forceinline__ const uint8_t *unit_ptr(const PlanProjD &P, int rt, int u) {
-  return P.pack + ((size_t)rt * P.U + u) * (size_t)Fam<T>::unit_bytes;
+  const uint8_t *pk = P.paired && (u & 1) ? P.pack2 : P.pack;
+  return pk + ((size_t)rt * P.U + (u >> P.paired)) * (size_t)Fam<T>::unit_bytes;
 }
 
 // SwiGLU + quant_act of block rt of FFN f (lane = row), its statistics, and — for the last
@@ -189,42 +201,56 @@ __device__ void ffn_block(const PlanArgs &g, int f, int rt, int lane) {
     if (row < F.n) F.peer_codes[p][row] = (int8_t)code;
     if (lane == 0) F.peer_exps[p][rt] = eb;
   }
-  __threadfence();  // every lane's stores before the block counts
-  __syncwarp();
+  // A refusal is rare: one atomic on the FFN's status word then.  The exponent statistics are
+  // not counted per block: the last block reads every block's exponent byte instead.
+  // Hand-offs through a counter: the lanes' stores, __syncwarp, then lane 0's release fence
+  // and relaxed atomic; the last arrival's lane 0 fences (acquire) before __syncwarp and the
+  // lanes' loads.
   int *st = g.ctl->stats[f];
+  if (lane == 0 && w_status != APX_OK) atomicMax(st + 2, w_status);
+  __syncwarp();
+  fence_acq_rel_gpu();  // every lane's stores (and the refusal) before the block counts
+  unsigned done = 0;
+  if (lane == 0) done = atomicAdd(&g.ctl->ready[f], 1u);
+  done = __shfl_sync(0xFFFFFFFFu, done, 0);
+  if (done != (unsigned)F.n_rt - 1) return;
+  // every block is in: every row tile of gate and up has finished (its outputs and its refusals
+  // were stored before its count), so their status words are final too
+  fence_acq_rel_gpu();
+  __syncwarp();
+  int emin = 1 << 30, emax = -1;
+  unsigned nz = 0;
+  for (int b = lane; b < F.n_rt; b += 32) {
+    const unsigned eb = __ldcg(F.exps + b);
+    if (eb != APX_EXP_ZERO) {
+      emin = min(emin, (int)eb);
+      emax = max(emax, (int)eb);
+      nz++;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    emin = min(emin, __shfl_xor_sync(0xFFFFFFFFu, emin, o));
+    emax = max(emax, __shfl_xor_sync(0xFFFFFFFFu, emax, o));
+    nz += __shfl_xor_sync(0xFFFFFFFFu, nz, o);
+  }
   if (lane == 0) {
-    // one address per statistic and FFN: an atomic only where it can change the value
-    if (w_status != APX_OK) atomicMax(st + 2, w_status);
-    if (e >= 0 && e != 99) {
-      if (__ldcg(st + 0) < 63 - e) atomicMax(st + 0, 63 - e);
-      if (__ldcg(st + 1) < e + 1) atomicMax(st + 1, e + 1);
-      atomicAdd(st + 3, 1);
-    }
-    __threadfence();
-    const unsigned done = atomicAdd(&g.ctl->ready[f], 1u);
-    if (done == (unsigned)F.n_rt - 1) {
-      // every block is in: every row tile of gate and up has finished (its outputs and its
-      // refusals were stored before its count), so their status words are final too
-      __threadfence();
-      const int nemin = atomicAdd(st + 0, 0), emax1 = atomicAdd(st + 1, 0);
-      int status = atomicAdd(st + 2, 0);
-      const unsigned nz = (unsigned)atomicAdd(st + 3, 0);
-      if (F.refused || __ldcg(F.gate_status) != ~0ull || __ldcg(F.up_status) != ~0ull)
-        status = max(status, (int)APX_ERR_QUANT_REFUSED);  // h is undefined where they refused
-      ActDesc d;
-      d.status = status;
-      d.emax = emax1 - 1;
-      d.emin = emax1 > 0 ? 63 - nemin : 0;
-      d.n_in = (int32_t)F.n;
-      d.nz = nz;
-      d.pad[0] = 0;  // quant_act codes are never -128
-      d.pad[1] = 0;
-      d.pad[2] = 0;
-      *F.desc = d;
-      for (int p = 0; p < F.n_peers; p++) *F.peer_desc[p] = d;
-      __threadfence();
-      atomicExch(&g.ctl->flag[f], 1u);
-    }
+    int status = __ldcg(st + 2);
+    if (F.refused || __ldcg(F.gate_status) != ~0ull || __ldcg(F.up_status) != ~0ull)
+      status = max(status, (int)APX_ERR_QUANT_REFUSED);  // h is undefined where they refused
+    ActDesc d;
+    d.status = status;
+    d.emax = emax;
+    d.emin = emax >= 0 ? emin : 0;
+    d.n_in = (int32_t)F.n;
+    d.nz = nz;
+    d.pad[0] = 0;  // quant_act codes are never -128
+    d.pad[1] = 0;
+    d.pad[2] = 0;
+    *F.desc = d;
+    for (int p = 0; p < F.n_peers; p++) *F.peer_desc[p] = d;
+    fence_acq_rel_gpu();
+    atomicExch(&g.ctl->flag[f], 1u);
   }
 }
 
@@ -420,10 +446,12 @@ __global__ void __launch_bounds__(PlanShape<T>::kThreads, PlanShape<T>::kCtas)
     const bool narrow = ok && fast_path<T>(desc, P.n_in);
     const bool wide = ok && !narrow && wide_path<T>(desc, P.n_in);
     const bool fast = narrow || wide;
-    if (fast && !act_pre) fetch(P, A, pc.u0, c0, c1);
+    const int sh = P.paired;  // units alternate gate, up: one activation chunk serves two
+    if (fast && !act_pre) fetch(P, A, pc.u0 >> sh, c0, c1);
     bool next_pre = false, copies_ok = true;
-    Acc128 acc;
+    Acc128 acc, acc2;  // acc2: the up projection's sums in a paired record
     acc_zero(acc);
+    acc_zero(acc2);
     for (int u = pc.u0; u < pc.u1; u++) {
       uint8_t *sl;
       const bool got = us.wait_front(sl);
@@ -433,26 +461,34 @@ __global__ void __launch_bounds__(PlanShape<T>::kThreads, PlanShape<T>::kCtas)
         us.top_up(g, pc, pn, xn >= 0, lane);
         continue;
       }
-      WarpAct<T> &wb = wa[u & 1];
-      store_chunk<T>(wb, c0, lane, lane < nch, desc.emin, wide);
-      if (nch > 32) store_chunk<T>(wb, c1, lane + 32, lane + 32 < nch, desc.emin, wide);
-      __syncwarp();
-      if (u + 1 < pc.u1) {
-        fetch(P, A, u + 1, c0, c1);
-      } else if (xn >= 0) {  // the next piece's first chunk, when its activation is ready now
-        const PlanProjD &Q = g.proj[pn.j];
-        const PlanActD &B = g.act[Q.act];
-        int r = 1;
-        if (B.ffn >= 0 && lane == 0) r = ld_acquire(&g.ctl->flag[B.ffn]) ? 1 : 0;
-        r = __shfl_sync(0xFFFFFFFFu, r, 0);
+      const int ru = u >> sh;               // the real unit
+      const bool second = sh && (u & 1);     // up's unit u, over the chunk gate's staged
+      WarpAct<T> &wb = wa[ru & 1];
+      if (!second) {
+        store_chunk<T>(wb, c0, lane, lane < nch, desc.emin, wide);
+        if (nch > 32) store_chunk<T>(wb, c1, lane + 32, lane + 32 < nch, desc.emin, wide);
         __syncwarp();
-        if (r) {
-          fetch(Q, B, pn.u0, c0, c1);
-          next_pre = true;
+        if (ru + 1 < (pc.u1 >> sh)) {
+          fetch(P, A, ru + 1, c0, c1);
+        } else if (xn >= 0) {  // the next piece's first chunk, when its activation is ready now
+          const PlanProjD &Q = g.proj[pn.j];
+          const PlanActD &B = g.act[Q.act];
+          int r = 1;
+          if (B.ffn >= 0 && lane == 0) r = ld_acquire(&g.ctl->flag[B.ffn]) ? 1 : 0;
+          r = __shfl_sync(0xFFFFFFFFu, r, 0);
+          __syncwarp();
+          if (r) {
+            fetch(Q, B, pn.u0 >> Q.paired, c0, c1);
+            next_pre = true;
+          }
         }
       }
-      fold_unit_smem<T>(acc, sl, lane, wb.codes + slot * slot_ints<T>(),
+      Acc128 t;
+      acc_zero(t);
+      fold_unit_smem<T>(t, sl, lane, wb.codes + slot * slot_ints<T>(),
                         wb.e + slot * (F::span / 32), wb.xs + slot * F::nxs, desc.emin, wide);
+      if (second) acc_add(acc2, t);
+      else acc_add(acc, t);
       us.release_front();  // the fold has read the slot: the next copy may refill it
       us.top_up(g, pc, pn, xn >= 0, lane);
     }
@@ -462,65 +498,98 @@ __global__ void __launch_bounds__(PlanShape<T>::kThreads, PlanShape<T>::kCtas)
       if (lane == 0) {
         atomicExch(&g.ctl->abort, 1u);
         atomicMin(P.status, pack_status(0, APX_ERR_DEVICE_TIMEOUT, 0));
+        if (sh) atomicMin(P.status2, pack_status(0, APX_ERR_DEVICE_TIMEOUT, 0));
       }
       done = lead;
     } else if (!ready) {
-      if (lead && lane == 0) atomicMin(P.status, pack_status(0, APX_ERR_DEVICE_TIMEOUT, 0));
+      if (lead && lane == 0) {
+        atomicMin(P.status, pack_status(0, APX_ERR_DEVICE_TIMEOUT, 0));
+        if (sh) atomicMin(P.status2, pack_status(0, APX_ERR_DEVICE_TIMEOUT, 0));
+      }
       done = lead;
     } else if (desc.status != APX_OK) {  // the activation is refused (chart/mod.rs:1904-1907)
-      if (lead && pc.rt == 0 && lane == 0)
+      if (lead && pc.rt == 0 && lane == 0) {
         atomicMin(P.status, pack_status(0, (unsigned)desc.status, 0));
+        if (sh) atomicMin(P.status2, pack_status(0, (unsigned)desc.status, 0));
+      }
       done = lead;
     } else if (!fast) {
-      if (lead && slot == 0)
+      if (lead && slot == 0) {
         checked_row<T>(PackGeo{P.pack, P.U, L}, (size_t)pc.rt * H + lane / L, P.n_out, P.n_in,
                        A.codes, A.exps, P.out_q32, P.out_f32, P.status);
+        if (sh)
+          checked_row<T>(PackGeo{P.pack2, P.U, L}, (size_t)pc.rt * H + lane / L, P.n_out,
+                         P.n_in, A.codes, A.exps, P.out2_q32, P.out2_f32, P.status2);
+      }
       done = lead;
     } else {
       for (int o = 1; o < L; o <<= 1) {  // the L lanes of a row combine
         const unsigned long long lo = __shfl_xor_sync(0xFFFFFFFFu, acc.lo, o);
         const unsigned long long hi = __shfl_xor_sync(0xFFFFFFFFu, acc.hi, o);
         acc_add(acc, lo, hi);
+        if (sh) {
+          const unsigned long long lo2 = __shfl_xor_sync(0xFFFFFFFFu, acc2.lo, o);
+          const unsigned long long hi2 = __shfl_xor_sync(0xFFFFFFFFu, acc2.hi, o);
+          acc_add(acc2, lo2, hi2);
+        }
       }
       bool fin = P.npieces == 1;
       if (!fin) {
-        Acc128 *dst = P.part + ((size_t)pc.rt * P.npieces + pc.q) * 32 + lane;
+        Acc128 *dst = P.part + (((size_t)pc.rt * P.npieces + pc.q) << sh) * 32 + lane;
         dst->lo = acc.lo;
         dst->hi = acc.hi;
-        __threadfence();
+        if (sh) {
+          dst[32].lo = acc2.lo;
+          dst[32].hi = acc2.hi;
+        }
         __syncwarp();
+        fence_acq_rel_gpu();
         unsigned ticket = 0;
         if (lane == 0) ticket = atomicAdd(P.cnt + pc.rt, 1u);
         ticket = __shfl_sync(0xFFFFFFFFu, ticket, 0);
         fin = ticket == (unsigned)P.npieces - 1;
         if (fin) {
-          __threadfence();
+          fence_acq_rel_gpu();
+          __syncwarp();
           acc_zero(acc);
+          acc_zero(acc2);
           for (int qq = 0; qq < P.npieces; qq++) {
-            const Acc128 *src = P.part + ((size_t)pc.rt * P.npieces + qq) * 32 + lane;
+            const Acc128 *src = P.part + (((size_t)pc.rt * P.npieces + qq) << sh) * 32 + lane;
             acc_add(acc, __ldcg(&src->lo), __ldcg(&src->hi));
+            if (sh) acc_add(acc2, __ldcg(&src[32].lo), __ldcg(&src[32].hi));
           }
           if (lane == 0) P.cnt[pc.rt] = 0u;  // ready for the next launch
         }
       }
-      if (fin && slot == 0)
+      if (fin && slot == 0) {
         finish_row(acc, (size_t)pc.rt * H + lane / L, P.n_out, P.out_q32, P.out_f32, P.status,
                    PeerRows{});
+        if (sh)
+          finish_row(acc2, (size_t)pc.rt * H + lane / L, P.n_out, P.out2_q32, P.out2_f32,
+                     P.status2, PeerRows{});
+      }
       done = fin;
     }
     // -- the FFN hand-off: a 32-row block of h covers L row tiles of gate and of up; the last
     // of them to finish runs the block's SwiGLU --
-    if (done && P.ffn >= 0) {
-      const int blk = pc.rt / L;
-      const int need = 2 * (min(P.n_rt, (blk + 1) * L) - blk * L);
-      __threadfence();
+    if (done && P.ffn >= 0 && sh && L == 1) {
+      // this warp finished the block's gate and up rows itself (lane = row): the SwiGLU reads
+      // back its own lanes' stores, so no counter and no fence stand between
       __syncwarp();
+      ffn_block(g, P.ffn, pc.rt, lane);
+    } else if (done && P.ffn >= 0) {
+      // the block's row tiles count in: each of gate and of up, or each paired one
+      const int blk = pc.rt / L;
+      const int need = (2 >> sh) * (min(P.n_rt, (blk + 1) * L) - blk * L);
+      __syncwarp();
+      fence_acq_rel_gpu();
       unsigned old = 0;
       if (lane == 0) old = atomicAdd(g.ffn[P.ffn].pair + blk, 1u);
       old = __shfl_sync(0xFFFFFFFFu, old, 0);
       if (old == (unsigned)need - 1) {
         if (lane == 0) g.ffn[P.ffn].pair[blk] = 0u;  // ready for the next launch
-        __threadfence();
+        fence_acq_rel_gpu();
+        __syncwarp();
         ffn_block(g, P.ffn, blk, lane);
       }
     }
@@ -681,6 +750,20 @@ int plan_build(const PlanSpec &s, int sm_count, PlanHost **out) {
   }
   const long long V = (long long)grid * (block / 32);
 
+  // Every FFN's gate and up run as one paired record (the up's own record takes no pieces):
+  // their units alternate over one staged activation, and the warp finishing a row tile runs
+  // its SwiGLU block directly.  APX_PLAN_PAIR=0 keeps them apart (hand-off by counters).
+  static const bool pair_on = [] {
+    const char *v = std::getenv("APX_PLAN_PAIR");
+    return !(v && v[0] == '0');
+  }();
+  std::vector<int> partner(n_proj, -1), dropped(n_proj, 0);
+  if (pair_on)
+    for (int f = 0; f < n_ffn; f++) {
+      partner[gate[f]] = up[f];
+      dropped[up[f]] = 1;
+    }
+
   // Pieces: at most kPlanPiece units, fewer when the plan is short, so that every warp of the
   // grid gets about two.
   std::vector<int> n_rt(n_proj), npieces(n_proj), plen(n_proj);
@@ -695,8 +778,14 @@ int plan_build(const PlanSpec &s, int sm_count, PlanHost **out) {
   long long total = 0;
   for (int i = 0; i < n_proj; i++) {
     const int U = s.projs[i].plan.units;
-    npieces[i] = (U + plen_t - 1) / plen_t;
-    plen[i] = (U + npieces[i] - 1) / npieces[i];
+    if (dropped[i]) {  // streamed by its gate's record
+      npieces[i] = 0;
+      plen[i] = 1;
+      continue;
+    }
+    const int Uv = partner[i] >= 0 ? 2 * U : U;  // units a row tile streams
+    npieces[i] = (Uv + plen_t - 1) / plen_t;
+    plen[i] = (U + npieces[i] - 1) / npieces[i];  // in real units: a pair stays in one piece
     npieces[i] = (U + plen[i] - 1) / plen[i];
     total += (long long)n_rt[i] * npieces[i];
   }
@@ -745,10 +834,18 @@ int plan_build(const PlanSpec &s, int sm_count, PlanHost **out) {
     d.piece0 = (int)first;
     d.act = p.act;
     d.ffn = p.ffn;
+    if (partner[i] >= 0) {
+      const PlanSpec::Proj &u = s.projs[partner[i]];
+      d.paired = 1;
+      d.pack2 = u.pack;
+      d.out2_q32 = u.out_q32;
+      d.out2_f32 = u.out_f32;
+      d.status2 = u.status;
+    }
     first += (long long)n_rt[i] * npieces[i];
     if (d.npieces > 1) {
       part_off[q] = scratch;
-      scratch += al256((size_t)d.n_rt * d.npieces * 32 * sizeof(Acc128));
+      scratch += al256((size_t)d.n_rt * d.npieces * (1 + d.paired) * 32 * sizeof(Acc128));
       cnt_off[q] = scratch;
       scratch += al256((size_t)d.n_rt * 4);
     }
