@@ -10,25 +10,29 @@
 //
 // Work.  Every projection's row tiles are cut into pieces of at most kPlanPiece units of the
 // tensor's repacked layout (fewer for a short plan); the pieces of all projections form one
-// queue, and warp v of the V in the grid takes pieces v, v + V, v + 2V, ... in order (no shared
-// counter: a counter on one address serialises every warp's take).  A warp streams its pieces'
-// units through a ring in shared memory (1D bulk copies, two units in flight while one folds; the
-// first piece's copies start before the wait for the previous kernel) and folds each exactly as
-// the one-wave GEMV kernel does; a row tile of one piece finishes in the warp, a row tile of
-// several through partial sums in the plan's scratch and a self-resetting arrival counter (the
-// last to arrive finishes it).
+// queue.  Warp v of the V in the grid starts on piece v; every later piece is taken from a shared
+// counter, one piece ahead (while the warp folds its current piece, the next one's weights
+// stream in behind it), so warps that draw short pieces take more of them.  A warp streams its
+// pieces' units through a ring in shared memory (1D bulk copies, one unit in flight while one
+// folds; the first piece's copies start before the wait for the previous kernel) and folds each
+// exactly as the one-wave GEMV kernel does; a row tile of one piece finishes in the warp, a row
+// tile of several through partial sums in the plan's scratch and a self-resetting arrival counter
+// (the last to arrive finishes it).
 //
-// Hand-off.  The finish of a gate or up row tile counts on the counter of its 32-row block of h
-// (one quant_act block: L row tiles of 32/L rows in each projection); the last of the block's
-// row tiles runs SwiGLU under the carrier and quant_act for the block and adds the block's
-// exponent statistics to the FFN's; the last block publishes the descriptor and raises the
-// FFN's flag.  A warp that takes a piece reading that activation waits
-// on the flag first, with a bound (about one second) after which the projection refuses with
-// APX_ERR_DEVICE_TIMEOUT.  The host queues projections by dependency level, an FFN's producers
-// ahead of the level's other work and its readers in the next level, so the flag is usually up
-// when a warp gets there.  A warp waits only at the start of a piece with nothing unfinished, and every
-// piece a wait depends on sits earlier in the queue: by induction on queue position the earliest
-// waiting piece's producers belong to warps that reach them, since the grid is sized to be
+// Hand-off.  An FFN's gate and up run as one paired record: a piece alternates gate and up units
+// over one staged activation chunk, so the warp that finishes a row tile holds both projections'
+// rows.  When a row tile is a whole 32-row block of h (one quant_act block, L = 1) that warp runs
+// the block's SwiGLU under the carrier and quant_act at once; otherwise the block's row tiles
+// count in on its counter and the last runs it.  The last block of the FFN computes the
+// descriptor from the blocks' exponent bytes and raises the FFN's flag.  A warp whose piece reads
+// that activation waits on the flag before it takes its next piece, with a bound (about one
+// second) after which the projection refuses with APX_ERR_DEVICE_TIMEOUT.  The host queues
+// projections by dependency level, an FFN's producers ahead of the level's other work and its
+// readers in the next level, so the flag is usually up when a warp gets there.  Every wait ends:
+// pieces are taken in queue order, a warp holds at most its current piece and the one after it,
+// and it waits only for its current piece, before taking the next; every piece a wait depends
+// on sits earlier in the queue, so by induction on queue position each piece's holder reaches
+// it (its current piece is earlier and completes) and its producers complete, the grid being
 // co-resident.  The last CTA out resets the counters and flags for the next launch.
 #include <algorithm>
 #include <climits>
@@ -435,8 +439,12 @@ __global__ void __launch_bounds__(PlanShape<T>::kThreads, PlanShape<T>::kCtas)
     } else {
       desc = *A.desc;
     }
-    // the next piece of this warp's sequence: its weights follow this piece's through the ring
-    const int xn = x + g.V < g.total ? x + g.V : -1;
+    // the next piece, taken now (after this piece's wait): its weights follow this piece's
+    // through the ring
+    unsigned nxq = 0;
+    if (lane == 0) nxq = (unsigned)g.V + atomicAdd(&g.ctl->queue, 1u);
+    nxq = __shfl_sync(0xFFFFFFFFu, nxq, 0);
+    const int xn = nxq < (unsigned)g.total ? (int)nxq : -1;
     if (xn >= 0) pn = decode_piece(g, s_p0, xn);
     us.top_up(g, pc, pn, xn >= 0, lane);
 
