@@ -57,6 +57,7 @@
 #include "apx_pack.cuh"
 #include "apx_quant.cuh"
 #include "apx_tc.cuh"
+#include "apx_unit.cuh"
 
 namespace apx {
 
@@ -75,9 +76,11 @@ constexpr size_t kLMaxK = 65536;
 constexpr int kLTileW = kLM * kLK;  // 8 KB: one weight digit tile
 constexpr int kLNMin = 64, kLNMax = 128;  // token tile widths (workspace bounds)
 constexpr int kLMinIters = 4;       // stages per stream-K CTA at least
-// A column's route: refused, the GEMM with two activation digits, the checked rows, or the GEMM
-// with three (a tile holding such a column runs a second pass over K for the third digit).
+// A column's route: refused, the GEMM with two activation digits, the checked rows, the GEMM
+// with three (a tile holding such a column runs a second pass over K for the third digit), or
+// the wide fold (a spread past three digits under the call bound: limb_wide_kernel).
 constexpr unsigned kRouteNone = 0, kRouteGemm = 1, kRouteChecked = 2, kRouteGemm3 = 3;
+constexpr unsigned kRouteWide = 4;
 constexpr long long kPartSlot = (long long)kLM * kLNMax;  // i64 per partial tile
 
 // The kernel's shape for D weight digits and N-token tiles.
@@ -416,7 +419,7 @@ __device__ __forceinline__ void lprep_common_start(const LPrepArgs &a) {
 __device__ __forceinline__ unsigned lroute(const LPrepArgs &a, int emin, int emax) {
   if (!bound_ok((long long)a.n_in, a.top, emax)) return kRouteChecked;
   if (emax < 0 || emax - emin <= kLMaxShift) return kRouteGemm;
-  return emax - emin <= a.smax3 ? kRouteGemm3 : kRouteChecked;
+  return emax - emin <= a.smax3 ? kRouteGemm3 : kRouteWide;
 }
 __device__ __forceinline__ bool on_gemm(unsigned route) {
   return route == kRouteGemm || route == kRouteGemm3;
@@ -704,6 +707,150 @@ __device__ __forceinline__ void lchecked_columns(const LArgs &g) {
                        g.status + (size_t)cc * 2);
     }
     __syncthreads();
+  }
+}
+
+// ---- the wide route -----------------------------------------------------------------------------
+// Columns whose activation spread is past the three-digit route while the call bound holds
+// (typically an FFN's hidden activations, whose exp tails spread far) fold exactly on the integer
+// pipes with the GEMV's wide fold (apx_unit.cuh), from the tensor's GEMV layout: a warp takes one
+// row tile and up to kWideCols such columns, copies each unit into its shared memory once and
+// folds it against every column's staged activation chunk.  Work items (row tile, column group)
+// are ordered row tile first, so the warps in flight share a few row tiles and the weights come
+// from HBM about once.  Every CTA lists the wide columns of a chunk of the call in column order
+// (warp ballots), so all CTAs agree on the groups.
+constexpr int kWideCols = 4;      // columns folded against one staged unit
+constexpr int kWideWarps = 8;     // warps per CTA, two CTAs per SM
+constexpr int kWideChunk = 2048;  // columns listed at a time
+
+struct WideArgs {
+  PackGeo geo;            // the tensor's GEMV layout
+  size_t n_out, n_in;
+  int n_cols, n_rt;       // n_rt: row tiles of 32 / L rows
+  const int8_t *codes;    // column c at codes + c·ld (f32 path: the prep's copies)
+  const uint8_t *exps;    // and exps + c·ldb
+  size_t ld, ldb;
+  const uint32_t *route;  // the prep's routes and emin
+  const int32_t *emin;
+  long long *out_q32;     // [n_cols][n_out] or null
+  float *out_f32;
+  unsigned long long *status;  // column c at status[c·2]
+};
+
+template <uint32_t T>
+__host__ __device__ constexpr size_t wide_smem_bytes() {
+  return (size_t)kWideWarps * (Fam<T>::unit_bytes + kWideCols * sizeof(WarpAct<T>)) +
+         kWideChunk * 4 + 64;
+}
+
+template <uint32_t T>
+__global__ void __launch_bounds__(32 * kWideWarps, 2) limb_wide_kernel(WideArgs g) {
+  using F = Fam<T>;
+  extern __shared__ __align__(16) uint8_t wsm[];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  uint8_t *unit_s = wsm + (size_t)warp * F::unit_bytes;
+  WarpAct<T> *wa = reinterpret_cast<WarpAct<T> *>(wsm + (size_t)kWideWarps * F::unit_bytes) +
+                   (size_t)warp * kWideCols;
+  int *s_cols = reinterpret_cast<int *>(wsm + (size_t)kWideWarps *
+                                                  (F::unit_bytes + kWideCols * sizeof(WarpAct<T>)));
+  int *s_n = s_cols + kWideChunk;  // [kWideWarps + 1]
+  pdl_launch_dependents();
+  pdl_wait();  // routes, codes and the GEMM's outputs of this call are final
+  const int L = g.geo.L, H = 32 / L, slot = lane % L, U = g.geo.units;
+  const int nch = L * F::span / 16;
+  for (int base = 0; base < g.n_cols; base += kWideChunk) {
+    const int span = min(kWideChunk, g.n_cols - base);
+    // the chunk's wide columns in column order: each warp counts a stripe, then places it
+    const int per = (span + kWideWarps - 1) / kWideWarps;
+    const int c0 = base + warp * per, c1 = min(base + span, c0 + per);
+    int cnt = 0;
+    for (int c = c0; c < c1; c += 32) {
+      const bool w = c + lane < c1 && __ldcg(g.route + c + lane) == kRouteWide;
+      cnt += __popc(__ballot_sync(0xFFFFFFFFu, w));
+    }
+    if (lane == 0) s_n[warp] = cnt;
+    __syncthreads();
+    int off = 0, n_w = 0;
+    for (int k = 0; k < kWideWarps; k++) {
+      if (k < warp) off += s_n[k];
+      n_w += s_n[k];
+    }
+    for (int c = c0; c < c1; c += 32) {
+      const bool w = c + lane < c1 && __ldcg(g.route + c + lane) == kRouteWide;
+      const unsigned m = __ballot_sync(0xFFFFFFFFu, w);
+      if (w) s_cols[off + __popc(m & ((1u << lane) - 1))] = c + lane;
+      off += __popc(m);
+    }
+    __syncthreads();
+    const int n_grp = (n_w + kWideCols - 1) / kWideCols;
+    const long long items = (long long)g.n_rt * n_grp;
+    for (long long it = (long long)blockIdx.x * kWideWarps + warp; it < items;
+         it += (long long)gridDim.x * kWideWarps) {
+      const int rt = (int)(it / n_grp), grp = (int)(it % n_grp);
+      const int nc = min(kWideCols, n_w - grp * kWideCols);
+      int col[kWideCols], em[kWideCols];
+#pragma unroll
+      for (int j = 0; j < kWideCols; j++) {
+        col[j] = j < nc ? s_cols[grp * kWideCols + j] : 0;
+        em[j] = j < nc ? __ldcg(g.emin + col[j]) : 0;
+      }
+      Acc128 acc[kWideCols];
+#pragma unroll
+      for (int j = 0; j < kWideCols; j++) acc_zero(acc[j]);
+      const uint8_t *src = g.geo.pack + (size_t)rt * U * F::unit_bytes;
+      for (int u = 0; u < U; u++, src += F::unit_bytes) {
+        // the unit into shared memory and every column's chunks, all loads in flight together
+        __syncwarp();  // the previous unit's folds are done with unit_s and the staging
+        constexpr int kV = F::unit_bytes / 16;
+        for (int i = lane; i < kV; i += 32)  // 16-byte asynchronous copies, no registers held
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                           smem_addr(unit_s + (size_t)i * 16)),
+                       "l"(src + (size_t)i * 16)
+                       : "memory");
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        Chunk ch[kWideCols][2];
+#pragma unroll
+        for (int j = 0; j < kWideCols; j++) {
+          ch[j][0] = ch[j][1] = Chunk{make_uint4(0, 0, 0, 0), APX_EXP_ZERO};
+          if (j < nc) {
+            const int8_t *cc = g.codes + (size_t)col[j] * g.ld;
+            const uint8_t *ce = g.exps + (size_t)col[j] * g.ldb;
+            if (lane < nch) ch[j][0] = load_chunk_cg(cc, ce, g.n_in, chunk_first<T>(u, L, lane));
+            if (lane + 32 < nch)
+              ch[j][1] = load_chunk_cg(cc, ce, g.n_in, chunk_first<T>(u, L, lane + 32));
+          }
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");
+#pragma unroll
+        for (int j = 0; j < kWideCols; j++) {
+          store_chunk<T>(wa[j], ch[j][0], lane, lane < nch, em[j], true);
+          if (nch > 32) store_chunk<T>(wa[j], ch[j][1], lane + 32, lane + 32 < nch, em[j], true);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < kWideCols; j++)
+          if (j < nc)
+            fold_unit_smem<T>(acc[j], unit_s, lane, wa[j].codes + slot * slot_ints<T>(),
+                              wa[j].e + slot * (F::span / 32), wa[j].xs + slot * F::nxs, em[j],
+                              true);
+      }
+#pragma unroll
+      for (int j = 0; j < kWideCols; j++) {
+        for (int o = 1; o < L; o <<= 1) {  // the L lanes of a row combine
+          const unsigned long long lo = __shfl_xor_sync(0xFFFFFFFFu, acc[j].lo, o);
+          const unsigned long long hi = __shfl_xor_sync(0xFFFFFFFFu, acc[j].hi, o);
+          acc_add(acc[j], lo, hi);
+        }
+        if (j < nc && slot == 0) {
+          const size_t c = (size_t)col[j];
+          finish_row(acc[j], (size_t)rt * H + lane / L, g.n_out,
+                     g.out_q32 ? g.out_q32 + c * g.n_out : nullptr,
+                     g.out_f32 ? g.out_f32 + c * g.n_out : nullptr, g.status + c * 2,
+                     PeerRows{});
+        }
+      }
+    }
+    __syncthreads();  // s_cols and s_n are rewritten for the next chunk
   }
 }
 
@@ -1192,6 +1339,55 @@ cudaError_t launch_main_any(uint32_t type, const GemvPlan &pl, const uint8_t *pa
   }
 }
 
+// The wide route's launch after a GEMM of the call: a programmatic dependent of it (its CTAs
+// wait for the GEMM, and through it the prep, before reading a route), two CTAs per SM.
+template <uint32_t T>
+cudaError_t launch_wide_t(const WideArgs &a, int sm_count, cudaStream_t stream) {
+  const size_t smem = wide_smem_bytes<T>();
+  cudaError_t e = cudaFuncSetAttribute(limb_wide_kernel<T>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * std::max(sm_count, 1)));
+  cfg.blockDim = dim3(32 * kWideWarps);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_allowed() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, limb_wide_kernel<T>, a);
+}
+
+cudaError_t launch_wide(uint32_t type, const GemvPlan &pl, const uint8_t *pack, size_t n_out,
+                        size_t n_in, size_t n_cols, const int8_t *codes, size_t ld,
+                        const uint8_t *exps, size_t ldb, const LWork &w, long long *out_q32,
+                        float *out_f32, unsigned long long *status, int sm_count,
+                        cudaStream_t stream) {
+  WideArgs a;
+  a.geo = PackGeo{pack, pl.units, pl.L};
+  a.n_out = n_out;
+  a.n_in = n_in;
+  a.n_cols = (int)n_cols;
+  a.n_rt = (int)((n_out + 32 / pl.L - 1) / (32 / pl.L));
+  a.codes = codes;
+  a.exps = exps;
+  a.ld = ld;
+  a.ldb = ldb;
+  a.route = w.route;
+  a.emin = w.emin;
+  a.out_q32 = out_q32;
+  a.out_f32 = out_f32;
+  a.status = status;
+  switch (type) {
+    case kQ8_0: return launch_wide_t<kQ8_0>(a, sm_count, stream);
+    case kQ4_K: return launch_wide_t<kQ4_K>(a, sm_count, stream);
+    case kQ6_K: return launch_wide_t<kQ6_K>(a, sm_count, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 // The largest activation spread s of the three-digit route on a tensor whose weights have
 // wbits bits: every sum T = Σ W'·X' and each of its two passes' parts stay below 2^61 when
 // kp·2^(wbits + 8 + s) <= 2^61 (|W'| < 2^wbits, |X'| <= 2^(7 + s), and the parts' digits add at
@@ -1350,9 +1546,13 @@ cudaError_t launch_limb_gemm(const GemvPlan &pl, uint32_t type, const uint8_t *p
   (void)carve;
   limb_prep_kernel<<<(unsigned)pa.np, 256, 0, stream>>>(pa);
   cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  return launch_main_any(type, pl, pack, lay, n_out, n_in, n_cols, codes, ld, exps, ldb, w,
-                         out_q32, out_f32, status, sm_count, stream);
+  if (e == cudaSuccess)
+    e = launch_main_any(type, pl, pack, lay, n_out, n_in, n_cols, codes, ld, exps, ldb, w,
+                        out_q32, out_f32, status, sm_count, stream);
+  if (e == cudaSuccess)
+    e = launch_wide(type, pl, pack, n_out, n_in, n_cols, codes, ld, exps, ldb, w, out_q32,
+                    out_f32, status, sm_count, stream);
+  return e;
 }
 
 bool limb_f32_ok(size_t n_in, const float *x, size_t ldx) {
@@ -1376,9 +1576,13 @@ cudaError_t launch_limb_gemm_f32(const GemvPlan &pl, uint32_t type, const uint8_
   (void)carve;
   limb_quant_prep_kernel<<<(unsigned)pa.np, 256, smem, stream>>>(pa);
   cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  return launch_main_any(type, pl, pack, lay, n_out, n_in, n_cols, w.qcodes, lay.kp, w.qexps,
-                         lay.kp / 32, w, out_q32, out_f32, status, sm_count, stream);
+  if (e == cudaSuccess)
+    e = launch_main_any(type, pl, pack, lay, n_out, n_in, n_cols, w.qcodes, lay.kp, w.qexps,
+                        lay.kp / 32, w, out_q32, out_f32, status, sm_count, stream);
+  if (e == cudaSuccess)
+    e = launch_wide(type, pl, pack, n_out, n_in, n_cols, w.qcodes, lay.kp, w.qexps, lay.kp / 32,
+                    w, out_q32, out_f32, status, sm_count, stream);
+  return e;
 }
 
 cudaError_t launch_limb_gemm_f32_group(uint32_t type, const LimbMember *m, int count,
@@ -1416,6 +1620,10 @@ cudaError_t launch_limb_gemm_f32_group(uint32_t type, const LimbMember *m, int c
     e = launch_main_any(type, *m[i].pl, m[i].pack, *m[i].lay, m[i].n_out, n_in, n_cols, w.qcodes,
                         m[i].lay->kp, w.qexps, m[i].lay->kp / 32, w, m[i].out_q32,
                         m[i].out_f32, m[i].status, sm_count, stream);
+  for (int i = 0; e == cudaSuccess && i < count; i++)
+    e = launch_wide(type, *m[i].pl, m[i].pack, m[i].n_out, n_in, n_cols, w.qcodes,
+                    m[i].lay->kp, w.qexps, m[i].lay->kp / 32, w, m[i].out_q32, m[i].out_f32,
+                    m[i].status, sm_count, stream);
   return e;
 }
 

@@ -473,6 +473,25 @@ __device__ __forceinline__ Chunk load_chunk(const int8_t *codes, const uint8_t *
   return s;
 }
 
+// The same for an activation written by this launch or the one before it: L2-coherent loads
+// (the read-only path could hold a line from before the writer's store).
+__device__ __forceinline__ Chunk load_chunk_cg(const int8_t *codes, const uint8_t *exps,
+                                               size_t n_in, size_t j) {
+  Chunk s{make_uint4(0, 0, 0, 0), APX_EXP_ZERO};
+  if (j < n_in) {
+    s.e = __ldcg(exps + j / 32);
+    if (j + 16 <= n_in && ((reinterpret_cast<uintptr_t>(codes + j) & 15) == 0)) {
+      s.v = __ldcg(reinterpret_cast<const uint4 *>(codes + j));
+    } else {
+      unsigned t[4] = {0, 0, 0, 0};
+      for (int i = 0; i < 16; i++)
+        if (j + i < n_in) t[i / 4] |= ((unsigned)(uint8_t)__ldcg(codes + j + i)) << (8 * (i % 4));
+      s.v = make_uint4(t[0], t[1], t[2], t[3]);
+    }
+  }
+  return s;
+}
+
 // Stage chunk c (of the staged region) with its sums; every lane of the warp calls this
 // for the same c-round (the pair sum is a shuffle).
 template <uint32_t T>

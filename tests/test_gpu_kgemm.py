@@ -195,8 +195,11 @@ def test_f32_prefill_equals_single_column(be, t, n_out, n_in, k):
     (Q4_K, 512, 2816, 8, 34, 4), (Q4_K, 256, 28672, 8, 34, 4), (Q8_0, 384, 1024, 6, 40, 4),
     (Q6_K, 256, 1024, 5, 30, 4),
     (Q4_K, 384, 2816, 100, 30, 9),    # spreads 8..9: the third activation digit's second pass
-    (Q8_0, 300, 1024, 70, 30, 14),    # up to 14
+    (Q8_0, 300, 1024, 70, 30, 14),    # up to 14 (past this tensor's three-digit limit: wide)
     (Q6_K, 256, 1024, 9, 20, 12),
+    # spreads past every three-digit limit under the call bound: the wide route
+    (Q4_K, 384, 2816, 40, 10, 30), (Q4_K, 256, 28672, 8, 10, 30), (Q4_K, 300, 896, 16, 10, 30),
+    (Q6_K, 256, 1024, 12, 10, 24), (Q8_0, 300, 1024, 20, 8, 40),
 ])
 def test_device_descriptors_and_large_exponents(be, t, n_out, n_in, k, e0, spread):
     """apx_matmat_async with descriptors computed on the device (apx_act_describe_cols_async), on

@@ -164,3 +164,38 @@ def test_wide_spread_plan(be, t):
                 assert np.array_equal(o[0].cpu().numpy(), want)
     finally:
         lib.apx_plan_destroy(plan)
+
+
+@pytest.mark.parametrize("t", [Q4_K, Q6_K])
+def test_wide_spread_prefill_f32(be, t):
+    """The f32 prefill entry (quantize + digit-plane GEMM): tokens whose blocks spread past the
+    three-digit route take the wide route, narrow tokens the tensor cores, in one call; every
+    column's Q32.32 outputs equal the oracle's, and a second call on the same tensor too."""
+    import torch
+    lib, ctx = be.lib, be.ctx
+    dev = torch.device("cuda:0")
+    st = torch.cuda.current_stream().cuda_stream
+    n_out, n_in, k = 700, 2048, 40
+    raw = synth.payload(t, n_out, n_in, 321)
+    ten = be.upload(t, raw, n_out, n_in)
+    xs = np.stack([wide_x(n_in, 500 + c, "blocks" if c % 3 == 0 else "super")
+                   if c % 2 == 0 else synth.activation_f32(n_in, 500 + c) for c in range(k)])
+    dx = torch.from_numpy(np.ascontiguousarray(xs, dtype=np.float32)).to(dev)
+    y = torch.zeros(k * n_out, dtype=torch.int64, device=dev)
+    ys = torch.full((2 * k,), -1, dtype=torch.int64, device=dev)
+    want = []
+    for c in range(k):
+        q = quant(xs[c])
+        if c % 2 == 0:
+            assert spread(q) > 15
+        want.append(O.matvec_q8act(t, raw, n_out, n_in, q.codes, q.scales))
+    for _ in range(2):
+        y.zero_()
+        ys.fill_(-1)
+        assert lib.apx_matmat_f32_async(ctx, ten.handle, n_out, n_in, k, dx.data_ptr(), n_in,
+                                        y.data_ptr(), None, ys.data_ptr(), st) == 0
+        torch.cuda.synchronize()
+        assert bool((ys[0::2] == -1).all().item())
+        got = y.cpu().numpy().reshape(k, n_out)
+        for c in range(k):
+            assert np.array_equal(got[c], want[c]), c
