@@ -216,6 +216,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
   return false;
 }
 
+// 16-byte asynchronous copy from global into shared memory (no register staging); complete after
+// cp_async_wait_all in the issuing thread (and __syncwarp for the warp's other lanes).
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
 // A release/acquire fence at GPU scope: with a relaxed atomic after it (writer) or before it
 // (reader) it orders the writer's earlier stores before the reader's later loads, which is all
 // the hand-offs through arrival counters need.  Lighter than __threadfence (sequentially

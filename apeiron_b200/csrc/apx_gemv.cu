@@ -116,6 +116,7 @@ struct GemvArgs {
   unsigned *counters;   // [n_rt] arrivals of a K-split row tile (self-resetting)
   int R, P, ksplit;     // row tiles per CTA, warps per row tile, CTAs per row tile along K
   int cluster;          // > 1: the ksplit CTAs of a row tile are one cluster (R = 1)
+  int w_off;            // shared offset of the warps' weight slots (one unit each)
   int act_bytes;        // shared bytes of the activation staging / partial sums
   PeerRows peers;       // also store the outputs there (row-sharded gather), n = 0 otherwise
   GemvGroup grp;        // several tensors sharing the activation, n = 0 otherwise
@@ -153,8 +154,10 @@ __device__ __forceinline__ GroupOut group_outputs(const GemvGroup &grp, size_t g
   return o;
 }
 
-template <uint32_t T>
-__global__ void __launch_bounds__(384, 2) gemv_kernel(GemvArgs g) {
+// kSmemW: the unit goes into a shared-memory slot by cp.async instead of into registers (see
+// the two kernels after the body).
+template <uint32_t T, bool kSmemW>
+__device__ __forceinline__ void gemv_body(const GemvArgs &g) {
   extern __shared__ __align__(16) unsigned char smem[];
   using F = Fam<T>;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -183,11 +186,22 @@ __global__ void __launch_bounds__(384, 2) gemv_kernel(GemvArgs g) {
   if (g.cluster > 1) cluster_arrive_relaxed();
 
   pdl_launch_dependents();
-  // weights first, straight into registers: they depend on nothing the previous kernel
-  // writes, and the plan gives every warp at most one unit (k1 - k0 <= P)
+  // weights first: they depend on nothing the previous kernel writes, and the plan gives every
+  // warp at most one unit (k1 - k0 <= P).  Into registers, or copied into this warp's
+  // shared-memory slot without passing through registers.
+  uint8_t *wslot = smem + g.w_off + (size_t)warp * F::unit_bytes;
   UnitRegs<T> cur;
   const bool first = active && k0 + p < k1;
-  if (first) load_unit(cur, base + (size_t)(k0 + p) * F::unit_bytes, lane);
+  if (first) {
+    const uint8_t *src = base + (size_t)(k0 + p) * F::unit_bytes;
+    if (kSmemW) {
+      for (int i = lane; i < F::unit_bytes / 16; i += 32)
+        cp_async16(wslot + (size_t)i * 16, src + (size_t)i * 16);
+    } else {
+      load_unit(cur, src, lane);
+    }
+  }
+  if (kSmemW) cp_async_commit();
   pdl_wait();
 
   // the descriptor and this warp's activation chunks in one round trip
@@ -199,6 +213,7 @@ __global__ void __launch_bounds__(384, 2) gemv_kernel(GemvArgs g) {
       ch1 = load_chunk(g.codes, g.exps, g.n_in, chunk_first<T>(k0 + p, L, lane + 32));
   }
   if (desc.status != APX_OK) {  // the activation itself is refused (chart/mod.rs:1904-1907)
+    if (kSmemW) cp_async_wait_all();  // no copy lands after the CTA exits
     if (blockIdx.x == 0 && threadIdx.x == 0) {
       if (!g.grp.n) atomicMin(g.status, pack_status(0, (unsigned)desc.status, 0));
 #pragma unroll
@@ -211,6 +226,7 @@ __global__ void __launch_bounds__(384, 2) gemv_kernel(GemvArgs g) {
   // bound holds, the checked rows otherwise
   const bool wide = !fast_path<T>(desc, g.n_in);
   if (wide && !wide_path<T>(desc, g.n_in)) {
+    if (kSmemW) cp_async_wait_all();
     if (ks == 0 && p == 0 && active && slot == 0) {
       GroupOut go{g.n_out, g.out_q32, g.out_f32, g.status};
       if (g.grp.n) go = group_outputs(g.grp, rt0 + r);
@@ -228,13 +244,22 @@ __global__ void __launch_bounds__(384, 2) gemv_kernel(GemvArgs g) {
   if (first) {
     store_chunk<T>(*w, ch0, lane, lane < nch, desc.emin, wide);
     if (nch > 32) store_chunk<T>(*w, ch1, lane + 32, lane + 32 < nch, desc.emin, wide);
-    __syncwarp();
-    if (wide)
-      fold_unit_wide(acc, cur, w->codes + slot * slot_ints<T>(), w->e + slot * (F::span / 32),
-                     w->xs + slot * F::nxs, desc.emin);
-    else
-      fold_unit(acc, cur, w->codes + slot * slot_ints<T>(), w->e + slot * (F::span / 32),
-                w->xs + slot * F::nxs, desc.emin);
+    if (kSmemW) {
+      cp_async_wait_all();
+      __syncwarp();  // every lane's staging and weight copies before any lane's fold
+      fold_unit_smem<T>(acc, wslot, lane, w->codes + slot * slot_ints<T>(),
+                        w->e + slot * (F::span / 32), w->xs + slot * F::nxs, desc.emin, wide);
+    } else {
+      __syncwarp();
+      if (wide)
+        fold_unit_wide(acc, cur, w->codes + slot * slot_ints<T>(), w->e + slot * (F::span / 32),
+                       w->xs + slot * F::nxs, desc.emin);
+      else
+        fold_unit(acc, cur, w->codes + slot * slot_ints<T>(), w->e + slot * (F::span / 32),
+                  w->xs + slot * F::nxs, desc.emin);
+    }
+  } else if (kSmemW) {
+    cp_async_wait_all();
   }
   // the L lanes of a row combine
   for (int o = 1; o < L; o <<= 1) {
@@ -299,6 +324,18 @@ __global__ void __launch_bounds__(384, 2) gemv_kernel(GemvArgs g) {
     if (g.grp.n) go = group_outputs(g.grp, rt0 + r);
     finish_row(s, rt * H + lane / L, go.n_out, go.q32, go.f32, go.status, g.peers);
   }
+}
+
+// Weights in registers (80 a thread): one CTA of a projection and one of the next fill an SM.
+template <uint32_t T>
+__global__ void __launch_bounds__(384, 2) gemv_kernel(GemvArgs g) {
+  gemv_body<T, false>(g);
+}
+// Weights in shared memory (64 registers a thread): for a plan whose CTAs would not all be
+// resident at 80 registers (a second wave of a few CTAs costs a whole dependency chain).
+template <uint32_t T>
+__global__ void __maxnreg__(64) gemv_kernel_smem(GemvArgs g) {
+  gemv_body<T, true>(g);
 }
 
 // ---- streaming kernel for matrices larger than one resident wave ---------------------------
@@ -605,7 +642,16 @@ GemvPlan plan_gemv(uint32_t type, size_t n_out, size_t n_in, int sm_count) {
   const size_t red = (size_t)pl.R * pl.P * 32 * sizeof(Acc128) + 64;
   pl.act_bytes = (int)((std::max(stage, red) + 15) & ~(size_t)15);
   // a cluster's partial sums: [ksplit][32] in CTA 0's shared memory, after the staging
-  pl.smem = pl.act_bytes + (pl.cluster ? (size_t)pl.cluster * 32 * sizeof(Acc128) : 0);
+  pl.w_off = (int)((pl.act_bytes + (pl.cluster ? (size_t)pl.cluster * 32 * sizeof(Acc128) : 0) +
+                    15) & ~(size_t)15);
+  // Weights in registers while every CTA is resident at once at 80 registers a thread (25 warps
+  // an SM); otherwise in shared memory at 64 (32 warps), e.g. 448 CTAs of 8 warps (3584x8192
+  // Q4_K): 7.0 -> 5.4 us.  Measured the other way on the configs[0]/[1] shapes, which fit:
+  // 2.58 -> 2.86 us (8960x1536), 3.70 -> 4.55 us (1536x8960): smaller CTAs let the block
+  // scheduler stack two of one launch on an SM.
+  const int per_sm80 = std::max(1, 25 / (pl.R * pl.P));
+  pl.smem_w = pl.grid > (unsigned)sm_count * (unsigned)per_sm80;
+  pl.smem = pl.w_off + (pl.smem_w ? (size_t)pl.R * pl.P * unit_bytes_of(type) : 0);
   return pl;
 }
 
@@ -718,12 +764,19 @@ cudaError_t launch_gemv(const GemvPlan &pl, uint32_t type, const uint8_t *pack, 
   a.ksplit = pl.ksplit;
   a.cluster = pl.cluster > 1 ? pl.cluster : 1;
   a.act_bytes = pl.act_bytes;
+  a.w_off = pl.w_off;
   a.peers = peers ? *peers : no_peers;
   a.grp = GemvGroup{};
   switch (type) {
-    case kQ8_0: return launch_cfg(gemv_kernel<kQ8_0>, pl, a, stream);
-    case kQ4_K: return launch_cfg(gemv_kernel<kQ4_K>, pl, a, stream);
-    case kQ6_K: return launch_cfg(gemv_kernel<kQ6_K>, pl, a, stream);
+    case kQ8_0:
+      return pl.smem_w ? launch_cfg(gemv_kernel_smem<kQ8_0>, pl, a, stream)
+                       : launch_cfg(gemv_kernel<kQ8_0>, pl, a, stream);
+    case kQ4_K:
+      return pl.smem_w ? launch_cfg(gemv_kernel_smem<kQ4_K>, pl, a, stream)
+                       : launch_cfg(gemv_kernel<kQ4_K>, pl, a, stream);
+    case kQ6_K:
+      return pl.smem_w ? launch_cfg(gemv_kernel_smem<kQ6_K>, pl, a, stream)
+                       : launch_cfg(gemv_kernel<kQ6_K>, pl, a, stream);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -751,11 +804,18 @@ cudaError_t launch_gemv_group(const GemvPlan &pl, uint32_t type, const GemvGroup
   a.ksplit = pl.ksplit;
   a.cluster = pl.cluster > 1 ? pl.cluster : 1;
   a.act_bytes = pl.act_bytes;
+  a.w_off = pl.w_off;
   a.grp = grp;
   switch (type) {
-    case kQ8_0: return launch_cfg(gemv_kernel<kQ8_0>, pl, a, stream);
-    case kQ4_K: return launch_cfg(gemv_kernel<kQ4_K>, pl, a, stream);
-    case kQ6_K: return launch_cfg(gemv_kernel<kQ6_K>, pl, a, stream);
+    case kQ8_0:
+      return pl.smem_w ? launch_cfg(gemv_kernel_smem<kQ8_0>, pl, a, stream)
+                       : launch_cfg(gemv_kernel<kQ8_0>, pl, a, stream);
+    case kQ4_K:
+      return pl.smem_w ? launch_cfg(gemv_kernel_smem<kQ4_K>, pl, a, stream)
+                       : launch_cfg(gemv_kernel<kQ4_K>, pl, a, stream);
+    case kQ6_K:
+      return pl.smem_w ? launch_cfg(gemv_kernel_smem<kQ6_K>, pl, a, stream)
+                       : launch_cfg(gemv_kernel<kQ6_K>, pl, a, stream);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -21,6 +21,8 @@ struct GemvPlan {
   long long chunk; // streaming: units per warp
   int kmax;        // streaming: most warps sharing one row tile
   int act_bytes;   // one-wave: shared bytes of activation staging / partial sums
+  int w_off;       // one-wave: shared offset of the warps' weight slots (one unit each)
+  bool smem_w;     // one-wave: weights in those slots (gemv_kernel_smem), not in registers
   unsigned grid;
   int block;
   size_t smem;
