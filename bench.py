@@ -420,12 +420,13 @@ SHARDED = [(12, 28672, 8192), (12, 28672, 8192), (12, 8192, 28672)]  # gate, up,
 def measure_sharded(be, lib, dev, stream, steps, warmup, pg, rank, local, world):
     """configs[4] decode: the Llama-3-70B-shaped Q4_K FFN as a chain, row-sharded over the
     ranks (apeiron_b200/shard.py).  Each rank holds the same row range of gate and up and a row
-    range of down.  Per step: one step plan (apx_plan_run_async) runs this rank's gate and up
-    rows with SwiGLU + quant_act in their finish, storing each 32-row block of h (int8 codes
-    and an exponent byte) and its slice's descriptor into every rank's buffer by NVLink peer
-    stores; a publication (flags, bounded wait) makes every rank's slice visible and merges the
-    descriptors; down projects this rank's rows from the whole h with its outputs stored into
-    every rank's buffer; a second publication.  Strong scaling: the same FFN at every N."""
+    range of down.  Per step: GEMVs of this rank's gate and up rows (one grouped launch when
+    their layouts allow), SwiGLU + quant_act of the slice (apx_swiglu_quant_shard_async) storing
+    each 32-row block of h (int8 codes and an exponent byte) and the slice's descriptor into
+    every rank's buffer by NVLink peer stores; a publication (flags, bounded wait) makes every
+    rank's slice visible and merges the descriptors; down projects this rank's rows from the
+    whole h with its outputs stored into every rank's buffer; a second publication.  Strong
+    scaling: the same FFN at every N."""
     import ctypes as C
 
     import torch
