@@ -21,6 +21,7 @@
 
 #include "apx_common.cuh"
 #include "apx_kernels.h"
+#include "apx_pack.cuh"
 #include "apx_quant.cuh"
 #include "apx_swiglu.cuh"
 
@@ -56,6 +57,10 @@ struct FfnArgs {
 __global__ void __launch_bounds__(32 * kFfnWarps) swiglu_quant_kernel(FfnArgs a) {
   __shared__ int s_emin, s_emax, s_status;
   __shared__ unsigned s_nz;
+  // a programmatic dependent of the projections that wrote gate and up: nothing is read or
+  // written before their grids complete
+  pdl_launch_dependents();
+  pdl_wait();
   if (threadIdx.x == 0) {
     s_emin = 1 << 30;
     s_emax = -1;
@@ -134,6 +139,8 @@ __global__ void __launch_bounds__(32 * kFfnWarps) swiglu_quant_kernel(FfnArgs a)
 // The descriptor from the CTAs' statistics (one CTA per column).
 __global__ void __launch_bounds__(256) ffn_desc_kernel(const int4 *part, int nparts, size_t n,
                                                        ActDesc *desc, ShardDests dst) {
+  pdl_launch_dependents();
+  pdl_wait();
   part += (size_t)blockIdx.x * nparts;
   desc += blockIdx.x;
   int emin = 1 << 30, emax = -1, status = APX_OK;
@@ -220,12 +227,22 @@ cudaError_t launch_swiglu_quant_cols(const long long *gate, const long long *up,
       a.dst.desc[i] = static_cast<ActDesc *>(dests->desc[i]);
     }
   }
-  swiglu_quant_kernel<<<dim3(grid, (unsigned)cols), 32 * kFfnWarps, 0, stream>>>(a);
-  cudaError_t e = cudaGetLastError();
+  // both as programmatic dependents: each launches while its predecessor finishes
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, (unsigned)cols);
+  cfg.blockDim = dim3(32 * kFfnWarps);
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_allowed() ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, swiglu_quant_kernel, a);
   if (e != cudaSuccess) return e;
-  ffn_desc_kernel<<<(unsigned)cols, 256, 0, stream>>>(a.part, (int)grid, n,
-                                                        static_cast<ActDesc *>(desc), a.dst);
-  return cudaGetLastError();
+  cfg.gridDim = dim3((unsigned)cols);
+  cfg.blockDim = dim3(256);
+  return cudaLaunchKernelEx(&cfg, ffn_desc_kernel, static_cast<const int4 *>(a.part), (int)grid,
+                            n, static_cast<ActDesc *>(desc), a.dst);
 }
 
 }  // namespace apx
