@@ -827,12 +827,22 @@ __global__ void __launch_bounds__(32 * kWideWarps, 2) limb_wide_kernel(WideArgs 
           if (nch > 32) store_chunk<T>(wa[j], ch[j][1], lane + 32, lane + 32 < nch, em[j], true);
         }
         __syncwarp();
+        // one copy of the (large) wide fold in the loop, not one per column: the unrolled
+        // copies overflowed the instruction cache
+#pragma unroll 1
+        for (int j = 0; j < nc; j++) {
+          Acc128 t;
+          acc_zero(t);
+          int emj = em[0];
 #pragma unroll
-        for (int j = 0; j < kWideCols; j++)
-          if (j < nc)
-            fold_unit_smem<T>(acc[j], unit_s, lane, wa[j].codes + slot * slot_ints<T>(),
-                              wa[j].e + slot * (F::span / 32), wa[j].xs + slot * F::nxs, em[j],
-                              true);
+          for (int k = 1; k < kWideCols; k++)
+            if (k == j) emj = em[k];
+          fold_unit_smem<T>(t, unit_s, lane, wa[j].codes + slot * slot_ints<T>(),
+                            wa[j].e + slot * (F::span / 32), wa[j].xs + slot * F::nxs, emj, true);
+#pragma unroll
+          for (int k = 0; k < kWideCols; k++)
+            if (k == j) acc_add(acc[k], t);
+        }
       }
 #pragma unroll
       for (int j = 0; j < kWideCols; j++) {
