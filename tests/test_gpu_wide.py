@@ -100,6 +100,8 @@ def test_wide_spread_extremes(be, t):
     (Q6_K, 64, 20480),    # clusters of 2
     (Q4_K, 40, 131072),   # 128 units a row tile: 11 CTAs, global scratch and counters
     (Q4_K, 1536, 8960),   # no split (192 CTAs of 9 warps)
+    (Q4_K, 3584, 8192),   # 448 CTAs of 8 warps: weights in shared memory (64 registers)
+    (Q8_0, 2048, 8192),   # shared-memory weights and clusters of 2
 ])
 def test_cluster_split_shapes(be, t, n_out, n_in):
     x = synth.activation_f32(n_in, 3 + n_in)
