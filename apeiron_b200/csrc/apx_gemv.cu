@@ -609,6 +609,21 @@ GemvPlan plan_gemv(uint32_t type, size_t n_out, size_t n_in, int sm_count) {
   pl.pipe = false;
   pl.L = 1;
   while (pl.L < 4 && (K + pl.L - 1) / pl.L > 12) pl.L *= 2;
+  // More row tiles than SMs whose units are too many for two to share a CTA would stack two
+  // CTAs of the launch on a few SMs (their late start is the launch's tail): then 2L lanes a
+  // row, when that gives one CTA per SM with an even share of row tiles.  Q8_0 4864x896
+  // (configs[0]): 152 CTAs of 7 warps 2.68 us, 148 CTAs of 3 row tiles x 4 warps 2.44 us.
+  auto shared_fit = [&](int L, bool &fits) {
+    const size_t u = (size_t)(K + L - 1) / L, rt = (n_out + 32 / L - 1) / (32 / L);
+    const size_t share = (rt + sm_count - 1) / sm_count;
+    fits = share * u <= 12;
+    return u <= 12 && rt > (size_t)sm_count;
+  };
+  for (bool fits = false; pl.L < 4 && shared_fit(pl.L, fits) && !fits;) {
+    bool fits2 = false;
+    if (!shared_fit(2 * pl.L, fits2) || !fits2) break;
+    pl.L *= 2;
+  }
   const int H = 32 / pl.L;
   const int U = (K + pl.L - 1) / pl.L;
   const size_t n_rt = (n_out + H - 1) / H;
