@@ -350,3 +350,53 @@ def test_plan_create_refuses_bad_records(be):
     plan, rc = _plan(lib, ctx, [good[0], _proj(tg, 1024, 896, 0, ou, 0, _abi.PLAN_GATE),
                                 good[2]], acts, ffn)
     assert not plan and rc == _abi.APX_ERR_INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("t,n_embd,n_ff", [(Q4_K, 896, 4864), (Q4_K, 8192, 1024)])
+def test_plan_ffn_peer_destinations(be, t, n_embd, n_ff):
+    """An FFN's peer destinations (apx_plan_ffn.n_peers: where a row shard's SwiGLU + quant_act
+    blocks and its slice descriptor also go, one per other rank) hold exactly what the FFN writes
+    into its own activation, on every launch; the chain's down is unchanged.  Here the
+    destinations are other buffers of the same GPU (L = 1 gate/up rows, and L = 4)."""
+    torch = _torch()
+    dev = torch.device("cuda:0")
+    lib, ctx = be.lib, be.ctx
+    projs, acts, ffns, keep = _ffn_layers(be, t, n_embd, n_ff, 1, 0, 950)
+    pad = lib.apx_act_padded_len(n_ff)
+    peers = [(torch.zeros(pad, dtype=torch.int8, device=dev),
+              torch.full((pad // 32,), 0xFF, dtype=torch.uint8, device=dev),
+              torch.zeros(8, dtype=torch.int32, device=dev)) for _ in range(3)]
+    f = ffns[0]
+    f.n_peers = len(peers)
+    for i, (pc, pe, pd) in enumerate(peers):
+        f.d_peer_codes[i] = pc.data_ptr()
+        f.d_peer_exps[i] = pe.data_ptr()
+        f.d_peer_desc[i] = pd.data_ptr()
+    plan, rc = _plan(lib, ctx, projs, acts, ffns)
+    assert plan, rc
+    try:
+        want = _separate_chain(be, keep[0], n_embd, n_ff, 0)
+        k = keep[0]
+        for rep in range(2):
+            for o in (k["og"], k["ou"], k["od"]):
+                o.reset()
+            k["f_status"].fill_(-1)
+            for pc, pe, pd in peers:
+                pc.zero_()
+                pe.fill_(0xFF)
+                pd.zero_()
+            _run(lib, plan)
+            assert int(k["f_status"][0].item()) == -1
+            hc = k["h"].codes.cpu().numpy()
+            he = k["h"].exps.cpu().numpy()
+            hd = k["h"].desc.cpu().numpy()
+            assert np.array_equal(hc, want["hc"]) and np.array_equal(he, want["he"])
+            assert np.array_equal(hd, want["hd"])
+            for pc, pe, pd in peers:
+                assert np.array_equal(pc.cpu().numpy()[:n_ff], hc[:n_ff]), rep
+                assert np.array_equal(pe.cpu().numpy()[:(n_ff + 31) // 32],
+                                      he[:(n_ff + 31) // 32]), rep
+                assert np.array_equal(pd.cpu().numpy(), hd), rep
+            assert np.array_equal(k["od"].q32.cpu().numpy()[:n_embd], want["y"][0])
+    finally:
+        lib.apx_plan_destroy(plan)
