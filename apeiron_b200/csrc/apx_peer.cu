@@ -81,15 +81,17 @@ __global__ void __launch_bounds__(32) gather_publish_kernel(const __grid_constan
   const unsigned long long *flags = reinterpret_cast<const unsigned long long *>(own + g.flag_off);
   const unsigned long long t0 = now_ns(), limit = (unsigned long long)g.timeout_us * 1000ull;
   bool ok = true;
+  // One thread of one warp polls: short sleeps (at most 64 ns) keep the hand-off's latency,
+  // which every step of a sharded chain pays twice, close to the last flag's arrival.
   for (int r = 0; r < g.world && ok; r++) {
-    unsigned ns = 32;
+    unsigned ns = 16;
     while (ld_acquire_sys(flags + r) < epoch) {
       if (now_ns() - t0 > limit) {
         ok = false;
         break;
       }
       __nanosleep(ns);
-      if (ns < 1024) ns *= 2;
+      if (ns < 64) ns *= 2;
     }
   }
   const long long *keys = reinterpret_cast<const long long *>(own + g.key_off);
