@@ -432,6 +432,56 @@ def measure_decode_step(be, lib, dev, stream, steps, warmup, pg, local, world):
         parts[name] = t0.elapsed_time(t1) / G
         del g2
     del gr
+
+    # e2e: every step copies the f32 input vector in (pinned), quantizes it on the device into
+    # the activation the plan and the head read, runs both, and copies the head's Q32.32 outputs
+    # out on a stream of its own (overlapping the next step; the output double-buffered)
+    hxv = torch.from_numpy(x).pin_memory()
+    dxv = torch.empty(n_embd, dtype=torch.float32, device=dev)
+    hy = torch.empty(mats[head][1], dtype=torch.int64).pin_memory()
+    dys = [outs[head], torch.zeros_like(outs[head])]
+    s_out = torch.cuda.Stream(device=dev)
+    ev_ready = [torch.cuda.Event() for _ in range(2)]
+    ev_free = [torch.cuda.Event() for _ in range(2)]
+
+    def e2e_step(i):
+        par = i % 2
+        with torch.cuda.stream(stream):
+            dxv.copy_(hxv, non_blocking=True)
+            assert lib.apx_quant_f32_async(be.ctx, dxv.data_ptr(), n_embd, codes.data_ptr(),
+                                           exps.data_ptr(), desc.data_ptr(), sp) == 0
+            assert lib.apx_plan_run_async(plans[i % copies], sp) == 0
+            stream.wait_event(ev_free[par])
+            assert lib.apx_matvec_async(be.ctx, tensors[i % copies][head].handle,
+                                        mats[head][1], mats[head][2], codes.data_ptr(),
+                                        exps.data_ptr(), desc.data_ptr(), dys[par].data_ptr(),
+                                        None, statuses[head].data_ptr(), sp) == 0
+            ev_ready[par].record(stream)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_ready[par])
+            hy.copy_(dys[par], non_blocking=True)
+            ev_free[par].record(s_out)
+
+    for i in range(2):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    barrier(pg, local)
+    e_steps = max(4, min(steps, 400)) // 2 * 2
+    ev_start = torch.cuda.Event()
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        ev_start.record(stream)
+    s_out.wait_event(ev_start)
+    for i in range(e_steps):
+        e2e_step(i)
+    with torch.cuda.stream(stream):
+        stream.wait_event(ev_free[(e_steps - 1) % 2])
+        t1.record(stream)
+    torch.cuda.synchronize()
+    barrier(pg, local)
+    e_ms = max_over_ranks(t0.elapsed_time(t1), pg, local) / e_steps
+    assert np.array_equal(hy.numpy(), want), "decode-step e2e head outputs differ"
+    assert bool((statuses == -1).all().item()), "refusal in the e2e steps"
     for pl in plans:
         lib.apx_plan_destroy(pl)
     hbm, _ = peaks()
@@ -463,6 +513,13 @@ def measure_decode_step(be, lib, dev, stream, steps, warmup, pg, local, world):
                      "us": parts["head"] * 1e3, "gbs": head_bytes / (parts["head"] / 1e3) / 1e9,
                      "frac": head_bytes / (parts["head"] / 1e3) / 1e9 / hbm}],
         "gpu_launches_per_step": 2,
+        "e2e": {"value": world * per_step / (e_ms / 1e3) / 1e9, "unit": "GB/s",
+                "ms_per_step": e_ms, "h2d_bytes_per_step": 4 * n_embd,
+                "d2h_bytes_per_step": 8 * mats[head][1],
+                "note": "per step: the pinned f32 input vector -> device, quant_act on the "
+                        "device (apx_quant_f32_async), the step plan and the head, the head's "
+                        "Q32.32 outputs -> pinned host on a stream of their own (overlapping "
+                        "the next step); CUDA events, max over ranks"},
     }
 
 
