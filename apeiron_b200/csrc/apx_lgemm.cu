@@ -1062,7 +1062,15 @@ __global__ void __launch_bounds__(kLThreads, 1)
       const int nk = min(g.kstages - ks0, nit - pi);
       const int mt = tile / g.n_tiles, nt = tile % g.n_tiles;
       const bool two = needs3(nt);
-      long long acc[kEpt];
+      // The piece's sums T = Σ_p 256^p·A_p go to this CTA's partial slot in global memory (they
+      // stay in L2) a chunk of kChunk tokens at a time, so that a warp holds no more than kChunk
+      // 64-bit sums in registers (all kEpt of them spilled to local memory, and the finish then
+      // waited on those loads one after another).  A split tile's slot is read by the CTA that
+      // finishes the tile; a whole tile's (slot 2b + 1, which only this CTA's last stream-K
+      // piece uses after it) by the same thread right after.
+      const bool split = !(ks0 == 0 && nk == g.kstages);  // stream-K: other CTAs hold the rest
+      const int slot = 2 * b + (split && pi == dp ? 0 : 1);
+      long long *mine = g.w.part + (size_t)slot * kPartSlot + (size_t)ew * (kEpt * 32);
       for (int pass = 0; pass < (two ? 2 : 1); pass++, npass++) {
         const bool got = mbar_wait_long(tfull, npass & 1);
         // every epilogue warp is done with the previous piece (tok_e included) past this barrier
@@ -1072,22 +1080,20 @@ __global__ void __launch_bounds__(kLThreads, 1)
           break;
         }
         tc_fence_after();
-        if (pass == 0) {
-          if (ew == 0)
-            for (int t = lane; t < N; t += 32) {
-              const int c = nt * N + t;
-              // coherent loads: the prep kernel wrote these while this grid was already
-              // resident (programmatic dependent launch), so the read-only path could serve a
-              // stale line
-              tok_e[t] = c < g.n_cols && on_gemm(__ldcg(g.w.route + c)) ? __ldcg(g.w.emin + c)
-                                                                          : -1;
-            }
-          // drain: T = Σ_p 256^p·A_p by Horner from the top accumulator, up to 16 columns per
-          // wait
+        if (pass == 0 && ew == 0)
+          for (int t = lane; t < N; t += 32) {
+            const int c = nt * N + t;
+            // coherent loads: the prep kernel wrote these while this grid was already resident
+            // (programmatic dependent launch), so the read-only path could serve a stale line
+            tok_e[t] = c < g.n_cols && on_gemm(__ldcg(g.w.route + c)) ? __ldcg(g.w.emin + c) : -1;
+          }
+#pragma unroll 1
+        for (int c = 0; c < kEpt / kChunk; c++) {
+          long long acc[kChunk];
+          if (pass == 0) {
+            // drain: T by Horner from the top accumulator
 #pragma unroll
-          for (int p = kAcc - 1; p >= 0; p--) {
-#pragma unroll
-            for (int c = 0; c < kEpt / kChunk; c++) {
+            for (int p = kAcc - 1; p >= 0; p--) {
               uint32_t v[kChunk];
 #pragma unroll
               for (int h = 0; h < kChunk / 8; h++)
@@ -1095,17 +1101,14 @@ __global__ void __launch_bounds__(kLThreads, 1)
               tmem_wait_ld();
 #pragma unroll
               for (int j = 0; j < kChunk; j++)
-                acc[kChunk * c + j] = p == kAcc - 1
-                                          ? (long long)(int)v[j]
-                                          : acc[kChunk * c + j] * 256 + (long long)(int)v[j];
+                acc[j] = p == kAcc - 1 ? (long long)(int)v[j] : acc[j] * 256 + (long long)(int)v[j];
             }
-          }
-        } else {
-          // the third digit's pass: T += Σ_p 2^(16 + 8p)·A_p
+          } else {
+            // the third digit's pass: T += Σ_p 2^(16 + 8p)·A_p
 #pragma unroll
-          for (int p = 0; p < D; p++) {
+            for (int j = 0; j < kChunk; j++) acc[j] = mine[(kChunk * c + j) * 32 + lane];
 #pragma unroll
-            for (int c = 0; c < kEpt / kChunk; c++) {
+            for (int p = 0; p < D; p++) {
               uint32_t v[kChunk];
 #pragma unroll
               for (int h = 0; h < kChunk / 8; h++)
@@ -1113,27 +1116,28 @@ __global__ void __launch_bounds__(kLThreads, 1)
               tmem_wait_ld();
 #pragma unroll
               for (int j = 0; j < kChunk; j++)
-                acc[kChunk * c + j] += (long long)(int)v[j] * (1ll << (16 + 8 * p));
+                acc[j] += (long long)(int)v[j] * (1ll << (16 + 8 * p));
             }
           }
+#pragma unroll
+          for (int j = 0; j < kChunk; j++) mine[(kChunk * c + j) * 32 + lane] = acc[j];
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(tempty);  // the next pass's MMAs may overwrite TMEM
       }
       if (failed) break;
-      bool finish = ks0 == 0 && nk == g.kstages;  // this CTA holds the whole tile
-      if (!finish) {
-        // split tile (stream-K): store the partial sums, arrive; the last to arrive adds the
-        // others'.  Slot 2b holds CTA b's first run piece, 2b + 1 its last.
-        const long long tbeg = (long long)(tile - g.waves * g.G) * g.kstages;
-        const int slot = 2 * b + (pi == dp ? 0 : 1);
-        long long *mine = g.w.part + (size_t)slot * kPartSlot + (size_t)ew * (kEpt * 32);
-#pragma unroll
-        for (int j = 0; j < kEpt; j++) mine[j * 32 + lane] = acc[j];
+      bool finish = !split;  // this CTA holds the whole tile
+      int bf = b, bl = b;
+      long long tbeg = 0;
+      if (split) {
+        // the partial sums are stored: arrive; the last to arrive adds the others'.  Slot 2b
+        // holds CTA b's first run piece, 2b + 1 its last.
+        tbeg = (long long)(tile - g.waves * g.G) * g.kstages;
         __threadfence();
         epi_sync();
-        const int bf = lowner(g, tbeg), bl = lowner(g, tbeg + g.kstages - 1);
+        bf = lowner(g, tbeg);
+        bl = lowner(g, tbeg + g.kstages - 1);
         if (ew == 0 && lane == 0) {
           const int old = atomicAdd(g.w.cnt + tile, 1);
           const int last = old == bl - bf;
@@ -1142,17 +1146,7 @@ __global__ void __launch_bounds__(kLThreads, 1)
         }
         epi_sync();
         finish = *slast != 0;
-        if (finish) {
-          __threadfence();
-          for (int b2 = bf; b2 <= bl; b2++) {
-            if (b2 == b) continue;
-            const int slot2 = 2 * b2 + ((b2 == bf && lstart(g, b2) < tbeg) ? 1 : 0);
-            const long long *other =
-                g.w.part + (size_t)slot2 * kPartSlot + (size_t)ew * (kEpt * 32);
-#pragma unroll
-            for (int j = 0; j < kEpt; j++) acc[j] += __ldcg(other + j * 32 + lane);
-          }
-        }
+        if (finish) __threadfence();
       } else {
         epi_sync();  // tok_e is written
       }
@@ -1162,56 +1156,70 @@ __global__ void __launch_bounds__(kLThreads, 1)
         const size_t row = (size_t)mt * kLM + rl;
         const bool live = row < g.n_out;
         const unsigned kmin = live ? (unsigned)__ldg(g.kmin + row) : 0u;
-        const int t0 = kEpt * tq, c0 = nt * N + t0;
-        float *of = g.out_f32 ? g.out_f32 + (size_t)c0 * g.n_out + row : nullptr;
-        long long *oq = g.out_q32 ? g.out_q32 + (size_t)c0 * g.n_out + row : nullptr;
-        // the tokens' exponents: when every live token's shift kmin + e lies in [32, 64) the
-        // loop has no call in it (the general case is out of line)
-        int emn = 1 << 20, emx = -1;
+#pragma unroll 1
+        for (int c = 0; c < kEpt / kChunk; c++) {
+          long long acc[kChunk];
 #pragma unroll
-        for (int j = 0; j < kEpt; j++) {
-          const int e = tok_e[t0 + j];
-          if (e >= 0) {
-            emn = min(emn, e);
-            emx = max(emx, e);
+          for (int j = 0; j < kChunk; j++) acc[j] = mine[(kChunk * c + j) * 32 + lane];
+          for (int b2 = bf; b2 <= bl; b2++) {
+            if (b2 == b) continue;
+            const int slot2 = 2 * b2 + ((b2 == bf && lstart(g, b2) < tbeg) ? 1 : 0);
+            const long long *other =
+                g.w.part + (size_t)slot2 * kPartSlot + (size_t)ew * (kEpt * 32);
+#pragma unroll
+            for (int j = 0; j < kChunk; j++) acc[j] += __ldcg(other + (kChunk * c + j) * 32 + lane);
           }
-        }
-        uint32_t bad = 0;  // bit j: token j's output leaves i64
-        if (emx < 0 || ((int)kmin + emn >= 32 && (int)kmin + emx < 64)) {
-          // v = T·2^t, t = kmin + e − 32 in [0, 32), its f32 image RN(T)·2^(t − 32)
+          const int t0 = kEpt * tq + kChunk * c, c0 = nt * N + t0;
+          float *of = g.out_f32 ? g.out_f32 + (size_t)c0 * g.n_out + row : nullptr;
+          long long *oq = g.out_q32 ? g.out_q32 + (size_t)c0 * g.n_out + row : nullptr;
+          // the tokens' exponents: when every live token's shift kmin + e lies in [32, 64) the
+          // loop has no call in it (the general case is out of line)
+          int emn = 1 << 20, emx = -1;
 #pragma unroll
-          for (int j = 0; j < kEpt; j++) {
+          for (int j = 0; j < kChunk; j++) {
             const int e = tok_e[t0 + j];
-            const unsigned t = kmin + (unsigned)e - 32u;
-            const int hi = (int)(acc[j] >> 32);
-            const bool fits = (hi >> (31 - (t & 31))) == (hi >> 31);
-            if (e >= 0 && live) {
-              if (of)
-                *of = fits ? __ll2float_rn(acc[j]) * __int_as_float((int)(t + 95) << 23)
-                           : __int_as_float(0x7FC00000);
-              if (oq) *oq = fits ? (long long)((unsigned long long)acc[j] << (t & 31)) : 0;
+            if (e >= 0) {
+              emn = min(emn, e);
+              emx = max(emx, e);
             }
-            bad |= (e >= 0 && live && !fits) ? 1u << j : 0u;
-            if (of) of += g.n_out;
-            if (oq) oq += g.n_out;
           }
-        } else {
+          uint32_t bad = 0;  // bit j: token j's output leaves i64
+          if (emx < 0 || ((int)kmin + emn >= 32 && (int)kmin + emx < 64)) {
+            // v = T·2^t, t = kmin + e − 32 in [0, 32), its f32 image RN(T)·2^(t − 32)
 #pragma unroll
-          for (int j = 0; j < kEpt; j++) {
-            const int e = tok_e[t0 + j];
-            if (e < 0 || !live) continue;
-            long long v;
-            float f;
-            const bool fits = finish_fast(acc[j], kmin + (unsigned)e, v, f);
-            if (of) of[(size_t)j * g.n_out] = fits ? f : __int_as_float(0x7FC00000);
-            if (oq) oq[(size_t)j * g.n_out] = fits ? v : 0;
-            bad |= fits ? 0u : 1u << j;
+            for (int j = 0; j < kChunk; j++) {
+              const int e = tok_e[t0 + j];
+              const unsigned t = kmin + (unsigned)e - 32u;
+              const int hi = (int)(acc[j] >> 32);
+              const bool fits = (hi >> (31 - (t & 31))) == (hi >> 31);
+              if (e >= 0 && live) {
+                if (of)
+                  *of = fits ? __ll2float_rn(acc[j]) * __int_as_float((int)(t + 95) << 23)
+                             : __int_as_float(0x7FC00000);
+                if (oq) *oq = fits ? (long long)((unsigned long long)acc[j] << (t & 31)) : 0;
+              }
+              bad |= (e >= 0 && live && !fits) ? 1u << j : 0u;
+              if (of) of += g.n_out;
+              if (oq) oq += g.n_out;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < kChunk; j++) {
+              const int e = tok_e[t0 + j];
+              if (e < 0 || !live) continue;
+              long long v;
+              float f;
+              const bool fits = finish_fast(acc[j], kmin + (unsigned)e, v, f);
+              if (of) of[(size_t)j * g.n_out] = fits ? f : __int_as_float(0x7FC00000);
+              if (oq) oq[(size_t)j * g.n_out] = fits ? v : 0;
+              bad |= fits ? 0u : 1u << j;
+            }
           }
-        }
-        while (bad) {  // output overflow: rare, one refusal per token
-          const int j = __ffs(bad) - 1;
-          bad &= bad - 1;
-          atomicMin(g.status + (size_t)(c0 + j) * 2, pack_status(row, kKindOutputOverflow, 0));
+          while (bad) {  // output overflow: rare, one refusal per token
+            const int j = __ffs(bad) - 1;
+            bad &= bad - 1;
+            atomicMin(g.status + (size_t)(c0 + j) * 2, pack_status(row, kKindOutputOverflow, 0));
+          }
         }
       }
       pi += nk;

@@ -1573,6 +1573,8 @@ def gemm_probe(args):
     dev = torch.device("cuda:0")
     be = Backend(0)
     lib = be.lib
+    route = {"auto": 0, "digits": 1, "fold": 2}[args.gemm_route]
+    assert lib.apx_ctx_set_gemm_route(be.ctx, route) == 0
     stream = torch.cuda.Stream(device=dev)
     sp = stream.cuda_stream
     raws = [synth.payload(t, n_out, n_in, 600 + c) for c in range(2)]
@@ -1609,7 +1611,8 @@ def gemm_probe(args):
     assert bool((st[0::2] == -1).all().item())
     us = t0.elapsed_time(t1) / steps * 1e3
     print(json.dumps({"probe": "gemm", "type": t, "n_out": n_out, "n_in": n_in, "tokens": k,
-                      "us_per_call": us, "tops": 2.0 * k * n_out * n_in / us / 1e6}), flush=True)
+                      "route": args.gemm_route, "us_per_call": us,
+                      "tops": 2.0 * k * n_out * n_in / us / 1e6}), flush=True)
     be.close()
 
 
@@ -1634,6 +1637,8 @@ def main():
     ap.add_argument("--gemm-probe", default=None,
                     help="TYPE,N_OUT,N_IN,TOKENS: time one prefill shape alone and exit (a small "
                          "case for profilers)")
+    ap.add_argument("--gemm-route", default="auto", choices=["auto", "digits", "fold"],
+                    help="the Q8_0 GEMM a --gemm-probe call takes (the bits are the same)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.gemm_probe:
