@@ -998,6 +998,12 @@ __global__ void __launch_bounds__(kLThreads, 1)
       lat(g, b, s0, pi, tile, ks0);
       const int nk = min(g.kstages - ks0, nit - pi);
       const int passes = needs3(tile % g.n_tiles) ? 2 : 1;
+      // The last token tile's MMAs cover only its live tokens, rounded up to the 16 the
+      // instruction takes (512 tokens in 96-token tiles: 32 of the last tile's 96).  The columns
+      // past them keep whatever TMEM held; they belong to padding tokens, which are never stored.
+      const int live_tok = g.n_cols - (tile % g.n_tiles) * N;
+      const int neff = live_tok >= N ? N : max(16, (live_tok + 15) & ~15);
+      const uint32_t idesc = (S::kIdesc & ~(0x3Fu << 17)) | ((uint32_t)(neff >> 3) << 17);
       for (int pass = 0; ok && pass < passes; pass++, npass++) {
         if (lane == 0) {
           if (npass > 0 && !mbar_wait(tempty, (npass - 1) & 1)) ok = 0;
@@ -1020,17 +1026,17 @@ __global__ void __launch_bounds__(kLThreads, 1)
                   const uint32_t acc = tmem + (uint32_t)(p * N);
                   if (p < D)  // (p, 0)
                     mma_i8(acc, wd + (uint64_t)(p * (kLTileW >> 4) + 2 * q),
-                           xd + (uint64_t)(2 * q), S::kIdesc, first ? 0u : 1u);
+                           xd + (uint64_t)(2 * q), idesc, first ? 0u : 1u);
                   if (p >= 1)  // (p − 1, 1)
                     mma_i8(acc, wd + (uint64_t)((p - 1) * (kLTileW >> 4) + 2 * q),
-                           xd + (uint64_t)((S::kTileX >> 4) + 2 * q), S::kIdesc,
+                           xd + (uint64_t)((S::kTileX >> 4) + 2 * q), idesc,
                            (first && p == D) ? 0u : 1u);
                 }
               } else {
 #pragma unroll
                 for (int p = 0; p < D; p++)  // (p, 2): the stage's first activation tile
                   mma_i8(tmem + (uint32_t)(p * N), wd + (uint64_t)(p * (kLTileW >> 4) + 2 * q),
-                         xd + (uint64_t)(2 * q), S::kIdesc, first ? 0u : 1u);
+                         xd + (uint64_t)(2 * q), idesc, first ? 0u : 1u);
               }
             }
             mma_commit(empty + st);
