@@ -645,9 +645,10 @@ struct LArgs {
   unsigned long long *status;  // column c at status[c·2]
   size_t n_out;
   int n_cols, kstages, n_tiles, tiles;  // tile = mt·n_tiles + nt
-  // Work split over G CTAs (one per SM at most): `waves` data-parallel waves of whole tiles (CTA
-  // b takes tiles b, b + G, ...: the CTAs of a wave share weight row tiles, so each row tile's
-  // digits stream from HBM once), then the remaining tiles' (tile, stage) space, sk_iters long,
+  // Work split over G CTAs (one per SM at most): `waves` data-parallel waves of whole tiles (in
+  // wave w CTA b takes tile w·G + (b + w) mod G: the CTAs of a wave share weight row tiles, so
+  // each row tile's digits stream from HBM once, and the rotation spreads the cheaper tiles of
+  // the last token tile evenly over the CTAs), then the remaining tiles' (tile, stage) space, sk_iters long,
   // split evenly in K-contiguous runs over the first Gs CTAs (stream-K: CTA b < Gs takes
   // [b·sk_iters/Gs, (b+1)·sk_iters/Gs); Gs <= sk_iters, so no run is empty and every CTA between
   // a split tile's first and last owner contributes to it).
@@ -672,7 +673,8 @@ __device__ __forceinline__ void lat(const LArgs &g, int b, long long s0, int i, 
                                     int &ks) {
   const int dp = g.waves * g.kstages;
   if (i < dp) {
-    tile = b + (i / g.kstages) * g.G;
+    const int w = i / g.kstages;
+    tile = w * g.G + (b + w) % g.G;
     ks = i % g.kstages;
   } else {
     const long long it = s0 + (i - dp);
