@@ -818,14 +818,21 @@ def measure_prefill70(be, lib, dev, stream, steps, warmup, pg, rank, local, worl
     sts = [st() for _ in rows]
 
     def step(check=False):
+        # each projection's all-gather runs on NCCL's stream while the next projection computes
+        # (the work's wait makes this stream wait for it only after that projection is queued)
+        pending = None
         for m in range(3):
             xin, n_in = ins[m]
             assert lib.apx_matmat_f32_async(be.ctx, shards[m].tensor.handle, rows[m], n_in, k,
                                             xin.data_ptr(), n_in,
                                             yq[m].data_ptr() if check else None,
                                             y_s[m].data_ptr(), sts[m].data_ptr(), sp) == 0
+            if pending is not None:
+                pending.wait()
             if world > 1:
-                pg.all_gather_into_tensor(y_g[m], y_s[m])
+                pending = pg.all_gather_into_tensor(y_g[m], y_s[m], async_op=True)
+        if pending is not None:
+            pending.wait()
 
     with torch.cuda.stream(stream):
         step(check=True)
@@ -891,16 +898,26 @@ def measure_prefill70(be, lib, dev, stream, steps, warmup, pg, rank, local, worl
         with torch.cuda.stream(stream):
             stream.wait_event(ev_in_ready[par])
             stream.wait_event(ev_out_free[par])
+            pending = None
             for m in range(3):
                 xin, n_in = (d_in[par][0], n_embd) if m < 2 else (d_in[par][1], n_ff)
                 assert lib.apx_matmat_f32_async(be.ctx, shards[m].tensor.handle, rows[m], n_in,
                                                 k, xin.data_ptr(), n_in, None,
                                                 d_ys[par][m].data_ptr(), sts[m].data_ptr(),
                                                 sp) == 0
+                if m == 2:
+                    ev_in_free[par].record(stream)
+                if pending is not None:  # the previous projection's gather, behind this one
+                    pending.wait()
+                    ev_out_ready[par][m - 1].record(stream)
                 if world > 1:
-                    pg.all_gather_into_tensor(d_yg[par][m], d_ys[par][m])
-                ev_out_ready[par][m].record(stream)
-            ev_in_free[par].record(stream)
+                    pending = pg.all_gather_into_tensor(d_yg[par][m], d_ys[par][m],
+                                                        async_op=True)
+                else:
+                    ev_out_ready[par][m].record(stream)
+            if pending is not None:
+                pending.wait()
+                ev_out_ready[par][2].record(stream)
         with torch.cuda.stream(s_out):
             for m in range(3):
                 s_out.wait_event(ev_out_ready[par][m])
